@@ -1,0 +1,824 @@
+/*
+ * sog_oracle.c — CPU restatement of SOG's Gaussian reciprocal-space solver.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the parity checker for the CUDA
+ * library in sog_b200/csrc: the tests, __graft_entry__.smoke() and the
+ * cpu_baseline / reference arm of bench.py load it.  The product path never
+ * calls it and there is no CPU fallback built on it.
+ *
+ * Parity anchors (paths relative to the reference project root):
+ *   - QuadS weights        src/sog/module/quads_spline.py:69-158
+ *   - QuadS influence      src/sog/module/quads_fft.py:119-197
+ *   - QuadS pipeline       src/sog/module/quads_fft.py:209-326
+ *   - B-spline weights     lmp/sog.cpp:89-110 (same recurrence as
+ *                          lmp/sog_spline.h:19-38, which oracle/_ref compiles)
+ *   - B-spline Green       lmp/sog.cpp:1113-1176 (sinc tables) and
+ *                          lmp/sog.cpp:1479-1578 (principal / alias sums)
+ *   - B-spline stencil     lmp/sog.cpp:1977-2018 (offsets ix0-(p-1)/2+a)
+ *   - ik forces, potential lmp/sog.cpp:2111-2127, quads_fft.py:301-313
+ *   - backward (dq, amp, bw2) src/sog/module/cubes2_fft.py:746-869
+ *   - virial               src/sog/module/cubes2_fft.py:874-921
+ *   - direct k-sum         src/sog/module/gaussian.py:1281-1337
+ *   - mode convention      quads_fft.py:246-258 (Nyquist at +N/2)
+ *   - irfftn semantics     torch.fft.irfftn: C2C over z,y then C2R along x
+ *                          using Re() of the mx=0 / mx=nx/2 columns
+ *
+ * Parity status: QuadS and direct paths are pinned against fixtures made by
+ * importing the reference (tests/golden/make_golden.py); the B-spline weights
+ * are pinned against the reference's own compiled sog_spline.h
+ * (oracle/_ref).  The B-spline Green function has no executable reference
+ * (lmp/sog.cpp needs LAMMPS); it is restated here from the source.
+ *
+ * Everything is double precision.  Plain C99 + OpenMP.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define ORC_PI 3.14159265358979323846
+
+/* ------------------------------------------------------------------------ */
+/* spline weights                                                            */
+/* ------------------------------------------------------------------------ */
+
+/* Cardinal B-spline weights of order n at fractional offset t (Cox-de Boor).
+ * w[a] is the weight of grid node ix0-(n-1)/2+a.  lmp/sog.cpp:89-110. */
+void orc_bspline_weights(int n, double t, double *w) {
+  double prev[8];
+  for (int a = 0; a < n; ++a) w[a] = 0.0;
+  w[0] = 1.0 - t;
+  w[1] = t;
+  for (int k = 3; k <= n; ++k) {
+    const double inv = 1.0 / (double)(k - 1);
+    for (int a = 0; a < n; ++a) prev[a] = w[a];
+    w[k - 1] = t * prev[k - 2] * inv;
+    for (int j = 1; j <= k - 2; ++j)
+      w[k - 1 - j] = ((t + (double)j) * prev[k - 2 - j] +
+                      ((double)(k - j) - t) * prev[k - 1 - j]) * inv;
+    w[0] = (1.0 - t) * prev[0] * inv;
+  }
+}
+
+/* QuadS xi for order 4/6: quads_spline.py:12-13 (Table I). */
+double orc_quads_xi(int order) {
+  return order == 4 ? 1.0 / sqrt(3.0) : 0.72879488;
+}
+
+/* Ascending monomial coefficients of the base polynomials c_1..c_nu
+ * (quads_spline.py:95-125), then the per-offset table with the reflection
+ * c_i(t) = c_{1-i}(1-t) (quads_spline.py:128-163).  coef[k*order + p] is the
+ * coefficient of t^p for offset index k (offset = 1-nu+k). */
+static void quads_base(int i, double xi, int order, double *c) {
+  const double x2 = xi * xi, x4 = x2 * x2;
+  for (int p = 0; p < order; ++p) c[p] = 0.0;
+  if (order == 4) {
+    if (i == 1) {
+      c[0] = x2 / 2.0; c[1] = -(3.0 * x2 - 2.0) / 2.0; c[2] = 0.5; c[3] = -0.5;
+    } else {
+      c[1] = (3.0 * x2 - 1.0) / 6.0; c[3] = 1.0 / 6.0;
+    }
+  } else {
+    if (i == 1) {
+      c[0] = -(3.0 * x4 - 4.0 * x2) / 6.0; c[1] = (5.0 * x4 - 7.0 * x2 + 4.0) / 4.0;
+      c[2] = -(3.0 * x2 - 2.0) / 3.0; c[3] = (10.0 * x2 - 7.0) / 12.0;
+      c[4] = -1.0 / 6.0; c[5] = 1.0 / 12.0;
+    } else if (i == 2) {
+      c[0] = (3.0 * x4 - x2) / 24.0; c[1] = -(5.0 * x4 - 7.0 * x2 + 2.0) / 8.0;
+      c[2] = (6.0 * x2 - 1.0) / 24.0; c[3] = -(10.0 * x2 - 7.0) / 24.0;
+      c[4] = 1.0 / 24.0; c[5] = -1.0 / 24.0;
+    } else {
+      c[1] = (15.0 * x4 - 15.0 * x2 + 4.0) / 120.0; c[3] = (2.0 * x2 - 1.0) / 24.0;
+      c[5] = 1.0 / 120.0;
+    }
+  }
+}
+
+static double binom_d(int n, int k) {
+  double r = 1.0;
+  for (int i = 1; i <= k; ++i) r = r * (double)(n - k + i) / (double)i;
+  return r;
+}
+
+void orc_quads_coeffs(int order, double *coef) {
+  const double xi = orc_quads_xi(order);
+  const int nu = order / 2;
+  for (int k = 0; k < order; ++k) {
+    const int off = 1 - nu + k;
+    double *c = coef + k * order;
+    if (off >= 1) {
+      quads_base(off, xi, order, c);
+    } else {
+      double b[6];
+      quads_base(1 - off, xi, order, b);
+      for (int j = 0; j < order; ++j) {
+        double s = 0.0;
+        for (int p = j; p < order; ++p) s += b[p] * binom_d(p, j);
+        c[j] = ((j & 1) ? -1.0 : 1.0) * s;
+      }
+    }
+  }
+}
+
+void orc_quads_weights(int order, double t, double *w) {
+  double coef[36];
+  orc_quads_coeffs(order, coef);
+  for (int k = 0; k < order; ++k) {
+    double v = 0.0, tp = 1.0;
+    for (int p = 0; p < order; ++p) { v += coef[k * order + p] * tp; tp *= t; }
+    w[k] = v;
+  }
+}
+
+/* |W_1(m)|^2 of the separable QuadS window: quads_fft.py:119-165. */
+double orc_quads_influence_1d(int m, int n, int order) {
+  const double alpha = (2.0 * ORC_PI / (double)n) * (double)m;
+  double coef[36];
+  orc_quads_coeffs(order, coef);
+  const int deg = order;
+  /* I_p(alpha) = int_0^1 t^p e^{i alpha t} dt */
+  double Ire[8], Iim[8];
+  if (fabs(alpha) < 1e-3) {
+    for (int p = 0; p < deg; ++p) {
+      double sre = 1.0 / (double)(p + 1), sim = 0.0;
+      double pre = 1.0, pim = 0.0, fact = 1.0;
+      for (int k = 1; k < 12; ++k) {
+        /* pw *= i*alpha */
+        const double nre = -pim * alpha, nim = pre * alpha;
+        pre = nre; pim = nim;
+        fact *= (double)k;
+        sre += pre / (fact * (double)(p + k + 1));
+        sim += pim / (fact * (double)(p + k + 1));
+      }
+      Ire[p] = sre; Iim[p] = sim;
+    }
+  } else {
+    const double ere = cos(alpha), eim = sin(alpha);
+    /* 1/(i a) = -i/a */
+    const double ire = 0.0, iim = -1.0 / alpha;
+    double are = ere - 1.0, aim = eim;
+    Ire[0] = are * ire - aim * iim; Iim[0] = are * iim + aim * ire;
+    for (int p = 1; p < deg; ++p) {
+      are = ere - (double)p * Ire[p - 1];
+      aim = eim - (double)p * Iim[p - 1];
+      Ire[p] = are * ire - aim * iim; Iim[p] = are * iim + aim * ire;
+    }
+  }
+  const int nu = order / 2;
+  double phre = 0.0, phim = 0.0;
+  for (int k = 0; k < order; ++k) {
+    const int off = 1 - nu + k;
+    double gre = 0.0, gim = 0.0;
+    for (int p = 0; p < deg; ++p) {
+      gre += coef[k * order + p] * Ire[p];
+      gim += coef[k * order + p] * Iim[p];
+    }
+    /* e^{i alpha off} * conj(g) */
+    const double cr = cos(alpha * (double)off), ci = sin(alpha * (double)off);
+    phre += cr * gre + ci * gim;
+    phim += ci * gre - cr * gim;
+  }
+  return phre * phre + phim * phim;
+}
+
+/* sinc(x)^(2p) table value and alias sum (lmp/sog.cpp:68-76, 1113-1176). */
+static double orc_sinc(double x) {
+  if (fabs(x) < 1e-14) return 1.0;
+  return sin(x) / x;
+}
+
+double orc_bspline_sinc2p(int mode, int n, int order, int j) {
+  const double arg = ORC_PI * (double)mode / (double)n + ORC_PI * (double)j;
+  return pow(orc_sinc(arg), (double)(2 * order));
+}
+
+double orc_bspline_sinc_sum(int mode, int n, int order, int alias_extent) {
+  double s = 0.0;
+  for (int j = -alias_extent; j <= alias_extent; ++j)
+    s += orc_bspline_sinc2p(mode, n, order, j);
+  return s;
+}
+
+/* ------------------------------------------------------------------------ */
+/* mixed-radix complex FFT (any 2,3,5-smooth length; generic small primes)   */
+/* ------------------------------------------------------------------------ */
+
+typedef struct { double re, im; } cplx;
+
+static int smallest_factor(int n) {
+  for (int p = 2; p * p <= n; ++p)
+    if (n % p == 0) return p;
+  return n;
+}
+
+/* out[k] = sum_j in[j*stride] * exp(sign*2*pi*i*j*k/n); recursive DIT. */
+static void fft_rec(const cplx *in, int stride, cplx *out, int n, int sign,
+                    cplx *scratch) {
+  if (n == 1) { out[0] = in[0]; return; }
+  const int p = smallest_factor(n);
+  const int m = n / p;
+  /* sub-transforms of the decimated sequences into scratch */
+  for (int r = 0; r < p; ++r)
+    fft_rec(in + r * stride, stride * p, scratch + r * m, m, sign, out);
+  /* combine: X[k + q*m] = sum_r W_n^{r(k+q m)} Y_r[k] */
+  for (int k = 0; k < m; ++k) {
+    for (int q = 0; q < p; ++q) {
+      const int kk = k + q * m;
+      double sre = 0.0, sim = 0.0;
+      for (int r = 0; r < p; ++r) {
+        const long e = ((long)r * (long)kk) % n;
+        const double ang = sign * 2.0 * ORC_PI * (double)e / (double)n;
+        const double c = cos(ang), s = sin(ang);
+        const cplx y = scratch[r * m + k];
+        sre += y.re * c - y.im * s;
+        sim += y.re * s + y.im * c;
+      }
+      out[kk].re = sre; out[kk].im = sim;
+    }
+  }
+}
+
+/* In-place 1-D transform of a strided line. */
+static void fft_line(cplx *base, long stride, int n, int sign, cplx *w1,
+                     cplx *w2, cplx *w3) {
+  for (int j = 0; j < n; ++j) w1[j] = base[(long)j * stride];
+  fft_rec(w1, 1, w2, n, sign, w3);
+  for (int j = 0; j < n; ++j) base[(long)j * stride] = w2[j];
+}
+
+/* Forward R2C over a [nz][ny][nx] real grid into [nz][ny][nx/2+1]. */
+static void orc_rfft3(const double *rho, cplx *out, int nx, int ny, int nz) {
+  const int nxh = nx / 2 + 1;
+  const int nmax = nx > ny ? (nx > nz ? nx : nz) : (ny > nz ? ny : nz);
+#pragma omp parallel
+  {
+    cplx *w1 = malloc(sizeof(cplx) * nmax), *w2 = malloc(sizeof(cplx) * nmax),
+         *w3 = malloc(sizeof(cplx) * nmax), *row = malloc(sizeof(cplx) * nmax);
+#pragma omp for schedule(static)
+    for (long zy = 0; zy < (long)nz * ny; ++zy) {
+      for (int x = 0; x < nx; ++x) { row[x].re = rho[zy * nx + x]; row[x].im = 0.0; }
+      fft_rec(row, 1, w2, nx, -1, w3);
+      for (int x = 0; x < nxh; ++x) out[zy * nxh + x] = w2[x];
+    }
+#pragma omp for schedule(static)
+    for (long zx = 0; zx < (long)nz * nxh; ++zx) {
+      const long z = zx / nxh, x = zx % nxh;
+      fft_line(out + z * ny * nxh + x, nxh, ny, -1, w1, w2, w3);
+    }
+#pragma omp for schedule(static)
+    for (long yx = 0; yx < (long)ny * nxh; ++yx)
+      fft_line(out + yx, (long)ny * nxh, nz, -1, w1, w2, w3);
+    free(w1); free(w2); free(w3); free(row);
+  }
+}
+
+/* Unnormalised inverse matching torch.fft.irfftn(X, s=(nz,ny,nx)) * N:
+ * C2C inverse over z and y, then C2R along x using Re() of the self-conjugate
+ * columns (the imaginary part of mx=0 and mx=nx/2 is ignored). */
+static void orc_irfft3(cplx *spec, double *out, int nx, int ny, int nz) {
+  const int nxh = nx / 2 + 1;
+  const int nmax = nx > ny ? (nx > nz ? nx : nz) : (ny > nz ? ny : nz);
+#pragma omp parallel
+  {
+    cplx *w1 = malloc(sizeof(cplx) * nmax), *w2 = malloc(sizeof(cplx) * nmax),
+         *w3 = malloc(sizeof(cplx) * nmax), *row = malloc(sizeof(cplx) * nmax);
+#pragma omp for schedule(static)
+    for (long yx = 0; yx < (long)ny * nxh; ++yx)
+      fft_line(spec + yx, (long)ny * nxh, nz, +1, w1, w2, w3);
+#pragma omp for schedule(static)
+    for (long zx = 0; zx < (long)nz * nxh; ++zx) {
+      const long z = zx / nxh, x = zx % nxh;
+      fft_line(spec + z * ny * nxh + x, nxh, ny, +1, w1, w2, w3);
+    }
+#pragma omp for schedule(static)
+    for (long zy = 0; zy < (long)nz * ny; ++zy) {
+      const cplx *h = spec + zy * nxh;
+      for (int x = 0; x < nxh; ++x) row[x] = h[x];
+      for (int m = 1; m < (nx + 1) / 2; ++m) { row[nx - m].re = h[m].re; row[nx - m].im = -h[m].im; }
+      fft_rec(row, 1, w2, nx, +1, w3);
+      for (int x = 0; x < nx; ++x) out[zy * nx + x] = w2[x].re;
+    }
+    free(w1); free(w2); free(w3); free(row);
+  }
+}
+
+/* exported for the FFT self-test against numpy */
+void orc_fft_c2c(const double *in_ri, double *out_ri, int n, int sign) {
+  cplx *a = malloc(sizeof(cplx) * n), *b = malloc(sizeof(cplx) * n),
+       *c = malloc(sizeof(cplx) * n);
+  memcpy(a, in_ri, sizeof(cplx) * n);
+  fft_rec(a, 1, b, n, sign, c);
+  memcpy(out_ri, b, sizeof(cplx) * n);
+  free(a); free(b); free(c);
+}
+void orc_rfftn(const double *rho, double *out_ri, int nx, int ny, int nz) {
+  orc_rfft3(rho, (cplx *)out_ri, nx, ny, nz);
+}
+void orc_irfftn_unnorm(double *spec_ri, double *out, int nx, int ny, int nz) {
+  orc_irfft3((cplx *)spec_ri, out, nx, ny, nz);
+}
+
+/* ------------------------------------------------------------------------ */
+/* mesh solve                                                                */
+/* ------------------------------------------------------------------------ */
+
+enum { ORC_BSPLINE = 0, ORC_QUADS = 1 };
+
+typedef struct {
+  int spline, order, nx, ny, nz, alias_extent;
+  int kconv;           /* 0: k = 2pi cell^-1 m (physical), 1: k = 2pi m cell^-1 */
+  int natoms;
+  const double *r;     /* [N,3] */
+  const double *q;     /* [N]   */
+  double cell[9];      /* rows = lattice vectors */
+  int M;
+  const double *amp, *bw2;
+  double k_sq_max, norm_factor, self_coeff;
+  int remove_self, want_force, want_pot, want_param_grad, want_virial;
+} orc_mesh_in;
+
+typedef struct {
+  double energy;     /* mesh energy incl. self terms, times norm (no k=0) */
+  double diag_sum;   /* sum_half w*Gself / (2V) */
+  double *forces;    /* [N,3] or NULL */
+  double *potential; /* [N]  dE/dq incl. self terms, or NULL */
+  double *grad_amp;  /* [M] or NULL */
+  double *grad_bw2;  /* [M] or NULL */
+  double virial[9];
+} orc_mesh_out;
+
+static void inv3(const double *c, double *ci, double *det_out) {
+  const double a = c[0], b = c[1], cc = c[2], d = c[3], e = c[4], f = c[5],
+               g = c[6], h = c[7], i = c[8];
+  const double A = e * i - f * h, B = -(d * i - f * g), C = d * h - e * g;
+  const double det = a * A + b * B + cc * C;
+  const double id = 1.0 / det;
+  ci[0] = A * id; ci[1] = -(b * i - cc * h) * id; ci[2] = (b * f - cc * e) * id;
+  ci[3] = B * id; ci[4] = (a * i - cc * g) * id;  ci[5] = -(a * f - cc * d) * id;
+  ci[6] = C * id; ci[7] = -(a * h - b * g) * id;  ci[8] = (a * e - b * d) * id;
+  *det_out = det;
+}
+
+static void atom_stencil(int spline, int order, const double *ci, const double *r,
+                         int nx, int ny, int nz, int *i0, double *wx, double *wy,
+                         double *wz) {
+  const int n3[3] = {nx, ny, nz};
+  double *ws[3] = {wx, wy, wz};
+  for (int a = 0; a < 3; ++a) {
+    double f = r[0] * ci[0 * 3 + a] + r[1] * ci[1 * 3 + a] + r[2] * ci[2 * 3 + a];
+    f = f - floor(f);                 /* torch.remainder(., 1.0) */
+    const double fx = f * (double)n3[a];
+    const double fl = floor(fx);
+    const double t = fx - fl;
+    int ib = (int)fl;
+    /* first stencil node = base + (1 - nu) for QuadS / base - (p-1)/2 */
+    const int first = (spline == ORC_QUADS) ? (1 - order / 2) : -((order - 1) / 2);
+    ib += first;
+    ib %= n3[a]; if (ib < 0) ib += n3[a];
+    i0[a] = ib;
+    if (spline == ORC_QUADS) orc_quads_weights(order, t, ws[a]);
+    else orc_bspline_weights(order, t, ws[a]);
+  }
+}
+
+/* Green-function factors at one half-spectrum mode.
+ * kv: k vector of the principal mode; returns kfac (bare kernel K(k^2)),
+ * gE (energy green), gF (force green), gS (self green), gV (virial green),
+ * kfacv (bare K_v), and per-Gaussian e_m*D factors for parameter gradients
+ * in em_d[M] (energy) and em_s[M] (self).  Returns 0 when the mode is masked.*/
+typedef struct {
+  int spline, order, alias_extent, nx, ny, nz, M, kconv;
+  const double *amp, *bw2;
+  double k_sq_max;
+  double ci[9];
+  double bound[3];    /* |a_alpha| * kmax / 2pi: alias pruning */
+  double *dx, *dy, *dz;   /* separable deconvolution per axis */
+  double *sx, *sy, *sz;   /* B-spline alias sums per axis */
+} green_ctx;
+
+/* Mode m -> Cartesian k.  kconv 0: k = 2pi cell^-1 m, the reciprocal vector
+ * for rows-are-lattice-vectors cells (as the direct path, gaussian.py:1040);
+ * kconv 1: k = 2pi m cell^-1, the form written in quads_fft.py:255-257, which
+ * equals the former only when cell^-1 is symmetric. */
+static void kvec(const green_ctx *g, double mx, double my, double mz, double *k) {
+  const double tp = 2.0 * ORC_PI;
+  for (int a = 0; a < 3; ++a) {
+    if (g->kconv)
+      k[a] = tp * (mx * g->ci[0 * 3 + a] + my * g->ci[1 * 3 + a] + mz * g->ci[2 * 3 + a]);
+    else
+      k[a] = tp * (mx * g->ci[a * 3 + 0] + my * g->ci[a * 3 + 1] + mz * g->ci[a * 3 + 2]);
+  }
+}
+
+static int green_at(const green_ctx *g, int mx, int my, int mz, int iy, int iz,
+                    double *kout, double *kfac, double *gE, double *gF,
+                    double *gS, double *gV, double *kfacv, double *emD,
+                    double *emS) {
+  double k[3];
+  kvec(g, mx, my, mz, k);
+  const double ksq = k[0] * k[0] + k[1] * k[1] + k[2] * k[2];
+  kout[0] = k[0]; kout[1] = k[1]; kout[2] = k[2];
+  if ((mx == 0 && my == 0 && mz == 0) || ksq > g->k_sq_max) return 0;
+  double K = 0.0, Kv = 0.0;
+  for (int m = 0; m < g->M; ++m) {
+    const double e = exp(-0.5 * g->bw2[m] * ksq);
+    K += g->amp[m] * e;
+    Kv += g->amp[m] * g->bw2[m] * e;
+  }
+  *kfac = K; *kfacv = Kv;
+  if (g->spline == ORC_QUADS) {
+    double infl = g->dx[mx] * g->dy[iy] * g->dz[iz];
+    if (infl < 1e-20) infl = 1e-20;           /* quads_fft.py:194 clamp */
+    const double D = 1.0 / infl;
+    *gE = K * D; *gF = K * D; *gS = K; *gV = Kv * D;
+    if (emD) for (int m = 0; m < g->M; ++m) {
+      const double e = exp(-0.5 * g->bw2[m] * ksq);
+      emD[m] = e * D; emS[m] = e;
+    }
+    return 1;
+  }
+  /* B-spline: sum over aliases q_j = k + 2pi (N*j) . cell_inv inside the
+   * k_max sphere (lmp/sog.cpp:1479-1578; the fast path is the j=0 term). */
+  const double denom_lin = g->sx[mx] * g->sy[iy] * g->sz[iz];
+  const double denom = denom_lin * denom_lin;
+  if (!(denom > 1e-20) || !isfinite(denom)) return 0;
+  const int E = g->alias_extent;
+  const int m3[3] = {mx, my, mz};
+  const int n3[3] = {g->nx, g->ny, g->nz};
+  int jlo[3], jhi[3];
+  for (int a = 0; a < 3; ++a) {
+    int lo = (int)ceil((-g->bound[a] - (double)m3[a]) / (double)n3[a]);
+    int hi = (int)floor((g->bound[a] - (double)m3[a]) / (double)n3[a]);
+    if (lo < -E) lo = -E;
+    if (hi > E) hi = E;
+    if (lo > 0) lo = 0;   /* principal is always inside */
+    if (hi < 0) hi = 0;
+    jlo[a] = lo; jhi[a] = hi;
+  }
+  double sum0 = 0.0, sum1 = 0.0, sumv = 0.0;
+  if (emD) for (int m = 0; m < g->M; ++m) { emD[m] = 0.0; emS[m] = 0.0; }
+  const double w0 = orc_bspline_sinc2p(mx, g->nx, g->order, 0) *
+                    orc_bspline_sinc2p(my, g->ny, g->order, 0) *
+                    orc_bspline_sinc2p(mz, g->nz, g->order, 0);
+  for (int jx = jlo[0]; jx <= jhi[0]; ++jx)
+    for (int jy = jlo[1]; jy <= jhi[1]; ++jy)
+      for (int jz = jlo[2]; jz <= jhi[2]; ++jz) {
+        double q[3];
+        kvec(g, mx + g->nx * jx, my + g->ny * jy, mz + g->nz * jz, q);
+        const double qsq = q[0] * q[0] + q[1] * q[1] + q[2] * q[2];
+        if (!(qsq > 0.0 && qsq <= g->k_sq_max)) continue;
+        double Kq = 0.0, Kvq = 0.0;
+        for (int m = 0; m < g->M; ++m) {
+          const double e = exp(-0.5 * g->bw2[m] * qsq);
+          Kq += g->amp[m] * e;
+          Kvq += g->amp[m] * g->bw2[m] * e;
+        }
+        const double wp = orc_bspline_sinc2p(mx, g->nx, g->order, jx) *
+                          orc_bspline_sinc2p(my, g->ny, g->order, jy) *
+                          orc_bspline_sinc2p(mz, g->nz, g->order, jz);
+        sum0 += Kq * wp;
+        sum1 += (k[0] * q[0] + k[1] * q[1] + k[2] * q[2]) * Kq * wp;
+        sumv += Kvq * wp;
+        if (emD) for (int m = 0; m < g->M; ++m) {
+          const double e = exp(-0.5 * g->bw2[m] * qsq);
+          emD[m] += e * wp / denom;
+          emS[m] += (w0 > 1e-20) ? e * wp / w0 : 0.0;
+        }
+      }
+  *gE = sum0 / denom;
+  *gF = sum1 / (ksq * denom);
+  *gS = (w0 > 1e-20) ? sum0 / w0 : 0.0;
+  *gV = sumv / denom;
+  return 1;
+}
+
+static void setup_green(green_ctx *g, const orc_mesh_in *in, const double *ci) {
+  g->spline = in->spline; g->order = in->order; g->alias_extent = in->alias_extent;
+  g->nx = in->nx; g->ny = in->ny; g->nz = in->nz; g->M = in->M;
+  g->amp = in->amp; g->bw2 = in->bw2; g->k_sq_max = in->k_sq_max;
+  g->kconv = in->kconv;
+  memcpy(g->ci, ci, sizeof(double) * 9);
+  const double kmax = sqrt(in->k_sq_max);
+  /* |m_a| <= |v_a| kmax / 2pi with v_a the lattice row (kconv 0) or the
+   * column of the cell (kconv 1): bounds the aliases inside the sphere. */
+  for (int a = 0; a < 3; ++a) {
+    double s = 0.0;
+    for (int b = 0; b < 3; ++b) {
+      const double v = in->kconv ? in->cell[3 * b + a] : in->cell[3 * a + b];
+      s += v * v;
+    }
+    g->bound[a] = sqrt(s) * kmax / (2.0 * ORC_PI) + 1e-9;
+  }
+  const int nxh = in->nx / 2 + 1;
+  g->dx = malloc(sizeof(double) * nxh);
+  g->dy = malloc(sizeof(double) * in->ny);
+  g->dz = malloc(sizeof(double) * in->nz);
+  g->sx = malloc(sizeof(double) * nxh);
+  g->sy = malloc(sizeof(double) * in->ny);
+  g->sz = malloc(sizeof(double) * in->nz);
+  for (int ix = 0; ix < nxh; ++ix) {
+    g->dx[ix] = (in->spline == ORC_QUADS) ? orc_quads_influence_1d(ix, in->nx, in->order) : 0.0;
+    g->sx[ix] = orc_bspline_sinc_sum(ix, in->nx, in->order, in->alias_extent);
+  }
+  for (int iy = 0; iy < in->ny; ++iy) {
+    const int my = iy <= in->ny / 2 ? iy : iy - in->ny;
+    g->dy[iy] = (in->spline == ORC_QUADS) ? orc_quads_influence_1d(my, in->ny, in->order) : 0.0;
+    g->sy[iy] = orc_bspline_sinc_sum(my, in->ny, in->order, in->alias_extent);
+  }
+  for (int iz = 0; iz < in->nz; ++iz) {
+    const int mz = iz <= in->nz / 2 ? iz : iz - in->nz;
+    g->dz[iz] = (in->spline == ORC_QUADS) ? orc_quads_influence_1d(mz, in->nz, in->order) : 0.0;
+    g->sz[iz] = orc_bspline_sinc_sum(mz, in->nz, in->order, in->alias_extent);
+  }
+}
+
+static void free_green(green_ctx *g) {
+  free(g->dx); free(g->dy); free(g->dz); free(g->sx); free(g->sy); free(g->sz);
+}
+
+int orc_mesh_solve(const orc_mesh_in *in, orc_mesh_out *out) {
+  const int nx = in->nx, ny = in->ny, nz = in->nz, p = in->order;
+  const int nxh = nx / 2 + 1;
+  const long ng = (long)nx * ny * nz, nh = (long)nz * ny * nxh;
+  const int M = in->M;
+  double ci[9], det;
+  inv3(in->cell, ci, &det);
+  const double vol = fabs(det);
+  const double N3 = (double)ng;
+  const double rho_scale = N3 / vol;
+
+  /* ---- spread (serial, input order, as lmp/sog.cpp:1977-2018) ---- */
+  double *rho = calloc(ng, sizeof(double));
+  for (int i = 0; i < in->natoms; ++i) {
+    int i0[3];
+    double wx[8], wy[8], wz[8];
+    atom_stencil(in->spline, p, ci, in->r + 3 * i, nx, ny, nz, i0, wx, wy, wz);
+    const double qs = rho_scale * in->q[i];
+    for (int c = 0; c < p; ++c) {
+      const int gz = (i0[2] + c) % nz;
+      for (int b = 0; b < p; ++b) {
+        const int gy = (i0[1] + b) % ny;
+        for (int a = 0; a < p; ++a) {
+          const int gx = (i0[0] + a) % nx;
+          rho[((long)gz * ny + gy) * nx + gx] += qs * wx[a] * wy[b] * wz[c];
+        }
+      }
+    }
+  }
+  cplx *rk = malloc(sizeof(cplx) * nh);
+  orc_rfft3(rho, rk, nx, ny, nz);
+  free(rho);
+
+  green_ctx g;
+  setup_green(&g, in, ci);
+  const int nf = in->want_force ? 3 : 0;
+  const int nfield = nf + (in->want_pot ? 1 : 0);
+  cplx *fields = nfield ? calloc(nh * nfield, sizeof(cplx)) : NULL;
+  const double s2 = 1.0 / (N3 * N3);
+
+  /* per-z-plane partial sums, combined serially: deterministic */
+  const int nacc = 2 + 4 * M + 13;
+  double *part = calloc((size_t)nz * nacc, sizeof(double));
+#pragma omp parallel for schedule(static)
+  for (int iz = 0; iz < nz; ++iz) {
+    double *acc = part + (size_t)iz * nacc;
+    double emD[64], emS[64];
+    const int mz = iz <= nz / 2 ? iz : iz - nz;
+    for (int iy = 0; iy < ny; ++iy) {
+      const int my = iy <= ny / 2 ? iy : iy - ny;
+      for (int mx = 0; mx < nxh; ++mx) {
+        const long idx = ((long)iz * ny + iy) * nxh + mx;
+        double k[3], K = 0, gE = 0, gF = 0, gS = 0, gV = 0, Kv = 0;
+        const int live = green_at(&g, mx, my, mz, iy, iz, k, &K, &gE, &gF, &gS, &gV,
+                                  &Kv, in->want_param_grad ? emD : NULL, emS);
+        if (!live) continue;
+        const double w = (mx == 0 || (nx % 2 == 0 && mx == nx / 2)) ? 1.0 : 2.0;
+        const cplx r = rk[idx];
+        const double r2 = r.re * r.re + r.im * r.im;
+        acc[0] += w * gE * r2;
+        acc[1] += w * gS;
+        if (in->want_param_grad) {
+          const double ksq = k[0] * k[0] + k[1] * k[1] + k[2] * k[2];
+          for (int m = 0; m < M; ++m) {
+            acc[2 + m] += w * emD[m] * r2;
+            acc[2 + M + m] += w * emS[m];
+            acc[2 + 2 * M + m] += w * (-0.5 * ksq) * in->amp[m] * emD[m] * r2;
+            acc[2 + 3 * M + m] += w * (-0.5 * ksq) * in->amp[m] * emS[m];
+          }
+        }
+        if (in->want_virial) {
+          double *v = acc + 2 + 4 * M;
+          const double kk[6] = {k[0] * k[0], k[1] * k[1], k[2] * k[2],
+                                k[0] * k[1], k[0] * k[2], k[1] * k[2]};
+          v[0] += w * r2 * gE;
+          for (int c = 0; c < 6; ++c) v[1 + c] += w * r2 * gV * kk[c];
+          for (int c = 0; c < 6; ++c) v[7 + c] += w * Kv * kk[c];
+        }
+        if (nfield) {
+          const double sre = gF * r.re / N3, sim = gF * r.im / N3;
+          if (in->want_force) {
+            for (int a = 0; a < 3; ++a) {
+              fields[a * nh + idx].re = -k[a] * sim;
+              fields[a * nh + idx].im = k[a] * sre;
+            }
+          }
+          if (in->want_pot) {
+            fields[nf * nh + idx].re = gE * r.re / N3;
+            fields[nf * nh + idx].im = gE * r.im / N3;
+          }
+        }
+      }
+    }
+  }
+  double acc[2 + 4 * 64 + 13];
+  memset(acc, 0, sizeof(double) * nacc);
+  for (int iz = 0; iz < nz; ++iz)
+    for (int c = 0; c < nacc; ++c) acc[c] += part[(size_t)iz * nacc + c];
+  free(part);
+  free(rk);
+
+  double qsq = 0.0;
+  for (int i = 0; i < in->natoms; ++i) qsq += in->q[i] * in->q[i];
+  const double diag = acc[1] / (2.0 * vol);
+  double e = 0.5 * vol * s2 * acc[0];
+  if (in->remove_self) e -= qsq * diag;
+  if (in->self_coeff != 0.0) e -= qsq * in->self_coeff;
+  out->energy = e * in->norm_factor;
+  out->diag_sum = diag;
+
+  if (in->want_param_grad) {
+    for (int m = 0; m < M; ++m) {
+      double ga = 0.5 * vol * s2 * acc[2 + m];
+      double gb = 0.5 * vol * s2 * acc[2 + 2 * M + m];
+      if (in->remove_self) {
+        ga -= qsq * acc[2 + M + m] / (2.0 * vol);
+        gb -= qsq * acc[2 + 3 * M + m] / (2.0 * vol);
+      }
+      if (out->grad_amp) out->grad_amp[m] = ga * in->norm_factor;
+      if (out->grad_bw2) out->grad_bw2[m] = gb * in->norm_factor;
+    }
+  }
+  if (in->want_virial) {
+    const double *v = acc + 2 + 4 * M;
+    const double pref = in->norm_factor * 0.5 * vol * s2;
+    const int comp[3][3] = {{0, 3, 4}, {3, 1, 5}, {4, 5, 2}};
+    for (int a = 0; a < 3; ++a)
+      for (int b = 0; b < 3; ++b) {
+        double W = -pref * v[1 + comp[a][b]];
+        if (a == b) W += pref * v[0];
+        if (in->remove_self) {
+          const double pv = qsq * in->norm_factor / (2.0 * vol);
+          W += pv * v[7 + comp[a][b]];
+          if (a == b) W -= qsq * in->norm_factor * diag;
+        }
+        out->virial[a * 3 + b] = W;
+      }
+  }
+
+  if (nfield) {
+    double *grids = malloc(sizeof(double) * ng * nfield);
+    for (int f = 0; f < nfield; ++f) orc_irfft3(fields + f * nh, grids + f * ng, nx, ny, nz);
+    free(fields);
+#pragma omp parallel for schedule(static)
+    for (int i = 0; i < in->natoms; ++i) {
+      int i0[3];
+      double wx[8], wy[8], wz[8];
+      atom_stencil(in->spline, p, ci, in->r + 3 * i, nx, ny, nz, i0, wx, wy, wz);
+      double accf[4] = {0, 0, 0, 0};
+      for (int c = 0; c < p; ++c) {
+        const int gz = (i0[2] + c) % nz;
+        for (int b = 0; b < p; ++b) {
+          const int gy = (i0[1] + b) % ny;
+          for (int a = 0; a < p; ++a) {
+            const int gx = (i0[0] + a) % nx;
+            const long idx = ((long)gz * ny + gy) * nx + gx;
+            const double w = wx[a] * wy[b] * wz[c];
+            for (int f = 0; f < nfield; ++f) accf[f] += w * grids[f * ng + idx];
+          }
+        }
+      }
+      if (in->want_force)
+        for (int a = 0; a < 3; ++a)
+          out->forces[3 * i + a] = -in->q[i] * accf[a] * in->norm_factor;
+      if (in->want_pot) {
+        double v = accf[nf];
+        if (in->remove_self) v -= 2.0 * in->q[i] * diag;
+        if (in->self_coeff != 0.0) v -= 2.0 * in->q[i] * in->self_coeff;
+        out->potential[i] = v * in->norm_factor;
+      }
+    }
+    free(grids);
+  }
+  free_green(&g);
+  return 0;
+}
+
+/* ------------------------------------------------------------------------ */
+/* direct k-sum (gaussian.py:906-1081, 1281-1337), explicit derivatives      */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+  int natoms;
+  const double *r, *q;
+  double cell[9];
+  int nk[3];
+  int M;
+  const double *amp, *bw2;
+  double k_sq_max, norm_factor, self_coeff;
+  int remove_self;
+} orc_direct_in;
+
+typedef struct {
+  double energy, diag_sum;
+  int nmodes_half;
+  double *forces, *potential, *grad_amp, *grad_bw2;
+} orc_direct_out;
+
+int orc_direct_solve(const orc_direct_in *in, orc_direct_out *out) {
+  double ci[9], det;
+  inv3(in->cell, ci, &det);
+  const double vol = fabs(det);
+  const int N = in->natoms, M = in->M;
+  const double tp = 2.0 * ORC_PI;
+  double e_rec = 0.0, ksum = 0.0;
+  double *ga = calloc(M, sizeof(double)), *gb = calloc(M, sizeof(double));
+  double *ga_s = calloc(M, sizeof(double)), *gb_s = calloc(M, sizeof(double));
+  double *fr = calloc((size_t)N * 3, sizeof(double)), *pot = calloc(N, sizeof(double));
+  double *cs = malloc(sizeof(double) * N), *sn = malloc(sizeof(double) * N);
+  int nmodes = 0;
+  for (int n0 = 0; n0 <= in->nk[0]; ++n0)
+    for (int n1 = -in->nk[1]; n1 <= in->nk[1]; ++n1)
+      for (int n2 = -in->nk[2]; n2 <= in->nk[2]; ++n2) {
+        /* half space: n0>0 | n0==0&n1>0 | n0==n1==0&n2>0 (gaussian.py:1318-1322
+         * applies the same rule to the Cartesian k; for a right-handed cell the
+         * pairing (k,-k) is the same set). */
+        if (!(n0 > 0 || (n0 == 0 && n1 > 0) || (n0 == 0 && n1 == 0 && n2 > 0))) continue;
+        double k[3];
+        for (int a = 0; a < 3; ++a)
+          k[a] = tp * (ci[a * 3 + 0] * n0 + ci[a * 3 + 1] * n1 + ci[a * 3 + 2] * n2);
+        const double ksq = k[0] * k[0] + k[1] * k[1] + k[2] * k[2];
+        if (ksq > in->k_sq_max) continue;
+        ++nmodes;
+        double K = 0.0;
+        for (int m = 0; m < M; ++m) K += in->amp[m] * exp(-0.5 * in->bw2[m] * ksq);
+        double sr = 0.0, si = 0.0;
+        for (int i = 0; i < N; ++i) {
+          const double kr = in->r[3 * i] * k[0] + in->r[3 * i + 1] * k[1] + in->r[3 * i + 2] * k[2];
+          cs[i] = cos(kr); sn[i] = sin(kr);
+          sr += in->q[i] * cs[i]; si += in->q[i] * sn[i];
+        }
+        const double s2 = sr * sr + si * si;
+        e_rec += K * s2;
+        ksum += K;
+        for (int m = 0; m < M; ++m) {
+          const double e = exp(-0.5 * in->bw2[m] * ksq);
+          ga[m] += e * s2; ga_s[m] += e;
+          gb[m] += -0.5 * ksq * in->amp[m] * e * s2;
+          gb_s[m] += -0.5 * ksq * in->amp[m] * e;
+        }
+        for (int i = 0; i < N; ++i) {
+          const double t = 2.0 * K * in->q[i] * (si * cs[i] - sr * sn[i]);
+          fr[3 * i] += t * k[0]; fr[3 * i + 1] += t * k[1]; fr[3 * i + 2] += t * k[2];
+          pot[i] += 2.0 * K * (sr * cs[i] + si * sn[i]);
+        }
+      }
+  /* full sphere = 2 * half sphere; E = (1/2V) sum_full K |S|^2 */
+  double qsq = 0.0;
+  for (int i = 0; i < N; ++i) qsq += in->q[i] * in->q[i];
+  const double diag = 2.0 * ksum / (2.0 * vol);
+  double e = 2.0 * e_rec / (2.0 * vol);
+  if (in->remove_self) e -= qsq * diag;
+  if (in->self_coeff != 0.0) e -= qsq * in->self_coeff;
+  out->energy = e * in->norm_factor;
+  out->diag_sum = diag;
+  out->nmodes_half = nmodes;
+  for (int i = 0; i < N; ++i) {
+    if (out->forces)
+      for (int a = 0; a < 3; ++a) out->forces[3 * i + a] = -in->norm_factor * fr[3 * i + a] / vol;
+    if (out->potential) {
+      double v = pot[i] / vol;
+      if (in->remove_self) v -= 2.0 * in->q[i] * diag;
+      if (in->self_coeff != 0.0) v -= 2.0 * in->q[i] * in->self_coeff;
+      out->potential[i] = v * in->norm_factor;
+    }
+  }
+  for (int m = 0; m < M; ++m) {
+    double a = ga[m] / vol, b = gb[m] / vol;
+    if (in->remove_self) { a -= qsq * ga_s[m] / vol; b -= qsq * gb_s[m] / vol; }
+    if (out->grad_amp) out->grad_amp[m] = a * in->norm_factor;
+    if (out->grad_bw2) out->grad_bw2[m] = b * in->norm_factor;
+  }
+  free(ga); free(gb); free(ga_s); free(gb_s); free(fr); free(pot); free(cs); free(sn);
+  return 0;
+}
+
+int orc_num_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
