@@ -1,0 +1,139 @@
+"""The oracle itself, pinned: golden fixtures from the reference and the
+reference's own compiled spline header (oracle/_ref)."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests._cases import DIRECT_CASES, MESH_CASES, direct_n_dl, direct_nk, grid_ndl, load
+
+
+@pytest.mark.parametrize("name", MESH_CASES)
+def test_oracle_quads_matches_reference(name):
+    c = load(name)
+    cells = c["cell"].reshape(-1, 3, 3)
+    grids, ksm = zip(*[grid_ndl(cl, float(c["n_dl"])) for cl in cells])
+    lam = None if c["lam"] < 0 else float(c["lam"])
+    res = O.bundle(c["r"], c["q"], cells, c["batch"], c["amp"], c["bw2"], solver="mesh",
+                   grids=grids, k_sq_max=ksm, spline=O.QUADS, order=int(c["order"]),
+                   remove_self=bool(c["remove_self"]), charge_neutral_lambda=lam,
+                   want_virial=True, kconv=1)
+    e_ref = c["energy"]
+    assert np.allclose(res["energy"], e_ref, rtol=1e-12, atol=1e-13 * np.abs(e_ref).max())
+    assert np.abs(res["forces"] - c["forces"]).max() < 1e-11
+    assert np.abs(res["virial"] - c["virial"]).max() < 1e-11 * max(1.0, np.abs(c["virial"]).max())
+    w = c["grad_weights"][c["batch"]]
+    q = c["q"] if c["q"].ndim == 2 else c["q"][:, None]
+    gq = (res["potential"] * w[:, None]).reshape(q.shape)
+    assert np.abs(gq - c["grad_q"].reshape(q.shape)).max() < 1e-11
+    ga = (res["grad_amp"] * c["grad_weights"][:, None]).sum(0)
+    gb = (res["grad_bw2"] * c["grad_weights"][:, None]).sum(0)
+    assert np.allclose(ga, c["grad_amp"], rtol=1e-10, atol=1e-12)
+    assert np.allclose(gb, c["grad_bw2"], rtol=1e-10, atol=1e-12)
+
+
+@pytest.mark.parametrize("name", DIRECT_CASES)
+def test_oracle_direct_matches_reference(name):
+    c = load(name)
+    cells = c["cell"].reshape(-1, 3, 3)
+    n_dl = direct_n_dl(c)
+    nks = [direct_nk(cl, n_dl) for cl in cells]
+    ksm = [(2.0 * np.pi / n_dl) ** 2] * len(cells)
+    lam = None if c["lam"] < 0 else float(c["lam"])
+    res = O.bundle(c["r"], c["q"], cells, c["batch"], c["amp"], c["bw2"], solver="direct",
+                   nks=nks, k_sq_max=ksm, remove_self=bool(c["remove_self"]),
+                   self_coeff=float(c["self_coeff"]), charge_neutral_lambda=lam)
+    e_ref = c["energy"]
+    assert np.allclose(res["energy"], e_ref, rtol=1e-12, atol=1e-13 * np.abs(e_ref).max())
+    w = c["grad_weights"][c["batch"]]
+    assert np.abs(res["forces"] * w[:, None] - c["forces"]).max() < 1e-11
+    q = c["q"] if c["q"].ndim == 2 else c["q"][:, None]
+    gq = res["potential"] * w[:, None]
+    assert np.abs(gq - c["grad_q"].reshape(q.shape)).max() < 1e-11
+    if "grad_amp" in c:
+        ga = (res["grad_amp"] * c["grad_weights"][:, None]).sum(0)
+        gb = (res["grad_bw2"] * c["grad_weights"][:, None]).sum(0)
+        # reference parameters live in fp32 when created by default (gaussian.py:162-171)
+        tol = 1e-5 if "float32" in str(c["amp_dtype"]) else 1e-10
+        assert np.allclose(ga, c["grad_amp"], rtol=tol, atol=tol * np.abs(ga).max())
+        assert np.allclose(gb, c["grad_bw2"], rtol=tol, atol=tol * np.abs(gb).max())
+
+
+@pytest.mark.parametrize("order", [4, 5, 6])
+def test_bspline_weights_match_reference_header(order):
+    ref = O.ref_lib()
+    if ref is None:
+        pytest.skip("oracle/_ref not built (reference tree absent when building)")
+    import ctypes
+    rng = np.random.default_rng(order)
+    for t in np.concatenate([[0.0, 0.5, 1.0 - 1e-16], rng.random(50)]):
+        w = O.bspline_weights(order, float(t))
+        wr = np.zeros(order)
+        ref.ref_bspline_weights(order, ctypes.c_double(t), wr.ctypes.data_as(ctypes.POINTER(ctypes.c_double)))
+        assert np.array_equal(w, wr)
+        assert abs(w.sum() - 1.0) < 1e-14
+
+
+@pytest.mark.parametrize("order", [4, 6])
+def test_quads_weights_and_influence_match_reference_header(order):
+    ref = O.ref_lib()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    import ctypes
+    rng = np.random.default_rng(order)
+    for t in rng.random(50):
+        w = O.quads_weights(order, float(t))
+        wr = np.zeros(order)
+        ref.ref_quads_weights(order, ctypes.c_double(t), wr.ctypes.data_as(ctypes.POINTER(ctypes.c_double)))
+        assert np.allclose(w, wr, rtol=0, atol=1e-15)
+    for n in (8, 25, 64, 100):
+        for m in range(-(n // 2), n // 2 + 1):
+            assert abs(O.quads_influence_1d(m, n, order) - ref.ref_quads_influence_1d(m, n, order)) < 1e-14
+
+
+@pytest.mark.parametrize("order", [4, 5, 6])
+def test_bspline_moments(order):
+    """Partition of unity and vanishing odd moments about the particle
+    (cardinal B-splines reproduce polynomials of degree 1 exactly)."""
+    first = -((order - 1) // 2)
+    for t in np.linspace(0.0, 1.0, 11, endpoint=False):
+        w = O.bspline_weights(order, float(t))
+        offs = first + np.arange(order)
+        assert abs(w.sum() - 1.0) < 1e-14
+        # center of mass of the stencil = particle position (even order)
+        if order % 2 == 0:
+            assert abs((w * (offs - t)).sum()) < 1e-13
+
+
+def test_oracle_fft_matches_numpy():
+    rng = np.random.default_rng(0)
+    for n in (8, 12, 25, 27, 45, 64, 75, 100, 108):
+        x = rng.standard_normal(n) + 1j * rng.standard_normal(n)
+        out = np.zeros(2 * n)
+        inp = np.ascontiguousarray(np.stack([x.real, x.imag], 1).reshape(-1))
+        import ctypes
+        P = ctypes.POINTER(ctypes.c_double)
+        O.lib().orc_fft_c2c(inp.ctypes.data_as(P), out.ctypes.data_as(P), n, -1)
+        y = out[0::2] + 1j * out[1::2]
+        assert np.abs(y - np.fft.fft(x)).max() < 1e-12 * n
+
+
+def test_bspline_mesh_converges_to_direct():
+    """The B-spline mesh energy approaches the direct k-sum as the spline order
+    rises (discretisation check; no executable reference for the B-spline)."""
+    rng = np.random.default_rng(5)
+    L, n = 12.0, 50
+    r = rng.random((n, 3)) * L
+    q = rng.random(n) - 0.5
+    q -= q.mean()
+    bw = np.array([1.5, 2.5, 4.0])
+    amp = 1.0 / (bw * np.sqrt(2 * np.pi)) * bw * bw
+    cell = np.eye(3) * L
+    (nx, ny, nz), ksm = grid_ndl(cell, 0.7)
+    d = O.direct_solve(r, q, cell, amp, bw * bw, nk=direct_nk(cell, 0.7), k_sq_max=ksm)
+    errs = []
+    for order in (4, 6):
+        m = O.mesh_solve(r, q, cell, amp, bw * bw, spline=O.BSPLINE, order=order, nx=nx, ny=ny,
+                         nz=nz, k_sq_max=ksm)
+        errs.append(abs(m["energy"] - d["energy"]) / abs(d["energy"]))
+        assert np.abs(m["forces"] - d["forces"]).max() < 1e-3
+    assert errs[1] < errs[0] < 1e-3
