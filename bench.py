@@ -1,0 +1,400 @@
+"""Benchmark: atom-evaluations per second (energy + forces) of the SOG mesh solver.
+
+Workload (default, the large single system): 1,048,576 atoms uniform in a
+cubic 220 A cell, neutral N(0, 0.6) charges, 12 Gaussians with bandwidths
+log-spaced 1.2-60 A and raw amplitudes 1/(bw sqrt(2 pi)), n_dl = 0.86 -> 512^3
+mesh, cardinal B-spline order 6, float64.  Synthetic, seeded (seed 0 + rank).
+
+One step = one energy + explicit-force evaluation of the whole system.
+  value   device throughput, inputs resident in HBM (CUDA events, max over ranks)
+  e2e     the same through the public API (sog_b200.Sog) with pinned host
+          inputs copied in and energy + forces copied out every step
+With N > 1 ranks (torchrun) every rank solves its own independent system
+(frame-parallel data parallelism, no collective on the data path): weak scaling.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sog_b200|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "atom-evals/sec (E+F)"
+UNIT = "atom-evals/s"
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def workload(name: str):
+    if name == "cfg5":
+        return dict(workload="large single system: 1,048,576 atoms, 220 A cubic, 512^3 mesh, "
+                             "B-spline order 6, 12 Gaussians bw 1.2-60 A", natoms=1 << 20, L=220.0,
+                    n_dl=0.86, order=6, m=12, bw_lo=1.2, bw_hi=60.0, qstd=0.6)
+    if name == "cfg5_eighth":
+        return dict(workload="1/8-scale large system: 131,072 atoms, 110 A cubic, 256^3 mesh, "
+                             "B-spline order 6, 12 Gaussians bw 1.2-60 A", natoms=1 << 17, L=110.0,
+                    n_dl=0.86, order=6, m=12, bw_lo=1.2, bw_hi=60.0, qstd=0.6)
+    if name == "cfg2":
+        return dict(workload="water-like box: 3,000 atoms, 31 A cubic, 64^3 mesh, B-spline order 6, "
+                             "12 Gaussians bw 1.2*1.62^m", natoms=3000, L=31.0, n_dl=1.0, order=6,
+                    m=12, bw_geom=(1.2, 1.62), qstd=None)
+    raise SystemExit(f"unknown config {name}")
+
+
+def make_inputs(cfg, seed: int):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    n, L = cfg["natoms"], cfg["L"]
+    r = rng.random((n, 3)) * L
+    if cfg.get("qstd"):
+        q = rng.standard_normal(n) * cfg["qstd"]
+    else:
+        q = np.where(np.arange(n) % 3 == 0, -0.8, 0.4) + 0.05 * rng.standard_normal(n)
+    q -= q.mean()
+    if "bw_geom" in cfg:
+        b0, f = cfg["bw_geom"]
+        bw = b0 * f ** np.arange(cfg["m"])
+    else:
+        bw = np.logspace(math.log10(cfg["bw_lo"]), math.log10(cfg["bw_hi"]), cfg["m"])
+    amp_raw = 1.0 / (bw * math.sqrt(2.0 * math.pi))
+    cell = np.eye(3) * L
+    return r, q, cell, amp_raw, bw
+
+
+def mesh_dims(cfg):
+    nk = int(math.floor(cfg["L"] / cfg["n_dl"]))
+    n = 2 * nk + 1
+    while True:
+        m = n
+        for p in (2, 3, 5):
+            while m % p == 0:
+                m //= p
+        if m == 1:
+            return n
+        n += 1
+
+
+def algorithmic_bytes(cfg, s: int = 8, nfield: int = 3):
+    """Minimal-pipeline bytes per evaluation (each array once per producer /
+    consumer pass) and per kernel launch."""
+    n = mesh_dims(cfg)
+    N = cfg["natoms"]
+    ng = n ** 3
+    nh = n * n * (n // 2 + 1)
+    per_kernel = {
+        "spread": s * ng + 4 * s * N,
+        "fft_r2c_x": s * ng + 2 * s * nh,
+        "fft_y_fwd": 4 * s * nh,
+        "fft_z_fwd": 4 * s * nh,
+        "kspace": 2 * s * nh + nfield * 2 * s * nh,
+        "fft_z_inv": nfield * 4 * s * nh,
+        "fft_y_inv": nfield * 4 * s * nh,
+        "fft_c2r_x": nfield * (2 * s * nh + s * ng),
+        "gather": nfield * s * ng + 4 * s * N + 3 * s * N,
+    }
+    b_ef = 7 * s * N + 8 * s * ng + 16 * s * nh
+    return b_ef, per_kernel
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle timing (cpu_baseline and the reference arm)
+# ---------------------------------------------------------------------------
+def oracle_eval_time(cfg_name: str, reps: int, warm: int = 1):
+    import numpy as np
+    from oracle import oracle as O
+    cfg = workload(cfg_name)
+    r, q, cell, amp_raw, bw = make_inputs(cfg, 0)
+    n = mesh_dims(cfg)
+    amp = amp_raw * bw * bw
+    ksm = (2.0 * math.pi / cfg["n_dl"]) ** 2
+    times = []
+    for i in range(warm + reps):
+        t0 = time.perf_counter()
+        O.mesh_solve(r, q, cell, amp, bw * bw, spline=O.BSPLINE, order=cfg["order"], nx=n, ny=n,
+                     nz=n, k_sq_max=ksm, want_force=True)
+        dt = time.perf_counter() - t0
+        if i >= warm:
+            times.append(dt)
+    return cfg, times, O.num_threads()
+
+
+def run_reference(args, rank: int):
+    if rank != 0:
+        return
+    sample = "cfg5_eighth"
+    cfg, times, threads = oracle_eval_time(sample, reps=args.steps, warm=args.warmup)
+    t = statistics.median(times)
+    val = cfg["natoms"] / t
+    main_cfg = workload(args.config)
+    line = {
+        "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)",
+        "impl": "reference",
+        "config": {"workload": main_cfg["workload"], "sample": cfg["workload"]},
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{cfg['workload']}; one E+F evaluation per step by the C/OpenMP "
+                                   "oracle (the reference's B-spline mesh restated), median of steps"},
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_gpu(args, rank: int, world: int):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from sog_b200 import Sog, _lib
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = workload(args.config)
+    dt = torch.float64 if args.dtype == "f64" else torch.float32
+    r, q, cell, amp_raw, bw = make_inputs(cfg, seed=rank)
+    n = mesh_dims(cfg)
+    N = cfg["natoms"]
+    model = Sog({"use_atomwise": False, "use_bspline_fft": True, "bspline_order": cfg["order"],
+                 "n_dl": cfg["n_dl"], "amp": torch.tensor(amp_raw, dtype=dt),
+                 "bandwidth": torch.tensor(bw, dtype=dt), "trainable_kernel": False}).to(dev)
+    gauss = model.gaussian
+    r_d = torch.tensor(r, dtype=dt, device=dev)
+    q_d = torch.tensor(q, dtype=dt, device=dev)
+    cell_d = torch.tensor(cell[None], dtype=dt, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def step_device():
+        return gauss.compute_bundle(q=q_d, r=r_d, cell=cell_d, compute_force=True)
+
+    # warm-up
+    for _ in range(args.warmup):
+        step_device()
+    torch.cuda.synchronize()
+    plan = next(p for p in _lib.PLANS.plans.values() if p.key[4] == (n, n, n))
+
+    # ---- device-resident timed region ----
+    stream = torch.cuda.current_stream()
+    plan.set_timing(True)
+    clocks = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    l0 = _lib.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        out = step_device()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = _lib.launch_count() - l0
+    clk = clocks.stop()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    kt = plan.timings()
+    plan.set_timing(False)
+    ms_all = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_all, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_all.item())
+    energy0 = float(out["energy"][0])
+
+    # ---- end-to-end through the public API with host buffers ----
+    r_h = torch.tensor(r, dtype=dt).pin_memory()
+    q_h = torch.tensor(q, dtype=dt).pin_memory()
+    e_h = torch.empty(1, dtype=dt).pin_memory()
+    f_h = torch.empty(N, 3, dtype=dt).pin_memory()
+    r_in = torch.empty(N, 3, dtype=dt, device=dev)
+    q_in = torch.empty(N, dtype=dt, device=dev)
+
+    def step_e2e():
+        r_in.copy_(r_h, non_blocking=True)
+        q_in.copy_(q_h, non_blocking=True)
+        o = model(positions=r_in, cell=cell_d, latent_charges=q_in, compute_force=True)
+        e_h.copy_(o["E_lr"], non_blocking=True)
+        f_h.copy_(o["forces"], non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        step_e2e()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step_e2e()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
+    ms_e2e = float(ms_e2e.item())
+
+    if rank != 0:
+        return
+    # ---- roofline of the dominant kernel ----
+    s = 8 if dt == torch.float64 else 4
+    b_ef, per_kernel = algorithmic_bytes(cfg, s=s)
+    tot, cnt = {}, {}
+    for name, t in kt:
+        tot[name] = tot.get(name, 0.0) + t
+        cnt[name] = cnt.get(name, 0) + 1
+    kernels = {k: {"launches": cnt[k], "total_ms": tot[k], "avg_ms": tot[k] / cnt[k],
+                   "share": tot[k] / sum(tot.values())} for k in tot}
+    dom = max(tot, key=tot.get) if tot else None
+    peak, peak_kind = measured_peak()
+    roof = None
+    if dom is not None and dom in per_kernel:
+        ach = per_kernel[dom] / (kernels[dom]["avg_ms"] * 1e-3) / 1e9
+        roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                "frac": ach / peak, "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                "algorithmic_bytes_per_launch": per_kernel[dom]}
+    for k, v in kernels.items():
+        if k in per_kernel:
+            v["achieved_gbs"] = per_kernel[k] / (v["avg_ms"] * 1e-3) / 1e9
+    step_gbs = b_ef / (ms * 1e-3) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        ccfg, times, threads = oracle_eval_time("cfg5_eighth", reps=3, warm=1)
+        tmed = statistics.median(times)
+        cpu = {"value": ccfg["natoms"] / tmed, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{ccfg['workload']}; C/OpenMP oracle E+F, median of 3 after 1 warm-up, "
+                         f"{tmed:.2f} s per evaluation"}
+    line = {
+        "metric": METRIC, "value": world * N / (ms_max * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic (seeded)",
+        "config": {"workload": cfg["workload"], "atoms_per_gpu": N, "mesh": [n, n, n],
+                   "spline": f"bspline{cfg['order']}", "gaussians": cfg["m"],
+                   "parallelism": f"frame-dp{world}" if world > 1 else "single",
+                   "l2": "inputs and mesh arrays larger than L2 (>= 1 GB each)"},
+        "e2e": {"value": world * N / (ms_e2e * 1e-3), "unit": UNIT, "ms_per_step": ms_e2e,
+                "h2d_bytes_per_step": N * 4 * s, "d2h_bytes_per_step": s + N * 3 * s},
+        "roofline": roof,
+        "step_roofline": {"algorithmic_bytes": b_ef, "achieved": step_gbs, "peak": peak,
+                          "unit": "GB/s", "frac": step_gbs / peak},
+        "kernels": kernels,
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "cpu_baseline": cpu,
+        "energy_frame0": energy0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="sog_b200", choices=["sog_b200", "reference"])
+    ap.add_argument("--config", default="cfg5", choices=["cfg5", "cfg5_eighth", "cfg2"])
+    ap.add_argument("--dtype", default="f64", choices=["f64", "f32"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    try:
+        run_gpu(args, rank, world)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,171 @@
+/*
+ * sog_b200.h — C ABI of the B200 (sm_100a) SOG reciprocal-space solver.
+ *
+ * Plain C: pointers, sizes and integer status codes; no exceptions cross it
+ * and no framework types appear in it.  All device arrays are owned by the
+ * caller; a plan owns only its scratch (mesh buffers, FFT twiddles, atom-sort
+ * buffers).  Work is ordered on the CUDA stream passed in (as void*); no host
+ * synchronisation happens inside a forward call except a short wait before a
+ * plan reuses its pinned upload buffer.  One plan per stream at a time.
+ *
+ * Reference interfaces this ABI replaces (paths in the reference project):
+ *   - the mesh solve of Gaussian.compute_bundle: src/sog/module/gaussian.py:380-820,
+ *     quads_fft.py:209-326 (QuadS) and the B-spline mesh of lmp/sog.cpp:1795-2398;
+ *   - its hand-written backward: src/sog/module/cubes2_fft.py:746-869;
+ *   - the direct k-sum: src/sog/module/gaussian.py:1180-1337;
+ *   - the plugin GPU hooks sog_gpu_create / sog_gpu_setup / sog_gpu_compute
+ *     called at lmp/sog.cpp:1049-1053 and lmp/sog.cpp:1804-1836 (their
+ *     source, sog_gpu.cu, is not part of the reference).
+ */
+#ifndef SOG_B200_H
+#define SOG_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SOG_API __attribute__((visibility("default")))
+#else
+#define SOG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define SOG_OK 0
+#define SOG_ERR_INVALID 1     /* bad argument (sizes, orders, null pointers)  */
+#define SOG_ERR_CUDA 2        /* a CUDA runtime call failed                   */
+#define SOG_ERR_NOMEM 3       /* device or pinned allocation failed           */
+#define SOG_ERR_UNSUPPORTED 4 /* valid request this build does not implement  */
+#define SOG_ERR_DEVICE 5      /* a kernel raised a status bit (see plan status) */
+
+#define SOG_DTYPE_F64 0
+#define SOG_DTYPE_F32 1
+
+#define SOG_SPLINE_BSPLINE 0 /* cardinal B-spline, order 4/5/6 (lmp/sog.cpp:89-110) */
+#define SOG_SPLINE_QUADS 1   /* separable QuadS, order 4/6 (quads_spline.py)       */
+
+/* Mode -> wave vector.  PHYSICAL: k = 2*pi * cell^-1 * m, the reciprocal
+ * vector for cells whose rows are lattice vectors (what the reference's direct
+ * path uses, gaussian.py:1040).  REFERENCE: k = 2*pi * m * cell^-1 exactly as
+ * written in quads_fft.py:255-257; the two agree whenever cell^-1 is
+ * symmetric (orthorhombic cells). */
+#define SOG_KCONV_PHYSICAL 0
+#define SOG_KCONV_REFERENCE 1
+
+/* plan status bits (sog_plan_status) */
+#define SOG_STATUS_NONFINITE 1u /* a position or charge was NaN/Inf           */
+#define SOG_STATUS_BAD_CELL 2u  /* a cell had |det| <= eps                    */
+
+SOG_API const char *sog_strerror(int code);
+/* Text of the last failure on this thread (empty string if none). */
+SOG_API const char *sog_last_error(void);
+/* Library version string. */
+SOG_API const char *sog_version(void);
+/* Number of kernels this library has launched in the process so far. */
+SOG_API unsigned long long sog_launch_count(void);
+
+/* ------------------------------------------------------------------------ */
+/* Mesh (particle-mesh) solver                                               */
+/* ------------------------------------------------------------------------ */
+
+typedef struct sog_plan sog_plan;
+
+typedef struct sog_plan_desc {
+  int dtype;        /* SOG_DTYPE_F64 | SOG_DTYPE_F32                         */
+  int spline;       /* SOG_SPLINE_BSPLINE | SOG_SPLINE_QUADS                 */
+  int order;        /* 4,5,6 (B-spline) or 4,6 (QuadS)                       */
+  int nx, ny, nz;   /* mesh; layout [nz][ny][nx], x fastest (quads_fft.py:66) */
+  int device;       /* CUDA device ordinal                                   */
+  int alias_extent; /* B-spline alias half-width; 0 -> 8 (lmp/sog.cpp:339)   */
+  int kconv;        /* SOG_KCONV_*                                           */
+} sog_plan_desc;
+
+/* Creates a plan for one mesh shape.  Replaces the reference's per-call
+ * grid set-up (quads_fft.py:234-284) and the plugin's ensure_fft_plan /
+ * precompute_green_functions (lmp/sog.cpp:892-1096, 1324-1476). */
+SOG_API int sog_plan_create(sog_plan **out, const sog_plan_desc *desc);
+SOG_API int sog_plan_destroy(sog_plan *plan);
+/* Reads and clears the plan's device status bits (synchronises the device). */
+SOG_API int sog_plan_status(sog_plan *plan, unsigned *bits);
+/* Per-kernel timing: when on, each forward records a CUDA event on the
+ * caller's stream after every kernel.  sog_plan_timings waits for the last
+ * event, returns up to `cap` (kernel name, ms) pairs of all calls since the
+ * previous read (or since timing was switched on) and clears them. */
+SOG_API int sog_plan_set_timing(sog_plan *plan, int on);
+SOG_API int sog_plan_timings(sog_plan *plan, const char **names, float *ms, int cap, int *count);
+
+typedef struct sog_mesh_args {
+  /* Frames solved by this call (all on this plan's mesh).  Host arrays. */
+  int nframes;
+  const int64_t *atom_begin; /* [nframes] first atom of each frame            */
+  const int64_t *atom_count; /* [nframes] atoms of each frame                 */
+  const double *k_sq_max;    /* [nframes] mode cutoff (cubes2_fft.py:102-175) */
+  /* Device inputs in the plan's dtype. */
+  int nchannels;             /* C: independent charge channels               */
+  const void *positions;     /* [N,3] Cartesian                               */
+  const void *charges;       /* [N,C]                                         */
+  const void *cells;         /* [nframes,3,3], rows = lattice vectors         */
+  int n_gauss;               /* M                                             */
+  const void *amp;           /* [M] internal amplitudes (amp * bw^2 for raw)  */
+  const void *bw2;           /* [M] squared bandwidths                        */
+  double norm_factor;        /* 14.3996454784255 by default                   */
+  double self_coeff;         /* real-space self term (gaussian.py:210-214)     */
+  int remove_self;           /* subtract the mesh self energy                 */
+  int k0_correction;         /* add the k=0 term of gaussian.py:769-793       */
+  double charge_neutral_lambda; /* > 0 adds lambda*mean(q)^2 (gaussian.py:796) */
+  /* Device outputs in the plan's dtype; any may be NULL. */
+  void *energy;              /* [nframes]                                     */
+  void *forces;              /* [N,3] written for the atoms of these frames   */
+  void *potential;           /* [N,C] dE/dq                                   */
+  void *grad_amp;            /* [nframes,M] dE/damp                           */
+  void *grad_bw2;            /* [nframes,M] dE/dbw2                           */
+  void *virial;              /* [nframes,3,3] (cubes2_fft.py:874-921)          */
+} sog_mesh_args;
+
+/* Energy (+ ik forces, dE/dq, dE/d(amp,bw2), virial) of every frame of the
+ * call.  Channels are solved independently and summed per frame; the k=0
+ * term uses the frame's total charge over channels (gaussian.py:577-654,
+ * 769-798).  Replaces compute_quads_fft (quads_fft.py:209-326) and the
+ * backward of Cubes2FFTFunction (cubes2_fft.py:746-869). */
+SOG_API int sog_mesh_forward(sog_plan *plan, const sog_mesh_args *args, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Direct k-sum                                                              */
+/* ------------------------------------------------------------------------ */
+
+typedef struct sog_direct sog_direct;
+
+SOG_API int sog_direct_create(sog_direct **out, int dtype, int device);
+SOG_API int sog_direct_destroy(sog_direct *d);
+SOG_API int sog_direct_set_timing(sog_direct *d, int on);
+SOG_API int sog_direct_timings(sog_direct *d, const char **names, float *ms, int cap, int *count);
+
+typedef struct sog_direct_args {
+  int nframes;
+  const int64_t *atom_begin; /* host [nframes]                                 */
+  const int64_t *atom_count; /* host [nframes]                                 */
+  const int32_t *nk;         /* host [nframes,3] integer mode box half-widths  */
+  const double *k_sq_max;    /* host [nframes] (2*pi/n_dl)^2                   */
+  int nchannels;
+  const void *positions, *charges, *cells;
+  int n_gauss;
+  const void *amp, *bw2;
+  double norm_factor, self_coeff;
+  int remove_self, k0_correction;
+  double charge_neutral_lambda;
+  void *energy, *forces, *potential, *grad_amp, *grad_bw2;
+  void *virial;              /* [nframes,3,3] reciprocal virial, or NULL        */
+} sog_direct_args;
+
+/* E = (1/2V) sum_{k!=0,|k|<=kmax} K(k^2) |S(k)|^2 with explicit derivatives.
+ * Replaces _compute_periodic_direct / _compute_bundle_direct_batched
+ * (gaussian.py:1180-1337), whose forces the reference takes by autograd. */
+SOG_API int sog_direct_forward(sog_direct *d, const sog_direct_args *args, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SOG_B200_H */

@@ -214,38 +214,47 @@ static int smallest_factor(int n) {
   return n;
 }
 
-/* out[k] = sum_j in[j*stride] * exp(sign*2*pi*i*j*k/n); recursive DIT. */
-static void fft_rec(const cplx *in, int stride, cplx *out, int n, int sign,
+/* out[k] = sum_j in[j*stride] * exp(sign*2*pi*i*j*k/n); recursive DIT.
+ * W[j*ws] = exp(sign*2*pi*i*j/n) for j in [0, n) (a root table of a multiple
+ * of n read with stride ws). */
+static void fft_rec(const cplx *in, int stride, cplx *out, int n, const cplx *W, int ws,
                     cplx *scratch) {
   if (n == 1) { out[0] = in[0]; return; }
   const int p = smallest_factor(n);
   const int m = n / p;
-  /* sub-transforms of the decimated sequences into scratch */
   for (int r = 0; r < p; ++r)
-    fft_rec(in + r * stride, stride * p, scratch + r * m, m, sign, out);
-  /* combine: X[k + q*m] = sum_r W_n^{r(k+q m)} Y_r[k] */
+    fft_rec(in + r * stride, stride * p, scratch + r * m, m, W, ws * p, out);
   for (int k = 0; k < m; ++k) {
     for (int q = 0; q < p; ++q) {
       const int kk = k + q * m;
       double sre = 0.0, sim = 0.0;
       for (int r = 0; r < p; ++r) {
         const long e = ((long)r * (long)kk) % n;
-        const double ang = sign * 2.0 * ORC_PI * (double)e / (double)n;
-        const double c = cos(ang), s = sin(ang);
+        const cplx w = W[e * ws];
         const cplx y = scratch[r * m + k];
-        sre += y.re * c - y.im * s;
-        sim += y.re * s + y.im * c;
+        sre += y.re * w.re - y.im * w.im;
+        sim += y.re * w.im + y.im * w.re;
       }
       out[kk].re = sre; out[kk].im = sim;
     }
   }
 }
 
+static cplx *root_table(int n, int sign) {
+  cplx *W = malloc(sizeof(cplx) * n);
+  for (int j = 0; j < n; ++j) {
+    const long double a = (long double)sign * 2.0L * 3.141592653589793238462643383279502884L *
+                          (long double)j / (long double)n;
+    W[j].re = (double)cosl(a);
+    W[j].im = (double)sinl(a);
+  }
+  return W;
+}
+
 /* In-place 1-D transform of a strided line. */
-static void fft_line(cplx *base, long stride, int n, int sign, cplx *w1,
-                     cplx *w2, cplx *w3) {
+static void fft_line(cplx *base, long stride, int n, const cplx *W, cplx *w1, cplx *w2, cplx *w3) {
   for (int j = 0; j < n; ++j) w1[j] = base[(long)j * stride];
-  fft_rec(w1, 1, w2, n, sign, w3);
+  fft_rec(w1, 1, w2, n, W, 1, w3);
   for (int j = 0; j < n; ++j) base[(long)j * stride] = w2[j];
 }
 
@@ -253,6 +262,7 @@ static void fft_line(cplx *base, long stride, int n, int sign, cplx *w1,
 static void orc_rfft3(const double *rho, cplx *out, int nx, int ny, int nz) {
   const int nxh = nx / 2 + 1;
   const int nmax = nx > ny ? (nx > nz ? nx : nz) : (ny > nz ? ny : nz);
+  cplx *Wx = root_table(nx, -1), *Wy = root_table(ny, -1), *Wz = root_table(nz, -1);
 #pragma omp parallel
   {
     cplx *w1 = malloc(sizeof(cplx) * nmax), *w2 = malloc(sizeof(cplx) * nmax),
@@ -260,19 +270,20 @@ static void orc_rfft3(const double *rho, cplx *out, int nx, int ny, int nz) {
 #pragma omp for schedule(static)
     for (long zy = 0; zy < (long)nz * ny; ++zy) {
       for (int x = 0; x < nx; ++x) { row[x].re = rho[zy * nx + x]; row[x].im = 0.0; }
-      fft_rec(row, 1, w2, nx, -1, w3);
+      fft_rec(row, 1, w2, nx, Wx, 1, w3);
       for (int x = 0; x < nxh; ++x) out[zy * nxh + x] = w2[x];
     }
 #pragma omp for schedule(static)
     for (long zx = 0; zx < (long)nz * nxh; ++zx) {
       const long z = zx / nxh, x = zx % nxh;
-      fft_line(out + z * ny * nxh + x, nxh, ny, -1, w1, w2, w3);
+      fft_line(out + z * ny * nxh + x, nxh, ny, Wy, w1, w2, w3);
     }
 #pragma omp for schedule(static)
     for (long yx = 0; yx < (long)ny * nxh; ++yx)
-      fft_line(out + yx, (long)ny * nxh, nz, -1, w1, w2, w3);
+      fft_line(out + yx, (long)ny * nxh, nz, Wz, w1, w2, w3);
     free(w1); free(w2); free(w3); free(row);
   }
+  free(Wx); free(Wy); free(Wz);
 }
 
 /* Unnormalised inverse matching torch.fft.irfftn(X, s=(nz,ny,nx)) * N:
@@ -281,28 +292,30 @@ static void orc_rfft3(const double *rho, cplx *out, int nx, int ny, int nz) {
 static void orc_irfft3(cplx *spec, double *out, int nx, int ny, int nz) {
   const int nxh = nx / 2 + 1;
   const int nmax = nx > ny ? (nx > nz ? nx : nz) : (ny > nz ? ny : nz);
+  cplx *Wx = root_table(nx, +1), *Wy = root_table(ny, +1), *Wz = root_table(nz, +1);
 #pragma omp parallel
   {
     cplx *w1 = malloc(sizeof(cplx) * nmax), *w2 = malloc(sizeof(cplx) * nmax),
          *w3 = malloc(sizeof(cplx) * nmax), *row = malloc(sizeof(cplx) * nmax);
 #pragma omp for schedule(static)
     for (long yx = 0; yx < (long)ny * nxh; ++yx)
-      fft_line(spec + yx, (long)ny * nxh, nz, +1, w1, w2, w3);
+      fft_line(spec + yx, (long)ny * nxh, nz, Wz, w1, w2, w3);
 #pragma omp for schedule(static)
     for (long zx = 0; zx < (long)nz * nxh; ++zx) {
       const long z = zx / nxh, x = zx % nxh;
-      fft_line(spec + z * ny * nxh + x, nxh, ny, +1, w1, w2, w3);
+      fft_line(spec + z * ny * nxh + x, nxh, ny, Wy, w1, w2, w3);
     }
 #pragma omp for schedule(static)
     for (long zy = 0; zy < (long)nz * ny; ++zy) {
       const cplx *h = spec + zy * nxh;
       for (int x = 0; x < nxh; ++x) row[x] = h[x];
       for (int m = 1; m < (nx + 1) / 2; ++m) { row[nx - m].re = h[m].re; row[nx - m].im = -h[m].im; }
-      fft_rec(row, 1, w2, nx, +1, w3);
+      fft_rec(row, 1, w2, nx, Wx, 1, w3);
       for (int x = 0; x < nx; ++x) out[zy * nx + x] = w2[x].re;
     }
     free(w1); free(w2); free(w3); free(row);
   }
+  free(Wx); free(Wy); free(Wz);
 }
 
 /* exported for the FFT self-test against numpy */
@@ -310,7 +323,9 @@ void orc_fft_c2c(const double *in_ri, double *out_ri, int n, int sign) {
   cplx *a = malloc(sizeof(cplx) * n), *b = malloc(sizeof(cplx) * n),
        *c = malloc(sizeof(cplx) * n);
   memcpy(a, in_ri, sizeof(cplx) * n);
-  fft_rec(a, 1, b, n, sign, c);
+  cplx *W = root_table(n, sign);
+  fft_rec(a, 1, b, n, W, 1, c);
+  free(W);
   memcpy(out_ri, b, sizeof(cplx) * n);
   free(a); free(b); free(c);
 }

@@ -1,0 +1,422 @@
+// Direct k-sum (gaussian.py:906-1081, 1180-1337) with explicit derivatives.
+//   E = (1/2V) sum_{k != 0, |k| <= k_max} K(k^2) |S(k)|^2,  S(k) = sum_i q_i e^{i k.r_i}
+// over the half space of integer modes n (each standing for the pair +-n);
+// k = 2 pi cell^-1 n.  Forces, dE/dq, dE/d(amp, bw2) and the virial are
+// explicit sums, where the reference differentiates with autograd.
+//   k_direct_sfac   thread per mode: S(k) per channel, K(k), energy partials
+//   k_direct_extra  parameter-gradient / virial partials (optional)
+//   k_direct_atoms  thread per atom: forces and potential
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "frames.cuh"
+#include "plan.hpp"
+
+namespace sogb {
+namespace {
+
+constexpr int kMaxCh = 8;
+constexpr int kDirThreads = 256;
+
+struct DirArgs {
+  const FrameGeom *geom;
+  const int *nk;      // [nf][3]
+  int64_t kmax_modes; // stride of per-frame mode arrays
+  int nch, M;
+  double *kvec;       // [nf][K][4]: kx, ky, kz, K
+  double *sfac;       // [nf][C][K][2]
+  double *part;       // [C][nf][nblk][2]
+  double *partx;      // [C][nf][nblk][4M+13]
+  int nx_acc;
+};
+
+__device__ __forceinline__ bool decode_mode(int64_t t, const int *nk, int &n0, int &n1, int &n2) {
+  const int w2 = 2 * nk[2] + 1, w1 = 2 * nk[1] + 1;
+  n2 = (int)(t % w2) - nk[2];
+  t /= w2;
+  n1 = (int)(t % w1) - nk[1];
+  n0 = (int)(t / w1);
+  if (n0 > nk[0]) return false;
+  // half space: n0 > 0 | n0 == 0 & n1 > 0 | n0 == n1 == 0 & n2 > 0
+  return n0 > 0 || (n0 == 0 && (n1 > 0 || (n1 == 0 && n2 > 0)));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kDirThreads) k_direct_sfac(DirArgs a, const T *__restrict__ pos,
+                                                            const T *__restrict__ q,
+                                                            const T *__restrict__ amp,
+                                                            const T *__restrict__ bw2) {
+  __shared__ double s_r[kDirThreads][3];
+  __shared__ double s_q[kDirThreads][kMaxCh];
+  __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
+  __shared__ double red[2 * kMaxCh + 1][kDirThreads / 32];
+  for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
+    s_amp[m] = (double)amp[m];
+    s_bw2[m] = (double)bw2[m];
+  }
+  const int f = blockIdx.y;
+  const FrameGeom &g = a.geom[f];
+  const int *nk = a.nk + 3 * f;
+  const int64_t nbox = (int64_t)(nk[0] + 1) * (2 * nk[1] + 1) * (2 * nk[2] + 1);
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int n0 = 0, n1 = 0, n2 = 0;
+  bool live = t < nbox && decode_mode(t, nk, n0, n1, n2);
+  double k[3] = {0.0, 0.0, 0.0}, ksq = 0.0;
+  if (live) {
+    for (int c = 0; c < 3; ++c) k[c] = g.kmat[c * 3 + 0] * n0 + g.kmat[c * 3 + 1] * n1 + g.kmat[c * 3 + 2] * n2;
+    ksq = k[0] * k[0] + k[1] * k[1] + k[2] * k[2];
+    live = ksq <= g.k_sq_max;
+  }
+  __syncthreads();
+  double K = 0.0;
+  if (live)
+    for (int m = 0; m < a.M; ++m) K += s_amp[m] * exp(-0.5 * s_bw2[m] * ksq);
+  double sr[kMaxCh], si[kMaxCh];
+#pragma unroll
+  for (int c = 0; c < kMaxCh; ++c) { sr[c] = 0.0; si[c] = 0.0; }
+  for (int base = 0; base < g.natoms; base += kDirThreads) {
+    const int i = base + threadIdx.x;
+    __syncthreads();
+    if (i < g.natoms) {
+      const int64_t atom = g.atom_begin + i;
+      for (int c = 0; c < 3; ++c) s_r[threadIdx.x][c] = (double)pos[atom * 3 + c];
+      for (int c = 0; c < a.nch; ++c) s_q[threadIdx.x][c] = (double)q[atom * a.nch + c];
+    }
+    __syncthreads();
+    const int cnt = min(kDirThreads, g.natoms - base);
+    if (live) {
+      for (int j = 0; j < cnt; ++j) {
+        const double kr = k[0] * s_r[j][0] + k[1] * s_r[j][1] + k[2] * s_r[j][2];
+        double sn, cs;
+        sincos(kr, &sn, &cs);
+#pragma unroll
+        for (int c = 0; c < kMaxCh; ++c)
+          if (c < a.nch) { sr[c] += s_q[j][c] * cs; si[c] += s_q[j][c] * sn; }
+      }
+    }
+  }
+  if (t < nbox) {
+    double *kv = a.kvec + ((int64_t)f * a.kmax_modes + t) * 4;
+    kv[0] = k[0]; kv[1] = k[1]; kv[2] = k[2]; kv[3] = live ? K : 0.0;
+    for (int c = 0; c < a.nch; ++c) {
+      double *s = a.sfac + (((int64_t)f * a.nch + c) * a.kmax_modes + t) * 2;
+      s[0] = live ? sr[c] : 0.0;
+      s[1] = live ? si[c] : 0.0;
+    }
+  }
+  // energy partials per channel (2 K |S|^2) and the self sum (2 K)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c = 0; c < a.nch; ++c) {
+    const double v = warp_sum(live ? 2.0 * K * (sr[c] * sr[c] + si[c] * si[c]) : 0.0);
+    if (lane == 0) red[c][warp] = v;
+  }
+  const double dsum = warp_sum(live ? 2.0 * K : 0.0);
+  if (lane == 0) red[kMaxCh * 2][warp] = dsum;
+  __syncthreads();
+  if (threadIdx.x < a.nch) {
+    const int c = threadIdx.x;
+    double e = 0.0, d = 0.0;
+    for (int w = 0; w < kDirThreads / 32; ++w) { e += red[c][w]; d += red[kMaxCh * 2][w]; }
+    double *p = a.part + (((int64_t)c * gridDim.y + f) * gridDim.x + blockIdx.x) * 2;
+    p[0] = e;
+    p[1] = d;
+  }
+}
+
+// dE/d(amp, bw2) and virial partial sums; same layout as the mesh extras.
+template <typename T>
+__global__ void __launch_bounds__(kDirThreads) k_direct_extra(DirArgs a, const T *__restrict__ amp,
+                                                             const T *__restrict__ bw2, int want_grad,
+                                                             int want_vir) {
+  __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
+  __shared__ double red[kDirThreads / 32][4 * kMaxGauss + 13];
+  for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
+    s_amp[m] = (double)amp[m];
+    s_bw2[m] = (double)bw2[m];
+  }
+  __syncthreads();
+  const int f = blockIdx.y, c = blockIdx.z;
+  const int *nk = a.nk + 3 * f;
+  const int64_t nbox = (int64_t)(nk[0] + 1) * (2 * nk[1] + 1) * (2 * nk[2] + 1);
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int M = a.M;
+  double k[3] = {0, 0, 0}, K = 0.0, s2 = 0.0;
+  if (t < nbox) {
+    const double *kv = a.kvec + ((int64_t)f * a.kmax_modes + t) * 4;
+    k[0] = kv[0]; k[1] = kv[1]; k[2] = kv[2]; K = kv[3];
+    const double *s = a.sfac + (((int64_t)f * a.nch + c) * a.kmax_modes + t) * 2;
+    s2 = s[0] * s[0] + s[1] * s[1];
+  }
+  const bool live = K != 0.0;
+  const double ksq = k[0] * k[0] + k[1] * k[1] + k[2] * k[2];
+  if (want_grad) {
+    for (int m = 0; m < M; ++m) {
+      const double e = live ? exp(-0.5 * s_bw2[m] * ksq) : 0.0;
+      const double hk = -0.5 * ksq * s_amp[m];
+      const double v0 = warp_sum(2.0 * e * s2), v1 = warp_sum(2.0 * e);
+      const double v2 = warp_sum(2.0 * hk * e * s2), v3 = warp_sum(2.0 * hk * e);
+      if (lane == 0) {
+        red[warp][m] = v0; red[warp][M + m] = v1; red[warp][2 * M + m] = v2; red[warp][3 * M + m] = v3;
+      }
+    }
+  }
+  if (want_vir) {
+    double Kv = 0.0;
+    if (live)
+      for (int m = 0; m < M; ++m) Kv += s_amp[m] * s_bw2[m] * exp(-0.5 * s_bw2[m] * ksq);
+    const double kk[6] = {k[0] * k[0], k[1] * k[1], k[2] * k[2], k[0] * k[1], k[0] * k[2], k[1] * k[2]};
+    double v = warp_sum(2.0 * s2 * K);
+    if (lane == 0) red[warp][4 * M] = v;
+    for (int q = 0; q < 6; ++q) {
+      v = warp_sum(live ? 2.0 * s2 * Kv * kk[q] : 0.0);
+      if (lane == 0) red[warp][4 * M + 1 + q] = v;
+      v = warp_sum(live ? 2.0 * Kv * kk[q] : 0.0);
+      if (lane == 0) red[warp][4 * M + 7 + q] = v;
+    }
+  }
+  __syncthreads();
+  const int nacc = 4 * M + 13;
+  double *p = a.partx + (((int64_t)c * gridDim.y + f) * gridDim.x + blockIdx.x) * a.nx_acc;
+  for (int i = threadIdx.x; i < nacc; i += blockDim.x) {
+    const bool used = (i < 4 * M) ? want_grad : want_vir;
+    double s = 0.0;
+    if (used)
+      for (int w = 0; w < kDirThreads / 32; ++w) s += red[w][i];
+    p[i] = s;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) k_direct_atoms(DirArgs a, const T *__restrict__ pos,
+                                                     const T *__restrict__ q, double norm,
+                                                     T *__restrict__ forces, T *__restrict__ pot) {
+  constexpr int CH = 128;
+  __shared__ double s_k[CH][4];
+  __shared__ double s_s[CH][kMaxCh][2];
+  const int f = blockIdx.y;
+  const FrameGeom &g = a.geom[f];
+  const int *nk = a.nk + 3 * f;
+  const int64_t nbox = (int64_t)(nk[0] + 1) * (2 * nk[1] + 1) * (2 * nk[2] + 1);
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const bool own = i < g.natoms;
+  const int64_t atom = g.atom_begin + (own ? i : 0);
+  double r[3] = {0, 0, 0}, qi[kMaxCh];
+  if (own)
+    for (int c = 0; c < 3; ++c) r[c] = (double)pos[atom * 3 + c];
+#pragma unroll
+  for (int c = 0; c < kMaxCh; ++c) qi[c] = (own && c < a.nch) ? (double)q[atom * a.nch + c] : 0.0;
+  double fx = 0, fy = 0, fz = 0, pc[kMaxCh];
+#pragma unroll
+  for (int c = 0; c < kMaxCh; ++c) pc[c] = 0.0;
+  for (int64_t base = 0; base < nbox; base += CH) {
+    __syncthreads();
+    const int64_t t = base + threadIdx.x;
+    if (t < nbox) {
+      const double *kv = a.kvec + ((int64_t)f * a.kmax_modes + t) * 4;
+      for (int c = 0; c < 4; ++c) s_k[threadIdx.x][c] = kv[c];
+      for (int c = 0; c < a.nch; ++c) {
+        const double *s = a.sfac + (((int64_t)f * a.nch + c) * a.kmax_modes + t) * 2;
+        s_s[threadIdx.x][c][0] = s[0];
+        s_s[threadIdx.x][c][1] = s[1];
+      }
+    } else {
+      s_k[threadIdx.x][3] = 0.0;
+    }
+    __syncthreads();
+    const int cnt = (int)min((int64_t)CH, nbox - base);
+    if (own) {
+      for (int j = 0; j < cnt; ++j) {
+        const double K = s_k[j][3];
+        if (K == 0.0) continue;
+        const double kr = s_k[j][0] * r[0] + s_k[j][1] * r[1] + s_k[j][2] * r[2];
+        double sn, cs;
+        sincos(kr, &sn, &cs);
+        double tsum = 0.0;
+#pragma unroll
+        for (int c = 0; c < kMaxCh; ++c) {
+          if (c < a.nch) {
+            const double sr = s_s[j][c][0], si = s_s[j][c][1];
+            tsum += qi[c] * (si * cs - sr * sn);
+            pc[c] += 2.0 * K * (sr * cs + si * sn);
+          }
+        }
+        const double tt = 2.0 * K * tsum;
+        fx += tt * s_k[j][0];
+        fy += tt * s_k[j][1];
+        fz += tt * s_k[j][2];
+      }
+    }
+  }
+  if (!own) return;
+  if (forces) {
+    const double sc = -norm / g.vol;
+    forces[atom * 3 + 0] = (T)(sc * fx);
+    forces[atom * 3 + 1] = (T)(sc * fy);
+    forces[atom * 3 + 2] = (T)(sc * fz);
+  }
+  if (pot)
+    for (int c = 0; c < a.nch; ++c) pot[atom * a.nch + c] = (T)(pc[c] / g.vol);
+}
+
+inline unsigned nblk(int64_t n, int b) { return (unsigned)((n + b - 1) / b); }
+
+inline void after(Tracer *tr, cudaStream_t st, const char *name) {
+  count_launch();
+  if (tr) tr->mark(st, name);
+}
+
+template <typename T>
+int direct_impl(sog_direct *d, const sog_direct_args *a, cudaStream_t st) {
+  const int nf = a->nframes, nch = a->nchannels, M = a->n_gauss;
+  std::vector<FrameHost> fh(nf);
+  int64_t kmax = 1, maxat = 0, slots = 0;
+  for (int f = 0; f < nf; ++f) {
+    for (int c = 0; c < 3; ++c)
+      if (a->nk[3 * f + c] < 0 || a->nk[3 * f + c] > 4096) return fail(SOG_ERR_INVALID, "nk out of range");
+    const int64_t nbox = (int64_t)(a->nk[3 * f] + 1) * (2 * a->nk[3 * f + 1] + 1) * (2 * a->nk[3 * f + 2] + 1);
+    kmax = std::max(kmax, nbox);
+    maxat = std::max<int64_t>(maxat, a->atom_count[f]);
+    fh[f].atom_begin = a->atom_begin[f];
+    fh[f].natoms = a->atom_count[f];
+    fh[f].slot_base = slots;
+    fh[f].k_sq_max = a->k_sq_max[f];
+    slots += a->atom_count[f];
+  }
+  if (kmax > ((int64_t)1 << 31)) return fail(SOG_ERR_INVALID, "mode box too large");
+  const unsigned kb = nblk(kmax, kDirThreads);
+  const int nx_acc = 4 * M + 13;
+  const bool want_grad = a->grad_amp || a->grad_bw2;
+  const bool want_vir = a->virial != nullptr;
+  int rc;
+  if ((rc = d->up.reserve(sizeof(FrameHost) * nf + sizeof(int) * 3 * nf)) != SOG_OK) return rc;
+  if ((rc = d->up.wait()) != SOG_OK) return rc;
+  std::memcpy(d->up.p, fh.data(), sizeof(FrameHost) * nf);
+  std::memcpy((char *)d->up.p + sizeof(FrameHost) * nf, a->nk, sizeof(int) * 3 * nf);
+  if (d->frames_host_dev.reserve(sizeof(FrameHost) * nf + sizeof(int) * 3 * nf) ||
+      d->geom.reserve(sizeof(FrameGeom) * nf) || d->status.reserve(16) ||
+      d->modes.reserve(sizeof(double) * 4 * kmax * nf) ||
+      d->sfac.reserve(sizeof(double) * 2 * kmax * nf * nch) ||
+      d->part.reserve(sizeof(double) * ((int64_t)2 + ((want_grad || want_vir) ? nx_acc : 0)) * kb * nf * nch +
+                      sizeof(double) * ((int64_t)nf * nch * (2 + nx_acc) + (int64_t)nf * 4)) ||
+      d->qsum.reserve(sizeof(double) * 2 * nf * nch))
+    return fail(SOG_ERR_NOMEM, "device allocation failed (direct)");
+  SOG_CUDA_TRY(cudaMemcpyAsync(d->frames_host_dev.p, d->up.p, sizeof(FrameHost) * nf + sizeof(int) * 3 * nf,
+                               cudaMemcpyHostToDevice, st));
+  SOG_CUDA_TRY(cudaEventRecord(d->up.done, st));
+  d->up.pending = true;
+  FrameGeom *geom = d->geom.as<FrameGeom>();
+  const FrameHost *fhd = d->frames_host_dev.as<FrameHost>();
+  const int *nkd = reinterpret_cast<const int *>(fhd + nf);
+  Tracer *tr = &d->tr;
+  tr->begin(st);
+  k_frame_setup<T><<<nblk(nf, 128), 128, 0, st>>>((const T *)a->cells, fhd, geom, nf, SOG_KCONV_PHYSICAL,
+                                                  1, 1, 1, d->status.as<unsigned>());
+  after(tr, st, "frame_setup");
+  k_qsums<T><<<dim3(nf, nch), 256, 0, st>>>((const T *)a->charges, nch, geom, d->qsum.as<double>());
+  after(tr, st, "qsums");
+  DirArgs da;
+  da.geom = geom;
+  da.nk = nkd;
+  da.kmax_modes = kmax;
+  da.nch = nch;
+  da.M = M;
+  da.kvec = d->modes.as<double>();
+  da.sfac = d->sfac.as<double>();
+  da.part = d->part.as<double>();
+  da.partx = da.part + (int64_t)2 * kb * nf * nch;
+  da.nx_acc = nx_acc;
+  double *redE = da.partx + ((want_grad || want_vir) ? (int64_t)nx_acc * kb * nf * nch : 0);
+  double *redX = redE + (int64_t)nf * nch * 2;
+  double *fscal = redX + (int64_t)nf * nch * nx_acc;
+  k_direct_sfac<T><<<dim3(kb, nf), kDirThreads, 0, st>>>(da, (const T *)a->positions, (const T *)a->charges,
+                                                         (const T *)a->amp, (const T *)a->bw2);
+  after(tr, st, "direct_sfac");
+  if (want_grad || want_vir)
+    k_direct_extra<T><<<dim3(kb, nf, nch), kDirThreads, 0, st>>>(da, (const T *)a->amp, (const T *)a->bw2,
+                                                                 want_grad, want_vir);
+  if (want_grad || want_vir) after(tr, st, "direct_extra");
+  if ((a->forces || a->potential) && maxat > 0)
+    k_direct_atoms<T><<<dim3(nblk(maxat, 128), nf), 128, 0, st>>>(da, (const T *)a->positions,
+                                                                  (const T *)a->charges, a->norm_factor,
+                                                                  (T *)a->forces, (T *)a->potential);
+  if ((a->forces || a->potential) && maxat > 0) after(tr, st, "direct_atoms");
+  k_reduce_parts<<<dim3(nf, nch), 256, 0, st>>>(da.part, nf, nch, kb, 2, 2, redE);
+  after(tr, st, "reduce");
+  if (want_grad || want_vir)
+    k_reduce_parts<<<dim3(nf, nch), 256, 0, st>>>(da.partx, nf, nch, kb, nx_acc, nx_acc, redX);
+  if (want_grad || want_vir) after(tr, st, "reduce_extra");
+  FinalArgs fa;
+  std::memset(&fa, 0, sizeof(fa));
+  fa.geom = geom;
+  fa.redE = redE;
+  fa.redX = redX;
+  fa.qsum = d->qsum.as<double>();
+  fa.amp = a->amp;
+  fa.bw2 = a->bw2;
+  fa.M = M; fa.nch = nch; fa.nx = 1; fa.ny = 1; fa.nz = 1;
+  fa.norm = a->norm_factor;
+  fa.self_coeff = a->self_coeff;
+  fa.lambda = a->charge_neutral_lambda;
+  fa.remove_self = a->remove_self;
+  fa.k0 = a->k0_correction;
+  fa.want_grad = want_grad;
+  fa.want_vir = want_vir;
+  fa.direct = 1;
+  fa.energy = a->energy;
+  fa.grad_amp = a->grad_amp;
+  fa.grad_bw2 = a->grad_bw2;
+  fa.virial = a->virial;
+  fa.fscal = fscal;
+  k_finalize_frames<T><<<nblk(nf, 64), 64, 0, st>>>(fa, nf);
+  after(tr, st, "finalize_frames");
+  if (a->potential && maxat > 0)
+    k_finalize_atoms<T><<<dim3(nblk(maxat, 256), nf), 256, 0, st>>>(
+        geom, fscal, d->qsum.as<double>(), (const T *)a->charges, (T *)a->potential, nch, a->norm_factor,
+        a->self_coeff, a->charge_neutral_lambda, a->remove_self, a->k0_correction);
+  if (a->potential && maxat > 0) after(tr, st, "finalize_atoms");
+  SOG_CUDA_TRY(cudaGetLastError());
+  return SOG_OK;
+}
+
+}  // namespace
+}  // namespace sogb
+
+using namespace sogb;
+
+extern "C" int sog_direct_create(sog_direct **out, int dtype, int device) {
+  if (!out) return fail(SOG_ERR_INVALID, "null argument");
+  if (dtype != SOG_DTYPE_F64 && dtype != SOG_DTYPE_F32) return fail(SOG_ERR_INVALID, "bad dtype");
+  sog_direct *d = new sog_direct();
+  d->dtype = dtype;
+  d->device = device;
+  *out = d;
+  return SOG_OK;
+}
+
+extern "C" int sog_direct_destroy(sog_direct *d) {
+  if (!d) return SOG_OK;
+  DeviceGuard dg(d->device);
+  DevBuf *bufs[] = {&d->frames_host_dev, &d->geom, &d->modes, &d->sfac, &d->part, &d->qsum, &d->status};
+  for (DevBuf *b : bufs) b->release();
+  d->up.release();
+  d->tr.release();
+  delete d;
+  return SOG_OK;
+}
+
+extern "C" int sog_direct_forward(sog_direct *d, const sog_direct_args *a, void *stream) {
+  if (!d || !a) return fail(SOG_ERR_INVALID, "null argument");
+  if (a->nframes <= 0) return SOG_OK;
+  if (!a->atom_begin || !a->atom_count || !a->nk || !a->k_sq_max || !a->positions || !a->charges ||
+      !a->cells || !a->amp || !a->bw2)
+    return fail(SOG_ERR_INVALID, "missing input array");
+  if (a->nchannels < 1 || a->nchannels > kMaxCh)
+    return fail(SOG_ERR_UNSUPPORTED, "direct k-sum supports 1..8 charge channels");
+  if (a->n_gauss < 1 || a->n_gauss > kMaxGauss) return fail(SOG_ERR_INVALID, "n_gauss must be in [1, 64]");
+  DeviceGuard dg(d->device);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (d->dtype == SOG_DTYPE_F64) return direct_impl<double>(d, a, st);
+  return direct_impl<float>(d, a, st);
+}

@@ -1,0 +1,237 @@
+// Mixed-radix (2,3,4,5,8) Stockham FFT in shared memory, plus the three pass
+// kernels of a 3-D real transform on the [nz][ny][nx] mesh:
+//   - rows along x: R2C (forward) and C2R (inverse, torch.fft.irfftn
+//     semantics: the imaginary parts of the self-conjugate columns are ignored),
+//   - strided C2C passes along y and z.
+// Each pass reads and writes its array once (HBM-bound); the smem transform
+// uses a per-axis table of n-th roots of unity computed on the host in double.
+#pragma once
+#include "common.cuh"
+
+namespace sogb {
+
+struct RadixPlan {
+  int n;
+  int nst;
+  int r[24];
+};
+
+// DFT of radix R in registers; DIR = -1 forward (e^{-i}), +1 inverse.
+template <typename T, int DIR>
+__device__ __forceinline__ void dft2(cplx_t<T> *v) {
+  cplx_t<T> a = v[0], b = v[1];
+  v[0] = cadd(a, b);
+  v[1] = csub(a, b);
+}
+
+// multiply by -i*DIR... helpers: rot(x) = x * (DIR<0 ? -i : +i)
+template <typename T, int DIR>
+__device__ __forceinline__ cplx_t<T> rot90(cplx_t<T> x) {
+  cplx_t<T> r;
+  if (DIR < 0) { r.x = x.y; r.y = -x.x; } else { r.x = -x.y; r.y = x.x; }
+  return r;
+}
+
+template <typename T, int DIR>
+__device__ __forceinline__ void dft4(cplx_t<T> *v) {
+  cplx_t<T> a = cadd(v[0], v[2]), b = csub(v[0], v[2]);
+  cplx_t<T> c = cadd(v[1], v[3]), d = rot90<T, DIR>(csub(v[1], v[3]));
+  v[0] = cadd(a, c);
+  v[2] = csub(a, c);
+  v[1] = cadd(b, d);
+  v[3] = csub(b, d);
+}
+
+template <typename T, int DIR>
+__device__ __forceinline__ void dft3(cplx_t<T> *v) {
+  const T c = T(-0.5);
+  const T s = T(0.86602540378443864676372317075294);  // sin(2 pi / 3)
+  cplx_t<T> t1 = cadd(v[1], v[2]), t2 = csub(v[1], v[2]);
+  cplx_t<T> x0 = cadd(v[0], t1);
+  cplx_t<T> a;
+  a.x = v[0].x + c * t1.x;
+  a.y = v[0].y + c * t1.y;
+  // b = s * t2 rotated by -i (forward)
+  cplx_t<T> b = rot90<T, DIR>(cmk<cplx_t<T>, T>(s * t2.x, s * t2.y));
+  v[0] = x0;
+  v[1] = cadd(a, b);
+  v[2] = csub(a, b);
+}
+
+template <typename T, int DIR>
+__device__ __forceinline__ void dft5(cplx_t<T> *v) {
+  const T c1 = T(0.30901699437494742410229341718282);   // cos(2 pi/5)
+  const T c2 = T(-0.80901699437494742410229341718282);  // cos(4 pi/5)
+  const T s1 = T(0.95105651629515357211643933337938);   // sin(2 pi/5)
+  const T s2 = T(0.58778525229247312916870595463907);   // sin(4 pi/5)
+  cplx_t<T> t1 = cadd(v[1], v[4]), t2 = cadd(v[2], v[3]);
+  cplx_t<T> t3 = csub(v[1], v[4]), t4 = csub(v[2], v[3]);
+  cplx_t<T> x0 = cadd(v[0], cadd(t1, t2));
+  cplx_t<T> a1 = cmk<cplx_t<T>, T>(v[0].x + c1 * t1.x + c2 * t2.x, v[0].y + c1 * t1.y + c2 * t2.y);
+  cplx_t<T> a2 = cmk<cplx_t<T>, T>(v[0].x + c2 * t1.x + c1 * t2.x, v[0].y + c2 * t1.y + c1 * t2.y);
+  cplx_t<T> b1 = rot90<T, DIR>(cmk<cplx_t<T>, T>(s1 * t3.x + s2 * t4.x, s1 * t3.y + s2 * t4.y));
+  cplx_t<T> b2 = rot90<T, DIR>(cmk<cplx_t<T>, T>(s2 * t3.x - s1 * t4.x, s2 * t3.y - s1 * t4.y));
+  v[0] = x0;
+  v[1] = cadd(a1, b1);
+  v[4] = csub(a1, b1);
+  v[2] = cadd(a2, b2);
+  v[3] = csub(a2, b2);
+}
+
+template <typename T, int DIR>
+__device__ __forceinline__ void dft8(cplx_t<T> *v) {
+  const T h = T(0.70710678118654752440084436210485);  // 1/sqrt(2)
+  cplx_t<T> e[4] = {v[0], v[2], v[4], v[6]};
+  cplx_t<T> o[4] = {v[1], v[3], v[5], v[7]};
+  dft4<T, DIR>(e);
+  dft4<T, DIR>(o);
+  // twiddles W8^m, W8 = e^{DIR i pi/4}
+  cplx_t<T> w1 = cmk<cplx_t<T>, T>(h * (o[1].x - T(DIR) * o[1].y), h * (o[1].y + T(DIR) * o[1].x));
+  cplx_t<T> w2 = rot90<T, DIR>(o[2]);
+  cplx_t<T> r3 = rot90<T, DIR>(o[3]);
+  cplx_t<T> w3 = cmk<cplx_t<T>, T>(h * (r3.x - T(DIR) * r3.y), h * (r3.y + T(DIR) * r3.x));
+  v[0] = cadd(e[0], o[0]);
+  v[4] = csub(e[0], o[0]);
+  v[1] = cadd(e[1], w1);
+  v[5] = csub(e[1], w1);
+  v[2] = cadd(e[2], w2);
+  v[6] = csub(e[2], w2);
+  v[3] = cadd(e[3], w3);
+  v[7] = csub(e[3], w3);
+}
+
+template <typename T, int DIR, int R>
+__device__ __forceinline__ void stage_body(const cplx_t<T> *src, cplx_t<T> *dst, int n, int Ns,
+                                           int j, int b, int sj, int sb,
+                                           const cplx_t<T> *__restrict__ tw) {
+  using C = cplx_t<T>;
+  const int nR = n / R;
+  C v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = src[(j + r * nR) * sj + b * sb];
+  const int k = j % Ns;
+  if (Ns > 1) {
+    const int step = n / (Ns * R);
+#pragma unroll
+    for (int r = 1; r < R; ++r) {
+      C w = tw[r * k * step];
+      if (DIR > 0) w.y = -w.y;
+      v[r] = cmul(v[r], w);
+    }
+  }
+  if (R == 2) dft2<T, DIR>(v);
+  else if (R == 3) dft3<T, DIR>(v);
+  else if (R == 4) dft4<T, DIR>(v);
+  else if (R == 5) dft5<T, DIR>(v);
+  else dft8<T, DIR>(v);
+  const int idxD = (j / Ns) * Ns * R + k;
+#pragma unroll
+  for (int r = 0; r < R; ++r) dst[(idxD + r * Ns) * sj + b * sb] = v[r];
+}
+
+// `batch` transforms of length rp.n held in smem: element j of transform b at
+// a[j*sj + b*sb].  Ping-pongs between a and b; returns the buffer with the
+// result.  All threads of the block must call it.
+template <typename T, int DIR>
+__device__ cplx_t<T> *fft_smem(cplx_t<T> *a, cplx_t<T> *bbuf, const RadixPlan &rp, int batch,
+                               int sj, int sb, const cplx_t<T> *__restrict__ tw) {
+  cplx_t<T> *src = a, *dst = bbuf;
+  int Ns = 1;
+  const int n = rp.n;
+  for (int s = 0; s < rp.nst; ++s) {
+    const int R = rp.r[s];
+    const int nR = n / R;
+    const int total = batch * nR;
+    for (int t = threadIdx.x; t < total; t += blockDim.x) {
+      const int b = t / nR, j = t - b * nR;
+      switch (R) {
+        case 2: stage_body<T, DIR, 2>(src, dst, n, Ns, j, b, sj, sb, tw); break;
+        case 3: stage_body<T, DIR, 3>(src, dst, n, Ns, j, b, sj, sb, tw); break;
+        case 4: stage_body<T, DIR, 4>(src, dst, n, Ns, j, b, sj, sb, tw); break;
+        case 5: stage_body<T, DIR, 5>(src, dst, n, Ns, j, b, sj, sb, tw); break;
+        default: stage_body<T, DIR, 8>(src, dst, n, Ns, j, b, sj, sb, tw); break;
+      }
+    }
+    __syncthreads();
+    cplx_t<T> *tmp = src; src = dst; dst = tmp;
+    Ns *= R;
+  }
+  return src;
+}
+
+// Forward R2C along x.  in: nrows rows of nx reals; out: nrows rows of nx/2+1.
+template <typename T>
+__global__ void k_fft_r2c_x(const T *__restrict__ in, cplx_t<T> *__restrict__ out, int nx,
+                            int64_t nrows, int rows_per_cta, RadixPlan rp,
+                            const cplx_t<T> *__restrict__ tw) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  C *a = reinterpret_cast<C *>(smem_raw);
+  C *b = a + (size_t)rows_per_cta * nx;
+  const int64_t row0 = (int64_t)blockIdx.x * rows_per_cta;
+  const int nr = (int)min((int64_t)rows_per_cta, nrows - row0);
+  const T *src = in + row0 * nx;
+  for (int i = threadIdx.x; i < nr * nx; i += blockDim.x) a[i] = cmk<C, T>(src[i], T(0));
+  __syncthreads();
+  C *res = fft_smem<T, -1>(a, b, rp, nr, 1, nx, tw);
+  const int nxh = nx / 2 + 1;
+  C *dst = out + row0 * nxh;
+  for (int i = threadIdx.x; i < nr * nxh; i += blockDim.x) {
+    const int r = i / nxh, x = i - r * nxh;
+    dst[i] = res[r * nx + x];
+  }
+}
+
+// Inverse C2R along x with torch.fft.irfftn semantics (unnormalised).
+template <typename T>
+__global__ void k_fft_c2r_x(const cplx_t<T> *__restrict__ in, T *__restrict__ out, int nx,
+                            int64_t nrows, int rows_per_cta, RadixPlan rp,
+                            const cplx_t<T> *__restrict__ tw) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  C *a = reinterpret_cast<C *>(smem_raw);
+  C *b = a + (size_t)rows_per_cta * nx;
+  const int64_t row0 = (int64_t)blockIdx.x * rows_per_cta;
+  const int nr = (int)min((int64_t)rows_per_cta, nrows - row0);
+  const int nxh = nx / 2 + 1;
+  const C *src = in + row0 * nxh;
+  for (int i = threadIdx.x; i < nr * nxh; i += blockDim.x) {
+    const int r = i / nxh, m = i - r * nxh;
+    const C v = src[i];
+    a[r * nx + m] = v;
+    if (m >= 1 && m < (nx + 1) / 2) a[r * nx + nx - m] = cmk<C, T>(v.x, -v.y);
+  }
+  __syncthreads();
+  C *res = fft_smem<T, +1>(a, b, rp, nr, 1, nx, tw);
+  T *dst = out + row0 * nx;
+  for (int i = threadIdx.x; i < nr * nx; i += blockDim.x) dst[i] = res[i].x;
+}
+
+// C2C along a strided axis: data viewed as [outer][n][inner]; a CTA handles one
+// outer index and `ic` consecutive inner columns.
+template <typename T, int DIR>
+__global__ void k_fft_strided(cplx_t<T> *__restrict__ data, int64_t inner, int64_t outer,
+                              int ic, RadixPlan rp, const cplx_t<T> *__restrict__ tw) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int n = rp.n;
+  C *a = reinterpret_cast<C *>(smem_raw);
+  C *b = a + (size_t)n * ic;
+  const int64_t nchunks = (inner + ic - 1) / ic;
+  const int64_t o = blockIdx.x / nchunks;
+  const int64_t i0 = (blockIdx.x - o * nchunks) * ic;
+  const int nic = (int)min((int64_t)ic, inner - i0);
+  C *base = data + o * (int64_t)n * inner + i0;
+  for (int t = threadIdx.x; t < n * ic; t += blockDim.x) {
+    const int j = t / ic, c = t - j * ic;
+    if (c < nic) a[t] = base[(int64_t)j * inner + c];
+  }
+  __syncthreads();
+  C *res = fft_smem<T, DIR>(a, b, rp, nic, ic, 1, tw);
+  for (int t = threadIdx.x; t < n * ic; t += blockDim.x) {
+    const int j = t / ic, c = t - j * ic;
+    if (c < nic) base[(int64_t)j * inner + c] = res[t];
+  }
+}
+
+}  // namespace sogb

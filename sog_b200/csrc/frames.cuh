@@ -1,0 +1,279 @@
+// Per-frame kernels shared by the mesh and direct solvers: geometry set-up,
+// charge sums, deterministic partial-sum reduction, energy / gradient /
+// virial finalisation and the per-atom potential epilogue.
+#pragma once
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace sogb {
+namespace {
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ------------------------------------------------------------------------
+// frame set-up
+// ------------------------------------------------------------------------
+template <typename T>
+__global__ void k_frame_setup(const T *__restrict__ cells, const FrameHost *__restrict__ fh,
+                              FrameGeom *__restrict__ geom, int nf, int kconv, int nx, int ny,
+                              int nz, unsigned *status) {
+  const int f = blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= nf) return;
+  FrameGeom g;
+  double c[9];
+  for (int i = 0; i < 9; ++i) c[i] = (double)cells[(int64_t)f * 9 + i];
+  const double A = c[4] * c[8] - c[5] * c[7], B = -(c[3] * c[8] - c[5] * c[6]),
+               Cc = c[3] * c[7] - c[4] * c[6];
+  const double det = c[0] * A + c[1] * B + c[2] * Cc;
+  double vol = fabs(det);
+  if (!(vol > DBL_EPSILON) || !isfinite(vol)) {
+    raise_status(status, kStatusBadCell);
+    vol = 1.0;
+  }
+  const double id = (det != 0.0 && isfinite(det)) ? 1.0 / det : 0.0;
+  double ci[9];
+  ci[0] = A * id;  ci[1] = -(c[1] * c[8] - c[2] * c[7]) * id; ci[2] = (c[1] * c[5] - c[2] * c[4]) * id;
+  ci[3] = B * id;  ci[4] = (c[0] * c[8] - c[2] * c[6]) * id;  ci[5] = -(c[0] * c[5] - c[2] * c[3]) * id;
+  ci[6] = Cc * id; ci[7] = -(c[0] * c[7] - c[1] * c[6]) * id; ci[8] = (c[0] * c[4] - c[1] * c[3]) * id;
+  const double tp = 2.0 * kPi;
+  for (int i = 0; i < 9; ++i) { g.cell[i] = c[i]; g.cinv[i] = ci[i]; }
+  for (int a = 0; a < 3; ++a)
+    for (int b = 0; b < 3; ++b) g.kmat[a * 3 + b] = tp * (kconv ? ci[b * 3 + a] : ci[a * 3 + b]);
+  g.vol = vol;
+  // reciprocal vectors b_i = 2 pi (a_j x a_k) / V   (gaussian.py:774-782)
+  const double *a1 = c, *a2 = c + 3, *a3 = c + 6;
+  double bb[3][3] = {{a2[1] * a3[2] - a2[2] * a3[1], a2[2] * a3[0] - a2[0] * a3[2], a2[0] * a3[1] - a2[1] * a3[0]},
+                     {a3[1] * a1[2] - a3[2] * a1[1], a3[2] * a1[0] - a3[0] * a1[2], a3[0] * a1[1] - a3[1] * a1[0]},
+                     {a1[1] * a2[2] - a1[2] * a2[1], a1[2] * a2[0] - a1[0] * a2[2], a1[0] * a2[1] - a1[1] * a2[0]}};
+  double kmin2 = 1e300;
+  for (int i = 0; i < 3; ++i) {
+    double s = 0.0;
+    for (int k = 0; k < 3; ++k) { const double v = tp * bb[i][k] / vol; s += v * v; }
+    kmin2 = fmin(kmin2, s);
+  }
+  g.kmin2 = kmin2;
+  g.k_sq_max = fh[f].k_sq_max;
+  const double kmax = sqrt(fmax(g.k_sq_max, 0.0));
+  for (int a = 0; a < 3; ++a) {
+    double s = 0.0;
+    for (int b = 0; b < 3; ++b) { const double v = kconv ? c[b * 3 + a] : c[a * 3 + b]; s += v * v; }
+    g.abound[a] = sqrt(s) * kmax / tp + 1e-9;
+  }
+  g.scale = (double)nx * (double)ny * (double)nz / vol;
+  g.atom_begin = fh[f].atom_begin;
+  g.slot_base = fh[f].slot_base;
+  g.natoms = (int32_t)fh[f].natoms;
+  // Alias flag.  Every non-zero alias displacement 2 pi (N o j) has length at
+  // least min_a 2 pi N_a / |v_a| (v_a: lattice row, or cell column for the
+  // reference convention).  If that exceeds 2 k_max no alias of a mode inside
+  // the k_max sphere is inside it, and the B-spline Green reduces to its
+  // principal term: the plugin's alias fast path (lmp/sog.cpp:1370-1374).
+  {
+    const int n3[3] = {nx, ny, nz};
+    double lmin = 1e300;
+    for (int a = 0; a < 3; ++a) {
+      double s = 0.0;
+      for (int b = 0; b < 3; ++b) { const double v = kconv ? c[b * 3 + a] : c[a * 3 + b]; s += v * v; }
+      lmin = fmin(lmin, tp * (double)n3[a] / sqrt(s));
+    }
+    g.pad = (lmin > 2.0 * kmax) ? 0 : 1;
+  }
+  geom[f] = g;
+}
+
+// per (frame, channel): sum q and sum q^2 (fixed-order tree reduction)
+template <typename T>
+__global__ void k_qsums(const T *__restrict__ q, int nch, const FrameGeom *__restrict__ geom,
+                        double *__restrict__ out) {
+  const int f = blockIdx.x, c = blockIdx.y;
+  const FrameGeom &g = geom[f];
+  double s1 = 0.0, s2 = 0.0;
+  for (int i = threadIdx.x; i < g.natoms; i += blockDim.x) {
+    double v = (double)q[(g.atom_begin + i) * nch + c];
+    if (!isfinite(v)) v = 0.0;
+    s1 += v;
+    s2 += v * v;
+  }
+  __shared__ double r1[256], r2[256];
+  r1[threadIdx.x] = s1;
+  r2[threadIdx.x] = s2;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) { r1[threadIdx.x] += r1[threadIdx.x + o]; r2[threadIdx.x] += r2[threadIdx.x + o]; }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    out[((int64_t)f * nch + c) * 2 + 0] = r1[0];
+    out[((int64_t)f * nch + c) * 2 + 1] = r2[0];
+  }
+}
+
+// ------------------------------------------------------------------------
+// reductions and finalisation
+// ------------------------------------------------------------------------
+// out[(f*nch + c)*nacc + i] = sum_b part[((c*nf + f)*nblk + b)*stride + i]
+__global__ void k_reduce_parts(const double *__restrict__ part, int nf, int nch, int64_t nblk,
+                               int stride, int nacc, double *__restrict__ out) {
+  const int f = blockIdx.x, c = blockIdx.y;
+  __shared__ double sh[256];
+  for (int i = 0; i < nacc; ++i) {
+    double s = 0.0;
+    const double *p = part + (((int64_t)c * nf + f) * nblk) * stride + i;
+    for (int64_t b = threadIdx.x; b < nblk; b += blockDim.x) s += p[b * stride];
+    sh[threadIdx.x] = s;
+    __syncthreads();
+    for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+      if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) out[((int64_t)f * nch + c) * nacc + i] = sh[0];
+    __syncthreads();
+  }
+}
+
+struct FinalArgs {
+  const FrameGeom *geom;
+  const double *redE;    // [nf][C][2]
+  const double *redX;    // [nf][C][4M+13] or null
+  const double *qsum;    // [nf][C][2]
+  const void *amp, *bw2;
+  int M, nch, nx, ny, nz;
+  double norm, self_coeff, lambda;
+  int remove_self, k0;
+  int want_grad, want_vir;
+  int direct;            // 1: sums are sum_half 2 K |S|^2 (scale 1/2V); 0: mesh (V/2 N^-2)
+  void *energy, *grad_amp, *grad_bw2, *virial;
+  double *fscal;         // [nf][4]: diag, kfe, Q, (unused)
+};
+
+template <typename T>
+__global__ void k_finalize_frames(FinalArgs a, int nf) {
+  const int f = blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= nf) return;
+  const FrameGeom &g = a.geom[f];
+  const double V = g.vol;
+  const double N3 = (double)a.nx * a.ny * a.nz;
+  const double sc = a.direct ? 1.0 / (2.0 * V) : 0.5 * V / (N3 * N3);
+  const T *amp = (const T *)a.amp;
+  const T *bw2 = (const T *)a.bw2;
+  const double diag = a.redE[((int64_t)f * a.nch + 0) * 2 + 1] / (2.0 * V);
+  double E = 0.0, Q = 0.0, QQ = 0.0, pen = 0.0;
+  for (int c = 0; c < a.nch; ++c) {
+    const double qs = a.qsum[((int64_t)f * a.nch + c) * 2 + 0];
+    const double qq = a.qsum[((int64_t)f * a.nch + c) * 2 + 1];
+    double e = sc * a.redE[((int64_t)f * a.nch + c) * 2 + 0];
+    if (a.remove_self) e -= qq * diag;
+    if (a.self_coeff != 0.0) e -= qq * a.self_coeff;
+    E += e;
+    Q += qs;
+    QQ += qq;
+    if (g.natoms > 0) { const double mean = qs / g.natoms; pen += mean * mean; }
+  }
+  E *= a.norm;
+  double kfe = 0.0;
+  if (a.k0) {
+    for (int m = 0; m < a.M; ++m) kfe += (double)amp[m] * exp(-0.5 * (double)bw2[m] * g.kmin2);
+    E += kfe * Q * Q / (2.0 * V) * a.norm;
+    if (a.remove_self) E -= kfe * QQ / (2.0 * V) * a.norm;
+  }
+  if (a.lambda > 0.0) E += a.lambda * pen;
+  if (a.energy) ((T *)a.energy)[f] = (T)E;
+  a.fscal[f * 4 + 0] = diag;
+  a.fscal[f * 4 + 1] = kfe;
+  a.fscal[f * 4 + 2] = Q;
+  a.fscal[f * 4 + 3] = 0.0;
+  const int M = a.M;
+  const int nacc = 4 * M + 13;
+  if (a.want_grad) {
+    for (int m = 0; m < M; ++m) {
+      double ga = 0.0, gb = 0.0;
+      for (int c = 0; c < a.nch; ++c) {
+        const double *x = a.redX + ((int64_t)f * a.nch + c) * nacc;
+        const double qq = a.qsum[((int64_t)f * a.nch + c) * 2 + 1];
+        double va = sc * x[m], vb = sc * x[2 * M + m];
+        if (a.remove_self) {
+          va -= qq * x[M + m] / (2.0 * V);
+          vb -= qq * x[3 * M + m] / (2.0 * V);
+        }
+        ga += va;
+        gb += vb;
+      }
+      ga *= a.norm;
+      gb *= a.norm;
+      if (a.k0) {
+        const double em = exp(-0.5 * (double)bw2[m] * g.kmin2);
+        double cA = Q * Q / (2.0 * V) * a.norm;
+        if (a.remove_self) cA -= QQ / (2.0 * V) * a.norm;
+        ga += em * cA;
+        gb += (double)amp[m] * em * (-0.5 * g.kmin2) * cA;
+      }
+      if (a.grad_amp) ((T *)a.grad_amp)[(int64_t)f * M + m] = (T)ga;
+      if (a.grad_bw2) ((T *)a.grad_bw2)[(int64_t)f * M + m] = (T)gb;
+    }
+  }
+  if (a.want_vir && a.virial) {
+    const int comp[3][3] = {{0, 3, 4}, {3, 1, 5}, {4, 5, 2}};
+    double W[9] = {0, 0, 0, 0, 0, 0, 0, 0, 0};
+    const double pref = a.norm * sc;
+    for (int c = 0; c < a.nch; ++c) {
+      const double *x = a.redX + ((int64_t)f * a.nch + c) * nacc + 4 * M;
+      const double qq = a.qsum[((int64_t)f * a.nch + c) * 2 + 1];
+      for (int i = 0; i < 3; ++i)
+        for (int j = 0; j < 3; ++j) {
+          double w = -pref * x[1 + comp[i][j]];
+          if (i == j) w += pref * x[0];
+          if (a.remove_self) {
+            w += qq * a.norm / (2.0 * V) * x[7 + comp[i][j]];
+            if (i == j) w -= qq * a.norm * diag;
+          }
+          W[i * 3 + j] += w;
+        }
+    }
+    for (int i = 0; i < 9; ++i) ((T *)a.virial)[(int64_t)f * 9 + i] = (T)W[i];
+  }
+}
+
+// potential: dE/dq = norm * (gathered - 2 q (rsi*diag + self)) + k=0 / penalty terms
+template <typename T>
+__global__ void k_finalize_atoms(const FrameGeom *__restrict__ geom, const double *__restrict__ fscal,
+                                 const double *__restrict__ qsum, const T *__restrict__ q,
+                                 T *__restrict__ pot, int nch, double norm, double self_coeff,
+                                 double lambda, int remove_self, int k0) {
+  const int f = blockIdx.y;
+  const FrameGeom &g = geom[f];
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= g.natoms) return;
+  const int64_t atom = g.atom_begin + i;
+  const double diag = fscal[f * 4 + 0], kfe = fscal[f * 4 + 1], Q = fscal[f * 4 + 2];
+  for (int c = 0; c < nch; ++c) {
+    const double qi = (double)q[atom * nch + c];
+    double v = (double)pot[atom * nch + c];
+    if (remove_self) v -= 2.0 * qi * diag;
+    if (self_coeff != 0.0) v -= 2.0 * qi * self_coeff;
+    v *= norm;
+    if (k0) {
+      v += kfe * 2.0 * Q / (2.0 * g.vol) * norm;
+      if (remove_self) v -= kfe * 2.0 * qi / (2.0 * g.vol) * norm;
+    }
+    if (lambda > 0.0 && g.natoms > 0) {
+      const double mean = qsum[((int64_t)f * nch + c) * 2 + 0] / g.natoms;
+      v += lambda * 2.0 * mean / g.natoms;
+    }
+    pot[atom * nch + c] = (T)v;
+  }
+}
+
+template <typename T>
+__global__ void k_zero(T *p, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = T(0);
+}
+
+
+}  // namespace
+}  // namespace sogb

@@ -1,0 +1,1225 @@
+// Particle-mesh SOG solver on B200: cell-sorted deterministic spread, 3-D
+// R2C/C2R FFT, fused Green / energy / ik-field k-space pass, gather.
+//
+// Pipeline of one call (all frames share the plan's mesh):
+//   k_frame_setup   cells -> inverse, wave-vector matrix, volume, k=0 data
+//   k_atom_bin      fractional coords -> stencil anchor, sort bin     (a6/a7)
+//   radix sort      (bin, slot) pairs, stable -> fixed spread order
+//   k_atom_sorted   sorted SoA: anchors, fractional offsets, charges
+//   per channel:
+//     k_spread      output-stationary tiles, smem candidate lists   (a7)
+//     FFT  x R2C, y, z                                              (a8)
+//     k_kspace      Green on the fly, energy/self partials, ik fields (a9/a10)
+//     k_kspace_extra  dE/d(amp,bw2) and virial partials (optional)  (a11/a13)
+//     FFT^-1 z, y, x C2R (fields batched)                          (a10)
+//     k_gather      forces and potential at the atoms               (a10/a11)
+//   k_reduce / k_finalize_frames / k_finalize_atoms
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "host_math.hpp"
+#include "plan.hpp"
+#include "sort.cuh"
+#include "frames.cuh"
+
+namespace sogb {
+
+struct QuadsCoef {
+  double c[36];
+};
+
+// ------------------------------------------------------------------------
+// atoms: stencil anchor + bin key
+// ------------------------------------------------------------------------
+struct AtomGrid {
+  int nx, ny, nz, first, nbx, nby, nbz;
+  uint32_t bins_per_frame;
+};
+
+// Fractional coordinate along axis a (r @ cell^-1, then remainder 1.0) and the
+// anchor (first stencil node, wrapped) with the in-cell offset t
+// (quads_fft.py:243, 45-53; lmp/sog.cpp:1977-2006).
+template <typename T>
+__device__ __forceinline__ void frac_anchor(const T *r, const double *ci, int a, int n, int first,
+                                            int &anchor, T &t, bool &ok) {
+  const double s = (double)r[0] * ci[0 * 3 + a] + (double)r[1] * ci[1 * 3 + a] + (double)r[2] * ci[2 * 3 + a];
+  T sT = (T)s;
+  T f = sT - floor(sT);
+  T fx = f * (T)n;
+  if (!isfinite(fx)) { ok = false; fx = T(0); }
+  const T fl = floor(fx);
+  t = fx - fl;
+  int b = (int)fl + first;
+  b %= n;
+  if (b < 0) b += n;
+  anchor = b;
+}
+
+template <typename T>
+__global__ void k_atom_bin(const T *__restrict__ pos, const T *__restrict__ q, int nch,
+                           const FrameGeom *__restrict__ geom, AtomGrid ag,
+                           uint32_t *__restrict__ keys, int32_t *__restrict__ vals, unsigned *status) {
+  const int f = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const FrameGeom &g = geom[f];
+  if (i >= g.natoms) return;
+  const int64_t atom = g.atom_begin + i;
+  const T *r = pos + atom * 3;
+  bool ok = true;
+  int ax, ay, az;
+  T t;
+  frac_anchor(r, g.cinv, 0, ag.nx, ag.first, ax, t, ok);
+  frac_anchor(r, g.cinv, 1, ag.ny, ag.first, ay, t, ok);
+  frac_anchor(r, g.cinv, 2, ag.nz, ag.first, az, t, ok);
+  for (int c = 0; c < nch; ++c)
+    if (!isfinite((double)q[atom * nch + c])) ok = false;
+  if (!ok) raise_status(status, kStatusNonFinite);
+  const uint32_t key = (uint32_t)f * ag.bins_per_frame +
+                       ((uint32_t)(az / kBin) * ag.nby + (uint32_t)(ay / kBin)) * ag.nbx + (uint32_t)(ax / kBin);
+  const int64_t slot = g.slot_base + i;
+  keys[slot] = key;
+  vals[slot] = (int32_t)slot;
+}
+
+// sorted SoA: anchor (ax, ay, az, frame), offsets t, charges [C][n], atom index
+template <typename T>
+__global__ void k_atom_sorted(const T *__restrict__ pos, const T *__restrict__ q, int nch,
+                              const FrameGeom *__restrict__ geom, AtomGrid ag,
+                              const uint32_t *__restrict__ skeys, const int32_t *__restrict__ svals,
+                              int64_t nslots, int4 *__restrict__ s_anchor, T *__restrict__ s_t,
+                              T *__restrict__ s_q, int32_t *__restrict__ s_atom) {
+  const int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= nslots) return;
+  const int f = (int)(skeys[s] / ag.bins_per_frame);
+  const FrameGeom &g = geom[f];
+  const int64_t atom = g.atom_begin + (svals[s] - g.slot_base);
+  const T *r = pos + atom * 3;
+  bool ok = true;
+  int ax, ay, az;
+  T tx, ty, tz;
+  frac_anchor(r, g.cinv, 0, ag.nx, ag.first, ax, tx, ok);
+  frac_anchor(r, g.cinv, 1, ag.ny, ag.first, ay, ty, ok);
+  frac_anchor(r, g.cinv, 2, ag.nz, ag.first, az, tz, ok);
+  s_anchor[s] = make_int4(ax, ay, az, f);
+  s_t[s * 3 + 0] = tx;
+  s_t[s * 3 + 1] = ty;
+  s_t[s * 3 + 2] = tz;
+  for (int c = 0; c < nch; ++c) {
+    T v = q[atom * nch + c];
+    if (!isfinite((double)v)) v = T(0);
+    s_q[(int64_t)c * nslots + s] = v;
+  }
+  s_atom[s] = (int32_t)atom;
+}
+
+// ------------------------------------------------------------------------
+// 1-D spline weights (device)
+// ------------------------------------------------------------------------
+// Cardinal B-spline, Cox-de Boor (lmp/sog.cpp:89-110); w[a] weights node
+// anchor + a.
+template <typename T, int P>
+__device__ __forceinline__ void bspline_w(T t, T *w) {
+  T prev[P];
+#pragma unroll
+  for (int a = 0; a < P; ++a) w[a] = T(0);
+  w[0] = T(1) - t;
+  w[1] = t;
+#pragma unroll
+  for (int k = 3; k <= P; ++k) {
+    const T inv = T(1) / T(k - 1);
+#pragma unroll
+    for (int a = 0; a < P; ++a) prev[a] = w[a];
+    w[k - 1] = t * prev[k - 2] * inv;
+#pragma unroll
+    for (int j = 1; j <= k - 2; ++j)
+      w[k - 1 - j] = ((t + T(j)) * prev[k - 2 - j] + (T(k - j) - t) * prev[k - 1 - j]) * inv;
+    w[0] = (T(1) - t) * prev[0] * inv;
+  }
+}
+
+template <typename T, int P>
+__device__ __forceinline__ void spline_w(int spline, T t, T *w, const QuadsCoef &qc) {
+  if (spline == SOG_SPLINE_QUADS) {
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      T v = T(0), tp = T(1);
+#pragma unroll
+      for (int p = 0; p < P; ++p) { v += (T)qc.c[k * P + p] * tp; tp *= t; }
+      w[k] = v;
+    }
+  } else {
+    bspline_w<T, P>(t, w);
+  }
+}
+
+// ------------------------------------------------------------------------
+// spread: output-stationary tiles, deterministic, no global atomics
+// ------------------------------------------------------------------------
+template <typename T>
+struct SpreadArgs {
+  const int4 *s_anchor;
+  const T *s_t;
+  const T *s_q;        // channel slice [nslots]
+  const uint32_t *bin_start;
+  const FrameGeom *geom;
+  T *rho;              // [nf][ng]
+  AtomGrid ag;
+  int spline;
+  int ntx, nty, ntz;
+  QuadsCoef qc;
+};
+
+constexpr int kSpreadThreads = kTileX * kTileY;
+constexpr int kMaxSeg = 48;
+
+__device__ __forceinline__ int imod(int a, int n) {
+  a %= n;
+  return a < 0 ? a + n : a;
+}
+
+// ascending, de-duplicated bins of anchors in [lo, lo+len) (mod n)
+__device__ int axis_bins(int lo, int len, int n, int nb, int *out) {
+  int cnt = 0;
+  if (len >= n) {
+    for (int b = 0; b < nb; ++b) out[cnt++] = b;
+    return cnt;
+  }
+  const int s = imod(lo, n), e = imod(lo + len - 1, n);
+  const int bs = s / kBin, be = e / kBin;
+  if (s <= e) {
+    for (int b = bs; b <= be; ++b) out[cnt++] = b;
+  } else if (be >= bs) {
+    for (int b = 0; b < nb; ++b) out[cnt++] = b;
+  } else {
+    for (int b = 0; b <= be; ++b) out[cnt++] = b;
+    for (int b = bs; b < nb; ++b) out[cnt++] = b;
+  }
+  return cnt;
+}
+
+template <typename T, int P>
+__global__ void __launch_bounds__(kSpreadThreads) k_spread(SpreadArgs<T> a) {
+  constexpr int CH = kSpreadThreads;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T *c_wz = reinterpret_cast<T *>(smem_raw);            // [CH][kTileZ]
+  T *c_wx = c_wz + CH * kTileZ;                         // [CH][P]
+  T *c_wy = c_wx + CH * P;                              // [CH][P]
+  T *c_q = c_wy + CH * P;                               // [CH]
+  int *c_ax = reinterpret_cast<int *>(c_q + CH);        // [CH]
+  int *c_ay = c_ax + CH;                                // [CH]
+  __shared__ uint32_t seg_lo[kMaxSeg], seg_pre[kMaxSeg + 1];
+  __shared__ int nseg_s;
+  __shared__ int warp_cnt[kSpreadThreads / 32];
+
+  const AtomGrid &ag = a.ag;
+  const int tiles_pf = a.ntx * a.nty * a.ntz;
+  const int f = blockIdx.x / tiles_pf;
+  int rem = blockIdx.x - f * tiles_pf;
+  const int tz = rem / (a.ntx * a.nty);
+  rem -= tz * a.ntx * a.nty;
+  const int ty = rem / a.ntx, tx = rem - ty * a.ntx;
+  const int x0 = tx * kTileX, y0 = ty * kTileY, z0 = tz * kTileZ;
+  const int txv = min(kTileX, ag.nx - x0), tyv = min(kTileY, ag.ny - y0), tzv = min(kTileZ, ag.nz - z0);
+  const FrameGeom &g = a.geom[f];
+  const T scale = (T)g.scale;
+
+  if (threadIdx.x == 0) {
+    int xl[16], yl[16], zl[16];
+    const int nxl = axis_bins(x0 - P + 1, txv + P - 1, ag.nx, ag.nbx, xl);
+    const int nyl = axis_bins(y0 - P + 1, tyv + P - 1, ag.ny, ag.nby, yl);
+    const int nzl = axis_bins(z0 - P + 1, tzv + P - 1, ag.nz, ag.nbz, zl);
+    int ns = 0;
+    uint32_t pre = 0;
+    const uint32_t fbase = (uint32_t)f * ag.bins_per_frame;
+    for (int iz = 0; iz < nzl; ++iz)
+      for (int iy = 0; iy < nyl; ++iy) {
+        int i = 0;
+        while (i < nxl) {
+          int j = i;
+          while (j + 1 < nxl && xl[j + 1] == xl[j] + 1) ++j;
+          const uint32_t row = fbase + ((uint32_t)zl[iz] * ag.nby + (uint32_t)yl[iy]) * ag.nbx;
+          const uint32_t lo = a.bin_start[row + xl[i]], hi = a.bin_start[row + xl[j] + 1];
+          if (hi > lo && ns < kMaxSeg) {
+            seg_lo[ns] = lo;
+            seg_pre[ns] = pre;
+            pre += hi - lo;
+            ++ns;
+          }
+          i = j + 1;
+        }
+      }
+    seg_pre[ns] = pre;
+    nseg_s = ns;
+  }
+  __syncthreads();
+  const int nseg = nseg_s;
+  const uint32_t ncand = seg_pre[nseg];
+
+  const int lx = threadIdx.x % kTileX, ly = threadIdx.x / kTileX;
+  const int gx = x0 + lx, gy = y0 + ly;
+  const bool own = lx < txv && ly < tyv;
+  T acc[kTileZ];
+#pragma unroll
+  for (int z = 0; z < kTileZ; ++z) acc[z] = T(0);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (uint32_t c0 = 0; c0 < ncand; c0 += CH) {
+    // ---- load and filter one chunk of candidates (order preserving) ----
+    const uint32_t ci = c0 + threadIdx.x;
+    bool rel = false;
+    int4 an = make_int4(0, 0, 0, 0);
+    uint32_t sidx = 0;
+    if (ci < ncand) {
+      int lo = 0, hi = nseg - 1;
+      while (lo < hi) {  // last segment with seg_pre <= ci
+        const int mid = (lo + hi + 1) >> 1;
+        if (seg_pre[mid] <= ci) lo = mid; else hi = mid - 1;
+      }
+      sidx = seg_lo[lo] + (ci - seg_pre[lo]);
+      an = a.s_anchor[sidx];
+      const bool rx = imod(x0 - an.x, ag.nx) < P || imod(an.x - x0, ag.nx) < txv;
+      const bool ry = imod(y0 - an.y, ag.ny) < P || imod(an.y - y0, ag.ny) < tyv;
+      const bool rz = imod(z0 - an.z, ag.nz) < P || imod(an.z - z0, ag.nz) < tzv;
+      rel = rx && ry && rz;
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, rel);
+    if (lane == 0) warp_cnt[warp] = __popc(bal);
+    __syncthreads();
+    int base = 0, total = 0;
+    for (int w = 0; w < kSpreadThreads / 32; ++w) {
+      if (w < warp) base += warp_cnt[w];
+      total += warp_cnt[w];
+    }
+    if (rel) {
+      const int slot = base + __popc(bal & ((1u << lane) - 1u));
+      T w1[P];
+      spline_w<T, P>(a.spline, a.s_t[(int64_t)sidx * 3 + 0], w1, a.qc);
+#pragma unroll
+      for (int k = 0; k < P; ++k) c_wx[slot * P + k] = w1[k];
+      spline_w<T, P>(a.spline, a.s_t[(int64_t)sidx * 3 + 1], w1, a.qc);
+#pragma unroll
+      for (int k = 0; k < P; ++k) c_wy[slot * P + k] = w1[k];
+      spline_w<T, P>(a.spline, a.s_t[(int64_t)sidx * 3 + 2], w1, a.qc);
+#pragma unroll
+      for (int z = 0; z < kTileZ; ++z) {
+        T wz = T(0);
+        if (z < tzv) {
+          const int d = imod(z0 + z - an.z, ag.nz);
+#pragma unroll
+          for (int k = 0; k < P; ++k) wz = (d == k) ? w1[k] : wz;
+        }
+        c_wz[slot * kTileZ + z] = wz;
+      }
+      c_q[slot] = a.s_q[sidx] * scale;
+      c_ax[slot] = an.x;
+      c_ay[slot] = an.y;
+    }
+    __syncthreads();
+    // ---- accumulate the chunk in candidate order ----
+    if (own) {
+      for (int j = 0; j < total; ++j) {
+        int dx = gx - c_ax[j];
+        if (dx < 0) dx += ag.nx;
+        if (dx >= P) continue;
+        int dy = gy - c_ay[j];
+        if (dy < 0) dy += ag.ny;
+        if (dy >= P) continue;
+        const T wxy = c_wx[j * P + dx] * c_wy[j * P + dy] * c_q[j];
+        const T *wz = c_wz + j * kTileZ;
+#pragma unroll
+        for (int z = 0; z < kTileZ; ++z) acc[z] += wxy * wz[z];
+      }
+    }
+    __syncthreads();
+  }
+  if (own) {
+    T *out = a.rho + (int64_t)f * ((int64_t)ag.nx * ag.ny * ag.nz) + (int64_t)gy * ag.nx + gx;
+    const int64_t plane = (int64_t)ag.nx * ag.ny;
+#pragma unroll
+    for (int z = 0; z < kTileZ; ++z)
+      if (z < tzv) out[(int64_t)(z0 + z) * plane] = acc[z];
+  }
+}
+
+// ------------------------------------------------------------------------
+// k-space
+// ------------------------------------------------------------------------
+template <typename T>
+struct KsArgs {
+  const cplx_t<T> *spec;   // [nf][nh]
+  cplx_t<T> *fspec;        // [nf][F][nh]
+  const FrameGeom *geom;
+  const double *tx, *ty, *tz;  // per-axis Green factors
+  const double *sx, *sy, *sz;  // B-spline alias sums
+  const T *amp, *bw2;
+  int M, spline, order, alias_extent;
+  int nx, ny, nz, nxh;
+  int64_t nh;
+  int nfield;              // 0, 3 or 4
+  int want_force;
+  double *part;            // [nf][gridDim.x][2]
+  double *partx;           // [nf][gridDim.x][NX] extras
+  int nx_acc;
+};
+
+// Green factors of one half-spectrum mode.
+struct ModeGreen {
+  double k[3], ksq, K, Kv, gE, gF, gS, gV;
+  bool live;
+};
+
+__device__ __forceinline__ double sinc2p_dev(int mode, int n, int order, int j) {
+  const double arg = kPi * (double)mode / (double)n + kPi * (double)j;
+  const double s = fabs(arg) < 1e-14 ? 1.0 : sin(arg) / arg;
+  double r = 1.0;
+  for (int i = 0; i < 2 * order; ++i) r *= s;
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ double kernel_sum(const double *amp, const double *bw2, int M, double ksq,
+                                             double *Kv) {
+  double K = 0.0, V = 0.0;
+  for (int m = 0; m < M; ++m) {
+    const double e = exp(-0.5 * bw2[m] * ksq);
+    K += amp[m] * e;
+    V += amp[m] * bw2[m] * e;
+  }
+  *Kv = V;
+  return K;
+}
+
+// Green function of a mode; with `alias` the B-spline alias sums of
+// lmp/sog.cpp:1516-1578 (pruned to aliases inside the k_max sphere), else the
+// principal (separable) form.  If emD/emS are given, the per-Gaussian factors
+// d gE / d amp_m and d gS / d amp_m are returned too.
+template <typename T>
+__device__ ModeGreen mode_green(const KsArgs<T> &a, const FrameGeom &g, const double *amp,
+                                const double *bw2, int mx, int iy, int iz, int mfor, double *emD,
+                                double *emS) {
+  ModeGreen r;
+  const int my = signed_mode(iy, a.ny), mz = signed_mode(iz, a.nz);
+  for (int c = 0; c < 3; ++c)
+    r.k[c] = g.kmat[c * 3 + 0] * mx + g.kmat[c * 3 + 1] * my + g.kmat[c * 3 + 2] * mz;
+  r.ksq = r.k[0] * r.k[0] + r.k[1] * r.k[1] + r.k[2] * r.k[2];
+  r.live = !((mx | my | mz) == 0) && r.ksq <= g.k_sq_max;
+  r.K = r.Kv = r.gE = r.gF = r.gS = r.gV = 0.0;
+  if (!r.live) return r;
+  r.K = kernel_sum<T>(amp, bw2, a.M, r.ksq, &r.Kv);
+  if (a.spline == SOG_SPLINE_QUADS) {
+    double infl = a.tx[mx] * a.ty[iy] * a.tz[iz];
+    if (infl < 1e-20) infl = 1e-20;  // quads_fft.py:194
+    const double D = 1.0 / infl;
+    r.gE = r.gF = r.K * D;
+    r.gS = r.K;
+    r.gV = r.Kv * D;
+    if (emD) {
+      const double e = exp(-0.5 * bw2[mfor] * r.ksq);
+      *emD = e * D;
+      *emS = e;
+    }
+    return r;
+  }
+  if (!g.pad) {
+    const double D = a.tx[mx] * a.ty[iy] * a.tz[iz];
+    r.gE = r.gF = r.K * D;
+    r.gS = r.K;
+    r.gV = r.Kv * D;
+    if (emD) {
+      const double e = exp(-0.5 * bw2[mfor] * r.ksq);
+      *emD = e * D;
+      *emS = e;
+    }
+    return r;
+  }
+  // alias sums
+  const double dl = a.sx[mx] * a.sy[iy] * a.sz[iz];
+  const double denom = dl * dl;
+  const int m3[3] = {mx, my, mz};
+  const int n3[3] = {a.nx, a.ny, a.nz};
+  int jlo[3], jhi[3];
+  for (int c = 0; c < 3; ++c) {
+    int lo = (int)ceil((-g.abound[c] - (double)m3[c]) / (double)n3[c]);
+    int hi = (int)floor((g.abound[c] - (double)m3[c]) / (double)n3[c]);
+    lo = max(min(lo, 0), -a.alias_extent);
+    hi = min(max(hi, 0), a.alias_extent);
+    jlo[c] = lo;
+    jhi[c] = hi;
+  }
+  const double w0 = sinc2p_dev(mx, a.nx, a.order, 0) * sinc2p_dev(my, a.ny, a.order, 0) *
+                    sinc2p_dev(mz, a.nz, a.order, 0);
+  double s0 = 0.0, s1 = 0.0, sv = 0.0, eD = 0.0, eS = 0.0;
+  for (int jx = jlo[0]; jx <= jhi[0]; ++jx)
+    for (int jy = jlo[1]; jy <= jhi[1]; ++jy)
+      for (int jz = jlo[2]; jz <= jhi[2]; ++jz) {
+        const double ax = mx + a.nx * jx, ay = my + a.ny * jy, az = mz + a.nz * jz;
+        double q[3];
+        for (int c = 0; c < 3; ++c) q[c] = g.kmat[c * 3 + 0] * ax + g.kmat[c * 3 + 1] * ay + g.kmat[c * 3 + 2] * az;
+        const double qsq = q[0] * q[0] + q[1] * q[1] + q[2] * q[2];
+        if (!(qsq > 0.0 && qsq <= g.k_sq_max)) continue;
+        double Kvq;
+        const double Kq = kernel_sum<T>(amp, bw2, a.M, qsq, &Kvq);
+        const double wp = sinc2p_dev(mx, a.nx, a.order, jx) * sinc2p_dev(my, a.ny, a.order, jy) *
+                          sinc2p_dev(mz, a.nz, a.order, jz);
+        s0 += Kq * wp;
+        s1 += (r.k[0] * q[0] + r.k[1] * q[1] + r.k[2] * q[2]) * Kq * wp;
+        sv += Kvq * wp;
+        if (emD) {
+          const double e = exp(-0.5 * bw2[mfor] * qsq);
+          eD += e * wp / denom;
+          eS += (w0 > 1e-20) ? e * wp / w0 : 0.0;
+        }
+      }
+  r.gE = s0 / denom;
+  r.gF = s1 / (r.ksq * denom);
+  r.gS = (w0 > 1e-20) ? s0 / w0 : 0.0;
+  r.gV = sv / denom;
+  if (emD) { *emD = eD; *emS = eS; }
+  return r;
+}
+
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_kspace(KsArgs<T> a) {
+  using C = cplx_t<T>;
+  __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
+  __shared__ double red[2][8];
+  for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
+    s_amp[m] = (double)a.amp[m];
+    s_bw2[m] = (double)a.bw2[m];
+  }
+  __syncthreads();
+  const int f = blockIdx.y;
+  const FrameGeom &g = a.geom[f];
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  double accE = 0.0, accD = 0.0;
+  if (idx < a.nh) {
+    const int mx = (int)(idx % a.nxh);
+    const int64_t zy = idx / a.nxh;
+    const int iy = (int)(zy % a.ny), iz = (int)(zy / a.ny);
+    const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr);
+    const C r = a.spec[(int64_t)f * a.nh + idx];
+    const double rr = (double)r.x, ri = (double)r.y;
+    const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
+    if (mg.live) {
+      accE = w * mg.gE * (rr * rr + ri * ri);
+      accD = w * mg.gS;
+    }
+    if (a.nfield) {
+      const double inv = 1.0 / ((double)a.nx * a.ny * a.nz);
+      C *out = a.fspec + (int64_t)f * a.nfield * a.nh + idx;
+      int fo = 0;
+      if (a.want_force) {
+        const double sre = mg.gF * rr * inv, sim = mg.gF * ri * inv;
+        for (int c = 0; c < 3; ++c) out[(int64_t)c * a.nh] = cmk<C, T>((T)(-mg.k[c] * sim), (T)(mg.k[c] * sre));
+        fo = 3;
+      }
+      if (a.nfield > fo) out[(int64_t)fo * a.nh] = cmk<C, T>((T)(mg.gE * rr * inv), (T)(mg.gE * ri * inv));
+    }
+  }
+  accE = warp_sum(accE);
+  accD = warp_sum(accD);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { red[0][warp] = accE; red[1][warp] = accD; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double e = 0.0, d = 0.0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { e += red[0][w]; d += red[1][w]; }
+    double *p = a.part + ((int64_t)f * gridDim.x + blockIdx.x) * 2;
+    p[0] = e;
+    p[1] = d;
+  }
+}
+
+// Extras: dE/d(amp_m, bw2_m) partial sums (cubes2_fft.py:822-862) and the
+// reciprocal virial sums (cubes2_fft.py:874-921).  Layout of one partial:
+//   [0, M)        sum w e_m D |rho|^2         (gA main)
+//   [M, 2M)       sum w e_m                   (gA self)
+//   [2M, 3M)      sum w (-k^2/2) amp_m e_m D |rho|^2
+//   [3M, 4M)      sum w (-k^2/2) amp_m e_m
+//   [4M]          sum w |rho|^2 gE            (virial diagonal)
+//   [4M+1, 4M+7)  sum w |rho|^2 gV k_a k_b    (xx yy zz xy xz yz)
+//   [4M+7, 4M+13) sum w Kv k_a k_b            (self-energy strain)
+template <typename T>
+__global__ void __launch_bounds__(256) k_kspace_extra(KsArgs<T> a, int want_grad, int want_vir) {
+  using C = cplx_t<T>;
+  __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
+  __shared__ double red[8][4 * kMaxGauss + 13];
+  for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
+    s_amp[m] = (double)a.amp[m];
+    s_bw2[m] = (double)a.bw2[m];
+  }
+  __syncthreads();
+  const int f = blockIdx.y;
+  const FrameGeom &g = a.geom[f];
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int M = a.M;
+  bool valid = idx < a.nh;
+  int mx = 0, iy = 0, iz = 0;
+  double rho2 = 0.0, w = 0.0;
+  if (valid) {
+    mx = (int)(idx % a.nxh);
+    const int64_t zy = idx / a.nxh;
+    iy = (int)(zy % a.ny);
+    iz = (int)(zy / a.ny);
+    const C r = a.spec[(int64_t)f * a.nh + idx];
+    rho2 = (double)r.x * r.x + (double)r.y * r.y;
+    w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
+  }
+  ModeGreen mg;
+  mg.live = false;
+  if (valid) mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr);
+  const bool live = valid && mg.live;
+  if (want_grad) {
+    for (int m = 0; m < M; ++m) {
+      double eD = 0.0, eS = 0.0;
+      if (live) {
+        if (a.spline == SOG_SPLINE_BSPLINE && g.pad) {
+          mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, m, &eD, &eS);
+        } else {
+          const double e = exp(-0.5 * s_bw2[m] * mg.ksq);
+          eS = e;
+          eD = (mg.K != 0.0) ? e * (mg.gE / mg.K) : 0.0;
+          if (mg.K == 0.0) {
+            // D recomputed when K underflows to zero
+            if (a.spline == SOG_SPLINE_QUADS) {
+              double infl = a.tx[mx] * a.ty[iy] * a.tz[iz];
+              if (infl < 1e-20) infl = 1e-20;
+              eD = e / infl;
+            } else {
+              eD = e * a.tx[mx] * a.ty[iy] * a.tz[iz];
+            }
+          }
+        }
+      }
+      const double hk = -0.5 * mg.ksq * s_amp[m];
+      const double v0 = warp_sum(live ? w * eD * rho2 : 0.0);
+      const double v1 = warp_sum(live ? w * eS : 0.0);
+      const double v2 = warp_sum(live ? w * hk * eD * rho2 : 0.0);
+      const double v3 = warp_sum(live ? w * hk * eS : 0.0);
+      if (lane == 0) {
+        red[warp][m] = v0;
+        red[warp][M + m] = v1;
+        red[warp][2 * M + m] = v2;
+        red[warp][3 * M + m] = v3;
+      }
+    }
+  }
+  if (want_vir) {
+    double kk[6] = {0, 0, 0, 0, 0, 0};
+    if (live) {
+      kk[0] = mg.k[0] * mg.k[0]; kk[1] = mg.k[1] * mg.k[1]; kk[2] = mg.k[2] * mg.k[2];
+      kk[3] = mg.k[0] * mg.k[1]; kk[4] = mg.k[0] * mg.k[2]; kk[5] = mg.k[1] * mg.k[2];
+    }
+    double v = warp_sum(live ? w * rho2 * mg.gE : 0.0);
+    if (lane == 0) red[warp][4 * M] = v;
+    for (int c = 0; c < 6; ++c) {
+      v = warp_sum(live ? w * rho2 * mg.gV * kk[c] : 0.0);
+      if (lane == 0) red[warp][4 * M + 1 + c] = v;
+      v = warp_sum(live ? w * mg.Kv * kk[c] : 0.0);
+      if (lane == 0) red[warp][4 * M + 7 + c] = v;
+    }
+  }
+  __syncthreads();
+  const int nacc = 4 * M + 13;
+  double *p = a.partx + ((int64_t)f * gridDim.x + blockIdx.x) * a.nx_acc;
+  for (int i = threadIdx.x; i < nacc; i += blockDim.x) {
+    const bool used = (i < 4 * M) ? want_grad : want_vir;
+    double s = 0.0;
+    if (used)
+      for (int wv = 0; wv < (int)(blockDim.x >> 5); ++wv) s += red[wv][i];
+    p[i] = s;
+  }
+}
+
+// ------------------------------------------------------------------------
+// gather
+// ------------------------------------------------------------------------
+template <typename T>
+struct GatherArgs {
+  const int4 *s_anchor;
+  const T *s_t;
+  const T *s_q;       // channel slice
+  const int32_t *s_atom;
+  const T *freal;     // [nf][F][ng]
+  int nfield, want_force, want_pot;
+  int64_t nslots, ng;
+  AtomGrid ag;
+  int spline;
+  QuadsCoef qc;
+  double norm;
+  int channel, nch, accumulate;
+  T *forces;          // [N,3]
+  T *pot_raw;         // [N,C]
+};
+
+template <typename T, int P>
+__global__ void __launch_bounds__(256) k_gather(GatherArgs<T> a) {
+  const int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= a.nslots) return;
+  const int4 an = a.s_anchor[s];
+  T wx[P], wy[P], wz[P];
+  spline_w<T, P>(a.spline, a.s_t[s * 3 + 0], wx, a.qc);
+  spline_w<T, P>(a.spline, a.s_t[s * 3 + 1], wy, a.qc);
+  spline_w<T, P>(a.spline, a.s_t[s * 3 + 2], wz, a.qc);
+  const AtomGrid &ag = a.ag;
+  int ix[P];
+#pragma unroll
+  for (int k = 0; k < P; ++k) { int v = an.x + k; ix[k] = v >= ag.nx ? v - ag.nx : v; }
+  const T *base = a.freal + (int64_t)an.w * a.nfield * a.ng;
+  T acc[4] = {T(0), T(0), T(0), T(0)};
+#pragma unroll 1
+  for (int c = 0; c < P; ++c) {
+    int gz = an.z + c;
+    if (gz >= ag.nz) gz -= ag.nz;
+#pragma unroll
+    for (int b = 0; b < P; ++b) {
+      int gy = an.y + b;
+      if (gy >= ag.ny) gy -= ag.ny;
+      const int64_t row = ((int64_t)gz * ag.ny + gy) * ag.nx;
+      const T wzy = wy[b] * wz[c];
+#pragma unroll
+      for (int k = 0; k < P; ++k) {
+        const T wv = wx[k] * wzy;
+        const int64_t id = row + ix[k];
+        for (int fl = 0; fl < a.nfield; ++fl) acc[fl] += wv * base[(int64_t)fl * a.ng + id];
+      }
+    }
+  }
+  const int64_t atom = a.s_atom[s];
+  const T q = a.s_q[s];
+  if (a.want_force) {
+    const T sc = -q * (T)a.norm;
+    for (int c = 0; c < 3; ++c) {
+      const T v = sc * acc[c];
+      if (a.accumulate) a.forces[atom * 3 + c] += v; else a.forces[atom * 3 + c] = v;
+    }
+  }
+  if (a.want_pot) a.pot_raw[atom * a.nch + a.channel] = acc[a.want_force ? 3 : 0];
+}
+
+}  // namespace sogb
+
+// ==========================================================================
+// host side
+// ==========================================================================
+using namespace sogb;
+
+namespace {
+
+inline unsigned nblocks(int64_t n, int b) { return (unsigned)((n + b - 1) / b); }
+
+// bookkeeping after a launch: launch counter and optional timing event
+inline void after(Tracer *tr, cudaStream_t st, const char *name, int n = 1) {
+  count_launch(n);
+  if (tr) tr->mark(st, name);
+}
+
+void make_twiddles(int n, int dtype, std::vector<unsigned char> &buf) {
+  if (dtype == SOG_DTYPE_F64) {
+    buf.resize(sizeof(double2) * n);
+    double2 *t = reinterpret_cast<double2 *>(buf.data());
+    for (int m = 0; m < n; ++m) {
+      const long double a = -2.0L * 3.141592653589793238462643383279502884L * (long double)m / (long double)n;
+      t[m].x = (double)cosl(a);
+      t[m].y = (double)sinl(a);
+    }
+  } else {
+    buf.resize(sizeof(float2) * n);
+    float2 *t = reinterpret_cast<float2 *>(buf.data());
+    for (int m = 0; m < n; ++m) {
+      const long double a = -2.0L * 3.141592653589793238462643383279502884L * (long double)m / (long double)n;
+      t[m].x = (float)cosl(a);
+      t[m].y = (float)sinl(a);
+    }
+  }
+}
+
+int upload(DevBuf &b, const void *src, size_t bytes) {
+  if (b.reserve(bytes) != SOG_OK) return fail(SOG_ERR_NOMEM, "device allocation failed");
+  SOG_CUDA_TRY(cudaMemcpy(b.p, src, bytes, cudaMemcpyHostToDevice));
+  return SOG_OK;
+}
+
+bool smooth235(int n) {
+  for (int p : {2, 3, 5})
+    while (n % p == 0) n /= p;
+  return n == 1;
+}
+
+// exclusive scan of n uint32 (in -> out), temp buffer sized by scan_temp_elems
+int64_t scan_temp_elems(int64_t n) { return (n + kScanBlock - 1) / kScanBlock + 1; }
+
+void launch_scan(const uint32_t *in, uint32_t *out, int64_t n, uint32_t *tmp, cudaStream_t st,
+                 Tracer *tr) {
+  const int64_t nb = (n + kScanBlock - 1) / kScanBlock;
+  if (nb == 0) return;
+  k_scan_local<<<(unsigned)nb, kScanBlock, 0, st>>>(in, out, n, tmp);
+  k_scan_sums<<<1, kScanBlock, 0, st>>>(tmp, nb);
+  k_scan_add<<<(unsigned)nb, kScanBlock, 0, st>>>(out, n, tmp);
+  after(tr, st, "scan", 3);
+}
+
+template <typename T>
+size_t fft_rows_smem(int n, int rows) { return 2 * (size_t)rows * n * sizeof(cplx_t<T>); }
+
+template <typename T>
+int rows_per_cta(int n) {
+  const size_t budget = 64 * 1024;
+  int r = (int)(budget / (2 * (size_t)n * sizeof(cplx_t<T>)));
+  return std::max(1, std::min(r, 64));
+}
+
+template <typename T>
+int cols_per_cta(int n) {
+  const size_t budget = 64 * 1024;
+  int r = (int)(budget / (2 * (size_t)n * sizeof(cplx_t<T>)));
+  return std::max(1, std::min(r, 16));
+}
+
+template <typename T>
+void fft_forward(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t nbatch, cudaStream_t st) {
+  using C = cplx_t<T>;
+  const int nx = p->d.nx, ny = p->d.ny, nz = p->d.nz, nxh = p->nxh;
+  {
+    const int rpc = rows_per_cta<T>(nx);
+    const int64_t rows = nbatch * nz * ny;
+    k_fft_r2c_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
+        rho, spec, nx, rows, rpc, p->rpx, p->twx.as<C>());
+    after(&p->tr, st, "fft_r2c_x");
+  }
+  {
+    const int ic = cols_per_cta<T>(ny);
+    const int64_t outer = nbatch * nz, inner = nxh;
+    const int64_t nchunks = (inner + ic - 1) / ic;
+    k_fft_strided<T, -1><<<(unsigned)(outer * nchunks), 256, fft_rows_smem<T>(ny, ic), st>>>(
+        spec, inner, outer, ic, p->rpy, p->twy.as<C>());
+    after(&p->tr, st, "fft_y_fwd");
+  }
+  {
+    const int ic = cols_per_cta<T>(nz);
+    const int64_t outer = nbatch, inner = (int64_t)ny * nxh;
+    const int64_t nchunks = (inner + ic - 1) / ic;
+    k_fft_strided<T, -1><<<(unsigned)(outer * nchunks), 256, fft_rows_smem<T>(nz, ic), st>>>(
+        spec, inner, outer, ic, p->rpz, p->twz.as<C>());
+    after(&p->tr, st, "fft_z_fwd");
+  }
+}
+
+template <typename T>
+void fft_inverse(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nbatch, cudaStream_t st) {
+  using C = cplx_t<T>;
+  const int nx = p->d.nx, ny = p->d.ny, nz = p->d.nz, nxh = p->nxh;
+  {
+    const int ic = cols_per_cta<T>(nz);
+    const int64_t outer = nbatch, inner = (int64_t)ny * nxh;
+    const int64_t nchunks = (inner + ic - 1) / ic;
+    k_fft_strided<T, +1><<<(unsigned)(outer * nchunks), 256, fft_rows_smem<T>(nz, ic), st>>>(
+        fspec, inner, outer, ic, p->rpz, p->twz.as<C>());
+    after(&p->tr, st, "fft_z_inv");
+  }
+  {
+    const int ic = cols_per_cta<T>(ny);
+    const int64_t outer = nbatch * nz, inner = nxh;
+    const int64_t nchunks = (inner + ic - 1) / ic;
+    k_fft_strided<T, +1><<<(unsigned)(outer * nchunks), 256, fft_rows_smem<T>(ny, ic), st>>>(
+        fspec, inner, outer, ic, p->rpy, p->twy.as<C>());
+    after(&p->tr, st, "fft_y_inv");
+  }
+  {
+    const int rpc = rows_per_cta<T>(nx);
+    const int64_t rows = nbatch * nz * ny;
+    k_fft_c2r_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
+        fspec, freal, nx, rows, rpc, p->rpx, p->twx.as<C>());
+    after(&p->tr, st, "fft_c2r_x");
+  }
+}
+
+template <typename T>
+void set_fft_smem_attrs() {
+  static bool done = false;
+  if (done) return;
+  done = true;
+  const int big = 200 * 1024;
+  cudaFuncSetAttribute(k_fft_r2c_x<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_fft_c2r_x<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_fft_strided<T, -1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_fft_strided<T, +1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+}
+
+template <typename T, int P>
+size_t spread_smem() {
+  constexpr int CH = kSpreadThreads;
+  return (size_t)CH * (kTileZ + 2 * P + 1) * sizeof(T) + 2 * (size_t)CH * sizeof(int);
+}
+
+template <typename T, int P>
+void launch_spread(const SpreadArgs<T> &sa, int nframes, cudaStream_t st, Tracer *tr) {
+  static bool attr = false;
+  const size_t sm = spread_smem<T, P>();
+  if (!attr) {
+    cudaFuncSetAttribute(k_spread<T, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    attr = true;
+  }
+  const int64_t tiles = (int64_t)sa.ntx * sa.nty * sa.ntz * nframes;
+  k_spread<T, P><<<(unsigned)tiles, kSpreadThreads, sm, st>>>(sa);
+  after(tr, st, "spread");
+}
+
+template <typename T>
+void dispatch_spread(const SpreadArgs<T> &sa, int order, int nframes, cudaStream_t st, Tracer *tr) {
+  switch (order) {
+    case 4: launch_spread<T, 4>(sa, nframes, st, tr); break;
+    case 5: launch_spread<T, 5>(sa, nframes, st, tr); break;
+    default: launch_spread<T, 6>(sa, nframes, st, tr); break;
+  }
+}
+
+template <typename T>
+void dispatch_gather(const GatherArgs<T> &ga, int order, cudaStream_t st, Tracer *tr) {
+  const unsigned nb = nblocks(ga.nslots, 256);
+  if (nb == 0) return;
+  switch (order) {
+    case 4: k_gather<T, 4><<<nb, 256, 0, st>>>(ga); break;
+    case 5: k_gather<T, 5><<<nb, 256, 0, st>>>(ga); break;
+    default: k_gather<T, 6><<<nb, 256, 0, st>>>(ga); break;
+  }
+  after(tr, st, "gather");
+}
+
+template <typename T>
+int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
+  using C = cplx_t<T>;
+  const int nf = a->nframes, nch = a->nchannels, M = a->n_gauss;
+  const int nx = p->d.nx, ny = p->d.ny, nz = p->d.nz, nxh = p->nxh, P = p->d.order;
+  const int64_t ng = p->ng, nh = p->nh;
+
+  // ---- frames ----
+  std::vector<FrameHost> fh(nf);
+  int64_t nslots = 0, maxat = 0;
+  for (int f = 0; f < nf; ++f) {
+    if (a->atom_count[f] < 0 || a->atom_begin[f] < 0) return fail(SOG_ERR_INVALID, "negative atom range");
+    fh[f].atom_begin = a->atom_begin[f];
+    fh[f].natoms = a->atom_count[f];
+    fh[f].slot_base = nslots;
+    fh[f].k_sq_max = a->k_sq_max[f];
+    nslots += a->atom_count[f];
+    maxat = std::max<int64_t>(maxat, a->atom_count[f]);
+  }
+  if (nslots >= (int64_t)1 << 31) return fail(SOG_ERR_INVALID, "more than 2^31 atoms in one call");
+  int rc;
+  if ((rc = p->up.reserve(sizeof(FrameHost) * nf)) != SOG_OK) return rc;
+  if ((rc = p->up.wait()) != SOG_OK) return rc;
+  std::memcpy(p->up.p, fh.data(), sizeof(FrameHost) * nf);
+  if (p->frames_host_dev.reserve(sizeof(FrameHost) * nf) || p->geom.reserve(sizeof(FrameGeom) * nf) ||
+      p->status.reserve(sizeof(unsigned) * 4))
+    return fail(SOG_ERR_NOMEM, "device allocation failed");
+  SOG_CUDA_TRY(cudaMemcpyAsync(p->frames_host_dev.p, p->up.p, sizeof(FrameHost) * nf,
+                               cudaMemcpyHostToDevice, st));
+  SOG_CUDA_TRY(cudaEventRecord(p->up.done, st));
+  p->up.pending = true;
+  FrameGeom *geom = p->geom.as<FrameGeom>();
+  unsigned *status = p->status.as<unsigned>();
+  Tracer *tr = &p->tr;
+  tr->begin(st);
+  k_frame_setup<T><<<nblocks(nf, 128), 128, 0, st>>>((const T *)a->cells, p->frames_host_dev.as<FrameHost>(),
+                                                     geom, nf, p->d.kconv, nx, ny, nz, status);
+  after(tr, st, "frame_setup");
+
+  // ---- atom sort ----
+  AtomGrid ag;
+  ag.nx = nx; ag.ny = ny; ag.nz = nz;
+  ag.first = (p->d.spline == SOG_SPLINE_QUADS) ? (1 - P / 2) : -((P - 1) / 2);
+  ag.nbx = p->nb_x; ag.nby = p->nb_y; ag.nbz = p->nb_z;
+  ag.bins_per_frame = (uint32_t)ag.nbx * ag.nby * ag.nbz;
+  const uint64_t nbins64 = (uint64_t)ag.bins_per_frame * nf;
+  if (nbins64 >= (1ull << 32) - 1) return fail(SOG_ERR_INVALID, "too many sort bins in one call");
+  const uint32_t nbins = (uint32_t)nbins64;
+  const int64_t sort_blocks = std::max<int64_t>(1, (nslots + kSortTile - 1) / kSortTile);
+  const int64_t hist_n = sort_blocks * kRadixBuckets;
+  const int64_t scan_n = std::max<int64_t>(hist_n, (int64_t)nbins + 1);
+  if (p->keys0.reserve(4 * std::max<int64_t>(nslots, 1)) || p->vals0.reserve(4 * std::max<int64_t>(nslots, 1)) ||
+      p->keys1.reserve(4 * std::max<int64_t>(nslots, 1)) || p->vals1.reserve(4 * std::max<int64_t>(nslots, 1)) ||
+      p->hist.reserve(4 * scan_n) || p->scan_tmp.reserve(4 * scan_temp_elems(scan_n)) ||
+      p->bin_start.reserve(4 * ((int64_t)nbins + 1)) ||
+      p->s_anchor.reserve(sizeof(int4) * std::max<int64_t>(nslots, 1)) ||
+      p->s_t.reserve(sizeof(T) * 3 * std::max<int64_t>(nslots, 1)) ||
+      p->s_q.reserve(sizeof(T) * nch * std::max<int64_t>(nslots, 1)) ||
+      p->s_atom.reserve(4 * std::max<int64_t>(nslots, 1)) ||
+      p->qsum.reserve(sizeof(double) * 2 * nf * nch))
+    return fail(SOG_ERR_NOMEM, "device allocation failed");
+  uint32_t *k0 = p->keys0.as<uint32_t>(), *k1 = p->keys1.as<uint32_t>();
+  int32_t *v0 = p->vals0.as<int32_t>(), *v1 = p->vals1.as<int32_t>();
+  if (maxat > 0)
+    k_atom_bin<T><<<dim3(nblocks(maxat, 256), nf), 256, 0, st>>>(
+        (const T *)a->positions, (const T *)a->charges, nch, geom, ag, k0, v0, status);
+  if (maxat > 0) after(tr, st, "atom_bin");
+  int keybits = 1;
+  while (keybits < 32 && (1ull << keybits) <= (uint64_t)nbins) ++keybits;
+  for (int shift = 0; shift < keybits; shift += kRadixBits) {
+    if (nslots == 0) break;
+    k_radix_hist<<<(unsigned)sort_blocks, kSortThreads, 0, st>>>(k0, nslots, shift, p->hist.as<uint32_t>(),
+                                                                 (int)sort_blocks);
+    after(tr, st, "radix_hist");
+    launch_scan(p->hist.as<uint32_t>(), p->hist.as<uint32_t>(), hist_n, p->scan_tmp.as<uint32_t>(), st, tr);
+    k_radix_scatter<<<(unsigned)sort_blocks, kSortThreads, 0, st>>>(k0, v0, k1, v1, nslots, shift,
+                                                                    p->hist.as<uint32_t>(), (int)sort_blocks);
+    after(tr, st, "radix_scatter");
+    std::swap(k0, k1);
+    std::swap(v0, v1);
+  }
+  k_bin_starts<<<nblocks(nslots + 1, 256), 256, 0, st>>>(k0, nslots, nbins, p->bin_start.as<uint32_t>());
+  after(tr, st, "bin_starts");
+  if (nslots > 0)
+    k_atom_sorted<T><<<nblocks(nslots, 256), 256, 0, st>>>(
+        (const T *)a->positions, (const T *)a->charges, nch, geom, ag, k0, v0, nslots,
+        p->s_anchor.as<int4>(), p->s_t.as<T>(), p->s_q.as<T>(), p->s_atom.as<int32_t>());
+  if (nslots > 0) after(tr, st, "atom_sorted");
+  k_qsums<T><<<dim3(nf, nch), 256, 0, st>>>((const T *)a->charges, nch, geom, p->qsum.as<double>());
+  after(tr, st, "qsums");
+
+  // ---- buffers ----
+  const bool want_force = a->forces != nullptr;
+  const bool want_pot = a->potential != nullptr;
+  const bool want_grad = a->grad_amp != nullptr || a->grad_bw2 != nullptr;
+  const bool want_vir = a->virial != nullptr;
+  const int nfield = (want_force ? 3 : 0) + (want_pot ? 1 : 0);
+  const unsigned ks_blocks = nblocks(nh, 256);
+  const int nx_acc = 4 * M + 13;
+  if (p->rho.reserve(sizeof(T) * ng * nf) || p->spec.reserve(sizeof(C) * nh * nf) ||
+      p->partE.reserve(sizeof(double) * 2 * (int64_t)ks_blocks * nf * nch) ||
+      (nfield && (p->fspec.reserve(sizeof(C) * nh * nf * nfield) ||
+                  p->freal.reserve(sizeof(T) * ng * nf * nfield))) ||
+      ((want_grad || want_vir) && p->partX.reserve(sizeof(double) * nx_acc * (int64_t)ks_blocks * nf * nch)) ||
+      p->red.reserve(sizeof(double) * ((int64_t)nf * nch * (2 + nx_acc) + (int64_t)nf * 4)))
+    return fail(SOG_ERR_NOMEM, "device allocation failed (mesh buffers)");
+
+  QuadsCoef qc;
+  std::memset(&qc, 0, sizeof(qc));
+  if (p->d.spline == SOG_SPLINE_QUADS) quads_coeffs(P, qc.c);
+
+  SpreadArgs<T> sa;
+  sa.s_anchor = p->s_anchor.as<int4>();
+  sa.s_t = p->s_t.as<T>();
+  sa.bin_start = p->bin_start.as<uint32_t>();
+  sa.geom = geom;
+  sa.rho = p->rho.as<T>();
+  sa.ag = ag;
+  sa.spline = p->d.spline;
+  sa.ntx = (nx + kTileX - 1) / kTileX;
+  sa.nty = (ny + kTileY - 1) / kTileY;
+  sa.ntz = (nz + kTileZ - 1) / kTileZ;
+  sa.qc = qc;
+
+  KsArgs<T> ka;
+  ka.spec = p->spec.as<C>();
+  ka.fspec = nfield ? p->fspec.as<C>() : nullptr;
+  ka.geom = geom;
+  ka.tx = p->tab.fx.as<double>(); ka.ty = p->tab.fy.as<double>(); ka.tz = p->tab.fz.as<double>();
+  ka.sx = p->tab.sx.as<double>(); ka.sy = p->tab.sy.as<double>(); ka.sz = p->tab.sz.as<double>();
+  ka.amp = (const T *)a->amp;
+  ka.bw2 = (const T *)a->bw2;
+  ka.M = M;
+  ka.spline = p->d.spline;
+  ka.order = P;
+  ka.alias_extent = p->d.alias_extent;
+  ka.nx = nx; ka.ny = ny; ka.nz = nz; ka.nxh = nxh;
+  ka.nh = nh;
+  ka.nfield = nfield;
+  ka.want_force = want_force;
+  ka.nx_acc = nx_acc;
+
+  GatherArgs<T> gar;
+  gar.s_anchor = p->s_anchor.as<int4>();
+  gar.s_t = p->s_t.as<T>();
+  gar.s_atom = p->s_atom.as<int32_t>();
+  gar.freal = p->freal.as<T>();
+  gar.nfield = nfield;
+  gar.want_force = want_force;
+  gar.want_pot = want_pot;
+  gar.nslots = nslots;
+  gar.ng = ng;
+  gar.ag = ag;
+  gar.spline = p->d.spline;
+  gar.qc = qc;
+  gar.norm = a->norm_factor;
+  gar.nch = nch;
+  gar.forces = (T *)a->forces;
+  gar.pot_raw = (T *)a->potential;
+
+  set_fft_smem_attrs<T>();
+  for (int c = 0; c < nch; ++c) {
+    sa.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
+    dispatch_spread<T>(sa, P, nf, st, tr);
+    fft_forward<T>(p, p->rho.as<T>(), p->spec.as<C>(), nf, st);
+    ka.part = p->partE.as<double>() + (int64_t)c * nf * ks_blocks * 2;
+    k_kspace<T><<<dim3(ks_blocks, nf), 256, 0, st>>>(ka);
+    after(tr, st, "kspace");
+    if (want_grad || want_vir) {
+      ka.partx = p->partX.as<double>() + (int64_t)c * nf * ks_blocks * nx_acc;
+      k_kspace_extra<T><<<dim3(ks_blocks, nf), 256, 0, st>>>(ka, want_grad, want_vir);
+      after(tr, st, "kspace_extra");
+    }
+    if (nfield) {
+      fft_inverse<T>(p, p->fspec.as<C>(), p->freal.as<T>(), (int64_t)nf * nfield, st);
+      gar.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
+      gar.channel = c;
+      gar.accumulate = c > 0;
+      dispatch_gather<T>(gar, P, st, tr);
+    }
+  }
+  // ---- reductions / finalisation ----
+  double *redE = p->red.as<double>();
+  double *redX = redE + (int64_t)nf * nch * 2;
+  double *fscal = redX + (int64_t)nf * nch * nx_acc;
+  k_reduce_parts<<<dim3(nf, nch), 256, 0, st>>>(p->partE.as<double>(), nf, nch, ks_blocks, 2, 2, redE);
+  after(tr, st, "reduce");
+  if (want_grad || want_vir)
+    k_reduce_parts<<<dim3(nf, nch), 256, 0, st>>>(p->partX.as<double>(), nf, nch, ks_blocks, nx_acc,
+                                                  nx_acc, redX);
+  if (want_grad || want_vir) after(tr, st, "reduce_extra");
+  FinalArgs fa;
+  fa.geom = geom;
+  fa.redE = redE;
+  fa.redX = redX;
+  fa.qsum = p->qsum.as<double>();
+  fa.amp = a->amp;
+  fa.bw2 = a->bw2;
+  fa.M = M; fa.nch = nch; fa.nx = nx; fa.ny = ny; fa.nz = nz;
+  fa.norm = a->norm_factor;
+  fa.self_coeff = a->self_coeff;
+  fa.lambda = a->charge_neutral_lambda;
+  fa.remove_self = a->remove_self;
+  fa.k0 = a->k0_correction;
+  fa.want_grad = want_grad;
+  fa.want_vir = want_vir;
+  fa.direct = 0;
+  fa.energy = a->energy;
+  fa.grad_amp = a->grad_amp;
+  fa.grad_bw2 = a->grad_bw2;
+  fa.virial = a->virial;
+  fa.fscal = fscal;
+  k_finalize_frames<T><<<nblocks(nf, 64), 64, 0, st>>>(fa, nf);
+  after(tr, st, "finalize_frames");
+  if (want_pot && maxat > 0)
+    k_finalize_atoms<T><<<dim3(nblocks(maxat, 256), nf), 256, 0, st>>>(
+        geom, fscal, p->qsum.as<double>(), (const T *)a->charges, (T *)a->potential, nch,
+        a->norm_factor, a->self_coeff, a->charge_neutral_lambda, a->remove_self, a->k0_correction);
+  if (want_pot && maxat > 0) after(tr, st, "finalize_atoms");
+  SOG_CUDA_TRY(cudaGetLastError());
+  return SOG_OK;
+}
+
+}  // namespace
+
+// ==========================================================================
+// C ABI
+// ==========================================================================
+extern "C" int sog_plan_create(sog_plan **out, const sog_plan_desc *desc) {
+  if (!out || !desc) return fail(SOG_ERR_INVALID, "null argument");
+  *out = nullptr;
+  const sog_plan_desc &d = *desc;
+  if (d.dtype != SOG_DTYPE_F64 && d.dtype != SOG_DTYPE_F32) return fail(SOG_ERR_INVALID, "dtype must be F64 or F32");
+  if (d.spline == SOG_SPLINE_BSPLINE) {
+    if (d.order < 4 || d.order > 6) return fail(SOG_ERR_INVALID, "B-spline order must be 4, 5 or 6");
+  } else if (d.spline == SOG_SPLINE_QUADS) {
+    if (d.order != 4 && d.order != 6) return fail(SOG_ERR_INVALID, "QuadS order must be 4 or 6");
+  } else {
+    return fail(SOG_ERR_UNSUPPORTED, "spline family not supported (CubeS2 is not built)");
+  }
+  if (d.nx < 8 || d.ny < 8 || d.nz < 8) return fail(SOG_ERR_INVALID, "mesh dims must be >= 8");
+  if (!smooth235(d.nx) || !smooth235(d.ny) || !smooth235(d.nz))
+    return fail(SOG_ERR_INVALID, "mesh dims must be 2,3,5-smooth");
+  if (d.nx > 4096 || d.ny > 4096 || d.nz > 4096) return fail(SOG_ERR_UNSUPPORTED, "mesh dim above 4096");
+  if (d.kconv != SOG_KCONV_PHYSICAL && d.kconv != SOG_KCONV_REFERENCE)
+    return fail(SOG_ERR_INVALID, "kconv must be PHYSICAL or REFERENCE");
+  DeviceGuard dg(d.device);
+  sog_plan *p = new sog_plan();
+  p->d = d;
+  if (p->d.alias_extent <= 0) p->d.alias_extent = 8;
+  p->nxh = d.nx / 2 + 1;
+  p->ng = (int64_t)d.nx * d.ny * d.nz;
+  p->nh = (int64_t)d.nz * d.ny * p->nxh;
+  build_radix_plan(d.nx, &p->rpx);
+  build_radix_plan(d.ny, &p->rpy);
+  build_radix_plan(d.nz, &p->rpz);
+  p->nb_x = (d.nx + kBin - 1) / kBin;
+  p->nb_y = (d.ny + kBin - 1) / kBin;
+  p->nb_z = (d.nz + kBin - 1) / kBin;
+  int rc = SOG_OK;
+  std::vector<unsigned char> tw;
+  make_twiddles(d.nx, d.dtype, tw);
+  if ((rc = upload(p->twx, tw.data(), tw.size())) != SOG_OK) goto bad;
+  make_twiddles(d.ny, d.dtype, tw);
+  if ((rc = upload(p->twy, tw.data(), tw.size())) != SOG_OK) goto bad;
+  make_twiddles(d.nz, d.dtype, tw);
+  if ((rc = upload(p->twz, tw.data(), tw.size())) != SOG_OK) goto bad;
+  {
+    // per-axis Green factors and alias sums over mode indices of each axis
+    auto axis = [&](int n, int len, bool half, DevBuf &fb, DevBuf &sb) -> int {
+      std::vector<double> fv(len), sv(len);
+      for (int i = 0; i < len; ++i) {
+        const int m = half ? i : (i <= n / 2 ? i : i - n);
+        sv[i] = bspline_sinc_sum(m, n, d.order, p->d.alias_extent);
+        if (d.spline == SOG_SPLINE_QUADS) fv[i] = quads_influence_1d(m, n, d.order);
+        else fv[i] = bspline_sinc2p(m, n, d.order, 0) / (sv[i] * sv[i]);
+      }
+      int r = upload(fb, fv.data(), sizeof(double) * len);
+      if (r == SOG_OK) r = upload(sb, sv.data(), sizeof(double) * len);
+      return r;
+    };
+    if ((rc = axis(d.nx, p->nxh, true, p->tab.fx, p->tab.sx)) != SOG_OK) goto bad;
+    if ((rc = axis(d.ny, d.ny, false, p->tab.fy, p->tab.sy)) != SOG_OK) goto bad;
+    if ((rc = axis(d.nz, d.nz, false, p->tab.fz, p->tab.sz)) != SOG_OK) goto bad;
+  }
+  if ((rc = p->up.reserve(4096)) != SOG_OK) goto bad;
+  *out = p;
+  return SOG_OK;
+bad:
+  sog_plan_destroy(p);
+  return rc;
+}
+
+extern "C" int sog_plan_destroy(sog_plan *p) {
+  if (!p) return SOG_OK;
+  DeviceGuard dg(p->d.device);
+  DevBuf *bufs[] = {&p->twx, &p->twy, &p->twz, &p->tab.fx, &p->tab.fy, &p->tab.fz, &p->tab.sx,
+                    &p->tab.sy, &p->tab.sz, &p->frames_host_dev, &p->geom, &p->status, &p->keys0,
+                    &p->vals0, &p->keys1, &p->vals1, &p->hist, &p->scan_tmp, &p->bin_start,
+                    &p->s_atom, &p->s_anchor, &p->s_t, &p->s_q, &p->qsum, &p->rho, &p->spec,
+                    &p->fspec, &p->freal, &p->partE, &p->partX, &p->red};
+  for (DevBuf *b : bufs) b->release();
+  p->up.release();
+  p->tr.release();
+  delete p;
+  return SOG_OK;
+}
+
+extern "C" int sog_plan_status(sog_plan *p, unsigned *bits) {
+  if (!p || !bits) return fail(SOG_ERR_INVALID, "null argument");
+  *bits = 0;
+  if (!p->status.p) return SOG_OK;
+  DeviceGuard dg(p->d.device);
+  SOG_CUDA_TRY(cudaDeviceSynchronize());
+  SOG_CUDA_TRY(cudaMemcpy(bits, p->status.p, sizeof(unsigned), cudaMemcpyDeviceToHost));
+  SOG_CUDA_TRY(cudaMemset(p->status.p, 0, sizeof(unsigned)));
+  return SOG_OK;
+}
+
+extern "C" int sog_mesh_forward(sog_plan *p, const sog_mesh_args *a, void *stream) {
+  if (!p || !a) return fail(SOG_ERR_INVALID, "null argument");
+  if (a->nframes <= 0) return SOG_OK;
+  if (!a->atom_begin || !a->atom_count || !a->k_sq_max || !a->positions || !a->charges || !a->cells ||
+      !a->amp || !a->bw2)
+    return fail(SOG_ERR_INVALID, "missing input array");
+  if (a->nchannels < 1) return fail(SOG_ERR_INVALID, "nchannels must be >= 1");
+  if (a->n_gauss < 1 || a->n_gauss > kMaxGauss) return fail(SOG_ERR_INVALID, "n_gauss must be in [1, 64]");
+  DeviceGuard dg(p->d.device);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p->d.dtype == SOG_DTYPE_F64) return mesh_forward_impl<double>(p, a, st);
+  return mesh_forward_impl<float>(p, a, st);
+}

@@ -1,0 +1,386 @@
+"""Drop-in ``Gaussian`` long-range SOG core (src/sog/module/gaussian.py).
+
+Same constructor, parameter modes (raw / internal), tensor modes (owned /
+external / auto), defaults, validation errors, ``forward`` and
+``compute_bundle`` as the reference.  Every solve runs on the sm_100a library
+through the C ABI; there is no CPU path.
+
+Solvers:
+  * direct k-sum (the reference default; gaussian.py:1180-1337),
+  * particle-mesh with cardinal B-splines (``use_bspline_fft=True``,
+    ``bspline_order`` 4/5/6; the plugin's B-spline mesh, lmp/sog.cpp),
+  * particle-mesh with QuadS (``use_quads_fft=True``, quads_fft.py:209-326).
+Added keys (defaults keep the reference behaviour): ``use_bspline_fft``,
+``bspline_order``, ``mesh_k_convention`` ("physical" | "reference") and
+``mesh_alias_extent``.
+
+Deliberate differences, each documented in DESIGN.md:
+  * raw-mode ``amp`` tensors are not scaled in place (gaussian.py:236 does);
+  * ``use_quads_fft`` selects the mesh even for all-periodic batches (the
+    reference's batched direct gate shadows it, gaussian.py:444-548);
+  * the mesh wave vector is k = 2 pi cell^-1 m (the reciprocal vector; the
+    reference's mesh uses m cell^-1, quads_fft.py:255-257, which differs for
+    triclinic cells) unless ``mesh_k_convention="reference"``;
+  * explicit forces (and virial) are returned for every solver, including the
+    direct k-sum where the reference returns None.
+"""
+from __future__ import annotations
+
+import math
+from typing import Any, Dict, List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+from .grid import resolve_grid
+from .ops import Bucket, SolveFunction, SolveSpec
+
+E2_PER_ANGSTROM_TO_EV = 14.3996454784255
+SOG_DEFAULT_B = 2
+SOG_DEFAULT_SIGMA = 2.180230445405648
+SOG_DEFAULT_M = 12
+RCUT_TO_SIGMA = 1.9892536839080267
+
+HAS_PYTORCH_FINUFFT = False  # the NUFFT path is not built (third-party finufft)
+
+
+def _as_1d_tensor_keep_input(value: object) -> torch.Tensor:
+    if isinstance(value, torch.Tensor):
+        return value.reshape(-1)
+    return torch.as_tensor(value, dtype=torch.get_default_dtype()).reshape(-1)
+
+
+def _normalize_mode(value: str, valid: set, name: str) -> str:
+    mode = str(value).strip().lower()
+    if mode not in valid:
+        raise ValueError(f"`{name}` should be one of {sorted(valid)}, got {value!r}.")
+    return mode
+
+
+def _is_differentiable_tensor(value: object) -> bool:
+    return isinstance(value, torch.Tensor) and bool(value.requires_grad)
+
+
+def _compute_w0(r0: float, b: float, nterms: int = 500, tol: float = 1e-14) -> float:
+    """Real-space correction factor w0 (gaussian.py:44-64):
+    w0 = (1/G(1,r0)) (1/(2 ln(b) r0) - sum_i b^-i G(1, b^-i r0)),
+    G(s, r) = exp(-r^2/(2 s^2)) / sqrt(2 pi s^2); the sum stops once a term
+    falls below tol times the running absolute sum (after 10 terms)."""
+    def G(s, r):
+        return math.exp(-r * r / (2.0 * s * s)) / math.sqrt(2.0 * math.pi * s * s)
+    s = 0.0
+    abs_sum = 0.0
+    for i in range(1, nterms + 1):
+        bi = b ** (-i)
+        term = bi * G(1.0, bi * r0)
+        s += term
+        abs_sum += abs(term)
+        if i >= 10 and abs(term) < tol * max(abs_sum, 1e-30):
+            break
+    return (1.0 / G(1.0, r0)) * (1.0 / (2.0 * math.log(b) * r0) - s)
+
+
+class Gaussian(nn.Module):
+    """Gaussian long-range SOG core on B200.
+
+    kernel_param_mode: "raw" (amp is the raw coefficient, bandwidth is bw) or
+    "internal" (amp is the internal amplitude, bandwidth is bw^2).
+    kernel_tensor_mode: "owned" (nn.Parameter), "external" (bind the caller's
+    tensors) or "auto" (external when a differentiable tensor is given and
+    trainable=False).
+    """
+
+    _diag_count = 0
+
+    def __init__(self, n_dl: Optional[float] = None, amp: Optional[float] = None,
+                 bandwidth: Optional[torch.Tensor] = None, b: float = SOG_DEFAULT_B,
+                 sigma: float = SOG_DEFAULT_SIGMA, m: int = SOG_DEFAULT_M,
+                 rcut: Optional[float] = None, nlayers: int = 1,
+                 remove_self_interaction: bool = True,
+                 charge_neutral_lambda: Optional[float] = None, use_nufft: bool = False,
+                 nufft_eps: float = 1e-6, norm_factor: float = E2_PER_ANGSTROM_TO_EV,
+                 trainable: bool = True, max_cache_size: int = 8, nufft: Optional[bool] = None,
+                 kernel_param_mode: str = "raw", kernel_tensor_mode: str = "owned",
+                 use_cubes2_fft: bool = False, cubes2_phi_max: Optional[float] = None,
+                 cubes2_order: int = 4, use_quads_fft: bool = False, quads_order: int = 6,
+                 use_bspline_fft: bool = False, bspline_order: int = 6,
+                 mesh_k_convention: str = "physical", mesh_alias_extent: int = 8,
+                 **_kwargs: Any):
+        super().__init__()
+        if _kwargs:
+            raise TypeError(f"Unexpected keyword arguments: {', '.join(sorted(_kwargs.keys()))}")
+        param_mode = _normalize_mode(kernel_param_mode, {"raw", "internal"}, "kernel_param_mode")
+        tensor_mode = _normalize_mode(kernel_tensor_mode, {"owned", "external", "auto"},
+                                      "kernel_tensor_mode")
+        self.self_coeff = 0.0
+        if n_dl is not None:
+            v = float(n_dl)
+            if (not math.isfinite(v)) or v <= 0.0:
+                raise ValueError("`n_dl` should be a positive finite number.")
+            self.n_dl = v
+        else:
+            self.n_dl = None
+        if cubes2_phi_max is not None:
+            pv = float(cubes2_phi_max)
+            if not math.isfinite(pv) or pv <= 0.0:
+                raise ValueError("`cubes2_phi_max` should be a positive finite number.")
+        use_fastsog_conv = rcut is not None and rcut > 0
+        if use_fastsog_conv:
+            sigma = float(rcut) * int(nlayers) / RCUT_TO_SIGMA
+
+        dflt = torch.get_default_dtype()
+        if bandwidth is None:
+            if sigma <= 0.0:
+                raise ValueError("`sigma` should be positive when `bandwidth` is not provided.")
+            m_value = max(1, int(m))
+            if use_fastsog_conv:
+                sigma2 = sigma * sigma
+                b2 = float(b) * float(b)
+                bw2 = torch.zeros(m_value, dtype=dflt)
+                bw2[0] = sigma2
+                for mm in range(1, m_value):
+                    bw2[mm] = bw2[mm - 1] * b2
+            else:
+                bw = sigma * torch.pow(torch.tensor(float(b), dtype=dflt),
+                                       torch.arange(m_value, dtype=dflt))
+                bw2 = bw.square()
+            bw_check = bw2
+        else:
+            bw_in = _as_1d_tensor_keep_input(bandwidth)
+            bw_check = bw_in
+        if bw_check.numel() == 0:
+            raise ValueError("`bandwidth` should not be empty.")
+        if not torch.isfinite(bw_check).all():
+            raise ValueError("`bandwidth` should be finite.")
+        if torch.any(bw_check <= 0.0):
+            raise ValueError("`bandwidth` values should be positive.")
+        if bandwidth is not None:
+            bw2 = bw_in if param_mode == "internal" else bw_in.square()
+
+        if amp is None:
+            if b <= 0.0:
+                raise ValueError("`b` should be positive when `amp` is not provided.")
+            if use_fastsog_conv:
+                sigma2 = sigma * sigma
+                b2 = float(b) * float(b)
+                logb = math.log(float(b))
+                r0 = float(rcut) / sigma
+                w0 = _compute_w0(r0, float(b))
+                fac = 4.0 * math.pi * logb
+                amp_tensor = torch.zeros(m_value, dtype=dflt)
+                amp_tensor[0] = fac * w0 * sigma2
+                if m_value > 1:
+                    amp_tensor[1] = fac * sigma2 * b2
+                for mm in range(2, m_value):
+                    amp_tensor[mm] = amp_tensor[mm - 1] * b2
+                sum_b_inv = sum(float(b) ** (-mm) for mm in range(1, m_value))
+                self.self_coeff = (logb / (math.sqrt(2.0 * math.pi) * sigma)) * (w0 + sum_b_inv)
+            else:
+                coef1 = float(4.0 * math.pi * math.log(float(b)))
+                amp_tensor = torch.full_like(bw2, fill_value=coef1)
+        else:
+            amp_tensor = _as_1d_tensor_keep_input(amp)
+            self.self_coeff = 0.0
+        if amp_tensor.numel() == 0:
+            raise ValueError("`amp` should not be empty.")
+        if not torch.isfinite(amp_tensor).all():
+            raise ValueError("`amp` should be finite.")
+        if amp_tensor.numel() == 1 and bw2.numel() > 1:
+            amp_tensor = amp_tensor.expand_as(bw2).clone()
+        elif amp_tensor.numel() != bw2.numel():
+            raise ValueError("`amp` should be scalar or have the same length as `bandwidth`.")
+        if ((param_mode == "raw") or (amp is None)) and not use_fastsog_conv:
+            # out of place (the caller's tensor is left unchanged), keeping the
+            # dtype an in-place `*=` would keep (gaussian.py:236)
+            amp_tensor = (amp_tensor * bw2).to(amp_tensor.dtype)
+
+        use_external = tensor_mode == "external"
+        if tensor_mode == "auto":
+            use_external = (not trainable) and (_is_differentiable_tensor(amp)
+                                                or _is_differentiable_tensor(bandwidth))
+        if use_external:
+            self.amp = amp_tensor
+            self.bandwidth = bw2
+        else:
+            self.amp = nn.Parameter(amp_tensor.detach().clone(), requires_grad=trainable)
+            self.bandwidth = nn.Parameter(bw2.detach().clone(), requires_grad=trainable)
+
+        self.remove_self_interaction = bool(remove_self_interaction)
+        self.charge_neutral_lambda = charge_neutral_lambda
+        self.use_nufft = bool(use_nufft if nufft is None else nufft)
+        self.nufft_eps = float(nufft_eps)
+        self.norm_factor = float(norm_factor)
+        self.use_cubes2_fft = bool(use_cubes2_fft)
+        self.cubes2_phi_max = float(cubes2_phi_max) if cubes2_phi_max is not None else None
+        self.cubes2_order = int(cubes2_order)
+        self.use_quads_fft = bool(use_quads_fft)
+        self.quads_order = int(quads_order)
+        self.use_bspline_fft = bool(use_bspline_fft)
+        self.bspline_order = int(bspline_order)
+        if self.use_bspline_fft and self.bspline_order not in (4, 5, 6):
+            raise ValueError("`bspline_order` should be 4, 5 or 6.")
+        if self.use_quads_fft and self.quads_order not in (4, 6):
+            raise ValueError(f"Unsupported QuadS order: {self.quads_order}. Supported: (4, 6).")
+        self.mesh_k_convention = _normalize_mode(mesh_k_convention, {"physical", "reference"},
+                                                 "mesh_k_convention")
+        self.mesh_alias_extent = int(mesh_alias_extent)
+        self.rcut = float(rcut) if rcut is not None else None
+        self.b = float(b)
+        self._max_cache_size = max(1, int(max_cache_size))
+
+    # ------------------------------------------------------------------
+    def forward(self, q: torch.Tensor, r: torch.Tensor, cell: Optional[torch.Tensor],
+                batch: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return self.compute_bundle(q=q, r=r, cell=cell, batch=batch, compute_force=False,
+                                   compute_virial=False)["energy"]
+
+    @staticmethod
+    def _greedy_group_by_nloc(nloc_per_frame: List[int], max_waste: float):
+        """Greedy grouping by atom count (gaussian.py:347-378); kept for API
+        parity — the GPU direct solver batches ragged frames without padding."""
+        indexed = sorted(enumerate(nloc_per_frame), key=lambda x: x[1])
+        groups = []
+        cur = [indexed[0]]
+        cur_max = cur_sum = indexed[0][1]
+        for idx, nl in indexed[1:]:
+            new_max = max(cur_max, nl)
+            new_sum = cur_sum + nl
+            waste = ((len(cur) + 1) * new_max - new_sum) / new_sum if new_sum > 0 else 0.0
+            if waste <= max_waste:
+                cur.append((idx, nl))
+                cur_max, cur_sum = new_max, new_sum
+            else:
+                groups.append(cur)
+                cur = [(idx, nl)]
+                cur_max = cur_sum = nl
+        groups.append(cur)
+        return groups
+
+    def _resolve_direct_n_dl(self, dtype: torch.dtype, device: torch.device) -> float:
+        """n_dl of the direct k-sum (gaussian.py:847-859)."""
+        if self.n_dl is not None:
+            return float(self.n_dl)
+        bw_min = self.bandwidth.detach().to(dtype=dtype).min().item()
+        kmax = math.sqrt(2.0 * math.log(1.0 / 1e-5) / max(bw_min, 1e-30))
+        return 2.0 * math.pi / max(kmax, 1e-30)
+
+    def _mesh_kind(self):
+        if self.use_cubes2_fft:
+            raise NotImplementedError("the CubeS2 mesh (use_cubes2_fft) is not built in sog_b200; "
+                                      "use use_bspline_fft or use_quads_fft")
+        if self.use_bspline_fft:
+            return _lib.SPLINE_BSPLINE, self.bspline_order
+        if self.use_quads_fft:
+            return _lib.SPLINE_QUADS, self.quads_order
+        return None
+
+    def compute_bundle(self, q: torch.Tensor, r: torch.Tensor, cell: Optional[torch.Tensor],
+                       batch: Optional[torch.Tensor] = None, compute_force: bool = False,
+                       compute_virial: bool = False) -> Dict[str, Optional[torch.Tensor]]:
+        if q.dim() == 1:
+            q = q.unsqueeze(1)
+        n, d = r.shape
+        assert d == 3, "r dimension error"
+        assert n == q.size(0), "q dimension error"
+        if batch is None:
+            batch = torch.zeros(n, dtype=torch.int64, device=r.device)
+        if cell is not None and (cell.dim() != 3 or cell.shape[-2:] != (3, 3)):
+            raise ValueError(f"`cell` should be [nbatch, 3, 3], got {tuple(cell.shape)}")
+        if r.device.type != "cuda":
+            raise _lib.SogError("sog_b200 runs on CUDA devices only; move r, q, cell and batch "
+                                "to a CUDA device")
+        need_force = bool(compute_force or compute_virial)
+        dt = r.dtype
+        dev = r.device
+        bids = torch.unique(batch).tolist()
+        if len(bids) == 0:
+            z = torch.zeros(0, dtype=dt, device=dev)
+            return {"energy": z, "forces": torch.zeros(n, 3, dtype=dt, device=dev) if need_force else None,
+                    "virial": torch.zeros(0, 3, 3, dtype=dt, device=dev) if compute_virial else None,
+                    "used_explicit_derivatives": need_force}
+        if cell is None:
+            raise NotImplementedError("the real-space path (cell=None) is not built yet")
+        cell_h = cell.detach().to("cpu", torch.float64)
+        vols = torch.abs(torch.linalg.det(cell_h))
+        eps = torch.finfo(cell.dtype).eps
+        for bid in bids:
+            if not bool(vols[bid] > eps):
+                raise NotImplementedError("non-periodic frames (singular cell) need the real-space "
+                                          "path, which is not built yet")
+
+        # ---- atoms grouped by frame (contiguous), in the order of `bids` ----
+        counts = torch.bincount(batch, minlength=max(bids) + 1)
+        sorted_ok = bool((batch[1:] >= batch[:-1]).all()) if n > 1 else True
+        perm = None
+        if not sorted_ok:
+            perm = torch.argsort(batch, stable=True)
+        counts_h = counts.tolist()
+        begins, acc = [], 0
+        for bid in bids:
+            begins.append(acc)
+            acc += counts_h[bid]
+        nat = [counts_h[bid] for bid in bids]
+        fidx = torch.repeat_interleave(torch.arange(len(bids), device=dev),
+                                       torch.tensor(nat, device=dev))
+        r_s = r if perm is None else r.index_select(0, perm)
+        q_s = q if perm is None else q.index_select(0, perm)
+        bid_t = torch.tensor(bids, device=dev, dtype=torch.long)
+        cells = cell.detach().to(dt).index_select(0, bid_t).contiguous()
+
+        amp = self.amp.to(dtype=dt, device=dev)
+        bw2 = self.bandwidth.to(dtype=dt, device=dev)
+        mesh = self._mesh_kind()
+        spec = SolveSpec(kind="mesh" if mesh else "direct", buckets=[], nframes=len(bids),
+                         cells=cells, frame_of_atom=fidx, norm_factor=self.norm_factor,
+                         self_coeff=self.self_coeff, remove_self=self.remove_self_interaction,
+                         k0_correction=True, charge_neutral_lambda=(
+                             float(self.charge_neutral_lambda)
+                             if self.charge_neutral_lambda is not None and self.charge_neutral_lambda > 0
+                             else None))
+        lens = torch.linalg.norm(cell_h, dim=2)
+        if mesh:
+            spline, order = mesh
+            spec.spline, spec.order = spline, order
+            spec.kconv = (_lib.KCONV_REFERENCE if self.mesh_k_convention == "reference"
+                          else _lib.KCONV_PHYSICAL)
+            spec.alias_extent = self.mesh_alias_extent
+            groups: Dict[Tuple[int, int, int], Bucket] = {}
+            for j, bid in enumerate(bids):
+                lx, ly, lz = (float(v) for v in lens[bid])
+                nx, ny, nz, ksm = resolve_grid(
+                    lx, ly, lz, n_dl=self.n_dl if self.cubes2_phi_max is None else None,
+                    cubes2_phi_max=self.cubes2_phi_max, r_c=self.rcut, b=self.b,
+                    spline_order=order if spline == _lib.SPLINE_QUADS else (4 if order < 6 else 6),
+                    min_grid=8)
+                bk = groups.setdefault((nx, ny, nz), Bucket([], [], [], [], dims=(nx, ny, nz)))
+                bk.frames.append(j)
+                bk.atom_begin.append(begins[j])
+                bk.atom_count.append(nat[j])
+                bk.k_sq_max.append(ksm)
+            spec.buckets = list(groups.values())
+        else:
+            n_dl = self._resolve_direct_n_dl(dt, dev)
+            bk = Bucket([], [], [], [], nk=[])
+            for j, bid in enumerate(bids):
+                nk = tuple(max(1, int(float(v) / n_dl)) for v in lens[bid])
+                bk.frames.append(j)
+                bk.atom_begin.append(begins[j])
+                bk.atom_count.append(nat[j])
+                bk.k_sq_max.append((2.0 * math.pi / n_dl) ** 2)
+                bk.nk.append(nk)
+            spec.buckets = [bk]
+
+        energy, forces, virial = SolveFunction.apply(q_s, r_s, amp, bw2, spec, need_force,
+                                                     bool(compute_virial))
+        if forces is not None and perm is not None:
+            f_out = torch.empty_like(forces)
+            f_out.index_copy_(0, perm, forces)
+            forces = f_out
+        return {"energy": energy, "forces": forces if need_force else None,
+                "virial": virial if compute_virial else None,
+                "used_explicit_derivatives": need_force}
+
+    def __repr__(self) -> str:
+        return (f"Gaussian(n_dl={self.n_dl}, remove_self_interaction={self.remove_self_interaction}, "
+                f"use_nufft=False)")

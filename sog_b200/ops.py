@@ -1,0 +1,147 @@
+"""Autograd functions around the C ABI.
+
+One forward launch computes the energy together with every derivative the
+graph will need (forces when positions require grad or explicit forces are
+asked for, dE/dq when charges do, dE/d(amp, bw2) when the kernel parameters
+do), so the backward is a per-frame scaling of saved results.  This is the
+hand-written backward of src/sog/module/cubes2_fft.py:746-869 generalised to
+all solvers: dE/dr is the ik-differentiated force (as there), dE/dq the
+gathered potential plus self and k=0 terms, dE/d(amp, bw2) the M-vector
+k-space reductions.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import List, Optional, Tuple
+
+import torch
+
+from . import _lib
+
+
+@dataclass
+class Bucket:
+    """Frames solved by one C-ABI call (same mesh, or the direct solver)."""
+    frames: List[int]            # positions in the output energy vector
+    atom_begin: List[int]
+    atom_count: List[int]
+    k_sq_max: List[float]
+    dims: Optional[Tuple[int, int, int]] = None   # mesh
+    nk: Optional[List[Tuple[int, int, int]]] = None  # direct
+
+
+@dataclass
+class SolveSpec:
+    kind: str                    # "mesh" | "direct"
+    buckets: List[Bucket]
+    nframes: int
+    cells: torch.Tensor          # [nf, 3, 3] (frames in output order), compute dtype
+    frame_of_atom: torch.Tensor  # [N] int64 output-frame index of each (sorted) atom
+    spline: int = _lib.SPLINE_BSPLINE
+    order: int = 6
+    kconv: int = _lib.KCONV_PHYSICAL
+    alias_extent: int = 8
+    norm_factor: float = 14.3996454784255
+    self_coeff: float = 0.0
+    remove_self: bool = True
+    k0_correction: bool = True
+    charge_neutral_lambda: Optional[float] = None
+    cache: dict = field(default_factory=dict)
+
+
+def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Tensor,
+               bw2: torch.Tensor, *, want_force: bool, want_pot: bool, want_grad: bool,
+               want_virial: bool):
+    """Launch every bucket of ``spec``; returns (energy, forces, pot, gamp, gbw2, virial)."""
+    dev = r.device
+    dt = r.dtype
+    nf = spec.nframes
+    M = amp.numel()
+    N = r.shape[0]
+    C = q.shape[1]
+    r = r.contiguous()
+    q = q.contiguous()
+    amp = amp.contiguous()
+    bw2 = bw2.contiguous()
+    energy = torch.empty(nf, dtype=dt, device=dev)
+    forces = torch.zeros(N, 3, dtype=dt, device=dev) if want_force else None
+    pot = torch.zeros(N, C, dtype=dt, device=dev) if want_pot else None
+    gamp = torch.empty(nf, M, dtype=dt, device=dev) if want_grad else None
+    gbw2 = torch.empty(nf, M, dtype=dt, device=dev) if want_grad else None
+    vir = torch.empty(nf, 3, 3, dtype=dt, device=dev) if want_virial else None
+    dcode = _lib.dtype_code(dt)
+    single = len(spec.buckets) == 1 and spec.buckets[0].frames == list(range(nf))
+    for b in spec.buckets:
+        if single:
+            cells_b, e_b, ga_b, gb_b, v_b = spec.cells, energy, gamp, gbw2, vir
+        else:
+            idx = torch.tensor(b.frames, device=dev, dtype=torch.long)
+            cells_b = spec.cells.index_select(0, idx).contiguous()
+            e_b = torch.empty(len(b.frames), dtype=dt, device=dev)
+            ga_b = torch.empty(len(b.frames), M, dtype=dt, device=dev) if want_grad else None
+            gb_b = torch.empty(len(b.frames), M, dtype=dt, device=dev) if want_grad else None
+            v_b = torch.empty(len(b.frames), 3, 3, dtype=dt, device=dev) if want_virial else None
+        common = dict(atom_begin=b.atom_begin, atom_count=b.atom_count, k_sq_max=b.k_sq_max,
+                      positions=r, charges=q, cells=cells_b, amp=amp, bw2=bw2,
+                      norm_factor=spec.norm_factor, self_coeff=spec.self_coeff,
+                      remove_self=spec.remove_self, k0_correction=spec.k0_correction,
+                      charge_neutral_lambda=spec.charge_neutral_lambda, energy=e_b,
+                      forces=forces, potential=pot, grad_amp=ga_b, grad_bw2=gb_b, virial=v_b)
+        if spec.kind == "mesh":
+            plan = _lib.PLANS.get(dev.index if dev.index is not None else torch.cuda.current_device(),
+                                  dcode, spec.spline, spec.order, b.dims, spec.kconv,
+                                  spec.alias_extent)
+            _lib.mesh_forward(plan, **common)
+        else:
+            ctx = _lib.direct_ctx(dev.index if dev.index is not None else torch.cuda.current_device(),
+                                  dcode)
+            _lib.direct_forward(ctx, nk=b.nk, **common)
+        if not single:
+            energy.index_copy_(0, idx, e_b)
+            if want_grad:
+                gamp.index_copy_(0, idx, ga_b)
+                gbw2.index_copy_(0, idx, gb_b)
+            if want_virial:
+                vir.index_copy_(0, idx, v_b)
+    return energy, forces, pot, gamp, gbw2, vir
+
+
+class SolveFunction(torch.autograd.Function):
+    """energy[nf] = SOG(q, r; amp, bw2); explicit forces / virial as extra,
+    non-differentiable outputs."""
+
+    @staticmethod
+    def forward(ctx, q, r, amp, bw2, spec: SolveSpec, want_force_out: bool, want_virial_out: bool):
+        need_q, need_r, need_a, need_b = ctx.needs_input_grad[:4]
+        want_grad = bool(need_a or need_b)
+        want_force = bool(need_r or want_force_out)
+        energy, forces, pot, gamp, gbw2, vir = run_solver(
+            spec, q, r, amp, bw2, want_force=want_force, want_pot=bool(need_q),
+            want_grad=want_grad, want_virial=bool(want_virial_out))
+        ctx.spec_frame = spec.frame_of_atom
+        ctx.save_for_backward(forces if need_r else None, pot, gamp, gbw2)
+        f_out = forces if want_force_out else None
+        v_out = vir if want_virial_out else None
+        outs = [energy, f_out, v_out]
+        nd = [t for t in (f_out, v_out) if t is not None]
+        if nd:
+            ctx.mark_non_differentiable(*nd)
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, gE, gF, gV):
+        forces, pot, gamp, gbw2 = ctx.saved_tensors
+        grad_q = grad_r = grad_a = grad_b = None
+        if gE is None:
+            return None, None, None, None, None, None, None
+        ga = gE.index_select(0, ctx.spec_frame)
+        if ctx.needs_input_grad[0] and pot is not None:
+            grad_q = pot * ga[:, None]
+        if ctx.needs_input_grad[1] and forces is not None:
+            grad_r = -forces * ga[:, None]
+        if ctx.needs_input_grad[2] and gamp is not None:
+            grad_a = (gE[:, None] * gamp).sum(0)
+        if ctx.needs_input_grad[3] and gbw2 is not None:
+            grad_b = (gE[:, None] * gbw2).sum(0)
+        return grad_q, grad_r, grad_a, grad_b, None, None, None
