@@ -314,8 +314,16 @@ int direct_impl(sog_direct *d, const sog_direct_args *a, cudaStream_t st) {
   k_frame_setup<T><<<nblk(nf, 128), 128, 0, st>>>((const T *)a->cells, fhd, geom, nf, SOG_KCONV_PHYSICAL,
                                                   1, 1, 1, d->status.as<unsigned>());
   after(tr, st, "frame_setup");
-  k_qsums<T><<<dim3(nf, nch), 256, 0, st>>>((const T *)a->charges, nch, geom, d->qsum.as<double>());
+  const int qs = (int)std::max<int64_t>(1, std::min<int64_t>(256, (maxat + 16383) / 16384));
+  if (d->qpart.reserve(sizeof(double) * 2 * (int64_t)nf * nch * qs) ||
+      d->redtmp.reserve(sizeof(double) * std::max(reduce_tmp_elems(nf, nch, kb, 2),
+                                                   reduce_tmp_elems(nf, nch, kb, nx_acc))))
+    return fail(SOG_ERR_NOMEM, "device allocation failed (direct)");
+  k_qsums<T><<<dim3(nf, nch, qs), 256, 0, st>>>((const T *)a->charges, nch, geom, d->qpart.as<double>());
+  k_reduce_parts<<<dim3(nf, nch, 1), 256, 0, st>>>(d->qpart.as<double>(), nf, nch, qs, 2, 2,
+                                                  d->qsum.as<double>());
   after(tr, st, "qsums");
+  count_launch();
   DirArgs da;
   da.geom = geom;
   da.nk = nkd;
@@ -342,11 +350,15 @@ int direct_impl(sog_direct *d, const sog_direct_args *a, cudaStream_t st) {
                                                                   (const T *)a->charges, a->norm_factor,
                                                                   (T *)a->forces, (T *)a->potential);
   if ((a->forces || a->potential) && maxat > 0) after(tr, st, "direct_atoms");
-  k_reduce_parts<<<dim3(nf, nch), 256, 0, st>>>(da.part, nf, nch, kb, 2, 2, redE);
+  reduce_parts(da.part, nf, nch, kb, 2, 2, redE, d->redtmp.as<double>(), st);
   after(tr, st, "reduce");
+  if (reduce_split(kb) > 1) count_launch();
   if (want_grad || want_vir)
-    k_reduce_parts<<<dim3(nf, nch), 256, 0, st>>>(da.partx, nf, nch, kb, nx_acc, nx_acc, redX);
-  if (want_grad || want_vir) after(tr, st, "reduce_extra");
+    reduce_parts(da.partx, nf, nch, kb, nx_acc, nx_acc, redX, d->redtmp.as<double>(), st);
+  if (want_grad || want_vir) {
+    after(tr, st, "reduce_extra");
+    if (reduce_split(kb) > 1) count_launch();
+  }
   FinalArgs fa;
   std::memset(&fa, 0, sizeof(fa));
   fa.geom = geom;
@@ -398,7 +410,8 @@ extern "C" int sog_direct_create(sog_direct **out, int dtype, int device) {
 extern "C" int sog_direct_destroy(sog_direct *d) {
   if (!d) return SOG_OK;
   DeviceGuard dg(d->device);
-  DevBuf *bufs[] = {&d->frames_host_dev, &d->geom, &d->modes, &d->sfac, &d->part, &d->qsum, &d->status};
+  DevBuf *bufs[] = {&d->frames_host_dev, &d->geom, &d->modes, &d->sfac, &d->part, &d->qsum, &d->status,
+                    &d->qpart, &d->redtmp};
   for (DevBuf *b : bufs) b->release();
   d->up.release();
   d->tr.release();

@@ -2,6 +2,7 @@
 // charge sums, deterministic partial-sum reduction, energy / gradient /
 // virial finalisation and the per-atom potential epilogue.
 #pragma once
+#include <algorithm>
 #include <cfloat>
 
 #include "common.cuh"
@@ -86,14 +87,17 @@ __global__ void k_frame_setup(const T *__restrict__ cells, const FrameHost *__re
   geom[f] = g;
 }
 
-// per (frame, channel): sum q and sum q^2 (fixed-order tree reduction)
+// per (frame, channel, split): partial sums of q and q^2 over a contiguous
+// chunk of the frame's atoms (fixed-order tree); reduced by reduce_parts.
 template <typename T>
 __global__ void k_qsums(const T *__restrict__ q, int nch, const FrameGeom *__restrict__ geom,
-                        double *__restrict__ out) {
-  const int f = blockIdx.x, c = blockIdx.y;
+                        double *__restrict__ part) {
+  const int f = blockIdx.x, c = blockIdx.y, z = blockIdx.z, nz = gridDim.z;
   const FrameGeom &g = geom[f];
+  const int64_t chunk = ((int64_t)g.natoms + nz - 1) / nz;
+  const int64_t i0 = (int64_t)z * chunk, i1 = min((int64_t)g.natoms, i0 + chunk);
   double s1 = 0.0, s2 = 0.0;
-  for (int i = threadIdx.x; i < g.natoms; i += blockDim.x) {
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
     double v = (double)q[(g.atom_begin + i) * nch + c];
     if (!isfinite(v)) v = 0.0;
     s1 += v;
@@ -108,32 +112,62 @@ __global__ void k_qsums(const T *__restrict__ q, int nch, const FrameGeom *__res
     __syncthreads();
   }
   if (threadIdx.x == 0) {
-    out[((int64_t)f * nch + c) * 2 + 0] = r1[0];
-    out[((int64_t)f * nch + c) * 2 + 1] = r2[0];
+    double *p = part + (((int64_t)c * gridDim.x + f) * nz + z) * 2;
+    p[0] = r1[0];
+    p[1] = r2[0];
   }
 }
 
 // ------------------------------------------------------------------------
 // reductions and finalisation
 // ------------------------------------------------------------------------
-// out[(f*nch + c)*nacc + i] = sum_b part[((c*nf + f)*nblk + b)*stride + i]
+// Sums partial results part[((c*nf + f)*nblk + b)*stride + i] over b in fixed
+// order.  With gridDim.z > 1 each z sums a contiguous chunk of b and writes
+// the same partial layout (nblk = gridDim.z, stride = nacc) for a second pass;
+// with gridDim.z == 1 it writes out[(f*nch + c)*nacc + i].
 __global__ void k_reduce_parts(const double *__restrict__ part, int nf, int nch, int64_t nblk,
                                int stride, int nacc, double *__restrict__ out) {
-  const int f = blockIdx.x, c = blockIdx.y;
+  const int f = blockIdx.x, c = blockIdx.y, z = blockIdx.z, nz = gridDim.z;
+  const int64_t chunk = (nblk + nz - 1) / nz;
+  const int64_t b0 = (int64_t)z * chunk, b1 = min(nblk, b0 + chunk);
   __shared__ double sh[256];
   for (int i = 0; i < nacc; ++i) {
     double s = 0.0;
     const double *p = part + (((int64_t)c * nf + f) * nblk) * stride + i;
-    for (int64_t b = threadIdx.x; b < nblk; b += blockDim.x) s += p[b * stride];
+    for (int64_t b = b0 + threadIdx.x; b < b1; b += blockDim.x) s += p[b * stride];
     sh[threadIdx.x] = s;
     __syncthreads();
     for (int o = blockDim.x / 2; o > 0; o >>= 1) {
       if (threadIdx.x < o) sh[threadIdx.x] += sh[threadIdx.x + o];
       __syncthreads();
     }
-    if (threadIdx.x == 0) out[((int64_t)f * nch + c) * nacc + i] = sh[0];
+    if (threadIdx.x == 0) {
+      if (nz > 1) out[(((int64_t)c * nf + f) * nz + z) * nacc + i] = sh[0];
+      else out[((int64_t)f * nch + c) * nacc + i] = sh[0];
+    }
     __syncthreads();
   }
+}
+
+// Two-level deterministic reduction (split chosen from the sizes only).
+inline int reduce_split(int64_t nblk) {
+  int64_t s = (nblk + 2047) / 2048;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(s, 512));
+}
+
+inline void reduce_parts(const double *part, int nf, int nch, int64_t nblk, int stride, int nacc,
+                         double *out, double *tmp, cudaStream_t st) {
+  const int split = reduce_split(nblk);
+  if (split == 1) {
+    k_reduce_parts<<<dim3(nf, nch, 1), 256, 0, st>>>(part, nf, nch, nblk, stride, nacc, out);
+    return;
+  }
+  k_reduce_parts<<<dim3(nf, nch, split), 256, 0, st>>>(part, nf, nch, nblk, stride, nacc, tmp);
+  k_reduce_parts<<<dim3(nf, nch, 1), 256, 0, st>>>(tmp, nf, nch, split, nacc, nacc, out);
+}
+
+inline int64_t reduce_tmp_elems(int nf, int nch, int64_t nblk, int nacc) {
+  return (int64_t)nf * nch * reduce_split(nblk) * nacc;
 }
 
 struct FinalArgs {

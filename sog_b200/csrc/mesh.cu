@@ -979,8 +979,15 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
         (const T *)a->positions, (const T *)a->charges, nch, geom, ag, k0, v0, nslots,
         p->s_anchor.as<int4>(), p->s_t.as<T>(), p->s_q.as<T>(), p->s_atom.as<int32_t>());
   if (nslots > 0) after(tr, st, "atom_sorted");
-  k_qsums<T><<<dim3(nf, nch), 256, 0, st>>>((const T *)a->charges, nch, geom, p->qsum.as<double>());
-  after(tr, st, "qsums");
+  {
+    const int qs = (int)std::max<int64_t>(1, std::min<int64_t>(256, (maxat + 16383) / 16384));
+    if (p->qpart.reserve(sizeof(double) * 2 * (int64_t)nf * nch * qs))
+      return fail(SOG_ERR_NOMEM, "device allocation failed");
+    k_qsums<T><<<dim3(nf, nch, qs), 256, 0, st>>>((const T *)a->charges, nch, geom, p->qpart.as<double>());
+    k_reduce_parts<<<dim3(nf, nch, 1), 256, 0, st>>>(p->qpart.as<double>(), nf, nch, qs, 2, 2,
+                                                    p->qsum.as<double>());
+    after(tr, st, "qsums", 2);
+  }
 
   // ---- buffers ----
   const bool want_force = a->forces != nullptr;
@@ -995,7 +1002,9 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
       (nfield && (p->fspec.reserve(sizeof(C) * nh * nf * nfield) ||
                   p->freal.reserve(sizeof(T) * ng * nf * nfield))) ||
       ((want_grad || want_vir) && p->partX.reserve(sizeof(double) * nx_acc * (int64_t)ks_blocks * nf * nch)) ||
-      p->red.reserve(sizeof(double) * ((int64_t)nf * nch * (2 + nx_acc) + (int64_t)nf * 4)))
+      p->red.reserve(sizeof(double) * ((int64_t)nf * nch * (2 + nx_acc) + (int64_t)nf * 4)) ||
+      p->redtmp.reserve(sizeof(double) * std::max(reduce_tmp_elems(nf, nch, ks_blocks, 2),
+                                                  reduce_tmp_elems(nf, nch, ks_blocks, nx_acc))))
     return fail(SOG_ERR_NOMEM, "device allocation failed (mesh buffers)");
 
   QuadsCoef qc;
@@ -1076,12 +1085,11 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   double *redE = p->red.as<double>();
   double *redX = redE + (int64_t)nf * nch * 2;
   double *fscal = redX + (int64_t)nf * nch * nx_acc;
-  k_reduce_parts<<<dim3(nf, nch), 256, 0, st>>>(p->partE.as<double>(), nf, nch, ks_blocks, 2, 2, redE);
-  after(tr, st, "reduce");
+  reduce_parts(p->partE.as<double>(), nf, nch, ks_blocks, 2, 2, redE, p->redtmp.as<double>(), st);
+  after(tr, st, "reduce", reduce_split(ks_blocks) > 1 ? 2 : 1);
   if (want_grad || want_vir)
-    k_reduce_parts<<<dim3(nf, nch), 256, 0, st>>>(p->partX.as<double>(), nf, nch, ks_blocks, nx_acc,
-                                                  nx_acc, redX);
-  if (want_grad || want_vir) after(tr, st, "reduce_extra");
+    reduce_parts(p->partX.as<double>(), nf, nch, ks_blocks, nx_acc, nx_acc, redX, p->redtmp.as<double>(), st);
+  if (want_grad || want_vir) after(tr, st, "reduce_extra", reduce_split(ks_blocks) > 1 ? 2 : 1);
   FinalArgs fa;
   fa.geom = geom;
   fa.redE = redE;
@@ -1191,7 +1199,7 @@ extern "C" int sog_plan_destroy(sog_plan *p) {
                     &p->tab.sy, &p->tab.sz, &p->frames_host_dev, &p->geom, &p->status, &p->keys0,
                     &p->vals0, &p->keys1, &p->vals1, &p->hist, &p->scan_tmp, &p->bin_start,
                     &p->s_atom, &p->s_anchor, &p->s_t, &p->s_q, &p->qsum, &p->rho, &p->spec,
-                    &p->fspec, &p->freal, &p->partE, &p->partX, &p->red};
+                    &p->fspec, &p->freal, &p->partE, &p->partX, &p->red, &p->redtmp, &p->qpart};
   for (DevBuf *b : bufs) b->release();
   p->up.release();
   p->tr.release();

@@ -76,6 +76,7 @@ struct sog_plan {
   sogb::DevBuf rho, spec, fspec, freal;
   sogb::DevBuf partE, partX;    // kspace partial sums
   sogb::DevBuf red;             // reduced sums and per-frame scalars
+  sogb::DevBuf redtmp, qpart;   // two-level reduction scratch, charge-sum partials
   sogb::PinnedBuf up;
   sogb::Tracer tr;
   int nb_x = 0, nb_y = 0, nb_z = 0;  // sort bins per axis
@@ -83,7 +84,7 @@ struct sog_plan {
 
 struct sog_direct {
   int dtype = 0, device = 0;
-  sogb::DevBuf frames_host_dev, geom, modes, sfac, part, qsum, status;
+  sogb::DevBuf frames_host_dev, geom, modes, sfac, part, qsum, status, qpart, redtmp;
   sogb::PinnedBuf up;
   sogb::Tracer tr;
 };

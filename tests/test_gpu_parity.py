@@ -189,7 +189,7 @@ def test_quads_physical_convention_matches_oracle_triclinic():
     g = Gaussian(n_dl=0.7, amp=torch.tensor(amp), bandwidth=torch.tensor(bw * bw),
                  kernel_param_mode="internal", use_quads_fft=True, quads_order=6).to(DEV)
     out = g.compute_bundle(q=_t(q), r=_t(r), cell=_t(cell[None]), compute_force=True)
-    assert _rel(out["energy"].cpu().numpy(), ref["energy"]) < E_TOL
+    assert _rel(out["energy"].detach().cpu().numpy(), ref["energy"]) < E_TOL
     assert np.abs(out["forces"].cpu().numpy() - ref["forces"]).max() < F_TOL
 
 
@@ -204,7 +204,7 @@ def test_fp32_mode_within_1e5():
     out = g.compute_bundle(q=_t(q, torch.float32), r=_t(r, torch.float32),
                            cell=_t(cell[None], torch.float32), compute_force=True)
     assert out["energy"].dtype == torch.float32
-    assert _rel(out["energy"].cpu().numpy(), ref["energy"]) < 1e-5
+    assert _rel(out["energy"].detach().cpu().numpy(), ref["energy"]) < 1e-5
     assert _rel(out["forces"].cpu().numpy(), ref["forces"]) < 1e-5
 
 
@@ -216,7 +216,7 @@ def test_config2_full_size_bspline6_vs_oracle_and_deterministic():
                  kernel_param_mode="internal", use_bspline_fft=True, bspline_order=6).to(DEV)
     outs = [g.compute_bundle(q=_t(c["q"]), r=_t(c["r"]), cell=_t(c["cell"]), compute_force=True)
             for _ in range(2)]
-    assert _rel(outs[0]["energy"].cpu().numpy(), ref["energy"]) < E_TOL
+    assert _rel(outs[0]["energy"].detach().cpu().numpy(), ref["energy"]) < E_TOL
     assert np.abs(outs[0]["forces"].cpu().numpy() - ref["forces"]).max() < F_TOL
     assert torch.equal(outs[0]["energy"], outs[1]["energy"])
     assert torch.equal(outs[0]["forces"], outs[1]["forces"])
