@@ -46,6 +46,8 @@ struct FrameGeom {
   int64_t slot_base;  // first sorted slot of the frame
   int32_t natoms;
   int32_t pad;        // 1: B-spline aliases may fall inside the k_max sphere
+  int32_t ortho;      // 1: kmat diagonal (k_a depends on m_a only)
+  int32_t pad2;
 };
 
 // Per-frame host-side description uploaded with each call.

@@ -1,0 +1,177 @@
+// Register-resident Stockham FFT for power-of-two lengths (radix 8/4/2).
+//
+// Each thread of a transform keeps EPT = 8 elements x[t + e*TPT] (TPT = n/8)
+// in registers for the whole transform.  In a stage of radix R a thread runs
+// 8/R butterflies j = t + u*TPT on its own elements, writes the outputs to
+// their Stockham positions in shared memory and, after a barrier, reads back
+// x[t + e*TPT] for the next stage.  The first stage takes its inputs straight
+// from HBM and the last stage leaves the outputs in registers in natural order
+// (thread t holds X[t + e*TPT]), so a pass costs one HBM read, one HBM write and
+// (stages - 1) shared-memory exchanges.
+#pragma once
+#include "fft.cuh"
+
+namespace sogb {
+
+constexpr int kEPT = 8;
+
+inline bool is_pow2(int n) { return n >= 8 && (n & (n - 1)) == 0; }
+
+template <typename T, int DIR, int R>
+__device__ __forceinline__ void dftR(cplx_t<T> *a) {
+  if (R == 2) dft2<T, DIR>(a);
+  else if (R == 4) dft4<T, DIR>(a);
+  else dft8<T, DIR>(a);
+}
+
+// Shared-memory slot of element i of a transform whose elements are sj slots
+// apart.  A quarter warp issues eight 16-byte accesses; column tiles of width
+// sj >= 8 put one full row in it and need no padding.  Rows (sj == 1) and
+// narrow tiles (PAD) skip one element-row every 8 so that the stride-8
+// Stockham writes of a quarter warp fall in distinct banks.
+template <bool PAD>
+__device__ __forceinline__ int sidx(int i, int sj) { return PAD ? (i + (i >> 3)) * sj : i * sj; }
+
+// One radix-R stage on the registers v; Ns = product of earlier radices.
+template <typename T, int DIR, int R, bool PAD>
+__device__ __forceinline__ void reg_stage(cplx_t<T> (&v)[kEPT], int t, int TPT, int n, int Ns,
+                                          const cplx_t<T> *__restrict__ tw, cplx_t<T> *sbase,
+                                          int sj, bool last) {
+  constexpr int B = kEPT / R;
+#pragma unroll
+  for (int u = 0; u < B; ++u) {
+    const int j = t + u * TPT;
+    const int k = j & (Ns - 1);
+    cplx_t<T> a[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) a[r] = v[u + r * B];
+    if (Ns > 1) {
+      const int step = n / (Ns * R);
+#pragma unroll
+      for (int r = 1; r < R; ++r) {
+        cplx_t<T> w = tw[r * k * step];
+        if (DIR > 0) w.y = -w.y;
+        a[r] = cmul(a[r], w);
+      }
+    }
+    dftR<T, DIR, R>(a);
+    if (last) {
+      // j < Ns here, so the outputs j + r*Ns = t + (u + r*B)*TPT stay in v
+#pragma unroll
+      for (int r = 0; r < R; ++r) v[u + r * B] = a[r];
+    } else {
+      const int idxD = (j / Ns) * Ns * R + k;
+#pragma unroll
+      for (int r = 0; r < R; ++r) sbase[sidx<PAD>(idxD + r * Ns, sj)] = a[r];
+    }
+  }
+}
+
+// Whole transform; every thread of the block must call it (barriers inside).
+template <typename T, int DIR, bool PAD = false>
+__device__ __forceinline__ void reg_fft(cplx_t<T> (&v)[kEPT], int t, const RadixPlan &rp,
+                                        const cplx_t<T> *__restrict__ tw, cplx_t<T> *sbase, int sj) {
+  const int n = rp.n, TPT = n / kEPT;
+  int Ns = 1;
+  for (int s = 0; s < rp.nst; ++s) {
+    const int R = rp.r[s];
+    const bool last = s == rp.nst - 1;
+    if (R == 8) reg_stage<T, DIR, 8, PAD>(v, t, TPT, n, Ns, tw, sbase, sj, last);
+    else if (R == 4) reg_stage<T, DIR, 4, PAD>(v, t, TPT, n, Ns, tw, sbase, sj, last);
+    else reg_stage<T, DIR, 2, PAD>(v, t, TPT, n, Ns, tw, sbase, sj, last);
+    if (!last) {
+      __syncthreads();
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) v[e] = sbase[sidx<PAD>(t + e * TPT, sj)];
+      __syncthreads();
+    }
+    Ns *= R;
+  }
+}
+
+// padded row length in shared memory
+__host__ __device__ inline int padded_row(int n) { return n + n / 8; }
+
+// C2C along a strided axis: data viewed as [outer][n][inner]; a CTA owns one
+// outer index and `ic` consecutive inner columns; thread (t, c), c fastest.
+template <typename T, int DIR, bool PAD>
+__global__ void k_cols_reg(cplx_t<T> *__restrict__ data, int64_t inner, int ic, RadixPlan rp,
+                           const cplx_t<T> *__restrict__ tw) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  C *sm = reinterpret_cast<C *>(smem_raw);
+  const int n = rp.n, TPT = n / kEPT;
+  const int c = threadIdx.x % ic, t = threadIdx.x / ic;
+  const int64_t nchunks = (inner + ic - 1) / ic;
+  const int64_t o = blockIdx.x / nchunks;
+  const int64_t i0 = (blockIdx.x - o * nchunks) * ic;
+  const bool ok = i0 + c < inner;
+  C *base = data + o * (int64_t)n * inner + i0 + c;
+  C v[kEPT];
+#pragma unroll
+  for (int e = 0; e < kEPT; ++e) v[e] = ok ? base[(int64_t)(t + e * TPT) * inner] : cmk<C, T>(T(0), T(0));
+  reg_fft<T, DIR, PAD>(v, t, rp, tw, sm + c, ic);
+  if (ok) {
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) base[(int64_t)(t + e * TPT) * inner] = v[e];
+  }
+}
+
+// Forward R2C along x: rows of n reals -> n/2+1 complex; thread (t, row), t fastest.
+template <typename T>
+__global__ void k_rows_r2c_reg(const T *__restrict__ in, cplx_t<T> *__restrict__ out, int64_t nrows,
+                               int rpc, RadixPlan rp, const cplx_t<T> *__restrict__ tw) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  C *sm = reinterpret_cast<C *>(smem_raw);
+  const int n = rp.n, TPT = n / kEPT, nxh = n / 2 + 1;
+  const int t = threadIdx.x % TPT, rr = threadIdx.x / TPT;
+  const int64_t row = (int64_t)blockIdx.x * rpc + rr;
+  const bool ok = row < nrows;
+  C v[kEPT];
+#pragma unroll
+  for (int e = 0; e < kEPT; ++e) v[e] = cmk<C, T>(ok ? in[row * n + t + e * TPT] : T(0), T(0));
+  reg_fft<T, -1, true>(v, t, rp, tw, sm + (size_t)rr * (n + n / 8), 1);
+  if (ok) {
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) {
+      const int idx = t + e * TPT;
+      if (idx < nxh) out[row * nxh + idx] = v[e];
+    }
+  }
+}
+
+// Inverse C2R along x (torch.fft.irfftn semantics, unnormalised).
+template <typename T>
+__global__ void k_rows_c2r_reg(const cplx_t<T> *__restrict__ in, T *__restrict__ out, int64_t nrows,
+                               int rpc, RadixPlan rp, const cplx_t<T> *__restrict__ tw) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  C *sm = reinterpret_cast<C *>(smem_raw);
+  const int n = rp.n, TPT = n / kEPT, nxh = n / 2 + 1;
+  const int t = threadIdx.x % TPT, rr = threadIdx.x / TPT;
+  const int64_t row = (int64_t)blockIdx.x * rpc + rr;
+  const bool ok = row < nrows;
+  C v[kEPT];
+#pragma unroll
+  for (int e = 0; e < kEPT; ++e) {
+    const int m = t + e * TPT;
+    C x = cmk<C, T>(T(0), T(0));
+    if (ok) {
+      if (m < nxh) {
+        x = in[row * nxh + m];
+      } else {
+        const C h = in[row * nxh + (n - m)];
+        x = cmk<C, T>(h.x, -h.y);
+      }
+    }
+    v[e] = x;
+  }
+  reg_fft<T, +1, true>(v, t, rp, tw, sm + (size_t)rr * (n + n / 8), 1);
+  if (ok) {
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) out[row * n + t + e * TPT] = v[e].x;
+  }
+}
+
+}  // namespace sogb

@@ -84,6 +84,9 @@ __global__ void k_frame_setup(const T *__restrict__ cells, const FrameHost *__re
     }
     g.pad = (lmin > 2.0 * kmax) ? 0 : 1;
   }
+  g.ortho = (g.kmat[1] == 0.0 && g.kmat[2] == 0.0 && g.kmat[3] == 0.0 && g.kmat[5] == 0.0 &&
+             g.kmat[6] == 0.0 && g.kmat[7] == 0.0) ? 1 : 0;
+  g.pad2 = 0;
   geom[f] = g;
 }
 

@@ -23,6 +23,7 @@
 #include "host_math.hpp"
 #include "plan.hpp"
 #include "sort.cuh"
+#include "fft_reg.cuh"
 #include "frames.cuh"
 
 namespace sogb {
@@ -363,7 +364,40 @@ struct KsArgs {
   double *part;            // [nf][gridDim.x][2]
   double *partx;           // [nf][gridDim.x][NX] extras
   int nx_acc;
+  // separable kernel factors exp(-bw2_m k_a^2 / 2) per axis for orthorhombic
+  // frames: per frame [M][nxh] (x), [M][ny] (y), [M][nz] (z)
+  const double *btab;
+  int64_t btab_stride;
 };
+
+// Per-axis Gaussian factors of the frame (the per-axis tables of
+// lmp/sog.cpp:1391-1430): K(k^2) = sum_m amp_m Bx_m By_m Bz_m when k_a
+// depends on m_a only.
+template <typename T>
+__global__ void k_axis_tables(const FrameGeom *__restrict__ geom, const T *__restrict__ bw2, int M, int nx,
+                              int ny, int nz, double *__restrict__ btab) {
+  const int f = blockIdx.y;
+  const FrameGeom &g = geom[f];
+  if (!g.ortho) return;
+  const int nxh = nx / 2 + 1;
+  const int per = nxh + ny + nz;
+  const int64_t total = (int64_t)M * per;
+  double *bt = btab + (int64_t)f * total;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    int i = (int)idx, axis, m;
+    double k;
+    if (i < M * nxh) {
+      m = i / nxh; const int mx = i - m * nxh; axis = 0; k = g.kmat[0] * mx;
+    } else if (i < M * (nxh + ny)) {
+      i -= M * nxh; m = i / ny; const int iy = i - m * ny; axis = 1; k = g.kmat[4] * signed_mode(iy, ny);
+    } else {
+      i -= M * (nxh + ny); m = i / nz; const int iz = i - m * nz; axis = 2; k = g.kmat[8] * signed_mode(iz, nz);
+    }
+    (void)axis;
+    bt[idx] = exp(-0.5 * (double)bw2[m] * k * k);
+  }
+}
 
 // Green factors of one half-spectrum mode.
 struct ModeGreen {
@@ -392,50 +426,12 @@ __device__ __forceinline__ double kernel_sum(const double *amp, const double *bw
   return K;
 }
 
-// Green function of a mode; with `alias` the B-spline alias sums of
-// lmp/sog.cpp:1516-1578 (pruned to aliases inside the k_max sphere), else the
-// principal (separable) form.  If emD/emS are given, the per-Gaussian factors
-// d gE / d amp_m and d gS / d amp_m are returned too.
+// B-spline alias sums of lmp/sog.cpp:1516-1578, pruned to the aliases that
+// can fall inside the k_max sphere (rarely taken, kept out of line).
 template <typename T>
-__device__ ModeGreen mode_green(const KsArgs<T> &a, const FrameGeom &g, const double *amp,
-                                const double *bw2, int mx, int iy, int iz, int mfor, double *emD,
-                                double *emS) {
-  ModeGreen r;
-  const int my = signed_mode(iy, a.ny), mz = signed_mode(iz, a.nz);
-  for (int c = 0; c < 3; ++c)
-    r.k[c] = g.kmat[c * 3 + 0] * mx + g.kmat[c * 3 + 1] * my + g.kmat[c * 3 + 2] * mz;
-  r.ksq = r.k[0] * r.k[0] + r.k[1] * r.k[1] + r.k[2] * r.k[2];
-  r.live = !((mx | my | mz) == 0) && r.ksq <= g.k_sq_max;
-  r.K = r.Kv = r.gE = r.gF = r.gS = r.gV = 0.0;
-  if (!r.live) return r;
-  r.K = kernel_sum<T>(amp, bw2, a.M, r.ksq, &r.Kv);
-  if (a.spline == SOG_SPLINE_QUADS) {
-    double infl = a.tx[mx] * a.ty[iy] * a.tz[iz];
-    if (infl < 1e-20) infl = 1e-20;  // quads_fft.py:194
-    const double D = 1.0 / infl;
-    r.gE = r.gF = r.K * D;
-    r.gS = r.K;
-    r.gV = r.Kv * D;
-    if (emD) {
-      const double e = exp(-0.5 * bw2[mfor] * r.ksq);
-      *emD = e * D;
-      *emS = e;
-    }
-    return r;
-  }
-  if (!g.pad) {
-    const double D = a.tx[mx] * a.ty[iy] * a.tz[iz];
-    r.gE = r.gF = r.K * D;
-    r.gS = r.K;
-    r.gV = r.Kv * D;
-    if (emD) {
-      const double e = exp(-0.5 * bw2[mfor] * r.ksq);
-      *emD = e * D;
-      *emS = e;
-    }
-    return r;
-  }
-  // alias sums
+__device__ __noinline__ void alias_green(const KsArgs<T> &a, const FrameGeom &g, const double *amp,
+                                         const double *bw2, int mx, int my, int mz, int iy, int iz,
+                                         int mfor, double *emD, double *emS, ModeGreen &r) {
   const double dl = a.sx[mx] * a.sy[iy] * a.sz[iz];
   const double denom = dl * dl;
   const int m3[3] = {mx, my, mz};
@@ -478,6 +474,65 @@ __device__ ModeGreen mode_green(const KsArgs<T> &a, const FrameGeom &g, const do
   r.gS = (w0 > 1e-20) ? s0 / w0 : 0.0;
   r.gV = sv / denom;
   if (emD) { *emD = eD; *emS = eS; }
+}
+
+// Green function of a mode; with `alias` the B-spline alias sums of
+// lmp/sog.cpp:1516-1578 (pruned to aliases inside the k_max sphere), else the
+// principal (separable) form.  If emD/emS are given, the per-Gaussian factors
+// d gE / d amp_m and d gS / d amp_m are returned too.
+template <typename T>
+__device__ ModeGreen mode_green(const KsArgs<T> &a, const FrameGeom &g, const double *amp,
+                                const double *bw2, int mx, int iy, int iz, int mfor, double *emD,
+                                double *emS, const double *bt = nullptr) {
+  ModeGreen r;
+  const int my = signed_mode(iy, a.ny), mz = signed_mode(iz, a.nz);
+  for (int c = 0; c < 3; ++c)
+    r.k[c] = g.kmat[c * 3 + 0] * mx + g.kmat[c * 3 + 1] * my + g.kmat[c * 3 + 2] * mz;
+  r.ksq = r.k[0] * r.k[0] + r.k[1] * r.k[1] + r.k[2] * r.k[2];
+  r.live = !((mx | my | mz) == 0) && r.ksq <= g.k_sq_max;
+  r.K = r.Kv = r.gE = r.gF = r.gS = r.gV = 0.0;
+  if (!r.live) return r;
+  if (bt) {
+    const int nxh = a.nxh;
+    const double *bx = bt, *by = bt + a.M * nxh, *bz = by + a.M * a.ny;
+    double K = 0.0, V = 0.0;
+    for (int m = 0; m < a.M; ++m) {
+      const double e = bx[m * nxh + mx] * by[m * a.ny + iy] * bz[m * a.nz + iz];
+      K += amp[m] * e;
+      V += amp[m] * bw2[m] * e;
+    }
+    r.K = K;
+    r.Kv = V;
+  } else {
+    r.K = kernel_sum<T>(amp, bw2, a.M, r.ksq, &r.Kv);
+  }
+  if (a.spline == SOG_SPLINE_QUADS) {
+    double infl = a.tx[mx] * a.ty[iy] * a.tz[iz];
+    if (infl < 1e-20) infl = 1e-20;  // quads_fft.py:194
+    const double D = 1.0 / infl;
+    r.gE = r.gF = r.K * D;
+    r.gS = r.K;
+    r.gV = r.Kv * D;
+    if (emD) {
+      const double e = exp(-0.5 * bw2[mfor] * r.ksq);
+      *emD = e * D;
+      *emS = e;
+    }
+    return r;
+  }
+  if (!g.pad) {
+    const double D = a.tx[mx] * a.ty[iy] * a.tz[iz];
+    r.gE = r.gF = r.K * D;
+    r.gS = r.K;
+    r.gV = r.Kv * D;
+    if (emD) {
+      const double e = exp(-0.5 * bw2[mfor] * r.ksq);
+      *emD = e * D;
+      *emS = e;
+    }
+    return r;
+  }
+  alias_green<T>(a, g, amp, bw2, mx, my, mz, iy, iz, mfor, emD, emS, r);
   return r;
 }
 
@@ -500,7 +555,8 @@ __global__ void __launch_bounds__(256) k_kspace(KsArgs<T> a) {
     const int mx = (int)(idx % a.nxh);
     const int64_t zy = idx / a.nxh;
     const int iy = (int)(zy % a.ny), iz = (int)(zy / a.ny);
-    const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr);
+    const double *bt = (g.ortho && a.btab) ? a.btab + (int64_t)f * a.btab_stride : nullptr;
+    const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr, bt);
     const C r = a.spec[(int64_t)f * a.nh + idx];
     const double rr = (double)r.x, ri = (double)r.y;
     const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
@@ -529,6 +585,115 @@ __global__ void __launch_bounds__(256) k_kspace(KsArgs<T> a) {
     double e = 0.0, d = 0.0;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { e += red[0][w]; d += red[1][w]; }
     double *p = a.part + ((int64_t)f * gridDim.x + blockIdx.x) * 2;
+    p[0] = e;
+    p[1] = d;
+  }
+}
+
+// Fused z pass for a power-of-two nz: forward z-FFT of a tile of ic spectrum
+// columns, the k-space step of k_kspace on the registers, and the inverse z-FFT
+// of every output field, so neither the z-transformed spectrum nor the field
+// spectra make an extra round trip through HBM.  Energy / self partial sums per
+// CTA go to a.part[(f*nchunks + chunk)*2].  With write_spec the transformed
+// spectrum is also stored (for k_kspace_extra).
+template <typename T>
+__global__ void __launch_bounds__(256, 2) k_zfused(KsArgs<T> a, int ic, RadixPlan rpz,
+                                                 const cplx_t<T> *__restrict__ twz, int write_spec) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  C *sm = reinterpret_cast<C *>(smem_raw);
+  __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
+  __shared__ double red[2][32];
+  for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
+    s_amp[m] = (double)a.amp[m];
+    s_bw2[m] = (double)a.bw2[m];
+  }
+  __syncthreads();
+  const int n = rpz.n, TPT = n / kEPT;
+  const int c = threadIdx.x % ic, t = threadIdx.x / ic;
+  const int64_t inner = (int64_t)a.ny * a.nxh;
+  const int64_t nchunks = (inner + ic - 1) / ic;
+  const int f = (int)(blockIdx.x / nchunks);
+  const int64_t chunk = blockIdx.x - (int64_t)f * nchunks;
+  const int64_t col = chunk * ic + c;
+  const bool ok = col < inner;
+  const FrameGeom &g = a.geom[f];
+  C *sp = const_cast<C *>(a.spec) + (int64_t)f * a.nh + (ok ? col : 0);
+  C v[kEPT];
+#pragma unroll
+  for (int e = 0; e < kEPT; ++e) v[e] = ok ? sp[(int64_t)(t + e * TPT) * inner] : cmk<C, T>(T(0), T(0));
+  reg_fft<T, -1, true>(v, t, rpz, twz, sm + c, ic);
+  if (write_spec && ok) {
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) sp[(int64_t)(t + e * TPT) * inner] = v[e];
+  }
+  // keep rho-hat and the two Green scalars of the thread's modes in shared
+  // memory (after the FFT buffer) so the field loop runs with few registers
+  const int nthr = blockDim.x;
+  C *s_rho = sm + (size_t)padded_row(n) * ic;                       // [kEPT][nthr]
+  double *s_g = reinterpret_cast<double *>(s_rho + (size_t)kEPT * nthr);  // [kEPT][2][nthr]
+  const int mx = ok ? (int)(col % a.nxh) : 0;
+  const int iy = ok ? (int)(col / a.nxh) : 0;
+  const int my = signed_mode(iy, a.ny);
+  const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
+  const double inv = 1.0 / ((double)a.nx * a.ny * a.nz);
+  double accE = 0.0, accD = 0.0;
+  const double *bt = (g.ortho && a.btab) ? a.btab + (int64_t)f * a.btab_stride : nullptr;
+#pragma unroll
+  for (int e = 0; e < kEPT; ++e) s_rho[e * nthr + threadIdx.x] = v[e];
+#pragma unroll 1
+  for (int e = 0; e < kEPT; ++e) {
+    const int iz = t + e * TPT;
+    const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr, bt);
+    const bool live = ok && mg.live;
+    const C r = s_rho[e * nthr + threadIdx.x];
+    if (live) {
+      const double rr = (double)r.x, ri = (double)r.y;
+      accE += w * mg.gE * (rr * rr + ri * ri);
+      accD += w * mg.gS;
+    }
+    s_g[(2 * e) * nthr + threadIdx.x] = live ? mg.gF * inv : 0.0;
+    s_g[(2 * e + 1) * nthr + threadIdx.x] = live ? mg.gE * inv : 0.0;
+  }
+  const int nfield = a.nfield;
+  C *out = a.fspec ? a.fspec + (int64_t)f * nfield * a.nh + (ok ? col : 0) : nullptr;
+  for (int fl = 0; fl < nfield; ++fl) {
+    const bool force = a.want_force && fl < 3;
+    double km = 0.0, kz = 0.0;
+    if (force) {
+      km = g.kmat[fl * 3 + 0] * mx + g.kmat[fl * 3 + 1] * my;
+      kz = g.kmat[fl * 3 + 2];
+    }
+    C wv[kEPT];
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) {
+      const C r = s_rho[e * nthr + threadIdx.x];
+      const double rr = (double)r.x, ri = (double)r.y;
+      if (force) {
+        const double kc = km + kz * signed_mode(t + e * TPT, a.nz);
+        const double sc = s_g[(2 * e) * nthr + threadIdx.x];
+        wv[e] = cmk<C, T>((T)(-kc * sc * ri), (T)(kc * sc * rr));
+      } else {
+        const double sc = s_g[(2 * e + 1) * nthr + threadIdx.x];
+        wv[e] = cmk<C, T>((T)(sc * rr), (T)(sc * ri));
+      }
+    }
+    reg_fft<T, +1, true>(wv, t, rpz, twz, sm + c, ic);
+    if (ok) {
+      C *o = out + (int64_t)fl * a.nh;
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) o[(int64_t)(t + e * TPT) * inner] = wv[e];
+    }
+  }
+  accE = warp_sum(accE);
+  accD = warp_sum(accD);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { red[0][warp] = accE; red[1][warp] = accD; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double e = 0.0, d = 0.0;
+    for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) { e += red[0][wi]; d += red[1][wi]; }
+    double *p = a.part + ((int64_t)f * nchunks + chunk) * 2;
     p[0] = e;
     p[1] = d;
   }
@@ -781,62 +946,71 @@ int cols_per_cta(int n) {
   return std::max(1, std::min(r, 16));
 }
 
+// ---- FFT passes: register-resident kernels for power-of-two axes, the
+// generic shared-memory Stockham otherwise ----
 template <typename T>
-void fft_forward(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t nbatch, cudaStream_t st) {
-  using C = cplx_t<T>;
-  const int nx = p->d.nx, ny = p->d.ny, nz = p->d.nz, nxh = p->nxh;
-  {
-    const int rpc = rows_per_cta<T>(nx);
-    const int64_t rows = nbatch * nz * ny;
-    k_fft_r2c_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
-        rho, spec, nx, rows, rpc, p->rpx, p->twx.as<C>());
-    after(&p->tr, st, "fft_r2c_x");
-  }
-  {
-    const int ic = cols_per_cta<T>(ny);
-    const int64_t outer = nbatch * nz, inner = nxh;
-    const int64_t nchunks = (inner + ic - 1) / ic;
-    k_fft_strided<T, -1><<<(unsigned)(outer * nchunks), 256, fft_rows_smem<T>(ny, ic), st>>>(
-        spec, inner, outer, ic, p->rpy, p->twy.as<C>());
-    after(&p->tr, st, "fft_y_fwd");
-  }
-  {
-    const int ic = cols_per_cta<T>(nz);
-    const int64_t outer = nbatch, inner = (int64_t)ny * nxh;
-    const int64_t nchunks = (inner + ic - 1) / ic;
-    k_fft_strided<T, -1><<<(unsigned)(outer * nchunks), 256, fft_rows_smem<T>(nz, ic), st>>>(
-        spec, inner, outer, ic, p->rpz, p->twz.as<C>());
-    after(&p->tr, st, "fft_z_fwd");
-  }
+int reg_width(int n, int max_threads, size_t smem_budget) {
+  const int tpt = n / kEPT;
+  const int by_threads = std::max(1, max_threads / tpt);
+  const int by_smem = std::max(1, (int)(smem_budget / ((size_t)n * sizeof(cplx_t<T>))));
+  return std::max(1, std::min(by_threads, by_smem));
 }
 
 template <typename T>
-void fft_inverse(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nbatch, cudaStream_t st) {
+void pass_x_fwd(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t nbatch, cudaStream_t st) {
   using C = cplx_t<T>;
-  const int nx = p->d.nx, ny = p->d.ny, nz = p->d.nz, nxh = p->nxh;
-  {
-    const int ic = cols_per_cta<T>(nz);
-    const int64_t outer = nbatch, inner = (int64_t)ny * nxh;
-    const int64_t nchunks = (inner + ic - 1) / ic;
-    k_fft_strided<T, +1><<<(unsigned)(outer * nchunks), 256, fft_rows_smem<T>(nz, ic), st>>>(
-        fspec, inner, outer, ic, p->rpz, p->twz.as<C>());
-    after(&p->tr, st, "fft_z_inv");
-  }
-  {
-    const int ic = cols_per_cta<T>(ny);
-    const int64_t outer = nbatch * nz, inner = nxh;
-    const int64_t nchunks = (inner + ic - 1) / ic;
-    k_fft_strided<T, +1><<<(unsigned)(outer * nchunks), 256, fft_rows_smem<T>(ny, ic), st>>>(
-        fspec, inner, outer, ic, p->rpy, p->twy.as<C>());
-    after(&p->tr, st, "fft_y_inv");
-  }
-  {
+  const int nx = p->d.nx;
+  const int64_t rows = nbatch * p->d.nz * p->d.ny;
+  if (is_pow2(nx)) {
+    const int rpc = reg_width<T>(nx, 512, 64 * 1024);
+    k_rows_r2c_reg<T><<<nblocks(rows, rpc), (nx / kEPT) * rpc, (size_t)rpc * padded_row(nx) * sizeof(C), st>>>(
+        rho, spec, rows, rpc, p->rpx, p->twx.as<C>());
+  } else {
     const int rpc = rows_per_cta<T>(nx);
-    const int64_t rows = nbatch * nz * ny;
+    k_fft_r2c_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
+        rho, spec, nx, rows, rpc, p->rpx, p->twx.as<C>());
+  }
+  after(&p->tr, st, "fft_r2c_x");
+}
+
+template <typename T>
+void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nbatch, cudaStream_t st) {
+  using C = cplx_t<T>;
+  const int nx = p->d.nx;
+  const int64_t rows = nbatch * p->d.nz * p->d.ny;
+  if (is_pow2(nx)) {
+    const int rpc = reg_width<T>(nx, 512, 64 * 1024);
+    k_rows_c2r_reg<T><<<nblocks(rows, rpc), (nx / kEPT) * rpc, (size_t)rpc * padded_row(nx) * sizeof(C), st>>>(
+        fspec, freal, rows, rpc, p->rpx, p->twx.as<C>());
+  } else {
+    const int rpc = rows_per_cta<T>(nx);
     k_fft_c2r_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
         fspec, freal, nx, rows, rpc, p->rpx, p->twx.as<C>());
-    after(&p->tr, st, "fft_c2r_x");
   }
+  after(&p->tr, st, "fft_c2r_x");
+}
+
+// C2C over an axis of length n with `inner` contiguous columns per slab.
+template <typename T, int DIR>
+void pass_cols(sog_plan *p, cplx_t<T> *data, int n, int64_t inner, int64_t outer, const RadixPlan &rp,
+               const cplx_t<T> *tw, cudaStream_t st, const char *name) {
+  using C = cplx_t<T>;
+  if (is_pow2(n)) {
+    const int ic = reg_width<T>(n, 512, 64 * 1024);
+    const int64_t nchunks = (inner + ic - 1) / ic;
+    if (ic >= 8)
+      k_cols_reg<T, DIR, false><<<(unsigned)(outer * nchunks), (n / kEPT) * ic, (size_t)n * ic * sizeof(C), st>>>(
+          data, inner, ic, rp, tw);
+    else
+      k_cols_reg<T, DIR, true><<<(unsigned)(outer * nchunks), (n / kEPT) * ic,
+                                 (size_t)padded_row(n) * ic * sizeof(C), st>>>(data, inner, ic, rp, tw);
+  } else {
+    const int ic = cols_per_cta<T>(n);
+    const int64_t nchunks = (inner + ic - 1) / ic;
+    k_fft_strided<T, DIR><<<(unsigned)(outer * nchunks), 256, fft_rows_smem<T>(n, ic), st>>>(
+        data, inner, outer, ic, rp, tw);
+  }
+  after(&p->tr, st, name);
 }
 
 template <typename T>
@@ -849,6 +1023,13 @@ void set_fft_smem_attrs() {
   cudaFuncSetAttribute(k_fft_c2r_x<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_fft_strided<T, -1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_fft_strided<T, +1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_cols_reg<T, -1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_cols_reg<T, +1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_cols_reg<T, -1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_cols_reg<T, +1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_rows_r2c_reg<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_rows_c2r_reg<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_zfused<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
 }
 
 template <typename T, int P>
@@ -996,14 +1177,16 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   const bool want_vir = a->virial != nullptr;
   const int nfield = (want_force ? 3 : 0) + (want_pot ? 1 : 0);
   const unsigned ks_blocks = nblocks(nh, 256);
+  // the fused z pass writes one partial per tile; the generic k-space kernel one per block
+  const int64_t part_blocks = std::max<int64_t>(ks_blocks, (int64_t)ny * nxh);
   const int nx_acc = 4 * M + 13;
   if (p->rho.reserve(sizeof(T) * ng * nf) || p->spec.reserve(sizeof(C) * nh * nf) ||
-      p->partE.reserve(sizeof(double) * 2 * (int64_t)ks_blocks * nf * nch) ||
+      p->partE.reserve(sizeof(double) * 2 * part_blocks * nf * nch) ||
       (nfield && (p->fspec.reserve(sizeof(C) * nh * nf * nfield) ||
                   p->freal.reserve(sizeof(T) * ng * nf * nfield))) ||
       ((want_grad || want_vir) && p->partX.reserve(sizeof(double) * nx_acc * (int64_t)ks_blocks * nf * nch)) ||
       p->red.reserve(sizeof(double) * ((int64_t)nf * nch * (2 + nx_acc) + (int64_t)nf * 4)) ||
-      p->redtmp.reserve(sizeof(double) * std::max(reduce_tmp_elems(nf, nch, ks_blocks, 2),
+      p->redtmp.reserve(sizeof(double) * std::max(reduce_tmp_elems(nf, nch, part_blocks, 2),
                                                   reduce_tmp_elems(nf, nch, ks_blocks, nx_acc))))
     return fail(SOG_ERR_NOMEM, "device allocation failed (mesh buffers)");
 
@@ -1041,6 +1224,12 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   ka.nfield = nfield;
   ka.want_force = want_force;
   ka.nx_acc = nx_acc;
+  ka.btab_stride = (int64_t)M * (nxh + ny + nz);
+  if (p->btab.reserve(sizeof(double) * ka.btab_stride * nf)) return fail(SOG_ERR_NOMEM, "device allocation failed");
+  ka.btab = p->btab.as<double>();
+  k_axis_tables<T><<<dim3(nblocks(ka.btab_stride, 256), nf), 256, 0, st>>>(geom, (const T *)a->bw2, M, nx, ny,
+                                                                          nz, p->btab.as<double>());
+  after(tr, st, "axis_tables");
 
   GatherArgs<T> gar;
   gar.s_anchor = p->s_anchor.as<int4>();
@@ -1061,20 +1250,39 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   gar.pot_raw = (T *)a->potential;
 
   set_fft_smem_attrs<T>();
+  const bool zfuse = is_pow2(nz);
+  const int zic = zfuse ? reg_width<T>(nz, 256, 32 * 1024) : 0;
+  const int64_t zchunks = zfuse ? ((int64_t)ny * nxh + zic - 1) / zic : 0;
+  const int64_t nblk_e = zfuse ? zchunks : (int64_t)ks_blocks;
   for (int c = 0; c < nch; ++c) {
     sa.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
     dispatch_spread<T>(sa, P, nf, st, tr);
-    fft_forward<T>(p, p->rho.as<T>(), p->spec.as<C>(), nf, st);
-    ka.part = p->partE.as<double>() + (int64_t)c * nf * ks_blocks * 2;
-    k_kspace<T><<<dim3(ks_blocks, nf), 256, 0, st>>>(ka);
-    after(tr, st, "kspace");
+    pass_x_fwd<T>(p, p->rho.as<T>(), p->spec.as<C>(), nf, st);
+    pass_cols<T, -1>(p, p->spec.as<C>(), ny, nxh, (int64_t)nf * nz, p->rpy, p->twy.as<C>(), st, "fft_y_fwd");
+    ka.part = p->partE.as<double>() + (int64_t)c * nf * nblk_e * 2;
+    if (zfuse) {
+      const size_t zsm = (size_t)padded_row(nz) * zic * sizeof(C) +
+                         (size_t)(nz / kEPT) * zic * kEPT * (sizeof(C) + 2 * sizeof(double));
+      k_zfused<T><<<(unsigned)(zchunks * nf), (nz / kEPT) * zic, zsm, st>>>(
+          ka, zic, p->rpz, p->twz.as<C>(), (want_grad || want_vir) ? 1 : 0);
+      after(tr, st, "zfused");
+    } else {
+      pass_cols<T, -1>(p, p->spec.as<C>(), nz, (int64_t)ny * nxh, nf, p->rpz, p->twz.as<C>(), st, "fft_z_fwd");
+      k_kspace<T><<<dim3(ks_blocks, nf), 256, 0, st>>>(ka);
+      after(tr, st, "kspace");
+    }
     if (want_grad || want_vir) {
       ka.partx = p->partX.as<double>() + (int64_t)c * nf * ks_blocks * nx_acc;
       k_kspace_extra<T><<<dim3(ks_blocks, nf), 256, 0, st>>>(ka, want_grad, want_vir);
       after(tr, st, "kspace_extra");
     }
     if (nfield) {
-      fft_inverse<T>(p, p->fspec.as<C>(), p->freal.as<T>(), (int64_t)nf * nfield, st);
+      const int64_t nb = (int64_t)nf * nfield;
+      if (!zfuse)
+        pass_cols<T, +1>(p, p->fspec.as<C>(), nz, (int64_t)ny * nxh, nb, p->rpz, p->twz.as<C>(), st,
+                         "fft_z_inv");
+      pass_cols<T, +1>(p, p->fspec.as<C>(), ny, nxh, nb * nz, p->rpy, p->twy.as<C>(), st, "fft_y_inv");
+      pass_x_inv<T>(p, p->fspec.as<C>(), p->freal.as<T>(), nb, st);
       gar.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
       gar.channel = c;
       gar.accumulate = c > 0;
@@ -1085,8 +1293,8 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   double *redE = p->red.as<double>();
   double *redX = redE + (int64_t)nf * nch * 2;
   double *fscal = redX + (int64_t)nf * nch * nx_acc;
-  reduce_parts(p->partE.as<double>(), nf, nch, ks_blocks, 2, 2, redE, p->redtmp.as<double>(), st);
-  after(tr, st, "reduce", reduce_split(ks_blocks) > 1 ? 2 : 1);
+  reduce_parts(p->partE.as<double>(), nf, nch, nblk_e, 2, 2, redE, p->redtmp.as<double>(), st);
+  after(tr, st, "reduce", reduce_split(nblk_e) > 1 ? 2 : 1);
   if (want_grad || want_vir)
     reduce_parts(p->partX.as<double>(), nf, nch, ks_blocks, nx_acc, nx_acc, redX, p->redtmp.as<double>(), st);
   if (want_grad || want_vir) after(tr, st, "reduce_extra", reduce_split(ks_blocks) > 1 ? 2 : 1);
@@ -1199,7 +1407,7 @@ extern "C" int sog_plan_destroy(sog_plan *p) {
                     &p->tab.sy, &p->tab.sz, &p->frames_host_dev, &p->geom, &p->status, &p->keys0,
                     &p->vals0, &p->keys1, &p->vals1, &p->hist, &p->scan_tmp, &p->bin_start,
                     &p->s_atom, &p->s_anchor, &p->s_t, &p->s_q, &p->qsum, &p->rho, &p->spec,
-                    &p->fspec, &p->freal, &p->partE, &p->partX, &p->red, &p->redtmp, &p->qpart};
+                    &p->fspec, &p->freal, &p->partE, &p->partX, &p->red, &p->redtmp, &p->qpart, &p->btab};
   for (DevBuf *b : bufs) b->release();
   p->up.release();
   p->tr.release();

@@ -77,6 +77,7 @@ struct sog_plan {
   sogb::DevBuf partE, partX;    // kspace partial sums
   sogb::DevBuf red;             // reduced sums and per-frame scalars
   sogb::DevBuf redtmp, qpart;   // two-level reduction scratch, charge-sum partials
+  sogb::DevBuf btab;            // per-axis kernel factors (orthorhombic frames)
   sogb::PinnedBuf up;
   sogb::Tracer tr;
   int nb_x = 0, nb_y = 0, nb_z = 0;  // sort bins per axis
