@@ -182,11 +182,13 @@ __global__ void k_fft_r2c_x(const T *__restrict__ in, cplx_t<T> *__restrict__ ou
   }
 }
 
-// Inverse C2R along x with torch.fft.irfftn semantics (unnormalised).
+// Inverse C2R along x with torch.fft.irfftn semantics (unnormalised).  Input
+// rows are field-major ((frame*F + f)*nzy + zy); the output is interleaved,
+// out[((frame*nzy + zy)*nx + x)*F + f].
 template <typename T>
 __global__ void k_fft_c2r_x(const cplx_t<T> *__restrict__ in, T *__restrict__ out, int nx,
                             int64_t nrows, int rows_per_cta, RadixPlan rp,
-                            const cplx_t<T> *__restrict__ tw) {
+                            const cplx_t<T> *__restrict__ tw, int F, int64_t nzy) {
   using C = cplx_t<T>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   C *a = reinterpret_cast<C *>(smem_raw);
@@ -203,8 +205,13 @@ __global__ void k_fft_c2r_x(const cplx_t<T> *__restrict__ in, T *__restrict__ ou
   }
   __syncthreads();
   C *res = fft_smem<T, +1>(a, b, rp, nr, 1, nx, tw);
-  T *dst = out + row0 * nx;
-  for (int i = threadIdx.x; i < nr * nx; i += blockDim.x) dst[i] = res[i].x;
+  for (int i = threadIdx.x; i < nr * nx; i += blockDim.x) {
+    const int r = i / nx, x = i - r * nx;
+    const int64_t row = row0 + r;                 // (frame*F + f)*nzy + zy
+    const int64_t ff = row / nzy, zy = row - ff * nzy;
+    const int64_t frame = ff / F, f = ff - frame * F;
+    out[((frame * nzy + zy) * nx + x) * F + f] = res[i].x;
+  }
 }
 
 // C2C along a strided axis: data viewed as [outer][n][inner]; a CTA handles one

@@ -174,4 +174,49 @@ __global__ void k_rows_c2r_reg(const cplx_t<T> *__restrict__ in, T *__restrict__
   }
 }
 
+// Inverse C2R along x of F fields with interleaved real output: a CTA
+// transforms all F fields of rpc consecutive mesh rows and writes
+// out[(row*n + x)*F + f] (the gather then reads one contiguous run of F*p
+// values per stencil row).  Input field f of global row g = frame*nzy + zy
+// sits at in[((frame*F + f)*nzy + zy)*nxh].
+template <typename T>
+__global__ void k_rows_c2r_il(const cplx_t<T> *__restrict__ in, T *__restrict__ out, int F, int64_t nzy,
+                              int64_t nrows, int rpc, RadixPlan rp, const cplx_t<T> *__restrict__ tw) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  C *sm = reinterpret_cast<C *>(smem_raw);
+  const int n = rp.n, TPT = n / kEPT, nxh = n / 2 + 1;
+  const int t = threadIdx.x % TPT, q = threadIdx.x / TPT;
+  const int f = q % F, rr = q / F;
+  const int64_t row0 = (int64_t)blockIdx.x * rpc;
+  const int64_t row = row0 + rr;
+  const bool ok = row < nrows;
+  const int64_t frame = ok ? row / nzy : 0, zy = ok ? row - frame * nzy : 0;
+  const C *src = in + ((frame * F + f) * nzy + zy) * nxh;
+  C v[kEPT];
+#pragma unroll
+  for (int e = 0; e < kEPT; ++e) {
+    const int m = t + e * TPT;
+    C x = cmk<C, T>(T(0), T(0));
+    if (ok) {
+      if (m < nxh) {
+        x = src[m];
+      } else {
+        const C h = src[n - m];
+        x = cmk<C, T>(h.x, -h.y);
+      }
+    }
+    v[e] = x;
+  }
+  reg_fft<T, +1, true>(v, t, rp, tw, sm + (size_t)(rr * F + f) * (n + n / 8), 1);
+  __syncthreads();
+  T *so = reinterpret_cast<T *>(smem_raw);
+#pragma unroll
+  for (int e = 0; e < kEPT; ++e) so[((size_t)rr * n + t + e * TPT) * F + f] = v[e].x;
+  __syncthreads();
+  const int64_t nvalid = min((int64_t)rpc, nrows - row0) * n * F;
+  T *dst = out + row0 * n * F;
+  for (int64_t i = threadIdx.x; i < nvalid; i += blockDim.x) dst[i] = so[i];
+}
+
 }  // namespace sogb

@@ -835,7 +835,8 @@ __global__ void __launch_bounds__(256) k_gather(GatherArgs<T> a) {
   int ix[P];
 #pragma unroll
   for (int k = 0; k < P; ++k) { int v = an.x + k; ix[k] = v >= ag.nx ? v - ag.nx : v; }
-  const T *base = a.freal + (int64_t)an.w * a.nfield * a.ng;
+  const int F = a.nfield;
+  const T *base = a.freal + (int64_t)an.w * F * a.ng;
   T acc[4] = {T(0), T(0), T(0), T(0)};
 #pragma unroll 1
   for (int c = 0; c < P; ++c) {
@@ -850,8 +851,14 @@ __global__ void __launch_bounds__(256) k_gather(GatherArgs<T> a) {
 #pragma unroll
       for (int k = 0; k < P; ++k) {
         const T wv = wx[k] * wzy;
-        const int64_t id = row + ix[k];
-        for (int fl = 0; fl < a.nfield; ++fl) acc[fl] += wv * base[(int64_t)fl * a.ng + id];
+        const T *pt = base + (row + ix[k]) * F;
+        if (F == 3) {
+          acc[0] += wv * pt[0]; acc[1] += wv * pt[1]; acc[2] += wv * pt[2];
+        } else if (F == 4) {
+          acc[0] += wv * pt[0]; acc[1] += wv * pt[1]; acc[2] += wv * pt[2]; acc[3] += wv * pt[3];
+        } else {
+          acc[0] += wv * pt[0];
+        }
       }
     }
   }
@@ -962,7 +969,7 @@ void pass_x_fwd(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t nbatch, cudaStream
   const int nx = p->d.nx;
   const int64_t rows = nbatch * p->d.nz * p->d.ny;
   if (is_pow2(nx)) {
-    const int rpc = reg_width<T>(nx, 512, 64 * 1024);
+    const int rpc = reg_width<T>(nx, 256, 64 * 1024);
     k_rows_r2c_reg<T><<<nblocks(rows, rpc), (nx / kEPT) * rpc, (size_t)rpc * padded_row(nx) * sizeof(C), st>>>(
         rho, spec, rows, rpc, p->rpx, p->twx.as<C>());
   } else {
@@ -973,19 +980,24 @@ void pass_x_fwd(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t nbatch, cudaStream
   after(&p->tr, st, "fft_r2c_x");
 }
 
+// F fields of nframes frames -> interleaved real fields [frame][zy][x][F]
 template <typename T>
-void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nbatch, cudaStream_t st) {
+void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nframes, int F, cudaStream_t st) {
   using C = cplx_t<T>;
   const int nx = p->d.nx;
-  const int64_t rows = nbatch * p->d.nz * p->d.ny;
+  const int64_t nzy = (int64_t)p->d.nz * p->d.ny;
   if (is_pow2(nx)) {
-    const int rpc = reg_width<T>(nx, 512, 64 * 1024);
-    k_rows_c2r_reg<T><<<nblocks(rows, rpc), (nx / kEPT) * rpc, (size_t)rpc * padded_row(nx) * sizeof(C), st>>>(
-        fspec, freal, rows, rpc, p->rpx, p->twx.as<C>());
+    const int tpt = nx / kEPT;
+    const int rpc = std::max(1, 256 / (tpt * F));
+    const int64_t rows = nframes * nzy;
+    const size_t sm = std::max((size_t)rpc * F * padded_row(nx) * sizeof(C), (size_t)rpc * nx * F * sizeof(T));
+    k_rows_c2r_il<T><<<nblocks(rows, rpc), tpt * F * rpc, sm, st>>>(fspec, freal, F, nzy, rows, rpc, p->rpx,
+                                                                      p->twx.as<C>());
   } else {
     const int rpc = rows_per_cta<T>(nx);
+    const int64_t rows = nframes * F * nzy;
     k_fft_c2r_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
-        fspec, freal, nx, rows, rpc, p->rpx, p->twx.as<C>());
+        fspec, freal, nx, rows, rpc, p->rpx, p->twx.as<C>(), F, nzy);
   }
   after(&p->tr, st, "fft_c2r_x");
 }
@@ -996,7 +1008,7 @@ void pass_cols(sog_plan *p, cplx_t<T> *data, int n, int64_t inner, int64_t outer
                const cplx_t<T> *tw, cudaStream_t st, const char *name) {
   using C = cplx_t<T>;
   if (is_pow2(n)) {
-    const int ic = reg_width<T>(n, 512, 64 * 1024);
+    const int ic = reg_width<T>(n, 256, 64 * 1024);
     const int64_t nchunks = (inner + ic - 1) / ic;
     if (ic >= 8)
       k_cols_reg<T, DIR, false><<<(unsigned)(outer * nchunks), (n / kEPT) * ic, (size_t)n * ic * sizeof(C), st>>>(
@@ -1029,6 +1041,7 @@ void set_fft_smem_attrs() {
   cudaFuncSetAttribute(k_cols_reg<T, +1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_rows_r2c_reg<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_rows_c2r_reg<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  cudaFuncSetAttribute(k_rows_c2r_il<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   cudaFuncSetAttribute(k_zfused<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
 }
 
@@ -1282,7 +1295,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
         pass_cols<T, +1>(p, p->fspec.as<C>(), nz, (int64_t)ny * nxh, nb, p->rpz, p->twz.as<C>(), st,
                          "fft_z_inv");
       pass_cols<T, +1>(p, p->fspec.as<C>(), ny, nxh, nb * nz, p->rpy, p->twy.as<C>(), st, "fft_y_inv");
-      pass_x_inv<T>(p, p->fspec.as<C>(), p->freal.as<T>(), nb, st);
+      pass_x_inv<T>(p, p->fspec.as<C>(), p->freal.as<T>(), nf, nfield, st);
       gar.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
       gar.channel = c;
       gar.accumulate = c > 0;
