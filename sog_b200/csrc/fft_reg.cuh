@@ -89,6 +89,83 @@ __device__ __forceinline__ void reg_fft(cplx_t<T> (&v)[kEPT], int t, const Radix
   }
 }
 
+// ---------------------------------------------------------------------------
+// Compile-time length n = 2^L: radix 8 stages, then one radix 4 or 2 stage;
+// stage s has Ns = 8^s, so every index and twiddle stride is a constant shift.
+// Twiddles are read from a shared-memory copy of the n-th-root table.
+// ---------------------------------------------------------------------------
+template <int L>
+struct Pow2Plan {
+  static constexpr int N = 1 << L;
+  static constexpr int TPT = N / kEPT;
+  static constexpr int NST = (L + 2) / 3;
+  __host__ __device__ static constexpr int radix(int s) {
+    return (L - 3 * s >= 3) ? 8 : ((L - 3 * s == 2) ? 4 : 2);
+  }
+  __host__ __device__ static constexpr int log2radix(int s) {
+    return (L - 3 * s >= 3) ? 3 : (L - 3 * s);
+  }
+};
+
+template <typename T, int DIR, int L, int S, bool PAD>
+__device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx_t<T> *stw,
+                                         cplx_t<T> *sbase, int sj) {
+  using PP = Pow2Plan<L>;
+  constexpr int R = PP::radix(S);
+  constexpr int LR = PP::log2radix(S);
+  constexpr int B = kEPT / R;
+  constexpr int LNS = 3 * S;             // log2 Ns
+  constexpr int NS = 1 << LNS;
+  constexpr bool LAST = S == PP::NST - 1;
+  constexpr int LSTEP = L - LNS - LR;    // log2 (n / (Ns R))
+#pragma unroll
+  for (int u = 0; u < B; ++u) {
+    const int j = t + u * PP::TPT;
+    const int k = j & (NS - 1);
+    cplx_t<T> a[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) a[r] = v[u + r * B];
+    if (S > 0) {
+#pragma unroll
+      for (int r = 1; r < R; ++r) {
+        cplx_t<T> w = stw[(r * k) << LSTEP];
+        if (DIR > 0) w.y = -w.y;
+        a[r] = cmul(a[r], w);
+      }
+    }
+    dftR<T, DIR, R>(a);
+    if (LAST) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) v[u + r * B] = a[r];
+    } else {
+      const int idxD = ((j >> LNS) << (LNS + LR)) + k;
+#pragma unroll
+      for (int r = 0; r < R; ++r) sbase[sidx<PAD>(idxD + r * NS, sj)] = a[r];
+    }
+  }
+  if (!LAST) {
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) v[e] = sbase[sidx<PAD>(t + e * PP::TPT, sj)];
+    __syncthreads();
+  }
+}
+
+template <typename T, int DIR, int L, bool PAD, int S = 0>
+__device__ __forceinline__ void ct_fft(cplx_t<T> (&v)[kEPT], int t, const cplx_t<T> *stw, cplx_t<T> *sbase,
+                                       int sj) {
+  if constexpr (S < Pow2Plan<L>::NST) {
+    ct_stage<T, DIR, L, S, PAD>(v, t, stw, sbase, sj);
+    ct_fft<T, DIR, L, PAD, S + 1>(v, t, stw, sbase, sj);
+  }
+}
+
+// copy the n-th roots of unity to shared memory (caller synchronises)
+template <typename T>
+__device__ __forceinline__ void load_twiddles(cplx_t<T> *stw, const cplx_t<T> *__restrict__ tw, int n) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) stw[i] = tw[i];
+}
+
 // padded row length in shared memory
 __host__ __device__ inline int padded_row(int n) { return n + n / 8; }
 

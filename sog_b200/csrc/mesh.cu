@@ -16,6 +16,7 @@
 //   k_reduce / k_finalize_frames / k_finalize_atoms
 #include <algorithm>
 #include <cfloat>
+#include <type_traits>
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -23,7 +24,7 @@
 #include "host_math.hpp"
 #include "plan.hpp"
 #include "sort.cuh"
-#include "fft_reg.cuh"
+#include "fft_pipe.cuh"
 #include "frames.cuh"
 
 namespace sogb {
@@ -699,6 +700,133 @@ __global__ void __launch_bounds__(256, 2) k_zfused(KsArgs<T> a, int ic, RadixPla
   }
 }
 
+// Persistent, double-buffered form of k_zfused: tile = f*nchunks + chunk,
+// the next tile's spectrum columns stream into shared memory with cp.async
+// while the current one is transformed.  The transformed rho-hat is kept in
+// the current input buffer (same slots), the Green scalars in s_g.
+template <typename T, int L>
+__global__ void __launch_bounds__(256, 1) k_zfused_pipe(KsArgs<T> a, int ic, int64_t ntiles,
+                                                        const cplx_t<T> *__restrict__ twz, int write_spec) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
+  __shared__ double red[2][32];
+  for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
+    s_amp[m] = (double)a.amp[m];
+    s_bw2[m] = (double)a.bw2[m];
+  }
+  constexpr int n = 1 << L, TPT = n / kEPT;
+  const int nthr = blockDim.x;
+  C *buf0 = reinterpret_cast<C *>(smem_raw);
+  C *buf1 = buf0 + (size_t)n * ic;
+  C *xbuf = buf1 + (size_t)n * ic;
+  C *stw = xbuf + (size_t)padded_row(n) * ic;
+  double *s_g = reinterpret_cast<double *>(stw + n);  // [kEPT][2][nthr]
+  load_twiddles<T>(stw, twz, n);
+  const int c = threadIdx.x % ic, t = threadIdx.x / ic;
+  const int64_t inner = (int64_t)a.ny * a.nxh;
+  const int64_t nchunks = (inner + ic - 1) / ic;
+  const int nfield = a.nfield;
+  const double inv = 1.0 / ((double)a.nx * a.ny * a.nz);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the input of tile f*nchunks + chunk is spec[f] viewed as [nz][inner]
+  auto issue = [&](C *buf, int64_t tile) {
+    const int64_t f = tile / nchunks;
+    cols_issue<T>(buf, a.spec + f * a.nh, inner, n, ic, nchunks, tile - f * nchunks);
+  };
+  int64_t tile = blockIdx.x;
+  if (tile < ntiles) issue(buf0, tile);
+  cp_async_commit();
+  __syncthreads();
+  for (int it = 0; tile < ntiles; ++it, tile += gridDim.x) {
+    C *cur = (it & 1) ? buf1 : buf0;
+    C *nxt = (it & 1) ? buf0 : buf1;
+    const int64_t next = tile + gridDim.x;
+    if (next < ntiles) issue(nxt, next);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const int f = (int)(tile / nchunks);
+    const int64_t chunk = tile - (int64_t)f * nchunks;
+    const int64_t col = chunk * ic + c;
+    const bool ok = col < inner;
+    const FrameGeom &g = a.geom[f];
+    C v[kEPT];
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) v[e] = cur[(t + e * TPT) * ic + c];
+    ct_fft<T, -1, L, true>(v, t, stw, xbuf + c, ic);
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) cur[(t + e * TPT) * ic + c] = v[e];  // own slots: no race
+    if (write_spec && ok) {
+      C *sp = const_cast<C *>(a.spec) + (int64_t)f * a.nh + col;
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) sp[(int64_t)(t + e * TPT) * inner] = v[e];
+    }
+    const int mx = ok ? (int)(col % a.nxh) : 0;
+    const int iy = ok ? (int)(col / a.nxh) : 0;
+    const int my = signed_mode(iy, a.ny);
+    const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
+    const double *bt = (g.ortho && a.btab) ? a.btab + (int64_t)f * a.btab_stride : nullptr;
+    double accE = 0.0, accD = 0.0;
+#pragma unroll 1
+    for (int e = 0; e < kEPT; ++e) {
+      const int iz = t + e * TPT;
+      const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr, bt);
+      const bool live = ok && mg.live;
+      const C r = cur[(t + e * TPT) * ic + c];
+      if (live) {
+        const double rr = (double)r.x, ri = (double)r.y;
+        accE += w * mg.gE * (rr * rr + ri * ri);
+        accD += w * mg.gS;
+      }
+      s_g[(2 * e) * nthr + threadIdx.x] = live ? mg.gF * inv : 0.0;
+      s_g[(2 * e + 1) * nthr + threadIdx.x] = live ? mg.gE * inv : 0.0;
+    }
+    C *out = a.fspec ? a.fspec + (int64_t)f * nfield * a.nh + (ok ? col : 0) : nullptr;
+    for (int fl = 0; fl < nfield; ++fl) {
+      const bool force = a.want_force && fl < 3;
+      double km = 0.0, kz = 0.0;
+      if (force) {
+        km = g.kmat[fl * 3 + 0] * mx + g.kmat[fl * 3 + 1] * my;
+        kz = g.kmat[fl * 3 + 2];
+      }
+      C wv[kEPT];
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) {
+        const C r = cur[(t + e * TPT) * ic + c];
+        const double rr = (double)r.x, ri = (double)r.y;
+        if (force) {
+          const double kc = km + kz * signed_mode(t + e * TPT, a.nz);
+          const double sc = s_g[(2 * e) * nthr + threadIdx.x];
+          wv[e] = cmk<C, T>((T)(-kc * sc * ri), (T)(kc * sc * rr));
+        } else {
+          const double sc = s_g[(2 * e + 1) * nthr + threadIdx.x];
+          wv[e] = cmk<C, T>((T)(sc * rr), (T)(sc * ri));
+        }
+      }
+      ct_fft<T, +1, L, true>(wv, t, stw, xbuf + c, ic);
+      if (ok) {
+        C *o = out + (int64_t)fl * a.nh;
+#pragma unroll
+        for (int e = 0; e < kEPT; ++e) o[(int64_t)(t + e * TPT) * inner] = wv[e];
+      }
+    }
+    accE = warp_sum(accE);
+    accD = warp_sum(accD);
+    if (lane == 0) { red[0][warp] = accE; red[1][warp] = accD; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double e = 0.0, d = 0.0;
+      for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) { e += red[0][wi]; d += red[1][wi]; }
+      double *p = a.part + ((int64_t)f * nchunks + chunk) * 2;
+      p[0] = e;
+      p[1] = d;
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+}
+
 // Extras: dE/d(amp_m, bw2_m) partial sums (cubes2_fft.py:822-862) and the
 // reciprocal virial sums (cubes2_fft.py:874-921).  Layout of one partial:
 //   [0, M)        sum w e_m D |rho|^2         (gA main)
@@ -953,6 +1081,46 @@ int cols_per_cta(int n) {
   return std::max(1, std::min(r, 16));
 }
 
+// Persistent grids: one wave of resident CTAs looping over the tiles.
+template <typename K>
+unsigned persistent_grid(K kernel, int threads, size_t smem, int64_t ntiles) {
+  static int nsm = 0;
+  if (!nsm) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    if (nsm <= 0) nsm = 1;
+  }
+  int per = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, threads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    per = 1;
+  }
+  per = std::max(per, 1);
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(ntiles, (int64_t)nsm * per));
+}
+
+// Calls f(std::integral_constant<int, L>) for n = 2^L, 8 <= n <= 1024.
+template <typename Fn>
+bool with_pow2(int n, Fn &&f) {
+  switch (n) {
+    case 8: f(std::integral_constant<int, 3>{}); return true;
+    case 16: f(std::integral_constant<int, 4>{}); return true;
+    case 32: f(std::integral_constant<int, 5>{}); return true;
+    case 64: f(std::integral_constant<int, 6>{}); return true;
+    case 128: f(std::integral_constant<int, 7>{}); return true;
+    case 256: f(std::integral_constant<int, 8>{}); return true;
+    case 512: f(std::integral_constant<int, 9>{}); return true;
+    case 1024: f(std::integral_constant<int, 10>{}); return true;
+    default: return false;
+  }
+}
+
+template <typename K>
+void allow_smem(K kernel) {
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+}
+
 // ---- FFT passes: register-resident kernels for power-of-two axes, the
 // generic shared-memory Stockham otherwise ----
 template <typename T>
@@ -968,14 +1136,27 @@ void pass_x_fwd(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t nbatch, cudaStream
   using C = cplx_t<T>;
   const int nx = p->d.nx;
   const int64_t rows = nbatch * p->d.nz * p->d.ny;
-  if (is_pow2(nx)) {
-    const int rpc = reg_width<T>(nx, 256, 64 * 1024);
-    k_rows_r2c_reg<T><<<nblocks(rows, rpc), (nx / kEPT) * rpc, (size_t)rpc * padded_row(nx) * sizeof(C), st>>>(
-        rho, spec, rows, rpc, p->rpx, p->twx.as<C>());
-  } else {
-    const int rpc = rows_per_cta<T>(nx);
-    k_fft_r2c_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
-        rho, spec, nx, rows, rpc, p->rpx, p->twx.as<C>());
+  const bool done = with_pow2(nx, [&](auto lc) {
+    constexpr int L = decltype(lc)::value;
+    constexpr int n = 1 << L;
+    const int rpc = std::max(1, 256 / (n / kEPT));
+    const int64_t ntiles = (rows + rpc - 1) / rpc;
+    const int thr = (n / kEPT) * rpc;
+    const size_t sm = 2 * (size_t)rpc * n * sizeof(T) + ((size_t)rpc * padded_row(n) + n) * sizeof(C);
+    allow_smem(k_r2c_pipe<T, L>);
+    k_r2c_pipe<T, L><<<persistent_grid(k_r2c_pipe<T, L>, thr, sm, ntiles), thr, sm, st>>>(
+        rho, spec, rows, rpc, ntiles, p->twx.as<C>());
+  });
+  if (!done) {
+    if (is_pow2(nx)) {
+      const int rpc = reg_width<T>(nx, 256, 64 * 1024);
+      k_rows_r2c_reg<T><<<nblocks(rows, rpc), (nx / kEPT) * rpc, (size_t)rpc * padded_row(nx) * sizeof(C), st>>>(
+          rho, spec, rows, rpc, p->rpx, p->twx.as<C>());
+    } else {
+      const int rpc = rows_per_cta<T>(nx);
+      k_fft_r2c_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
+          rho, spec, nx, rows, rpc, p->rpx, p->twx.as<C>());
+    }
   }
   after(&p->tr, st, "fft_r2c_x");
 }
@@ -986,18 +1167,35 @@ void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nframes, int F,
   using C = cplx_t<T>;
   const int nx = p->d.nx;
   const int64_t nzy = (int64_t)p->d.nz * p->d.ny;
-  if (is_pow2(nx)) {
-    const int tpt = nx / kEPT;
+  const bool done = with_pow2(nx, [&](auto lc) {
+    constexpr int L = decltype(lc)::value;
+    constexpr int n = 1 << L;
+    const int tpt = n / kEPT;
     const int rpc = std::max(1, 256 / (tpt * F));
     const int64_t rows = nframes * nzy;
-    const size_t sm = std::max((size_t)rpc * F * padded_row(nx) * sizeof(C), (size_t)rpc * nx * F * sizeof(T));
-    k_rows_c2r_il<T><<<nblocks(rows, rpc), tpt * F * rpc, sm, st>>>(fspec, freal, F, nzy, rows, rpc, p->rpx,
-                                                                      p->twx.as<C>());
-  } else {
-    const int rpc = rows_per_cta<T>(nx);
-    const int64_t rows = nframes * F * nzy;
-    k_fft_c2r_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
-        fspec, freal, nx, rows, rpc, p->rpx, p->twx.as<C>(), F, nzy);
+    const int64_t ntiles = (rows + rpc - 1) / rpc;
+    const int nxh = n / 2 + 1;
+    const int thr = tpt * F * rpc;
+    const size_t xsz = std::max((size_t)rpc * F * padded_row(n) * sizeof(C), (size_t)rpc * n * F * sizeof(T));
+    const size_t sm = 2 * (size_t)rpc * F * nxh * sizeof(C) + ((xsz + 15) & ~(size_t)15) + (size_t)n * sizeof(C);
+    allow_smem(k_c2r_pipe<T, L>);
+    k_c2r_pipe<T, L><<<persistent_grid(k_c2r_pipe<T, L>, thr, sm, ntiles), thr, sm, st>>>(
+        fspec, freal, F, nzy, rows, rpc, ntiles, p->twx.as<C>());
+  });
+  if (!done) {
+    if (is_pow2(nx)) {
+      const int tpt = nx / kEPT;
+      const int rpc = std::max(1, 256 / (tpt * F));
+      const int64_t rows = nframes * nzy;
+      const size_t sm = std::max((size_t)rpc * F * padded_row(nx) * sizeof(C), (size_t)rpc * nx * F * sizeof(T));
+      k_rows_c2r_il<T><<<nblocks(rows, rpc), tpt * F * rpc, sm, st>>>(fspec, freal, F, nzy, rows, rpc, p->rpx,
+                                                                        p->twx.as<C>());
+    } else {
+      const int rpc = rows_per_cta<T>(nx);
+      const int64_t rows = nframes * F * nzy;
+      k_fft_c2r_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
+          fspec, freal, nx, rows, rpc, p->rpx, p->twx.as<C>(), F, nzy);
+    }
   }
   after(&p->tr, st, "fft_c2r_x");
 }
@@ -1007,20 +1205,41 @@ template <typename T, int DIR>
 void pass_cols(sog_plan *p, cplx_t<T> *data, int n, int64_t inner, int64_t outer, const RadixPlan &rp,
                const cplx_t<T> *tw, cudaStream_t st, const char *name) {
   using C = cplx_t<T>;
-  if (is_pow2(n)) {
-    const int ic = reg_width<T>(n, 256, 64 * 1024);
+  const bool done = with_pow2(n, [&](auto lc) {
+    constexpr int L = decltype(lc)::value;
+    constexpr int nn = 1 << L;
+    const int ic = reg_width<T>(nn, 256, 64 * 1024);
     const int64_t nchunks = (inner + ic - 1) / ic;
-    if (ic >= 8)
-      k_cols_reg<T, DIR, false><<<(unsigned)(outer * nchunks), (n / kEPT) * ic, (size_t)n * ic * sizeof(C), st>>>(
-          data, inner, ic, rp, tw);
-    else
-      k_cols_reg<T, DIR, true><<<(unsigned)(outer * nchunks), (n / kEPT) * ic,
-                                 (size_t)padded_row(n) * ic * sizeof(C), st>>>(data, inner, ic, rp, tw);
-  } else {
-    const int ic = cols_per_cta<T>(n);
-    const int64_t nchunks = (inner + ic - 1) / ic;
-    k_fft_strided<T, DIR><<<(unsigned)(outer * nchunks), 256, fft_rows_smem<T>(n, ic), st>>>(
-        data, inner, outer, ic, rp, tw);
+    const int64_t ntiles = outer * nchunks;
+    const int thr = (nn / kEPT) * ic;
+    if (ic >= 8) {
+      const size_t sm = (3 * (size_t)nn * ic + nn) * sizeof(C);
+      allow_smem(k_cols_pipe<T, DIR, false, L>);
+      k_cols_pipe<T, DIR, false, L><<<persistent_grid(k_cols_pipe<T, DIR, false, L>, thr, sm, ntiles), thr, sm,
+                                      st>>>(data, inner, ic, ntiles, tw);
+    } else {
+      const size_t sm = ((2 * (size_t)nn + padded_row(nn)) * ic + nn) * sizeof(C);
+      allow_smem(k_cols_pipe<T, DIR, true, L>);
+      k_cols_pipe<T, DIR, true, L><<<persistent_grid(k_cols_pipe<T, DIR, true, L>, thr, sm, ntiles), thr, sm,
+                                     st>>>(data, inner, ic, ntiles, tw);
+    }
+  });
+  if (!done) {
+    if (is_pow2(n)) {
+      const int ic = reg_width<T>(n, 256, 64 * 1024);
+      const int64_t nchunks = (inner + ic - 1) / ic;
+      if (ic >= 8)
+        k_cols_reg<T, DIR, false><<<(unsigned)(outer * nchunks), (n / kEPT) * ic, (size_t)n * ic * sizeof(C), st>>>(
+            data, inner, ic, rp, tw);
+      else
+        k_cols_reg<T, DIR, true><<<(unsigned)(outer * nchunks), (n / kEPT) * ic,
+                                   (size_t)padded_row(n) * ic * sizeof(C), st>>>(data, inner, ic, rp, tw);
+    } else {
+      const int ic = cols_per_cta<T>(n);
+      const int64_t nchunks = (inner + ic - 1) / ic;
+      k_fft_strided<T, DIR><<<(unsigned)(outer * nchunks), 256, fft_rows_smem<T>(n, ic), st>>>(
+          data, inner, outer, ic, rp, tw);
+    }
   }
   after(&p->tr, st, name);
 }
@@ -1267,6 +1486,26 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   const int zic = zfuse ? reg_width<T>(nz, 256, 32 * 1024) : 0;
   const int64_t zchunks = zfuse ? ((int64_t)ny * nxh + zic - 1) / zic : 0;
   const int64_t nblk_e = zfuse ? zchunks : (int64_t)ks_blocks;
+  auto launch_zfused = [&]() {
+    const int write_spec = (want_grad || want_vir) ? 1 : 0;
+    const bool done = with_pow2(nz, [&](auto lc) {
+      constexpr int L = decltype(lc)::value;
+      constexpr int n = 1 << L;
+      const int zthr = (n / kEPT) * zic;
+      const size_t zsm = ((2 * (size_t)n + padded_row(n)) * zic + n) * sizeof(C) +
+                         (size_t)zthr * kEPT * 2 * sizeof(double);
+      const int64_t ztiles = zchunks * nf;
+      allow_smem(k_zfused_pipe<T, L>);
+      k_zfused_pipe<T, L><<<persistent_grid(k_zfused_pipe<T, L>, zthr, zsm, ztiles), zthr, zsm, st>>>(
+          ka, zic, ztiles, p->twz.as<C>(), write_spec);
+    });
+    if (!done) {
+      const size_t zsm = (size_t)padded_row(nz) * zic * sizeof(C) +
+                         (size_t)(nz / kEPT) * zic * kEPT * (sizeof(C) + 2 * sizeof(double));
+      k_zfused<T><<<(unsigned)(zchunks * nf), (nz / kEPT) * zic, zsm, st>>>(ka, zic, p->rpz, p->twz.as<C>(),
+                                                                            write_spec);
+    }
+  };
   for (int c = 0; c < nch; ++c) {
     sa.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
     dispatch_spread<T>(sa, P, nf, st, tr);
@@ -1274,10 +1513,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
     pass_cols<T, -1>(p, p->spec.as<C>(), ny, nxh, (int64_t)nf * nz, p->rpy, p->twy.as<C>(), st, "fft_y_fwd");
     ka.part = p->partE.as<double>() + (int64_t)c * nf * nblk_e * 2;
     if (zfuse) {
-      const size_t zsm = (size_t)padded_row(nz) * zic * sizeof(C) +
-                         (size_t)(nz / kEPT) * zic * kEPT * (sizeof(C) + 2 * sizeof(double));
-      k_zfused<T><<<(unsigned)(zchunks * nf), (nz / kEPT) * zic, zsm, st>>>(
-          ka, zic, p->rpz, p->twz.as<C>(), (want_grad || want_vir) ? 1 : 0);
+      launch_zfused();
       after(tr, st, "zfused");
     } else {
       pass_cols<T, -1>(p, p->spec.as<C>(), nz, (int64_t)ny * nxh, nf, p->rpz, p->twz.as<C>(), st, "fft_z_fwd");
