@@ -97,18 +97,22 @@ __global__ void k_cols_pipe(cplx_t<T> *__restrict__ data, int64_t inner, int ic,
 }
 
 // ---------------------------------------------------------------------------
-// rows, forward R2C: tile = rpc rows of n reals
+// rows, forward R2C of length n = 2^L as a length n/2 complex FFT
+//   z[m] = x[2m] + i x[2m+1],  Z = DFT_{n/2}(z),
+//   X[k] = (Z[k] + conj Z[n/2-k]) / 2 - i W_n^k (Z[k] - conj Z[n/2-k]) / 2,
+// Z[n/2] = Z[0]; k = 0 .. n/2.  tile = rpc rows; TPT = n/16 threads per row.
 // ---------------------------------------------------------------------------
 template <typename T, int L>
 __global__ void k_r2c_pipe(const T *__restrict__ in, cplx_t<T> *__restrict__ out, int64_t nrows, int rpc,
                            int64_t ntiles, const cplx_t<T> *__restrict__ tw) {
   using C = cplx_t<T>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  constexpr int n = 1 << L, TPT = n / kEPT, nxh = n / 2 + 1;
+  constexpr int n = 1 << L, h = n / 2, TPT = h / kEPT, nxh = h + 1;
+  constexpr int hp = padded_row(h);
   T *buf0 = reinterpret_cast<T *>(smem_raw);
   T *buf1 = buf0 + (size_t)rpc * n;
   C *xbuf = reinterpret_cast<C *>(buf1 + (size_t)rpc * n);
-  C *stw = xbuf + (size_t)rpc * padded_row(n);
+  C *stw = xbuf + (size_t)rpc * hp;
   load_twiddles<T>(stw, tw, n);
   const int t = threadIdx.x % TPT, rr = threadIdx.x / TPT;
   constexpr int per = 16 / (int)sizeof(T);
@@ -125,6 +129,7 @@ __global__ void k_r2c_pipe(const T *__restrict__ in, cplx_t<T> *__restrict__ out
   int64_t tile = blockIdx.x;
   if (tile < ntiles) issue(buf0, tile);
   cp_async_commit();
+  C *zrow = xbuf + (size_t)rr * hp;
   for (int it = 0; tile < ntiles; ++it, tile += gridDim.x) {
     T *cur = (it & 1) ? buf1 : buf0;
     T *nxt = (it & 1) ? buf0 : buf1;
@@ -134,15 +139,31 @@ __global__ void k_r2c_pipe(const T *__restrict__ in, cplx_t<T> *__restrict__ out
     cp_async_wait<1>();
     __syncthreads();
     C v[kEPT];
+    const T *xr = cur + (size_t)rr * n;
 #pragma unroll
-    for (int e = 0; e < kEPT; ++e) v[e] = cmk<C, T>(cur[rr * n + t + e * TPT], T(0));
-    ct_fft<T, -1, L, true>(v, t, stw, xbuf + (size_t)rr * padded_row(n), 1);
+    for (int e = 0; e < kEPT; ++e) {
+      const int m = t + e * TPT;
+      v[e] = cmk<C, T>(xr[2 * m], xr[2 * m + 1]);
+    }
+    ct_fft<T, -1, L - 1, true, 1>(v, t, stw, zrow, 1);
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) zrow[sidx<true>(t + e * TPT, 1)] = v[e];
+    __syncthreads();
     const int64_t row = tile * rpc + rr;
     if (row < nrows) {
+      C *o = out + row * nxh;
 #pragma unroll
       for (int e = 0; e < kEPT; ++e) {
-        const int idx = t + e * TPT;
-        if (idx < nxh) out[row * nxh + idx] = v[e];
+        const int k = t + e * TPT;
+        const C a = v[e];
+        const C b = zrow[sidx<true>((h - k) & (h - 1), 1)];
+        const T er = T(0.5) * (a.x + b.x), ei = T(0.5) * (a.y - b.y);   // (Z + conj Z')/2
+        const T dr = T(0.5) * (a.x - b.x), di = T(0.5) * (a.y + b.y);   // (Z - conj Z')/2
+        const C w = stw[k];                                             // W_n^k
+        // -i * w * d
+        const T pr = w.x * dr - w.y * di, pi = w.x * di + w.y * dr;
+        o[k] = cmk<C, T>(er + pi, ei - pr);
+        if (k == 0) o[h] = cmk<C, T>(er - pi, ei + pr);                 // k = n/2: W^{n/2} = -1
       }
     }
     __syncthreads();
@@ -151,21 +172,24 @@ __global__ void k_r2c_pipe(const T *__restrict__ in, cplx_t<T> *__restrict__ out
 }
 
 // ---------------------------------------------------------------------------
-// rows, inverse C2R of F fields with interleaved output (see k_rows_c2r_il)
+// rows, inverse C2R of F fields (interleaved output) as length n/2 complex
+// inverse FFTs:  Z[k] = A + i e^{2 pi i k/n} B  with
+//   A = X[k] + conj X[n/2-k],  B = X[k] - conj X[n/2-k]   (1 <= k < n/2),
+//   Z[0] = (Re X0 + Re Xh) + i (Re X0 - Re Xh),
+// then x[2m] = Re z[m], x[2m+1] = Im z[m] for z = IDFT_{n/2}(Z) (unnormalised);
+// the imaginary parts of X[0], X[n/2] are ignored as in torch.fft.irfftn.
 // ---------------------------------------------------------------------------
-// Shared memory: 2 input tiles (rpc*F half rows), the exchange / output
-// staging area and the n roots of unity.
 template <typename T, int L>
 __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out, int F, int64_t nzy,
                            int64_t nrows, int rpc, int64_t ntiles, const cplx_t<T> *__restrict__ tw) {
   using C = cplx_t<T>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  constexpr int n = 1 << L, TPT = n / kEPT, nxh = n / 2 + 1;
-  const int hrow = nxh;
+  constexpr int n = 1 << L, h = n / 2, TPT = h / kEPT, nxh = h + 1;
+  constexpr int hp = padded_row(h);
   C *buf0 = reinterpret_cast<C *>(smem_raw);
-  C *buf1 = buf0 + (size_t)rpc * F * hrow;
-  C *xbuf = buf1 + (size_t)rpc * F * hrow;  // exchanges, then the interleaved output staging
-  const size_t xsz = max((size_t)rpc * F * padded_row(n) * sizeof(C), (size_t)rpc * n * F * sizeof(T));
+  C *buf1 = buf0 + (size_t)rpc * F * nxh;
+  C *xbuf = buf1 + (size_t)rpc * F * nxh;  // exchanges, then the interleaved output staging
+  const size_t xsz = max((size_t)rpc * F * hp * sizeof(C), (size_t)rpc * n * F * sizeof(T));
   C *stw = reinterpret_cast<C *>(reinterpret_cast<unsigned char *>(xbuf) + ((xsz + 15) & ~(size_t)15));
   load_twiddles<T>(stw, tw, n);
   const int t = threadIdx.x % TPT, q = threadIdx.x / TPT;
@@ -180,7 +204,7 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
       const bool ok = row < nrows;
       const int64_t frame = ok ? row / nzy : 0, zy = ok ? row - frame * nzy : 0;
       const C *src = in + ((frame * F + f2) * nzy + zy) * nxh + col;
-      cp_async_elem(buf + (size_t)hr * hrow + col, ok ? src : in, ok);
+      cp_async_elem(buf + qq, ok ? src : in, ok);
     }
   };
   int64_t tile = blockIdx.x;
@@ -194,23 +218,32 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    const C *h = cur + (size_t)(rr * F + f) * hrow;
+    const C *X = cur + (size_t)(rr * F + f) * nxh;
     C v[kEPT];
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) {
-      const int m = t + e * TPT;
-      if (m < nxh) {
-        v[e] = h[m];
+      const int k = t + e * TPT;
+      if (k == 0) {
+        const T x0 = X[0].x, xh = X[h].x;
+        v[e] = cmk<C, T>(x0 + xh, x0 - xh);
       } else {
-        const C x = h[n - m];
-        v[e] = cmk<C, T>(x.x, -x.y);
+        const C a = X[k], b = X[h - k];
+        const T Ar = a.x + b.x, Ai = a.y - b.y;      // X[k] + conj X[h-k]
+        const T Br = a.x - b.x, Bi = a.y + b.y;      // X[k] - conj X[h-k]
+        const C w = stw[k];                          // e^{-2 pi i k/n}; use its conjugate
+        const T cr = w.x * Br + w.y * Bi, ci = w.x * Bi - w.y * Br;   // conj(w) * B
+        v[e] = cmk<C, T>(Ar - ci, Ai + cr);          // A + i conj(w) B
       }
     }
-    ct_fft<T, +1, L, true>(v, t, stw, xbuf + (size_t)(rr * F + f) * padded_row(n), 1);
+    ct_fft<T, +1, L - 1, true, 1>(v, t, stw, xbuf + (size_t)(rr * F + f) * hp, 1);
     __syncthreads();
     T *so = reinterpret_cast<T *>(xbuf);
 #pragma unroll
-    for (int e = 0; e < kEPT; ++e) so[((size_t)rr * n + t + e * TPT) * F + f] = v[e].x;
+    for (int e = 0; e < kEPT; ++e) {
+      const int m = t + e * TPT;
+      so[((size_t)rr * n + 2 * m) * F + f] = v[e].x;
+      so[((size_t)rr * n + 2 * m + 1) * F + f] = v[e].y;
+    }
     __syncthreads();
     const int64_t row0 = tile * rpc;
     const int64_t nvalid = min((int64_t)rpc, nrows - row0) * n * F;

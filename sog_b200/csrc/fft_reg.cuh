@@ -107,7 +107,8 @@ struct Pow2Plan {
   }
 };
 
-template <typename T, int DIR, int L, int S, bool PAD>
+// TWS: the shared twiddle table holds the roots of unity of order 2^(L+TWS).
+template <typename T, int DIR, int L, int S, bool PAD, int TWS>
 __device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx_t<T> *stw,
                                          cplx_t<T> *sbase, int sj) {
   using PP = Pow2Plan<L>;
@@ -128,7 +129,7 @@ __device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx
     if (S > 0) {
 #pragma unroll
       for (int r = 1; r < R; ++r) {
-        cplx_t<T> w = stw[(r * k) << LSTEP];
+        cplx_t<T> w = stw[(r * k) << (LSTEP + TWS)];
         if (DIR > 0) w.y = -w.y;
         a[r] = cmul(a[r], w);
       }
@@ -151,12 +152,12 @@ __device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx
   }
 }
 
-template <typename T, int DIR, int L, bool PAD, int S = 0>
+template <typename T, int DIR, int L, bool PAD, int TWS = 0, int S = 0>
 __device__ __forceinline__ void ct_fft(cplx_t<T> (&v)[kEPT], int t, const cplx_t<T> *stw, cplx_t<T> *sbase,
                                        int sj) {
   if constexpr (S < Pow2Plan<L>::NST) {
-    ct_stage<T, DIR, L, S, PAD>(v, t, stw, sbase, sj);
-    ct_fft<T, DIR, L, PAD, S + 1>(v, t, stw, sbase, sj);
+    ct_stage<T, DIR, L, S, PAD, TWS>(v, t, stw, sbase, sj);
+    ct_fft<T, DIR, L, PAD, TWS, S + 1>(v, t, stw, sbase, sj);
   }
 }
 
@@ -167,7 +168,7 @@ __device__ __forceinline__ void load_twiddles(cplx_t<T> *stw, const cplx_t<T> *_
 }
 
 // padded row length in shared memory
-__host__ __device__ inline int padded_row(int n) { return n + n / 8; }
+__host__ __device__ constexpr int padded_row(int n) { return n + n / 8; }
 
 // C2C along a strided axis: data viewed as [outer][n][inner]; a CTA owns one
 // outer index and `ic` consecutive inner columns; thread (t, c), c fastest.

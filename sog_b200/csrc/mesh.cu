@@ -1136,13 +1136,14 @@ void pass_x_fwd(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t nbatch, cudaStream
   using C = cplx_t<T>;
   const int nx = p->d.nx;
   const int64_t rows = nbatch * p->d.nz * p->d.ny;
-  const bool done = with_pow2(nx, [&](auto lc) {
-    constexpr int L = decltype(lc)::value;
+  const bool done = nx >= 16 && with_pow2(nx, [&](auto lc) {
+    constexpr int L = decltype(lc)::value < 4 ? 4 : decltype(lc)::value;
     constexpr int n = 1 << L;
-    const int rpc = std::max(1, 256 / (n / kEPT));
+    const int tpt = n / 2 / kEPT;
+    const int rpc = std::max(1, 256 / tpt);
     const int64_t ntiles = (rows + rpc - 1) / rpc;
-    const int thr = (n / kEPT) * rpc;
-    const size_t sm = 2 * (size_t)rpc * n * sizeof(T) + ((size_t)rpc * padded_row(n) + n) * sizeof(C);
+    const int thr = tpt * rpc;
+    const size_t sm = 2 * (size_t)rpc * n * sizeof(T) + ((size_t)rpc * padded_row(n / 2) + n) * sizeof(C);
     allow_smem(k_r2c_pipe<T, L>);
     k_r2c_pipe<T, L><<<persistent_grid(k_r2c_pipe<T, L>, thr, sm, ntiles), thr, sm, st>>>(
         rho, spec, rows, rpc, ntiles, p->twx.as<C>());
@@ -1167,16 +1168,16 @@ void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nframes, int F,
   using C = cplx_t<T>;
   const int nx = p->d.nx;
   const int64_t nzy = (int64_t)p->d.nz * p->d.ny;
-  const bool done = with_pow2(nx, [&](auto lc) {
-    constexpr int L = decltype(lc)::value;
+  const bool done = nx >= 16 && with_pow2(nx, [&](auto lc) {
+    constexpr int L = decltype(lc)::value < 4 ? 4 : decltype(lc)::value;
     constexpr int n = 1 << L;
-    const int tpt = n / kEPT;
+    const int tpt = n / 2 / kEPT;
     const int rpc = std::max(1, 256 / (tpt * F));
     const int64_t rows = nframes * nzy;
     const int64_t ntiles = (rows + rpc - 1) / rpc;
     const int nxh = n / 2 + 1;
     const int thr = tpt * F * rpc;
-    const size_t xsz = std::max((size_t)rpc * F * padded_row(n) * sizeof(C), (size_t)rpc * n * F * sizeof(T));
+    const size_t xsz = std::max((size_t)rpc * F * padded_row(n / 2) * sizeof(C), (size_t)rpc * n * F * sizeof(T));
     const size_t sm = 2 * (size_t)rpc * F * nxh * sizeof(C) + ((xsz + 15) & ~(size_t)15) + (size_t)n * sizeof(C);
     allow_smem(k_c2r_pipe<T, L>);
     k_c2r_pipe<T, L><<<persistent_grid(k_c2r_pipe<T, L>, thr, sm, ntiles), thr, sm, st>>>(
