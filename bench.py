@@ -132,19 +132,17 @@ class ClockSampler:
         self.t = None
 
     def start(self):
+        # nvidia-smi writes to a file: no reader thread competes with the
+        # launching thread during the timed region
+        import tempfile
+        self.path = tempfile.mktemp(prefix="sog_clocks_", suffix=".csv")
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+                 "--format=csv,noheader,nounits", "-lms", "200", "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
 
     def stop(self):
         if self.proc is None:
@@ -154,8 +152,12 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        if self.t:
-            self.t.join(timeout=2)
+        try:
+            with open(self.path) as fh:
+                self.lines = [ln.strip() for ln in fh if ln.strip()]
+            os.remove(self.path)
+        except Exception:
+            self.lines = []
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:

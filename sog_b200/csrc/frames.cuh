@@ -177,6 +177,7 @@ struct FinalArgs {
   const FrameGeom *geom;
   const double *redE;    // [nf][C][2]
   const double *redX;    // [nf][C][4M+13] or null
+  const double *redD;    // [nf] self sums (sum_w gS) when not in redE, or null
   const double *qsum;    // [nf][C][2]
   const void *amp, *bw2;
   int M, nch, nx, ny, nz;
@@ -198,7 +199,7 @@ __global__ void k_finalize_frames(FinalArgs a, int nf) {
   const double sc = a.direct ? 1.0 / (2.0 * V) : 0.5 * V / (N3 * N3);
   const T *amp = (const T *)a.amp;
   const T *bw2 = (const T *)a.bw2;
-  const double diag = a.redE[((int64_t)f * a.nch + 0) * 2 + 1] / (2.0 * V);
+  const double diag = (a.redD ? a.redD[f] : a.redE[((int64_t)f * a.nch + 0) * 2 + 1]) / (2.0 * V);
   double E = 0.0, Q = 0.0, QQ = 0.0, pen = 0.0;
   for (int c = 0; c < a.nch; ++c) {
     const double qs = a.qsum[((int64_t)f * a.nch + c) * 2 + 0];

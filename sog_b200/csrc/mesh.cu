@@ -369,6 +369,10 @@ struct KsArgs {
   // frames: per frame [M][nxh] (x), [M][ny] (y), [M][nz] (z)
   const double *btab;
   int64_t btab_stride;
+  // Green tables [nf][nh]: gE (energy / potential) and, for frames whose
+  // B-spline aliases fall inside the cutoff, gF (ik forces)
+  double *gtab, *gtabF;
+  double *partD;           // [nf][gridDim.x] self-sum partials of k_green
 };
 
 // Per-axis Gaussian factors of the frame (the per-axis tables of
@@ -821,6 +825,194 @@ __global__ void __launch_bounds__(256, 1) k_zfused_pipe(KsArgs<T> a, int ic, int
       double *p = a.part + ((int64_t)f * nchunks + chunk) * 2;
       p[0] = e;
       p[1] = d;
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+}
+
+// Green tables: one thread per half-spectrum mode writes gE(k) (and gF(k)
+// for alias frames) and the block's share of the self sum sum_w gS.  The
+// Green function depends on the box and the kernel parameters only, so the
+// fused z pass below just streams it next to the spectrum.
+template <typename T>
+__global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
+  __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
+  __shared__ double red[8];
+  for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
+    s_amp[m] = (double)a.amp[m];
+    s_bw2[m] = (double)a.bw2[m];
+  }
+  __syncthreads();
+  const int f = blockIdx.y;
+  const FrameGeom &g = a.geom[f];
+  const int64_t inner = (int64_t)a.ny * a.nxh;
+  const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // (iy, mx) column
+  double accD = 0.0;
+  if (col < inner) {
+    const int mx = (int)(col % a.nxh), iy = (int)(col / a.nxh);
+    const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
+    double *gout = a.gtab + (int64_t)f * a.nh + col;
+    double *gfout = (g.pad && a.gtabF) ? a.gtabF + (int64_t)f * a.nh + col : nullptr;
+    if (g.ortho && a.btab && !g.pad) {
+      // separable path: K = sum_m amp_m (Bx_m By_m) Bz_m, hoisting Bx_m By_m
+      const int M = a.M;
+      const double *bt = a.btab + (int64_t)f * a.btab_stride;
+      const double *bx = bt, *by = bt + M * a.nxh, *bz = by + M * a.ny;
+      double axy[kMaxGauss];
+#pragma unroll 16
+      for (int m = 0; m < M; ++m) axy[m] = s_amp[m] * bx[m * a.nxh + mx] * by[m * a.ny + iy];
+      const double kx = g.kmat[0] * mx, ky = g.kmat[4] * signed_mode(iy, a.ny);
+      const double kxy2 = kx * kx + ky * ky;
+      const double txy = a.tx[mx] * a.ty[iy];
+      const bool quads = a.spline == SOG_SPLINE_QUADS;
+      for (int iz = 0; iz < a.nz; ++iz) {
+        const int mz = signed_mode(iz, a.nz);
+        const double kz = g.kmat[8] * mz;
+        const double ksq = kxy2 + kz * kz;
+        const bool live = !((mx | iy | mz) == 0) && ksq <= g.k_sq_max;
+        double K = 0.0;
+        if (live) {
+#pragma unroll 16
+          for (int m = 0; m < M; ++m) K += axy[m] * bz[m * a.nz + iz];
+        }
+        double D = txy * a.tz[iz];
+        if (quads) D = 1.0 / (D < 1e-20 ? 1e-20 : D);
+        const double gE = live ? K * D : 0.0;
+        gout[(int64_t)iz * inner] = gE;
+        if (live) accD += w * K;
+      }
+    } else {
+      const double *bt = (g.ortho && a.btab) ? a.btab + (int64_t)f * a.btab_stride : nullptr;
+      for (int iz = 0; iz < a.nz; ++iz) {
+        const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr, bt);
+        gout[(int64_t)iz * inner] = mg.live ? mg.gE : 0.0;
+        if (gfout) gfout[(int64_t)iz * inner] = mg.live ? mg.gF : 0.0;
+        if (mg.live) accD += w * mg.gS;
+      }
+    }
+  }
+  accD = warp_sum(accD);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = accD;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double d = 0.0;
+    for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) d += red[wi];
+    a.partD[(int64_t)f * gridDim.x + blockIdx.x] = d;
+  }
+}
+
+// one 8-byte element per call (the gE table tile)
+__device__ __forceinline__ void cp_async_f64(double *dst, const double *src, bool valid) {
+  cp_async8(dst, src, valid);
+}
+
+// Fused z pass (power-of-two nz) with the Green function read from k_green's
+// table: forward z-FFT of ic spectrum columns, energy partial sum, and for
+// every field the scaled spectrum (i k_a gF rho / N or gE rho / N) inverse
+// z-transformed.  Spectrum and gE tiles are double-buffered with cp.async.
+template <typename T, int L>
+__global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_t ntiles,
+                                                     const cplx_t<T> *__restrict__ twz, int write_spec) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ double red[8];
+  constexpr int n = 1 << L, TPT = n / kEPT;
+  C *buf0 = reinterpret_cast<C *>(smem_raw);
+  C *buf1 = buf0 + (size_t)n * ic;
+  C *xbuf = buf1 + (size_t)n * ic;
+  C *stw = xbuf + (size_t)padded_row(n) * ic;
+  load_twiddles<T>(stw, twz, n);
+  const int c = threadIdx.x % ic, t = threadIdx.x / ic;
+  const int64_t inner = (int64_t)a.ny * a.nxh;
+  const int64_t nchunks = (inner + ic - 1) / ic;
+  const int nfield = a.nfield;
+  const double inv = 1.0 / ((double)a.nx * a.ny * a.nz);
+  auto issue = [&](C *buf, int64_t tile) {
+    const int64_t f = tile / nchunks;
+    cols_issue<T>(buf, a.spec + f * a.nh, inner, n, ic, nchunks, tile - f * nchunks);
+  };
+  int64_t tile = blockIdx.x;
+  if (tile < ntiles) issue(buf0, tile);
+  cp_async_commit();
+  for (int it = 0; tile < ntiles; ++it, tile += gridDim.x) {
+    C *cur = (it & 1) ? buf1 : buf0;
+    const int64_t next = tile + gridDim.x;
+    if (next < ntiles) issue((it & 1) ? buf0 : buf1, next);
+    cp_async_commit();
+    const int f = (int)(tile / nchunks);
+    const int64_t chunk = tile - (int64_t)f * nchunks;
+    const int64_t col = chunk * ic + c;
+    const bool ok = col < inner;
+    const FrameGeom &g = a.geom[f];
+    // Green values of this thread's modes: loads in flight during the FFT
+    double gs[kEPT];
+    const double *gp = a.gtab + (int64_t)f * a.nh + (ok ? col : 0);
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) gs[e] = ok ? gp[(int64_t)(t + e * TPT) * inner] : 0.0;
+    cp_async_wait<1>();
+    __syncthreads();
+    C v[kEPT];
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) v[e] = cur[(t + e * TPT) * ic + c];
+    ct_fft<T, -1, L, true>(v, t, stw, xbuf + c, ic);
+    const int mx = ok ? (int)(col % a.nxh) : 0;
+    const int iy = ok ? (int)(col / a.nxh) : 0;
+    const int my = signed_mode(iy, a.ny);
+    const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
+    double accE = 0.0;
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) {
+      const int slot = (t + e * TPT) * ic + c;
+      const double rr = (double)v[e].x, ri = (double)v[e].y;
+      accE += w * gs[e] * (rr * rr + ri * ri);
+      cur[slot] = v[e];             // own slots: no race
+      gs[e] *= inv;
+    }
+    if (write_spec && ok) {
+      C *sp = const_cast<C *>(a.spec) + (int64_t)f * a.nh + col;
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) sp[(int64_t)(t + e * TPT) * inner] = v[e];
+    }
+    const double *gFp = (g.pad && a.gtabF) ? a.gtabF + (int64_t)f * a.nh + (ok ? col : 0) : nullptr;
+    C *out = a.fspec ? a.fspec + (int64_t)f * nfield * a.nh + (ok ? col : 0) : nullptr;
+    for (int fl = 0; fl < nfield; ++fl) {
+      const bool force = a.want_force && fl < 3;
+      double km = 0.0, kz = 0.0;
+      if (force) {
+        km = g.kmat[fl * 3 + 0] * mx + g.kmat[fl * 3 + 1] * my;
+        kz = g.kmat[fl * 3 + 2];
+      }
+      C wv[kEPT];
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) {
+        const int slot = (t + e * TPT) * ic + c;
+        const C r = cur[slot];
+        const double rr = (double)r.x, ri = (double)r.y;
+        if (force) {
+          const double kc = km + kz * signed_mode(t + e * TPT, a.nz);
+          const double sc = gFp ? (ok ? gFp[(int64_t)(t + e * TPT) * inner] * inv : 0.0) : gs[e];
+          wv[e] = cmk<C, T>((T)(-kc * sc * ri), (T)(kc * sc * rr));
+        } else {
+          wv[e] = cmk<C, T>((T)(gs[e] * rr), (T)(gs[e] * ri));
+        }
+      }
+      ct_fft<T, +1, L, true>(wv, t, stw, xbuf + c, ic);
+      if (ok) {
+        C *o = out + (int64_t)fl * a.nh;
+#pragma unroll
+        for (int e = 0; e < kEPT; ++e) o[(int64_t)(t + e * TPT) * inner] = wv[e];
+      }
+    }
+    accE = warp_sum(accE);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = accE;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double e = 0.0;
+      for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) e += red[wi];
+      double *p = a.part + ((int64_t)f * nchunks + chunk) * 2;
+      p[0] = e;
+      p[1] = 0.0;
     }
     __syncthreads();
   }
@@ -1463,6 +1655,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   k_axis_tables<T><<<dim3(nblocks(ka.btab_stride, 256), nf), 256, 0, st>>>(geom, (const T *)a->bw2, M, nx, ny,
                                                                           nz, p->btab.as<double>());
   after(tr, st, "axis_tables");
+  ka.gtab = ka.gtabF = ka.partD = nullptr;
 
   GatherArgs<T> gar;
   gar.s_anchor = p->s_anchor.as<int4>();
@@ -1487,17 +1680,34 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   const int zic = zfuse ? reg_width<T>(nz, 256, 32 * 1024) : 0;
   const int64_t zchunks = zfuse ? ((int64_t)ny * nxh + zic - 1) / zic : 0;
   const int64_t nblk_e = zfuse ? zchunks : (int64_t)ks_blocks;
+  double *redD = nullptr;
+  if (zfuse) {
+    // Green tables and the self sum, once per call (independent of the charges)
+    const bool aliasable = p->d.spline == SOG_SPLINE_BSPLINE;
+    if (p->gtab.reserve(sizeof(double) * nh * nf) ||
+        (aliasable && p->gtabF.reserve(sizeof(double) * nh * nf)) ||
+        p->partD.reserve(sizeof(double) * ((int64_t)ks_blocks * nf + nf + reduce_tmp_elems(nf, 1, ks_blocks, 1))))
+      return fail(SOG_ERR_NOMEM, "device allocation failed (Green tables)");
+    ka.gtab = p->gtab.as<double>();
+    ka.gtabF = aliasable ? p->gtabF.as<double>() : nullptr;
+    ka.partD = p->partD.as<double>();
+    const unsigned gblocks = nblocks((int64_t)ny * nxh, 256);
+    k_green<T><<<dim3(gblocks, nf), 256, 0, st>>>(ka);
+    after(tr, st, "green");
+    redD = ka.partD + (int64_t)gblocks * nf;
+    reduce_parts(ka.partD, nf, 1, gblocks, 1, 1, redD, redD + nf, st);
+    after(tr, st, "reduce_green", reduce_split(gblocks) > 1 ? 2 : 1);
+  }
   auto launch_zfused = [&]() {
     const int write_spec = (want_grad || want_vir) ? 1 : 0;
     const bool done = with_pow2(nz, [&](auto lc) {
       constexpr int L = decltype(lc)::value;
       constexpr int n = 1 << L;
       const int zthr = (n / kEPT) * zic;
-      const size_t zsm = ((2 * (size_t)n + padded_row(n)) * zic + n) * sizeof(C) +
-                         (size_t)zthr * kEPT * 2 * sizeof(double);
+      const size_t zsm = ((2 * (size_t)n + padded_row(n)) * zic + n) * sizeof(C);
       const int64_t ztiles = zchunks * nf;
-      allow_smem(k_zfused_pipe<T, L>);
-      k_zfused_pipe<T, L><<<persistent_grid(k_zfused_pipe<T, L>, zthr, zsm, ztiles), zthr, zsm, st>>>(
+      allow_smem(k_zfused_g<T, L>);
+      k_zfused_g<T, L><<<persistent_grid(k_zfused_g<T, L>, zthr, zsm, ztiles), zthr, zsm, st>>>(
           ka, zic, ztiles, p->twz.as<C>(), write_spec);
     });
     if (!done) {
@@ -1552,6 +1762,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   fa.geom = geom;
   fa.redE = redE;
   fa.redX = redX;
+  fa.redD = (zfuse && is_pow2(nz) && nz <= 1024) ? redD : nullptr;
   fa.qsum = p->qsum.as<double>();
   fa.amp = a->amp;
   fa.bw2 = a->bw2;
@@ -1657,7 +1868,7 @@ extern "C" int sog_plan_destroy(sog_plan *p) {
                     &p->tab.sy, &p->tab.sz, &p->frames_host_dev, &p->geom, &p->status, &p->keys0,
                     &p->vals0, &p->keys1, &p->vals1, &p->hist, &p->scan_tmp, &p->bin_start,
                     &p->s_atom, &p->s_anchor, &p->s_t, &p->s_q, &p->qsum, &p->rho, &p->spec,
-                    &p->fspec, &p->freal, &p->partE, &p->partX, &p->red, &p->redtmp, &p->qpart, &p->btab};
+                    &p->fspec, &p->freal, &p->partE, &p->partX, &p->red, &p->redtmp, &p->qpart, &p->btab, &p->gtab, &p->gtabF, &p->partD};
   for (DevBuf *b : bufs) b->release();
   p->up.release();
   p->tr.release();

@@ -27,6 +27,7 @@ Deliberate differences, each documented in DESIGN.md:
 from __future__ import annotations
 
 import math
+import weakref
 from typing import Any, Dict, List, Optional, Tuple
 
 import torch
@@ -228,6 +229,10 @@ class Gaussian(nn.Module):
         self.rcut = float(rcut) if rcut is not None else None
         self.b = float(b)
         self._max_cache_size = max(1, int(max_cache_size))
+        # frame layout of the last call, reused while `batch` and `cell` are the
+        # same unmodified tensors (checked by weak reference and version); the
+        # analogue of the reference's per-box caches (gaussian.py:268-329)
+        self._layout: Optional[Dict[str, Any]] = None
 
     # ------------------------------------------------------------------
     def forward(self, q: torch.Tensor, r: torch.Tensor, cell: Optional[torch.Tensor],
@@ -275,47 +280,41 @@ class Gaussian(nn.Module):
             return _lib.SPLINE_QUADS, self.quads_order
         return None
 
-    def compute_bundle(self, q: torch.Tensor, r: torch.Tensor, cell: Optional[torch.Tensor],
-                       batch: Optional[torch.Tensor] = None, compute_force: bool = False,
-                       compute_virial: bool = False) -> Dict[str, Optional[torch.Tensor]]:
-        if q.dim() == 1:
-            q = q.unsqueeze(1)
-        n, d = r.shape
-        assert d == 3, "r dimension error"
-        assert n == q.size(0), "q dimension error"
-        if batch is None:
-            batch = torch.zeros(n, dtype=torch.int64, device=r.device)
-        if cell is not None and (cell.dim() != 3 or cell.shape[-2:] != (3, 3)):
-            raise ValueError(f"`cell` should be [nbatch, 3, 3], got {tuple(cell.shape)}")
-        if r.device.type != "cuda":
-            raise _lib.SogError("sog_b200 runs on CUDA devices only; move r, q, cell and batch "
-                                "to a CUDA device")
-        need_force = bool(compute_force or compute_virial)
-        dt = r.dtype
-        dev = r.device
-        bids = torch.unique(batch).tolist()
-        if len(bids) == 0:
-            z = torch.zeros(0, dtype=dt, device=dev)
-            return {"energy": z, "forces": torch.zeros(n, 3, dtype=dt, device=dev) if need_force else None,
-                    "virial": torch.zeros(0, 3, 3, dtype=dt, device=dev) if compute_virial else None,
-                    "used_explicit_derivatives": need_force}
-        if cell is None:
-            raise NotImplementedError("the real-space path (cell=None) is not built yet")
+    def _frame_layout(self, batch: Optional[torch.Tensor], cell: torch.Tensor, n: int,
+                      dt: torch.dtype, dev: torch.device) -> Optional[Dict[str, Any]]:
+        """Frames of the call (sorted unique batch ids, atom ranges, mesh or
+        direct buckets).  Needs the cell on the host and, for an explicit
+        batch, its frame counts; both are reused while the same tensors are
+        passed unchanged, so repeated calls launch without host syncs."""
+        settings = (n, dt, str(dev), self.n_dl, self.cubes2_phi_max, self.rcut, self.b,
+                    self.use_bspline_fft, self.bspline_order, self.use_quads_fft, self.quads_order,
+                    self.use_cubes2_fft, tuple(self.bandwidth.shape), id(self.bandwidth),
+                    self.bandwidth._version)
+        c = self._layout
+        if (c is not None and c["settings"] == settings and c["cell_ref"]() is cell
+                and c["cell_ver"] == cell._version
+                and ((batch is None and c["batch_ref"] is None) or
+                     (batch is not None and c["batch_ref"] is not None and c["batch_ref"]() is batch
+                      and c["batch_ver"] == batch._version))):
+            return c
         cell_h = cell.detach().to("cpu", torch.float64)
+        if batch is None:
+            bids, counts_h, perm = [0], [n], None
+        else:
+            if n == 0:
+                return None
+            bids = torch.unique(batch).tolist()
+            counts_h = torch.bincount(batch, minlength=max(bids) + 1).tolist()
+            sorted_ok = bool((batch[1:] >= batch[:-1]).all()) if n > 1 else True
+            perm = None if sorted_ok else torch.argsort(batch, stable=True)
+        if len(bids) == 0 or n == 0:
+            return None
         vols = torch.abs(torch.linalg.det(cell_h))
         eps = torch.finfo(cell.dtype).eps
         for bid in bids:
             if not bool(vols[bid] > eps):
                 raise NotImplementedError("non-periodic frames (singular cell) need the real-space "
                                           "path, which is not built yet")
-
-        # ---- atoms grouped by frame (contiguous), in the order of `bids` ----
-        counts = torch.bincount(batch, minlength=max(bids) + 1)
-        sorted_ok = bool((batch[1:] >= batch[:-1]).all()) if n > 1 else True
-        perm = None
-        if not sorted_ok:
-            perm = torch.argsort(batch, stable=True)
-        counts_h = counts.tolist()
         begins, acc = [], 0
         for bid in bids:
             begins.append(acc)
@@ -323,28 +322,10 @@ class Gaussian(nn.Module):
         nat = [counts_h[bid] for bid in bids]
         fidx = torch.repeat_interleave(torch.arange(len(bids), device=dev),
                                        torch.tensor(nat, device=dev))
-        r_s = r if perm is None else r.index_select(0, perm)
-        q_s = q if perm is None else q.index_select(0, perm)
-        bid_t = torch.tensor(bids, device=dev, dtype=torch.long)
-        cells = cell.detach().to(dt).index_select(0, bid_t).contiguous()
-
-        amp = self.amp.to(dtype=dt, device=dev)
-        bw2 = self.bandwidth.to(dtype=dt, device=dev)
-        mesh = self._mesh_kind()
-        spec = SolveSpec(kind="mesh" if mesh else "direct", buckets=[], nframes=len(bids),
-                         cells=cells, frame_of_atom=fidx, norm_factor=self.norm_factor,
-                         self_coeff=self.self_coeff, remove_self=self.remove_self_interaction,
-                         k0_correction=True, charge_neutral_lambda=(
-                             float(self.charge_neutral_lambda)
-                             if self.charge_neutral_lambda is not None and self.charge_neutral_lambda > 0
-                             else None))
         lens = torch.linalg.norm(cell_h, dim=2)
+        mesh = self._mesh_kind()
         if mesh:
             spline, order = mesh
-            spec.spline, spec.order = spline, order
-            spec.kconv = (_lib.KCONV_REFERENCE if self.mesh_k_convention == "reference"
-                          else _lib.KCONV_PHYSICAL)
-            spec.alias_extent = self.mesh_alias_extent
             groups: Dict[Tuple[int, int, int], Bucket] = {}
             for j, bid in enumerate(bids):
                 lx, ly, lz = (float(v) for v in lens[bid])
@@ -358,19 +339,72 @@ class Gaussian(nn.Module):
                 bk.atom_begin.append(begins[j])
                 bk.atom_count.append(nat[j])
                 bk.k_sq_max.append(ksm)
-            spec.buckets = list(groups.values())
+            buckets = list(groups.values())
         else:
             n_dl = self._resolve_direct_n_dl(dt, dev)
             bk = Bucket([], [], [], [], nk=[])
             for j, bid in enumerate(bids):
-                nk = tuple(max(1, int(float(v) / n_dl)) for v in lens[bid])
                 bk.frames.append(j)
                 bk.atom_begin.append(begins[j])
                 bk.atom_count.append(nat[j])
                 bk.k_sq_max.append((2.0 * math.pi / n_dl) ** 2)
-                bk.nk.append(nk)
-            spec.buckets = [bk]
+                bk.nk.append(tuple(max(1, int(float(v) / n_dl)) for v in lens[bid]))
+            buckets = [bk]
+        lay = {"settings": settings, "cell_ref": weakref.ref(cell), "cell_ver": cell._version,
+               "batch_ref": None if batch is None else weakref.ref(batch),
+               "batch_ver": None if batch is None else batch._version,
+               "perm": perm, "fidx": fidx, "nframes": len(bids), "buckets": buckets,
+               "bid_t": torch.tensor(bids, device=dev, dtype=torch.long),
+               "identity_frames": bids == list(range(cell.shape[0])),
+               "kind": "mesh" if mesh else "direct", "mesh": mesh}
+        self._layout = lay
+        return lay
 
+    def compute_bundle(self, q: torch.Tensor, r: torch.Tensor, cell: Optional[torch.Tensor],
+                       batch: Optional[torch.Tensor] = None, compute_force: bool = False,
+                       compute_virial: bool = False) -> Dict[str, Optional[torch.Tensor]]:
+        if q.dim() == 1:
+            q = q.unsqueeze(1)
+        n, d = r.shape
+        assert d == 3, "r dimension error"
+        assert n == q.size(0), "q dimension error"
+        if cell is not None and (cell.dim() != 3 or cell.shape[-2:] != (3, 3)):
+            raise ValueError(f"`cell` should be [nbatch, 3, 3], got {tuple(cell.shape)}")
+        if r.device.type != "cuda":
+            raise _lib.SogError("sog_b200 runs on CUDA devices only; move r, q, cell and batch "
+                                "to a CUDA device")
+        need_force = bool(compute_force or compute_virial)
+        dt = r.dtype
+        dev = r.device
+        if cell is None:
+            raise NotImplementedError("the real-space path (cell=None) is not built yet")
+        lay = self._frame_layout(batch, cell, n, dt, dev)
+        if lay is None:
+            return {"energy": torch.zeros(0, dtype=dt, device=dev),
+                    "forces": torch.zeros(n, 3, dtype=dt, device=dev) if need_force else None,
+                    "virial": torch.zeros(0, 3, 3, dtype=dt, device=dev) if compute_virial else None,
+                    "used_explicit_derivatives": need_force}
+        perm = lay["perm"]
+        r_s = r if perm is None else r.index_select(0, perm)
+        q_s = q if perm is None else q.index_select(0, perm)
+        cells = cell.detach().to(dt)
+        if not lay["identity_frames"]:
+            cells = cells.index_select(0, lay["bid_t"])
+        cells = cells.contiguous()
+        amp = self.amp.to(dtype=dt, device=dev)
+        bw2 = self.bandwidth.to(dtype=dt, device=dev)
+        spec = SolveSpec(kind=lay["kind"], buckets=lay["buckets"], nframes=lay["nframes"],
+                         cells=cells, frame_of_atom=lay["fidx"], norm_factor=self.norm_factor,
+                         self_coeff=self.self_coeff, remove_self=self.remove_self_interaction,
+                         k0_correction=True, charge_neutral_lambda=(
+                             float(self.charge_neutral_lambda)
+                             if self.charge_neutral_lambda is not None and self.charge_neutral_lambda > 0
+                             else None))
+        if lay["kind"] == "mesh":
+            spec.spline, spec.order = lay["mesh"]
+            spec.kconv = (_lib.KCONV_REFERENCE if self.mesh_k_convention == "reference"
+                          else _lib.KCONV_PHYSICAL)
+            spec.alias_extent = self.mesh_alias_extent
         energy, forces, virial = SolveFunction.apply(q_s, r_s, amp, bw2, spec, need_force,
                                                      bool(compute_virial))
         if forces is not None and perm is not None:

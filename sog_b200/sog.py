@@ -139,6 +139,7 @@ class Sog(nn.Module):
                 compute_bec: bool = False, bec_output_index: Optional[int] = None, *,
                 compute_force: bool = False, compute_virial: bool = False
                 ) -> Dict[str, Optional[torch.Tensor]]:
+        batch_given = batch
         if batch is None:
             batch = torch.zeros(positions.shape[0], dtype=torch.int64, device=positions.device)
         if latent_charges is not None:
@@ -165,7 +166,7 @@ class Sog(nn.Module):
         used = False
         if compute_energy or compute_force or compute_virial:
             out = self.gaussian.compute_bundle(q=latent_charges, r=positions, cell=cell,
-                                               batch=batch, compute_force=compute_force,
+                                               batch=batch_given, compute_force=compute_force,
                                                compute_virial=compute_virial)
             e_lr = out["energy"] if compute_energy else None
             forces, virial = out["forces"], out["virial"]
