@@ -164,6 +164,38 @@ typedef struct sog_direct_args {
  * (gaussian.py:1180-1337), whose forces the reference takes by autograd. */
 SOG_API int sog_direct_forward(sog_direct *d, const sog_direct_args *args, void *stream);
 
+/* ------------------------------------------------------------------------ */
+/* Direct k-sum without allocation (no counterpart in the reference)         */
+/* ------------------------------------------------------------------------ */
+
+/* Scratch held in one fixed device array per device, and the most frames
+ * one call may carry. */
+#define SOG_NOALLOC_SCRATCH_BYTES (8u << 20)
+#define SOG_NOALLOC_MAX_FRAMES 64
+
+/* Same result as sog_direct_forward (same kernels, same arguments) on the
+ * calling thread's current device, for callers that may not allocate device
+ * or pinned host memory inside a force call: an MD engine that hands out
+ * device memory only from its own arena and forbids cudaMalloc after setup
+ * (cudaMalloc / cudaHostAlloc can wait on queued device work and can fail
+ * under memory pressure mid-run), or an integrator that keeps no per-context
+ * state.  The call makes no allocation: its scratch is a file-scope
+ * __device__ array of SOG_NOALLOC_SCRATCH_BYTES bytes, and the per-frame
+ * metadata travels as a kernel parameter.
+ *  - The first call on each device resolves the array's address (which may
+ *    load the module on that device); make it before any stream capture.
+ *  - A call whose scratch would exceed the array (about 48 bytes per mode of
+ *    the largest frame's mode box per frame and channel, more with
+ *    parameter gradients or the virial), or with more than
+ *    SOG_NOALLOC_MAX_FRAMES frames, returns SOG_ERR_INVALID and launches
+ *    nothing; sog_last_error() gives the bytes needed.
+ *  - Nothing in the scratch has to start at zero: each call writes every
+ *    scratch word before reading it.
+ *  - All calls on one device share the array: two calls in flight at once
+ *    on one device (different streams or host threads) race.  Serialise
+ *    them on one stream or with an event. */
+SOG_API int sog_direct_forward_noalloc(int dtype, const sog_direct_args *args, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

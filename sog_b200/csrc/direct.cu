@@ -8,6 +8,8 @@
 //   k_direct_atoms  thread per atom: forces and potential
 #include <algorithm>
 #include <cstring>
+#include <mutex>
+#include <string>
 #include <vector>
 
 #include "frames.cuh"
@@ -432,4 +434,237 @@ extern "C" int sog_direct_forward(sog_direct *d, const sog_direct_args *a, void 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (d->dtype == SOG_DTYPE_F64) return direct_impl<double>(d, a, st);
   return direct_impl<float>(d, a, st);
+}
+
+// ==========================================================================
+// No-allocation variant of the direct k-sum.
+//
+// Some callers cannot allocate device or pinned memory inside their force
+// call: an MD engine that hands out device memory only from its own arena
+// and forbids cudaMalloc after setup (cudaMalloc and cudaHostAlloc can block
+// on work already queued on the device and can fail under memory pressure in
+// the middle of a run), or an integrator that must not create per-context
+// state.  sog_direct_forward_noalloc runs the same kernels as
+// sog_direct_forward with all scratch in one fixed file-scope device array
+// and the per-frame metadata passed by value as a kernel parameter, so a
+// call makes no allocation of any kind.
+//
+// Limits: SOG_NOALLOC_SCRATCH_BYTES of scratch per device and at most
+// SOG_NOALLOC_MAX_FRAMES frames per call; a call that needs more is rejected
+// with SOG_ERR_INVALID before anything is launched.  Nothing in the scratch
+// has to start at zero: every word a call reads was written earlier in the
+// same call (the status word is cleared by the call's first kernel).  The
+// scratch is shared by every call on a device, so two calls in flight at
+// once on one device (different streams or host threads) race; callers
+// serialise them (one stream, or an event between them).
+// ==========================================================================
+namespace sogb {
+namespace {
+
+constexpr size_t kNoAllocBytes = SOG_NOALLOC_SCRATCH_BYTES;
+constexpr int kNoAllocFrames = SOG_NOALLOC_MAX_FRAMES;
+
+static __device__ __align__(256) unsigned char g_direct_scratch[kNoAllocBytes];
+
+struct NoAllocFrames {
+  FrameHost fh[kNoAllocFrames];
+  int nk[kNoAllocFrames][3];
+  int nf;
+};
+static_assert(sizeof(NoAllocFrames) <= 4000, "frame table must fit the kernel parameter space");
+
+__global__ void k_noalloc_frames(const NoAllocFrames p, FrameHost *fh, int *nk, unsigned *status) {
+  for (int f = threadIdx.x; f < p.nf; f += blockDim.x) {
+    fh[f] = p.fh[f];
+    nk[3 * f + 0] = p.nk[f][0];
+    nk[3 * f + 1] = p.nk[f][1];
+    nk[3 * f + 2] = p.nk[f][2];
+  }
+  if (threadIdx.x == 0) status[0] = 0u;
+}
+
+// Device address of the scratch array for the current device.  The first
+// call on a device resolves it (this may load the module on that device).
+int noalloc_scratch(unsigned char **out) {
+  static std::mutex mu;
+  static unsigned char *addr[64] = {};
+  int dev = 0;
+  SOG_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(SOG_ERR_UNSUPPORTED, "device ordinal above 63");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_direct_scratch);
+    if (e != cudaSuccess) return fail(SOG_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    addr[dev] = static_cast<unsigned char *>(p);
+  }
+  *out = addr[dev];
+  return SOG_OK;
+}
+
+// Carves 256-byte aligned regions off the scratch array in order.
+struct Carve {
+  size_t off = 0;
+  size_t take(size_t bytes) {
+    const size_t at = off;
+    off += (bytes + 255) & ~(size_t)255;
+    return at;
+  }
+};
+
+template <typename T>
+int direct_noalloc_impl(const sog_direct_args *a, cudaStream_t st) {
+  const int nf = a->nframes, nch = a->nchannels, M = a->n_gauss;
+  if (nf > kNoAllocFrames) return fail(SOG_ERR_INVALID, "no-alloc direct k-sum: more than 64 frames in one call");
+  NoAllocFrames frames;
+  std::memset(&frames, 0, sizeof(frames));
+  frames.nf = nf;
+  int64_t kmax = 1, maxat = 0, slots = 0;
+  for (int f = 0; f < nf; ++f) {
+    for (int c = 0; c < 3; ++c) {
+      if (a->nk[3 * f + c] < 0 || a->nk[3 * f + c] > 4096) return fail(SOG_ERR_INVALID, "nk out of range");
+      frames.nk[f][c] = a->nk[3 * f + c];
+    }
+    const int64_t nbox = (int64_t)(a->nk[3 * f] + 1) * (2 * a->nk[3 * f + 1] + 1) * (2 * a->nk[3 * f + 2] + 1);
+    kmax = std::max(kmax, nbox);
+    maxat = std::max<int64_t>(maxat, a->atom_count[f]);
+    frames.fh[f].atom_begin = a->atom_begin[f];
+    frames.fh[f].natoms = a->atom_count[f];
+    frames.fh[f].slot_base = slots;
+    frames.fh[f].k_sq_max = a->k_sq_max[f];
+    slots += a->atom_count[f];
+  }
+  if (kmax > ((int64_t)1 << 31)) return fail(SOG_ERR_INVALID, "mode box too large");
+  const unsigned kb = nblk(kmax, kDirThreads);
+  const int nx_acc = 4 * M + 13;
+  const bool want_grad = a->grad_amp || a->grad_bw2;
+  const bool want_vir = a->virial != nullptr;
+  const bool want_x = want_grad || want_vir;
+  const int qs = (int)std::max<int64_t>(1, std::min<int64_t>(256, (maxat + 16383) / 16384));
+  const size_t d8 = sizeof(double);
+  Carve cv;
+  const size_t o_fh = cv.take(sizeof(FrameHost) * nf);
+  const size_t o_nk = cv.take(sizeof(int) * 3 * nf);
+  const size_t o_geom = cv.take(sizeof(FrameGeom) * nf);
+  const size_t o_status = cv.take(16);
+  const size_t o_modes = cv.take(d8 * 4 * kmax * nf);
+  const size_t o_sfac = cv.take(d8 * 2 * kmax * nf * nch);
+  const size_t o_part = cv.take(d8 * 2 * kb * nf * nch);
+  const size_t o_partx = cv.take(want_x ? d8 * nx_acc * kb * nf * nch : 0);
+  const size_t o_redE = cv.take(d8 * 2 * nf * nch);
+  const size_t o_redX = cv.take(d8 * nx_acc * nf * nch);
+  const size_t o_fscal = cv.take(d8 * 4 * nf);
+  const size_t o_qsum = cv.take(d8 * 2 * nf * nch);
+  const size_t o_qpart = cv.take(d8 * 2 * nf * nch * qs);
+  const size_t o_tmp = cv.take(d8 * std::max(reduce_tmp_elems(nf, nch, kb, 2), reduce_tmp_elems(nf, nch, kb, nx_acc)));
+  if (cv.off > kNoAllocBytes)
+    return fail(SOG_ERR_INVALID, "no-alloc direct k-sum: the call needs " + std::to_string(cv.off) +
+                                     " bytes of scratch, the fixed array holds " + std::to_string(kNoAllocBytes) +
+                                     " (fewer modes, channels or frames per call, or sog_direct_forward)");
+  unsigned char *s = nullptr;
+  int rc = noalloc_scratch(&s);
+  if (rc != SOG_OK) return rc;
+  FrameHost *fhd = reinterpret_cast<FrameHost *>(s + o_fh);
+  int *nkd = reinterpret_cast<int *>(s + o_nk);
+  FrameGeom *geom = reinterpret_cast<FrameGeom *>(s + o_geom);
+  unsigned *status = reinterpret_cast<unsigned *>(s + o_status);
+  double *qsum = reinterpret_cast<double *>(s + o_qsum);
+  double *qpart = reinterpret_cast<double *>(s + o_qpart);
+  double *tmp = reinterpret_cast<double *>(s + o_tmp);
+
+  k_noalloc_frames<<<1, 64, 0, st>>>(frames, fhd, nkd, status);
+  count_launch();
+  k_frame_setup<T><<<nblk(nf, 128), 128, 0, st>>>((const T *)a->cells, fhd, geom, nf, SOG_KCONV_PHYSICAL, 1, 1, 1,
+                                                  status);
+  count_launch();
+  k_qsums<T><<<dim3(nf, nch, qs), 256, 0, st>>>((const T *)a->charges, nch, geom, qpart);
+  k_reduce_parts<<<dim3(nf, nch, 1), 256, 0, st>>>(qpart, nf, nch, qs, 2, 2, qsum);
+  count_launch();
+  count_launch();
+  DirArgs da;
+  da.geom = geom;
+  da.nk = nkd;
+  da.kmax_modes = kmax;
+  da.nch = nch;
+  da.M = M;
+  da.kvec = reinterpret_cast<double *>(s + o_modes);
+  da.sfac = reinterpret_cast<double *>(s + o_sfac);
+  da.part = reinterpret_cast<double *>(s + o_part);
+  da.partx = want_x ? reinterpret_cast<double *>(s + o_partx) : nullptr;
+  da.nx_acc = nx_acc;
+  double *redE = reinterpret_cast<double *>(s + o_redE);
+  double *redX = reinterpret_cast<double *>(s + o_redX);
+  double *fscal = reinterpret_cast<double *>(s + o_fscal);
+  k_direct_sfac<T><<<dim3(kb, nf), kDirThreads, 0, st>>>(da, (const T *)a->positions, (const T *)a->charges,
+                                                         (const T *)a->amp, (const T *)a->bw2);
+  count_launch();
+  if (want_x) {
+    k_direct_extra<T><<<dim3(kb, nf, nch), kDirThreads, 0, st>>>(da, (const T *)a->amp, (const T *)a->bw2,
+                                                                 want_grad, want_vir);
+    count_launch();
+  }
+  if ((a->forces || a->potential) && maxat > 0) {
+    k_direct_atoms<T><<<dim3(nblk(maxat, 128), nf), 128, 0, st>>>(da, (const T *)a->positions,
+                                                                  (const T *)a->charges, a->norm_factor,
+                                                                  (T *)a->forces, (T *)a->potential);
+    count_launch();
+  }
+  reduce_parts(da.part, nf, nch, kb, 2, 2, redE, tmp, st);
+  count_launch();
+  if (reduce_split(kb) > 1) count_launch();
+  if (want_x) {
+    reduce_parts(da.partx, nf, nch, kb, nx_acc, nx_acc, redX, tmp, st);
+    count_launch();
+    if (reduce_split(kb) > 1) count_launch();
+  }
+  FinalArgs fa;
+  std::memset(&fa, 0, sizeof(fa));
+  fa.geom = geom;
+  fa.redE = redE;
+  fa.redX = redX;
+  fa.qsum = qsum;
+  fa.amp = a->amp;
+  fa.bw2 = a->bw2;
+  fa.M = M; fa.nch = nch; fa.nx = 1; fa.ny = 1; fa.nz = 1;
+  fa.norm = a->norm_factor;
+  fa.self_coeff = a->self_coeff;
+  fa.lambda = a->charge_neutral_lambda;
+  fa.remove_self = a->remove_self;
+  fa.k0 = a->k0_correction;
+  fa.want_grad = want_grad;
+  fa.want_vir = want_vir;
+  fa.direct = 1;
+  fa.energy = a->energy;
+  fa.grad_amp = a->grad_amp;
+  fa.grad_bw2 = a->grad_bw2;
+  fa.virial = a->virial;
+  fa.fscal = fscal;
+  k_finalize_frames<T><<<nblk(nf, 64), 64, 0, st>>>(fa, nf);
+  count_launch();
+  if (a->potential && maxat > 0) {
+    k_finalize_atoms<T><<<dim3(nblk(maxat, 256), nf), 256, 0, st>>>(
+        geom, fscal, qsum, (const T *)a->charges, (T *)a->potential, nch, a->norm_factor, a->self_coeff,
+        a->charge_neutral_lambda, a->remove_self, a->k0_correction);
+    count_launch();
+  }
+  SOG_CUDA_TRY(cudaGetLastError());
+  return SOG_OK;
+}
+
+}  // namespace
+}  // namespace sogb
+
+extern "C" int sog_direct_forward_noalloc(int dtype, const sog_direct_args *a, void *stream) {
+  if (!a) return fail(SOG_ERR_INVALID, "null argument");
+  if (dtype != SOG_DTYPE_F64 && dtype != SOG_DTYPE_F32) return fail(SOG_ERR_INVALID, "bad dtype");
+  if (a->nframes <= 0) return SOG_OK;
+  if (!a->atom_begin || !a->atom_count || !a->nk || !a->k_sq_max || !a->positions || !a->charges ||
+      !a->cells || !a->amp || !a->bw2)
+    return fail(SOG_ERR_INVALID, "missing input array");
+  if (a->nchannels < 1 || a->nchannels > kMaxCh)
+    return fail(SOG_ERR_UNSUPPORTED, "direct k-sum supports 1..8 charge channels");
+  if (a->n_gauss < 1 || a->n_gauss > kMaxGauss) return fail(SOG_ERR_INVALID, "n_gauss must be in [1, 64]");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == SOG_DTYPE_F64) return direct_noalloc_impl<double>(a, st);
+  return direct_noalloc_impl<float>(a, st);
 }
