@@ -65,8 +65,8 @@ __global__ void k_cols_pipe(cplx_t<T> *__restrict__ data, int64_t inner, int ic,
   C *buf0 = reinterpret_cast<C *>(smem_raw);
   C *buf1 = buf0 + (size_t)n * ic;
   C *xbuf = buf1 + (size_t)n * ic;
-  C *stw = xbuf + (size_t)(PAD ? padded_row(n) : n) * ic;
-  load_twiddles<T>(stw, tw, n);
+  C *stg = xbuf + (size_t)(PAD ? padded_row(n) : n) * ic;
+  load_stage_twiddles<T, L, 0>(stg, tw);
   const int c = threadIdx.x % ic, t = threadIdx.x / ic;
   const int64_t nchunks = (inner + ic - 1) / ic;
   int64_t tile = blockIdx.x;
@@ -83,7 +83,7 @@ __global__ void k_cols_pipe(cplx_t<T> *__restrict__ data, int64_t inner, int ic,
     C v[kEPT];
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) v[e] = cur[(t + e * TPT) * ic + c];
-    ct_fft<T, DIR, L, PAD>(v, t, stw, xbuf + c, ic);
+    ct_fft<T, DIR, L, PAD>(v, t, stg, xbuf + c, ic);
     const int64_t o = tile / nchunks;
     const int64_t i0 = (tile - o * nchunks) * ic;
     if (i0 + c < inner) {
@@ -112,8 +112,10 @@ __global__ void k_r2c_pipe(const T *__restrict__ in, cplx_t<T> *__restrict__ out
   T *buf0 = reinterpret_cast<T *>(smem_raw);
   T *buf1 = buf0 + (size_t)rpc * n;
   C *xbuf = reinterpret_cast<C *>(buf1 + (size_t)rpc * n);
-  C *stw = xbuf + (size_t)rpc * hp;
+  C *stw = xbuf + (size_t)rpc * hp;  // n-th roots of unity (post-processing)
+  C *stg = stw + n;                    // stage table of the length n/2 transform
   load_twiddles<T>(stw, tw, n);
+  load_stage_twiddles<T, L - 1, 1>(stg, tw);
   const int t = threadIdx.x % TPT, rr = threadIdx.x / TPT;
   constexpr int per = 16 / (int)sizeof(T);
   auto issue = [&](T *buf, int64_t tile) {
@@ -145,7 +147,7 @@ __global__ void k_r2c_pipe(const T *__restrict__ in, cplx_t<T> *__restrict__ out
       const int m = t + e * TPT;
       v[e] = cmk<C, T>(xr[2 * m], xr[2 * m + 1]);
     }
-    ct_fft<T, -1, L - 1, true, 1>(v, t, stw, zrow, 1);
+    ct_fft<T, -1, L - 1, true, 1>(v, t, stg, zrow, 1);
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) zrow[sidx<true>(t + e * TPT, 1)] = v[e];
     __syncthreads();
@@ -186,37 +188,43 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
   extern __shared__ __align__(16) unsigned char smem_raw[];
   constexpr int n = 1 << L, h = n / 2, TPT = h / kEPT, nxh = h + 1;
   constexpr int hp = padded_row(h);
-  C *buf0 = reinterpret_cast<C *>(smem_raw);
-  C *buf1 = buf0 + (size_t)rpc * F * nxh;
-  C *xbuf = buf1 + (size_t)rpc * F * nxh;  // exchanges, then the interleaved output staging
-  const size_t xsz = max((size_t)rpc * F * hp * sizeof(C), (size_t)rpc * n * F * sizeof(T));
-  C *stw = reinterpret_cast<C *>(reinterpret_cast<unsigned char *>(xbuf) + ((xsz + 15) & ~(size_t)15));
+  // three input buffers: tiles i+1 and i+2 are in flight while tile i is
+  // transformed
+  const size_t tsz = (size_t)rpc * F * nxh;
+  C *bufs = reinterpret_cast<C *>(smem_raw);
+  C *xbuf = bufs + 3 * tsz;  // exchanges of the row transforms
+  C *stw = xbuf + (size_t)rpc * F * hp;  // n-th roots of unity (pre-processing)
+  C *stg = stw + n;                        // stage table of the length n/2 transform
   load_twiddles<T>(stw, tw, n);
+  load_stage_twiddles<T, L - 1, 1>(stg, tw);
   const int t = threadIdx.x % TPT, q = threadIdx.x / TPT;
   const int f = q % F, rr = q / F;
   auto issue = [&](C *buf, int64_t tile) {
     const int64_t row0 = tile * rpc;
+    // one 64-bit division per tile; rows of the tile step (frame, zy) on
+    const int64_t frame0 = row0 / nzy, zy0 = row0 - frame0 * nzy;
     const int total = rpc * F * nxh;
     for (int qq = threadIdx.x; qq < total; qq += blockDim.x) {
       const int hr = qq / nxh, col = qq - hr * nxh;
       const int r2 = hr / F, f2 = hr - r2 * F;
-      const int64_t row = row0 + r2;
-      const bool ok = row < nrows;
-      const int64_t frame = ok ? row / nzy : 0, zy = ok ? row - frame * nzy : 0;
+      const bool ok = row0 + r2 < nrows;
+      int64_t frame = frame0, zy = zy0 + r2;
+      while (zy >= nzy) { zy -= nzy; ++frame; }
       const C *src = in + ((frame * F + f2) * nzy + zy) * nxh + col;
       cp_async_elem(buf + qq, ok ? src : in, ok);
     }
   };
   int64_t tile = blockIdx.x;
-  if (tile < ntiles) issue(buf0, tile);
+  if (tile < ntiles) issue(bufs, tile);
+  cp_async_commit();
+  if (tile + gridDim.x < ntiles) issue(bufs + tsz, tile + gridDim.x);
   cp_async_commit();
   for (int it = 0; tile < ntiles; ++it, tile += gridDim.x) {
-    C *cur = (it & 1) ? buf1 : buf0;
-    C *nxt = (it & 1) ? buf0 : buf1;
-    const int64_t next = tile + gridDim.x;
-    if (next < ntiles) issue(nxt, next);
+    const C *cur = bufs + (size_t)(it % 3) * tsz;
+    const int64_t next = tile + 2 * (int64_t)gridDim.x;
+    if (next < ntiles) issue(bufs + (size_t)((it + 2) % 3) * tsz, next);
     cp_async_commit();
-    cp_async_wait<1>();
+    cp_async_wait<2>();
     __syncthreads();
     const C *X = cur + (size_t)(rr * F + f) * nxh;
     C v[kEPT];
@@ -235,20 +243,19 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
         v[e] = cmk<C, T>(Ar - ci, Ai + cr);          // A + i conj(w) B
       }
     }
-    ct_fft<T, +1, L - 1, true, 1>(v, t, stw, xbuf + (size_t)(rr * F + f) * hp, 1);
-    __syncthreads();
-    T *so = reinterpret_cast<T *>(xbuf);
+    ct_fft<T, +1, L - 1, true, 1>(v, t, stg, xbuf + (size_t)(rr * F + f) * hp, 1);
+    // interleaved output straight from registers: the F fields of a row are
+    // written by the same CTA, so every sector is completed in L2
+    const int64_t row = tile * rpc + rr;
+    if (row < nrows) {
+      T *dst = out + row * n * F + f;
 #pragma unroll
-    for (int e = 0; e < kEPT; ++e) {
-      const int m = t + e * TPT;
-      so[((size_t)rr * n + 2 * m) * F + f] = v[e].x;
-      so[((size_t)rr * n + 2 * m + 1) * F + f] = v[e].y;
+      for (int e = 0; e < kEPT; ++e) {
+        const int m = t + e * TPT;
+        dst[(2 * m) * F] = v[e].x;
+        dst[(2 * m + 1) * F] = v[e].y;
+      }
     }
-    __syncthreads();
-    const int64_t row0 = tile * rpc;
-    const int64_t nvalid = min((int64_t)rpc, nrows - row0) * n * F;
-    T *dst = out + row0 * n * F;
-    for (int64_t i = threadIdx.x; i < nvalid; i += blockDim.x) dst[i] = so[i];
     __syncthreads();
   }
   cp_async_wait<0>();

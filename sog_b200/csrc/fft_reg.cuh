@@ -107,9 +107,41 @@ struct Pow2Plan {
   }
 };
 
-// TWS: the shared twiddle table holds the roots of unity of order 2^(L+TWS).
+// Stage twiddle table of a 2^L transform: for every stage S >= 1 the rows
+// W^{r k step_S}, r = 1..R_S-1, k = 0..Ns-1, stored [r-1][k] so that lanes
+// with consecutive k read consecutive words (a table indexed by r k step
+// would put the lanes of a stage-1 butterfly 8 step words apart, all in one
+// bank).  At most 2^L entries.
+template <int L>
+struct StageTw {
+  __host__ __device__ static constexpr int off(int S) {
+    int o = 0;
+    for (int s = 1; s < S; ++s) o += (Pow2Plan<L>::radix(s) - 1) << (3 * s);
+    return o;
+  }
+  static constexpr int size = off(Pow2Plan<L>::NST);
+  static_assert(size <= (1 << L), "stage table larger than the transform");
+};
+
+// Builds the stage table of a 2^L transform from the global roots of unity of
+// order 2^(L+TWS) (caller synchronises before use).
+template <typename T, int L, int TWS>
+__device__ __forceinline__ void load_stage_twiddles(cplx_t<T> *stg, const cplx_t<T> *__restrict__ tw) {
+  using PP = Pow2Plan<L>;
+  for (int i = threadIdx.x; i < StageTw<L>::size; i += blockDim.x) {
+    int S = 1;
+    while (S + 1 < PP::NST && i >= StageTw<L>::off(S + 1)) ++S;
+    const int li = i - StageTw<L>::off(S);
+    const int lns = 3 * S;
+    const int r = (li >> lns) + 1, k = li & ((1 << lns) - 1);
+    const int lstep = L - lns - PP::log2radix(S);
+    stg[i] = tw[(r * k) << (lstep + TWS)];
+  }
+}
+
+// stg: the stage table of the 2^L transform (load_stage_twiddles).
 template <typename T, int DIR, int L, int S, bool PAD, int TWS>
-__device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx_t<T> *stw,
+__device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx_t<T> *stg,
                                          cplx_t<T> *sbase, int sj) {
   using PP = Pow2Plan<L>;
   constexpr int R = PP::radix(S);
@@ -118,7 +150,6 @@ __device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx
   constexpr int LNS = 3 * S;             // log2 Ns
   constexpr int NS = 1 << LNS;
   constexpr bool LAST = S == PP::NST - 1;
-  constexpr int LSTEP = L - LNS - LR;    // log2 (n / (Ns R))
 #pragma unroll
   for (int u = 0; u < B; ++u) {
     const int j = t + u * PP::TPT;
@@ -129,7 +160,7 @@ __device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx
     if (S > 0) {
 #pragma unroll
       for (int r = 1; r < R; ++r) {
-        cplx_t<T> w = stw[(r * k) << (LSTEP + TWS)];
+        cplx_t<T> w = stg[StageTw<L>::off(S) + (r - 1) * NS + k];
         if (DIR > 0) w.y = -w.y;
         a[r] = cmul(a[r], w);
       }
@@ -153,11 +184,11 @@ __device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx
 }
 
 template <typename T, int DIR, int L, bool PAD, int TWS = 0, int S = 0>
-__device__ __forceinline__ void ct_fft(cplx_t<T> (&v)[kEPT], int t, const cplx_t<T> *stw, cplx_t<T> *sbase,
+__device__ __forceinline__ void ct_fft(cplx_t<T> (&v)[kEPT], int t, const cplx_t<T> *stg, cplx_t<T> *sbase,
                                        int sj) {
   if constexpr (S < Pow2Plan<L>::NST) {
-    ct_stage<T, DIR, L, S, PAD, TWS>(v, t, stw, sbase, sj);
-    ct_fft<T, DIR, L, PAD, TWS, S + 1>(v, t, stw, sbase, sj);
+    ct_stage<T, DIR, L, S, PAD, TWS>(v, t, stg, sbase, sj);
+    ct_fft<T, DIR, L, PAD, TWS, S + 1>(v, t, stg, sbase, sj);
   }
 }
 
@@ -219,38 +250,6 @@ __global__ void k_rows_r2c_reg(const T *__restrict__ in, cplx_t<T> *__restrict__
   }
 }
 
-// Inverse C2R along x (torch.fft.irfftn semantics, unnormalised).
-template <typename T>
-__global__ void k_rows_c2r_reg(const cplx_t<T> *__restrict__ in, T *__restrict__ out, int64_t nrows,
-                               int rpc, RadixPlan rp, const cplx_t<T> *__restrict__ tw) {
-  using C = cplx_t<T>;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  C *sm = reinterpret_cast<C *>(smem_raw);
-  const int n = rp.n, TPT = n / kEPT, nxh = n / 2 + 1;
-  const int t = threadIdx.x % TPT, rr = threadIdx.x / TPT;
-  const int64_t row = (int64_t)blockIdx.x * rpc + rr;
-  const bool ok = row < nrows;
-  C v[kEPT];
-#pragma unroll
-  for (int e = 0; e < kEPT; ++e) {
-    const int m = t + e * TPT;
-    C x = cmk<C, T>(T(0), T(0));
-    if (ok) {
-      if (m < nxh) {
-        x = in[row * nxh + m];
-      } else {
-        const C h = in[row * nxh + (n - m)];
-        x = cmk<C, T>(h.x, -h.y);
-      }
-    }
-    v[e] = x;
-  }
-  reg_fft<T, +1, true>(v, t, rp, tw, sm + (size_t)rr * (n + n / 8), 1);
-  if (ok) {
-#pragma unroll
-    for (int e = 0; e < kEPT; ++e) out[row * n + t + e * TPT] = v[e].x;
-  }
-}
 
 // Inverse C2R along x of F fields with interleaved real output: a CTA
 // transforms all F fields of rpc consecutive mesh rows and writes

@@ -15,6 +15,10 @@
 //     k_gather      forces and potential at the atoms               (a10/a11)
 //   k_reduce / k_finalize_frames / k_finalize_atoms
 #include <algorithm>
+#include <atomic>
+#include <mutex>
+#include <set>
+#include <utility>
 #include <cfloat>
 #include <type_traits>
 #include <cmath>
@@ -202,19 +206,31 @@ __device__ int axis_bins(int lo, int len, int n, int nb, int *out) {
   return cnt;
 }
 
+// Per chunk of candidates the relevant ones are bucketed by their x anchor
+// relative to the tile (key = (ax - x0 + P - 1) mod nx, at most kTileX + P - 1
+// keys); a thread at tile column lx then visits only the P buckets whose
+// anchors reach it, with the x offset fixed per bucket.  Bucket positions come
+// from warp match ranks and a warp-ordered prefix, so the summation order at
+// every mesh point is fixed (bucket, then candidate order) and the result is
+// bitwise reproducible.
 template <typename T, int P>
-__global__ void __launch_bounds__(kSpreadThreads) k_spread(SpreadArgs<T> a) {
+__global__ void __launch_bounds__(kSpreadThreads, 3) k_spread(SpreadArgs<T> a) {
   constexpr int CH = kSpreadThreads;
+  constexpr int NW = kSpreadThreads / 32;
+  constexpr int NK = kTileX + P - 1;       // x-anchor buckets of a tile
+  static_assert(NK <= 64, "bucket scan covers two keys per lane");
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  T *c_wz = reinterpret_cast<T *>(smem_raw);            // [CH][kTileZ]
-  T *c_wx = c_wz + CH * kTileZ;                         // [CH][P]
-  T *c_wy = c_wx + CH * P;                              // [CH][P]
+  // candidate arrays, component-major so that lanes reading neighbouring
+  // buckets hit different banks
+  T *c_wz = reinterpret_cast<T *>(smem_raw);            // [kTileZ][CH]
+  T *c_wx = c_wz + CH * kTileZ;                         // [P][CH]
+  T *c_wy = c_wx + CH * P;                              // [P][CH]
   T *c_q = c_wy + CH * P;                               // [CH]
-  int *c_ax = reinterpret_cast<int *>(c_q + CH);        // [CH]
-  int *c_ay = c_ax + CH;                                // [CH]
+  int *c_ay = reinterpret_cast<int *>(c_q + CH);        // [CH]
   __shared__ uint32_t seg_lo[kMaxSeg], seg_pre[kMaxSeg + 1];
   __shared__ int nseg_s;
-  __shared__ int warp_cnt[kSpreadThreads / 32];
+  __shared__ int kcnt[NW][NK];      // per-warp bucket counts, then bases
+  __shared__ int kstart[NK + 1];
 
   const AtomGrid &ag = a.ag;
   const int tiles_pf = a.ntx * a.nty * a.ntz;
@@ -228,116 +244,197 @@ __global__ void __launch_bounds__(kSpreadThreads) k_spread(SpreadArgs<T> a) {
   const FrameGeom &g = a.geom[f];
   const T scale = (T)g.scale;
 
-  if (threadIdx.x == 0) {
-    int xl[16], yl[16], zl[16];
-    const int nxl = axis_bins(x0 - P + 1, txv + P - 1, ag.nx, ag.nbx, xl);
-    const int nyl = axis_bins(y0 - P + 1, tyv + P - 1, ag.ny, ag.nby, yl);
-    const int nzl = axis_bins(z0 - P + 1, tzv + P - 1, ag.nz, ag.nbz, zl);
-    int ns = 0;
-    uint32_t pre = 0;
-    const uint32_t fbase = (uint32_t)f * ag.bins_per_frame;
-    for (int iz = 0; iz < nzl; ++iz)
-      for (int iy = 0; iy < nyl; ++iy) {
-        int i = 0;
-        while (i < nxl) {
-          int j = i;
-          while (j + 1 < nxl && xl[j + 1] == xl[j] + 1) ++j;
-          const uint32_t row = fbase + ((uint32_t)zl[iz] * ag.nby + (uint32_t)yl[iy]) * ag.nbx;
-          const uint32_t lo = a.bin_start[row + xl[i]], hi = a.bin_start[row + xl[j] + 1];
-          if (hi > lo && ns < kMaxSeg) {
-            seg_lo[ns] = lo;
-            seg_pre[ns] = pre;
-            pre += hi - lo;
-            ++ns;
-          }
-          i = j + 1;
-        }
+  for (int i = threadIdx.x; i < NW * NK; i += blockDim.x) (&kcnt[0][0])[i] = 0;
+  if (threadIdx.x < 32) {
+    // Segments of the cell-sorted atom array: one lane per (z, y) bin row;
+    // a row gives at most two runs of consecutive x bins (two when the tile
+    // halo wraps).  Runs are numbered in lane order by a warp scan.
+    constexpr int kRows = ((kTileY + P - 2) / kBin + 2) * ((kTileZ + P - 2) / kBin + 2);
+    static_assert(kRows <= 32 && 2 * kRows <= kMaxSeg, "segment table too small for the tile");
+    __shared__ int bl[3][16];
+    __shared__ int nbl[3];
+    const int lane = threadIdx.x;
+    if (lane < 3) {
+      const int lo = (lane == 0 ? x0 : lane == 1 ? y0 : z0) - P + 1;
+      const int len = (lane == 0 ? txv : lane == 1 ? tyv : tzv) + P - 1;
+      const int n = lane == 0 ? ag.nx : lane == 1 ? ag.ny : ag.nz;
+      const int nb = lane == 0 ? ag.nbx : lane == 1 ? ag.nby : ag.nbz;
+      nbl[lane] = axis_bins(lo, len, n, nb, bl[lane]);
+    }
+    __syncwarp();
+    const int nxl = nbl[0], nyl = nbl[1], nzl = nbl[2];
+    uint32_t lo2[2] = {0, 0}, cnt2[2] = {0, 0};
+    if (lane < nzl * nyl) {
+      const int iz = lane / nyl, iy = lane - iz * nyl;
+      const uint32_t row = (uint32_t)f * ag.bins_per_frame +
+                           ((uint32_t)bl[2][iz] * ag.nby + (uint32_t)bl[1][iy]) * ag.nbx;
+      // x bins are ascending with at most one break
+      int brk = nxl;
+      for (int i = 1; i < nxl; ++i)
+        if (brk == nxl && bl[0][i] != bl[0][i - 1] + 1) brk = i;
+      lo2[0] = a.bin_start[row + bl[0][0]];
+      cnt2[0] = a.bin_start[row + bl[0][brk - 1] + 1] - lo2[0];
+      if (brk < nxl) {
+        lo2[1] = a.bin_start[row + bl[0][brk]];
+        cnt2[1] = a.bin_start[row + bl[0][nxl - 1] + 1] - lo2[1];
       }
-    seg_pre[ns] = pre;
-    nseg_s = ns;
+    }
+    const int ne = (cnt2[0] > 0) + (cnt2[1] > 0);
+    int eo = ne;
+    uint32_t co = cnt2[0] + cnt2[1];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int ue = __shfl_up_sync(0xffffffffu, eo, o);
+      const uint32_t uc = __shfl_up_sync(0xffffffffu, co, o);
+      if (lane >= o) { eo += ue; co += uc; }
+    }
+    int sg = eo - ne;
+    uint32_t pre = co - (cnt2[0] + cnt2[1]);
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (cnt2[h] > 0) {
+        seg_lo[sg] = lo2[h];
+        seg_pre[sg] = pre;
+        pre += cnt2[h];
+        ++sg;
+      }
+    if (lane == 31) {
+      nseg_s = eo;
+      seg_pre[eo] = co;
+    }
   }
   __syncthreads();
   const int nseg = nseg_s;
   const uint32_t ncand = seg_pre[nseg];
 
   const int lx = threadIdx.x % kTileX, ly = threadIdx.x / kTileX;
-  const int gx = x0 + lx, gy = y0 + ly;
+  const int gy = y0 + ly;
   const bool own = lx < txv && ly < tyv;
   T acc[kTileZ];
 #pragma unroll
   for (int z = 0; z < kTileZ; ++z) acc[z] = T(0);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
   for (uint32_t c0 = 0; c0 < ncand; c0 += CH) {
-    // ---- load and filter one chunk of candidates (order preserving) ----
+    // ---- load and filter one chunk of candidates ----
     const uint32_t ci = c0 + threadIdx.x;
     bool rel = false;
     int4 an = make_int4(0, 0, 0, 0);
-    uint32_t sidx = 0;
+    int key = 0;
+    T tf[3] = {T(0), T(0), T(0)}, qv = T(0);
     if (ci < ncand) {
       int lo = 0, hi = nseg - 1;
       while (lo < hi) {  // last segment with seg_pre <= ci
         const int mid = (lo + hi + 1) >> 1;
         if (seg_pre[mid] <= ci) lo = mid; else hi = mid - 1;
       }
-      sidx = seg_lo[lo] + (ci - seg_pre[lo]);
+      const uint32_t sidx = seg_lo[lo] + (ci - seg_pre[lo]);
       an = a.s_anchor[sidx];
-      const bool rx = imod(x0 - an.x, ag.nx) < P || imod(an.x - x0, ag.nx) < txv;
+      // issued with the anchor so that one memory latency covers all four
+      tf[0] = a.s_t[(int64_t)sidx * 3 + 0];
+      tf[1] = a.s_t[(int64_t)sidx * 3 + 1];
+      tf[2] = a.s_t[(int64_t)sidx * 3 + 2];
+      qv = a.s_q[sidx];
+      key = imod(an.x - x0 + P - 1, ag.nx);
+      const bool rx = key < txv + P - 1;
       const bool ry = imod(y0 - an.y, ag.ny) < P || imod(an.y - y0, ag.ny) < tyv;
       const bool rz = imod(z0 - an.z, ag.nz) < P || imod(an.z - z0, ag.nz) < tzv;
       rel = rx && ry && rz;
     }
-    const unsigned bal = __ballot_sync(0xffffffffu, rel);
-    if (lane == 0) warp_cnt[warp] = __popc(bal);
+    // ---- bucket positions: warp match ranks + warp-ordered prefix ----
+    const unsigned peers = __match_any_sync(0xffffffffu, rel ? key : NK + lane);
+    const int rank = __popc(peers & lt);
+    if (rel && rank == 0) kcnt[warp][key] = __popc(peers);
     __syncthreads();
-    int base = 0, total = 0;
-    for (int w = 0; w < kSpreadThreads / 32; ++w) {
-      if (w < warp) base += warp_cnt[w];
-      total += warp_cnt[w];
+    if (warp == 0) {
+      int tot[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int k = lane + 32 * h;
+        int run = 0;
+        if (k < NK) {
+#pragma unroll
+          for (int w = 0; w < NW; ++w) {
+            const int c = kcnt[w][k];
+            kcnt[w][k] = run;
+            run += c;
+          }
+        }
+        tot[h] = run;
+      }
+      // exclusive scan of the bucket totals over keys 0..63
+      int inc0 = tot[0], inc1 = tot[1];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u0 = __shfl_up_sync(0xffffffffu, inc0, o), u1 = __shfl_up_sync(0xffffffffu, inc1, o);
+        if (lane >= o) { inc0 += u0; inc1 += u1; }
+      }
+      const int all0 = __shfl_sync(0xffffffffu, inc0, 31);
+      const int st0 = inc0 - tot[0], st1 = all0 + inc1 - tot[1];
+      if (lane < NK) kstart[lane] = st0;
+      if (lane + 32 < NK) kstart[lane + 32] = st1;
+      if (lane == 31) kstart[NK] = all0 + inc1;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int k = lane + 32 * h;
+        if (k < NK) {
+          const int s = h ? st1 : st0;
+#pragma unroll
+          for (int w = 0; w < NW; ++w) kcnt[w][k] += s;
+        }
+      }
     }
+    __syncthreads();
     if (rel) {
-      const int slot = base + __popc(bal & ((1u << lane) - 1u));
+      const int slot = kcnt[warp][key] + rank;
       T w1[P];
-      spline_w<T, P>(a.spline, a.s_t[(int64_t)sidx * 3 + 0], w1, a.qc);
+      spline_w<T, P>(a.spline, tf[0], w1, a.qc);
 #pragma unroll
-      for (int k = 0; k < P; ++k) c_wx[slot * P + k] = w1[k];
-      spline_w<T, P>(a.spline, a.s_t[(int64_t)sidx * 3 + 1], w1, a.qc);
+      for (int k = 0; k < P; ++k) c_wx[k * CH + slot] = w1[k];
+      spline_w<T, P>(a.spline, tf[1], w1, a.qc);
 #pragma unroll
-      for (int k = 0; k < P; ++k) c_wy[slot * P + k] = w1[k];
-      spline_w<T, P>(a.spline, a.s_t[(int64_t)sidx * 3 + 2], w1, a.qc);
+      for (int k = 0; k < P; ++k) c_wy[k * CH + slot] = w1[k];
+      spline_w<T, P>(a.spline, tf[2], w1, a.qc);
+      const int dz0 = imod(z0 - an.z, ag.nz);
 #pragma unroll
       for (int z = 0; z < kTileZ; ++z) {
         T wz = T(0);
         if (z < tzv) {
-          const int d = imod(z0 + z - an.z, ag.nz);
+          int d = dz0 + z;
+          if (d >= ag.nz) d -= ag.nz;
 #pragma unroll
           for (int k = 0; k < P; ++k) wz = (d == k) ? w1[k] : wz;
         }
-        c_wz[slot * kTileZ + z] = wz;
+        c_wz[z * CH + slot] = wz;
       }
-      c_q[slot] = a.s_q[sidx] * scale;
-      c_ax[slot] = an.x;
+      c_q[slot] = qv * scale;
       c_ay[slot] = an.y;
     }
     __syncthreads();
-    // ---- accumulate the chunk in candidate order ----
+    // counts for the next chunk; kcnt is not read again in this one
+    for (int i = threadIdx.x; i < NW * NK; i += blockDim.x) (&kcnt[0][0])[i] = 0;
+    // ---- accumulate: bucket of x offset dx holds the anchors gx - dx ----
     if (own) {
-      for (int j = 0; j < total; ++j) {
-        int dx = gx - c_ax[j];
-        if (dx < 0) dx += ag.nx;
-        if (dx >= P) continue;
-        int dy = gy - c_ay[j];
-        if (dy < 0) dy += ag.ny;
-        if (dy >= P) continue;
-        const T wxy = c_wx[j * P + dx] * c_wy[j * P + dy] * c_q[j];
-        const T *wz = c_wz + j * kTileZ;
 #pragma unroll
-        for (int z = 0; z < kTileZ; ++z) acc[z] += wxy * wz[z];
+      for (int dx = 0; dx < P; ++dx) {
+        int k = lx + P - 1 - dx;
+        if (k >= ag.nx) k -= ag.nx;
+        const int jb = kstart[k], je = kstart[k + 1];
+        for (int j = jb; j < je; ++j) {
+          int dy = gy - c_ay[j];
+          if (dy < 0) dy += ag.ny;
+          if (dy >= P) continue;
+          const T wxy = c_wx[dx * CH + j] * c_wy[dy * CH + j] * c_q[j];
+#pragma unroll
+          for (int z = 0; z < kTileZ; ++z) acc[z] += wxy * c_wz[z * CH + j];
+        }
       }
     }
     __syncthreads();
   }
   if (own) {
+    const int gx = x0 + lx;
     T *out = a.rho + (int64_t)f * ((int64_t)ag.nx * ag.ny * ag.nz) + (int64_t)gy * ag.nx + gx;
     const int64_t plane = (int64_t)ag.nx * ag.ny;
 #pragma unroll
@@ -704,133 +801,6 @@ __global__ void __launch_bounds__(256, 2) k_zfused(KsArgs<T> a, int ic, RadixPla
   }
 }
 
-// Persistent, double-buffered form of k_zfused: tile = f*nchunks + chunk,
-// the next tile's spectrum columns stream into shared memory with cp.async
-// while the current one is transformed.  The transformed rho-hat is kept in
-// the current input buffer (same slots), the Green scalars in s_g.
-template <typename T, int L>
-__global__ void __launch_bounds__(256, 1) k_zfused_pipe(KsArgs<T> a, int ic, int64_t ntiles,
-                                                        const cplx_t<T> *__restrict__ twz, int write_spec) {
-  using C = cplx_t<T>;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
-  __shared__ double red[2][32];
-  for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
-    s_amp[m] = (double)a.amp[m];
-    s_bw2[m] = (double)a.bw2[m];
-  }
-  constexpr int n = 1 << L, TPT = n / kEPT;
-  const int nthr = blockDim.x;
-  C *buf0 = reinterpret_cast<C *>(smem_raw);
-  C *buf1 = buf0 + (size_t)n * ic;
-  C *xbuf = buf1 + (size_t)n * ic;
-  C *stw = xbuf + (size_t)padded_row(n) * ic;
-  double *s_g = reinterpret_cast<double *>(stw + n);  // [kEPT][2][nthr]
-  load_twiddles<T>(stw, twz, n);
-  const int c = threadIdx.x % ic, t = threadIdx.x / ic;
-  const int64_t inner = (int64_t)a.ny * a.nxh;
-  const int64_t nchunks = (inner + ic - 1) / ic;
-  const int nfield = a.nfield;
-  const double inv = 1.0 / ((double)a.nx * a.ny * a.nz);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // the input of tile f*nchunks + chunk is spec[f] viewed as [nz][inner]
-  auto issue = [&](C *buf, int64_t tile) {
-    const int64_t f = tile / nchunks;
-    cols_issue<T>(buf, a.spec + f * a.nh, inner, n, ic, nchunks, tile - f * nchunks);
-  };
-  int64_t tile = blockIdx.x;
-  if (tile < ntiles) issue(buf0, tile);
-  cp_async_commit();
-  __syncthreads();
-  for (int it = 0; tile < ntiles; ++it, tile += gridDim.x) {
-    C *cur = (it & 1) ? buf1 : buf0;
-    C *nxt = (it & 1) ? buf0 : buf1;
-    const int64_t next = tile + gridDim.x;
-    if (next < ntiles) issue(nxt, next);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-    const int f = (int)(tile / nchunks);
-    const int64_t chunk = tile - (int64_t)f * nchunks;
-    const int64_t col = chunk * ic + c;
-    const bool ok = col < inner;
-    const FrameGeom &g = a.geom[f];
-    C v[kEPT];
-#pragma unroll
-    for (int e = 0; e < kEPT; ++e) v[e] = cur[(t + e * TPT) * ic + c];
-    ct_fft<T, -1, L, true>(v, t, stw, xbuf + c, ic);
-#pragma unroll
-    for (int e = 0; e < kEPT; ++e) cur[(t + e * TPT) * ic + c] = v[e];  // own slots: no race
-    if (write_spec && ok) {
-      C *sp = const_cast<C *>(a.spec) + (int64_t)f * a.nh + col;
-#pragma unroll
-      for (int e = 0; e < kEPT; ++e) sp[(int64_t)(t + e * TPT) * inner] = v[e];
-    }
-    const int mx = ok ? (int)(col % a.nxh) : 0;
-    const int iy = ok ? (int)(col / a.nxh) : 0;
-    const int my = signed_mode(iy, a.ny);
-    const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
-    const double *bt = (g.ortho && a.btab) ? a.btab + (int64_t)f * a.btab_stride : nullptr;
-    double accE = 0.0, accD = 0.0;
-#pragma unroll 1
-    for (int e = 0; e < kEPT; ++e) {
-      const int iz = t + e * TPT;
-      const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr, bt);
-      const bool live = ok && mg.live;
-      const C r = cur[(t + e * TPT) * ic + c];
-      if (live) {
-        const double rr = (double)r.x, ri = (double)r.y;
-        accE += w * mg.gE * (rr * rr + ri * ri);
-        accD += w * mg.gS;
-      }
-      s_g[(2 * e) * nthr + threadIdx.x] = live ? mg.gF * inv : 0.0;
-      s_g[(2 * e + 1) * nthr + threadIdx.x] = live ? mg.gE * inv : 0.0;
-    }
-    C *out = a.fspec ? a.fspec + (int64_t)f * nfield * a.nh + (ok ? col : 0) : nullptr;
-    for (int fl = 0; fl < nfield; ++fl) {
-      const bool force = a.want_force && fl < 3;
-      double km = 0.0, kz = 0.0;
-      if (force) {
-        km = g.kmat[fl * 3 + 0] * mx + g.kmat[fl * 3 + 1] * my;
-        kz = g.kmat[fl * 3 + 2];
-      }
-      C wv[kEPT];
-#pragma unroll
-      for (int e = 0; e < kEPT; ++e) {
-        const C r = cur[(t + e * TPT) * ic + c];
-        const double rr = (double)r.x, ri = (double)r.y;
-        if (force) {
-          const double kc = km + kz * signed_mode(t + e * TPT, a.nz);
-          const double sc = s_g[(2 * e) * nthr + threadIdx.x];
-          wv[e] = cmk<C, T>((T)(-kc * sc * ri), (T)(kc * sc * rr));
-        } else {
-          const double sc = s_g[(2 * e + 1) * nthr + threadIdx.x];
-          wv[e] = cmk<C, T>((T)(sc * rr), (T)(sc * ri));
-        }
-      }
-      ct_fft<T, +1, L, true>(wv, t, stw, xbuf + c, ic);
-      if (ok) {
-        C *o = out + (int64_t)fl * a.nh;
-#pragma unroll
-        for (int e = 0; e < kEPT; ++e) o[(int64_t)(t + e * TPT) * inner] = wv[e];
-      }
-    }
-    accE = warp_sum(accE);
-    accD = warp_sum(accD);
-    if (lane == 0) { red[0][warp] = accE; red[1][warp] = accD; }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      double e = 0.0, d = 0.0;
-      for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) { e += red[0][wi]; d += red[1][wi]; }
-      double *p = a.part + ((int64_t)f * nchunks + chunk) * 2;
-      p[0] = e;
-      p[1] = d;
-    }
-    __syncthreads();
-  }
-  cp_async_wait<0>();
-}
-
 // Green tables: one thread per half-spectrum mode writes gE(k) (and gF(k)
 // for alias frames) and the block's share of the self sum sum_w gS.  The
 // Green function depends on the box and the kernel parameters only, so the
@@ -854,14 +824,15 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
     const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
     double *gout = a.gtab + (int64_t)f * a.nh + col;
     double *gfout = (g.pad && a.gtabF) ? a.gtabF + (int64_t)f * a.nh + col : nullptr;
-    if (g.ortho && a.btab && !g.pad) {
-      // separable path: K = sum_m amp_m (Bx_m By_m) Bz_m, hoisting Bx_m By_m
+    if (g.ortho && a.btab && !g.pad && a.M <= 16) {
+      // separable path: K = sum_m amp_m (Bx_m By_m) Bz_m with the x-y
+      // products of up to 16 Gaussians held in registers
       const int M = a.M;
       const double *bt = a.btab + (int64_t)f * a.btab_stride;
       const double *bx = bt, *by = bt + M * a.nxh, *bz = by + M * a.ny;
-      double axy[kMaxGauss];
-#pragma unroll 16
-      for (int m = 0; m < M; ++m) axy[m] = s_amp[m] * bx[m * a.nxh + mx] * by[m * a.ny + iy];
+      double axy[16];
+#pragma unroll
+      for (int m = 0; m < 16; ++m) axy[m] = m < M ? s_amp[m] * bx[m * a.nxh + mx] * by[m * a.ny + iy] : 0.0;
       const double kx = g.kmat[0] * mx, ky = g.kmat[4] * signed_mode(iy, a.ny);
       const double kxy2 = kx * kx + ky * ky;
       const double txy = a.tx[mx] * a.ty[iy];
@@ -873,13 +844,14 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
         const bool live = !((mx | iy | mz) == 0) && ksq <= g.k_sq_max;
         double K = 0.0;
         if (live) {
-#pragma unroll 16
-          for (int m = 0; m < M; ++m) K += axy[m] * bz[m * a.nz + iz];
+          const double *bzi = bz + iz;
+#pragma unroll
+          for (int m = 0; m < 16; ++m)
+            if (m < M) K += axy[m] * bzi[m * a.nz];
         }
         double D = txy * a.tz[iz];
         if (quads) D = 1.0 / (D < 1e-20 ? 1e-20 : D);
-        const double gE = live ? K * D : 0.0;
-        gout[(int64_t)iz * inner] = gE;
+        gout[(int64_t)iz * inner] = live ? K * D : 0.0;
         if (live) accD += w * K;
       }
     } else {
@@ -902,11 +874,6 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
   }
 }
 
-// one 8-byte element per call (the gE table tile)
-__device__ __forceinline__ void cp_async_f64(double *dst, const double *src, bool valid) {
-  cp_async8(dst, src, valid);
-}
-
 // Fused z pass (power-of-two nz) with the Green function read from k_green's
 // table: forward z-FFT of ic spectrum columns, energy partial sum, and for
 // every field the scaled spectrum (i k_a gF rho / N or gE rho / N) inverse
@@ -921,8 +888,8 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
   C *buf0 = reinterpret_cast<C *>(smem_raw);
   C *buf1 = buf0 + (size_t)n * ic;
   C *xbuf = buf1 + (size_t)n * ic;
-  C *stw = xbuf + (size_t)padded_row(n) * ic;
-  load_twiddles<T>(stw, twz, n);
+  C *stg = xbuf + (size_t)padded_row(n) * ic;
+  load_stage_twiddles<T, L, 0>(stg, twz);
   const int c = threadIdx.x % ic, t = threadIdx.x / ic;
   const int64_t inner = (int64_t)a.ny * a.nxh;
   const int64_t nchunks = (inner + ic - 1) / ic;
@@ -955,7 +922,7 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
     C v[kEPT];
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) v[e] = cur[(t + e * TPT) * ic + c];
-    ct_fft<T, -1, L, true>(v, t, stw, xbuf + c, ic);
+    ct_fft<T, -1, L, true>(v, t, stg, xbuf + c, ic);
     const int mx = ok ? (int)(col % a.nxh) : 0;
     const int iy = ok ? (int)(col / a.nxh) : 0;
     const int my = signed_mode(iy, a.ny);
@@ -997,7 +964,7 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
           wv[e] = cmk<C, T>((T)(gs[e] * rr), (T)(gs[e] * ri));
         }
       }
-      ct_fft<T, +1, L, true>(wv, t, stw, xbuf + c, ic);
+      ct_fft<T, +1, L, true>(wv, t, stg, xbuf + c, ic);
       if (ok) {
         C *o = out + (int64_t)fl * a.nh;
 #pragma unroll
@@ -1276,12 +1243,14 @@ int cols_per_cta(int n) {
 // Persistent grids: one wave of resident CTAs looping over the tiles.
 template <typename K>
 unsigned persistent_grid(K kernel, int threads, size_t smem, int64_t ntiles) {
-  static int nsm = 0;
+  static std::atomic<int> sm_count[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int nsm = sm_count[dev & 63].load(std::memory_order_relaxed);
   if (!nsm) {
-    int dev = 0;
-    cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     if (nsm <= 0) nsm = 1;
+    sm_count[dev & 63].store(nsm, std::memory_order_relaxed);
   }
   int per = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, threads, smem) != cudaSuccess) {
@@ -1308,9 +1277,17 @@ bool with_pow2(int n, Fn &&f) {
   }
 }
 
+// Raises the dynamic shared-memory limit of `kernel` once per device (the
+// attribute is per device); later calls only look the pair up.
 template <typename K>
-void allow_smem(K kernel) {
-  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+void allow_smem(K kernel, int bytes = 220 * 1024) {
+  static std::mutex mu;
+  static std::set<std::pair<const void *, int>> seen;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (seen.insert({reinterpret_cast<const void *>(kernel), dev}).second)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 // ---- FFT passes: register-resident kernels for power-of-two axes, the
@@ -1335,7 +1312,7 @@ void pass_x_fwd(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t nbatch, cudaStream
     const int rpc = std::max(1, 256 / tpt);
     const int64_t ntiles = (rows + rpc - 1) / rpc;
     const int thr = tpt * rpc;
-    const size_t sm = 2 * (size_t)rpc * n * sizeof(T) + ((size_t)rpc * padded_row(n / 2) + n) * sizeof(C);
+    const size_t sm = 2 * (size_t)rpc * n * sizeof(T) + ((size_t)rpc * padded_row(n / 2) + n + n / 2) * sizeof(C);
     allow_smem(k_r2c_pipe<T, L>);
     k_r2c_pipe<T, L><<<persistent_grid(k_r2c_pipe<T, L>, thr, sm, ntiles), thr, sm, st>>>(
         rho, spec, rows, rpc, ntiles, p->twx.as<C>());
@@ -1369,8 +1346,7 @@ void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nframes, int F,
     const int64_t ntiles = (rows + rpc - 1) / rpc;
     const int nxh = n / 2 + 1;
     const int thr = tpt * F * rpc;
-    const size_t xsz = std::max((size_t)rpc * F * padded_row(n / 2) * sizeof(C), (size_t)rpc * n * F * sizeof(T));
-    const size_t sm = 2 * (size_t)rpc * F * nxh * sizeof(C) + ((xsz + 15) & ~(size_t)15) + (size_t)n * sizeof(C);
+    const size_t sm = (3 * (size_t)rpc * F * nxh + (size_t)rpc * F * padded_row(n / 2) + n + n / 2) * sizeof(C);
     allow_smem(k_c2r_pipe<T, L>);
     k_c2r_pipe<T, L><<<persistent_grid(k_c2r_pipe<T, L>, thr, sm, ntiles), thr, sm, st>>>(
         fspec, freal, F, nzy, rows, rpc, ntiles, p->twx.as<C>());
@@ -1439,38 +1415,30 @@ void pass_cols(sog_plan *p, cplx_t<T> *data, int n, int64_t inner, int64_t outer
 
 template <typename T>
 void set_fft_smem_attrs() {
-  static bool done = false;
-  if (done) return;
-  done = true;
   const int big = 200 * 1024;
-  cudaFuncSetAttribute(k_fft_r2c_x<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_fft_c2r_x<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_fft_strided<T, -1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_fft_strided<T, +1>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_cols_reg<T, -1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_cols_reg<T, +1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_cols_reg<T, -1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_cols_reg<T, +1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_rows_r2c_reg<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_rows_c2r_reg<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_rows_c2r_il<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  cudaFuncSetAttribute(k_zfused<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  allow_smem(k_fft_r2c_x<T>, big);
+  allow_smem(k_fft_c2r_x<T>, big);
+  allow_smem(k_fft_strided<T, -1>, big);
+  allow_smem(k_fft_strided<T, +1>, big);
+  allow_smem(k_cols_reg<T, -1, false>, big);
+  allow_smem(k_cols_reg<T, +1, false>, big);
+  allow_smem(k_cols_reg<T, -1, true>, big);
+  allow_smem(k_cols_reg<T, +1, true>, big);
+  allow_smem(k_rows_r2c_reg<T>, big);
+  allow_smem(k_rows_c2r_il<T>, big);
+  allow_smem(k_zfused<T>, big);
 }
 
 template <typename T, int P>
 size_t spread_smem() {
   constexpr int CH = kSpreadThreads;
-  return (size_t)CH * (kTileZ + 2 * P + 1) * sizeof(T) + 2 * (size_t)CH * sizeof(int);
+  return (size_t)CH * (kTileZ + 2 * P + 1) * sizeof(T) + (size_t)CH * sizeof(int);
 }
 
 template <typename T, int P>
 void launch_spread(const SpreadArgs<T> &sa, int nframes, cudaStream_t st, Tracer *tr) {
-  static bool attr = false;
   const size_t sm = spread_smem<T, P>();
-  if (!attr) {
-    cudaFuncSetAttribute(k_spread<T, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    attr = true;
-  }
+  allow_smem(k_spread<T, P>, (int)sm);
   const int64_t tiles = (int64_t)sa.ntx * sa.nty * sa.ntz * nframes;
   k_spread<T, P><<<(unsigned)tiles, kSpreadThreads, sm, st>>>(sa);
   after(tr, st, "spread");
