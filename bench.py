@@ -102,9 +102,31 @@ def algorithmic_bytes(cfg, s: int = 8, nfield: int = 3):
         "fft_y_inv": nfield * 4 * s * nh,
         "fft_c2r_x": nfield * (2 * s * nh + s * ng),
         "gather": nfield * s * ng + 4 * s * N + 3 * s * N,
+        # fused z pass: spectrum in, nfield transformed fields out (the Green
+        # table it reads is not part of the minimal pipeline)
+        "zfused": 2 * s * nh + nfield * 2 * s * nh,
+        # Green table written once per evaluation
+        "green": s * nh,
     }
     b_ef = 7 * s * N + 8 * s * ng + 16 * s * nh
     return b_ef, per_kernel
+
+
+def profiled_traffic(kernel: str, config: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary of the
+    512^3 workload (profiles/dram_mesh512_bspline6.md), or None."""
+    if config != "cfg5":
+        return None
+    p = os.path.join(ROOT, "profiles", "dram_mesh512_bspline6.md")
+    try:
+        with open(p) as f:
+            for line in f:
+                cells = [c.strip().strip("`") for c in line.strip().strip("|").split("|")]
+                if len(cells) >= 5 and cells[1] == kernel:
+                    return float(cells[4]) * 1e9
+    except (OSError, ValueError):
+        return None
+    return None
 
 
 def measured_peak():
@@ -334,7 +356,8 @@ def run_gpu(args, rank: int, world: int):
     if dom is not None and dom in per_kernel:
         ach = per_kernel[dom] / (kernels[dom]["avg_ms"] * 1e-3) / 1e9
         roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
-                "frac": ach / peak, "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                "frac": ach / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                "traffic": profiled_traffic(dom, args.config),
                 "algorithmic_bytes_per_launch": per_kernel[dom]}
     for k, v in kernels.items():
         if k in per_kernel:

@@ -181,7 +181,7 @@ class _PlanCache:
         self.plans.clear()
 
 
-def _timings(fn, handle, cap: int = 256):
+def _timings(fn, handle, cap: int = 8192):
     names = (ctypes.c_char_p * cap)()
     ms = (ctypes.c_float * cap)()
     cnt = ctypes.c_int(0)
