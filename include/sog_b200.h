@@ -39,6 +39,7 @@ extern "C" {
 #define SOG_ERR_NOMEM 3       /* device or pinned allocation failed           */
 #define SOG_ERR_UNSUPPORTED 4 /* valid request this build does not implement  */
 #define SOG_ERR_DEVICE 5      /* a kernel raised a status bit (see plan status) */
+#define SOG_ERR_COMM 6        /* the caller's exchange callback failed        */
 
 #define SOG_DTYPE_F64 0
 #define SOG_DTYPE_F32 1
@@ -130,6 +131,51 @@ typedef struct sog_mesh_args {
  * 769-798).  Replaces compute_quads_fft (quads_fft.py:209-326) and the
  * backward of Cubes2FFTFunction (cubes2_fft.py:746-869). */
 SOG_API int sog_mesh_forward(sog_plan *plan, const sog_mesh_args *args, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* One large system over several GPUs: z-slab decomposition                  */
+/* ------------------------------------------------------------------------ */
+/* Rank r of `size` (one GPU each, every rank with the whole atom set) owns
+ * real-space planes [r*nz/size, (r+1)*nz/size) and, after the transpose,
+ * half-spectrum rows [r*ny/size, (r+1)*ny/size).  The caller supplies the
+ * collective as a callback that must run in stream order on `stream`:
+ *   SOG_EXCH_ALLTOALL  send block k (bytes each, at send_off + k*bytes) to
+ *                      rank k; receive rank k's block at recv_off + k*bytes;
+ *   SOG_EXCH_HALO      send `bytes` at send_off to rank r-1, receive rank
+ *                      r+1's `bytes` at recv_off (ranks mod size);
+ *   SOG_EXCH_SUM_F64   in-place sum over ranks of bytes/8 doubles at send_off.
+ * Offsets are bytes into `workspace`, which has sog_mesh_slab_workspace()
+ * bytes at the same layout on every rank.  No counterpart in the reference,
+ * which solves the whole mesh on every rank (the plugin's FFT3d spans the
+ * full grid on each MPI rank, lmp/sog.cpp:1084-1087). */
+#define SOG_EXCH_ALLTOALL 0
+#define SOG_EXCH_HALO 1
+#define SOG_EXCH_SUM_F64 2
+
+typedef int (*sog_exchange_fn)(void *ctx, int kind, int64_t send_off, int64_t recv_off, int64_t bytes,
+                               void *stream);
+
+typedef struct sog_slab_desc {
+  int rank, size;
+  void *workspace;          /* device, sog_mesh_slab_workspace() bytes        */
+  size_t workspace_bytes;
+  sog_exchange_fn exchange;
+  void *ctx;                /* passed back to exchange                       */
+} sog_slab_desc;
+
+/* Workspace bytes for a plan split over `size` ranks with `nfield` fields
+ * (3 for forces, +1 for dE/dq). */
+SOG_API int sog_mesh_slab_workspace(const sog_plan *plan, int nfield, int size, size_t *bytes);
+
+/* sog_mesh_forward for one frame split over the ranks of `slab`: energy (the
+ * same on every rank), and forces / dE/dq of the atoms whose stencil anchor
+ * lies in this rank's planes (the other rows are zeroed; summing the arrays
+ * over ranks gives every atom's).  Requires nframes = 1, nz a power of two
+ * up to 1024, nz and ny divisible by size, nz/size a multiple of 8 and at
+ * least order-1.  Parameter gradients and the virial are not available in
+ * this mode (SOG_ERR_UNSUPPORTED). */
+SOG_API int sog_mesh_slab_forward(sog_plan *plan, const sog_mesh_args *args, const sog_slab_desc *slab,
+                                  void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* Direct k-sum                                                              */

@@ -56,10 +56,22 @@ class DirectArgs(ctypes.Structure):
                 ("grad_bw2", _vp), ("virial", _vp)]
 
 
+# int exchange(void *ctx, int kind, int64 send_off, int64 recv_off, int64 bytes, void *stream)
+EXCHANGE_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
+                               ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p)
+EXCH_ALLTOALL, EXCH_HALO, EXCH_SUM_F64 = 0, 1, 2
+
+
+class SlabDesc(ctypes.Structure):
+    _fields_ = [("rank", ctypes.c_int), ("size", ctypes.c_int), ("workspace", _vp),
+                ("workspace_bytes", ctypes.c_size_t), ("exchange", EXCHANGE_FN), ("ctx", _vp)]
+
+
 EXPORTS = ["sog_strerror", "sog_last_error", "sog_version", "sog_launch_count", "sog_plan_create",
            "sog_plan_destroy", "sog_plan_status", "sog_plan_set_timing", "sog_plan_timings",
            "sog_mesh_forward", "sog_direct_create", "sog_direct_destroy", "sog_direct_set_timing",
-           "sog_direct_timings", "sog_direct_forward"]
+           "sog_direct_timings", "sog_direct_forward", "sog_direct_forward_noalloc",
+           "sog_mesh_slab_workspace", "sog_mesh_slab_forward"]
 
 _lib = None
 _lock = threading.Lock()
@@ -87,6 +99,10 @@ def load():
         lib.sog_plan_destroy.argtypes = [_vp]
         lib.sog_plan_status.argtypes = [_vp, ctypes.POINTER(ctypes.c_uint)]
         lib.sog_mesh_forward.argtypes = [_vp, ctypes.POINTER(MeshArgs), _vp]
+        lib.sog_mesh_slab_workspace.argtypes = [_vp, ctypes.c_int, ctypes.c_int,
+                                                ctypes.POINTER(ctypes.c_size_t)]
+        lib.sog_mesh_slab_forward.argtypes = [_vp, ctypes.POINTER(MeshArgs), ctypes.POINTER(SlabDesc),
+                                              _vp]
         lib.sog_direct_create.argtypes = [ctypes.POINTER(_vp), ctypes.c_int, ctypes.c_int]
         lib.sog_direct_destroy.argtypes = [_vp]
         lib.sog_direct_forward.argtypes = [_vp, ctypes.POINTER(DirectArgs), _vp]
@@ -218,6 +234,60 @@ def _host_i64(vals: Sequence[int]):
 
 def _host_f64(vals: Sequence[float]):
     return (ctypes.c_double * len(vals))(*[float(v) for v in vals])
+
+
+def _mesh_args(atom_begin, atom_count, k_sq_max, positions, charges, cells, amp, bw2, norm_factor,
+               self_coeff, remove_self, k0_correction, charge_neutral_lambda, energy, forces,
+               potential, grad_amp, grad_bw2, virial):
+    nf = len(atom_begin)
+    ab, ac, km = _host_i64(atom_begin), _host_i64(atom_count), _host_f64(k_sq_max)
+    args = MeshArgs()
+    args.nframes = nf
+    args.atom_begin = ctypes.cast(ab, _c_i64p)
+    args.atom_count = ctypes.cast(ac, _c_i64p)
+    args.k_sq_max = ctypes.cast(km, _c_dp)
+    args.nchannels = charges.shape[1]
+    args.positions, args.charges, args.cells = _ptr(positions), _ptr(charges), _ptr(cells)
+    args.n_gauss = amp.numel()
+    args.amp, args.bw2 = _ptr(amp), _ptr(bw2)
+    args.norm_factor, args.self_coeff = float(norm_factor), float(self_coeff)
+    args.remove_self, args.k0_correction = int(remove_self), int(k0_correction)
+    args.charge_neutral_lambda = float(charge_neutral_lambda or 0.0)
+    args.energy, args.forces, args.potential = _ptr(energy), _ptr(forces), _ptr(potential)
+    args.grad_amp, args.grad_bw2, args.virial = _ptr(grad_amp), _ptr(grad_bw2), _ptr(virial)
+    return args, (ab, ac, km)
+
+
+def slab_workspace_bytes(plan: "Plan", nfield: int, size: int) -> int:
+    out = ctypes.c_size_t(0)
+    check(load().sog_mesh_slab_workspace(plan.handle, int(nfield), int(size), ctypes.byref(out)),
+          "sog_mesh_slab_workspace")
+    return int(out.value)
+
+
+def mesh_slab_forward(plan: "Plan", group, *, atom_begin, atom_count, k_sq_max, positions, charges,
+                      cells, amp, bw2, norm_factor, self_coeff, remove_self, k0_correction,
+                      charge_neutral_lambda, energy, forces=None, potential=None, stream=None):
+    """One frame split over the ranks of ``group`` (a ``sog_b200.slab.SlabGroup``).
+    Forces / dE/dq come back for this rank's slab atoms only (others zero)."""
+    _require_cuda(positions)
+    args, keep = _mesh_args(atom_begin, atom_count, k_sq_max, positions, charges, cells, amp, bw2,
+                            norm_factor, self_coeff, remove_self, k0_correction,
+                            charge_neutral_lambda, energy, forces, potential, None, None, None)
+    nfield = (3 if forces is not None else 0) + (1 if potential is not None else 0)
+    ws = group.workspace(slab_workspace_bytes(plan, nfield, group.size), positions.device)
+    cb = EXCHANGE_FN(group.callback(ws))
+    desc = SlabDesc()
+    desc.rank, desc.size = group.rank, group.size
+    desc.workspace, desc.workspace_bytes = ws.data_ptr(), ws.numel()
+    desc.exchange, desc.ctx = cb, None
+    if stream is None:
+        stream = torch.cuda.current_stream(positions.device).cuda_stream
+    rc = load().sog_mesh_slab_forward(plan.handle, ctypes.byref(args), ctypes.byref(desc),
+                                      ctypes.c_void_p(stream))
+    group.raise_pending()
+    check(rc, "sog_mesh_slab_forward")
+    del keep
 
 
 def mesh_forward(plan: Plan, *, atom_begin, atom_count, k_sq_max, positions, charges, cells, amp,

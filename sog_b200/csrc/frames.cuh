@@ -277,16 +277,14 @@ __global__ void k_finalize_frames(FinalArgs a, int nf) {
 }
 
 // potential: dE/dq = norm * (gathered - 2 q (rsi*diag + self)) + k=0 / penalty terms
+// dE/dq of one atom from its raw potential (all channels): self and k=0
+// terms, the neutrality penalty, times norm (cubes2_fft.py:536-583,
+// gaussian.py:784-798).
 template <typename T>
-__global__ void k_finalize_atoms(const FrameGeom *__restrict__ geom, const double *__restrict__ fscal,
-                                 const double *__restrict__ qsum, const T *__restrict__ q,
-                                 T *__restrict__ pot, int nch, double norm, double self_coeff,
-                                 double lambda, int remove_self, int k0) {
-  const int f = blockIdx.y;
-  const FrameGeom &g = geom[f];
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= g.natoms) return;
-  const int64_t atom = g.atom_begin + i;
+__device__ __forceinline__ void finalize_atom_pot(const FrameGeom &g, const double *__restrict__ fscal, int f,
+                                                  const double *__restrict__ qsum, const T *__restrict__ q,
+                                                  T *__restrict__ pot, int64_t atom, int nch, double norm,
+                                                  double self_coeff, double lambda, int remove_self, int k0) {
   const double diag = fscal[f * 4 + 0], kfe = fscal[f * 4 + 1], Q = fscal[f * 4 + 2];
   for (int c = 0; c < nch; ++c) {
     const double qi = (double)q[atom * nch + c];
@@ -304,6 +302,19 @@ __global__ void k_finalize_atoms(const FrameGeom *__restrict__ geom, const doubl
     }
     pot[atom * nch + c] = (T)v;
   }
+}
+
+template <typename T>
+__global__ void k_finalize_atoms(const FrameGeom *__restrict__ geom, const double *__restrict__ fscal,
+                                 const double *__restrict__ qsum, const T *__restrict__ q,
+                                 T *__restrict__ pot, int nch, double norm, double self_coeff,
+                                 double lambda, int remove_self, int k0) {
+  const int f = blockIdx.y;
+  const FrameGeom &g = geom[f];
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= g.natoms) return;
+  finalize_atom_pot<T>(g, fscal, f, qsum, q, pot, g.atom_begin + i, nch, norm, self_coeff, lambda, remove_self,
+                       k0);
 }
 
 template <typename T>

@@ -20,6 +20,8 @@
 #include <set>
 #include <utility>
 #include <cfloat>
+#include <climits>
+#include <string>
 #include <type_traits>
 #include <cmath>
 #include <cstring>
@@ -176,6 +178,8 @@ struct SpreadArgs {
   int spline;
   int ntx, nty, ntz;
   QuadsCoef qc;
+  // z planes written: [zlo, zlo + zcnt) of nz, stored as rho[f][zcnt][ny][nx]
+  int zlo, zcnt;
 };
 
 constexpr int kSpreadThreads = kTileX * kTileY;
@@ -239,8 +243,9 @@ __global__ void __launch_bounds__(kSpreadThreads, 3) k_spread(SpreadArgs<T> a) {
   const int tz = rem / (a.ntx * a.nty);
   rem -= tz * a.ntx * a.nty;
   const int ty = rem / a.ntx, tx = rem - ty * a.ntx;
-  const int x0 = tx * kTileX, y0 = ty * kTileY, z0 = tz * kTileZ;
-  const int txv = min(kTileX, ag.nx - x0), tyv = min(kTileY, ag.ny - y0), tzv = min(kTileZ, ag.nz - z0);
+  const int x0 = tx * kTileX, y0 = ty * kTileY, z0 = a.zlo + tz * kTileZ;
+  const int txv = min(kTileX, ag.nx - x0), tyv = min(kTileY, ag.ny - y0);
+  const int tzv = min(kTileZ, a.zlo + a.zcnt - z0);
   const FrameGeom &g = a.geom[f];
   const T scale = (T)g.scale;
 
@@ -435,11 +440,11 @@ __global__ void __launch_bounds__(kSpreadThreads, 3) k_spread(SpreadArgs<T> a) {
   }
   if (own) {
     const int gx = x0 + lx;
-    T *out = a.rho + (int64_t)f * ((int64_t)ag.nx * ag.ny * ag.nz) + (int64_t)gy * ag.nx + gx;
     const int64_t plane = (int64_t)ag.nx * ag.ny;
+    T *out = a.rho + (int64_t)f * plane * a.zcnt + (int64_t)gy * ag.nx + gx;
 #pragma unroll
     for (int z = 0; z < kTileZ; ++z)
-      if (z < tzv) out[(int64_t)(z0 + z) * plane] = acc[z];
+      if (z < tzv) out[(int64_t)(z0 - a.zlo + z) * plane] = acc[z];
   }
 }
 
@@ -469,7 +474,13 @@ struct KsArgs {
   // Green tables [nf][nh]: gE (energy / potential) and, for frames whose
   // B-spline aliases fall inside the cutoff, gF (ik forces)
   double *gtab, *gtabF;
-  double *partD;           // [nf][gridDim.x] self-sum partials of k_green
+  double *partD;           // [nf][gridDim.z * gridDim.x] self-sum partials of k_green
+  // y slab of the half spectrum held by this call (k_green, k_zfused_g): rows
+  // y0 .. y0+nyl-1 of ny; the spectrum, tables and fields are [nz][nyl][nxh]
+  int y0, nyl;
+  // k_zfused_g writes the fields of z planes [b*zblk, (b+1)*zblk) as block b
+  // of [nz/zblk][nfield][zblk][nyl][nxh] (zblk = nz: plain [nfield][nz][..])
+  int zblk;
 };
 
 // Per-axis Gaussian factors of the frame (the per-axis tables of
@@ -816,11 +827,14 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
   __syncthreads();
   const int f = blockIdx.y;
   const FrameGeom &g = a.geom[f];
-  const int64_t inner = (int64_t)a.ny * a.nxh;
+  const int64_t inner = (int64_t)a.nyl * a.nxh;
   const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // (iy, mx) column
+  // z planes of this block: the columns are split over gridDim.z
+  const int zper = (a.nz + gridDim.z - 1) / gridDim.z;
+  const int izb = blockIdx.z * zper, ize = min(a.nz, izb + zper);
   double accD = 0.0;
   if (col < inner) {
-    const int mx = (int)(col % a.nxh), iy = (int)(col / a.nxh);
+    const int mx = (int)(col % a.nxh), iy = a.y0 + (int)(col / a.nxh);
     const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
     double *gout = a.gtab + (int64_t)f * a.nh + col;
     double *gfout = (g.pad && a.gtabF) ? a.gtabF + (int64_t)f * a.nh + col : nullptr;
@@ -837,7 +851,7 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
       const double kxy2 = kx * kx + ky * ky;
       const double txy = a.tx[mx] * a.ty[iy];
       const bool quads = a.spline == SOG_SPLINE_QUADS;
-      for (int iz = 0; iz < a.nz; ++iz) {
+      for (int iz = izb; iz < ize; ++iz) {
         const int mz = signed_mode(iz, a.nz);
         const double kz = g.kmat[8] * mz;
         const double ksq = kxy2 + kz * kz;
@@ -856,7 +870,7 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
       }
     } else {
       const double *bt = (g.ortho && a.btab) ? a.btab + (int64_t)f * a.btab_stride : nullptr;
-      for (int iz = 0; iz < a.nz; ++iz) {
+      for (int iz = izb; iz < ize; ++iz) {
         const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr, bt);
         gout[(int64_t)iz * inner] = mg.live ? mg.gE : 0.0;
         if (gfout) gfout[(int64_t)iz * inner] = mg.live ? mg.gF : 0.0;
@@ -870,7 +884,7 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
   if (threadIdx.x == 0) {
     double d = 0.0;
     for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) d += red[wi];
-    a.partD[(int64_t)f * gridDim.x + blockIdx.x] = d;
+    a.partD[((int64_t)f * gridDim.z + blockIdx.z) * gridDim.x + blockIdx.x] = d;
   }
 }
 
@@ -891,7 +905,7 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
   C *stg = xbuf + (size_t)padded_row(n) * ic;
   load_stage_twiddles<T, L, 0>(stg, twz);
   const int c = threadIdx.x % ic, t = threadIdx.x / ic;
-  const int64_t inner = (int64_t)a.ny * a.nxh;
+  const int64_t inner = (int64_t)a.nyl * a.nxh;
   const int64_t nchunks = (inner + ic - 1) / ic;
   const int nfield = a.nfield;
   const double inv = 1.0 / ((double)a.nx * a.ny * a.nz);
@@ -924,7 +938,7 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
     for (int e = 0; e < kEPT; ++e) v[e] = cur[(t + e * TPT) * ic + c];
     ct_fft<T, -1, L, true>(v, t, stg, xbuf + c, ic);
     const int mx = ok ? (int)(col % a.nxh) : 0;
-    const int iy = ok ? (int)(col / a.nxh) : 0;
+    const int iy = a.y0 + (ok ? (int)(col / a.nxh) : 0);
     const int my = signed_mode(iy, a.ny);
     const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
     double accE = 0.0;
@@ -943,6 +957,7 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
     }
     const double *gFp = (g.pad && a.gtabF) ? a.gtabF + (int64_t)f * a.nh + (ok ? col : 0) : nullptr;
     C *out = a.fspec ? a.fspec + (int64_t)f * nfield * a.nh + (ok ? col : 0) : nullptr;
+    const int64_t zbs = (int64_t)a.zblk * inner;   // one field's z block
     for (int fl = 0; fl < nfield; ++fl) {
       const bool force = a.want_force && fl < 3;
       double km = 0.0, kz = 0.0;
@@ -966,9 +981,11 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
       }
       ct_fft<T, +1, L, true>(wv, t, stg, xbuf + c, ic);
       if (ok) {
-        C *o = out + (int64_t)fl * a.nh;
 #pragma unroll
-        for (int e = 0; e < kEPT; ++e) o[(int64_t)(t + e * TPT) * inner] = wv[e];
+        for (int e = 0; e < kEPT; ++e) {
+          const int iz = t + e * TPT, b = iz / a.zblk;
+          out[((int64_t)b * nfield + fl) * zbs + (int64_t)(iz - b * a.zblk) * inner] = wv[e];
+        }
       }
     }
     accE = warp_sum(accE);
@@ -1107,12 +1124,24 @@ struct GatherArgs {
   int channel, nch, accumulate;
   T *forces;          // [N,3]
   T *pot_raw;         // [N,C]
+  // slots slot_lo .. slot_lo+nslots-1; field plane of anchor plane z + c is
+  // z - zlo + c, wrapped at zwrap (nz when the fields hold the whole mesh)
+  int64_t slot_lo;
+  int zlo, zwrap;
+  // when set, the slot range is [*range_lo, *range_hi) read on the device
+  // (the sorted-atom bin offsets of a z slab) and nslots bounds the grid
+  const uint32_t *range_lo, *range_hi;
 };
 
 template <typename T, int P>
 __global__ void __launch_bounds__(256) k_gather(GatherArgs<T> a) {
-  const int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (s >= a.nslots) return;
+  const int64_t si = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (si >= a.nslots) return;
+  int64_t s = a.slot_lo + si;
+  if (a.range_lo) {
+    s = (int64_t)*a.range_lo + si;
+    if (s >= (int64_t)*a.range_hi) return;
+  }
   const int4 an = a.s_anchor[s];
   T wx[P], wy[P], wz[P];
   spline_w<T, P>(a.spline, a.s_t[s * 3 + 0], wx, a.qc);
@@ -1127,8 +1156,8 @@ __global__ void __launch_bounds__(256) k_gather(GatherArgs<T> a) {
   T acc[4] = {T(0), T(0), T(0), T(0)};
 #pragma unroll 1
   for (int c = 0; c < P; ++c) {
-    int gz = an.z + c;
-    if (gz >= ag.nz) gz -= ag.nz;
+    int gz = an.z - a.zlo + c;
+    if (gz >= a.zwrap) gz -= a.zwrap;
 #pragma unroll
     for (int b = 0; b < P; ++b) {
       int gy = an.y + b;
@@ -1159,6 +1188,45 @@ __global__ void __launch_bounds__(256) k_gather(GatherArgs<T> a) {
     }
   }
   if (a.want_pot) a.pot_raw[atom * a.nch + a.channel] = acc[a.want_force ? 3 : 0];
+}
+
+// ---- z-slab decomposition: transpose packing and slab dE/dq ----
+// spec [zs][ny][nxh] -> send [rank d][zs][ys][nxh]; one CTA per send row
+template <typename C>
+__global__ void k_slab_pack(const C *__restrict__ src, C *__restrict__ dst, int zs, int ny, int ys, int nxh) {
+  const int r = blockIdx.x;                 // (d * zs + z) * ys + yl
+  const int yl = r % ys, dz = r / ys;
+  const int z = dz % zs, d = dz / zs;
+  const C *s = src + ((int64_t)z * ny + (int64_t)d * ys + yl) * nxh;
+  C *o = dst + (int64_t)r * nxh;
+  for (int x = threadIdx.x; x < nxh; x += blockDim.x) o[x] = s[x];
+}
+
+// receive [rank s][F][zs][ys][nxh] -> fspec [F][zs][ny][nxh]; one CTA per row
+template <typename C>
+__global__ void k_slab_unpack(const C *__restrict__ src, C *__restrict__ dst, int F, int zs, int ny, int ys,
+                              int nxh) {
+  const int r = blockIdx.x;                 // (f * zs + z) * ny + y
+  const int y = r % ny, fz = r / ny;
+  const int z = fz % zs, f = fz / zs;
+  const int s = y / ys, yl = y - s * ys;
+  const C *in = src + ((((int64_t)s * F + f) * zs + z) * ys + yl) * nxh;
+  C *o = dst + (int64_t)r * nxh;
+  for (int x = threadIdx.x; x < nxh; x += blockDim.x) o[x] = in[x];
+}
+
+// dE/dq finalisation for the atoms of this rank's slab (slots [*lo, *hi))
+template <typename T>
+__global__ void k_finalize_slab(const FrameGeom *__restrict__ geom, const double *__restrict__ fscal,
+                                const double *__restrict__ qsum, const T *__restrict__ q, T *__restrict__ pot,
+                                const int32_t *__restrict__ s_atom, const uint32_t *lo, const uint32_t *hi,
+                                int64_t bound, int nch, double norm, double self_coeff, double lambda,
+                                int remove_self, int k0) {
+  const int64_t si = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (si >= bound) return;
+  const int64_t s = (int64_t)*lo + si;
+  if (s >= (int64_t)*hi) return;
+  finalize_atom_pot<T>(geom[0], fscal, 0, qsum, q, pot, s_atom[s], nch, norm, self_coeff, lambda, remove_self, k0);
 }
 
 }  // namespace sogb
@@ -1301,10 +1369,9 @@ int reg_width(int n, int max_threads, size_t smem_budget) {
 }
 
 template <typename T>
-void pass_x_fwd(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t nbatch, cudaStream_t st) {
+void pass_x_fwd(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t rows, cudaStream_t st) {
   using C = cplx_t<T>;
   const int nx = p->d.nx;
-  const int64_t rows = nbatch * p->d.nz * p->d.ny;
   const bool done = nx >= 16 && with_pow2(nx, [&](auto lc) {
     constexpr int L = decltype(lc)::value < 4 ? 4 : decltype(lc)::value;
     constexpr int n = 1 << L;
@@ -1333,10 +1400,11 @@ void pass_x_fwd(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t nbatch, cudaStream
 
 // F fields of nframes frames -> interleaved real fields [frame][zy][x][F]
 template <typename T>
-void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nframes, int F, cudaStream_t st) {
+// nzy rows per field and frame: fspec [nframes][F][nzy][nx/2+1] -> freal
+// [nframes][nzy][nx][F]
+void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nframes, int64_t nzy, int F, cudaStream_t st) {
   using C = cplx_t<T>;
   const int nx = p->d.nx;
-  const int64_t nzy = (int64_t)p->d.nz * p->d.ny;
   const bool done = nx >= 16 && with_pow2(nx, [&](auto lc) {
     constexpr int L = decltype(lc)::value < 4 ? 4 : decltype(lc)::value;
     constexpr int n = 1 << L;
@@ -1444,6 +1512,16 @@ void launch_spread(const SpreadArgs<T> &sa, int nframes, cudaStream_t st, Tracer
   after(tr, st, "spread");
 }
 
+// z split of the Green-table pass when its (mx, y) columns do not fill one
+// wave of resident CTAs (two per SM); splitting a full wave further costs
+// more (the x-y kernel products are rebuilt per split) than it gains
+inline unsigned green_zsplit(unsigned gblocks, int nf, int nz) {
+  const int64_t have = (int64_t)gblocks * nf;
+  const int64_t want = 2 * 148;
+  const int64_t gz = std::max<int64_t>(1, std::min<int64_t>({8, (want + have - 1) / have, (int64_t)nz}));
+  return (unsigned)gz;
+}
+
 template <typename T>
 void dispatch_spread(const SpreadArgs<T> &sa, int order, int nframes, cudaStream_t st, Tracer *tr) {
   switch (order) {
@@ -1465,13 +1543,20 @@ void dispatch_gather(const GatherArgs<T> &ga, int order, cudaStream_t st, Tracer
   after(tr, st, "gather");
 }
 
-template <typename T>
-int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
-  using C = cplx_t<T>;
-  const int nf = a->nframes, nch = a->nchannels, M = a->n_gauss;
-  const int nx = p->d.nx, ny = p->d.ny, nz = p->d.nz, nxh = p->nxh, P = p->d.order;
-  const int64_t ng = p->ng, nh = p->nh;
+// Frames, geometry, cell sort and charge sums of one call (shared by the
+// single-device and the slab paths).
+struct Prep {
+  FrameGeom *geom = nullptr;
+  unsigned *status = nullptr;
+  AtomGrid ag{};
+  int64_t nslots = 0, maxat = 0;
+};
 
+template <typename T>
+int prepare_atoms(sog_plan *p, const sog_mesh_args *a, cudaStream_t st, Prep &pr) {
+  const int nf = a->nframes, nch = a->nchannels;
+  const int nx = p->d.nx, ny = p->d.ny, nz = p->d.nz, P = p->d.order;
+  Tracer *tr = &p->tr;
   // ---- frames ----
   std::vector<FrameHost> fh(nf);
   int64_t nslots = 0, maxat = 0;
@@ -1498,7 +1583,6 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   p->up.pending = true;
   FrameGeom *geom = p->geom.as<FrameGeom>();
   unsigned *status = p->status.as<unsigned>();
-  Tracer *tr = &p->tr;
   tr->begin(st);
   k_frame_setup<T><<<nblocks(nf, 128), 128, 0, st>>>((const T *)a->cells, p->frames_host_dev.as<FrameHost>(),
                                                      geom, nf, p->d.kconv, nx, ny, nz, status);
@@ -1563,6 +1647,28 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
     after(tr, st, "qsums", 2);
   }
 
+  pr.geom = geom;
+  pr.status = status;
+  pr.ag = ag;
+  pr.nslots = nslots;
+  pr.maxat = maxat;
+  return SOG_OK;
+}
+
+template <typename T>
+int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
+  using C = cplx_t<T>;
+  const int nf = a->nframes, nch = a->nchannels, M = a->n_gauss;
+  const int nx = p->d.nx, ny = p->d.ny, nz = p->d.nz, nxh = p->nxh, P = p->d.order;
+  const int64_t ng = p->ng, nh = p->nh;
+  Prep pr;
+  int rc = prepare_atoms<T>(p, a, st, pr);
+  if (rc != SOG_OK) return rc;
+  FrameGeom *geom = pr.geom;
+  const AtomGrid ag = pr.ag;
+  const int64_t nslots = pr.nslots, maxat = pr.maxat;
+  Tracer *tr = &p->tr;
+
   // ---- buffers ----
   const bool want_force = a->forces != nullptr;
   const bool want_pot = a->potential != nullptr;
@@ -1599,6 +1705,8 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   sa.nty = (ny + kTileY - 1) / kTileY;
   sa.ntz = (nz + kTileZ - 1) / kTileZ;
   sa.qc = qc;
+  sa.zlo = 0;
+  sa.zcnt = nz;
 
   KsArgs<T> ka;
   ka.spec = p->spec.as<C>();
@@ -1614,6 +1722,9 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   ka.alias_extent = p->d.alias_extent;
   ka.nx = nx; ka.ny = ny; ka.nz = nz; ka.nxh = nxh;
   ka.nh = nh;
+  ka.y0 = 0;
+  ka.nyl = ny;
+  ka.zblk = nz;
   ka.nfield = nfield;
   ka.want_force = want_force;
   ka.nx_acc = nx_acc;
@@ -1642,6 +1753,10 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   gar.nch = nch;
   gar.forces = (T *)a->forces;
   gar.pot_raw = (T *)a->potential;
+  gar.slot_lo = 0;
+  gar.zlo = 0;
+  gar.zwrap = nz;
+  gar.range_lo = gar.range_hi = nullptr;
 
   set_fft_smem_attrs<T>();
   const bool zfuse = is_pow2(nz);
@@ -1652,19 +1767,21 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   if (zfuse) {
     // Green tables and the self sum, once per call (independent of the charges)
     const bool aliasable = p->d.spline == SOG_SPLINE_BSPLINE;
+    const unsigned gblocks = nblocks((int64_t)ny * nxh, 256);
+    const unsigned gz = green_zsplit(gblocks, nf, nz);
+    const int64_t gparts = (int64_t)gblocks * gz;
     if (p->gtab.reserve(sizeof(double) * nh * nf) ||
         (aliasable && p->gtabF.reserve(sizeof(double) * nh * nf)) ||
-        p->partD.reserve(sizeof(double) * ((int64_t)ks_blocks * nf + nf + reduce_tmp_elems(nf, 1, ks_blocks, 1))))
+        p->partD.reserve(sizeof(double) * (gparts * nf + nf + reduce_tmp_elems(nf, 1, gparts, 1))))
       return fail(SOG_ERR_NOMEM, "device allocation failed (Green tables)");
     ka.gtab = p->gtab.as<double>();
     ka.gtabF = aliasable ? p->gtabF.as<double>() : nullptr;
     ka.partD = p->partD.as<double>();
-    const unsigned gblocks = nblocks((int64_t)ny * nxh, 256);
-    k_green<T><<<dim3(gblocks, nf), 256, 0, st>>>(ka);
+    k_green<T><<<dim3(gblocks, nf, gz), 256, 0, st>>>(ka);
     after(tr, st, "green");
-    redD = ka.partD + (int64_t)gblocks * nf;
-    reduce_parts(ka.partD, nf, 1, gblocks, 1, 1, redD, redD + nf, st);
-    after(tr, st, "reduce_green", reduce_split(gblocks) > 1 ? 2 : 1);
+    redD = ka.partD + gparts * nf;
+    reduce_parts(ka.partD, nf, 1, gparts, 1, 1, redD, redD + nf, st);
+    after(tr, st, "reduce_green", reduce_split(gparts) > 1 ? 2 : 1);
   }
   auto launch_zfused = [&]() {
     const int write_spec = (want_grad || want_vir) ? 1 : 0;
@@ -1688,7 +1805,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   for (int c = 0; c < nch; ++c) {
     sa.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
     dispatch_spread<T>(sa, P, nf, st, tr);
-    pass_x_fwd<T>(p, p->rho.as<T>(), p->spec.as<C>(), nf, st);
+    pass_x_fwd<T>(p, p->rho.as<T>(), p->spec.as<C>(), (int64_t)nf * nz * ny, st);
     pass_cols<T, -1>(p, p->spec.as<C>(), ny, nxh, (int64_t)nf * nz, p->rpy, p->twy.as<C>(), st, "fft_y_fwd");
     ka.part = p->partE.as<double>() + (int64_t)c * nf * nblk_e * 2;
     if (zfuse) {
@@ -1710,7 +1827,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
         pass_cols<T, +1>(p, p->fspec.as<C>(), nz, (int64_t)ny * nxh, nb, p->rpz, p->twz.as<C>(), st,
                          "fft_z_inv");
       pass_cols<T, +1>(p, p->fspec.as<C>(), ny, nxh, nb * nz, p->rpy, p->twy.as<C>(), st, "fft_y_inv");
-      pass_x_inv<T>(p, p->fspec.as<C>(), p->freal.as<T>(), nf, nfield, st);
+      pass_x_inv<T>(p, p->fspec.as<C>(), p->freal.as<T>(), nf, (int64_t)nz * ny, nfield, st);
       gar.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
       gar.channel = c;
       gar.accumulate = c > 0;
@@ -1755,6 +1872,259 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
         geom, fscal, p->qsum.as<double>(), (const T *)a->charges, (T *)a->potential, nch,
         a->norm_factor, a->self_coeff, a->charge_neutral_lambda, a->remove_self, a->k0_correction);
   if (want_pot && maxat > 0) after(tr, st, "finalize_atoms");
+  SOG_CUDA_TRY(cudaGetLastError());
+  return SOG_OK;
+}
+
+// ==========================================================================
+// z-slab decomposition of one frame over `size` ranks
+// ==========================================================================
+struct SlabLayout {
+  int zs = 0, ys = 0, F = 0;
+  size_t fs = 0, fr = 0, is = 0, ir = 0, fe = 0, red = 0, total = 0;  // workspace byte offsets
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Workspace: forward send / receive (one rank's share of the spectrum each),
+// inverse send / receive (nfield shares), the real fields with order-1 halo
+// planes, and the scalars summed over ranks.
+SlabLayout slab_layout(const sog_plan *p, int nfield, int size) {
+  SlabLayout L;
+  const size_t sc = p->d.dtype == SOG_DTYPE_F64 ? 16 : 8, sr = sc / 2;
+  L.zs = p->d.nz / size;
+  L.ys = p->d.ny / size;
+  L.F = nfield;
+  const size_t share = (size_t)L.zs * p->d.ny * p->nxh * sc;
+  size_t off = 0;
+  L.fs = off; off += align256(share);
+  L.fr = off; off += align256(share);
+  L.is = off; off += align256(share * nfield);
+  L.ir = off; off += align256(share * nfield);
+  L.fe = off; off += align256((size_t)(L.zs + p->d.order - 1) * p->d.ny * p->d.nx * nfield * sr);
+  L.red = off; off += 4096;
+  L.total = off;
+  return L;
+}
+
+template <typename T>
+int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd, cudaStream_t st) {
+  using C = cplx_t<T>;
+  const int nch = a->nchannels, M = a->n_gauss;
+  const int nx = p->d.nx, ny = p->d.ny, nz = p->d.nz, nxh = p->nxh, P = p->d.order;
+  const int rank = sd->rank, size = sd->size;
+  const bool want_force = a->forces != nullptr;
+  const bool want_pot = a->potential != nullptr;
+  const int nfield = (want_force ? 3 : 0) + (want_pot ? 1 : 0);
+  const SlabLayout L = slab_layout(p, nfield, size);
+  if (sd->workspace_bytes < L.total) return fail(SOG_ERR_INVALID, "slab workspace smaller than sog_mesh_slab_workspace()");
+  unsigned char *ws = static_cast<unsigned char *>(sd->workspace);
+  const int zs = L.zs, ys = L.ys, zlo = rank * zs, y0 = rank * ys;
+  auto exchange = [&](int kind, size_t so, size_t ro, size_t bytes) -> int {
+    const int r = sd->exchange(sd->ctx, kind, (int64_t)so, (int64_t)ro, (int64_t)bytes, st);
+    if (r != 0) return fail(SOG_ERR_COMM, "exchange callback returned " + std::to_string(r));
+    return SOG_OK;
+  };
+
+  Prep pr;
+  int rc = prepare_atoms<T>(p, a, st, pr);
+  if (rc != SOG_OK) return rc;
+  FrameGeom *geom = pr.geom;
+  const AtomGrid ag = pr.ag;
+  const int64_t nslots = pr.nslots;
+  Tracer *tr = &p->tr;
+
+  const int64_t nh_loc = (int64_t)nz * ys * nxh;       // spectrum rows of this rank after the transpose
+  const int64_t spec_loc = (int64_t)zs * ny * nxh;     // spectrum of this rank's planes
+  const int zic = reg_width<T>(nz, 256, 32 * 1024);
+  const int64_t zchunks = ((int64_t)ys * nxh + zic - 1) / zic;
+  if (p->rho.reserve(sizeof(T) * (int64_t)zs * ny * nx) || p->spec.reserve(sizeof(C) * spec_loc) ||
+      p->partE.reserve(sizeof(double) * 2 * zchunks * nch) ||
+      (nfield && p->fspec.reserve(sizeof(C) * spec_loc * nfield)) ||
+      p->redtmp.reserve(sizeof(double) * std::max<int64_t>(reduce_tmp_elems(1, nch, zchunks, 2), 1)) ||
+      p->red.reserve(sizeof(double) * (4 * 1 + 8)))
+    return fail(SOG_ERR_NOMEM, "device allocation failed (slab buffers)");
+
+  QuadsCoef qc;
+  std::memset(&qc, 0, sizeof(qc));
+  if (p->d.spline == SOG_SPLINE_QUADS) quads_coeffs(P, qc.c);
+  SpreadArgs<T> sa;
+  sa.s_anchor = p->s_anchor.as<int4>();
+  sa.s_t = p->s_t.as<T>();
+  sa.bin_start = p->bin_start.as<uint32_t>();
+  sa.geom = geom;
+  sa.rho = p->rho.as<T>();
+  sa.ag = ag;
+  sa.spline = p->d.spline;
+  sa.ntx = (nx + kTileX - 1) / kTileX;
+  sa.nty = (ny + kTileY - 1) / kTileY;
+  sa.ntz = (zs + kTileZ - 1) / kTileZ;
+  sa.qc = qc;
+  sa.zlo = zlo;
+  sa.zcnt = zs;
+
+  KsArgs<T> ka;
+  std::memset(&ka, 0, sizeof(ka));
+  ka.spec = reinterpret_cast<C *>(ws + L.fr);
+  ka.fspec = nfield ? reinterpret_cast<C *>(ws + L.is) : nullptr;
+  ka.geom = geom;
+  ka.tx = p->tab.fx.as<double>(); ka.ty = p->tab.fy.as<double>(); ka.tz = p->tab.fz.as<double>();
+  ka.sx = p->tab.sx.as<double>(); ka.sy = p->tab.sy.as<double>(); ka.sz = p->tab.sz.as<double>();
+  ka.amp = (const T *)a->amp;
+  ka.bw2 = (const T *)a->bw2;
+  ka.M = M;
+  ka.spline = p->d.spline;
+  ka.order = P;
+  ka.alias_extent = p->d.alias_extent;
+  ka.nx = nx; ka.ny = ny; ka.nz = nz; ka.nxh = nxh;
+  ka.nh = nh_loc;
+  ka.nfield = nfield;
+  ka.want_force = want_force;
+  ka.nx_acc = 4 * M + 13;
+  ka.y0 = y0;
+  ka.nyl = ys;
+  ka.zblk = zs;
+  ka.btab_stride = (int64_t)M * (nxh + ny + nz);
+  if (p->btab.reserve(sizeof(double) * ka.btab_stride)) return fail(SOG_ERR_NOMEM, "device allocation failed");
+  ka.btab = p->btab.as<double>();
+  k_axis_tables<T><<<dim3(nblocks(ka.btab_stride, 256), 1), 256, 0, st>>>(geom, (const T *)a->bw2, M, nx, ny, nz,
+                                                                         p->btab.as<double>());
+  after(tr, st, "axis_tables");
+  set_fft_smem_attrs<T>();
+
+  // Green table of this rank's spectrum rows and its self-sum partials
+  double *red = reinterpret_cast<double *>(ws + L.red);   // [nch][2] energy sums, then the self sum
+  {
+    const bool aliasable = p->d.spline == SOG_SPLINE_BSPLINE;
+    const unsigned gblocks = nblocks((int64_t)ys * nxh, 256);
+    const unsigned gz = green_zsplit(gblocks, 1, nz);
+    const int64_t gparts = (int64_t)gblocks * gz;
+    if (p->gtab.reserve(sizeof(double) * nh_loc) || (aliasable && p->gtabF.reserve(sizeof(double) * nh_loc)) ||
+        p->partD.reserve(sizeof(double) * (gparts + 1 + reduce_tmp_elems(1, 1, gparts, 1))))
+      return fail(SOG_ERR_NOMEM, "device allocation failed (Green tables)");
+    ka.gtab = p->gtab.as<double>();
+    ka.gtabF = aliasable ? p->gtabF.as<double>() : nullptr;
+    ka.partD = p->partD.as<double>();
+    k_green<T><<<dim3(gblocks, 1, gz), 256, 0, st>>>(ka);
+    after(tr, st, "green");
+    reduce_parts(ka.partD, 1, 1, gparts, 1, 1, red + 2 * nch, ka.partD + gparts + 1, st);
+    after(tr, st, "reduce_green", reduce_split(gparts) > 1 ? 2 : 1);
+  }
+
+  GatherArgs<T> gar;
+  std::memset(&gar, 0, sizeof(gar));
+  gar.s_anchor = p->s_anchor.as<int4>();
+  gar.s_t = p->s_t.as<T>();
+  gar.s_atom = p->s_atom.as<int32_t>();
+  gar.freal = reinterpret_cast<T *>(ws + L.fe);
+  gar.nfield = nfield;
+  gar.want_force = want_force;
+  gar.want_pot = want_pot;
+  gar.nslots = nslots;
+  gar.ng = 0;
+  gar.ag = ag;
+  gar.spline = p->d.spline;
+  gar.qc = qc;
+  gar.norm = a->norm_factor;
+  gar.nch = nch;
+  gar.forces = (T *)a->forces;
+  gar.pot_raw = (T *)a->potential;
+  gar.slot_lo = 0;
+  gar.zlo = zlo;
+  gar.zwrap = INT_MAX;
+  const uint32_t *bs = p->bin_start.as<uint32_t>();
+  const int64_t bins_per_z = (int64_t)ag.nbx * ag.nby;
+  gar.range_lo = bs + (int64_t)(zlo / kBin) * bins_per_z;
+  gar.range_hi = bs + (int64_t)((zlo + zs) / kBin) * bins_per_z;
+
+  // outputs of atoms outside the slab stay zero
+  const int64_t natoms = a->atom_begin[0] + a->atom_count[0];
+  if (want_force) {
+    k_zero<T><<<nblocks(3 * natoms, 256), 256, 0, st>>>((T *)a->forces, 3 * natoms);
+    count_launch();
+  }
+  if (want_pot) {
+    k_zero<T><<<nblocks(natoms * nch, 256), 256, 0, st>>>((T *)a->potential, natoms * nch);
+    count_launch();
+  }
+
+  const size_t share = (size_t)zs * ys * nxh * sizeof(C);
+  for (int c = 0; c < nch; ++c) {
+    sa.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
+    dispatch_spread<T>(sa, P, 1, st, tr);
+    pass_x_fwd<T>(p, p->rho.as<T>(), p->spec.as<C>(), (int64_t)zs * ny, st);
+    pass_cols<T, -1>(p, p->spec.as<C>(), ny, nxh, zs, p->rpy, p->twy.as<C>(), st, "fft_y_fwd");
+    k_slab_pack<C><<<(unsigned)((int64_t)zs * ny), 256, 0, st>>>(p->spec.as<C>(), reinterpret_cast<C *>(ws + L.fs),
+                                                                 zs, ny, ys, nxh);
+    after(tr, st, "slab_pack");
+    if ((rc = exchange(SOG_EXCH_ALLTOALL, L.fs, L.fr, share)) != SOG_OK) return rc;
+    after(tr, st, "exchange_fwd", 0);
+    ka.part = p->partE.as<double>() + (int64_t)c * zchunks * 2;
+    {
+      const int write_spec = 0;
+      const bool done = with_pow2(nz, [&](auto lc) {
+        constexpr int Lz = decltype(lc)::value;
+        constexpr int n = 1 << Lz;
+        const int zthr = (n / kEPT) * zic;
+        const size_t zsm = ((2 * (size_t)n + padded_row(n)) * zic + n) * sizeof(C);
+        allow_smem(k_zfused_g<T, Lz>);
+        k_zfused_g<T, Lz><<<persistent_grid(k_zfused_g<T, Lz>, zthr, zsm, zchunks), zthr, zsm, st>>>(
+            ka, zic, zchunks, p->twz.as<C>(), write_spec);
+      });
+      if (!done) return fail(SOG_ERR_UNSUPPORTED, "slab mode needs a power-of-two nz up to 1024");
+      after(tr, st, "zfused");
+    }
+    if (nfield) {
+      if ((rc = exchange(SOG_EXCH_ALLTOALL, L.is, L.ir, share * nfield)) != SOG_OK) return rc;
+      after(tr, st, "exchange_inv", 0);
+      k_slab_unpack<C><<<(unsigned)((int64_t)nfield * zs * ny), 256, 0, st>>>(
+          reinterpret_cast<const C *>(ws + L.ir), p->fspec.as<C>(), nfield, zs, ny, ys, nxh);
+      after(tr, st, "slab_unpack");
+      pass_cols<T, +1>(p, p->fspec.as<C>(), ny, nxh, (int64_t)nfield * zs, p->rpy, p->twy.as<C>(), st,
+                       "fft_y_inv");
+      pass_x_inv<T>(p, p->fspec.as<C>(), reinterpret_cast<T *>(ws + L.fe), 1, (int64_t)zs * ny, nfield, st);
+      const size_t plane = (size_t)ny * nx * nfield * sizeof(T);
+      if ((rc = exchange(SOG_EXCH_HALO, L.fe, L.fe + plane * zs, plane * (P - 1))) != SOG_OK) return rc;
+      after(tr, st, "exchange_halo", 0);
+      gar.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
+      gar.channel = c;
+      gar.accumulate = c > 0;
+      dispatch_gather<T>(gar, P, st, tr);
+    }
+  }
+  // energy sums of this rank's spectrum rows, summed over ranks
+  reduce_parts(p->partE.as<double>(), 1, nch, zchunks, 2, 2, red, p->redtmp.as<double>(), st);
+  after(tr, st, "reduce", reduce_split(zchunks) > 1 ? 2 : 1);
+  if ((rc = exchange(SOG_EXCH_SUM_F64, L.red, L.red, sizeof(double) * (2 * nch + 1))) != SOG_OK) return rc;
+  after(tr, st, "exchange_sum", 0);
+  FinalArgs fa;
+  std::memset(&fa, 0, sizeof(fa));
+  fa.geom = geom;
+  fa.redE = red;
+  fa.redX = nullptr;
+  fa.redD = red + 2 * nch;
+  fa.qsum = p->qsum.as<double>();
+  fa.amp = a->amp;
+  fa.bw2 = a->bw2;
+  fa.M = M; fa.nch = nch; fa.nx = nx; fa.ny = ny; fa.nz = nz;
+  fa.norm = a->norm_factor;
+  fa.self_coeff = a->self_coeff;
+  fa.lambda = a->charge_neutral_lambda;
+  fa.remove_self = a->remove_self;
+  fa.k0 = a->k0_correction;
+  fa.direct = 0;
+  fa.energy = a->energy;
+  double *fscal = p->red.as<double>();
+  fa.fscal = fscal;
+  k_finalize_frames<T><<<1, 64, 0, st>>>(fa, 1);
+  after(tr, st, "finalize_frames");
+  if (want_pot && nslots > 0) {
+    k_finalize_slab<T><<<nblocks(nslots, 256), 256, 0, st>>>(
+        geom, fscal, p->qsum.as<double>(), (const T *)a->charges, (T *)a->potential, p->s_atom.as<int32_t>(),
+        gar.range_lo, gar.range_hi, nslots, nch, a->norm_factor, a->self_coeff, a->charge_neutral_lambda,
+        a->remove_self, a->k0_correction);
+    after(tr, st, "finalize_atoms");
+  }
   SOG_CUDA_TRY(cudaGetLastError());
   return SOG_OK;
 }
@@ -1867,4 +2237,45 @@ extern "C" int sog_mesh_forward(sog_plan *p, const sog_mesh_args *a, void *strea
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (p->d.dtype == SOG_DTYPE_F64) return mesh_forward_impl<double>(p, a, st);
   return mesh_forward_impl<float>(p, a, st);
+}
+
+// Checks the slab constraints of a plan for `size` ranks ("" when valid).
+static std::string slab_check(const sog_plan *p, int size) {
+  const sog_plan_desc &d = p->d;
+  if (size < 1) return "slab size must be >= 1";
+  if (!is_pow2(d.nz) || d.nz > 1024) return "slab mode needs a power-of-two nz up to 1024";
+  if (d.nz % size || d.ny % size) return "nz and ny must be divisible by the number of ranks";
+  const int zs = d.nz / size;
+  if (zs % kBin) return "nz / ranks must be a multiple of 8";
+  if (zs < d.order - 1) return "nz / ranks must be at least order - 1 (halo from one neighbour)";
+  return "";
+}
+
+extern "C" int sog_mesh_slab_workspace(const sog_plan *p, int nfield, int size, size_t *bytes) {
+  if (!p || !bytes) return fail(SOG_ERR_INVALID, "null argument");
+  if (nfield < 0 || nfield > 4) return fail(SOG_ERR_INVALID, "nfield must be in [0, 4]");
+  const std::string why = slab_check(p, size);
+  if (!why.empty()) return fail(SOG_ERR_UNSUPPORTED, why);
+  *bytes = slab_layout(p, nfield, size).total;
+  return SOG_OK;
+}
+
+extern "C" int sog_mesh_slab_forward(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd, void *stream) {
+  if (!p || !a || !sd) return fail(SOG_ERR_INVALID, "null argument");
+  if (a->nframes != 1) return fail(SOG_ERR_UNSUPPORTED, "slab mode solves exactly one frame per call");
+  if (!a->atom_begin || !a->atom_count || !a->k_sq_max || !a->positions || !a->charges || !a->cells ||
+      !a->amp || !a->bw2)
+    return fail(SOG_ERR_INVALID, "missing input array");
+  if (a->nchannels < 1 || a->nchannels > 8) return fail(SOG_ERR_INVALID, "slab mode takes 1..8 charge channels");
+  if (a->n_gauss < 1 || a->n_gauss > kMaxGauss) return fail(SOG_ERR_INVALID, "n_gauss must be in [1, 64]");
+  if (a->grad_amp || a->grad_bw2 || a->virial)
+    return fail(SOG_ERR_UNSUPPORTED, "slab mode computes energy, forces and dE/dq only");
+  if (!sd->exchange || !sd->workspace) return fail(SOG_ERR_INVALID, "slab needs an exchange callback and a workspace");
+  if (sd->rank < 0 || sd->rank >= sd->size) return fail(SOG_ERR_INVALID, "slab rank out of range");
+  const std::string why = slab_check(p, sd->size);
+  if (!why.empty()) return fail(SOG_ERR_UNSUPPORTED, why);
+  DeviceGuard dg(p->d.device);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p->d.dtype == SOG_DTYPE_F64) return mesh_slab_impl<double>(p, a, sd, st);
+  return mesh_slab_impl<float>(p, a, sd, st);
 }

@@ -201,6 +201,7 @@ extern "C" const char *sog_strerror(int code) {
     case SOG_ERR_NOMEM: return "out of memory";
     case SOG_ERR_UNSUPPORTED: return "unsupported";
     case SOG_ERR_DEVICE: return "device status raised";
+    case SOG_ERR_COMM: return "exchange callback failed";
     default: return "unknown error";
   }
 }

@@ -11,8 +11,11 @@ Solvers:
     ``bspline_order`` 4/5/6; the plugin's B-spline mesh, lmp/sog.cpp),
   * particle-mesh with QuadS (``use_quads_fft=True``, quads_fft.py:209-326).
 Added keys (defaults keep the reference behaviour): ``use_bspline_fft``,
-``bspline_order``, ``mesh_k_convention`` ("physical" | "reference") and
-``mesh_alias_extent``.
+``bspline_order``, ``mesh_k_convention`` ("physical" | "reference"),
+``mesh_alias_extent``, and ``mesh_decomposition`` ("none" | "slab") with
+``process_group``: "slab" splits one frame's mesh over the ranks of the
+process group (z slabs, all-to-all transposes; ``sog_b200.slab``), each rank
+passing the whole system and getting the whole result.
 
 Deliberate differences, each documented in DESIGN.md:
   * raw-mode ``amp`` tensors are not scaled in place (gaussian.py:236 does);
@@ -107,6 +110,7 @@ class Gaussian(nn.Module):
                  cubes2_order: int = 4, use_quads_fft: bool = False, quads_order: int = 6,
                  use_bspline_fft: bool = False, bspline_order: int = 6,
                  mesh_k_convention: str = "physical", mesh_alias_extent: int = 8,
+                 mesh_decomposition: str = "none", process_group: Optional[Any] = None,
                  **_kwargs: Any):
         super().__init__()
         if _kwargs:
@@ -226,6 +230,10 @@ class Gaussian(nn.Module):
         self.mesh_k_convention = _normalize_mode(mesh_k_convention, {"physical", "reference"},
                                                  "mesh_k_convention")
         self.mesh_alias_extent = int(mesh_alias_extent)
+        self.mesh_decomposition = _normalize_mode(mesh_decomposition, {"none", "slab"},
+                                                  "mesh_decomposition")
+        self._process_group = process_group
+        self._slab = None
         self.rcut = float(rcut) if rcut is not None else None
         self.b = float(b)
         self._max_cache_size = max(1, int(max_cache_size))
@@ -405,6 +413,11 @@ class Gaussian(nn.Module):
             spec.kconv = (_lib.KCONV_REFERENCE if self.mesh_k_convention == "reference"
                           else _lib.KCONV_PHYSICAL)
             spec.alias_extent = self.mesh_alias_extent
+            if self.mesh_decomposition == "slab":
+                if self._slab is None:
+                    from .slab import SlabGroup
+                    self._slab = SlabGroup(self._process_group)
+                spec.slab = self._slab
         energy, forces, virial = SolveFunction.apply(q_s, r_s, amp, bw2, spec, need_force,
                                                      bool(compute_virial))
         if forces is not None and perm is not None:

@@ -48,6 +48,7 @@ class SolveSpec:
     k0_correction: bool = True
     charge_neutral_lambda: Optional[float] = None
     cache: dict = field(default_factory=dict)
+    slab: Optional[object] = None    # sog_b200.slab.SlabGroup: one frame over several ranks
 
 
 def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Tensor,
@@ -88,7 +89,24 @@ def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Ten
                       remove_self=spec.remove_self, k0_correction=spec.k0_correction,
                       charge_neutral_lambda=spec.charge_neutral_lambda, energy=e_b,
                       forces=forces, potential=pot, grad_amp=ga_b, grad_bw2=gb_b, virial=v_b)
-        if spec.kind == "mesh":
+        if spec.kind == "mesh" and spec.slab is not None:
+            if len(b.frames) != 1 or nf != 1:
+                raise NotImplementedError("mesh_decomposition='slab' solves one frame per call")
+            if want_grad or want_virial:
+                raise NotImplementedError("mesh_decomposition='slab' computes energy, forces and "
+                                          "dE/dq; parameter gradients and the virial need 'none'")
+            plan = _lib.PLANS.get(dev.index if dev.index is not None else torch.cuda.current_device(),
+                                  dcode, spec.spline, spec.order, b.dims, spec.kconv,
+                                  spec.alias_extent)
+            for k in ("grad_amp", "grad_bw2", "virial"):
+                common.pop(k)
+            _lib.mesh_slab_forward(plan, spec.slab, **common)
+            # each rank holds its slab's atoms; the sum gives every atom's
+            if forces is not None:
+                spec.slab.sum_(forces)
+            if pot is not None:
+                spec.slab.sum_(pot)
+        elif spec.kind == "mesh":
             plan = _lib.PLANS.get(dev.index if dev.index is not None else torch.cuda.current_device(),
                                   dcode, spec.spline, spec.order, b.dims, spec.kconv,
                                   spec.alias_extent)

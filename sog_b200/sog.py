@@ -5,7 +5,8 @@ Same dict / YAML arguments, legacy-key mapping and errors as the reference.
 reference's own tests and README call (test_sog_class.py:24-42) and returns
 ``forces``, ``virial`` and ``used_explicit_derivatives`` next to ``E_lr``,
 ``latent_charges`` and ``BEC``.  New optional keys: ``use_bspline_fft``,
-``bspline_order``, ``mesh_k_convention``, ``mesh_alias_extent``.
+``bspline_order``, ``mesh_k_convention``, ``mesh_alias_extent``,
+``mesh_decomposition``.
 """
 from __future__ import annotations
 
@@ -51,7 +52,8 @@ class Sog(nn.Module):
             kernel_tensor_mode=self.kernel_tensor_mode, use_cubes2_fft=self.use_cubes2_fft,
             use_quads_fft=self.use_quads_fft, quads_order=self.quads_order,
             use_bspline_fft=self.use_bspline_fft, bspline_order=self.bspline_order,
-            mesh_k_convention=self.mesh_k_convention, mesh_alias_extent=self.mesh_alias_extent)
+            mesh_k_convention=self.mesh_k_convention, mesh_alias_extent=self.mesh_alias_extent,
+            mesh_decomposition=self.mesh_decomposition)
         self.bec = BEC(remove_mean=self.remove_mean, epsilon_factor=self.epsilon_factor)
 
     def _parse_arguments(self, args: Dict[str, Any]) -> None:
@@ -78,6 +80,7 @@ class Sog(nn.Module):
         self.bspline_order = int(args.get("bspline_order", 6))
         self.mesh_k_convention = str(args.get("mesh_k_convention", "physical"))
         self.mesh_alias_extent = int(args.get("mesh_alias_extent", 8))
+        self.mesh_decomposition = str(args.get("mesh_decomposition", "none"))
         self.amp = args.get("amp", None)
         self.bandwidth = args.get("bandwidth", None)
         self.kernel_param_mode = str(args.get("kernel_param_mode", "raw")).strip().lower()
