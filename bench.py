@@ -85,9 +85,10 @@ def mesh_dims(cfg):
         n += 1
 
 
-def algorithmic_bytes(cfg, s: int = 8, nfield: int = 3):
+def algorithmic_bytes(cfg, s: int = 8, nfield: int = 3, parts: int = 1):
     """Minimal-pipeline bytes per evaluation (each array once per producer /
-    consumer pass) and per kernel launch."""
+    consumer pass) and per kernel launch; with the mesh split into `parts`
+    slabs, the per-launch figures of one rank."""
     n = mesh_dims(cfg)
     N = cfg["natoms"]
     ng = n ** 3
@@ -109,6 +110,9 @@ def algorithmic_bytes(cfg, s: int = 8, nfield: int = 3):
         "green": s * nh,
     }
     b_ef = 7 * s * N + 8 * s * ng + 16 * s * nh
+    if parts > 1:
+        per_kernel = {k: v / parts for k, v in per_kernel.items()}
+        b_ef = b_ef / parts
     return b_ef, per_kernel
 
 
@@ -257,12 +261,22 @@ def run_gpu(args, rank: int, world: int):
     dev = torch.device("cuda", local)
     cfg = workload(args.config)
     dt = torch.float64 if args.dtype == "f64" else torch.float32
-    r, q, cell, amp_raw, bw = make_inputs(cfg, seed=rank)
+    slab = world > 1 and args.mode == "slab"
+    # slab: every rank holds the same system and its mesh is split over the
+    # ranks; frames: every rank solves its own system (seeded by rank)
+    r, q, cell, amp_raw, bw = make_inputs(cfg, seed=0 if slab else rank)
     n = mesh_dims(cfg)
     N = cfg["natoms"]
-    model = Sog({"use_atomwise": False, "use_bspline_fft": True, "bspline_order": cfg["order"],
-                 "n_dl": cfg["n_dl"], "amp": torch.tensor(amp_raw, dtype=dt),
-                 "bandwidth": torch.tensor(bw, dtype=dt), "trainable_kernel": False}).to(dev)
+    transport = args.transport
+
+    def build_model(tr):
+        return Sog({"use_atomwise": False, "use_bspline_fft": True, "bspline_order": cfg["order"],
+                    "n_dl": cfg["n_dl"], "amp": torch.tensor(amp_raw, dtype=dt),
+                    "bandwidth": torch.tensor(bw, dtype=dt), "trainable_kernel": False,
+                    "mesh_decomposition": "slab" if slab else "none",
+                    "slab_transport": tr}).to(dev)
+
+    model = build_model(transport)
     gauss = model.gaussian
     r_d = torch.tensor(r, dtype=dt, device=dev)
     q_d = torch.tensor(q, dtype=dt, device=dev)
@@ -275,8 +289,20 @@ def run_gpu(args, rank: int, world: int):
     def step_device():
         return gauss.compute_bundle(q=q_d, r=r_d, cell=cell_d, compute_force=True)
 
-    # warm-up
-    for _ in range(args.warmup):
+    # warm-up (every rank fails the same way when peer memory is unavailable:
+    # the library agrees on it collectively, so all fall back together)
+    try:
+        step_device()
+    except _lib.SogError as exc:
+        if not (slab and transport == "peer" and "peer memory" in str(exc)):
+            raise
+        print(f"rank {rank}: peer transport unavailable ({exc}); using the exchange transport",
+              file=sys.stderr, flush=True)
+        transport = "exchange"
+        model = build_model(transport)
+        gauss = model.gaussian
+        step_device()
+    for _ in range(args.warmup - 1):
         step_device()
     torch.cuda.synchronize()
     plan = next(p for p in _lib.PLANS.plans.values() if p.key[4] == (n, n, n))
@@ -343,7 +369,7 @@ def run_gpu(args, rank: int, world: int):
         return
     # ---- roofline of the dominant kernel ----
     s = 8 if dt == torch.float64 else 4
-    b_ef, per_kernel = algorithmic_bytes(cfg, s=s)
+    b_ef, per_kernel = algorithmic_bytes(cfg, s=s, parts=world if slab else 1)
     tot, cnt = {}, {}
     for name, t in kt:
         tot[name] = tot.get(name, 0.0) + t
@@ -357,7 +383,9 @@ def run_gpu(args, rank: int, world: int):
         ach = per_kernel[dom] / (kernels[dom]["avg_ms"] * 1e-3) / 1e9
         roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
                 "frac": ach / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                "traffic": profiled_traffic(dom, args.config),
+                "traffic": (profiled_traffic(dom, args.config) / world
+                            if slab and profiled_traffic(dom, args.config) else
+                            profiled_traffic(dom, args.config)),
                 "algorithmic_bytes_per_launch": per_kernel[dom]}
     for k, v in kernels.items():
         if k in per_kernel:
@@ -370,17 +398,43 @@ def run_gpu(args, rank: int, world: int):
         cpu = {"value": ccfg["natoms"] / tmed, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"{ccfg['workload']}; C/OpenMP oracle E+F, median of 3 after 1 warm-up, "
                          f"{tmed:.2f} s per evaluation"}
+    systems = 1 if slab else world      # systems evaluated per step by the whole job
+    nvlink = None
+    if slab:
+        # bytes each rank sends per evaluation: (P-1)/P of its spectrum share
+        # forward and of its three field shares back, plus the halo planes
+        share = (n // world) * n * (n // 2 + 1) * 2 * s
+        sent = (share + 3 * share) * (world - 1) / world + (cfg["order"] - 1) * n * n * 3 * s
+        ex_ms = sum(v["total_ms"] for k, v in kernels.items()
+                    if k.startswith("exchange") or k.startswith("barrier")) / args.steps
+        nvlink = {"bytes_per_rank_per_step": sent, "exchange_ms_per_step": ex_ms,
+                  "achieved_gbs": (sent / (ex_ms * 1e-3) / 1e9
+                                   if ex_ms > 0 and transport == "exchange" else None),
+                  "peak": 770.0, "unit": "GB/s", "peak_source": "measured peer copy per direction",
+                  "transport": transport,
+                  "note": ("peer: the transposes travel inside the y-FFT and fused z kernels; "
+                           "exchange_ms is the stream time of the barriers and sums only"
+                           if transport == "peer" else
+                           "exchange time is the stream time of the NCCL calls (all-to-all, halo, sums)")}
+    if slab:
+        parallelism = (f"slab{world} (z slabs; transposes stored by the FFT kernels into peer GPUs' "
+                       "buffers over NVLink, NCCL sums as barriers)" if transport == "peer" else
+                       f"slab{world} (z slabs, NCCL all-to-all transposes)")
+    else:
+        parallelism = f"frame-dp{world}" if world > 1 else "single"
     line = {
-        "metric": METRIC, "value": world * N / (ms_max * 1e-3), "unit": UNIT, "n_gpus": world,
+        "metric": METRIC, "value": systems * N / (ms_max * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic (seeded)",
-        "config": {"workload": cfg["workload"], "atoms_per_gpu": N, "mesh": [n, n, n],
-                   "spline": f"bspline{cfg['order']}", "gaussians": cfg["m"],
-                   "parallelism": f"frame-dp{world}" if world > 1 else "single",
+        "scaling": "strong" if slab else "weak", "vs_baseline": None, "dtype": args.dtype,
+        "data": "synthetic (seeded)",
+        "config": {"workload": cfg["workload"], "atoms_per_gpu": N // world if slab else N,
+                   "mesh": [n, n, n], "spline": f"bspline{cfg['order']}", "gaussians": cfg["m"],
+                   "parallelism": parallelism,
                    "l2": "inputs and mesh arrays larger than L2 (>= 1 GB each)"},
-        "e2e": {"value": world * N / (ms_e2e * 1e-3), "unit": UNIT, "ms_per_step": ms_e2e,
+        "e2e": {"value": systems * N / (ms_e2e * 1e-3), "unit": UNIT, "ms_per_step": ms_e2e,
                 "h2d_bytes_per_step": N * 4 * s, "d2h_bytes_per_step": s + N * 3 * s},
         "roofline": roof,
+        "nvlink": nvlink,
         "step_roofline": {"algorithmic_bytes": b_ef, "achieved": step_gbs, "peak": peak,
                           "unit": "GB/s", "frac": step_gbs / peak},
         "kernels": kernels,
@@ -401,6 +455,11 @@ def main():
     ap.add_argument("--config", default="cfg5", choices=["cfg5", "cfg5_eighth", "cfg2"])
     ap.add_argument("--dtype", default="f64", choices=["f64", "f32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--transport", default="peer", choices=["peer", "exchange"],
+                    help="slab mode: NVLink stores from the FFT kernels (peer) or NCCL all-to-all")
+    ap.add_argument("--mode", default="slab", choices=["slab", "frames"],
+                    help="N>1: split one system's mesh over the GPUs (slab) or give each GPU "
+                         "its own system (frames)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

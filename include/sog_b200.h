@@ -151,12 +151,28 @@ SOG_API int sog_mesh_forward(sog_plan *plan, const sog_mesh_args *args, void *st
 #define SOG_EXCH_ALLTOALL 0
 #define SOG_EXCH_HALO 1
 #define SOG_EXCH_SUM_F64 2
+#define SOG_EXCH_ALLGATHER 3   /* `bytes` at send_off from every rank to recv_off + k*bytes */
+
+/* Transports of the transposes and the halo:
+ *  SOG_SLAB_EXCHANGE  pack / unpack kernels around the caller's ALLTOALL and
+ *                     HALO callbacks (any collective library);
+ *  SOG_SLAB_PEER      the column FFT and fused z kernels store straight into
+ *                     the other ranks' receive buffers over NVLink (CUDA IPC
+ *                     handles swapped once with ALLGATHER); the callbacks then
+ *                     only carry ALLGATHER and SUM_F64 (the latter doubles as
+ *                     the stream-ordered barrier between the passes).  All
+ *                     ranks must be GPUs of one node with peer access; at
+ *                     most 8 ranks.  The receive buffers stay exported for
+ *                     the plan's life: destroy the plans of a group together. */
+#define SOG_SLAB_EXCHANGE 0
+#define SOG_SLAB_PEER 1
 
 typedef int (*sog_exchange_fn)(void *ctx, int kind, int64_t send_off, int64_t recv_off, int64_t bytes,
                                void *stream);
 
 typedef struct sog_slab_desc {
   int rank, size;
+  int transport;            /* SOG_SLAB_EXCHANGE | SOG_SLAB_PEER              */
   void *workspace;          /* device, sog_mesh_slab_workspace() bytes        */
   size_t workspace_bytes;
   sog_exchange_fn exchange;
@@ -164,8 +180,9 @@ typedef struct sog_slab_desc {
 } sog_slab_desc;
 
 /* Workspace bytes for a plan split over `size` ranks with `nfield` fields
- * (3 for forces, +1 for dE/dq). */
-SOG_API int sog_mesh_slab_workspace(const sog_plan *plan, int nfield, int size, size_t *bytes);
+ * (3 for forces, +1 for dE/dq) and the given transport. */
+SOG_API int sog_mesh_slab_workspace(const sog_plan *plan, int nfield, int size, int transport,
+                                    size_t *bytes);
 
 /* sog_mesh_forward for one frame split over the ranks of `slab`: energy (the
  * same on every rank), and forces / dE/dq of the atoms whose stencil anchor

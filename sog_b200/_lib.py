@@ -59,12 +59,14 @@ class DirectArgs(ctypes.Structure):
 # int exchange(void *ctx, int kind, int64 send_off, int64 recv_off, int64 bytes, void *stream)
 EXCHANGE_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
                                ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p)
-EXCH_ALLTOALL, EXCH_HALO, EXCH_SUM_F64 = 0, 1, 2
+EXCH_ALLTOALL, EXCH_HALO, EXCH_SUM_F64, EXCH_ALLGATHER = 0, 1, 2, 3
+SLAB_EXCHANGE, SLAB_PEER = 0, 1
 
 
 class SlabDesc(ctypes.Structure):
-    _fields_ = [("rank", ctypes.c_int), ("size", ctypes.c_int), ("workspace", _vp),
-                ("workspace_bytes", ctypes.c_size_t), ("exchange", EXCHANGE_FN), ("ctx", _vp)]
+    _fields_ = [("rank", ctypes.c_int), ("size", ctypes.c_int), ("transport", ctypes.c_int),
+                ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t), ("exchange", EXCHANGE_FN),
+                ("ctx", _vp)]
 
 
 EXPORTS = ["sog_strerror", "sog_last_error", "sog_version", "sog_launch_count", "sog_plan_create",
@@ -99,7 +101,7 @@ def load():
         lib.sog_plan_destroy.argtypes = [_vp]
         lib.sog_plan_status.argtypes = [_vp, ctypes.POINTER(ctypes.c_uint)]
         lib.sog_mesh_forward.argtypes = [_vp, ctypes.POINTER(MeshArgs), _vp]
-        lib.sog_mesh_slab_workspace.argtypes = [_vp, ctypes.c_int, ctypes.c_int,
+        lib.sog_mesh_slab_workspace.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                 ctypes.POINTER(ctypes.c_size_t)]
         lib.sog_mesh_slab_forward.argtypes = [_vp, ctypes.POINTER(MeshArgs), ctypes.POINTER(SlabDesc),
                                               _vp]
@@ -258,10 +260,10 @@ def _mesh_args(atom_begin, atom_count, k_sq_max, positions, charges, cells, amp,
     return args, (ab, ac, km)
 
 
-def slab_workspace_bytes(plan: "Plan", nfield: int, size: int) -> int:
+def slab_workspace_bytes(plan: "Plan", nfield: int, size: int, transport: int) -> int:
     out = ctypes.c_size_t(0)
-    check(load().sog_mesh_slab_workspace(plan.handle, int(nfield), int(size), ctypes.byref(out)),
-          "sog_mesh_slab_workspace")
+    check(load().sog_mesh_slab_workspace(plan.handle, int(nfield), int(size), int(transport),
+                                         ctypes.byref(out)), "sog_mesh_slab_workspace")
     return int(out.value)
 
 
@@ -275,10 +277,11 @@ def mesh_slab_forward(plan: "Plan", group, *, atom_begin, atom_count, k_sq_max, 
                             norm_factor, self_coeff, remove_self, k0_correction,
                             charge_neutral_lambda, energy, forces, potential, None, None, None)
     nfield = (3 if forces is not None else 0) + (1 if potential is not None else 0)
-    ws = group.workspace(slab_workspace_bytes(plan, nfield, group.size), positions.device)
+    ws = group.workspace(slab_workspace_bytes(plan, nfield, group.size, group.transport),
+                         positions.device)
     cb = EXCHANGE_FN(group.callback(ws))
     desc = SlabDesc()
-    desc.rank, desc.size = group.rank, group.size
+    desc.rank, desc.size, desc.transport = group.rank, group.size, group.transport
     desc.workspace, desc.workspace_bytes = ws.data_ptr(), ws.numel()
     desc.exchange, desc.ctx = cb, None
     if stream is None:

@@ -262,3 +262,84 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
 }
 
 }  // namespace sogb
+
+namespace sogb {
+
+// ---------------------------------------------------------------------------
+// Row maps for the column passes of the slab decomposition.  Row `row` of
+// outer slab `o` lives at
+//   tab[b] + (b * bstride + o * ostride + (row - b * rb)) * inner,  b = row / rb,
+// which covers the plain layout [outer][n][inner] (rb = n, ostride = n), the
+// transposed send blocks written straight into the peers' receive buffers
+// (one base pointer per destination rank) and the received blocks read in
+// place [src][F][zs][ys][inner].
+// ---------------------------------------------------------------------------
+constexpr int kMaxSlabRanks = 8;
+
+template <typename C>
+struct RowMap {
+  C *tab[kMaxSlabRanks];
+  int rb;
+  int64_t ostride, bstride;
+  __device__ __forceinline__ C *row(int64_t o, int r, int64_t inner) const {
+    const int b = r / rb;
+    return tab[b] + ((int64_t)b * bstride + o * ostride + (r - b * rb)) * inner;
+  }
+};
+
+// Column FFT (length 2^L) of the tiles [o][*][i0 .. i0+ic) from `in` to
+// `out`, both addressed through row maps.  Same pipeline as k_cols_pipe;
+// stores may go to another GPU's memory over NVLink (made visible to the
+// peers by a system-scope fence before the kernel ends).
+template <typename T, int DIR, bool PAD, int L>
+__global__ void k_cols_map(RowMap<cplx_t<T>> in, RowMap<cplx_t<T>> out, int64_t inner, int ic, int64_t ntiles,
+                           const cplx_t<T> *__restrict__ tw) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  constexpr int n = 1 << L, TPT = n / kEPT;
+  C *buf0 = reinterpret_cast<C *>(smem_raw);
+  C *buf1 = buf0 + (size_t)n * ic;
+  C *xbuf = buf1 + (size_t)n * ic;
+  C *stg = xbuf + (size_t)(PAD ? padded_row(n) : n) * ic;
+  load_stage_twiddles<T, L, 0>(stg, tw);
+  const int c = threadIdx.x % ic, t = threadIdx.x / ic;
+  const int64_t nchunks = (inner + ic - 1) / ic;
+  auto issue = [&](C *buf, int64_t tile) {
+    const int64_t o = tile / nchunks;
+    const int64_t i0 = (tile - o * nchunks) * ic;
+    const int total = n * ic;
+    for (int q = threadIdx.x; q < total; q += blockDim.x) {
+      const int r = q / ic, col = q - r * ic;
+      const bool ok = i0 + col < inner;
+      const C *src = in.row(o, r, inner) + i0 + col;
+      cp_async_elem(buf + q, ok ? src : in.tab[0], ok);
+    }
+  };
+  int64_t tile = blockIdx.x;
+  if (tile < ntiles) issue(buf0, tile);
+  cp_async_commit();
+  for (int it = 0; tile < ntiles; ++it, tile += gridDim.x) {
+    C *cur = (it & 1) ? buf1 : buf0;
+    C *nxt = (it & 1) ? buf0 : buf1;
+    const int64_t next = tile + gridDim.x;
+    if (next < ntiles) issue(nxt, next);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    C v[kEPT];
+#pragma unroll
+    for (int e = 0; e < kEPT; ++e) v[e] = cur[(t + e * TPT) * ic + c];
+    ct_fft<T, DIR, L, PAD>(v, t, stg, xbuf + c, ic);
+    const int64_t o = tile / nchunks;
+    const int64_t i0 = (tile - o * nchunks) * ic;
+    if (i0 + c < inner) {
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) out.row(o, t + e * TPT, inner)[i0 + c] = v[e];
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+  __threadfence_system();
+}
+
+}  // namespace sogb

@@ -21,6 +21,7 @@
 #include <utility>
 #include <cfloat>
 #include <climits>
+#include <functional>
 #include <string>
 #include <type_traits>
 #include <cmath>
@@ -479,8 +480,11 @@ struct KsArgs {
   // y0 .. y0+nyl-1 of ny; the spectrum, tables and fields are [nz][nyl][nxh]
   int y0, nyl;
   // k_zfused_g writes the fields of z planes [b*zblk, (b+1)*zblk) as block b
-  // of [nz/zblk][nfield][zblk][nyl][nxh] (zblk = nz: plain [nfield][nz][..])
+  // of [nz/zblk][nfield][zblk][nyl][nxh] (zblk = nz: plain [nfield][nz][..]);
+  // with zdst[0] set, block b goes to zdst[b] + [nfield][zblk][nyl][nxh]
+  // instead (the receive buffer of rank b, possibly on another GPU)
   int zblk;
+  cplx_t<T> *zdst[kMaxSlabRanks];
 };
 
 // Per-axis Gaussian factors of the frame (the per-axis tables of
@@ -984,7 +988,8 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
 #pragma unroll
         for (int e = 0; e < kEPT; ++e) {
           const int iz = t + e * TPT, b = iz / a.zblk;
-          out[((int64_t)b * nfield + fl) * zbs + (int64_t)(iz - b * a.zblk) * inner] = wv[e];
+          C *ob = a.zdst[0] ? a.zdst[b] + (int64_t)fl * zbs + col : out + ((int64_t)b * nfield + fl) * zbs;
+          ob[(int64_t)(iz - b * a.zblk) * inner] = wv[e];
         }
       }
     }
@@ -1001,6 +1006,7 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
     __syncthreads();
   }
   cp_async_wait<0>();
+  if (a.zdst[0]) __threadfence_system();
 }
 
 // Extras: dE/d(amp_m, bw2_m) partial sums (cubes2_fft.py:822-862) and the
@@ -1191,6 +1197,14 @@ __global__ void __launch_bounds__(256) k_gather(GatherArgs<T> a) {
 }
 
 // ---- z-slab decomposition: transpose packing and slab dE/dq ----
+// plain copy into another rank's halo planes (peer transport)
+template <typename T>
+__global__ void k_halo_push(const T *__restrict__ src, T *__restrict__ dst, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+  __threadfence_system();
+}
+
 // spec [zs][ny][nxh] -> send [rank d][zs][ys][nxh]; one CTA per send row
 template <typename C>
 __global__ void k_slab_pack(const C *__restrict__ src, C *__restrict__ dst, int zs, int ny, int ys, int nxh) {
@@ -1709,6 +1723,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   sa.zcnt = nz;
 
   KsArgs<T> ka;
+  std::memset(&ka, 0, sizeof(ka));
   ka.spec = p->spec.as<C>();
   ka.fspec = nfield ? p->fspec.as<C>() : nullptr;
   ka.geom = geom;
@@ -1889,22 +1904,126 @@ inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 // Workspace: forward send / receive (one rank's share of the spectrum each),
 // inverse send / receive (nfield shares), the real fields with order-1 halo
 // planes, and the scalars summed over ranks.
-SlabLayout slab_layout(const sog_plan *p, int nfield, int size) {
+// With the peer transport the receive buffers belong to the plan (exported
+// to the other ranks) and the workspace holds only the IPC handles being
+// swapped and the summed scalars.
+SlabLayout slab_layout(const sog_plan *p, int nfield, int size, int transport) {
   SlabLayout L;
   const size_t sc = p->d.dtype == SOG_DTYPE_F64 ? 16 : 8, sr = sc / 2;
   L.zs = p->d.nz / size;
   L.ys = p->d.ny / size;
   L.F = nfield;
-  const size_t share = (size_t)L.zs * p->d.ny * p->nxh * sc;
   size_t off = 0;
-  L.fs = off; off += align256(share);
-  L.fr = off; off += align256(share);
-  L.is = off; off += align256(share * nfield);
-  L.ir = off; off += align256(share * nfield);
-  L.fe = off; off += align256((size_t)(L.zs + p->d.order - 1) * p->d.ny * p->d.nx * nfield * sr);
+  if (transport == SOG_SLAB_PEER) {
+    L.fs = off; off += align256(3 * sizeof(cudaIpcMemHandle_t));                       // own handles
+    L.fr = off; off += align256(3 * sizeof(cudaIpcMemHandle_t) * (size_t)size);        // everyone's
+  } else {
+    const size_t share = (size_t)L.zs * p->d.ny * p->nxh * sc;
+    L.fs = off; off += align256(share);
+    L.fr = off; off += align256(share);
+    L.is = off; off += align256(share * nfield);
+    L.ir = off; off += align256(share * nfield);
+    L.fe = off; off += align256((size_t)(L.zs + p->d.order - 1) * p->d.ny * p->d.nx * nfield * sr);
+  }
   L.red = off; off += 4096;
   L.total = off;
   return L;
+}
+
+void close_peers(sog_plan *p) {
+  for (int s = 0; s < p->peer_size; ++s) {
+    if (s == p->peer_rank) continue;
+    for (void **pp : {&p->peer_fwd[s], &p->peer_inv[s], &p->peer_fe[s]})
+      if (*pp) {
+        cudaIpcCloseMemHandle(*pp);
+        *pp = nullptr;
+      }
+  }
+  for (int s = 0; s < 8; ++s) p->peer_fwd[s] = p->peer_inv[s] = p->peer_fe[s] = nullptr;
+  p->peer_rank = -1;
+  p->peer_size = 0;
+}
+
+// Peer transport set-up, once per (plan, group): receive buffers of the
+// largest field count, their IPC handles swapped with ALLGATHER, the peers'
+// buffers opened.  Every rank learns through SUM_F64 whether all ranks
+// succeeded, so a failure returns the same error everywhere.
+template <typename T>
+int peer_setup(sog_plan *p, const sog_slab_desc *sd, unsigned char *ws, const SlabLayout &L, cudaStream_t st,
+               const std::function<int(int, size_t, size_t, size_t)> &exchange) {
+  if (p->peer_rank == sd->rank && p->peer_size == sd->size) return SOG_OK;
+  close_peers(p);
+  using C = cplx_t<T>;
+  const sog_plan_desc &d = p->d;
+  const int64_t share = (int64_t)L.zs * d.ny * p->nxh;
+  if (p->xr_fwd.reserve(sizeof(C) * share) || p->xr_inv.reserve(sizeof(C) * share * 4) ||
+      p->xr_fe.reserve(sizeof(T) * (int64_t)(L.zs + d.order - 1) * d.ny * d.nx * 4))
+    return fail(SOG_ERR_NOMEM, "device allocation failed (slab receive buffers)");
+  cudaIpcMemHandle_t own[3];
+  SOG_CUDA_TRY(cudaIpcGetMemHandle(&own[0], p->xr_fwd.p));
+  SOG_CUDA_TRY(cudaIpcGetMemHandle(&own[1], p->xr_inv.p));
+  SOG_CUDA_TRY(cudaIpcGetMemHandle(&own[2], p->xr_fe.p));
+  SOG_CUDA_TRY(cudaMemcpyAsync(ws + L.fs, own, sizeof(own), cudaMemcpyHostToDevice, st));
+  int rc = exchange(SOG_EXCH_ALLGATHER, L.fs, L.fr, sizeof(own));
+  if (rc != SOG_OK) return rc;
+  std::vector<cudaIpcMemHandle_t> all(3 * (size_t)sd->size);
+  SOG_CUDA_TRY(cudaMemcpyAsync(all.data(), ws + L.fr, sizeof(own) * sd->size, cudaMemcpyDeviceToHost, st));
+  SOG_CUDA_TRY(cudaStreamSynchronize(st));
+  p->peer_rank = sd->rank;
+  p->peer_size = sd->size;
+  double failed = 0.0;
+  for (int s = 0; s < sd->size; ++s) {
+    void **dst[3] = {&p->peer_fwd[s], &p->peer_inv[s], &p->peer_fe[s]};
+    void *local[3] = {p->xr_fwd.p, p->xr_inv.p, p->xr_fe.p};
+    for (int i = 0; i < 3; ++i) {
+      if (s == sd->rank) {
+        *dst[i] = local[i];
+      } else if (cudaIpcOpenMemHandle(dst[i], all[3 * (size_t)s + i], cudaIpcMemLazyEnablePeerAccess) !=
+                 cudaSuccess) {
+        cudaGetLastError();
+        *dst[i] = nullptr;
+        failed += 1.0;
+      }
+    }
+  }
+  double *flag = reinterpret_cast<double *>(ws + L.red);
+  SOG_CUDA_TRY(cudaMemcpyAsync(flag, &failed, sizeof(double), cudaMemcpyHostToDevice, st));
+  if ((rc = exchange(SOG_EXCH_SUM_F64, L.red, L.red, sizeof(double))) != SOG_OK) return rc;
+  double total = 0.0;
+  SOG_CUDA_TRY(cudaMemcpyAsync(&total, flag, sizeof(double), cudaMemcpyDeviceToHost, st));
+  SOG_CUDA_TRY(cudaStreamSynchronize(st));
+  if (total > 0.0) {
+    close_peers(p);
+    return fail(SOG_ERR_UNSUPPORTED, "peer memory between the ranks is not available (CUDA IPC open failed on " +
+                                         std::to_string((int)total) + " buffers); use the exchange transport");
+  }
+  return SOG_OK;
+}
+
+// Row-mapped column FFT pass (power-of-two n only).
+template <typename T, int DIR>
+void pass_cols_map(sog_plan *p, const RowMap<cplx_t<T>> &in, const RowMap<cplx_t<T>> &out, int n, int64_t inner,
+                   int64_t outer, const cplx_t<T> *tw, cudaStream_t st, const char *name) {
+  using C = cplx_t<T>;
+  with_pow2(n, [&](auto lc) {
+    constexpr int L = decltype(lc)::value;
+    constexpr int nn = 1 << L;
+    const int ic = reg_width<T>(nn, 256, 64 * 1024);
+    const int64_t ntiles = outer * ((inner + ic - 1) / ic);
+    const int thr = (nn / kEPT) * ic;
+    if (ic >= 8) {
+      const size_t sm = (3 * (size_t)nn * ic + nn) * sizeof(C);
+      allow_smem(k_cols_map<T, DIR, false, L>);
+      k_cols_map<T, DIR, false, L><<<persistent_grid(k_cols_map<T, DIR, false, L>, thr, sm, ntiles), thr, sm, st>>>(
+          in, out, inner, ic, ntiles, tw);
+    } else {
+      const size_t sm = ((2 * (size_t)nn + padded_row(nn)) * ic + nn) * sizeof(C);
+      allow_smem(k_cols_map<T, DIR, true, L>);
+      k_cols_map<T, DIR, true, L><<<persistent_grid(k_cols_map<T, DIR, true, L>, thr, sm, ntiles), thr, sm, st>>>(
+          in, out, inner, ic, ntiles, tw);
+    }
+  });
+  after(&p->tr, st, name);
 }
 
 template <typename T>
@@ -1916,15 +2035,30 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
   const bool want_force = a->forces != nullptr;
   const bool want_pot = a->potential != nullptr;
   const int nfield = (want_force ? 3 : 0) + (want_pot ? 1 : 0);
-  const SlabLayout L = slab_layout(p, nfield, size);
+  const bool peer = sd->transport == SOG_SLAB_PEER;
+  const SlabLayout L = slab_layout(p, nfield, size, sd->transport);
   if (sd->workspace_bytes < L.total) return fail(SOG_ERR_INVALID, "slab workspace smaller than sog_mesh_slab_workspace()");
   unsigned char *ws = static_cast<unsigned char *>(sd->workspace);
   const int zs = L.zs, ys = L.ys, zlo = rank * zs, y0 = rank * ys;
-  auto exchange = [&](int kind, size_t so, size_t ro, size_t bytes) -> int {
+  std::function<int(int, size_t, size_t, size_t)> exchange = [&](int kind, size_t so, size_t ro,
+                                                                 size_t bytes) -> int {
     const int r = sd->exchange(sd->ctx, kind, (int64_t)so, (int64_t)ro, (int64_t)bytes, st);
     if (r != 0) return fail(SOG_ERR_COMM, "exchange callback returned " + std::to_string(r));
     return SOG_OK;
   };
+  // stream-ordered barrier of the peer transport: a one-double sum (all
+  // ranks' earlier kernels, and so their stores into this rank's buffers,
+  // are complete when it completes)
+  const size_t barrier_off = L.red + 2048;
+  auto barrier = [&](const char *name) -> int {
+    const int r = exchange(SOG_EXCH_SUM_F64, barrier_off, barrier_off, sizeof(double));
+    if (r == SOG_OK) after(&p->tr, st, name, 0);
+    return r;
+  };
+  if (peer) {
+    const int r = peer_setup<T>(p, sd, ws, L, st, exchange);
+    if (r != SOG_OK) return r;
+  }
 
   Prep pr;
   int rc = prepare_atoms<T>(p, a, st, pr);
@@ -1965,8 +2099,13 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
 
   KsArgs<T> ka;
   std::memset(&ka, 0, sizeof(ka));
-  ka.spec = reinterpret_cast<C *>(ws + L.fr);
-  ka.fspec = nfield ? reinterpret_cast<C *>(ws + L.is) : nullptr;
+  ka.spec = peer ? p->xr_fwd.as<C>() : reinterpret_cast<C *>(ws + L.fr);
+  ka.fspec = nfield ? (peer ? p->xr_inv.as<C>() : reinterpret_cast<C *>(ws + L.is)) : nullptr;
+  if (peer && nfield) {
+    // block b of the fields goes to rank b's receive buffer, slot of this rank
+    const int64_t blk = (int64_t)nfield * zs * ys * nxh;
+    for (int b = 0; b < size; ++b) ka.zdst[b] = static_cast<C *>(p->peer_inv[b]) + (int64_t)rank * blk;
+  }
   ka.geom = geom;
   ka.tx = p->tab.fx.as<double>(); ka.ty = p->tab.fy.as<double>(); ka.tz = p->tab.fz.as<double>();
   ka.sx = p->tab.sx.as<double>(); ka.sy = p->tab.sy.as<double>(); ka.sz = p->tab.sz.as<double>();
@@ -2016,7 +2155,8 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
   gar.s_anchor = p->s_anchor.as<int4>();
   gar.s_t = p->s_t.as<T>();
   gar.s_atom = p->s_atom.as<int32_t>();
-  gar.freal = reinterpret_cast<T *>(ws + L.fe);
+  T *fields = peer ? p->xr_fe.as<T>() : reinterpret_cast<T *>(ws + L.fe);
+  gar.freal = fields;
   gar.nfield = nfield;
   gar.want_force = want_force;
   gar.want_pot = want_pot;
@@ -2053,12 +2193,25 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
     sa.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
     dispatch_spread<T>(sa, P, 1, st, tr);
     pass_x_fwd<T>(p, p->rho.as<T>(), p->spec.as<C>(), (int64_t)zs * ny, st);
-    pass_cols<T, -1>(p, p->spec.as<C>(), ny, nxh, zs, p->rpy, p->twy.as<C>(), st, "fft_y_fwd");
-    k_slab_pack<C><<<(unsigned)((int64_t)zs * ny), 256, 0, st>>>(p->spec.as<C>(), reinterpret_cast<C *>(ws + L.fs),
-                                                                 zs, ny, ys, nxh);
-    after(tr, st, "slab_pack");
-    if ((rc = exchange(SOG_EXCH_ALLTOALL, L.fs, L.fr, share)) != SOG_OK) return rc;
-    after(tr, st, "exchange_fwd", 0);
+    if (peer) {
+      // y transform stored straight into every rank's receive buffer:
+      // rows [d*ys, (d+1)*ys) of plane z go to rank d at [this rank][z][..]
+      RowMap<C> in{}, out{};
+      in.tab[0] = p->spec.as<C>();
+      in.rb = ny; in.ostride = ny; in.bstride = 0;
+      for (int d = 0; d < size; ++d)
+        out.tab[d] = static_cast<C *>(p->peer_fwd[d]) + (int64_t)rank * zs * ys * nxh;
+      out.rb = ys; out.ostride = ys; out.bstride = 0;
+      pass_cols_map<T, -1>(p, in, out, ny, nxh, zs, p->twy.as<C>(), st, "fft_y_fwd");
+      if ((rc = barrier("barrier_fwd")) != SOG_OK) return rc;
+    } else {
+      pass_cols<T, -1>(p, p->spec.as<C>(), ny, nxh, zs, p->rpy, p->twy.as<C>(), st, "fft_y_fwd");
+      k_slab_pack<C><<<(unsigned)((int64_t)zs * ny), 256, 0, st>>>(
+          p->spec.as<C>(), reinterpret_cast<C *>(ws + L.fs), zs, ny, ys, nxh);
+      after(tr, st, "slab_pack");
+      if ((rc = exchange(SOG_EXCH_ALLTOALL, L.fs, L.fr, share)) != SOG_OK) return rc;
+      after(tr, st, "exchange_fwd", 0);
+    }
     ka.part = p->partE.as<double>() + (int64_t)c * zchunks * 2;
     {
       const int write_spec = 0;
@@ -2075,17 +2228,36 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
       after(tr, st, "zfused");
     }
     if (nfield) {
-      if ((rc = exchange(SOG_EXCH_ALLTOALL, L.is, L.ir, share * nfield)) != SOG_OK) return rc;
-      after(tr, st, "exchange_inv", 0);
-      k_slab_unpack<C><<<(unsigned)((int64_t)nfield * zs * ny), 256, 0, st>>>(
-          reinterpret_cast<const C *>(ws + L.ir), p->fspec.as<C>(), nfield, zs, ny, ys, nxh);
-      after(tr, st, "slab_unpack");
-      pass_cols<T, +1>(p, p->fspec.as<C>(), ny, nxh, (int64_t)nfield * zs, p->rpy, p->twy.as<C>(), st,
-                       "fft_y_inv");
-      pass_x_inv<T>(p, p->fspec.as<C>(), reinterpret_cast<T *>(ws + L.fe), 1, (int64_t)zs * ny, nfield, st);
       const size_t plane = (size_t)ny * nx * nfield * sizeof(T);
-      if ((rc = exchange(SOG_EXCH_HALO, L.fe, L.fe + plane * zs, plane * (P - 1))) != SOG_OK) return rc;
-      after(tr, st, "exchange_halo", 0);
+      if (peer) {
+        if ((rc = barrier("barrier_inv")) != SOG_OK) return rc;
+        // y inverse read in place from the received blocks [src][F][zs][ys][..]
+        RowMap<C> in{}, out{};
+        for (int s = 0; s < size; ++s) in.tab[s] = p->xr_inv.as<C>();
+        in.rb = ys; in.ostride = ys; in.bstride = (int64_t)nfield * zs * ys;
+        out.tab[0] = p->fspec.as<C>();
+        out.rb = ny; out.ostride = ny; out.bstride = 0;
+        pass_cols_map<T, +1>(p, in, out, ny, nxh, (int64_t)nfield * zs, p->twy.as<C>(), st, "fft_y_inv");
+        pass_x_inv<T>(p, p->fspec.as<C>(), fields, 1, (int64_t)zs * ny, nfield, st);
+        // first order-1 planes to the halo of rank r-1
+        const int prev = (rank + size - 1) % size;
+        const int64_t nh_el = (int64_t)(P - 1) * ny * nx * nfield;
+        k_halo_push<T><<<nblocks(nh_el, 256), 256, 0, st>>>(
+            fields, static_cast<T *>(p->peer_fe[prev]) + (int64_t)zs * ny * nx * nfield, nh_el);
+        after(tr, st, "halo_push");
+        if ((rc = barrier("barrier_halo")) != SOG_OK) return rc;
+      } else {
+        if ((rc = exchange(SOG_EXCH_ALLTOALL, L.is, L.ir, share * nfield)) != SOG_OK) return rc;
+        after(tr, st, "exchange_inv", 0);
+        k_slab_unpack<C><<<(unsigned)((int64_t)nfield * zs * ny), 256, 0, st>>>(
+            reinterpret_cast<const C *>(ws + L.ir), p->fspec.as<C>(), nfield, zs, ny, ys, nxh);
+        after(tr, st, "slab_unpack");
+        pass_cols<T, +1>(p, p->fspec.as<C>(), ny, nxh, (int64_t)nfield * zs, p->rpy, p->twy.as<C>(), st,
+                         "fft_y_inv");
+        pass_x_inv<T>(p, p->fspec.as<C>(), fields, 1, (int64_t)zs * ny, nfield, st);
+        if ((rc = exchange(SOG_EXCH_HALO, L.fe, L.fe + plane * zs, plane * (P - 1))) != SOG_OK) return rc;
+        after(tr, st, "exchange_halo", 0);
+      }
       gar.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
       gar.channel = c;
       gar.accumulate = c > 0;
@@ -2208,6 +2380,10 @@ extern "C" int sog_plan_destroy(sog_plan *p) {
                     &p->s_atom, &p->s_anchor, &p->s_t, &p->s_q, &p->qsum, &p->rho, &p->spec,
                     &p->fspec, &p->freal, &p->partE, &p->partX, &p->red, &p->redtmp, &p->qpart, &p->btab, &p->gtab, &p->gtabF, &p->partD};
   for (DevBuf *b : bufs) b->release();
+  close_peers(p);
+  p->xr_fwd.release();
+  p->xr_inv.release();
+  p->xr_fe.release();
   p->up.release();
   p->tr.release();
   delete p;
@@ -2240,9 +2416,13 @@ extern "C" int sog_mesh_forward(sog_plan *p, const sog_mesh_args *a, void *strea
 }
 
 // Checks the slab constraints of a plan for `size` ranks ("" when valid).
-static std::string slab_check(const sog_plan *p, int size) {
+static std::string slab_check(const sog_plan *p, int size, int transport) {
   const sog_plan_desc &d = p->d;
   if (size < 1) return "slab size must be >= 1";
+  if (transport == SOG_SLAB_PEER) {
+    if (size > kMaxSlabRanks) return "the peer transport spans at most 8 ranks (one node)";
+    if (!is_pow2(d.ny) || d.ny > 1024) return "the peer transport needs a power-of-two ny up to 1024";
+  }
   if (!is_pow2(d.nz) || d.nz > 1024) return "slab mode needs a power-of-two nz up to 1024";
   if (d.nz % size || d.ny % size) return "nz and ny must be divisible by the number of ranks";
   const int zs = d.nz / size;
@@ -2251,12 +2431,13 @@ static std::string slab_check(const sog_plan *p, int size) {
   return "";
 }
 
-extern "C" int sog_mesh_slab_workspace(const sog_plan *p, int nfield, int size, size_t *bytes) {
+extern "C" int sog_mesh_slab_workspace(const sog_plan *p, int nfield, int size, int transport, size_t *bytes) {
   if (!p || !bytes) return fail(SOG_ERR_INVALID, "null argument");
   if (nfield < 0 || nfield > 4) return fail(SOG_ERR_INVALID, "nfield must be in [0, 4]");
-  const std::string why = slab_check(p, size);
+  if (transport != SOG_SLAB_EXCHANGE && transport != SOG_SLAB_PEER) return fail(SOG_ERR_INVALID, "bad transport");
+  const std::string why = slab_check(p, size, transport);
   if (!why.empty()) return fail(SOG_ERR_UNSUPPORTED, why);
-  *bytes = slab_layout(p, nfield, size).total;
+  *bytes = slab_layout(p, nfield, size, transport).total;
   return SOG_OK;
 }
 
@@ -2272,7 +2453,8 @@ extern "C" int sog_mesh_slab_forward(sog_plan *p, const sog_mesh_args *a, const 
     return fail(SOG_ERR_UNSUPPORTED, "slab mode computes energy, forces and dE/dq only");
   if (!sd->exchange || !sd->workspace) return fail(SOG_ERR_INVALID, "slab needs an exchange callback and a workspace");
   if (sd->rank < 0 || sd->rank >= sd->size) return fail(SOG_ERR_INVALID, "slab rank out of range");
-  const std::string why = slab_check(p, sd->size);
+  if (sd->transport != SOG_SLAB_EXCHANGE && sd->transport != SOG_SLAB_PEER) return fail(SOG_ERR_INVALID, "bad transport");
+  const std::string why = slab_check(p, sd->size, sd->transport);
   if (!why.empty()) return fail(SOG_ERR_UNSUPPORTED, why);
   DeviceGuard dg(p->d.device);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

@@ -82,6 +82,11 @@ struct sog_plan {
   sogb::PinnedBuf up;
   sogb::Tracer tr;
   int nb_x = 0, nb_y = 0, nb_z = 0;  // sort bins per axis
+  // z-slab peer transport: receive buffers exported to the other ranks of a
+  // group (CUDA IPC) and the peers' buffers mapped here (own rank: local)
+  sogb::DevBuf xr_fwd, xr_inv, xr_fe;
+  void *peer_fwd[8] = {}, *peer_inv[8] = {}, *peer_fe[8] = {};
+  int peer_rank = -1, peer_size = 0;
 };
 
 struct sog_direct {

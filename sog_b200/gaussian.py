@@ -13,9 +13,10 @@ Solvers:
 Added keys (defaults keep the reference behaviour): ``use_bspline_fft``,
 ``bspline_order``, ``mesh_k_convention`` ("physical" | "reference"),
 ``mesh_alias_extent``, and ``mesh_decomposition`` ("none" | "slab") with
-``process_group``: "slab" splits one frame's mesh over the ranks of the
-process group (z slabs, all-to-all transposes; ``sog_b200.slab``), each rank
-passing the whole system and getting the whole result.
+``process_group`` and ``slab_transport`` ("peer" | "exchange"): "slab"
+splits one frame's mesh over the ranks of the process group (z slabs,
+transposes over NVLink; ``sog_b200.slab``), each rank passing the whole
+system and getting the whole result.
 
 Deliberate differences, each documented in DESIGN.md:
   * raw-mode ``amp`` tensors are not scaled in place (gaussian.py:236 does);
@@ -111,7 +112,7 @@ class Gaussian(nn.Module):
                  use_bspline_fft: bool = False, bspline_order: int = 6,
                  mesh_k_convention: str = "physical", mesh_alias_extent: int = 8,
                  mesh_decomposition: str = "none", process_group: Optional[Any] = None,
-                 **_kwargs: Any):
+                 slab_transport: str = "peer", **_kwargs: Any):
         super().__init__()
         if _kwargs:
             raise TypeError(f"Unexpected keyword arguments: {', '.join(sorted(_kwargs.keys()))}")
@@ -233,6 +234,7 @@ class Gaussian(nn.Module):
         self.mesh_decomposition = _normalize_mode(mesh_decomposition, {"none", "slab"},
                                                   "mesh_decomposition")
         self._process_group = process_group
+        self.slab_transport = _normalize_mode(slab_transport, {"peer", "exchange"}, "slab_transport")
         self._slab = None
         self.rcut = float(rcut) if rcut is not None else None
         self.b = float(b)
@@ -416,7 +418,7 @@ class Gaussian(nn.Module):
             if self.mesh_decomposition == "slab":
                 if self._slab is None:
                     from .slab import SlabGroup
-                    self._slab = SlabGroup(self._process_group)
+                    self._slab = SlabGroup(self._process_group, self.slab_transport)
                 spec.slab = self._slab
         energy, forces, virial = SolveFunction.apply(q_s, r_s, amp, bw2, spec, need_force,
                                                      bool(compute_virial))

@@ -13,7 +13,15 @@ Exchange kinds (the contract of ``include/sog_b200.h``):
   rank k; rank k's block lands at ``recv_off + k*bytes``;
 * ``EXCH_HALO``: ``bytes`` at ``send_off`` go to rank r-1, rank r+1's land at
   ``recv_off`` (ranks mod size);
-* ``EXCH_SUM_F64``: in-place sum over ranks of ``bytes/8`` doubles.
+* ``EXCH_SUM_F64``: in-place sum over ranks of ``bytes/8`` doubles;
+* ``EXCH_ALLGATHER``: ``bytes`` at ``send_off`` from every rank to
+  ``recv_off + k*bytes``.
+
+Transports: ``"peer"`` (default) lets the library's kernels store the
+transposed spectra straight into the other GPUs' receive buffers (CUDA IPC,
+one node); the callbacks then carry only the handle swap and small sums, the
+latter also serving as stream-ordered barriers.  ``"exchange"`` packs the
+blocks and moves them with ``all_to_all_single`` / point-to-point calls.
 
 The reference solves the whole mesh on every rank (its plugin's FFT3d spans
 the full grid, lmp/sog.cpp:1084-1087), so this class has no reference
@@ -30,7 +38,10 @@ from . import _lib
 
 
 class SlabGroup:
-    def __init__(self, group: Optional["dist.ProcessGroup"] = None):
+    def __init__(self, group: Optional["dist.ProcessGroup"] = None, transport: str = "peer"):
+        if transport not in ("peer", "exchange"):
+            raise ValueError("`transport` should be 'peer' or 'exchange'.")
+        self.transport = _lib.SLAB_PEER if transport == "peer" else _lib.SLAB_EXCHANGE
         self.group = group
         if dist.is_available() and dist.is_initialized():
             self.rank = dist.get_rank(group)
@@ -72,6 +83,13 @@ class SlabGroup:
                        dist.P2POp(dist.irecv, recv, nxt, self.group)]
                 for req in dist.batch_isend_irecv(ops):
                     req.wait()
+        elif kind == _lib.EXCH_ALLGATHER:
+            send = ws[send_off:send_off + nbytes]
+            recv = ws[recv_off:recv_off + nbytes * self.size]
+            if self.size == 1:
+                recv.copy_(send)
+            else:
+                dist.all_gather_into_tensor(recv, send, group=self.group)
         elif kind == _lib.EXCH_SUM_F64:
             if nbytes % 8 or send_off % 8:
                 raise ValueError("EXCH_SUM_F64 needs 8-byte aligned doubles")

@@ -53,7 +53,7 @@ class Sog(nn.Module):
             use_quads_fft=self.use_quads_fft, quads_order=self.quads_order,
             use_bspline_fft=self.use_bspline_fft, bspline_order=self.bspline_order,
             mesh_k_convention=self.mesh_k_convention, mesh_alias_extent=self.mesh_alias_extent,
-            mesh_decomposition=self.mesh_decomposition)
+            mesh_decomposition=self.mesh_decomposition, slab_transport=self.slab_transport)
         self.bec = BEC(remove_mean=self.remove_mean, epsilon_factor=self.epsilon_factor)
 
     def _parse_arguments(self, args: Dict[str, Any]) -> None:
@@ -81,6 +81,7 @@ class Sog(nn.Module):
         self.mesh_k_convention = str(args.get("mesh_k_convention", "physical"))
         self.mesh_alias_extent = int(args.get("mesh_alias_extent", 8))
         self.mesh_decomposition = str(args.get("mesh_decomposition", "none"))
+        self.slab_transport = str(args.get("slab_transport", "peer"))
         self.amp = args.get("amp", None)
         self.bandwidth = args.get("bandwidth", None)
         self.kernel_param_mode = str(args.get("kernel_param_mode", "raw")).strip().lower()

@@ -32,17 +32,17 @@ def _system(n, L, seed, tric=False, nch=1):
     return r, q, cell
 
 
-def _gauss(decomp, order=6, n_dl=1.0):
+def _gauss(decomp, order=6, n_dl=1.0, transport="peer"):
     from sog_b200 import Gaussian
     bw = 1.2 * 1.62 ** np.arange(8)
     amp = 1.0 / (bw * np.sqrt(2 * np.pi))
     return Gaussian(n_dl=n_dl, amp=torch.tensor(amp), bandwidth=torch.tensor(bw),
                     use_bspline_fft=True, bspline_order=order, trainable=False,
-                    mesh_decomposition=decomp)
+                    mesh_decomposition=decomp, slab_transport=transport)
 
 
-def _solve(decomp, r, q, cell, dev, order=6, want_pot=False):
-    g = _gauss(decomp, order).to(dev)
+def _solve(decomp, r, q, cell, dev, order=6, want_pot=False, transport="peer"):
+    g = _gauss(decomp, order, transport=transport).to(dev)
     rt = torch.tensor(r, device=dev)
     qt = torch.tensor(q, device=dev, requires_grad=want_pot)
     ct = torch.tensor(cell[None], device=dev)
@@ -53,12 +53,13 @@ def _solve(decomp, r, q, cell, dev, order=6, want_pot=False):
     return out["energy"].detach(), out["forces"].detach(), pot
 
 
-@pytest.mark.parametrize("tric,order,nch", [(False, 6, 1), (True, 4, 1), (False, 5, 2)])
-def test_slab_one_rank_matches_mesh(tric, order, nch):
+@pytest.mark.parametrize("tric,order,nch,transport", [(False, 6, 1, "peer"), (False, 6, 1, "exchange"),
+                                                     (True, 4, 1, "exchange"), (False, 5, 2, "peer")])
+def test_slab_one_rank_matches_mesh(tric, order, nch, transport):
     dev = torch.device("cuda:0")
     r, q, cell = _system(2500, 31.0, 11, tric, nch)
     e0, f0, p0 = _solve("none", r, q, cell, dev, order, want_pot=True)
-    e1, f1, p1 = _solve("slab", r, q, cell, dev, order, want_pot=True)
+    e1, f1, p1 = _solve("slab", r, q, cell, dev, order, want_pot=True, transport=transport)
     torch.testing.assert_close(e1, e0, rtol=E_RTOL, atol=0.0)
     torch.testing.assert_close(f1, f0, rtol=0.0, atol=F_ATOL)
     torch.testing.assert_close(p1, p0, rtol=0.0, atol=F_ATOL)
@@ -84,7 +85,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _child(rank, world, port, tric, res):
+def _child(rank, world, port, tric, transport, res):
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -97,7 +98,7 @@ def _child(rank, world, port, tric, res):
         dev = torch.device("cuda", rank)
         r, q, cell = _system(3000, 31.0, 5, tric)
         e0, f0, p0 = _solve("none", r, q, cell, dev, 6, want_pot=True)
-        e1, f1, p1 = _solve("slab", r, q, cell, dev, 6, want_pot=True)
+        e1, f1, p1 = _solve("slab", r, q, cell, dev, 6, want_pot=True, transport=transport)
         err = [float((e1 - e0).abs().max() / e0.abs().max()), float((f1 - f0).abs().max()),
                float((p1 - p0).abs().max())]
         res[rank] = err
@@ -106,8 +107,8 @@ def _child(rank, world, port, tric, res):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("tric", [False, True])
-def test_slab_two_ranks_nccl(tric):
+@pytest.mark.parametrize("tric,transport", [(False, "peer"), (False, "exchange"), (True, "exchange")])
+def test_slab_two_ranks_nccl(tric, transport):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -115,7 +116,7 @@ def test_slab_two_ranks_nccl(tric):
     with ctx.Manager() as man:
         res = man.dict()
         port = _free_port()
-        procs = [ctx.Process(target=_child, args=(k, 2, port, tric, res)) for k in range(2)]
+        procs = [ctx.Process(target=_child, args=(k, 2, port, tric, transport, res)) for k in range(2)]
         for p in procs:
             p.start()
         for p in procs:

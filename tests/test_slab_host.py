@@ -45,6 +45,10 @@ def _rank_main(rank, world, port, out):
         d[:] = torch.tensor([1.0, rank, 2.5 * rank], dtype=torch.float64)
         g.exchange(ws, _lib.EXCH_SUM_F64, 3072, 3072, 24)
         sums = ws[3072:3072 + 24].view(torch.float64).tolist()
+        # all-gather: 8 bytes of value 50+rank from every rank, rank-major
+        ws[3584:3592] = 50 + rank
+        g.exchange(ws, _lib.EXCH_ALLGATHER, 3584, 3712, 8)
+        gathered = [int(ws[3712 + 8 * k]) for k in range(world)]
         # the C callback reports a failure as status 1 and keeps the exception
         fn = g.callback(ws)
         bad = fn(None, 99, 0, 0, 8, None)
@@ -53,7 +57,7 @@ def _rank_main(rank, world, port, out):
             g.raise_pending()
         except ValueError as exc:
             pending = str(exc)
-        out[rank] = (got, halo, sums, bad, pending)
+        out[rank] = (got, halo, sums, bad, pending, gathered)
     finally:
         dist.destroy_process_group()
 
@@ -75,16 +79,19 @@ def test_exchange_two_gloo_ranks():
                 p.kill()
         assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
         for r in range(world):
-            got, halo, sums, bad, pending = out[r]
+            got, halo, sums, bad, pending, gathered = out[r]
             assert got == [10 * k + r for k in range(world)]       # rank k's block r, rank-major
             assert halo == 100 + (r + 1) % world                     # from rank r+1
             assert sums == [2.0, 1.0, 2.5]
             assert bad == 1 and "unknown exchange kind" in pending
+            assert gathered == [50 + k for k in range(world)]
 
 
 def test_exchange_one_process_is_local_copy():
     g = SlabGroup()
-    assert (g.rank, g.size) == (0, 1)
+    assert (g.rank, g.size) == (0, 1) and g.transport == _lib.SLAB_PEER
+    with pytest.raises(ValueError):
+        SlabGroup(transport="smoke-signals")
     ws = g.workspace(256, torch.device("cpu"))
     ws[:64] = torch.arange(64, dtype=torch.uint8)
     g.exchange(ws, _lib.EXCH_ALLTOALL, 0, 128, 64)
