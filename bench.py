@@ -318,8 +318,10 @@ def run_gpu(args, rank: int, world: int):
     l0 = _lib.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
+    h0 = time.perf_counter()
     for _ in range(args.steps):
         out = step_device()
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps   # enqueue time per step
     ev1.record(stream)
     torch.cuda.synchronize()
     launches = _lib.launch_count() - l0
@@ -439,6 +441,7 @@ def run_gpu(args, rank: int, world: int):
                           "unit": "GB/s", "frac": step_gbs / peak},
         "kernels": kernels,
         "gpu_launches": int(launches),
+        "host_enqueue_ms_per_step": host_ms,
         "clocks": clk,
         "cpu_baseline": cpu,
         "energy_frame0": energy0,

@@ -317,6 +317,18 @@ __global__ void k_finalize_atoms(const FrameGeom *__restrict__ geom, const doubl
                        k0);
 }
 
+// Frame table passed by value (small calls): written to device memory by
+// the first kernel of the call, with no pinned staging buffer and no host wait.
+constexpr int kFramesByValue = 32;
+struct FrameTable {
+  FrameHost fh[kFramesByValue];
+  int nf;
+};
+
+__global__ void k_store_frames(const FrameTable t, FrameHost *__restrict__ dst) {
+  for (int f = threadIdx.x; f < t.nf; f += blockDim.x) dst[f] = t.fh[f];
+}
+
 template <typename T>
 __global__ void k_zero(T *p, int64_t n) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;

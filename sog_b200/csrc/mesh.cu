@@ -17,7 +17,9 @@
 #include <algorithm>
 #include <atomic>
 #include <mutex>
+#include <map>
 #include <set>
+#include <tuple>
 #include <utility>
 #include <cfloat>
 #include <climits>
@@ -820,7 +822,11 @@ __global__ void __launch_bounds__(256, 2) k_zfused(KsArgs<T> a, int ic, RadixPla
 // for alias frames) and the block's share of the self sum sum_w gS.  The
 // Green function depends on the box and the kernel parameters only, so the
 // fused z pass below just streams it next to the spectrum.
-template <typename T>
+// SEP: the separable fast path (orthorhombic frames without aliases inside
+// the cutoff, M <= 16); !SEP: every other frame.  Both are launched on the
+// same grid and each leaves the frames of the other, so the fast path gets
+// a register allocation of its own.
+template <typename T, bool SEP>
 __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
   __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
   __shared__ double red[8];
@@ -831,6 +837,8 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
   __syncthreads();
   const int f = blockIdx.y;
   const FrameGeom &g = a.geom[f];
+  const bool sep = g.ortho && a.btab && !g.pad && a.M <= 16;
+  if (sep != SEP) return;                 // block-uniform: the frame belongs to the other launch
   const int64_t inner = (int64_t)a.nyl * a.nxh;
   const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // (iy, mx) column
   // z planes of this block: the columns are split over gridDim.z
@@ -841,8 +849,7 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
     const int mx = (int)(col % a.nxh), iy = a.y0 + (int)(col / a.nxh);
     const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
     double *gout = a.gtab + (int64_t)f * a.nh + col;
-    double *gfout = (g.pad && a.gtabF) ? a.gtabF + (int64_t)f * a.nh + col : nullptr;
-    if (g.ortho && a.btab && !g.pad && a.M <= 16) {
+    if constexpr (SEP) {
       // separable path: K = sum_m amp_m (Bx_m By_m) Bz_m with the x-y
       // products of up to 16 Gaussians held in registers
       const int M = a.M;
@@ -873,6 +880,7 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
         if (live) accD += w * K;
       }
     } else {
+      double *gfout = (g.pad && a.gtabF) ? a.gtabF + (int64_t)f * a.nh + col : nullptr;
       const double *bt = (g.ortho && a.btab) ? a.btab + (int64_t)f * a.btab_stride : nullptr;
       for (int iz = izb; iz < ize; ++iz) {
         const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr, bt);
@@ -1334,12 +1342,25 @@ unsigned persistent_grid(K kernel, int threads, size_t smem, int64_t ntiles) {
     if (nsm <= 0) nsm = 1;
     sm_count[dev & 63].store(nsm, std::memory_order_relaxed);
   }
+  // resident CTAs per SM, cached per (kernel, threads, smem, device)
+  static std::mutex mu;
+  static std::map<std::tuple<const void *, int, size_t, int>, int> cache;
+  const auto key = std::make_tuple(reinterpret_cast<const void *>(kernel), threads, smem, dev);
   int per = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, threads, smem) != cudaSuccess) {
-    cudaGetLastError();
-    per = 1;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto it = cache.find(key);
+    if (it != cache.end()) per = it->second;
   }
-  per = std::max(per, 1);
+  if (per == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, threads, smem) != cudaSuccess) {
+      cudaGetLastError();
+      per = 1;
+    }
+    per = std::max(per, 1);
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = per;
+  }
   return (unsigned)std::max<int64_t>(1, std::min<int64_t>(ntiles, (int64_t)nsm * per));
 }
 
@@ -1585,16 +1606,27 @@ int prepare_atoms(sog_plan *p, const sog_mesh_args *a, cudaStream_t st, Prep &pr
   }
   if (nslots >= (int64_t)1 << 31) return fail(SOG_ERR_INVALID, "more than 2^31 atoms in one call");
   int rc;
-  if ((rc = p->up.reserve(sizeof(FrameHost) * nf)) != SOG_OK) return rc;
-  if ((rc = p->up.wait()) != SOG_OK) return rc;
-  std::memcpy(p->up.p, fh.data(), sizeof(FrameHost) * nf);
   if (p->frames_host_dev.reserve(sizeof(FrameHost) * nf) || p->geom.reserve(sizeof(FrameGeom) * nf) ||
       p->status.reserve(sizeof(unsigned) * 4))
     return fail(SOG_ERR_NOMEM, "device allocation failed");
-  SOG_CUDA_TRY(cudaMemcpyAsync(p->frames_host_dev.p, p->up.p, sizeof(FrameHost) * nf,
-                               cudaMemcpyHostToDevice, st));
-  SOG_CUDA_TRY(cudaEventRecord(p->up.done, st));
-  p->up.pending = true;
+  if (nf <= kFramesByValue) {
+    // small frame tables travel as a kernel parameter: no host wait
+    FrameTable ft;
+    std::memset(&ft, 0, sizeof(ft));
+    std::memcpy(ft.fh, fh.data(), sizeof(FrameHost) * nf);
+    ft.nf = nf;
+    k_store_frames<<<1, 32, 0, st>>>(ft, p->frames_host_dev.as<FrameHost>());
+    count_launch();
+  } else {
+    // larger tables through the pinned staging buffer (waits for its previous copy)
+    if ((rc = p->up.reserve(sizeof(FrameHost) * nf)) != SOG_OK) return rc;
+    if ((rc = p->up.wait()) != SOG_OK) return rc;
+    std::memcpy(p->up.p, fh.data(), sizeof(FrameHost) * nf);
+    SOG_CUDA_TRY(cudaMemcpyAsync(p->frames_host_dev.p, p->up.p, sizeof(FrameHost) * nf,
+                                 cudaMemcpyHostToDevice, st));
+    SOG_CUDA_TRY(cudaEventRecord(p->up.done, st));
+    p->up.pending = true;
+  }
   FrameGeom *geom = p->geom.as<FrameGeom>();
   unsigned *status = p->status.as<unsigned>();
   tr->begin(st);
@@ -1792,7 +1824,9 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
     ka.gtab = p->gtab.as<double>();
     ka.gtabF = aliasable ? p->gtabF.as<double>() : nullptr;
     ka.partD = p->partD.as<double>();
-    k_green<T><<<dim3(gblocks, nf, gz), 256, 0, st>>>(ka);
+    k_green<T, true><<<dim3(gblocks, nf, gz), 256, 0, st>>>(ka);
+    k_green<T, false><<<dim3(gblocks, nf, gz), 256, 0, st>>>(ka);
+    count_launch();
     after(tr, st, "green");
     redD = ka.partD + gparts * nf;
     reduce_parts(ka.partD, nf, 1, gparts, 1, 1, redD, redD + nf, st);
@@ -2144,7 +2178,9 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
     ka.gtab = p->gtab.as<double>();
     ka.gtabF = aliasable ? p->gtabF.as<double>() : nullptr;
     ka.partD = p->partD.as<double>();
-    k_green<T><<<dim3(gblocks, 1, gz), 256, 0, st>>>(ka);
+    k_green<T, true><<<dim3(gblocks, 1, gz), 256, 0, st>>>(ka);
+    k_green<T, false><<<dim3(gblocks, 1, gz), 256, 0, st>>>(ka);
+    count_launch();
     after(tr, st, "green");
     reduce_parts(ka.partD, 1, 1, gparts, 1, 1, red + 2 * nch, ka.partD + gparts + 1, st);
     after(tr, st, "reduce_green", reduce_split(gparts) > 1 ? 2 : 1);
