@@ -266,26 +266,44 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
 namespace sogb {
 
 // ---------------------------------------------------------------------------
-// Row maps for the column passes of the slab decomposition.  Row `row` of
-// outer slab `o` lives at
-//   tab[b] + (b * bstride + o * ostride + (row - b * rb)) * inner,  b = row / rb,
-// which covers the plain layout [outer][n][inner] (rb = n, ostride = n), the
-// transposed send blocks written straight into the peers' receive buffers
-// (one base pointer per destination rank) and the received blocks read in
-// place [src][F][zs][ys][inner].
+// Address maps for the column passes of the slab decomposition.  Element x of
+// row `r` of outer slab `o` lives at
+//   tab[b] + b*bstride + (o / osplit)*ohi + (o % osplit)*olo + (r - b*rb)*rstride
+//          + (x / cw)*cstride + x % cw,                             b = r / rb,
+// which covers the plain layout [outer][n][inner] (rb = n, olo = n*inner,
+// rstride = inner, cw = cstride = 1), the transposed blocks stored straight
+// into the peers' receive buffers (one base pointer per destination rank) in
+// the column-chunked layout, and those blocks read back in place.
 // ---------------------------------------------------------------------------
 constexpr int kMaxSlabRanks = 8;
 
 template <typename C>
 struct RowMap {
   C *tab[kMaxSlabRanks];
-  int rb;
-  int64_t ostride, bstride;
-  __device__ __forceinline__ C *row(int64_t o, int r, int64_t inner) const {
+  int rb, osplit, cw;
+  int64_t bstride, ohi, olo, rstride, cstride;
+  __device__ __forceinline__ C *at(int64_t o, int r, int64_t x) const {
     const int b = r / rb;
-    return tab[b] + ((int64_t)b * bstride + o * ostride + (r - b * rb)) * inner;
+    const int64_t oh = o / osplit, xc = x / cw;
+    return tab[b] + b * bstride + oh * ohi + (o - oh * osplit) * olo + (int64_t)(r - b * rb) * rstride +
+           xc * cstride + (x - xc * cw);
   }
 };
+
+template <typename C>
+inline RowMap<C> plain_map(C *base, int n, int64_t inner) {
+  RowMap<C> m{};
+  m.tab[0] = base;
+  m.rb = n;
+  m.osplit = 1 << 30;
+  m.cw = 1;
+  m.bstride = 0;
+  m.ohi = 0;
+  m.olo = (int64_t)n * inner;
+  m.rstride = inner;
+  m.cstride = 1;
+  return m;
+}
 
 // Column FFT (length 2^L) of the tiles [o][*][i0 .. i0+ic) from `in` to
 // `out`, both addressed through row maps.  Same pipeline as k_cols_pipe;
@@ -311,7 +329,7 @@ __global__ void k_cols_map(RowMap<cplx_t<T>> in, RowMap<cplx_t<T>> out, int64_t 
     for (int q = threadIdx.x; q < total; q += blockDim.x) {
       const int r = q / ic, col = q - r * ic;
       const bool ok = i0 + col < inner;
-      const C *src = in.row(o, r, inner) + i0 + col;
+      const C *src = in.at(o, r, i0 + col);
       cp_async_elem(buf + q, ok ? src : in.tab[0], ok);
     }
   };
@@ -334,7 +352,7 @@ __global__ void k_cols_map(RowMap<cplx_t<T>> in, RowMap<cplx_t<T>> out, int64_t 
     const int64_t i0 = (tile - o * nchunks) * ic;
     if (i0 + c < inner) {
 #pragma unroll
-      for (int e = 0; e < kEPT; ++e) out.row(o, t + e * TPT, inner)[i0 + c] = v[e];
+      for (int e = 0; e < kEPT; ++e) *out.at(o, t + e * TPT, i0 + c) = v[e];
     }
     __syncthreads();
   }

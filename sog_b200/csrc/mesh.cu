@@ -487,7 +487,36 @@ struct KsArgs {
   // instead (the receive buffer of rank b, possibly on another GPU)
   int zblk;
   cplx_t<T> *zdst[kMaxSlabRanks];
+  // column layout of the spectrum rows held by this call: 0 = plain
+  // (col = y*nxh + mx); cw > 0 = chunked (col = (xc*nyl + y)*cw + xw,
+  // mx = xc*cw + xw), the receive layout of the peer slab transport in which
+  // one tile of cw columns is contiguous for every z; with cw > 0 the fields
+  // of z block b go to zdst[b] as [nfield][xc*nyl + y][zblk][cw]
+  int cw;
 };
+
+// Column `col` of the spectrum rows -> (mx, local y); false for the pad
+// columns (mx >= nx/2+1) of the chunked layout.
+template <typename T>
+__device__ __forceinline__ bool col_mode(const KsArgs<T> &a, int64_t col, int &mx, int &yl) {
+  if (a.cw == 0) {
+    mx = (int)(col % a.nxh);
+    yl = (int)(col / a.nxh);
+    return true;
+  }
+  const int64_t q = col / a.cw;
+  const int xw = (int)(col - q * a.cw);
+  const int xc = (int)(q / a.nyl);
+  yl = (int)(q - (int64_t)xc * a.nyl);
+  mx = xc * a.cw + xw;
+  return mx < a.nxh;
+}
+
+// columns per z plane of the spectrum rows held by this call
+template <typename T>
+__host__ __device__ __forceinline__ int64_t cols_inner(const KsArgs<T> &a) {
+  return a.cw == 0 ? (int64_t)a.nyl * a.nxh : (int64_t)((a.nxh + a.cw - 1) / a.cw) * a.nyl * a.cw;
+}
 
 // Per-axis Gaussian factors of the frame (the per-axis tables of
 // lmp/sog.cpp:1391-1430): K(k^2) = sum_m amp_m Bx_m By_m Bz_m when k_a
@@ -839,14 +868,20 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
   const FrameGeom &g = a.geom[f];
   const bool sep = g.ortho && a.btab && !g.pad && a.M <= 16;
   if (sep != SEP) return;                 // block-uniform: the frame belongs to the other launch
-  const int64_t inner = (int64_t)a.nyl * a.nxh;
+  const int64_t inner = cols_inner(a);
   const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // (iy, mx) column
   // z planes of this block: the columns are split over gridDim.z
   const int zper = (a.nz + gridDim.z - 1) / gridDim.z;
   const int izb = blockIdx.z * zper, ize = min(a.nz, izb + zper);
   double accD = 0.0;
-  if (col < inner) {
-    const int mx = (int)(col % a.nxh), iy = a.y0 + (int)(col / a.nxh);
+  int mx = 0, yl = 0;
+  const bool valid = col < inner && col_mode(a, col, mx, yl);
+  if (col < inner && !valid) {
+    // pad column of the chunked layout: a zero table entry
+    for (int iz = izb; iz < ize; ++iz) a.gtab[(int64_t)f * a.nh + col + (int64_t)iz * inner] = 0.0;
+  }
+  if (valid) {
+    const int iy = a.y0 + yl;
     const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
     double *gout = a.gtab + (int64_t)f * a.nh + col;
     if constexpr (SEP) {
@@ -917,7 +952,7 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
   C *stg = xbuf + (size_t)padded_row(n) * ic;
   load_stage_twiddles<T, L, 0>(stg, twz);
   const int c = threadIdx.x % ic, t = threadIdx.x / ic;
-  const int64_t inner = (int64_t)a.nyl * a.nxh;
+  const int64_t inner = cols_inner(a);
   const int64_t nchunks = (inner + ic - 1) / ic;
   const int nfield = a.nfield;
   const double inv = 1.0 / ((double)a.nx * a.ny * a.nz);
@@ -936,7 +971,8 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
     const int f = (int)(tile / nchunks);
     const int64_t chunk = tile - (int64_t)f * nchunks;
     const int64_t col = chunk * ic + c;
-    const bool ok = col < inner;
+    int mx = 0, yl = 0;
+    const bool ok = col < inner && col_mode(a, col, mx, yl);
     const FrameGeom &g = a.geom[f];
     // Green values of this thread's modes: loads in flight during the FFT
     double gs[kEPT];
@@ -949,8 +985,7 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) v[e] = cur[(t + e * TPT) * ic + c];
     ct_fft<T, -1, L, true>(v, t, stg, xbuf + c, ic);
-    const int mx = ok ? (int)(col % a.nxh) : 0;
-    const int iy = a.y0 + (ok ? (int)(col / a.nxh) : 0);
+    const int iy = a.y0 + yl;
     const int my = signed_mode(iy, a.ny);
     const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
     double accE = 0.0;
@@ -958,7 +993,7 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
     for (int e = 0; e < kEPT; ++e) {
       const int slot = (t + e * TPT) * ic + c;
       const double rr = (double)v[e].x, ri = (double)v[e].y;
-      accE += w * gs[e] * (rr * rr + ri * ri);
+      if (ok) accE += w * gs[e] * (rr * rr + ri * ri);
       cur[slot] = v[e];             // own slots: no race
       gs[e] *= inv;
     }
@@ -995,9 +1030,15 @@ __global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_
       if (ok) {
 #pragma unroll
         for (int e = 0; e < kEPT; ++e) {
-          const int iz = t + e * TPT, b = iz / a.zblk;
-          C *ob = a.zdst[0] ? a.zdst[b] + (int64_t)fl * zbs + col : out + ((int64_t)b * nfield + fl) * zbs;
-          ob[(int64_t)(iz - b * a.zblk) * inner] = wv[e];
+          const int iz = t + e * TPT, b = iz / a.zblk, zl = iz - b * a.zblk;
+          if (a.cw) {
+            // chunked: this tile's cw columns are contiguous for every z
+            const int64_t q = col / a.cw;
+            a.zdst[b][(int64_t)fl * zbs + (q * a.zblk + zl) * a.cw + (col - q * a.cw)] = wv[e];
+          } else {
+            C *ob = a.zdst[0] ? a.zdst[b] + (int64_t)fl * zbs + col : out + ((int64_t)b * nfield + fl) * zbs;
+            ob[(int64_t)zl * inner] = wv[e];
+          }
         }
       }
     }
@@ -1982,17 +2023,22 @@ void close_peers(sog_plan *p) {
 // largest field count, their IPC handles swapped with ALLGATHER, the peers'
 // buffers opened.  Every rank learns through SUM_F64 whether all ranks
 // succeeded, so a failure returns the same error everywhere.
+// recv_el: complex elements of one spectrum's receive buffer (nz x the
+// chunked columns of this rank's rows).
 template <typename T>
-int peer_setup(sog_plan *p, const sog_slab_desc *sd, unsigned char *ws, const SlabLayout &L, cudaStream_t st,
-               const std::function<int(int, size_t, size_t, size_t)> &exchange) {
-  if (p->peer_rank == sd->rank && p->peer_size == sd->size) return SOG_OK;
+int peer_setup(sog_plan *p, const sog_slab_desc *sd, unsigned char *ws, const SlabLayout &L, int64_t recv_el,
+               cudaStream_t st, const std::function<int(int, size_t, size_t, size_t)> &exchange) {
+  if (p->peer_rank == sd->rank && p->peer_size == sd->size && p->xr_fwd.bytes >= sizeof(cplx_t<T>) * recv_el)
+    return SOG_OK;
   close_peers(p);
   using C = cplx_t<T>;
   const sog_plan_desc &d = p->d;
-  const int64_t share = (int64_t)L.zs * d.ny * p->nxh;
-  if (p->xr_fwd.reserve(sizeof(C) * share) || p->xr_inv.reserve(sizeof(C) * share * 4) ||
+  if (p->xr_fwd.reserve(sizeof(C) * recv_el) || p->xr_inv.reserve(sizeof(C) * recv_el * 4) ||
       p->xr_fe.reserve(sizeof(T) * (int64_t)(L.zs + d.order - 1) * d.ny * d.nx * 4))
     return fail(SOG_ERR_NOMEM, "device allocation failed (slab receive buffers)");
+  // the pad columns of the chunked layout are never written: keep them zero
+  SOG_CUDA_TRY(cudaMemsetAsync(p->xr_fwd.p, 0, p->xr_fwd.bytes, st));
+  SOG_CUDA_TRY(cudaMemsetAsync(p->xr_inv.p, 0, p->xr_inv.bytes, st));
   cudaIpcMemHandle_t own[3];
   SOG_CUDA_TRY(cudaIpcGetMemHandle(&own[0], p->xr_fwd.p));
   SOG_CUDA_TRY(cudaIpcGetMemHandle(&own[1], p->xr_inv.p));
@@ -2089,8 +2135,14 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
     if (r == SOG_OK) after(&p->tr, st, name, 0);
     return r;
   };
+  // spectrum rows of this rank after the transpose: plain [nz][ys][nxh], or
+  // with the peer transport chunked into tiles of W = (fused z tile width)
+  // columns, [nz][nxh/W][ys][W], so that every tile a peer stores is contiguous
+  const int zic = reg_width<T>(nz, 256, 32 * 1024);
+  const int W = peer ? zic : 0;
+  const int64_t inner_loc = peer ? (int64_t)((nxh + W - 1) / W) * ys * W : (int64_t)ys * nxh;
   if (peer) {
-    const int r = peer_setup<T>(p, sd, ws, L, st, exchange);
+    const int r = peer_setup<T>(p, sd, ws, L, (int64_t)nz * inner_loc, st, exchange);
     if (r != SOG_OK) return r;
   }
 
@@ -2102,10 +2154,9 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
   const int64_t nslots = pr.nslots;
   Tracer *tr = &p->tr;
 
-  const int64_t nh_loc = (int64_t)nz * ys * nxh;       // spectrum rows of this rank after the transpose
+  const int64_t nh_loc = (int64_t)nz * inner_loc;      // spectrum rows of this rank after the transpose
   const int64_t spec_loc = (int64_t)zs * ny * nxh;     // spectrum of this rank's planes
-  const int zic = reg_width<T>(nz, 256, 32 * 1024);
-  const int64_t zchunks = ((int64_t)ys * nxh + zic - 1) / zic;
+  const int64_t zchunks = (inner_loc + zic - 1) / zic;
   if (p->rho.reserve(sizeof(T) * (int64_t)zs * ny * nx) || p->spec.reserve(sizeof(C) * spec_loc) ||
       p->partE.reserve(sizeof(double) * 2 * zchunks * nch) ||
       (nfield && p->fspec.reserve(sizeof(C) * spec_loc * nfield)) ||
@@ -2135,9 +2186,10 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
   std::memset(&ka, 0, sizeof(ka));
   ka.spec = peer ? p->xr_fwd.as<C>() : reinterpret_cast<C *>(ws + L.fr);
   ka.fspec = nfield ? (peer ? p->xr_inv.as<C>() : reinterpret_cast<C *>(ws + L.is)) : nullptr;
+  ka.cw = W;
   if (peer && nfield) {
     // block b of the fields goes to rank b's receive buffer, slot of this rank
-    const int64_t blk = (int64_t)nfield * zs * ys * nxh;
+    const int64_t blk = (int64_t)nfield * zs * inner_loc;
     for (int b = 0; b < size; ++b) ka.zdst[b] = static_cast<C *>(p->peer_inv[b]) + (int64_t)rank * blk;
   }
   ka.geom = geom;
@@ -2169,7 +2221,7 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
   double *red = reinterpret_cast<double *>(ws + L.red);   // [nch][2] energy sums, then the self sum
   {
     const bool aliasable = p->d.spline == SOG_SPLINE_BSPLINE;
-    const unsigned gblocks = nblocks((int64_t)ys * nxh, 256);
+    const unsigned gblocks = nblocks(inner_loc, 256);
     const unsigned gz = green_zsplit(gblocks, 1, nz);
     const int64_t gparts = (int64_t)gblocks * gz;
     if (p->gtab.reserve(sizeof(double) * nh_loc) || (aliasable && p->gtabF.reserve(sizeof(double) * nh_loc)) ||
@@ -2232,12 +2284,14 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
     if (peer) {
       // y transform stored straight into every rank's receive buffer:
       // rows [d*ys, (d+1)*ys) of plane z go to rank d at [this rank][z][..]
-      RowMap<C> in{}, out{};
-      in.tab[0] = p->spec.as<C>();
-      in.rb = ny; in.ostride = ny; in.bstride = 0;
-      for (int d = 0; d < size; ++d)
-        out.tab[d] = static_cast<C *>(p->peer_fwd[d]) + (int64_t)rank * zs * ys * nxh;
-      out.rb = ys; out.ostride = ys; out.bstride = 0;
+      const RowMap<C> in = plain_map(p->spec.as<C>(), ny, nxh);
+      RowMap<C> out = plain_map<C>(nullptr, ny, nxh);
+      for (int d = 0; d < size; ++d) out.tab[d] = static_cast<C *>(p->peer_fwd[d]) + (int64_t)rank * zs * inner_loc;
+      out.rb = ys;
+      out.olo = inner_loc;            // plane zl
+      out.rstride = W;                // row yl
+      out.cw = W;
+      out.cstride = (int64_t)ys * W;  // column chunk xc
       pass_cols_map<T, -1>(p, in, out, ny, nxh, zs, p->twy.as<C>(), st, "fft_y_fwd");
       if ((rc = barrier("barrier_fwd")) != SOG_OK) return rc;
     } else {
@@ -2268,11 +2322,18 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
       if (peer) {
         if ((rc = barrier("barrier_inv")) != SOG_OK) return rc;
         // y inverse read in place from the received blocks [src][F][zs][ys][..]
-        RowMap<C> in{}, out{};
+        // received blocks [src][F][xc*ys + yl][zs][W], read in place
+        RowMap<C> in = plain_map<C>(nullptr, ny, nxh);
         for (int s = 0; s < size; ++s) in.tab[s] = p->xr_inv.as<C>();
-        in.rb = ys; in.ostride = ys; in.bstride = (int64_t)nfield * zs * ys;
-        out.tab[0] = p->fspec.as<C>();
-        out.rb = ny; out.ostride = ny; out.bstride = 0;
+        in.rb = ys;
+        in.bstride = (int64_t)nfield * zs * inner_loc;   // source rank
+        in.osplit = zs;
+        in.ohi = (int64_t)zs * inner_loc;                // field
+        in.olo = W;                                      // plane zl
+        in.rstride = (int64_t)zs * W;                    // row yl
+        in.cw = W;
+        in.cstride = (int64_t)ys * zs * W;               // column chunk xc
+        const RowMap<C> out = plain_map(p->fspec.as<C>(), ny, nxh);
         pass_cols_map<T, +1>(p, in, out, ny, nxh, (int64_t)nfield * zs, p->twy.as<C>(), st, "fft_y_inv");
         pass_x_inv<T>(p, p->fspec.as<C>(), fields, 1, (int64_t)zs * ny, nfield, st);
         // first order-1 planes to the halo of rank r-1
