@@ -169,6 +169,18 @@ class ClockSampler:
                 stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        # nvidia-smi's start-up (driver and NVML initialisation) can hold the
+        # driver for a while; wait for its first sample so that it is not
+        # under way inside the timed region
+        t0 = time.time()
+        while time.time() - t0 < 10.0:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.05)
 
     def stop(self):
         if self.proc is None:
@@ -317,13 +329,17 @@ def run_gpu(args, rank: int, world: int):
     time.sleep(0.3)
     l0 = _lib.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     ev0.record(stream)
+    marks[0].record(stream)
     h0 = time.perf_counter()
-    for _ in range(args.steps):
+    for i in range(args.steps):
         out = step_device()
+        marks[i + 1].record(stream)
     host_ms = (time.perf_counter() - h0) * 1e3 / args.steps   # enqueue time per step
     ev1.record(stream)
     torch.cuda.synchronize()
+    step_ms = [marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)]
     launches = _lib.launch_count() - l0
     clk = clocks.stop()
     barrier()
@@ -442,6 +458,7 @@ def run_gpu(args, rank: int, world: int):
         "kernels": kernels,
         "gpu_launches": int(launches),
         "host_enqueue_ms_per_step": host_ms,
+        "step_ms": [round(x, 4) for x in step_ms],
         "clocks": clk,
         "cpu_baseline": cpu,
         "energy_frame0": energy0,

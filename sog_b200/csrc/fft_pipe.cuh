@@ -39,19 +39,23 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // ---------------------------------------------------------------------------
 // columns: data [outer][n][inner] complex, tile = (outer o, columns i0..i0+ic)
 // ---------------------------------------------------------------------------
+// ic is a power of two (the tile widths chosen for power-of-two transforms):
+// element q of the tile is row q >> log2(ic), column q & (ic - 1); a thread's
+// column is fixed and its rows advance by blockDim.x / ic.
 template <typename T>
 __device__ __forceinline__ void cols_issue(cplx_t<T> *buf, const cplx_t<T> *data, int64_t inner, int n,
                                            int ic, int64_t nchunks, int64_t tile) {
   using C = cplx_t<T>;
   const int64_t o = tile / nchunks;
   const int64_t i0 = (tile - o * nchunks) * ic;
-  const C *base = data + o * (int64_t)n * inner + i0;
-  const int total = n * ic;
-  for (int q = threadIdx.x; q < total; q += blockDim.x) {
-    const int row = q / ic, col = q - row * ic;
-    const bool ok = i0 + col < inner;
-    cp_async_elem(buf + q, ok ? base + (int64_t)row * inner + col : data, ok);
-  }
+  const int lic = __ffs(ic) - 1;
+  const int col = threadIdx.x & (ic - 1);
+  const bool ok = i0 + col < inner;
+  const int rstep = blockDim.x >> lic;
+  const C *src = data + o * (int64_t)n * inner + i0 + col + (int64_t)(threadIdx.x >> lic) * inner;
+  const int64_t sstep = (int64_t)rstep * inner;
+  for (int q = threadIdx.x; q < n * ic; q += blockDim.x, src += sstep)
+    cp_async_elem(buf + q, ok ? src : data, ok);
 }
 
 // Shared memory: 2 input tiles (n*ic), the exchange tile (padded if PAD) and
@@ -147,10 +151,12 @@ __global__ void k_r2c_pipe(const T *__restrict__ in, cplx_t<T> *__restrict__ out
       const int m = t + e * TPT;
       v[e] = cmk<C, T>(xr[2 * m], xr[2 * m + 1]);
     }
-    ct_fft<T, -1, L - 1, true, 1>(v, t, stg, zrow, 1);
+    // a row's TPT threads are consecutive lanes of one warp when TPT <= 32
+    constexpr bool kWarpRow = TPT <= 32;
+    ct_fft<T, -1, L - 1, true, 1, kWarpRow>(v, t, stg, zrow, 1);
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) zrow[sidx<true>(t + e * TPT, 1)] = v[e];
-    __syncthreads();
+    xsync<kWarpRow>();
     const int64_t row = tile * rpc + rr;
     if (row < nrows) {
       C *o = out + row * nxh;
@@ -201,17 +207,29 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
   const int f = q % F, rr = q / F;
   auto issue = [&](C *buf, int64_t tile) {
     const int64_t row0 = tile * rpc;
-    // one 64-bit division per tile; rows of the tile step (frame, zy) on
+    // one 64-bit division per tile; a thread's (row, field, column) then
+    // advances by blockDim.x elements without further divisions
     const int64_t frame0 = row0 / nzy, zy0 = row0 - frame0 * nzy;
     const int total = rpc * F * nxh;
-    for (int qq = threadIdx.x; qq < total; qq += blockDim.x) {
-      const int hr = qq / nxh, col = qq - hr * nxh;
-      const int r2 = hr / F, f2 = hr - r2 * F;
-      const bool ok = row0 + r2 < nrows;
-      int64_t frame = frame0, zy = zy0 + r2;
+    int hr = threadIdx.x / nxh, col = threadIdx.x - hr * nxh;
+    int r2 = hr / F, f2 = hr - r2 * F;
+    auto row_src = [&](int rr2, int ff2) -> const C * {
+      int64_t frame = frame0, zy = zy0 + rr2;
       while (zy >= nzy) { zy -= nzy; ++frame; }
-      const C *src = in + ((frame * F + f2) * nzy + zy) * nxh + col;
-      cp_async_elem(buf + qq, ok ? src : in, ok);
+      return in + ((frame * F + ff2) * nzy + zy) * nxh;
+    };
+    const C *rsrc = row_src(r2, f2);
+    for (int qq = threadIdx.x; qq < total; qq += blockDim.x) {
+      const bool ok = row0 + r2 < nrows;
+      cp_async_elem(buf + qq, ok ? rsrc + col : in, ok);
+      col += blockDim.x;
+      if (col >= nxh) {
+        do {
+          col -= nxh;
+          if (++f2 == F) { f2 = 0; ++r2; }
+        } while (col >= nxh);
+        rsrc = row_src(r2, f2);
+      }
     }
   };
   int64_t tile = blockIdx.x;
@@ -243,7 +261,7 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
         v[e] = cmk<C, T>(Ar - ci, Ai + cr);          // A + i conj(w) B
       }
     }
-    ct_fft<T, +1, L - 1, true, 1>(v, t, stg, xbuf + (size_t)(rr * F + f) * hp, 1);
+    ct_fft<T, +1, L - 1, true, 1, (TPT <= 32)>(v, t, stg, xbuf + (size_t)(rr * F + f) * hp, 1);
     // interleaved output straight from registers: the F fields of a row are
     // written by the same CTA, so every sector is completed in L2
     const int64_t row = tile * rpc + rr;

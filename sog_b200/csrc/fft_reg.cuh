@@ -139,8 +139,16 @@ __device__ __forceinline__ void load_stage_twiddles(cplx_t<T> *stg, const cplx_t
   }
 }
 
+// exchange barrier: the whole CTA, or only the warp when every transform
+// lives inside one warp (its TPT threads are consecutive lanes)
+template <bool WSYNC>
+__device__ __forceinline__ void xsync() {
+  if constexpr (WSYNC) __syncwarp();
+  else __syncthreads();
+}
+
 // stg: the stage table of the 2^L transform (load_stage_twiddles).
-template <typename T, int DIR, int L, int S, bool PAD, int TWS>
+template <typename T, int DIR, int L, int S, bool PAD, int TWS, bool WSYNC = false>
 __device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx_t<T> *stg,
                                          cplx_t<T> *sbase, int sj) {
   using PP = Pow2Plan<L>;
@@ -176,19 +184,19 @@ __device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx
     }
   }
   if (!LAST) {
-    __syncthreads();
+    xsync<WSYNC>();
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) v[e] = sbase[sidx<PAD>(t + e * PP::TPT, sj)];
-    __syncthreads();
+    xsync<WSYNC>();
   }
 }
 
-template <typename T, int DIR, int L, bool PAD, int TWS = 0, int S = 0>
+template <typename T, int DIR, int L, bool PAD, int TWS = 0, bool WSYNC = false, int S = 0>
 __device__ __forceinline__ void ct_fft(cplx_t<T> (&v)[kEPT], int t, const cplx_t<T> *stg, cplx_t<T> *sbase,
                                        int sj) {
   if constexpr (S < Pow2Plan<L>::NST) {
-    ct_stage<T, DIR, L, S, PAD, TWS>(v, t, stg, sbase, sj);
-    ct_fft<T, DIR, L, PAD, TWS, S + 1>(v, t, stg, sbase, sj);
+    ct_stage<T, DIR, L, S, PAD, TWS, WSYNC>(v, t, stg, sbase, sj);
+    ct_fft<T, DIR, L, PAD, TWS, WSYNC, S + 1>(v, t, stg, sbase, sj);
   }
 }
 

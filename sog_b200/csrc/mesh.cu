@@ -1441,7 +1441,9 @@ int reg_width(int n, int max_threads, size_t smem_budget) {
   const int tpt = n / kEPT;
   const int by_threads = std::max(1, max_threads / tpt);
   const int by_smem = std::max(1, (int)(smem_budget / ((size_t)n * sizeof(cplx_t<T>))));
-  return std::max(1, std::min(by_threads, by_smem));
+  int w = std::max(1, std::min(by_threads, by_smem));
+  while (w & (w - 1)) w &= w - 1;   // a power of two (the column loads shift and mask)
+  return w;
 }
 
 template <typename T>

@@ -163,10 +163,25 @@ static int timings_of(sogb::Tracer &tr, const char **names, float *ms, int cap, 
   return SOG_OK;
 }
 
+// A pool of events is created when timing is switched on, so that none is
+// created inside the calls being timed.
+static void tracer_reserve(sogb::Tracer &tr, int n) {
+  while ((int)tr.ev.size() < n) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) { cudaGetLastError(); return; }
+    tr.ev.push_back(e);
+    tr.names.push_back(nullptr);
+  }
+}
+
 extern "C" int sog_plan_set_timing(sog_plan *p, int on) {
   if (!p) return sogb::fail(SOG_ERR_INVALID, "null plan");
   p->tr.on = on != 0;
   p->tr.used = 0;
+  if (p->tr.on) {
+    sogb::DeviceGuard dg(p->d.device);
+    tracer_reserve(p->tr, 2048);
+  }
   return SOG_OK;
 }
 
@@ -180,6 +195,10 @@ extern "C" int sog_direct_set_timing(sog_direct *d, int on) {
   if (!d) return sogb::fail(SOG_ERR_INVALID, "null context");
   d->tr.on = on != 0;
   d->tr.used = 0;
+  if (d->tr.on) {
+    sogb::DeviceGuard dg(d->device);
+    tracer_reserve(d->tr, 2048);
+  }
   return SOG_OK;
 }
 
