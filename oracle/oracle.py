@@ -33,6 +33,7 @@ _REF = None
 
 BSPLINE = 0
 QUADS = 1
+CUBES2 = 2
 
 
 def build() -> None:
@@ -51,6 +52,7 @@ def lib():
         _LIB.orc_bspline_sinc_sum.restype = ctypes.c_double
         _LIB.orc_bspline_sinc2p.restype = ctypes.c_double
         _LIB.orc_quads_xi.restype = ctypes.c_double
+        _LIB.orc_cubes2_xi.restype = ctypes.c_double
     return _LIB
 
 
@@ -132,6 +134,22 @@ def quads_weights(order: int, t: float) -> np.ndarray:
     w = np.zeros(order)
     lib().orc_quads_weights(order, ctypes.c_double(t), _ptr(w))
     return w
+
+
+def cubes2_weights(order: int, t) -> np.ndarray:
+    """Node weights of CubeS2 order 4 / 6 at fractional offsets t[3], in the
+    order of ``cubes2_nodes``."""
+    w = np.zeros(216)
+    tt = _f64(np.asarray(t, dtype=np.float64).reshape(3))
+    n = lib().orc_cubes2_weights(order, _ptr(tt), _ptr(w))
+    return w[:n].copy()
+
+
+def cubes2_nodes(order: int) -> np.ndarray:
+    """[n, 3] node offsets of CubeS2 order 4 / 6 (offsets from the floor index)."""
+    d = np.zeros(3 * 216, dtype=np.int32)
+    n = lib().orc_cubes2_nodes(order, d.ctypes.data_as(ctypes.c_void_p), None)
+    return d[:3 * n].reshape(n, 3).copy()
 
 
 def quads_influence_1d(m: int, n: int, order: int) -> float:

@@ -185,6 +185,164 @@ double orc_quads_influence_1d(int m, int n, int order) {
 }
 
 /* sinc(x)^(2p) table value and alias sum (lmp/sog.cpp:68-76, 1113-1176). */
+/* ------------------------------------------------------------------------ */
+/* CubeS2 splines (cubes2_spline.py:16-406; Predescu et al., JCP 153, 224117) */
+/* ------------------------------------------------------------------------ */
+
+/* xi of order 4 / 6: cubes2_spline.py:18-19. */
+double orc_cubes2_xi(int order) {
+  return order == 6 ? 0.6503998764035732 : 1.0 / sqrt(3.0);
+}
+
+/* One assignment node: offset d from the floor grid index, symmetry class,
+ * special (or, for class 3, normal) axis and the sign bits of the special
+ * coordinates (cubes2_spline.py:44-56, 170-228). */
+typedef struct { int d[3], cls, sp, neg; } c2node;
+
+static int c2_is01(int c) { return c == 0 || c == 1; }
+
+/* The node table: order 4, classes {0,1}^3 and one axis at -1 or 2
+ * (cubes2_spline.py:60-97); order 6, the points of [-2,3]^3 within squared
+ * distance 4 of the unit cube, classified by their coordinate pattern
+ * (cubes2_spline.py:170-228).  Returns the number of nodes. */
+int orc_cubes2_nodes(int order, int *d_out, int *cls_out) {
+  int n = 0;
+  const int lo = order == 6 ? -2 : -1, hi = order == 6 ? 3 : 2;
+  for (int dx = lo; dx <= hi; ++dx)
+    for (int dy = lo; dy <= hi; ++dy)
+      for (int dz = lo; dz <= hi; ++dz) {
+        const int c[3] = {dx, dy, dz};
+        double dist = 0.0;
+        int nsp = 0;
+        for (int a = 0; a < 3; ++a) {
+          if (c[a] < 0) dist += (double)c[a] * c[a];
+          if (c[a] > 1) dist += (double)(c[a] - 1) * (c[a] - 1);
+          if (!c2_is01(c[a])) ++nsp;
+        }
+        const int keep = order == 6 ? dist <= 4.0 + 1e-10
+                                    : (nsp == 0 || (nsp == 1 && dist <= 1.0 + 1e-10));
+        if (!keep) continue;
+        if (d_out) { d_out[3 * n] = dx; d_out[3 * n + 1] = dy; d_out[3 * n + 2] = dz; }
+        if (cls_out) cls_out[n] = nsp;
+        ++n;
+      }
+  return n;
+}
+
+static void c2_classify(int order, const int *c, c2node *nd) {
+  nd->d[0] = c[0]; nd->d[1] = c[1]; nd->d[2] = c[2];
+  int sp[3], nsp = 0;
+  for (int a = 0; a < 3; ++a) if (!c2_is01(c[a])) sp[nsp++] = a;
+  nd->sp = -1; nd->neg = 0;
+  if (nsp == 0) { nd->cls = 0; return; }
+  if (nsp == 1) {
+    const int a = sp[0];
+    nd->sp = a;
+    if (c[a] == -1 || c[a] == 2) { nd->cls = 1; nd->neg = c[a] == -1; }
+    else { nd->cls = 2; nd->neg = c[a] == -2; }
+    (void)order;
+    return;
+  }
+  if (nsp == 2) {   /* class 3: sp holds the normal axis, bits the sorted special axes */
+    nd->cls = 3;
+    for (int a = 0; a < 3; ++a) if (a != sp[0] && a != sp[1]) nd->sp = a;
+    for (int i = 0; i < 2; ++i) if (c[sp[i]] == -1) nd->neg |= 1 << i;
+    return;
+  }
+  nd->cls = 4;
+  for (int a = 0; a < 3; ++a) if (c[a] == -1) nd->neg |= 1 << a;
+}
+
+/* Eq. 15 / 16 of the paper (cubes2_spline.py:99-110) */
+static double c2_L4(double t, double xi) {
+  const double x2 = xi * xi;
+  return -0.5 * t * t * t + 0.5 * t * t - (9.0 * x2 - 2.0) / 6.0 * t + 0.5 * x2;
+}
+static double c2_R(double t, double xi) {
+  return t * t * t / 6.0 + (3.0 * xi * xi - 1.0) / 6.0 * t;
+}
+/* order-6 pieces (cubes2_spline.py:126-166) */
+static double c2_L111(double t, double xi) {
+  const double x2 = xi * xi, x4 = x2 * x2;
+  const double t2 = t * t, t3 = t2 * t;
+  return t3 * t2 / 12.0 - t2 * t2 / 6.0 + (10.0 * x2 - 1.0) / 12.0 * t3 - (6.0 * x2 - 1.0) / 6.0 * t2 +
+         (5.0 * x4 - x2) / 4.0 * t - (3.0 * x4 - x2) / 6.0;
+}
+static double c2_L311(double t, double xi) {
+  const double x2 = xi * xi, x4 = x2 * x2;
+  const double t3 = t * t * t;
+  return t3 * t * t / 120.0 + (2.0 * x2 - 1.0) / 24.0 * t3 + (15.0 * x4 - 15.0 * x2 + 4.0) / 120.0 * t;
+}
+static double c2_L211(double t, double xi) { return -0.25 * c2_L111(t, xi) - 2.5 * c2_L311(t, xi); }
+static double c2_S6(double t, double xi) {
+  const double x2 = xi * xi;
+  return -0.5 * t * t * t + 0.5 * t * t - (3.0 * x2 - 2.0) / 2.0 * t + 0.5 * x2;
+}
+
+/* eta of a coordinate at a node offset in {0,1}: t at offset 1, 1 - t at 0 */
+static double c2_eta01(double t, int d) { return d == 1 ? t : 1.0 - t; }
+
+/* Weight of one node at fractional offsets t[3] in [0,1)
+ * (cubes2_weight_4 / cubes2_weight_6, cubes2_spline.py:231-380). */
+static double c2_weight(int order, const double *t, const c2node *nd, double xi) {
+  const int *d = nd->d;
+  if (order == 4) {
+    if (nd->cls == 0) {
+      const double ex = c2_eta01(t[0], d[0]), ey = c2_eta01(t[1], d[1]), ez = c2_eta01(t[2], d[2]);
+      return c2_L4(ex, xi) * ey * ez + c2_L4(ey, xi) * ez * ex + c2_L4(ez, xi) * ex * ey;
+    }
+    const int s = nd->sp;
+    const double es = nd->neg ? 1.0 - t[s] : t[s];
+    double prod = 1.0;
+    for (int a = 0; a < 3; ++a) if (a != s) prod *= c2_eta01(t[a], d[a]);
+    return c2_R(es, xi) * prod;
+  }
+  switch (nd->cls) {
+    case 0: {
+      const double ex = c2_eta01(t[0], d[0]), ey = c2_eta01(t[1], d[1]), ez = c2_eta01(t[2], d[2]);
+      return c2_L111(ex, xi) * ey * ez + c2_L111(ey, xi) * ez * ex + c2_L111(ez, xi) * ex * ey +
+             c2_S6(ex, xi) * c2_S6(ey, xi) * c2_S6(ez, xi);
+    }
+    case 1: case 2: {
+      const int s = nd->sp;
+      const double es = nd->neg ? 1.0 - t[s] : t[s];
+      double en[2];
+      int k = 0;
+      for (int a = 0; a < 3; ++a) if (a != s) en[k++] = c2_eta01(t[a], d[a]);
+      if (nd->cls == 2) return c2_L311(es, xi) * en[0] * en[1];
+      return c2_L211(es, xi) * en[0] * en[1] + c2_R(es, xi) * c2_S6(en[0], xi) * c2_S6(en[1], xi);
+    }
+    case 3: {
+      const int nrm = nd->sp;
+      int sa[2], k = 0;
+      for (int a = 0; a < 3; ++a) if (a != nrm) sa[k++] = a;
+      const double en = c2_eta01(t[nrm], d[nrm]);
+      const double e1 = (nd->neg & 1) ? 1.0 - t[sa[0]] : t[sa[0]];
+      const double e2 = (nd->neg & 2) ? 1.0 - t[sa[1]] : t[sa[1]];
+      return c2_S6(en, xi) * c2_R(e1, xi) * c2_R(e2, xi);
+    }
+    default: {
+      const double ex = (nd->neg & 1) ? 1.0 - t[0] : t[0];
+      const double ey = (nd->neg & 2) ? 1.0 - t[1] : t[1];
+      const double ez = (nd->neg & 4) ? 1.0 - t[2] : t[2];
+      return c2_R(ex, xi) * c2_R(ey, xi) * c2_R(ez, xi);
+    }
+  }
+}
+
+/* Weights of all nodes at fractional offsets t (w[node] in table order). */
+int orc_cubes2_weights(int order, const double *t, double *w) {
+  int d[3 * 216], cls[216];
+  const int n = orc_cubes2_nodes(order, d, cls);
+  const double xi = orc_cubes2_xi(order);
+  for (int i = 0; i < n; ++i) {
+    c2node nd;
+    c2_classify(order, d + 3 * i, &nd);
+    w[i] = c2_weight(order, t, &nd, xi);
+  }
+  return n;
+}
+
 static double orc_sinc(double x) {
   if (fabs(x) < 1e-14) return 1.0;
   return sin(x) / x;
@@ -340,7 +498,7 @@ void orc_irfftn_unnorm(double *spec_ri, double *out, int nx, int ny, int nz) {
 /* mesh solve                                                                */
 /* ------------------------------------------------------------------------ */
 
-enum { ORC_BSPLINE = 0, ORC_QUADS = 1 };
+enum { ORC_BSPLINE = 0, ORC_QUADS = 1, ORC_CUBES2 = 2 };
 
 typedef struct {
   int spline, order, nx, ny, nz, alias_extent;
@@ -399,6 +557,23 @@ static void atom_stencil(int spline, int order, const double *ci, const double *
   }
 }
 
+/* CubeS2 stencil of one atom: floor grid index per axis (no offset) and the
+ * node weights (cubes2_fft.py:408-470). */
+static int c2_stencil(int order, const double *ci, const double *r, int nx, int ny, int nz,
+                      int *i0, double *w) {
+  const int n3[3] = {nx, ny, nz};
+  double t[3];
+  for (int a = 0; a < 3; ++a) {
+    double f = r[0] * ci[0 * 3 + a] + r[1] * ci[1 * 3 + a] + r[2] * ci[2 * 3 + a];
+    f = f - floor(f);
+    const double fx = f * (double)n3[a];
+    const double fl = floor(fx);
+    t[a] = fx - fl;
+    i0[a] = (int)fl % n3[a];
+  }
+  return orc_cubes2_weights(order, t, w);
+}
+
 /* Green-function factors at one half-spectrum mode.
  * kv: k vector of the principal mode; returns kfac (bare kernel K(k^2)),
  * gE (energy green), gF (force green), gS (self green), gV (virial green),
@@ -412,6 +587,7 @@ typedef struct {
   double bound[3];    /* |a_alpha| * kmax / 2pi: alias pruning */
   double *dx, *dy, *dz;   /* separable deconvolution per axis */
   double *sx, *sy, *sz;   /* B-spline alias sums per axis */
+  double sig2[3];         /* CubeS2: (xi |a_alpha| / n_alpha)^2 */
 } green_ctx;
 
 /* Mode m -> Cartesian k.  kconv 0: k = 2pi cell^-1 m, the reciprocal vector
@@ -444,6 +620,17 @@ static int green_at(const green_ctx *g, int mx, int my, int mz, int iy, int iz,
     Kv += g->amp[m] * g->bw2[m] * e;
   }
   *kfac = K; *kfacv = Kv;
+  if (g->spline == ORC_CUBES2) {
+    /* variance subtraction, G = K exp(sum_a sigma_a^2 k_a^2) over the
+     * Cartesian components (cubes2_fft.py:1039-1049) */
+    const double D = exp(g->sig2[0] * k[0] * k[0] + g->sig2[1] * k[1] * k[1] + g->sig2[2] * k[2] * k[2]);
+    *gE = K * D; *gF = K * D; *gS = K; *gV = Kv * D;
+    if (emD) for (int m = 0; m < g->M; ++m) {
+      const double e = exp(-0.5 * g->bw2[m] * ksq);
+      emD[m] = e * D; emS[m] = e;
+    }
+    return 1;
+  }
   if (g->spline == ORC_QUADS) {
     double infl = g->dx[mx] * g->dy[iy] * g->dz[iz];
     if (infl < 1e-20) infl = 1e-20;           /* quads_fft.py:194 clamp */
@@ -516,6 +703,16 @@ static void setup_green(green_ctx *g, const orc_mesh_in *in, const double *ci) {
   g->amp = in->amp; g->bw2 = in->bw2; g->k_sq_max = in->k_sq_max;
   g->kconv = in->kconv;
   memcpy(g->ci, ci, sizeof(double) * 9);
+  {
+    const int n3[3] = {in->nx, in->ny, in->nz};
+    const double xi = orc_cubes2_xi(in->order);
+    for (int a = 0; a < 3; ++a) {
+      const double la = sqrt(in->cell[3 * a] * in->cell[3 * a] + in->cell[3 * a + 1] * in->cell[3 * a + 1] +
+                             in->cell[3 * a + 2] * in->cell[3 * a + 2]);
+      const double s = xi * la / n3[a];
+      g->sig2[a] = s * s;
+    }
+  }
   const double kmax = sqrt(in->k_sq_max);
   /* |m_a| <= |v_a| kmax / 2pi with v_a the lattice row (kconv 0) or the
    * column of the cell (kconv 1): bounds the aliases inside the sphere. */
@@ -567,7 +764,21 @@ int orc_mesh_solve(const orc_mesh_in *in, orc_mesh_out *out) {
 
   /* ---- spread (serial, input order, as lmp/sog.cpp:1977-2018) ---- */
   double *rho = calloc(ng, sizeof(double));
-  for (int i = 0; i < in->natoms; ++i) {
+  int c2d[3 * 216];
+  if (in->spline == ORC_CUBES2) orc_cubes2_nodes(p, c2d, NULL);
+  for (int i = 0; i < in->natoms && in->spline == ORC_CUBES2; ++i) {
+    int i0[3];
+    double w[216];
+    const int nn = c2_stencil(p, ci, in->r + 3 * i, nx, ny, nz, i0, w);
+    const double qs = rho_scale * in->q[i];
+    for (int k = 0; k < nn; ++k) {
+      const int gx = ((i0[0] + c2d[3 * k]) % nx + nx) % nx;
+      const int gy = ((i0[1] + c2d[3 * k + 1]) % ny + ny) % ny;
+      const int gz = ((i0[2] + c2d[3 * k + 2]) % nz + nz) % nz;
+      rho[((long)gz * ny + gy) * nx + gx] += qs * w[k];
+    }
+  }
+  for (int i = 0; i < in->natoms && in->spline != ORC_CUBES2; ++i) {
     int i0[3];
     double wx[8], wy[8], wz[8];
     atom_stencil(in->spline, p, ci, in->r + 3 * i, nx, ny, nz, i0, wx, wy, wz);
@@ -701,8 +912,19 @@ int orc_mesh_solve(const orc_mesh_in *in, orc_mesh_out *out) {
     for (int i = 0; i < in->natoms; ++i) {
       int i0[3];
       double wx[8], wy[8], wz[8];
-      atom_stencil(in->spline, p, ci, in->r + 3 * i, nx, ny, nz, i0, wx, wy, wz);
       double accf[4] = {0, 0, 0, 0};
+      if (in->spline == ORC_CUBES2) {
+        double w[216];
+        const int nn = c2_stencil(p, ci, in->r + 3 * i, nx, ny, nz, i0, w);
+        for (int k = 0; k < nn; ++k) {
+          const int gx = ((i0[0] + c2d[3 * k]) % nx + nx) % nx;
+          const int gy = ((i0[1] + c2d[3 * k + 1]) % ny + ny) % ny;
+          const int gz = ((i0[2] + c2d[3 * k + 2]) % nz + nz) % nz;
+          const long idx = ((long)gz * ny + gy) * nx + gx;
+          for (int f = 0; f < nfield; ++f) accf[f] += w[k] * grids[f * ng + idx];
+        }
+      } else {
+      atom_stencil(in->spline, p, ci, in->r + 3 * i, nx, ny, nz, i0, wx, wy, wz);
       for (int c = 0; c < p; ++c) {
         const int gz = (i0[2] + c) % nz;
         for (int b = 0; b < p; ++b) {
@@ -714,6 +936,7 @@ int orc_mesh_solve(const orc_mesh_in *in, orc_mesh_out *out) {
             for (int f = 0; f < nfield; ++f) accf[f] += w * grids[f * ng + idx];
           }
         }
+      }
       }
       if (in->want_force)
         for (int a = 0; a < 3; ++a)

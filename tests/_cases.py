@@ -9,6 +9,8 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 
 MESH_CASES = ["quads4_cubic", "quads6_cubic", "quads4_triclinic", "quads6_triclinic",
               "quads6_2frames_2ch", "quads4_2frames_keepself", "cfg2_quads6"]
+CUBES2_CASES = ["cubes2_4_cubic", "cubes2_4_triclinic", "cubes2_6_cubic", "cubes2_6_triclinic",
+                "cubes2_4_2frames_2ch"]
 DIRECT_CASES = ["cfg1_direct", "direct_triclinic_2ch_rsi1", "direct_triclinic_2ch_rsi0",
                 "direct_mixed_batch", "direct_rcut", "direct_internal"]
 

@@ -6,7 +6,8 @@ $SOG_REFERENCE); the fixtures are committed so the GPU box never needs it:
     python tests/golden/make_golden.py
 
 Every case stores its inputs and the reference's outputs (fp64).  Sources:
-  * QuadS mesh path: ``Gaussian(use_quads_fft=True)`` with
+  * QuadS and CubeS2 mesh paths: ``Gaussian(use_quads_fft=True)`` /
+    ``Gaussian(use_cubes2_fft=True)`` with
     ``_enable_batched_direct=False`` (the switch the reference's own
     test_batched_mixed.py uses), ``compute_bundle(compute_force=True,
     compute_virial=True)`` -> explicit ik forces and virial
@@ -58,13 +59,15 @@ def params_log(m, lo, hi):
 
 
 def run_mesh_case(name, r, q, cell, batch, amp_raw, bw_raw, order, n_dl,
-                  remove_self=True, lam=None, autograd=True):
-    """QuadS through the reference compute_bundle, explicit E/F/virial, plus
-    autograd dE/dq, dE/damp, dE/dbw2 of the energy-only path."""
+                  remove_self=True, lam=None, autograd=True, family="quads"):
+    """QuadS (or CubeS2) through the reference compute_bundle, explicit
+    E/F/virial, plus autograd dE/dq, dE/damp, dE/dbw2 of the energy-only path."""
     def make():
+        spline = (dict(use_quads_fft=True, quads_order=order) if family == "quads"
+                  else dict(use_cubes2_fft=True, cubes2_order=order))
         g = Gaussian(n_dl=n_dl, amp=amp_raw.clone(), bandwidth=bw_raw.clone(),
-                     use_quads_fft=True, quads_order=order, trainable=True,
-                     remove_self_interaction=remove_self, charge_neutral_lambda=lam)
+                     trainable=True, remove_self_interaction=remove_self,
+                     charge_neutral_lambda=lam, **spline)
         g._enable_batched_direct = False
         return g
     g = make()
@@ -249,6 +252,44 @@ def main():
     print("host_logic written")
 
 
+def cubes2_cases():
+    """CubeS2 mesh path (cubes2_fft.py:925-1133 explicit E/F/virial, and
+    Cubes2FFTFunction.backward, cubes2_fft.py:747-869, for dE/dq and
+    dE/d(amp, bw2)); its own generator, so the other fixtures stay as they are."""
+    gen = torch.Generator().manual_seed(2025)
+    amp3, bw3 = params_log(3, 1.5, 4.0)
+    for order in (4, 6):
+        n = 40
+        cell = torch.eye(3, dtype=F64) * 12.0
+        r = torch.rand(n, 3, generator=gen, dtype=F64) * 12.0
+        q = torch.rand(n, generator=gen, dtype=F64) - 0.5
+        q = q - q.mean()
+        run_mesh_case(f"cubes2_{order}_cubic", r, q, cell.unsqueeze(0),
+                      torch.zeros(n, dtype=torch.int64), amp3, bw3, order, 0.7, family="cubes2")
+        cell = triclinic(12.0, 12.6, 13.5, 80.0, 95.0, 105.0)
+        s = torch.rand(n, 3, generator=gen, dtype=F64)
+        r = s @ cell
+        q = torch.randn(n, generator=gen, dtype=F64) * 0.5
+        q = q - q.mean()
+        run_mesh_case(f"cubes2_{order}_triclinic", r, q, cell.unsqueeze(0),
+                      torch.zeros(n, dtype=torch.int64), amp3, bw3, order, 0.7, family="cubes2")
+    # two frames, two channels (one non-neutral: k=0 term) and the penalty
+    cells = torch.stack([triclinic(9.0, 8.8, 9.4, 85.0, 92.0, 98.0),
+                         torch.eye(3, dtype=F64) * 10.0])
+    na, nb = 30, 22
+    ra = torch.rand(na, 3, generator=gen, dtype=F64) @ cells[0]
+    rb = torch.rand(nb, 3, generator=gen, dtype=F64) * 10.0
+    q = torch.rand(na + nb, 2, generator=gen, dtype=F64) - 0.5
+    q[:, 0] -= q[:, 0].mean()
+    batch = torch.cat([torch.zeros(na, dtype=torch.int64), torch.ones(nb, dtype=torch.int64)])
+    run_mesh_case("cubes2_4_2frames_2ch", torch.cat([ra, rb]), q, cells, batch, amp3, bw3, 4, 0.6,
+                  lam=0.3, family="cubes2")
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    main()
+    if sys.argv[1:] == ["cubes2"]:
+        cubes2_cases()
+    else:
+        main()
+        cubes2_cases()

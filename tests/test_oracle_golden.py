@@ -4,19 +4,25 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from tests._cases import DIRECT_CASES, MESH_CASES, direct_n_dl, direct_nk, grid_ndl, load
+from tests._cases import (CUBES2_CASES, DIRECT_CASES, MESH_CASES, direct_n_dl, direct_nk,
+                          grid_ndl, load)
 
 
-@pytest.mark.parametrize("name", MESH_CASES)
-def test_oracle_quads_matches_reference(name):
+def _mesh_case_vs_oracle(name, spline):
     c = load(name)
     cells = c["cell"].reshape(-1, 3, 3)
     grids, ksm = zip(*[grid_ndl(cl, float(c["n_dl"])) for cl in cells])
     lam = None if c["lam"] < 0 else float(c["lam"])
     res = O.bundle(c["r"], c["q"], cells, c["batch"], c["amp"], c["bw2"], solver="mesh",
-                   grids=grids, k_sq_max=ksm, spline=O.QUADS, order=int(c["order"]),
+                   grids=grids, k_sq_max=ksm, spline=spline, order=int(c["order"]),
                    remove_self=bool(c["remove_self"]), charge_neutral_lambda=lam,
                    want_virial=True, kconv=1)
+    return c, res
+
+
+@pytest.mark.parametrize("name", MESH_CASES + CUBES2_CASES)
+def test_oracle_mesh_matches_reference(name):
+    c, res = _mesh_case_vs_oracle(name, O.CUBES2 if name.startswith("cubes2") else O.QUADS)
     e_ref = c["energy"]
     assert np.allclose(res["energy"], e_ref, rtol=1e-12, atol=1e-13 * np.abs(e_ref).max())
     assert np.abs(res["forces"] - c["forces"]).max() < 1e-11
@@ -71,6 +77,21 @@ def test_bspline_weights_match_reference_header(order):
         ref.ref_bspline_weights(order, ctypes.c_double(t), wr.ctypes.data_as(ctypes.POINTER(ctypes.c_double)))
         assert np.array_equal(w, wr)
         assert abs(w.sum() - 1.0) < 1e-14
+
+
+@pytest.mark.parametrize("order", [4, 6])
+def test_cubes2_node_table_and_moments(order):
+    """32 / 88 nodes (cubes2_spline.py:33-38); the weights reproduce
+    polynomials through degree order-1 exactly (the moment conditions
+    checked by the reference's verify_order6 / test_cubes2_order6.py)."""
+    d = O.cubes2_nodes(order)
+    assert len(d) == {4: 32, 6: 88}[order]
+    rng = np.random.default_rng(order)
+    for t in rng.random((20, 3)):
+        w = O.cubes2_weights(order, t)
+        assert abs(w.sum() - 1.0) < 1e-13
+        # first moments: sum_k w_k (d_k - t) = 0 per axis
+        assert np.abs((w[:, None] * (d - t[None, :])).sum(0)).max() < 1e-13
 
 
 @pytest.mark.parametrize("order", [4, 6])
