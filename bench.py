@@ -17,6 +17,7 @@ With N > 1 ranks (torchrun) every rank solves its own independent system
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -330,6 +331,8 @@ def run_gpu(args, rank: int, world: int):
     l0 = _lib.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    gc.collect()
+    gc.disable()          # no collector pause inside the timed steps
     ev0.record(stream)
     marks[0].record(stream)
     h0 = time.perf_counter()
@@ -339,6 +342,7 @@ def run_gpu(args, rank: int, world: int):
     host_ms = (time.perf_counter() - h0) * 1e3 / args.steps   # enqueue time per step
     ev1.record(stream)
     torch.cuda.synchronize()
+    gc.enable()
     step_ms = [marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)]
     launches = _lib.launch_count() - l0
     clk = clocks.stop()

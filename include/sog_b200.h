@@ -46,6 +46,7 @@ extern "C" {
 
 #define SOG_SPLINE_BSPLINE 0 /* cardinal B-spline, order 4/5/6 (lmp/sog.cpp:89-110) */
 #define SOG_SPLINE_QUADS 1   /* separable QuadS, order 4/6 (quads_spline.py)       */
+#define SOG_SPLINE_CUBES2 2  /* CubeS2, order 4/6 (cubes2_spline.py, cubes2_fft.py) */
 
 /* Mode -> wave vector.  PHYSICAL: k = 2*pi * cell^-1 * m, the reciprocal
  * vector for cells whose rows are lattice vectors (what the reference's direct
@@ -75,8 +76,8 @@ typedef struct sog_plan sog_plan;
 
 typedef struct sog_plan_desc {
   int dtype;        /* SOG_DTYPE_F64 | SOG_DTYPE_F32                         */
-  int spline;       /* SOG_SPLINE_BSPLINE | SOG_SPLINE_QUADS                 */
-  int order;        /* 4,5,6 (B-spline) or 4,6 (QuadS)                       */
+  int spline;       /* SOG_SPLINE_BSPLINE | SOG_SPLINE_QUADS | SOG_SPLINE_CUBES2 */
+  int order;        /* 4,5,6 (B-spline) or 4,6 (QuadS, CubeS2)               */
   int nx, ny, nz;   /* mesh; layout [nz][ny][nx], x fastest (quads_fft.py:66) */
   int device;       /* CUDA device ordinal                                   */
   int alias_extent; /* B-spline alias half-width; 0 -> 8 (lmp/sog.cpp:339)   */

@@ -20,7 +20,7 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libsog_b200.so")
 
 SOG_OK = 0
 DTYPE_F64, DTYPE_F32 = 0, 1
-SPLINE_BSPLINE, SPLINE_QUADS = 0, 1
+SPLINE_BSPLINE, SPLINE_QUADS, SPLINE_CUBES2 = 0, 1, 2
 KCONV_PHYSICAL, KCONV_REFERENCE = 0, 1
 
 _c_i64p = ctypes.POINTER(ctypes.c_int64)

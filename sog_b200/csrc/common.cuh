@@ -48,6 +48,7 @@ struct FrameGeom {
   int32_t pad;        // 1: B-spline aliases may fall inside the k_max sphere
   int32_t ortho;      // 1: kmat diagonal (k_a depends on m_a only)
   int32_t pad2;
+  double sig2[3];     // CubeS2: (xi |a_alpha| / n_alpha)^2 of the Green factor, else 0
 };
 
 // Per-frame host-side description uploaded with each call.

@@ -19,10 +19,12 @@ __device__ __forceinline__ double warp_sum(double v) {
 // ------------------------------------------------------------------------
 // frame set-up
 // ------------------------------------------------------------------------
+// c2xi > 0: CubeS2 with that xi (its Green factor exp(sum_a sig2_a k_a^2)
+// uses sig_a = xi |a_alpha| / n_alpha, cubes2_fft.py:1039-1045; no aliasing).
 template <typename T>
 __global__ void k_frame_setup(const T *__restrict__ cells, const FrameHost *__restrict__ fh,
                               FrameGeom *__restrict__ geom, int nf, int kconv, int nx, int ny,
-                              int nz, unsigned *status) {
+                              int nz, unsigned *status, double c2xi = 0.0) {
   const int f = blockIdx.x * blockDim.x + threadIdx.x;
   if (f >= nf) return;
   FrameGeom g;
@@ -87,6 +89,15 @@ __global__ void k_frame_setup(const T *__restrict__ cells, const FrameHost *__re
   g.ortho = (g.kmat[1] == 0.0 && g.kmat[2] == 0.0 && g.kmat[3] == 0.0 && g.kmat[5] == 0.0 &&
              g.kmat[6] == 0.0 && g.kmat[7] == 0.0) ? 1 : 0;
   g.pad2 = 0;
+  {
+    const int n3[3] = {nx, ny, nz};
+    for (int a = 0; a < 3; ++a) {
+      const double la = sqrt(c[3 * a] * c[3 * a] + c[3 * a + 1] * c[3 * a + 1] + c[3 * a + 2] * c[3 * a + 2]);
+      const double s = c2xi * la / (double)n3[a];
+      g.sig2[a] = s * s;
+    }
+    if (c2xi > 0.0) g.pad = 0;
+  }
   geom[f] = g;
 }
 

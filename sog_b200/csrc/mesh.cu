@@ -166,6 +166,106 @@ __device__ __forceinline__ void spline_w(int spline, T t, T *w, const QuadsCoef 
   }
 }
 
+// CubeS2 (cubes2_spline.py): every node weight is a sum of products of 1-D
+// polynomials of the three offsets, and summing the classes node by node
+// gives a sum of separable stencils over the P = order window
+// (offsets 1 - P/2 .. P/2):
+//   order 4:  W = A_x e_y e_z + e_x A_y e_z + e_x e_y A_z
+//   order 6:  W = A_x e_y e_z + e_x A_y e_z + e_x e_y A_z + B_x B_y B_z
+// with, per axis and offset d (eta = t at d = 1, 2, 3 and 1 - t at d = 0,
+// -1, -2):  e = eta on {0,1};  A = L (order 4) / L111 (order 6) on {0,1},
+// R (order 4) / L211 (order 6) on {-1,2}, L311 on {-2,3};  B = S on {0,1},
+// R on {-1,2}.  The node tables and class formulas this reproduces are
+// cubes2_spline.py:60-97, 170-228 (nodes) and 231-380 (weights).
+constexpr double kCubeS2Xi4 = 0.57735026918962576451;   // 1/sqrt(3), cubes2_spline.py:18
+constexpr double kCubeS2Xi6 = 0.6503998764035732;       // cubes2_spline.py:19
+
+__host__ __device__ constexpr double cubes2_xi(int order) { return order == 6 ? kCubeS2Xi6 : kCubeS2Xi4; }
+
+// kinds[k][j] for offset d = j + 1 - P/2: kind 0 = e, 1 = A, 2 = B (kinds has
+// three rows; B is zero for order 4)
+template <typename T, int P>
+__device__ __forceinline__ void cubes2_axis(T t, T (*kinds)[P]) {
+  constexpr double xi = cubes2_xi(P);
+  const T x2 = (T)(xi * xi), x4 = x2 * x2;
+  auto L4 = [&](T u) { return -T(0.5) * u * u * u + T(0.5) * u * u - (T(9) * x2 - T(2)) / T(6) * u + T(0.5) * x2; };
+  auto R = [&](T u) { return u * u * u / T(6) + (T(3) * x2 - T(1)) / T(6) * u; };
+  auto L111 = [&](T u) {
+    const T u2 = u * u, u3 = u2 * u;
+    return u3 * u2 / T(12) - u2 * u2 / T(6) + (T(10) * x2 - T(1)) / T(12) * u3 - (T(6) * x2 - T(1)) / T(6) * u2 +
+           (T(5) * x4 - x2) / T(4) * u - (T(3) * x4 - x2) / T(6);
+  };
+  auto L311 = [&](T u) {
+    const T u3 = u * u * u;
+    return u3 * u * u / T(120) + (T(2) * x2 - T(1)) / T(24) * u3 + (T(15) * x4 - T(15) * x2 + T(4)) / T(120) * u;
+  };
+  auto S6 = [&](T u) { return -T(0.5) * u * u * u + T(0.5) * u * u - (T(3) * x2 - T(2)) / T(2) * u + T(0.5) * x2; };
+  constexpr int first = 1 - P / 2;
+#pragma unroll
+  for (int j = 0; j < P; ++j) {
+    const int d = j + first;
+    T e = T(0), A = T(0), B = T(0);
+    if (d == 0 || d == 1) {
+      const T eta = d == 1 ? t : T(1) - t;
+      e = eta;
+      A = P == 4 ? L4(eta) : L111(eta);
+      B = P == 4 ? T(0) : S6(eta);
+    } else if (d == -1 || d == 2) {
+      const T eta = d == 2 ? t : T(1) - t;
+      A = P == 4 ? R(eta) : (-T(0.25) * L111(eta) - T(2.5) * L311(eta));
+      B = P == 4 ? T(0) : R(eta);
+    } else {
+      const T eta = d == 3 ? t : T(1) - t;
+      A = L311(eta);
+    }
+    kinds[0][j] = e;
+    kinds[1][j] = A;
+    kinds[2][j] = B;
+  }
+}
+
+// Term tables of the stencils: term i is kind TX[i] along x times TY[i]
+// along y times TZ[i] along z (NT = 1: the separable splines, one kind).
+template <int NT>
+struct StencilTerms;
+template <>
+struct StencilTerms<1> {
+  static constexpr int K = 1;
+  __device__ static constexpr int x(int) { return 0; }
+  __device__ static constexpr int y(int) { return 0; }
+  __device__ static constexpr int z(int) { return 0; }
+};
+template <>
+struct StencilTerms<3> {
+  static constexpr int K = 2;
+  __device__ static constexpr int x(int i) { return i == 0 ? 1 : 0; }
+  __device__ static constexpr int y(int i) { return i == 1 ? 1 : 0; }
+  __device__ static constexpr int z(int i) { return i == 2 ? 1 : 0; }
+};
+template <>
+struct StencilTerms<4> {
+  static constexpr int K = 3;
+  __device__ static constexpr int x(int i) { return i == 3 ? 2 : (i == 0 ? 1 : 0); }
+  __device__ static constexpr int y(int i) { return i == 3 ? 2 : (i == 1 ? 1 : 0); }
+  __device__ static constexpr int z(int i) { return i == 3 ? 2 : (i == 2 ? 1 : 0); }
+};
+
+// Per-axis kinds of one coordinate: the spline weights (NT = 1) or the
+// CubeS2 kinds.
+template <typename T, int P, int NT>
+__device__ __forceinline__ void axis_kinds(int spline, T t, T (*kinds)[P], const QuadsCoef &qc) {
+  if constexpr (NT == 1) {
+    spline_w<T, P>(spline, t, kinds[0], qc);
+  } else {
+    T tmp[3][P];
+    cubes2_axis<T, P>(t, tmp);
+#pragma unroll
+    for (int k = 0; k < StencilTerms<NT>::K; ++k)
+#pragma unroll
+      for (int j = 0; j < P; ++j) kinds[k][j] = tmp[k][j];
+  }
+}
+
 // ------------------------------------------------------------------------
 // spread: output-stationary tiles, deterministic, no global atomics
 // ------------------------------------------------------------------------
@@ -220,19 +320,24 @@ __device__ int axis_bins(int lo, int len, int n, int nb, int *out) {
 // from warp match ranks and a warp-ordered prefix, so the summation order at
 // every mesh point is fixed (bucket, then candidate order) and the result is
 // bitwise reproducible.
-template <typename T, int P>
-__global__ void __launch_bounds__(kSpreadThreads, 3) k_spread(SpreadArgs<T> a) {
-  constexpr int CH = kSpreadThreads;
+// NT stencil terms (StencilTerms): 1 for the separable splines, 3 / 4 for
+// CubeS2 order 4 / 6.  CH candidates per chunk (fewer with three kinds, to
+// keep the staged weights at two CTAs per SM).
+template <typename T, int P, int NT = 1>
+__global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? 3 : 2) k_spread(SpreadArgs<T> a) {
+  using ST = StencilTerms<NT>;
+  constexpr int KK = ST::K;
+  constexpr int CH = KK == 3 ? kSpreadThreads / 2 : kSpreadThreads;
   constexpr int NW = kSpreadThreads / 32;
   constexpr int NK = kTileX + P - 1;       // x-anchor buckets of a tile
   static_assert(NK <= 64, "bucket scan covers two keys per lane");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // candidate arrays, component-major so that lanes reading neighbouring
   // buckets hit different banks
-  T *c_wz = reinterpret_cast<T *>(smem_raw);            // [kTileZ][CH]
-  T *c_wx = c_wz + CH * kTileZ;                         // [P][CH]
-  T *c_wy = c_wx + CH * P;                              // [P][CH]
-  T *c_q = c_wy + CH * P;                               // [CH]
+  T *c_wz = reinterpret_cast<T *>(smem_raw);            // [KK][kTileZ][CH]
+  T *c_wx = c_wz + KK * CH * kTileZ;                    // [KK][P][CH]
+  T *c_wy = c_wx + KK * CH * P;                         // [KK][P][CH]
+  T *c_q = c_wy + KK * CH * P;                          // [CH]
   int *c_ay = reinterpret_cast<int *>(c_q + CH);        // [CH]
   __shared__ uint32_t seg_lo[kMaxSeg], seg_pre[kMaxSeg + 1];
   __shared__ int nseg_s;
@@ -331,7 +436,7 @@ __global__ void __launch_bounds__(kSpreadThreads, 3) k_spread(SpreadArgs<T> a) {
     int4 an = make_int4(0, 0, 0, 0);
     int key = 0;
     T tf[3] = {T(0), T(0), T(0)}, qv = T(0);
-    if (ci < ncand) {
+    if (threadIdx.x < CH && ci < ncand) {
       int lo = 0, hi = nseg - 1;
       while (lo < hi) {  // last segment with seg_pre <= ci
         const int mid = (lo + hi + 1) >> 1;
@@ -396,25 +501,32 @@ __global__ void __launch_bounds__(kSpreadThreads, 3) k_spread(SpreadArgs<T> a) {
     __syncthreads();
     if (rel) {
       const int slot = kcnt[warp][key] + rank;
-      T w1[P];
-      spline_w<T, P>(a.spline, tf[0], w1, a.qc);
+      T w1[KK][P];
+      axis_kinds<T, P, NT>(a.spline, tf[0], w1, a.qc);
 #pragma unroll
-      for (int k = 0; k < P; ++k) c_wx[k * CH + slot] = w1[k];
-      spline_w<T, P>(a.spline, tf[1], w1, a.qc);
+      for (int kk = 0; kk < KK; ++kk)
 #pragma unroll
-      for (int k = 0; k < P; ++k) c_wy[k * CH + slot] = w1[k];
-      spline_w<T, P>(a.spline, tf[2], w1, a.qc);
+        for (int k = 0; k < P; ++k) c_wx[(kk * P + k) * CH + slot] = w1[kk][k];
+      axis_kinds<T, P, NT>(a.spline, tf[1], w1, a.qc);
+#pragma unroll
+      for (int kk = 0; kk < KK; ++kk)
+#pragma unroll
+        for (int k = 0; k < P; ++k) c_wy[(kk * P + k) * CH + slot] = w1[kk][k];
+      axis_kinds<T, P, NT>(a.spline, tf[2], w1, a.qc);
       const int dz0 = imod(z0 - an.z, ag.nz);
 #pragma unroll
       for (int z = 0; z < kTileZ; ++z) {
-        T wz = T(0);
-        if (z < tzv) {
-          int d = dz0 + z;
-          if (d >= ag.nz) d -= ag.nz;
+        int d = dz0 + z;
+        if (d >= ag.nz) d -= ag.nz;
 #pragma unroll
-          for (int k = 0; k < P; ++k) wz = (d == k) ? w1[k] : wz;
+        for (int kk = 0; kk < KK; ++kk) {
+          T wz = T(0);
+          if (z < tzv) {
+#pragma unroll
+            for (int k = 0; k < P; ++k) wz = (d == k) ? w1[kk][k] : wz;
+          }
+          c_wz[(kk * kTileZ + z) * CH + slot] = wz;
         }
-        c_wz[z * CH + slot] = wz;
       }
       c_q[slot] = qv * scale;
       c_ay[slot] = an.y;
@@ -433,9 +545,14 @@ __global__ void __launch_bounds__(kSpreadThreads, 3) k_spread(SpreadArgs<T> a) {
           int dy = gy - c_ay[j];
           if (dy < 0) dy += ag.ny;
           if (dy >= P) continue;
-          const T wxy = c_wx[dx * CH + j] * c_wy[dy * CH + j] * c_q[j];
+          const T qj = c_q[j];
 #pragma unroll
-          for (int z = 0; z < kTileZ; ++z) acc[z] += wxy * c_wz[z * CH + j];
+          for (int tt = 0; tt < NT; ++tt) {
+            const T wxy = c_wx[(ST::x(tt) * P + dx) * CH + j] * c_wy[(ST::y(tt) * P + dy) * CH + j] * qj;
+            const T *wz = c_wz + ST::z(tt) * kTileZ * CH + j;
+#pragma unroll
+            for (int z = 0; z < kTileZ; ++z) acc[z] += wxy * wz[z * CH];
+          }
         }
       }
     }
@@ -654,6 +771,20 @@ __device__ ModeGreen mode_green(const KsArgs<T> &a, const FrameGeom &g, const do
   } else {
     r.K = kernel_sum<T>(amp, bw2, a.M, r.ksq, &r.Kv);
   }
+  if (a.spline == SOG_SPLINE_CUBES2) {
+    // variance subtraction: G = K exp(sum_a sig_a^2 k_a^2) over the Cartesian
+    // components (cubes2_fft.py:1039-1049); no aliasing, no deconvolution
+    const double D = exp(g.sig2[0] * r.k[0] * r.k[0] + g.sig2[1] * r.k[1] * r.k[1] + g.sig2[2] * r.k[2] * r.k[2]);
+    r.gE = r.gF = r.K * D;
+    r.gS = r.K;
+    r.gV = r.Kv * D;
+    if (emD) {
+      const double e = exp(-0.5 * bw2[mfor] * r.ksq);
+      *emD = e * D;
+      *emS = e;
+    }
+    return r;
+  }
   if (a.spline == SOG_SPLINE_QUADS) {
     double infl = a.tx[mx] * a.ty[iy] * a.tz[iz];
     if (infl < 1e-20) infl = 1e-20;  // quads_fft.py:194
@@ -866,7 +997,7 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
   __syncthreads();
   const int f = blockIdx.y;
   const FrameGeom &g = a.geom[f];
-  const bool sep = g.ortho && a.btab && !g.pad && a.M <= 16;
+  const bool sep = g.ortho && a.btab && !g.pad && a.M <= 16 && a.spline != SOG_SPLINE_CUBES2;
   if (sep != SEP) return;                 // block-uniform: the frame belongs to the other launch
   const int64_t inner = cols_inner(a);
   const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // (iy, mx) column
@@ -1188,8 +1319,11 @@ struct GatherArgs {
   const uint32_t *range_lo, *range_hi;
 };
 
-template <typename T, int P>
+// NT stencil terms as in k_spread (the weight of node (k, b, c) is
+// sum_t X_t[k] Y_t[b] Z_t[c]).
+template <typename T, int P, int NT = 1>
 __global__ void __launch_bounds__(256) k_gather(GatherArgs<T> a) {
+  using ST = StencilTerms<NT>;
   const int64_t si = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (si >= a.nslots) return;
   int64_t s = a.slot_lo + si;
@@ -1198,10 +1332,10 @@ __global__ void __launch_bounds__(256) k_gather(GatherArgs<T> a) {
     if (s >= (int64_t)*a.range_hi) return;
   }
   const int4 an = a.s_anchor[s];
-  T wx[P], wy[P], wz[P];
-  spline_w<T, P>(a.spline, a.s_t[s * 3 + 0], wx, a.qc);
-  spline_w<T, P>(a.spline, a.s_t[s * 3 + 1], wy, a.qc);
-  spline_w<T, P>(a.spline, a.s_t[s * 3 + 2], wz, a.qc);
+  T wx[ST::K][P], wy[ST::K][P], wz[ST::K][P];
+  axis_kinds<T, P, NT>(a.spline, a.s_t[s * 3 + 0], wx, a.qc);
+  axis_kinds<T, P, NT>(a.spline, a.s_t[s * 3 + 1], wy, a.qc);
+  axis_kinds<T, P, NT>(a.spline, a.s_t[s * 3 + 2], wz, a.qc);
   const AtomGrid &ag = a.ag;
   int ix[P];
 #pragma unroll
@@ -1218,10 +1352,14 @@ __global__ void __launch_bounds__(256) k_gather(GatherArgs<T> a) {
       int gy = an.y + b;
       if (gy >= ag.ny) gy -= ag.ny;
       const int64_t row = ((int64_t)gz * ag.ny + gy) * ag.nx;
-      const T wzy = wy[b] * wz[c];
+      T wzy[NT];
+#pragma unroll
+      for (int tt = 0; tt < NT; ++tt) wzy[tt] = wy[ST::y(tt)][b] * wz[ST::z(tt)][c];
 #pragma unroll
       for (int k = 0; k < P; ++k) {
-        const T wv = wx[k] * wzy;
+        T wv = T(0);
+#pragma unroll
+        for (int tt = 0; tt < NT; ++tt) wv += wx[ST::x(tt)][k] * wzy[tt];
         const T *pt = base + (row + ix[k]) * F;
         if (F == 3) {
           acc[0] += wv * pt[0]; acc[1] += wv * pt[1]; acc[2] += wv * pt[2];
@@ -1575,18 +1713,19 @@ void set_fft_smem_attrs() {
   allow_smem(k_zfused<T>, big);
 }
 
-template <typename T, int P>
+template <typename T, int P, int NT = 1>
 size_t spread_smem() {
-  constexpr int CH = kSpreadThreads;
-  return (size_t)CH * (kTileZ + 2 * P + 1) * sizeof(T) + (size_t)CH * sizeof(int);
+  constexpr int KK = StencilTerms<NT>::K;
+  constexpr int CH = KK == 3 ? kSpreadThreads / 2 : kSpreadThreads;
+  return (size_t)CH * (KK * (kTileZ + 2 * P) + 1) * sizeof(T) + (size_t)CH * sizeof(int);
 }
 
-template <typename T, int P>
+template <typename T, int P, int NT = 1>
 void launch_spread(const SpreadArgs<T> &sa, int nframes, cudaStream_t st, Tracer *tr) {
-  const size_t sm = spread_smem<T, P>();
-  allow_smem(k_spread<T, P>, (int)sm);
+  const size_t sm = spread_smem<T, P, NT>();
+  allow_smem(k_spread<T, P, NT>, (int)sm);
   const int64_t tiles = (int64_t)sa.ntx * sa.nty * sa.ntz * nframes;
-  k_spread<T, P><<<(unsigned)tiles, kSpreadThreads, sm, st>>>(sa);
+  k_spread<T, P, NT><<<(unsigned)tiles, kSpreadThreads, sm, st>>>(sa);
   after(tr, st, "spread");
 }
 
@@ -1602,6 +1741,11 @@ inline unsigned green_zsplit(unsigned gblocks, int nf, int nz) {
 
 template <typename T>
 void dispatch_spread(const SpreadArgs<T> &sa, int order, int nframes, cudaStream_t st, Tracer *tr) {
+  if (sa.spline == SOG_SPLINE_CUBES2) {
+    if (order == 4) launch_spread<T, 4, 3>(sa, nframes, st, tr);
+    else launch_spread<T, 6, 4>(sa, nframes, st, tr);
+    return;
+  }
   switch (order) {
     case 4: launch_spread<T, 4>(sa, nframes, st, tr); break;
     case 5: launch_spread<T, 5>(sa, nframes, st, tr); break;
@@ -1613,6 +1757,12 @@ template <typename T>
 void dispatch_gather(const GatherArgs<T> &ga, int order, cudaStream_t st, Tracer *tr) {
   const unsigned nb = nblocks(ga.nslots, 256);
   if (nb == 0) return;
+  if (ga.spline == SOG_SPLINE_CUBES2) {
+    if (order == 4) k_gather<T, 4, 3><<<nb, 256, 0, st>>>(ga);
+    else k_gather<T, 6, 4><<<nb, 256, 0, st>>>(ga);
+    after(tr, st, "gather");
+    return;
+  }
   switch (order) {
     case 4: k_gather<T, 4><<<nb, 256, 0, st>>>(ga); break;
     case 5: k_gather<T, 5><<<nb, 256, 0, st>>>(ga); break;
@@ -1674,13 +1824,16 @@ int prepare_atoms(sog_plan *p, const sog_mesh_args *a, cudaStream_t st, Prep &pr
   unsigned *status = p->status.as<unsigned>();
   tr->begin(st);
   k_frame_setup<T><<<nblocks(nf, 128), 128, 0, st>>>((const T *)a->cells, p->frames_host_dev.as<FrameHost>(),
-                                                     geom, nf, p->d.kconv, nx, ny, nz, status);
+                                                     geom, nf, p->d.kconv, nx, ny, nz, status,
+                                                     p->d.spline == SOG_SPLINE_CUBES2 ? cubes2_xi(P) : 0.0);
   after(tr, st, "frame_setup");
 
   // ---- atom sort ----
   AtomGrid ag;
   ag.nx = nx; ag.ny = ny; ag.nz = nz;
-  ag.first = (p->d.spline == SOG_SPLINE_QUADS) ? (1 - P / 2) : -((P - 1) / 2);
+  // first stencil node: floor index + 1 - P/2 for QuadS (quads_fft.py) and
+  // CubeS2 (offsets -1..2 / -2..3, cubes2_spline.py), - (P-1)/2 for B-splines
+  ag.first = (p->d.spline == SOG_SPLINE_BSPLINE) ? -((P - 1) / 2) : (1 - P / 2);
   ag.nbx = p->nb_x; ag.nby = p->nb_y; ag.nbz = p->nb_z;
   ag.bins_per_frame = (uint32_t)ag.nbx * ag.nby * ag.nbz;
   const uint64_t nbins64 = (uint64_t)ag.bins_per_frame * nf;
@@ -2414,8 +2567,10 @@ extern "C" int sog_plan_create(sog_plan **out, const sog_plan_desc *desc) {
     if (d.order < 4 || d.order > 6) return fail(SOG_ERR_INVALID, "B-spline order must be 4, 5 or 6");
   } else if (d.spline == SOG_SPLINE_QUADS) {
     if (d.order != 4 && d.order != 6) return fail(SOG_ERR_INVALID, "QuadS order must be 4 or 6");
+  } else if (d.spline == SOG_SPLINE_CUBES2) {
+    if (d.order != 4 && d.order != 6) return fail(SOG_ERR_INVALID, "CubeS2 order must be 4 or 6");
   } else {
-    return fail(SOG_ERR_UNSUPPORTED, "spline family not supported (CubeS2 is not built)");
+    return fail(SOG_ERR_INVALID, "unknown spline family");
   }
   if (d.nx < 8 || d.ny < 8 || d.nz < 8) return fail(SOG_ERR_INVALID, "mesh dims must be >= 8");
   if (!smooth235(d.nx) || !smooth235(d.ny) || !smooth235(d.nz))

@@ -9,7 +9,9 @@ Solvers:
   * direct k-sum (the reference default; gaussian.py:1180-1337),
   * particle-mesh with cardinal B-splines (``use_bspline_fft=True``,
     ``bspline_order`` 4/5/6; the plugin's B-spline mesh, lmp/sog.cpp),
-  * particle-mesh with QuadS (``use_quads_fft=True``, quads_fft.py:209-326).
+  * particle-mesh with QuadS (``use_quads_fft=True``, quads_fft.py:209-326),
+  * particle-mesh with CubeS2 (``use_cubes2_fft=True``, ``cubes2_order`` 4/6;
+    cubes2_fft.py:925-1133, Cubes2FFTFunction.backward :747-869).
 Added keys (defaults keep the reference behaviour): ``use_bspline_fft``,
 ``bspline_order``, ``mesh_k_convention`` ("physical" | "reference"),
 ``mesh_alias_extent``, and ``mesh_decomposition`` ("none" | "slab") with
@@ -282,8 +284,10 @@ class Gaussian(nn.Module):
 
     def _mesh_kind(self):
         if self.use_cubes2_fft:
-            raise NotImplementedError("the CubeS2 mesh (use_cubes2_fft) is not built in sog_b200; "
-                                      "use use_bspline_fft or use_quads_fft")
+            if self.cubes2_order not in (4, 6):
+                # the reference raises from _get_xi (cubes2_spline.py:22-28)
+                raise ValueError(f"Unsupported CubeS₂ order: {self.cubes2_order}. Supported: 4, 6.")
+            return _lib.SPLINE_CUBES2, self.cubes2_order
         if self.use_bspline_fft:
             return _lib.SPLINE_BSPLINE, self.bspline_order
         if self.use_quads_fft:
@@ -342,7 +346,7 @@ class Gaussian(nn.Module):
                 nx, ny, nz, ksm = resolve_grid(
                     lx, ly, lz, n_dl=self.n_dl if self.cubes2_phi_max is None else None,
                     cubes2_phi_max=self.cubes2_phi_max, r_c=self.rcut, b=self.b,
-                    spline_order=order if spline == _lib.SPLINE_QUADS else (4 if order < 6 else 6),
+                    spline_order=order if spline != _lib.SPLINE_BSPLINE else (4 if order < 6 else 6),
                     min_grid=8)
                 bk = groups.setdefault((nx, ny, nz), Bucket([], [], [], [], dims=(nx, ny, nz)))
                 bk.frames.append(j)

@@ -11,7 +11,7 @@ import torch
 
 from oracle import oracle as O
 from sog_b200 import Gaussian, Sog
-from tests._cases import DIRECT_CASES, MESH_CASES, direct_n_dl, grid_ndl, load
+from tests._cases import CUBES2_CASES, DIRECT_CASES, MESH_CASES, direct_n_dl, grid_ndl, load
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -29,17 +29,19 @@ def _rel(a, b):
 
 
 # --------------------------------------------------------------------------
-# QuadS mesh vs the reference itself (mesh_k_convention="reference")
+# QuadS and CubeS2 meshes vs the reference itself (mesh_k_convention="reference")
 # --------------------------------------------------------------------------
-@pytest.mark.parametrize("name", MESH_CASES)
+@pytest.mark.parametrize("name", MESH_CASES + CUBES2_CASES)
 def test_quads_matches_reference(name):
     c = load(name)
     lam = None if c["lam"] < 0 else float(c["lam"])
+    spline = (dict(use_cubes2_fft=True, cubes2_order=int(c["order"])) if name.startswith("cubes2")
+              else dict(use_quads_fft=True, quads_order=int(c["order"])))
     def make():
         return Gaussian(n_dl=float(c["n_dl"]), amp=torch.tensor(c["amp"]), bandwidth=torch.tensor(c["bw2"]),
-                        kernel_param_mode="internal", use_quads_fft=True, quads_order=int(c["order"]),
+                        kernel_param_mode="internal",
                         remove_self_interaction=bool(c["remove_self"]), charge_neutral_lambda=lam,
-                        mesh_k_convention="reference", trainable=True).to(DEV)
+                        mesh_k_convention="reference", trainable=True, **spline).to(DEV)
     g = make()
     out = g.compute_bundle(q=_t(c["q"]), r=_t(c["r"]), cell=_t(c["cell"]), batch=_t(c["batch"], torch.long),
                            compute_force=True, compute_virial=True)
@@ -233,3 +235,28 @@ def test_status_word_flags_nonfinite_positions():
     plan = next(iter(_lib.PLANS.plans.values()))
     bits = [p.status() for p in _lib.PLANS.plans.values()]
     assert any(b & 1 for b in bits)
+
+
+# --------------------------------------------------------------------------
+# CubeS2 in the physical wave-vector convention vs the oracle
+# --------------------------------------------------------------------------
+@pytest.mark.parametrize("order", [4, 6])
+def test_cubes2_physical_convention_matches_oracle_triclinic(order):
+    rng = np.random.default_rng(40 + order)
+    cell = np.array([[13.0, 0.0, 0.0], [1.1, 12.4, 0.0], [-0.9, 0.7, 12.8]])
+    n = 300
+    r = rng.random((n, 3)) @ cell
+    q = rng.normal(size=n)
+    q -= q.mean()
+    bw = np.geomspace(1.0, 6.0, 5)
+    amp = 1.0 / (bw * np.sqrt(2 * np.pi))
+    g = Gaussian(n_dl=0.8, amp=torch.tensor(amp), bandwidth=torch.tensor(bw), use_cubes2_fft=True,
+                 cubes2_order=order, trainable=False).to(DEV)
+    out = g.compute_bundle(q=_t(q), r=_t(r), cell=_t(cell[None]), compute_force=True, compute_virial=True)
+    grid, ksm = grid_ndl(cell, 0.8)
+    ref = O.bundle(r, q, cell[None], np.zeros(n, dtype=np.int64), g.amp.detach().cpu().numpy(),
+                   g.bandwidth.detach().cpu().numpy(), solver="mesh", grids=[grid], k_sq_max=[ksm],
+                   spline=O.CUBES2, order=order, want_virial=True, kconv=0)
+    assert _rel(out["energy"].cpu().numpy(), ref["energy"]) < E_TOL
+    assert np.abs(out["forces"].cpu().numpy() - ref["forces"]).max() < F_TOL
+    assert _rel(out["virial"].cpu().numpy(), ref["virial"]) < E_TOL

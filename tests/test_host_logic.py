@@ -162,7 +162,8 @@ def test_abi_rejects_bad_plan_descs_without_gpu():
         _lib.PlanDesc(5, 0, 6, 64, 64, 64, 0, 8, 0),     # dtype
         _lib.PlanDesc(0, 0, 7, 64, 64, 64, 0, 8, 0),     # B-spline order
         _lib.PlanDesc(0, 1, 5, 64, 64, 64, 0, 8, 0),     # QuadS order
-        _lib.PlanDesc(0, 2, 4, 64, 64, 64, 0, 8, 0),     # spline family
+        _lib.PlanDesc(0, 2, 5, 64, 64, 64, 0, 8, 0),     # CubeS2 order
+        _lib.PlanDesc(0, 3, 4, 64, 64, 64, 0, 8, 0),     # spline family
         _lib.PlanDesc(0, 0, 6, 7, 64, 64, 0, 8, 0),      # too small
         _lib.PlanDesc(0, 0, 6, 64, 66, 64, 0, 8, 0),     # 66 = 2*3*11 not smooth
         _lib.PlanDesc(0, 0, 6, 64, 64, 64, 0, 8, 9),     # k convention
