@@ -229,6 +229,37 @@ typedef struct sog_direct_args {
 SOG_API int sog_direct_forward(sog_direct *d, const sog_direct_args *args, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* Real-space pair sum (non-periodic frames)                                 */
+/* ------------------------------------------------------------------------ */
+
+typedef struct sog_realspace_args {
+  int nframes;
+  const int64_t *atom_begin; /* host [nframes]                                 */
+  const int64_t *atom_count; /* host [nframes]                                 */
+  int nchannels;             /* 1..8                                           */
+  const void *positions;     /* device [N,3]                                   */
+  const void *charges;       /* device [N,C]                                   */
+  int n_gauss;
+  const void *amp, *bw2;     /* device [M] internal amplitudes, bandwidth^2    */
+  double norm_factor;
+  int remove_self;           /* 0: add 1/2 sum |q|^2 sum amp                   */
+  double charge_neutral_lambda; /* <= 0: no penalty                            */
+  void *energy;              /* [nframes]                                      */
+  void *forces, *potential;  /* [N,3], [N,C] (dE/dq), or NULL                  */
+  void *grad_amp, *grad_bw2; /* [nframes,M], or NULL                           */
+  void *virial;              /* [nframes,3,3] written as zeros, or NULL        */
+} sog_realspace_args;
+
+/* E_f = norm (1/2 sum_{i != j} (q_i . q_j) sum_m amp_m exp(-r_ij^2 / (2 bw2_m))
+ *             + [!remove_self] 1/2 sum_i |q_i|^2 sum_m amp_m) + lambda sum_c mean_c(q)^2
+ * over each frame's atoms, with explicit forces, dE/dq and dE/d(amp, bw2).
+ * Replaces compute_potential_realspace (gaussian.py:822-845), the path the
+ * reference's compute_bundle takes for cell=None and singular cells
+ * (gaussian.py:735-746), whose derivatives it takes by autograd.  Runs on a
+ * direct-solver context (its scratch and timing); dtype as the context's. */
+SOG_API int sog_realspace_forward(sog_direct *d, const sog_realspace_args *args, void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* Direct k-sum without allocation (no counterpart in the reference)         */
 /* ------------------------------------------------------------------------ */
 

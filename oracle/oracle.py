@@ -53,6 +53,11 @@ def lib():
         _LIB.orc_bspline_sinc2p.restype = ctypes.c_double
         _LIB.orc_quads_xi.restype = ctypes.c_double
         _LIB.orc_cubes2_xi.restype = ctypes.c_double
+        _LIB.orc_realspace_solve.restype = ctypes.c_double
+        _LIB.orc_realspace_solve.argtypes = [
+            ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_double, ctypes.c_int, ctypes.c_void_p,
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     return _LIB
 
 
@@ -224,6 +229,43 @@ def direct_solve(r, q, cell, amp, bw2, *, nk: Sequence[int], k_sq_max: float,
             "forces": f, "potential": p, "grad_amp": ga, "grad_bw2": gb}
 
 
+def realspace_solve(r, q, amp, bw2, *, norm_factor: float = 14.3996454784255,
+                    remove_self: bool = True) -> Dict[str, np.ndarray]:
+    """Real-space pair sum of one non-periodic frame over all channels
+    (compute_potential_realspace, gaussian.py:822-845), explicit derivatives.
+    q is [n] or [n, C]; the energy includes the self term when remove_self is
+    False and excludes the neutrality penalty."""
+    r = np.ascontiguousarray(_f64(r).reshape(-1, 3))
+    q = _f64(q)
+    if q.ndim == 1:
+        q = q[:, None]
+    q = np.ascontiguousarray(q)
+    amp = np.ascontiguousarray(_f64(amp).reshape(-1))
+    bw2 = np.ascontiguousarray(_f64(bw2).reshape(-1))
+    n, C = q.shape
+    M = amp.shape[0]
+    f, p, ga, gb = np.zeros((n, 3)), np.zeros((n, C)), np.zeros(M), np.zeros(M)
+    e = lib().orc_realspace_solve(n, C, _ptr(r), _ptr(q), M, _ptr(amp), _ptr(bw2),
+                                  float(norm_factor), int(remove_self), _ptr(f), _ptr(p),
+                                  _ptr(ga), _ptr(gb))
+    return {"energy": float(e), "forces": f, "potential": p, "grad_amp": ga, "grad_bw2": gb}
+
+
+def penalty(q_frame: np.ndarray, charge_neutral_lambda: Optional[float]):
+    """Charge-neutral penalty lambda * sum_c mean_c(q)^2 of one frame
+    (gaussian.py:795-798): (energy, dE/dq [n, C])."""
+    q_frame = _f64(q_frame)
+    if q_frame.ndim == 1:
+        q_frame = q_frame[:, None]
+    if charge_neutral_lambda is None or not charge_neutral_lambda > 0:
+        return 0.0, np.zeros_like(q_frame)
+    mean = q_frame.mean(axis=0)
+    e = float(charge_neutral_lambda) * float((mean ** 2).sum())
+    dq = np.broadcast_to(float(charge_neutral_lambda) * 2.0 * mean[None, :] / q_frame.shape[0],
+                         q_frame.shape).copy()
+    return e, dq
+
+
 def k0_correction(q_frame: np.ndarray, cell, amp, bw2, *, norm_factor: float,
                   remove_self: bool, charge_neutral_lambda: Optional[float] = None):
     """k=0 charge / self correction and the optional neutrality penalty of one
@@ -253,11 +295,8 @@ def k0_correction(q_frame: np.ndarray, cell, amp, bw2, *, norm_factor: float,
         c_amp -= qq / (2.0 * vol) * norm_factor
     ga = em * c_amp
     gb = amp * em * (-0.5 * kmin2) * c_amp
-    if charge_neutral_lambda is not None and charge_neutral_lambda > 0:
-        mean = q_frame.mean(axis=0)
-        e += float(charge_neutral_lambda) * float((mean ** 2).sum())
-        dq += float(charge_neutral_lambda) * 2.0 * mean[None, :] / q_frame.shape[0]
-    return e, dq, ga, gb
+    e_p, dq_p = penalty(q_frame, charge_neutral_lambda)
+    return e + e_p, dq + dq_p, ga, gb
 
 
 def bundle(r, q, cell, batch, amp, bw2, *, solver: str, grids=None, nks=None,
@@ -267,15 +306,20 @@ def bundle(r, q, cell, batch, amp, bw2, *, solver: str, grids=None, nks=None,
            want_virial: bool = False, alias_extent: int = 8, kconv: int = 0):
     """Reference-equivalent per-frame energies and explicit derivatives for a
     batch (compute_bundle, gaussian.py:380-820), solver "mesh" or "direct".
-    grids[f] = (nx, ny, nz); nks[f] = (n1, n2, n3); k_sq_max[f] per frame."""
+    grids[f] = (nx, ny, nz); nks[f] = (n1, n2, n3); k_sq_max[f] per frame.
+    Frames without a cell (cell=None) or with a singular cell take the
+    real-space pair sum (gaussian.py:735-746) and no k=0 term."""
     r = _f64(r).reshape(-1, 3)
     q = _f64(q)
     if q.ndim == 1:
         q = q[:, None]
-    cell = _f64(cell).reshape(-1, 3, 3)
     batch = np.asarray(batch, dtype=np.int64).reshape(-1)
     amp = _f64(amp)
     bw2 = _f64(bw2)
+    if cell is None:
+        nf = int(batch.max()) + 1 if batch.size else 0
+        cell = np.zeros((nf, 3, 3))
+    cell = _f64(cell).reshape(-1, 3, 3)
     nf = cell.shape[0]
     n, C = q.shape
     M = amp.shape[0]
@@ -288,6 +332,16 @@ def bundle(r, q, cell, batch, amp, bw2, *, solver: str, grids=None, nks=None,
     for f in range(nf):
         idx = np.nonzero(batch == f)[0]
         if idx.size == 0:
+            continue
+        if not abs(np.linalg.det(cell[f])) > np.finfo(np.float64).eps:
+            res = realspace_solve(r[idx], q[idx], amp, bw2, norm_factor=norm_factor,
+                                  remove_self=remove_self)
+            e_p, dq_p = penalty(q[idx], charge_neutral_lambda)
+            energy[f] = res["energy"] + e_p
+            forces[idx] = res["forces"]
+            pot[idx] = res["potential"] + dq_p
+            gamp[f] = res["grad_amp"]
+            gbw2[f] = res["grad_bw2"]
             continue
         for c in range(C):
             if solver == "mesh":

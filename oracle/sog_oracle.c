@@ -19,11 +19,13 @@
  *   - backward (dq, amp, bw2) src/sog/module/cubes2_fft.py:746-869
  *   - virial               src/sog/module/cubes2_fft.py:874-921
  *   - direct k-sum         src/sog/module/gaussian.py:1281-1337
+ *   - real-space pair sum  src/sog/module/gaussian.py:822-845 (frames with
+ *                          cell=None or a singular cell, gaussian.py:735-746)
  *   - mode convention      quads_fft.py:246-258 (Nyquist at +N/2)
  *   - irfftn semantics     torch.fft.irfftn: C2C over z,y then C2R along x
  *                          using Re() of the mx=0 / mx=nx/2 columns
  *
- * Parity status: QuadS and direct paths are pinned against fixtures made by
+ * Parity status: QuadS, CubeS2, direct and real-space paths are pinned against fixtures made by
  * importing the reference (tests/golden/make_golden.py); the B-spline weights
  * are pinned against the reference's own compiled sog_spline.h
  * (oracle/_ref).  The B-spline Green function has no executable reference
@@ -1059,4 +1061,82 @@ int orc_num_threads(void) {
 #else
   return 1;
 #endif
+}
+
+/* ------------------------------------------------------------------------ */
+/* real-space pair sum (non-periodic frames)                                */
+/* ------------------------------------------------------------------------ */
+
+/* One non-periodic frame, all channels (compute_potential_realspace,
+ * src/sog/module/gaussian.py:822-845):
+ *   E = norm * ( 1/2 sum_{i != j} (q_i . q_j) sum_m amp_m exp(-r_ij^2 / (2 bw2_m))
+ *                + [!remove_self] 1/2 sum_i |q_i|^2 sum_m amp_m )
+ * q is [n, C] row-major.  Explicit derivatives (the reference takes them by
+ * autograd): forces [n,3], dE/dq [n,C], dE/damp [M], dE/dbw2 [M]; any output
+ * pointer may be NULL.  Returns the energy. */
+double orc_realspace_solve(int n, int C, const double *r, const double *q, int M, const double *amp,
+                           const double *bw2, double norm_factor, int remove_self, double *forces,
+                           double *potential, double *grad_amp, double *grad_bw2) {
+  double e_pair = 0.0;
+  double *ga = calloc((size_t)M, sizeof(double)), *gb = calloc((size_t)M, sizeof(double));
+#pragma omp parallel
+  {
+    double *ga_t = calloc((size_t)M, sizeof(double)), *gb_t = calloc((size_t)M, sizeof(double));
+    double *ex = malloc(sizeof(double) * (size_t)M);
+    double e_t = 0.0;
+#pragma omp for schedule(static)
+    for (int i = 0; i < n; ++i) {
+      double f[3] = {0.0, 0.0, 0.0};
+      double pi[8] = {0.0};
+      double *pv = C <= 8 ? pi : calloc((size_t)C, sizeof(double));
+      for (int j = 0; j < n; ++j) {
+        if (j == i) continue;
+        const double dx = r[3 * i] - r[3 * j], dy = r[3 * i + 1] - r[3 * j + 1], dz = r[3 * i + 2] - r[3 * j + 2];
+        const double r2 = dx * dx + dy * dy + dz * dz;
+        double K = 0.0, Kd = 0.0, qq = 0.0;
+        for (int m = 0; m < M; ++m) {
+          ex[m] = exp(-0.5 * r2 / bw2[m]);
+          K += amp[m] * ex[m];
+          Kd += amp[m] * ex[m] / bw2[m];
+        }
+        for (int c = 0; c < C; ++c) {
+          qq += q[(size_t)i * C + c] * q[(size_t)j * C + c];
+          pv[c] += K * q[(size_t)j * C + c];
+        }
+        /* d/dr_i of 1/2 sum_{a != b} qq K(r_ab^2) = -sum_j qq Kd (r_i - r_j) */
+        f[0] += qq * Kd * dx; f[1] += qq * Kd * dy; f[2] += qq * Kd * dz;
+        e_t += 0.5 * qq * K;
+        for (int m = 0; m < M; ++m) {
+          ga_t[m] += 0.5 * qq * ex[m];
+          gb_t[m] += 0.5 * qq * amp[m] * ex[m] * 0.5 * r2 / (bw2[m] * bw2[m]);
+        }
+      }
+      if (forces)
+        for (int a = 0; a < 3; ++a) forces[3 * i + a] = norm_factor * f[a];
+      if (potential)
+        for (int c = 0; c < C; ++c) potential[(size_t)i * C + c] = norm_factor * pv[c];
+      if (pv != pi) free(pv);
+    }
+#pragma omp critical
+    {
+      e_pair += e_t;
+      for (int m = 0; m < M; ++m) { ga[m] += ga_t[m]; gb[m] += gb_t[m]; }
+    }
+    free(ga_t); free(gb_t); free(ex);
+  }
+  double e = e_pair;
+  double qsq = 0.0, asum = 0.0;
+  for (size_t k = 0; k < (size_t)n * C; ++k) qsq += q[k] * q[k];
+  for (int m = 0; m < M; ++m) asum += amp[m];
+  if (!remove_self) {
+    e += 0.5 * qsq * asum;
+    if (potential)
+      for (size_t k = 0; k < (size_t)n * C; ++k) potential[k] += norm_factor * q[k] * asum;
+  }
+  for (int m = 0; m < M; ++m) {
+    if (grad_amp) grad_amp[m] = norm_factor * (ga[m] + (remove_self ? 0.0 : 0.5 * qsq));
+    if (grad_bw2) grad_bw2[m] = norm_factor * gb[m];
+  }
+  free(ga); free(gb);
+  return e * norm_factor;
 }

@@ -56,6 +56,15 @@ class DirectArgs(ctypes.Structure):
                 ("grad_bw2", _vp), ("virial", _vp)]
 
 
+class RealspaceArgs(ctypes.Structure):
+    _fields_ = [("nframes", ctypes.c_int), ("atom_begin", _c_i64p), ("atom_count", _c_i64p),
+                ("nchannels", ctypes.c_int), ("positions", _vp), ("charges", _vp),
+                ("n_gauss", ctypes.c_int), ("amp", _vp), ("bw2", _vp),
+                ("norm_factor", ctypes.c_double), ("remove_self", ctypes.c_int),
+                ("charge_neutral_lambda", ctypes.c_double), ("energy", _vp), ("forces", _vp),
+                ("potential", _vp), ("grad_amp", _vp), ("grad_bw2", _vp), ("virial", _vp)]
+
+
 # int exchange(void *ctx, int kind, int64 send_off, int64 recv_off, int64 bytes, void *stream)
 EXCHANGE_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
                                ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p)
@@ -73,7 +82,7 @@ EXPORTS = ["sog_strerror", "sog_last_error", "sog_version", "sog_launch_count", 
            "sog_plan_destroy", "sog_plan_status", "sog_plan_set_timing", "sog_plan_timings",
            "sog_mesh_forward", "sog_direct_create", "sog_direct_destroy", "sog_direct_set_timing",
            "sog_direct_timings", "sog_direct_forward", "sog_direct_forward_noalloc",
-           "sog_mesh_slab_workspace", "sog_mesh_slab_forward"]
+           "sog_mesh_slab_workspace", "sog_mesh_slab_forward", "sog_realspace_forward"]
 
 _lib = None
 _lock = threading.Lock()
@@ -108,6 +117,7 @@ def load():
         lib.sog_direct_create.argtypes = [ctypes.POINTER(_vp), ctypes.c_int, ctypes.c_int]
         lib.sog_direct_destroy.argtypes = [_vp]
         lib.sog_direct_forward.argtypes = [_vp, ctypes.POINTER(DirectArgs), _vp]
+        lib.sog_realspace_forward.argtypes = [_vp, ctypes.POINTER(RealspaceArgs), _vp]
         lib.sog_launch_count.restype = ctypes.c_ulonglong
         for name in ("sog_plan_set_timing", "sog_direct_set_timing"):
             getattr(lib, name).argtypes = [_vp, ctypes.c_int]
@@ -349,3 +359,29 @@ def direct_forward(ctx, *, atom_begin, atom_count, nk, k_sq_max, positions, char
         stream = torch.cuda.current_stream(positions.device).cuda_stream
     check(load().sog_direct_forward(ctx, ctypes.byref(args), ctypes.c_void_p(stream)),
           "sog_direct_forward")
+
+
+def realspace_forward(ctx, *, atom_begin, atom_count, positions, charges, amp, bw2, norm_factor,
+                      remove_self, charge_neutral_lambda, energy, forces=None, potential=None,
+                      grad_amp=None, grad_bw2=None, virial=None, stream=None, **_unused):
+    """sog_realspace_forward on a direct-solver context (non-periodic frames)."""
+    _require_cuda(positions)
+    nf = len(atom_begin)
+    ab, ac = _host_i64(atom_begin), _host_i64(atom_count)
+    args = RealspaceArgs()
+    args.nframes = nf
+    args.atom_begin = ctypes.cast(ab, _c_i64p)
+    args.atom_count = ctypes.cast(ac, _c_i64p)
+    args.nchannels = charges.shape[1]
+    args.positions, args.charges = _ptr(positions), _ptr(charges)
+    args.n_gauss = amp.numel()
+    args.amp, args.bw2 = _ptr(amp), _ptr(bw2)
+    args.norm_factor = float(norm_factor)
+    args.remove_self = int(remove_self)
+    args.charge_neutral_lambda = float(charge_neutral_lambda or 0.0)
+    args.energy, args.forces, args.potential = _ptr(energy), _ptr(forces), _ptr(potential)
+    args.grad_amp, args.grad_bw2, args.virial = _ptr(grad_amp), _ptr(grad_bw2), _ptr(virial)
+    if stream is None:
+        stream = torch.cuda.current_stream(positions.device).cuda_stream
+    check(load().sog_realspace_forward(ctx, ctypes.byref(args), ctypes.c_void_p(stream)),
+          "sog_realspace_forward")

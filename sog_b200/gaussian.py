@@ -294,24 +294,28 @@ class Gaussian(nn.Module):
             return _lib.SPLINE_QUADS, self.quads_order
         return None
 
-    def _frame_layout(self, batch: Optional[torch.Tensor], cell: torch.Tensor, n: int,
+    def _frame_layout(self, batch: Optional[torch.Tensor], cell: Optional[torch.Tensor], n: int,
                       dt: torch.dtype, dev: torch.device) -> Optional[Dict[str, Any]]:
-        """Frames of the call (sorted unique batch ids, atom ranges, mesh or
-        direct buckets).  Needs the cell on the host and, for an explicit
-        batch, its frame counts; both are reused while the same tensors are
-        passed unchanged, so repeated calls launch without host syncs."""
+        """Frames of the call (sorted unique batch ids, atom ranges, mesh,
+        direct or real-space buckets).  Needs the cell on the host and, for an
+        explicit batch, its frame counts; both are reused while the same
+        tensors are passed unchanged, so repeated calls launch without host
+        syncs.  Frames without a cell (cell=None) or with a singular cell go
+        to the real-space pair sum (gaussian.py:735-746)."""
         settings = (n, dt, str(dev), self.n_dl, self.cubes2_phi_max, self.rcut, self.b,
                     self.use_bspline_fft, self.bspline_order, self.use_quads_fft, self.quads_order,
                     self.use_cubes2_fft, tuple(self.bandwidth.shape), id(self.bandwidth),
                     self.bandwidth._version)
         c = self._layout
-        if (c is not None and c["settings"] == settings and c["cell_ref"]() is cell
-                and c["cell_ver"] == cell._version
+        if (c is not None and c["settings"] == settings
+                and ((cell is None and c["cell_ref"] is None) or
+                     (cell is not None and c["cell_ref"] is not None and c["cell_ref"]() is cell
+                      and c["cell_ver"] == cell._version))
                 and ((batch is None and c["batch_ref"] is None) or
                      (batch is not None and c["batch_ref"] is not None and c["batch_ref"]() is batch
                       and c["batch_ver"] == batch._version))):
             return c
-        cell_h = cell.detach().to("cpu", torch.float64)
+        cell_h = None if cell is None else cell.detach().to("cpu", torch.float64)
         if batch is None:
             bids, counts_h, perm = [0], [n], None
         else:
@@ -323,12 +327,12 @@ class Gaussian(nn.Module):
             perm = None if sorted_ok else torch.argsort(batch, stable=True)
         if len(bids) == 0 or n == 0:
             return None
-        vols = torch.abs(torch.linalg.det(cell_h))
-        eps = torch.finfo(cell.dtype).eps
-        for bid in bids:
-            if not bool(vols[bid] > eps):
-                raise NotImplementedError("non-periodic frames (singular cell) need the real-space "
-                                          "path, which is not built yet")
+        if cell_h is None:
+            periodic = [False] * len(bids)
+        else:
+            vols = torch.abs(torch.linalg.det(cell_h))
+            eps = torch.finfo(cell.dtype).eps
+            periodic = [bool(vols[bid] > eps) for bid in bids]
         begins, acc = [], 0
         for bid in bids:
             begins.append(acc)
@@ -336,12 +340,17 @@ class Gaussian(nn.Module):
         nat = [counts_h[bid] for bid in bids]
         fidx = torch.repeat_interleave(torch.arange(len(bids), device=dev),
                                        torch.tensor(nat, device=dev))
-        lens = torch.linalg.norm(cell_h, dim=2)
+        lens = None if cell_h is None else torch.linalg.norm(cell_h, dim=2)
         mesh = self._mesh_kind()
-        if mesh:
+        per = [j for j in range(len(bids)) if periodic[j]]
+        buckets: List[Bucket] = []
+        if not per:
+            pass
+        elif mesh:
             spline, order = mesh
             groups: Dict[Tuple[int, int, int], Bucket] = {}
-            for j, bid in enumerate(bids):
+            for j in per:
+                bid = bids[j]
                 lx, ly, lz = (float(v) for v in lens[bid])
                 nx, ny, nz, ksm = resolve_grid(
                     lx, ly, lz, n_dl=self.n_dl if self.cubes2_phi_max is None else None,
@@ -357,19 +366,30 @@ class Gaussian(nn.Module):
         else:
             n_dl = self._resolve_direct_n_dl(dt, dev)
             bk = Bucket([], [], [], [], nk=[])
-            for j, bid in enumerate(bids):
+            for j in per:
+                bid = bids[j]
                 bk.frames.append(j)
                 bk.atom_begin.append(begins[j])
                 bk.atom_count.append(nat[j])
                 bk.k_sq_max.append((2.0 * math.pi / n_dl) ** 2)
                 bk.nk.append(tuple(max(1, int(float(v) / n_dl)) for v in lens[bid]))
             buckets = [bk]
-        lay = {"settings": settings, "cell_ref": weakref.ref(cell), "cell_ver": cell._version,
+        if len(per) < len(bids):
+            rs = Bucket([], [], [], [], kind="realspace")
+            for j in range(len(bids)):
+                if not periodic[j]:
+                    rs.frames.append(j)
+                    rs.atom_begin.append(begins[j])
+                    rs.atom_count.append(nat[j])
+                    rs.k_sq_max.append(0.0)
+            buckets.append(rs)
+        lay = {"settings": settings, "cell_ref": None if cell is None else weakref.ref(cell),
+               "cell_ver": None if cell is None else cell._version,
                "batch_ref": None if batch is None else weakref.ref(batch),
                "batch_ver": None if batch is None else batch._version,
                "perm": perm, "fidx": fidx, "nframes": len(bids), "buckets": buckets,
                "bid_t": torch.tensor(bids, device=dev, dtype=torch.long),
-               "identity_frames": bids == list(range(cell.shape[0])),
+               "identity_frames": cell is not None and bids == list(range(cell.shape[0])),
                "kind": "mesh" if mesh else "direct", "mesh": mesh}
         self._layout = lay
         return lay
@@ -390,8 +410,6 @@ class Gaussian(nn.Module):
         need_force = bool(compute_force or compute_virial)
         dt = r.dtype
         dev = r.device
-        if cell is None:
-            raise NotImplementedError("the real-space path (cell=None) is not built yet")
         lay = self._frame_layout(batch, cell, n, dt, dev)
         if lay is None:
             return {"energy": torch.zeros(0, dtype=dt, device=dev),
@@ -401,10 +419,13 @@ class Gaussian(nn.Module):
         perm = lay["perm"]
         r_s = r if perm is None else r.index_select(0, perm)
         q_s = q if perm is None else q.index_select(0, perm)
-        cells = cell.detach().to(dt)
-        if not lay["identity_frames"]:
-            cells = cells.index_select(0, lay["bid_t"])
-        cells = cells.contiguous()
+        if cell is None:
+            cells = None
+        else:
+            cells = cell.detach().to(dt)
+            if not lay["identity_frames"]:
+                cells = cells.index_select(0, lay["bid_t"])
+            cells = cells.contiguous()
         amp = self.amp.to(dtype=dt, device=dev)
         bw2 = self.bandwidth.to(dtype=dt, device=dev)
         spec = SolveSpec(kind=lay["kind"], buckets=lay["buckets"], nframes=lay["nframes"],

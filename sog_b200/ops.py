@@ -7,7 +7,8 @@ do), so the backward is a per-frame scaling of saved results.  This is the
 hand-written backward of src/sog/module/cubes2_fft.py:746-869 generalised to
 all solvers: dE/dr is the ik-differentiated force (as there), dE/dq the
 gathered potential plus self and k=0 terms, dE/d(amp, bw2) the M-vector
-k-space reductions.
+k-space reductions.  Non-periodic frames (no cell, or a singular one) take the
+real-space pair sum (gaussian.py:822-845) with the same explicit outputs.
 """
 from __future__ import annotations
 
@@ -29,14 +30,15 @@ class Bucket:
     k_sq_max: List[float]
     dims: Optional[Tuple[int, int, int]] = None   # mesh
     nk: Optional[List[Tuple[int, int, int]]] = None  # direct
+    kind: Optional[str] = None   # "realspace" for non-periodic frames, else the spec's kind
 
 
 @dataclass
 class SolveSpec:
-    kind: str                    # "mesh" | "direct"
+    kind: str                    # "mesh" | "direct" (buckets may say "realspace")
     buckets: List[Bucket]
     nframes: int
-    cells: torch.Tensor          # [nf, 3, 3] (frames in output order), compute dtype
+    cells: Optional[torch.Tensor]  # [nf, 3, 3] (frames in output order), compute dtype; None: no cell
     frame_of_atom: torch.Tensor  # [N] int64 output-frame index of each (sorted) atom
     spline: int = _lib.SPLINE_BSPLINE
     order: int = 6
@@ -78,7 +80,7 @@ def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Ten
             cells_b, e_b, ga_b, gb_b, v_b = spec.cells, energy, gamp, gbw2, vir
         else:
             idx = torch.tensor(b.frames, device=dev, dtype=torch.long)
-            cells_b = spec.cells.index_select(0, idx).contiguous()
+            cells_b = None if spec.cells is None else spec.cells.index_select(0, idx).contiguous()
             e_b = torch.empty(len(b.frames), dtype=dt, device=dev)
             ga_b = torch.empty(len(b.frames), M, dtype=dt, device=dev) if want_grad else None
             gb_b = torch.empty(len(b.frames), M, dtype=dt, device=dev) if want_grad else None
@@ -89,7 +91,12 @@ def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Ten
                       remove_self=spec.remove_self, k0_correction=spec.k0_correction,
                       charge_neutral_lambda=spec.charge_neutral_lambda, energy=e_b,
                       forces=forces, potential=pot, grad_amp=ga_b, grad_bw2=gb_b, virial=v_b)
-        if spec.kind == "mesh" and spec.slab is not None:
+        kind = b.kind or spec.kind
+        if kind == "realspace":
+            ctx = _lib.direct_ctx(dev.index if dev.index is not None else torch.cuda.current_device(),
+                                  dcode)
+            _lib.realspace_forward(ctx, **common)
+        elif kind == "mesh" and spec.slab is not None:
             if len(b.frames) != 1 or nf != 1:
                 raise NotImplementedError("mesh_decomposition='slab' solves one frame per call")
             if want_grad or want_virial:
@@ -106,7 +113,7 @@ def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Ten
                 spec.slab.sum_(forces)
             if pot is not None:
                 spec.slab.sum_(pot)
-        elif spec.kind == "mesh":
+        elif kind == "mesh":
             plan = _lib.PLANS.get(dev.index if dev.index is not None else torch.cuda.current_device(),
                                   dcode, spec.spline, spec.order, b.dims, spec.kconv,
                                   spec.alias_extent)

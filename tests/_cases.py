@@ -11,6 +11,8 @@ MESH_CASES = ["quads4_cubic", "quads6_cubic", "quads4_triclinic", "quads6_tricli
               "quads6_2frames_2ch", "quads4_2frames_keepself", "cfg2_quads6"]
 CUBES2_CASES = ["cubes2_4_cubic", "cubes2_4_triclinic", "cubes2_6_cubic", "cubes2_6_triclinic",
                 "cubes2_4_2frames_2ch"]
+REALSPACE_CASES = ["realspace_defaults", "realspace_internal", "realspace_batch_2ch_keepself",
+                   "realspace_mixed_cells"]
 DIRECT_CASES = ["cfg1_direct", "direct_triclinic_2ch_rsi1", "direct_triclinic_2ch_rsi0",
                 "direct_mixed_batch", "direct_rcut", "direct_internal"]
 

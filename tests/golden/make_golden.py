@@ -15,6 +15,8 @@ Every case stores its inputs and the reference's outputs (fp64).  Sources:
     dE/d(amp, bw2) by autograd through the energy-only call.
   * direct k-sum: ``Sog({"use_atomwise": False})`` / ``Gaussian`` default path
     (gaussian.py:444-548, 1180-1337), derivatives by autograd.
+  * real-space pair sum: ``cell=None`` or a singular cell
+    (gaussian.py:735-746, 822-845), derivatives by autograd.
   * host logic: ``_resolve_grid`` / ``_next_fft_friendly``
     (cubes2_fft.py:75-188) and the kernel-parameter construction of
     ``Gaussian.__init__`` (gaussian.py:89-279).
@@ -286,10 +288,89 @@ def cubes2_cases():
                   lam=0.3, family="cubes2")
 
 
+def run_realspace_case(name, r, q, cell, batch, sog_args=None, gauss_kwargs=None):
+    """Non-periodic frames (cell=None, or singular cells mixed with periodic
+    ones), energy from ``Gaussian.forward``, derivatives by autograd."""
+    torch.manual_seed(0)
+    if sog_args is not None:
+        g = Sog(dict(sog_args)).gaussian
+    else:
+        g = Gaussian(**gauss_kwargs)
+    rg = r.clone().requires_grad_(True)
+    qg = q.clone().requires_grad_(True)
+    e = g(q=qg, r=rg, cell=cell, batch=batch)
+    w = torch.arange(1, e.shape[0] + 1, dtype=F64)
+    (e * w).sum().backward()
+    rec = dict(r=r.numpy(), q=q.numpy(), has_cell=int(cell is not None),
+               cell=np.zeros((0, 3, 3)) if cell is None else cell.numpy(),
+               batch=np.zeros(r.shape[0], dtype=np.int64) if batch is None else batch.numpy(),
+               amp=g.amp.detach().to(F64).numpy(), bw2=g.bandwidth.detach().to(F64).numpy(),
+               amp_dtype=str(g.amp.dtype), self_coeff=float(g.self_coeff),
+               remove_self=int(g.remove_self_interaction),
+               lam=-1.0 if g.charge_neutral_lambda is None else float(g.charge_neutral_lambda),
+               n_dl=-1.0 if g.n_dl is None else float(g.n_dl),
+               energy=e.detach().numpy(), grad_weights=w.numpy(),
+               forces=(-rg.grad).numpy(), grad_q=qg.grad.numpy())
+    if isinstance(g.amp, torch.nn.Parameter) and g.amp.grad is not None:
+        rec["grad_amp"] = g.amp.grad.to(F64).numpy()
+        rec["grad_bw2"] = g.bandwidth.grad.to(F64).numpy()
+    np.savez_compressed(os.path.join(OUT, f"{name}.npz"), **rec)
+    print(name, rec["energy"])
+
+
+def realspace_cases():
+    """Real-space path; its own generator, so the other fixtures stay as they are."""
+    gen = torch.Generator().manual_seed(2026)
+    # the reference's test_force_fd_realspace.py configuration: defaults, 6 atoms
+    r = torch.rand(6, 3, generator=gen, dtype=F64)
+    q = torch.rand(6, generator=gen, dtype=F64) - 0.5
+    q = q - q.mean()
+    run_realspace_case("realspace_defaults", r, q, None, None,
+                       sog_args={"use_atomwise": False, "use_nufft": False,
+                                 "remove_self_interaction": True, "trainable_kernel": False})
+    # one molecule, internal-mode trainable parameters
+    n = 40
+    r = torch.rand(n, 3, generator=gen, dtype=F64) * 8.0
+    q = torch.rand(n, generator=gen, dtype=F64) - 0.5
+    q = q - q.mean()
+    run_realspace_case("realspace_internal", r, q, None, None,
+                       gauss_kwargs=dict(n_dl=2.0, amp=torch.tensor([0.7, 1.1, 1.4], dtype=F64),
+                                         bandwidth=torch.tensor([1.3, 2.1, 3.4], dtype=F64),
+                                         kernel_param_mode="internal", trainable=True))
+    # three molecules (one of a single atom), interleaved batch ids, two
+    # channels, self term kept, neutrality penalty
+    nloc = [13, 1, 20]
+    batch = torch.cat([torch.full((k,), i, dtype=torch.int64) for i, k in enumerate(nloc)])
+    batch = batch[torch.randperm(batch.numel(), generator=gen)]
+    nt = sum(nloc)
+    r = torch.randn(nt, 3, generator=gen, dtype=F64) * 2.5
+    q = torch.rand(nt, 2, generator=gen, dtype=F64) - 0.5
+    amp4, bw4 = params_log(4, 1.2, 5.0)
+    run_realspace_case("realspace_batch_2ch_keepself", r, q, None, batch,
+                       gauss_kwargs=dict(n_dl=2.0, amp=amp4.clone(), bandwidth=bw4.clone(),
+                                         remove_self_interaction=False,
+                                         charge_neutral_lambda=0.2, trainable=True))
+    # a periodic frame (direct k-sum) next to a singular cell (real space)
+    na, nb = 18, 15
+    cells = torch.stack([torch.tensor([[9.0, 0.0, 0.0], [0.8, 8.5, 0.0], [0.4, 0.6, 8.2]], dtype=F64),
+                         torch.zeros(3, 3, dtype=F64)])
+    r = torch.cat([torch.rand(na, 3, generator=gen, dtype=F64) @ cells[0],
+                   torch.randn(nb, 3, generator=gen, dtype=F64) * 2.0])
+    q = torch.rand(na + nb, generator=gen, dtype=F64) - 0.5
+    q[:na] -= q[:na].mean()
+    batch = torch.cat([torch.zeros(na, dtype=torch.int64), torch.ones(nb, dtype=torch.int64)])
+    run_realspace_case("realspace_mixed_cells", r, q, cells, batch,
+                       gauss_kwargs=dict(n_dl=2.0, amp=amp4.clone(), bandwidth=bw4.clone(),
+                                         trainable=True))
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     if sys.argv[1:] == ["cubes2"]:
         cubes2_cases()
+    elif sys.argv[1:] == ["realspace"]:
+        realspace_cases()
     else:
         main()
         cubes2_cases()
+        realspace_cases()

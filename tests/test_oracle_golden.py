@@ -4,8 +4,8 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from tests._cases import (CUBES2_CASES, DIRECT_CASES, MESH_CASES, direct_n_dl, direct_nk,
-                          grid_ndl, load)
+from tests._cases import (CUBES2_CASES, DIRECT_CASES, MESH_CASES, REALSPACE_CASES, direct_n_dl,
+                          direct_nk, grid_ndl, load)
 
 
 def _mesh_case_vs_oracle(name, spline):
@@ -62,6 +62,34 @@ def test_oracle_direct_matches_reference(name):
         tol = 1e-5 if "float32" in str(c["amp_dtype"]) else 1e-10
         assert np.allclose(ga, c["grad_amp"], rtol=tol, atol=tol * np.abs(ga).max())
         assert np.allclose(gb, c["grad_bw2"], rtol=tol, atol=tol * np.abs(gb).max())
+
+
+@pytest.mark.parametrize("name", REALSPACE_CASES)
+def test_oracle_realspace_matches_reference(name):
+    c = load(name)
+    cells = c["cell"].reshape(-1, 3, 3) if int(c["has_cell"]) else None
+    n_dl = direct_n_dl(c)
+    nks = None if cells is None else [direct_nk(cl, n_dl) for cl in cells]
+    ksm = None if cells is None else [(2.0 * np.pi / n_dl) ** 2] * len(cells)
+    lam = None if c["lam"] < 0 else float(c["lam"])
+    res = O.bundle(c["r"], c["q"], cells, c["batch"], c["amp"], c["bw2"], solver="direct",
+                   nks=nks, k_sq_max=ksm, remove_self=bool(c["remove_self"]),
+                   self_coeff=float(c["self_coeff"]), charge_neutral_lambda=lam)
+    e_ref = c["energy"]
+    assert np.allclose(res["energy"], e_ref, rtol=1e-12, atol=1e-13 * np.abs(e_ref).max())
+    w = c["grad_weights"][c["batch"]]
+    fscale = max(1.0, np.abs(c["forces"]).max())
+    assert np.abs(res["forces"] * w[:, None] - c["forces"]).max() < 1e-11 * fscale
+    q = c["q"] if c["q"].ndim == 2 else c["q"][:, None]
+    gq = res["potential"] * w[:, None]
+    assert np.abs(gq - c["grad_q"].reshape(q.shape)).max() < 1e-11 * max(1.0, np.abs(gq).max())
+    if "grad_amp" in c:
+        ga = (res["grad_amp"] * c["grad_weights"][:, None]).sum(0)
+        gb = (res["grad_bw2"] * c["grad_weights"][:, None]).sum(0)
+        assert np.allclose(ga, c["grad_amp"], rtol=1e-10, atol=1e-12 * np.abs(ga).max())
+        assert np.allclose(gb, c["grad_bw2"], rtol=1e-10, atol=1e-12 * np.abs(gb).max())
+    # a one-atom molecule has only the self term (or nothing)
+    assert np.isfinite(res["energy"]).all()
 
 
 @pytest.mark.parametrize("order", [4, 5, 6])
