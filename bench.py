@@ -9,10 +9,18 @@ One step = one energy + explicit-force evaluation of the whole system.
   value   device throughput, inputs resident in HBM (CUDA events, max over ranks)
   e2e     the same through the public API (sog_b200.Sog) with pinned host
           inputs copied in and energy + forces copied out every step
-With N > 1 ranks (torchrun) every rank solves its own independent system
-(frame-parallel data parallelism, no collective on the data path): weak scaling.
+With N > 1 ranks (torchrun) the system's mesh is split into z slabs over the
+GPUs (--mode slab, default: strong scaling), or every rank solves its own
+independent system (--mode frames: weak scaling).
+
+--config cfg4 times the batched-frames workload instead: 512 independent
+cubic frames of 200-5000 atoms (density 0.1 / A^3, n_dl = 1.0, per-frame
+meshes 25^3-75^3, B-spline order 6); with N ranks the frames are shared out
+by the longest-processing-time rule (sog_b200.shard), no collective on the
+data path: strong scaling of the fixed batch.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sog_b200|reference]
+                    [--config cfg5|cfg5_eighth|cfg2|cfg4]
 """
 from __future__ import annotations
 
@@ -51,6 +59,49 @@ def workload(name: str):
                              "12 Gaussians bw 1.2*1.62^m", natoms=3000, L=31.0, n_dl=1.0, order=6,
                     m=12, bw_geom=(1.2, 1.62), qstd=None)
     raise SystemExit(f"unknown config {name}")
+
+
+def make_batch(seed: int = 0, nframes: int = 512):
+    """Batched-frames workload: frame sizes U{200..5000}, cubic cells of
+    density 0.1 atoms / A^3, uniform positions, U(-1, 1) charges neutral per
+    frame, 12 Gaussians bw 1.2 * 1.62^m with raw amplitudes."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    ns = rng.integers(200, 5001, nframes)
+    rs, qs, cells = [], [], []
+    for n in ns:
+        L = (n / 0.1) ** (1.0 / 3.0)
+        rs.append(rng.random((n, 3)) * L)
+        qq = rng.uniform(-1.0, 1.0, n)
+        qs.append(qq - qq.mean())
+        cells.append(np.eye(3) * L)
+    bw = 1.2 * 1.62 ** np.arange(12)
+    amp_raw = 1.0 / (bw * math.sqrt(2.0 * math.pi))
+    return [int(n) for n in ns], np.concatenate(rs), np.concatenate(qs), np.stack(cells), amp_raw, bw
+
+
+def bucket_bytes(dims, nframes: int, natoms: int, s: int = 8, nfield: int = 3):
+    """Minimal-pipeline bytes per kernel name of one mesh bucket (the same
+    accounting as algorithmic_bytes, for nframes frames of one mesh)."""
+    nx, ny, nz = dims
+    ng = nx * ny * nz * nframes
+    nh = nz * ny * (nx // 2 + 1) * nframes
+    N = natoms
+    out = {
+        "spread": s * ng + 4 * s * N,
+        "fft_r2c_x": s * ng + 2 * s * nh,
+        "fft_y_fwd": 4 * s * nh,
+        "fft_y_inv": nfield * 4 * s * nh,
+        "fft_c2r_x": nfield * (2 * s * nh + s * ng),
+        "gather": nfield * s * ng + 7 * s * N,
+        "green": s * nh,
+    }
+    if nz & (nz - 1) == 0:        # fused z pass
+        out["zfused"] = 2 * s * nh + nfield * 2 * s * nh
+    else:                         # z passes around the k-space kernel
+        out.update({"fft_z_fwd": 4 * s * nh, "kspace": 2 * s * nh + nfield * 2 * s * nh,
+                    "fft_z_inv": nfield * 4 * s * nh})
+    return out, 7 * s * N + 8 * s * ng + 16 * s * nh
 
 
 def make_inputs(cfg, seed: int):
@@ -237,8 +288,44 @@ def oracle_eval_time(cfg_name: str, reps: int, warm: int = 1):
     return cfg, times, O.num_threads()
 
 
+def oracle_batch_time(frames: int = 120):
+    """The oracle's E+F on the first `frames` frames of the batched workload."""
+    from oracle import oracle as O
+    from tests._cases import friendly
+    counts, r, q, cells, amp_raw, bw = make_batch(0)
+    amp = amp_raw * bw * bw
+    ksm = (2.0 * math.pi / 1.0) ** 2
+    t, atoms, b = 0.0, 0, 0
+    for j in range(frames):
+        n = counts[j]
+        L = float(cells[j][0, 0])
+        g = friendly(max(8, 2 * int(math.floor(L / 1.0)) + 1))
+        t0 = time.perf_counter()
+        O.mesh_solve(r[b:b + n], q[b:b + n], cells[j], amp, bw * bw, spline=O.BSPLINE, order=6,
+                     nx=g, ny=g, nz=g, k_sq_max=ksm, want_force=True)
+        t += time.perf_counter() - t0
+        atoms += n
+        b += n
+    return atoms, t, O.num_threads()
+
+
 def run_reference(args, rank: int):
     if rank != 0:
+        return
+    if args.config == "cfg4":
+        atoms, t, threads = oracle_batch_time()
+        val = atoms / t
+        line = {
+            "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus, "steps": 1,
+            "warmup": 0, "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)", "impl": "reference",
+            "config": {"workload": BATCH_WORKLOAD, "sample": f"first 120 frames ({atoms} atoms)"},
+            "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"first 120 frames of the batch ({atoms} atoms), E+F by the "
+                                       "C/OpenMP oracle"},
+            "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
         return
     sample = "cfg5_eighth"
     cfg, times, threads = oracle_eval_time(sample, reps=args.steps, warm=args.warmup)
@@ -262,6 +349,177 @@ def run_reference(args, rank: int):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+BATCH_WORKLOAD = ("batched frames: 512 cubic frames of 200-5000 atoms (1,382,639 atoms), density "
+                  "0.1/A^3, n_dl 1.0 (meshes 25^3-75^3), B-spline order 6, 12 Gaussians "
+                  "bw 1.2*1.62^m")
+
+
+def run_gpu_batch(args, rank: int, world: int):
+    """Batched independent frames, shared out over the ranks by LPT."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from sog_b200 import Sog, _lib
+    from sog_b200.grid import resolve_grid
+    from sog_b200.shard import FrameShards, frame_costs, lpt_partition
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dt = torch.float64 if args.dtype == "f64" else torch.float32
+    s = 8 if dt == torch.float64 else 4
+    counts, r, q, cells, amp_raw, bw = make_batch(0)
+    import warnings
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore", DeprecationWarning)
+        grids = [resolve_grid(*(float(c[i, i]) for i in range(3)), n_dl=1.0, cubes2_phi_max=None,
+                              r_c=None, min_grid=8)[:3] for c in cells]
+    costs = frame_costs(counts, [g[0] * g[1] * g[2] for g in grids], order=6)
+    sh = FrameShards(counts, lpt_partition(costs, world), rank, dev)
+    model = Sog({"use_atomwise": False, "use_bspline_fft": True, "bspline_order": 6, "n_dl": 1.0,
+                 "amp": torch.tensor(amp_raw, dtype=dt), "bandwidth": torch.tensor(bw, dtype=dt),
+                 "trainable_kernel": False}).to(dev)
+    gauss = model.gaussian
+    r_all = torch.tensor(r, dtype=dt, device=dev)
+    q_all = torch.tensor(q, dtype=dt, device=dev)[:, None]
+    c_all = torch.tensor(cells, dtype=dt, device=dev)
+    r_d, q_d, c_d, b_d = sh.select(r_all, q_all, c_all)
+    del r_all, q_all
+    N = int(r_d.shape[0])
+    nf_local = len(sh.frames)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def step_device():
+        return gauss.compute_bundle(q=q_d, r=r_d, cell=c_d, batch=b_d, compute_force=True)
+
+    for _ in range(max(1, args.warmup)):
+        step_device()
+    torch.cuda.synchronize()
+    lay = gauss._layout
+    plans = [p for p in _lib.PLANS.plans.values()
+             if any(p.key[4] == tuple(b.dims) for b in lay["buckets"])]
+    for p in plans:
+        p.set_timing(True)
+    stream = torch.cuda.current_stream()
+    clocks = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    l0 = _lib.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gc.collect()
+    gc.disable()
+    ev0.record(stream)
+    h0 = time.perf_counter()
+    for _ in range(args.steps):
+        out = step_device()
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    gc.enable()
+    launches = _lib.launch_count() - l0
+    clk = clocks.stop()
+    barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    tot, cnt = {}, {}
+    for p in plans:
+        for name, t in p.timings():
+            tot[name] = tot.get(name, 0.0) + t
+            cnt[name] = cnt.get(name, 0) + 1
+        p.set_timing(False)
+    ms_all = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_all, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_all.item())
+    e_sum = float(out["energy"].sum())
+
+    # ---- end to end through Sog.forward with this rank's share in pinned host memory ----
+    r_h = r_d.cpu().pin_memory()
+    q_h = q_d[:, 0].cpu().pin_memory()
+    e_h = torch.empty(nf_local, dtype=dt).pin_memory()
+    f_h = torch.empty(N, 3, dtype=dt).pin_memory()
+    r_in = torch.empty_like(r_d)
+    q_in = torch.empty(N, dtype=dt, device=dev)
+
+    def step_e2e():
+        r_in.copy_(r_h, non_blocking=True)
+        q_in.copy_(q_h, non_blocking=True)
+        o = model(positions=r_in, cell=c_d, latent_charges=q_in, batch=b_d, compute_force=True)
+        e_h.copy_(o["E_lr"], non_blocking=True)
+        f_h.copy_(o["forces"], non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        step_e2e()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step_e2e()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
+    ms_e2e = float(ms_e2e.item())
+    if rank != 0:
+        return
+    per_kernel, b_ef = {}, 0.0
+    for b in lay["buckets"]:
+        kb, be = bucket_bytes(b.dims, len(b.frames), sum(b.atom_count), s=s)
+        b_ef += be
+        for k, v in kb.items():
+            per_kernel[k] = per_kernel.get(k, 0.0) + v
+    kernels = {k: {"launches": cnt[k] // args.steps, "total_ms": tot[k] / args.steps,
+                   "share": tot[k] / sum(tot.values())} for k in tot}
+    dom = max(tot, key=tot.get) if tot else None
+    peak, peak_kind = measured_peak()
+    roof = None
+    for k, v in kernels.items():
+        if k in per_kernel:
+            v["achieved_gbs"] = per_kernel[k] / (v["total_ms"] * 1e-3) / 1e9
+    if dom is not None and dom in per_kernel:
+        ach = kernels[dom]["achieved_gbs"]
+        roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                "frac": ach / peak, "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                "algorithmic_bytes_per_step": per_kernel[dom],
+                "note": "rank 0's share; all launches of the kernel in one step (one per mesh bucket)"}
+    cpu = None
+    if not args.no_cpu_baseline:
+        atoms, t, threads = oracle_batch_time()
+        cpu = {"value": atoms / t, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"first 120 frames of the batch ({atoms} atoms), E+F by the C/OpenMP oracle"}
+    total = sum(counts)
+    step_gbs = b_ef / (ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": total / (ms_max * 1e-3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic (seeded)",
+        "config": {"workload": BATCH_WORKLOAD, "frames": len(counts), "atoms": total,
+                   "frames_rank0": nf_local, "atoms_rank0": N, "mesh_buckets_rank0": len(lay["buckets"]),
+                   "parallelism": f"frame-dp{world} (LPT by estimated cost)" if world > 1 else "single",
+                   "l2": "meshes of all frames (~1 GB per array) larger than L2"},
+        "e2e": {"value": total / (ms_e2e * 1e-3), "unit": UNIT, "ms_per_step": ms_e2e,
+                "h2d_bytes_per_step": N * 4 * s, "d2h_bytes_per_step": nf_local * s + N * 3 * s},
+        "roofline": roof,
+        "step_roofline": {"algorithmic_bytes": b_ef, "achieved": step_gbs, "peak": peak, "unit": "GB/s",
+                          "frac": step_gbs / peak},
+        "kernels": kernels,
+        "gpu_launches": int(launches),
+        "host_enqueue_ms_per_step": host_ms,
+        "clocks": clk,
+        "cpu_baseline": cpu,
+        "energy_sum_rank0": e_sum,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_gpu(args, rank: int, world: int):
     import numpy as np
     import torch
@@ -476,7 +734,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="sog_b200", choices=["sog_b200", "reference"])
-    ap.add_argument("--config", default="cfg5", choices=["cfg5", "cfg5_eighth", "cfg2"])
+    ap.add_argument("--config", default="cfg5", choices=["cfg5", "cfg5_eighth", "cfg2", "cfg4"])
     ap.add_argument("--dtype", default="f64", choices=["f64", "f32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--transport", default="peer", choices=["peer", "exchange"],
@@ -497,7 +755,10 @@ def main():
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     try:
-        run_gpu(args, rank, world)
+        if args.config == "cfg4":
+            run_gpu_batch(args, rank, world)
+        else:
+            run_gpu(args, rank, world)
     finally:
         if world > 1:
             import torch.distributed as dist

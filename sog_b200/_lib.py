@@ -240,12 +240,28 @@ def _ptr(t: Optional[torch.Tensor]):
 
 
 def _host_i64(vals: Sequence[int]):
-    arr = (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
-    return arr
+    if isinstance(vals, ctypes.Array):  # converted once and cached by the caller
+        return vals
+    return (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
 
 
 def _host_f64(vals: Sequence[float]):
+    if isinstance(vals, ctypes.Array):
+        return vals
     return (ctypes.c_double * len(vals))(*[float(v) for v in vals])
+
+
+def _host_nk(nk):
+    if isinstance(nk, ctypes.Array):
+        return nk
+    return (ctypes.c_int32 * (3 * len(nk)))(*[int(v) for row in nk for v in row])
+
+
+def host_tables(atom_begin, atom_count, k_sq_max, nk=None):
+    """ctypes copies of a bucket's per-frame host arrays, made once per frame
+    layout so that repeated calls pass them without conversion."""
+    return dict(atom_begin=_host_i64(atom_begin), atom_count=_host_i64(atom_count),
+                k_sq_max=_host_f64(k_sq_max), nk=None if nk is None else _host_nk(nk))
 
 
 def _mesh_args(atom_begin, atom_count, k_sq_max, positions, charges, cells, amp, bw2, norm_factor,
@@ -339,7 +355,7 @@ def direct_forward(ctx, *, atom_begin, atom_count, nk, k_sq_max, positions, char
     _require_cuda(positions)
     nf = len(atom_begin)
     ab, ac, km = _host_i64(atom_begin), _host_i64(atom_count), _host_f64(k_sq_max)
-    nkflat = (ctypes.c_int32 * (3 * nf))(*[int(v) for row in nk for v in row])
+    nkflat = _host_nk(nk)
     args = DirectArgs()
     args.nframes = nf
     args.atom_begin = ctypes.cast(ab, _c_i64p)

@@ -132,18 +132,29 @@ __device__ __forceinline__ void stage_body(const cplx_t<T> *src, cplx_t<T> *dst,
 // `batch` transforms of length rp.n held in smem: element j of transform b at
 // a[j*sj + b*sb].  Ping-pongs between a and b; returns the buffer with the
 // result.  All threads of the block must call it.
+// Column layout (sb == 1, sj = 2^lg_cols >= batch): consecutive threads take
+// consecutive transforms of the same element index, so a warp reads
+// consecutive words; row layout (sj == 1): consecutive element indices.
 template <typename T, int DIR>
 __device__ cplx_t<T> *fft_smem(cplx_t<T> *a, cplx_t<T> *bbuf, const RadixPlan &rp, int batch,
-                               int sj, int sb, const cplx_t<T> *__restrict__ tw) {
+                               int sj, int sb, const cplx_t<T> *__restrict__ tw, int lg_cols = -1) {
   cplx_t<T> *src = a, *dst = bbuf;
   int Ns = 1;
   const int n = rp.n;
   for (int s = 0; s < rp.nst; ++s) {
     const int R = rp.r[s];
     const int nR = n / R;
-    const int total = batch * nR;
+    const int total = lg_cols >= 0 ? (nR << lg_cols) : batch * nR;
     for (int t = threadIdx.x; t < total; t += blockDim.x) {
-      const int b = t / nR, j = t - b * nR;
+      int b, j;
+      if (lg_cols >= 0) {
+        b = t & ((1 << lg_cols) - 1);
+        j = t >> lg_cols;
+        if (b >= batch) continue;
+      } else {
+        b = t / nR;
+        j = t - b * nR;
+      }
       switch (R) {
         case 2: stage_body<T, DIR, 2>(src, dst, n, Ns, j, b, sj, sb, tw); break;
         case 3: stage_body<T, DIR, 3>(src, dst, n, Ns, j, b, sj, sb, tw); break;
@@ -183,39 +194,45 @@ __global__ void k_fft_r2c_x(const T *__restrict__ in, cplx_t<T> *__restrict__ ou
 }
 
 // Inverse C2R along x with torch.fft.irfftn semantics (unnormalised).  Input
-// rows are field-major ((frame*F + f)*nzy + zy); the output is interleaved,
-// out[((frame*nzy + zy)*nx + x)*F + f].
+// rows are field-major, in[((frame*F + f)*nzy + zy)*(nx/2+1) + m]; the output
+// is interleaved, out[((frame*nzy + zy)*nx + x)*F + f].  A CTA transforms the
+// F fields of `rows_per_cta` consecutive (frame, zy) rows together, so its
+// output is one contiguous run of rows_per_cta*nx*F values.  Transform rows
+// are nx+1 apart in shared memory.
 template <typename T>
 __global__ void k_fft_c2r_x(const cplx_t<T> *__restrict__ in, T *__restrict__ out, int nx,
                             int64_t nrows, int rows_per_cta, RadixPlan rp,
                             const cplx_t<T> *__restrict__ tw, int F, int64_t nzy) {
   using C = cplx_t<T>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int ld = nx + 1;
   C *a = reinterpret_cast<C *>(smem_raw);
-  C *b = a + (size_t)rows_per_cta * nx;
-  const int64_t row0 = (int64_t)blockIdx.x * rows_per_cta;
+  C *b = a + (size_t)rows_per_cta * F * ld;
+  const int64_t row0 = (int64_t)blockIdx.x * rows_per_cta;   // (frame, zy) rows
   const int nr = (int)min((int64_t)rows_per_cta, nrows - row0);
   const int nxh = nx / 2 + 1;
-  const C *src = in + row0 * nxh;
-  for (int i = threadIdx.x; i < nr * nxh; i += blockDim.x) {
-    const int r = i / nxh, m = i - r * nxh;
-    const C v = src[i];
-    a[r * nx + m] = v;
-    if (m >= 1 && m < (nx + 1) / 2) a[r * nx + nx - m] = cmk<C, T>(v.x, -v.y);
+  const int nt = nr * F;
+  for (int i = threadIdx.x; i < nt * nxh; i += blockDim.x) {
+    const int tr = i / nxh, m = i - tr * nxh;      // transform (rl, f), mode m
+    const int rl = tr / F, f = tr - rl * F;
+    const int64_t row = row0 + rl, frame = row / nzy, zy = row - frame * nzy;
+    const C v = in[((frame * F + f) * nzy + zy) * nxh + m];
+    C *ar = a + (size_t)tr * ld;
+    ar[m] = v;
+    if (m >= 1 && m < (nx + 1) / 2) ar[nx - m] = cmk<C, T>(v.x, -v.y);
   }
   __syncthreads();
-  C *res = fft_smem<T, +1>(a, b, rp, nr, 1, nx, tw);
-  for (int i = threadIdx.x; i < nr * nx; i += blockDim.x) {
-    const int r = i / nx, x = i - r * nx;
-    const int64_t row = row0 + r;                 // (frame*F + f)*nzy + zy
-    const int64_t ff = row / nzy, zy = row - ff * nzy;
-    const int64_t frame = ff / F, f = ff - frame * F;
-    out[((frame * nzy + zy) * nx + x) * F + f] = res[i].x;
+  C *res = fft_smem<T, +1>(a, b, rp, nt, 1, ld, tw);
+  T *dst = out + row0 * nx * F;
+  for (int i = threadIdx.x; i < nr * nx * F; i += blockDim.x) {
+    const int rl = i / (nx * F), rem = i - rl * nx * F;
+    const int x = rem / F, f = rem - x * F;
+    dst[i] = res[(size_t)(rl * F + f) * ld + x].x;
   }
 }
 
 // C2C along a strided axis: data viewed as [outer][n][inner]; a CTA handles one
-// outer index and `ic` consecutive inner columns.
+// outer index and `ic` (a power of two) consecutive inner columns.
 template <typename T, int DIR>
 __global__ void k_fft_strided(cplx_t<T> *__restrict__ data, int64_t inner, int64_t outer,
                               int ic, RadixPlan rp, const cplx_t<T> *__restrict__ tw) {
@@ -229,14 +246,15 @@ __global__ void k_fft_strided(cplx_t<T> *__restrict__ data, int64_t inner, int64
   const int64_t i0 = (blockIdx.x - o * nchunks) * ic;
   const int nic = (int)min((int64_t)ic, inner - i0);
   C *base = data + o * (int64_t)n * inner + i0;
+  const int lg = 31 - __clz(ic);
   for (int t = threadIdx.x; t < n * ic; t += blockDim.x) {
-    const int j = t / ic, c = t - j * ic;
+    const int j = t >> lg, c = t & (ic - 1);
     if (c < nic) a[t] = base[(int64_t)j * inner + c];
   }
   __syncthreads();
-  C *res = fft_smem<T, DIR>(a, b, rp, nic, ic, 1, tw);
+  C *res = fft_smem<T, DIR>(a, b, rp, nic, ic, 1, tw, lg);
   for (int t = threadIdx.x; t < n * ic; t += blockDim.x) {
-    const int j = t / ic, c = t - j * ic;
+    const int j = t >> lg, c = t & (ic - 1);
     if (c < nic) base[(int64_t)j * inner + c] = res[t];
   }
 }

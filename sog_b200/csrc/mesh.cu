@@ -869,6 +869,68 @@ __global__ void __launch_bounds__(256) k_kspace(KsArgs<T> a) {
   }
 }
 
+// k-space step with the Green function read from k_green's tables (any nz):
+// thread per (iy, mx) column walking its share of the z planes, energy
+// partial sum and the ik / potential field spectra.  Same arithmetic as the
+// field step of k_zfused_g.
+template <typename T>
+__global__ void __launch_bounds__(256) k_kspace_tab(KsArgs<T> a) {
+  using C = cplx_t<T>;
+  __shared__ double red[8];
+  const int f = blockIdx.y;
+  const FrameGeom &g = a.geom[f];
+  const int64_t inner = (int64_t)a.ny * a.nxh;
+  const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int zper = (a.nz + gridDim.z - 1) / gridDim.z;
+  const int izb = blockIdx.z * zper, ize = min(a.nz, izb + zper);
+  double accE = 0.0;
+  if (col < inner) {
+    const int iy = (int)(col / a.nxh), mx = (int)(col - (int64_t)iy * a.nxh);
+    const int my = signed_mode(iy, a.ny);
+    const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
+    const double inv = 1.0 / ((double)a.nx * a.ny * a.nz);
+    const C *sp = a.spec + (int64_t)f * a.nh + col;
+    const double *ge = a.gtab + (int64_t)f * a.nh + col;
+    const double *gf = (g.pad && a.gtabF) ? a.gtabF + (int64_t)f * a.nh + col : nullptr;
+    C *out = a.nfield ? a.fspec + (int64_t)f * a.nfield * a.nh + col : nullptr;
+    double kxy[3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) kxy[c] = g.kmat[c * 3 + 0] * mx + g.kmat[c * 3 + 1] * my;
+    for (int iz = izb; iz < ize; ++iz) {
+      const int64_t o = (int64_t)iz * inner;
+      const C r = sp[o];
+      const double gE = ge[o];
+      const double rr = (double)r.x, ri = (double)r.y;
+      accE += w * gE * (rr * rr + ri * ri);
+      if (out) {
+        int fo = 0;
+        if (a.want_force) {
+          const double gF = gf ? gf[o] : gE;
+          const double sre = gF * inv * rr, sim = gF * inv * ri;
+          const int mz = signed_mode(iz, a.nz);
+#pragma unroll
+          for (int c = 0; c < 3; ++c) {
+            const double kc = kxy[c] + g.kmat[c * 3 + 2] * mz;
+            out[(int64_t)c * a.nh + o] = cmk<C, T>((T)(-kc * sim), (T)(kc * sre));
+          }
+          fo = 3;
+        }
+        if (a.nfield > fo) out[(int64_t)fo * a.nh + o] = cmk<C, T>((T)(gE * inv * rr), (T)(gE * inv * ri));
+      }
+    }
+  }
+  accE = warp_sum(accE);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = accE;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double e = 0.0;
+    for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) e += red[wi];
+    double *p = a.part + ((int64_t)f * gridDim.z * gridDim.x + (int64_t)blockIdx.z * gridDim.x + blockIdx.x) * 2;
+    p[0] = e;
+    p[1] = 0.0;
+  }
+}
+
 // Fused z pass for a power-of-two nz: forward z-FFT of a tile of ic spectrum
 // columns, the k-space step of k_kspace on the registers, and the inverse z-FFT
 // of every output field, so neither the z-transformed spectrum nor the field
@@ -1502,11 +1564,15 @@ int rows_per_cta(int n) {
   return std::max(1, std::min(r, 64));
 }
 
+// columns per CTA of the generic strided pass: a power of two (the smem
+// transform maps lanes to columns with a mask)
 template <typename T>
 int cols_per_cta(int n) {
   const size_t budget = 64 * 1024;
-  int r = (int)(budget / (2 * (size_t)n * sizeof(cplx_t<T>)));
-  return std::max(1, std::min(r, 16));
+  const int r = (int)(budget / (2 * (size_t)n * sizeof(cplx_t<T>)));
+  int ic = 1;
+  while (ic * 2 <= std::min(r, 16)) ic *= 2;
+  return ic;
 }
 
 // Persistent grids: one wave of resident CTAs looping over the tiles.
@@ -1644,9 +1710,9 @@ void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nframes, int64_
       k_rows_c2r_il<T><<<nblocks(rows, rpc), tpt * F * rpc, sm, st>>>(fspec, freal, F, nzy, rows, rpc, p->rpx,
                                                                         p->twx.as<C>());
     } else {
-      const int rpc = rows_per_cta<T>(nx);
-      const int64_t rows = nframes * F * nzy;
-      k_fft_c2r_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
+      const int rpc = std::max(1, rows_per_cta<T>(nx + 1) / F);
+      const int64_t rows = nframes * nzy;
+      k_fft_c2r_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx + 1, rpc * F), st>>>(
           fspec, freal, nx, rows, rpc, p->rpx, p->twx.as<C>(), F, nzy);
     }
   }
@@ -2002,12 +2068,17 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   gar.range_lo = gar.range_hi = nullptr;
 
   set_fft_smem_attrs<T>();
+  // power-of-two nz: fused z pass; otherwise separate z passes around
+  // k_kspace_tab.  Both read the Green tables k_green writes once per call.
   const bool zfuse = is_pow2(nz);
+  const bool zgeneric = zfuse && nz > 1024;  // runtime-plan fused pass, Green on the fly
   const int zic = zfuse ? reg_width<T>(nz, 256, 32 * 1024) : 0;
   const int64_t zchunks = zfuse ? ((int64_t)ny * nxh + zic - 1) / zic : 0;
-  const int64_t nblk_e = zfuse ? zchunks : (int64_t)ks_blocks;
+  const unsigned tblocks = nblocks((int64_t)ny * nxh, 256);
+  const unsigned tz = green_zsplit(tblocks, nf, nz);
+  const int64_t nblk_e = zfuse ? zchunks : (int64_t)tblocks * tz;
   double *redD = nullptr;
-  if (zfuse) {
+  if (!zgeneric) {
     // Green tables and the self sum, once per call (independent of the charges)
     const bool aliasable = p->d.spline == SOG_SPLINE_BSPLINE;
     const unsigned gblocks = nblocks((int64_t)ny * nxh, 256);
@@ -2058,7 +2129,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
       after(tr, st, "zfused");
     } else {
       pass_cols<T, -1>(p, p->spec.as<C>(), nz, (int64_t)ny * nxh, nf, p->rpz, p->twz.as<C>(), st, "fft_z_fwd");
-      k_kspace<T><<<dim3(ks_blocks, nf), 256, 0, st>>>(ka);
+      k_kspace_tab<T><<<dim3(tblocks, nf, tz), 256, 0, st>>>(ka);
       after(tr, st, "kspace");
     }
     if (want_grad || want_vir) {
@@ -2092,7 +2163,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   fa.geom = geom;
   fa.redE = redE;
   fa.redX = redX;
-  fa.redD = (zfuse && is_pow2(nz) && nz <= 1024) ? redD : nullptr;
+  fa.redD = zgeneric ? nullptr : redD;
   fa.qsum = p->qsum.as<double>();
   fa.amp = a->amp;
   fa.bw2 = a->bw2;

@@ -31,6 +31,13 @@ class Bucket:
     dims: Optional[Tuple[int, int, int]] = None   # mesh
     nk: Optional[List[Tuple[int, int, int]]] = None  # direct
     kind: Optional[str] = None   # "realspace" for non-periodic frames, else the spec's kind
+    _host: Optional[dict] = None
+
+    def host(self) -> dict:
+        """The per-frame arrays as ctypes arrays, converted on first use."""
+        if self._host is None:
+            self._host = _lib.host_tables(self.atom_begin, self.atom_count, self.k_sq_max, self.nk)
+        return self._host
 
 
 @dataclass
@@ -85,7 +92,8 @@ def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Ten
             ga_b = torch.empty(len(b.frames), M, dtype=dt, device=dev) if want_grad else None
             gb_b = torch.empty(len(b.frames), M, dtype=dt, device=dev) if want_grad else None
             v_b = torch.empty(len(b.frames), 3, 3, dtype=dt, device=dev) if want_virial else None
-        common = dict(atom_begin=b.atom_begin, atom_count=b.atom_count, k_sq_max=b.k_sq_max,
+        h = b.host()
+        common = dict(atom_begin=h["atom_begin"], atom_count=h["atom_count"], k_sq_max=h["k_sq_max"],
                       positions=r, charges=q, cells=cells_b, amp=amp, bw2=bw2,
                       norm_factor=spec.norm_factor, self_coeff=spec.self_coeff,
                       remove_self=spec.remove_self, k0_correction=spec.k0_correction,
@@ -121,7 +129,7 @@ def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Ten
         else:
             ctx = _lib.direct_ctx(dev.index if dev.index is not None else torch.cuda.current_device(),
                                   dcode)
-            _lib.direct_forward(ctx, nk=b.nk, **common)
+            _lib.direct_forward(ctx, nk=h["nk"], **common)
         if not single:
             energy.index_copy_(0, idx, e_b)
             if want_grad:
