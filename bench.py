@@ -579,35 +579,79 @@ def run_gpu(args, rank: int, world: int):
     plan = next(p for p in _lib.PLANS.plans.values() if p.key[4] == (n, n, n))
 
     # ---- device-resident timed region ----
+    # Without a collective inside the step (one GPU, or independent systems
+    # per rank) the K steps are captured into one CUDA graph and replayed as
+    # the timed region: the host enqueues them at once, so a pause of the
+    # launching thread cannot leave the GPU idle between steps.  The slab
+    # step calls NCCL between its kernels and is launched eagerly.
     stream = torch.cuda.current_stream()
-    plan.set_timing(True)
+    graph = None
+    if not slab and not args.eager:
+        plan.set_timing(True, events=48 * args.steps + 64)
+        l0 = _lib.launch_count()
+        graph = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.graph(graph):
+                for _ in range(args.steps):
+                    out = step_device()
+            launches = _lib.launch_count() - l0
+            graph.replay()                   # upload; one untimed pass
+            torch.cuda.synchronize()
+        except Exception as exc:             # fall back to eager launches
+            print(f"rank {rank}: CUDA graph capture failed ({exc}); timing eager launches",
+                  file=sys.stderr, flush=True)
+            graph = None
+            torch.cuda.synchronize()
+    if graph is None:
+        plan.set_timing(True)
     clocks = ClockSampler(local)
     barrier()
     torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
-    l0 = _lib.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     gc.collect()
     gc.disable()          # no collector pause inside the timed steps
-    ev0.record(stream)
-    marks[0].record(stream)
-    h0 = time.perf_counter()
-    for i in range(args.steps):
-        out = step_device()
-        marks[i + 1].record(stream)
-    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps   # enqueue time per step
-    ev1.record(stream)
+    if graph is not None:
+        ev0.record(stream)
+        h0 = time.perf_counter()
+        graph.replay()
+        host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
+        ev1.record(stream)
+    else:
+        l0 = _lib.launch_count()
+        ev0.record(stream)
+        marks[0].record(stream)
+        h0 = time.perf_counter()
+        for i in range(args.steps):
+            out = step_device()
+            marks[i + 1].record(stream)
+        host_ms = (time.perf_counter() - h0) * 1e3 / args.steps   # enqueue time per step
+        ev1.record(stream)
     torch.cuda.synchronize()
     gc.enable()
-    step_ms = [marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)]
-    launches = _lib.launch_count() - l0
+    if graph is None:
+        launches = _lib.launch_count() - l0
+        step_ms = [marks[i].elapsed_time(marks[i + 1]) for i in range(args.steps)]
     clk = clocks.stop()
     barrier()
     ms = ev0.elapsed_time(ev1) / args.steps
     kt = plan.timings()
     plan.set_timing(False)
+    graph_used = graph is not None
+    if graph is not None:
+        # per-step device time from the kernels of each call (the first kernel
+        # of a call is its frame set-up)
+        step_ms, acc = [], None
+        for name, t in kt:
+            if name == "frame_setup":
+                if acc is not None:
+                    step_ms.append(acc)
+                acc = 0.0
+            acc = (acc or 0.0) + t
+        if acc is not None:
+            step_ms.append(acc)
     ms_all = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(ms_all, op=dist.ReduceOp.MAX)
@@ -632,12 +676,30 @@ def run_gpu(args, rank: int, world: int):
     for _ in range(max(1, args.warmup)):
         step_e2e()
     torch.cuda.synchronize()
+    g_e2e = None
+    if graph is not None:
+        del graph                      # its memory pool is no longer needed
+        g_e2e = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.graph(g_e2e):
+                for _ in range(args.steps):
+                    step_e2e()
+            g_e2e.replay()
+            torch.cuda.synchronize()
+        except Exception as exc:
+            print(f"rank {rank}: CUDA graph capture of the e2e step failed ({exc})", file=sys.stderr,
+                  flush=True)
+            g_e2e = None
+            torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        step_e2e()
+    if g_e2e is not None:
+        g_e2e.replay()
+    else:
+        for _ in range(args.steps):
+            step_e2e()
     e1.record(stream)
     torch.cuda.synchronize()
     ms_e2e = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=dev)
@@ -720,6 +782,7 @@ def run_gpu(args, rank: int, world: int):
         "kernels": kernels,
         "gpu_launches": int(launches),
         "host_enqueue_ms_per_step": host_ms,
+        "cuda_graph": {"device": graph_used, "e2e": g_e2e is not None},
         "step_ms": [round(x, 4) for x in step_ms],
         "clocks": clk,
         "cpu_baseline": cpu,
@@ -739,6 +802,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--transport", default="peer", choices=["peer", "exchange"],
                     help="slab mode: NVLink stores from the FFT kernels (peer) or NCCL all-to-all")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch the timed steps one by one instead of replaying a CUDA graph")
     ap.add_argument("--mode", default="slab", choices=["slab", "frames"],
                     help="N>1: split one system's mesh over the GPUs (slab) or give each GPU "
                          "its own system (frames)")

@@ -94,7 +94,10 @@ SOG_API int sog_plan_status(sog_plan *plan, unsigned *bits);
 /* Per-kernel timing: when on, each forward records a CUDA event on the
  * caller's stream after every kernel.  sog_plan_timings waits for the last
  * event, returns up to `cap` (kernel name, ms) pairs of all calls since the
- * previous read (or since timing was switched on) and clears them. */
+ * previous read (or since timing was switched on) and clears them.  Switching
+ * timing on creates a pool of max(2048, on) events, so that calls captured
+ * into a CUDA graph (which record one event per kernel per call) create none;
+ * a replayed graph re-records its events, so read once per replay. */
 SOG_API int sog_plan_set_timing(sog_plan *plan, int on);
 SOG_API int sog_plan_timings(sog_plan *plan, const char **names, float *ms, int cap, int *count);
 

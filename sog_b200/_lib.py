@@ -171,8 +171,11 @@ class Plan:
         except Exception:
             pass
 
-    def set_timing(self, on: bool) -> None:
-        check(load().sog_plan_set_timing(self.handle, int(on)), "sog_plan_set_timing")
+    def set_timing(self, on, events: int = 0) -> None:
+        """Per-kernel event timing on / off; `events` sizes the event pool
+        (for calls captured into a CUDA graph)."""
+        check(load().sog_plan_set_timing(self.handle, max(int(bool(on)), int(events) if on else 0)),
+              "sog_plan_set_timing")
 
     def timings(self):
         """[(kernel name, ms)] of the latest forward (waits for it)."""

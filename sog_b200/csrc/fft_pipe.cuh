@@ -6,6 +6,7 @@
 // HBM traffic overlaps the radix-8 arithmetic.  The transform itself is the
 // register Stockham of fft_reg.cuh, with its exchanges in a third buffer.
 #pragma once
+#include <type_traits>
 #include "fft_reg.cuh"
 
 namespace sogb {
@@ -262,17 +263,26 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
       }
     }
     ct_fft<T, +1, L - 1, true, 1, (TPT <= 32)>(v, t, stg, xbuf + (size_t)(rr * F + f) * hp, 1);
-    // interleaved output straight from registers: the F fields of a row are
-    // written by the same CTA, so every sector is completed in L2
-    const int64_t row = tile * rpc + rr;
-    if (row < nrows) {
-      T *dst = out + row * n * F + f;
+    // interleave the F fields of the tile's rows in shared memory (the
+    // exchange buffer is free once every thread is past its transform), then
+    // store the tile's contiguous output with vector stores
+    __syncthreads();
+    T *so = reinterpret_cast<T *>(xbuf);
 #pragma unroll
-      for (int e = 0; e < kEPT; ++e) {
-        const int m = t + e * TPT;
-        dst[(2 * m) * F] = v[e].x;
-        dst[(2 * m + 1) * F] = v[e].y;
-      }
+    for (int e = 0; e < kEPT; ++e) {
+      const int m = t + e * TPT;
+      so[((size_t)rr * n + 2 * m) * F + f] = v[e].x;
+      so[((size_t)rr * n + 2 * m + 1) * F + f] = v[e].y;
+    }
+    __syncthreads();
+    {
+      using V2 = typename std::conditional<sizeof(T) == 8, double2, float2>::type;
+      const int64_t row0 = tile * rpc;
+      const int nv = (int)min((int64_t)rpc, nrows - row0);
+      const int cnt = nv * n * F / 2;
+      const V2 *src = reinterpret_cast<const V2 *>(so);
+      V2 *dst = reinterpret_cast<V2 *>(out + row0 * n * F);
+      for (int i = threadIdx.x; i < cnt; i += blockDim.x) dst[i] = src[i];
     }
     __syncthreads();
   }

@@ -125,7 +125,14 @@ void Tracer::mark(cudaStream_t st, const char *name) {
     names.push_back(nullptr);
   }
   names[used] = name;
-  cudaEventRecord(ev[used], st);
+  // inside a stream capture a plain record only orders captured streams;
+  // the external flag makes it an event-record node of the graph
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) cudaGetLastError();
+  if (cs == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(ev[used], st, cudaEventRecordExternal);
+  else
+    cudaEventRecord(ev[used], st);
   ++used;
 }
 
@@ -180,7 +187,7 @@ extern "C" int sog_plan_set_timing(sog_plan *p, int on) {
   p->tr.used = 0;
   if (p->tr.on) {
     sogb::DeviceGuard dg(p->d.device);
-    tracer_reserve(p->tr, 2048);
+    tracer_reserve(p->tr, on > 2048 ? on : 2048);
   }
   return SOG_OK;
 }
@@ -197,7 +204,7 @@ extern "C" int sog_direct_set_timing(sog_direct *d, int on) {
   d->tr.used = 0;
   if (d->tr.on) {
     sogb::DeviceGuard dg(d->device);
-    tracer_reserve(d->tr, 2048);
+    tracer_reserve(d->tr, on > 2048 ? on : 2048);
   }
   return SOG_OK;
 }
