@@ -1050,6 +1050,7 @@ __global__ void __launch_bounds__(256, 2) k_zfused(KsArgs<T> a, int ic, RadixPla
 // a register allocation of its own.
 template <typename T, bool SEP>
 __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
+  extern __shared__ __align__(16) double s_bzt[];   // separable path: [z][m] z factors
   __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
   __shared__ double red[8];
   for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
@@ -1066,6 +1067,16 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
   // z planes of this block: the columns are split over gridDim.z
   const int zper = (a.nz + gridDim.z - 1) / gridDim.z;
   const int izb = blockIdx.z * zper, ize = min(a.nz, izb + zper);
+  if constexpr (SEP) {
+    // the frame's z factors of this block's planes, transposed to [z][m]
+    const int M = a.M, mp = (M + 1) & ~1;
+    const double *bz = a.btab + (int64_t)f * a.btab_stride + (int64_t)M * (a.nxh + a.ny);
+    for (int i = threadIdx.x; i < (ize - izb) * mp; i += blockDim.x) {
+      const int zl = i / mp, m = i - zl * mp;
+      s_bzt[i] = m < M ? bz[m * a.nz + izb + zl] : 0.0;
+    }
+    __syncthreads();
+  }
   double accD = 0.0;
   int mx = 0, yl = 0;
   const bool valid = col < inner && col_mode(a, col, mx, yl);
@@ -1079,10 +1090,11 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
     double *gout = a.gtab + (int64_t)f * a.nh + col;
     if constexpr (SEP) {
       // separable path: K = sum_m amp_m (Bx_m By_m) Bz_m with the x-y
-      // products of up to 16 Gaussians held in registers
+      // products of up to 16 Gaussians held in registers and the block's z
+      // factors in shared memory, [z][m] (two per 16-byte load)
       const int M = a.M;
       const double *bt = a.btab + (int64_t)f * a.btab_stride;
-      const double *bx = bt, *by = bt + M * a.nxh, *bz = by + M * a.ny;
+      const double *bx = bt, *by = bt + M * a.nxh;
       double axy[16];
 #pragma unroll
       for (int m = 0; m < 16; ++m) axy[m] = m < M ? s_amp[m] * bx[m * a.nxh + mx] * by[m * a.ny + iy] : 0.0;
@@ -1090,6 +1102,7 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
       const double kxy2 = kx * kx + ky * ky;
       const double txy = a.tx[mx] * a.ty[iy];
       const bool quads = a.spline == SOG_SPLINE_QUADS;
+      const int mp = (M + 1) & ~1;
       for (int iz = izb; iz < ize; ++iz) {
         const int mz = signed_mode(iz, a.nz);
         const double kz = g.kmat[8] * mz;
@@ -1097,10 +1110,14 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
         const bool live = !((mx | iy | mz) == 0) && ksq <= g.k_sq_max;
         double K = 0.0;
         if (live) {
-          const double *bzi = bz + iz;
+          const double2 *row = reinterpret_cast<const double2 *>(s_bzt + (size_t)(iz - izb) * mp);
 #pragma unroll
-          for (int m = 0; m < 16; ++m)
-            if (m < M) K += axy[m] * bzi[m * a.nz];
+          for (int m2 = 0; m2 < 8; ++m2)
+            if (2 * m2 < M) {
+              const double2 v = row[m2];
+              K += axy[2 * m2] * v.x;
+              if (2 * m2 + 1 < M) K += axy[2 * m2 + 1] * v.y;
+            }
         }
         double D = txy * a.tz[iz];
         if (quads) D = 1.0 / (D < 1e-20 ? 1e-20 : D);
@@ -1798,10 +1815,17 @@ void launch_spread(const SpreadArgs<T> &sa, int nframes, cudaStream_t st, Tracer
 // z split of the Green-table pass when its (mx, y) columns do not fill one
 // wave of resident CTAs (two per SM); splitting a full wave further costs
 // more (the x-y kernel products are rebuilt per split) than it gains
+// Launches both Green kernels (separable frames, others) on one grid; the
+// separable one holds its planes' z factors in shared memory.
+template <typename T>
+void launch_green(const KsArgs<T> &ka, unsigned gblocks, int nf, unsigned gz, cudaStream_t st);
+
 inline unsigned green_zsplit(unsigned gblocks, int nf, int nz) {
   const int64_t have = (int64_t)gblocks * nf;
   const int64_t want = 2 * 148;
-  const int64_t gz = std::max<int64_t>(1, std::min<int64_t>({8, (want + have - 1) / have, (int64_t)nz}));
+  int64_t gz = std::max<int64_t>(1, std::min<int64_t>({8, (want + have - 1) / have, (int64_t)nz}));
+  // a block's z factors ([zper][16] doubles at most) stay within 96 KB
+  while ((nz + gz - 1) / gz * 16 * (int64_t)sizeof(double) > 96 * 1024) ++gz;
   return (unsigned)gz;
 }
 
@@ -1964,6 +1988,15 @@ int prepare_atoms(sog_plan *p, const sog_mesh_args *a, cudaStream_t st, Prep &pr
 }
 
 template <typename T>
+void launch_green(const KsArgs<T> &ka, unsigned gblocks, int nf, unsigned gz, cudaStream_t st) {
+  const int zper = (ka.nz + (int)gz - 1) / (int)gz;
+  const size_t sm = ka.M <= 16 ? (size_t)zper * ((ka.M + 1) & ~1) * sizeof(double) : 0;
+  allow_smem(k_green<T, true>);
+  k_green<T, true><<<dim3(gblocks, nf, gz), 256, sm, st>>>(ka);
+  k_green<T, false><<<dim3(gblocks, nf, gz), 256, 0, st>>>(ka);
+}
+
+template <typename T>
 int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   using C = cplx_t<T>;
   const int nf = a->nframes, nch = a->nchannels, M = a->n_gauss;
@@ -2091,8 +2124,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
     ka.gtab = p->gtab.as<double>();
     ka.gtabF = aliasable ? p->gtabF.as<double>() : nullptr;
     ka.partD = p->partD.as<double>();
-    k_green<T, true><<<dim3(gblocks, nf, gz), 256, 0, st>>>(ka);
-    k_green<T, false><<<dim3(gblocks, nf, gz), 256, 0, st>>>(ka);
+    launch_green<T>(ka, gblocks, nf, gz, st);
     count_launch();
     after(tr, st, "green");
     redD = ka.partD + gparts * nf;
@@ -2456,8 +2488,7 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
     ka.gtab = p->gtab.as<double>();
     ka.gtabF = aliasable ? p->gtabF.as<double>() : nullptr;
     ka.partD = p->partD.as<double>();
-    k_green<T, true><<<dim3(gblocks, 1, gz), 256, 0, st>>>(ka);
-    k_green<T, false><<<dim3(gblocks, 1, gz), 256, 0, st>>>(ka);
+    launch_green<T>(ka, gblocks, 1, gz, st);
     count_launch();
     after(tr, st, "green");
     reduce_parts(ka.partD, 1, 1, gparts, 1, 1, red + 2 * nch, ka.partD + gparts + 1, st);
