@@ -47,8 +47,33 @@ struct QuadsCoef {
 // ------------------------------------------------------------------------
 struct AtomGrid {
   int nx, ny, nz, first, nbx, nby, nbz;
+  int zb;             // z bin layers per block of the bin order (1: plain z-major)
   uint32_t bins_per_frame;
 };
+
+// Bin order: blocks of zb bin layers along z; inside a block the (y, z) rows
+// run y-major, and the x bins of a row are consecutive (the spread's segment
+// table relies on that).  A stencil's z neighbours inside a block are one row
+// apart, so the gather (atoms in bin order) finds them in L2.
+__host__ __device__ __forceinline__ uint32_t bin_row(const AtomGrid &ag, int bz, int by) {
+  const int B = bz / ag.zb, zl = bz - B * ag.zb;
+  const int zbe = min(ag.zb, ag.nbz - B * ag.zb);
+  return ((uint32_t)B * ag.zb * ag.nby + (uint32_t)by * zbe + zl) * ag.nbx;
+}
+
+#ifndef SOG_BIN_ZB
+#define SOG_BIN_ZB 1
+#endif
+// resident blocks per SM the register allocation of these kernels aims at
+#ifndef SOG_GATHER_MINB
+#define SOG_GATHER_MINB 1
+#endif
+#ifndef SOG_ZFUSED_MINB
+#define SOG_ZFUSED_MINB 2
+#endif
+#ifndef SOG_SPREAD_MINB
+#define SOG_SPREAD_MINB 3
+#endif
 
 // Fractional coordinate along axis a (r @ cell^-1, then remainder 1.0) and the
 // anchor (first stencil node, wrapped) with the in-cell offset t
@@ -88,8 +113,7 @@ __global__ void k_atom_bin(const T *__restrict__ pos, const T *__restrict__ q, i
   for (int c = 0; c < nch; ++c)
     if (!isfinite((double)q[atom * nch + c])) ok = false;
   if (!ok) raise_status(status, kStatusNonFinite);
-  const uint32_t key = (uint32_t)f * ag.bins_per_frame +
-                       ((uint32_t)(az / kBin) * ag.nby + (uint32_t)(ay / kBin)) * ag.nbx + (uint32_t)(ax / kBin);
+  const uint32_t key = (uint32_t)f * ag.bins_per_frame + bin_row(ag, az / kBin, ay / kBin) + (uint32_t)(ax / kBin);
   const int64_t slot = g.slot_base + i;
   keys[slot] = key;
   vals[slot] = (int32_t)slot;
@@ -324,7 +348,7 @@ __device__ int axis_bins(int lo, int len, int n, int nb, int *out) {
 // CubeS2 order 4 / 6.  CH candidates per chunk (fewer with three kinds, to
 // keep the staged weights at two CTAs per SM).
 template <typename T, int P, int NT = 1>
-__global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? 3 : 2) k_spread(SpreadArgs<T> a) {
+__global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? SOG_SPREAD_MINB : 2) k_spread(SpreadArgs<T> a) {
   using ST = StencilTerms<NT>;
   constexpr int KK = ST::K;
   constexpr int CH = KK == 3 ? kSpreadThreads / 2 : kSpreadThreads;
@@ -379,8 +403,7 @@ __global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? 3 : 2) k_spread(Spre
     uint32_t lo2[2] = {0, 0}, cnt2[2] = {0, 0};
     if (lane < nzl * nyl) {
       const int iz = lane / nyl, iy = lane - iz * nyl;
-      const uint32_t row = (uint32_t)f * ag.bins_per_frame +
-                           ((uint32_t)bl[2][iz] * ag.nby + (uint32_t)bl[1][iy]) * ag.nbx;
+      const uint32_t row = (uint32_t)f * ag.bins_per_frame + bin_row(ag, bl[2][iz], bl[1][iy]);
       // x bins are ascending with at most one break
       int brk = nxl;
       for (int i = 1; i < nxl; ++i)
@@ -1150,7 +1173,7 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
 // every field the scaled spectrum (i k_a gF rho / N or gE rho / N) inverse
 // z-transformed.  Spectrum and gE tiles are double-buffered with cp.async.
 template <typename T, int L>
-__global__ void __launch_bounds__(256, 2) k_zfused_g(KsArgs<T> a, int ic, int64_t ntiles,
+__global__ void __launch_bounds__(256, SOG_ZFUSED_MINB) k_zfused_g(KsArgs<T> a, int ic, int64_t ntiles,
                                                      const cplx_t<T> *__restrict__ twz, int write_spec) {
   using C = cplx_t<T>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -1401,7 +1424,7 @@ struct GatherArgs {
 // NT stencil terms as in k_spread (the weight of node (k, b, c) is
 // sum_t X_t[k] Y_t[b] Z_t[c]).
 template <typename T, int P, int NT = 1>
-__global__ void __launch_bounds__(256) k_gather(GatherArgs<T> a) {
+__global__ void __launch_bounds__(256, SOG_GATHER_MINB) k_gather(GatherArgs<T> a) {
   using ST = StencilTerms<NT>;
   const int64_t si = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (si >= a.nslots) return;
@@ -1871,7 +1894,7 @@ struct Prep {
 };
 
 template <typename T>
-int prepare_atoms(sog_plan *p, const sog_mesh_args *a, cudaStream_t st, Prep &pr) {
+int prepare_atoms(sog_plan *p, const sog_mesh_args *a, cudaStream_t st, Prep &pr, int zb = SOG_BIN_ZB) {
   const int nf = a->nframes, nch = a->nchannels;
   const int nx = p->d.nx, ny = p->d.ny, nz = p->d.nz, P = p->d.order;
   Tracer *tr = &p->tr;
@@ -1925,6 +1948,7 @@ int prepare_atoms(sog_plan *p, const sog_mesh_args *a, cudaStream_t st, Prep &pr
   // CubeS2 (offsets -1..2 / -2..3, cubes2_spline.py), - (P-1)/2 for B-splines
   ag.first = (p->d.spline == SOG_SPLINE_BSPLINE) ? -((P - 1) / 2) : (1 - P / 2);
   ag.nbx = p->nb_x; ag.nby = p->nb_y; ag.nbz = p->nb_z;
+  ag.zb = std::max(1, std::min(zb, ag.nbz));
   ag.bins_per_frame = (uint32_t)ag.nbx * ag.nby * ag.nbz;
   const uint64_t nbins64 = (uint64_t)ag.bins_per_frame * nf;
   if (nbins64 >= (1ull << 32) - 1) return fail(SOG_ERR_INVALID, "too many sort bins in one call");
@@ -2405,7 +2429,8 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
   }
 
   Prep pr;
-  int rc = prepare_atoms<T>(p, a, st, pr);
+  // slab ranks take z ranges of bins: plain z-major bin order
+  int rc = prepare_atoms<T>(p, a, st, pr, 1);
   if (rc != SOG_OK) return rc;
   FrameGeom *geom = pr.geom;
   const AtomGrid ag = pr.ag;
