@@ -1172,12 +1172,16 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
 // table: forward z-FFT of ic spectrum columns, energy partial sum, and for
 // every field the scaled spectrum (i k_a gF rho / N or gE rho / N) inverse
 // z-transformed.  Spectrum and gE tiles are double-buffered with cp.async.
-template <typename T, int L>
-__global__ void __launch_bounds__(256, SOG_ZFUSED_MINB) k_zfused_g(KsArgs<T> a, int ic, int64_t ntiles,
+// NTH threads per CTA: 512 for a 512-point z transform gives tiles of 8
+// columns, so every field row it stores is 128 contiguous bytes (4-column
+// rows of 64 bytes store at half the bandwidth).
+template <typename T, int L, int NTH = 256>
+__global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfused_g(KsArgs<T> a, int ic,
+                                                                                  int64_t ntiles,
                                                      const cplx_t<T> *__restrict__ twz, int write_spec) {
   using C = cplx_t<T>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ double red[8];
+  __shared__ double red[NTH / 32];
   constexpr int n = 1 << L, TPT = n / kEPT;
   C *buf0 = reinterpret_cast<C *>(smem_raw);
   C *buf1 = buf0 + (size_t)n * ic;
@@ -1238,42 +1242,70 @@ __global__ void __launch_bounds__(256, SOG_ZFUSED_MINB) k_zfused_g(KsArgs<T> a, 
     const double *gFp = (g.pad && a.gtabF) ? a.gtabF + (int64_t)f * a.nh + (ok ? col : 0) : nullptr;
     C *out = a.fspec ? a.fspec + (int64_t)f * nfield * a.nh + (ok ? col : 0) : nullptr;
     const int64_t zbs = (int64_t)a.zblk * inner;   // one field's z block
-    for (int fl = 0; fl < nfield; ++fl) {
-      const bool force = a.want_force && fl < 3;
-      double km = 0.0, kz = 0.0;
-      if (force) {
-        km = g.kmat[fl * 3 + 0] * mx + g.kmat[fl * 3 + 1] * my;
-        kz = g.kmat[fl * 3 + 2];
+    auto store_field = [&](int fl, const C (&wv)[kEPT]) {
+      if (!ok) return;
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) {
+        const int iz = t + e * TPT, b = iz / a.zblk, zl = iz - b * a.zblk;
+        if (a.cw) {
+          // chunked: this tile's cw columns are contiguous for every z
+          const int64_t q = col / a.cw;
+          a.zdst[b][(int64_t)fl * zbs + (q * a.zblk + zl) * a.cw + (col - q * a.cw)] = wv[e];
+        } else {
+          C *ob = a.zdst[0] ? a.zdst[b] + (int64_t)fl * zbs + col : out + ((int64_t)b * nfield + fl) * zbs;
+          ob[(int64_t)zl * inner] = wv[e];
+        }
       }
-      C wv[kEPT];
+    };
+    // The ik field spectra along this column are i k_a s rho with
+    // k_a = kxy_a + kz_a mz and kxy_a fixed on the column, so two inverse
+    // transforms serve all three: Y1 = IFFT(s rho), Y2 = IFFT(i mz s rho),
+    // field a = i kxy_a Y1 + kz_a Y2.  The potential field (s = gE) is Y1
+    // itself unless the force uses the alias-summed gF.
+    bool pot_done = !(nfield > (a.want_force ? 3 : 0));
+    if (a.want_force) {
+      C y1[kEPT], y2[kEPT];
 #pragma unroll
       for (int e = 0; e < kEPT; ++e) {
         const int slot = (t + e * TPT) * ic + c;
         const C r = cur[slot];
-        const double rr = (double)r.x, ri = (double)r.y;
-        if (force) {
-          const double kc = km + kz * signed_mode(t + e * TPT, a.nz);
-          const double sc = gFp ? (ok ? gFp[(int64_t)(t + e * TPT) * inner] * inv : 0.0) : gs[e];
-          wv[e] = cmk<C, T>((T)(-kc * sc * ri), (T)(kc * sc * rr));
-        } else {
-          wv[e] = cmk<C, T>((T)(gs[e] * rr), (T)(gs[e] * ri));
-        }
+        const double sc = gFp ? (ok ? gFp[(int64_t)(t + e * TPT) * inner] * inv : 0.0) : gs[e];
+        y1[e] = cmk<C, T>((T)(sc * (double)r.x), (T)(sc * (double)r.y));
+      }
+      ct_fft<T, +1, L, true>(y1, t, stg, xbuf + c, ic);
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) {
+        const int slot = (t + e * TPT) * ic + c;
+        const C r = cur[slot];
+        const double sc = gFp ? (ok ? gFp[(int64_t)(t + e * TPT) * inner] * inv : 0.0) : gs[e];
+        const double mzs = (double)signed_mode(t + e * TPT, a.nz) * sc;
+        y2[e] = cmk<C, T>((T)(-mzs * (double)r.y), (T)(mzs * (double)r.x));
+      }
+      ct_fft<T, +1, L, true>(y2, t, stg, xbuf + c, ic);
+      for (int fl = 0; fl < 3; ++fl) {
+        const double kxy = g.kmat[fl * 3 + 0] * mx + g.kmat[fl * 3 + 1] * my;
+        const double kz = g.kmat[fl * 3 + 2];
+        C wv[kEPT];
+#pragma unroll
+        for (int e = 0; e < kEPT; ++e)
+          wv[e] = cmk<C, T>((T)(-kxy * (double)y1[e].y + kz * (double)y2[e].x),
+                            (T)(kxy * (double)y1[e].x + kz * (double)y2[e].y));
+        store_field(fl, wv);
+      }
+      if (!pot_done && !gFp) {
+        store_field(3, y1);
+        pot_done = true;
+      }
+    }
+    if (!pot_done) {
+      C wv[kEPT];
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) {
+        const C r = cur[(t + e * TPT) * ic + c];
+        wv[e] = cmk<C, T>((T)(gs[e] * (double)r.x), (T)(gs[e] * (double)r.y));
       }
       ct_fft<T, +1, L, true>(wv, t, stg, xbuf + c, ic);
-      if (ok) {
-#pragma unroll
-        for (int e = 0; e < kEPT; ++e) {
-          const int iz = t + e * TPT, b = iz / a.zblk, zl = iz - b * a.zblk;
-          if (a.cw) {
-            // chunked: this tile's cw columns are contiguous for every z
-            const int64_t q = col / a.cw;
-            a.zdst[b][(int64_t)fl * zbs + (q * a.zblk + zl) * a.cw + (col - q * a.cw)] = wv[e];
-          } else {
-            C *ob = a.zdst[0] ? a.zdst[b] + (int64_t)fl * zbs + col : out + ((int64_t)b * nfield + fl) * zbs;
-            ob[(int64_t)zl * inner] = wv[e];
-          }
-        }
-      }
+      store_field(a.want_force ? 3 : 0, wv);
     }
     accE = warp_sum(accE);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = accE;
@@ -2129,7 +2161,10 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   // k_kspace_tab.  Both read the Green tables k_green writes once per call.
   const bool zfuse = is_pow2(nz);
   const bool zgeneric = zfuse && nz > 1024;  // runtime-plan fused pass, Green on the fly
-  const int zic = zfuse ? reg_width<T>(nz, 256, 32 * 1024) : 0;
+  // fused z pass: 512 threads (8-column tiles) for 512 and 1024 points
+  const int zic = zfuse ? (nz >= 512 && nz <= 1024 ? reg_width<T>(nz, 512, 64 * 1024)
+                                                   : reg_width<T>(nz, 256, 32 * 1024))
+                        : 0;
   const int64_t zchunks = zfuse ? ((int64_t)ny * nxh + zic - 1) / zic : 0;
   const unsigned tblocks = nblocks((int64_t)ny * nxh, 256);
   const unsigned tz = green_zsplit(tblocks, nf, nz);
@@ -2163,9 +2198,15 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
       const int zthr = (n / kEPT) * zic;
       const size_t zsm = ((2 * (size_t)n + padded_row(n)) * zic + n) * sizeof(C);
       const int64_t ztiles = zchunks * nf;
-      allow_smem(k_zfused_g<T, L>);
-      k_zfused_g<T, L><<<persistent_grid(k_zfused_g<T, L>, zthr, zsm, ztiles), zthr, zsm, st>>>(
-          ka, zic, ztiles, p->twz.as<C>(), write_spec);
+      if (zthr == 512) {
+        allow_smem(k_zfused_g<T, L, 512>);
+        k_zfused_g<T, L, 512><<<persistent_grid(k_zfused_g<T, L, 512>, zthr, zsm, ztiles), zthr, zsm, st>>>(
+            ka, zic, ztiles, p->twz.as<C>(), write_spec);
+      } else {
+        allow_smem(k_zfused_g<T, L>);
+        k_zfused_g<T, L><<<persistent_grid(k_zfused_g<T, L>, zthr, zsm, ztiles), zthr, zsm, st>>>(
+            ka, zic, ztiles, p->twz.as<C>(), write_spec);
+      }
     });
     if (!done) {
       const size_t zsm = (size_t)padded_row(nz) * zic * sizeof(C) +
