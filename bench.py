@@ -54,6 +54,11 @@ def workload(name: str):
         return dict(workload="1/8-scale large system: 131,072 atoms, 110 A cubic, 256^3 mesh, "
                              "B-spline order 6, 12 Gaussians bw 1.2-60 A", natoms=1 << 17, L=110.0,
                     n_dl=0.86, order=6, m=12, bw_lo=1.2, bw_hi=60.0, qstd=0.6)
+    if name == "cfg5_quarter":
+        return dict(workload="quarter-height slab of the large system: 262,144 atoms, 220 x 220 x 55 A, "
+                             "512 x 512 x 128 mesh, B-spline order 6, 12 Gaussians bw 1.2-60 A "
+                             "(profiling case: about 3 GB on the device)", natoms=1 << 18, L=220.0,
+                    box=(220.0, 220.0, 55.0), n_dl=0.86, order=6, m=12, bw_lo=1.2, bw_hi=60.0, qstd=0.6)
     if name == "cfg2":
         return dict(workload="water-like box: 3,000 atoms, 31 A cubic, 64^3 mesh, B-spline order 6, "
                              "12 Gaussians bw 1.2*1.62^m", natoms=3000, L=31.0, n_dl=1.0, order=6,
@@ -108,7 +113,8 @@ def make_inputs(cfg, seed: int):
     import numpy as np
     rng = np.random.default_rng(seed)
     n, L = cfg["natoms"], cfg["L"]
-    r = rng.random((n, 3)) * L
+    box = np.array(cfg.get("box", (L, L, L)))
+    r = rng.random((n, 3)) * box
     if cfg.get("qstd"):
         q = rng.standard_normal(n) * cfg["qstd"]
     else:
@@ -120,31 +126,35 @@ def make_inputs(cfg, seed: int):
     else:
         bw = np.logspace(math.log10(cfg["bw_lo"]), math.log10(cfg["bw_hi"]), cfg["m"])
     amp_raw = 1.0 / (bw * math.sqrt(2.0 * math.pi))
-    cell = np.eye(3) * L
+    cell = np.diag(box)
     return r, q, cell, amp_raw, bw
 
 
 def mesh_dims(cfg):
-    nk = int(math.floor(cfg["L"] / cfg["n_dl"]))
-    n = 2 * nk + 1
-    while True:
-        m = n
-        for p in (2, 3, 5):
-            while m % p == 0:
-                m //= p
-        if m == 1:
-            return n
-        n += 1
+    """(nx, ny, nz) of the n_dl grid rule for the workload's box."""
+    dims = []
+    for L in cfg.get("box", (cfg["L"],) * 3):
+        n = 2 * int(math.floor(L / cfg["n_dl"])) + 1
+        while True:
+            m = n
+            for p in (2, 3, 5):
+                while m % p == 0:
+                    m //= p
+            if m == 1:
+                break
+            n += 1
+        dims.append(n)
+    return tuple(dims)
 
 
 def algorithmic_bytes(cfg, s: int = 8, nfield: int = 3, parts: int = 1):
     """Minimal-pipeline bytes per evaluation (each array once per producer /
     consumer pass) and per kernel launch; with the mesh split into `parts`
     slabs, the per-launch figures of one rank."""
-    n = mesh_dims(cfg)
+    nx, ny, nz = mesh_dims(cfg)
     N = cfg["natoms"]
-    ng = n ** 3
-    nh = n * n * (n // 2 + 1)
+    ng = nx * ny * nz
+    nh = nz * ny * (nx // 2 + 1)
     per_kernel = {
         "spread": s * ng + 4 * s * N,
         "fft_r2c_x": s * ng + 2 * s * nh,
@@ -274,14 +284,14 @@ def oracle_eval_time(cfg_name: str, reps: int, warm: int = 1):
     from oracle import oracle as O
     cfg = workload(cfg_name)
     r, q, cell, amp_raw, bw = make_inputs(cfg, 0)
-    n = mesh_dims(cfg)
+    nx, ny, nz = mesh_dims(cfg)
     amp = amp_raw * bw * bw
     ksm = (2.0 * math.pi / cfg["n_dl"]) ** 2
     times = []
     for i in range(warm + reps):
         t0 = time.perf_counter()
-        O.mesh_solve(r, q, cell, amp, bw * bw, spline=O.BSPLINE, order=cfg["order"], nx=n, ny=n,
-                     nz=n, k_sq_max=ksm, want_force=True)
+        O.mesh_solve(r, q, cell, amp, bw * bw, spline=O.BSPLINE, order=cfg["order"], nx=nx, ny=ny,
+                     nz=nz, k_sq_max=ksm, want_force=True)
         dt = time.perf_counter() - t0
         if i >= warm:
             times.append(dt)
@@ -536,7 +546,7 @@ def run_gpu(args, rank: int, world: int):
     # slab: every rank holds the same system and its mesh is split over the
     # ranks; frames: every rank solves its own system (seeded by rank)
     r, q, cell, amp_raw, bw = make_inputs(cfg, seed=0 if slab else rank)
-    n = mesh_dims(cfg)
+    dims = mesh_dims(cfg)
     N = cfg["natoms"]
     transport = args.transport
 
@@ -576,7 +586,7 @@ def run_gpu(args, rank: int, world: int):
     for _ in range(args.warmup - 1):
         step_device()
     torch.cuda.synchronize()
-    plan = next(p for p in _lib.PLANS.plans.values() if p.key[4] == (n, n, n))
+    plan = next(p for p in _lib.PLANS.plans.values() if p.key[4] == dims)
 
     # ---- device-resident timed region ----
     # Without a collective inside the step (one GPU, or independent systems
@@ -745,8 +755,9 @@ def run_gpu(args, rank: int, world: int):
     if slab:
         # bytes each rank sends per evaluation: (P-1)/P of its spectrum share
         # forward and of its three field shares back, plus the halo planes
-        share = (n // world) * n * (n // 2 + 1) * 2 * s
-        sent = (share + 3 * share) * (world - 1) / world + (cfg["order"] - 1) * n * n * 3 * s
+        nx, ny, nz = dims
+        share = (nz // world) * ny * (nx // 2 + 1) * 2 * s
+        sent = (share + 3 * share) * (world - 1) / world + (cfg["order"] - 1) * nx * ny * 3 * s
         ex_ms = sum(v["total_ms"] for k, v in kernels.items()
                     if k.startswith("exchange") or k.startswith("barrier")) / args.steps
         nvlink = {"bytes_per_rank_per_step": sent, "exchange_ms_per_step": ex_ms,
@@ -770,7 +781,7 @@ def run_gpu(args, rank: int, world: int):
         "scaling": "strong" if slab else "weak", "vs_baseline": None, "dtype": args.dtype,
         "data": "synthetic (seeded)",
         "config": {"workload": cfg["workload"], "atoms_per_gpu": N // world if slab else N,
-                   "mesh": [n, n, n], "spline": f"bspline{cfg['order']}", "gaussians": cfg["m"],
+                   "mesh": list(dims), "spline": f"bspline{cfg['order']}", "gaussians": cfg["m"],
                    "parallelism": parallelism,
                    "l2": "inputs and mesh arrays larger than L2 (>= 1 GB each)"},
         "e2e": {"value": systems * N / (ms_e2e * 1e-3), "unit": UNIT, "ms_per_step": ms_e2e,
@@ -797,7 +808,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="sog_b200", choices=["sog_b200", "reference"])
-    ap.add_argument("--config", default="cfg5", choices=["cfg5", "cfg5_eighth", "cfg2", "cfg4"])
+    ap.add_argument("--config", default="cfg5", choices=["cfg5", "cfg5_eighth", "cfg5_quarter", "cfg2", "cfg4"])
     ap.add_argument("--dtype", default="f64", choices=["f64", "f32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--transport", default="peer", choices=["peer", "exchange"],
