@@ -195,12 +195,15 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
   extern __shared__ __align__(16) unsigned char smem_raw[];
   constexpr int n = 1 << L, h = n / 2, TPT = h / kEPT, nxh = h + 1;
   constexpr int hp = padded_row(h);
-  // three input buffers: tiles i+1 and i+2 are in flight while tile i is
-  // transformed
-  const size_t tsz = (size_t)rpc * F * nxh;
+  // Two tile buffers: tile i+1 is in flight while tile i is transformed.  A
+  // row's slot is wide enough for its exchanges (hp) as well as its input
+  // (nxh): once the inputs are in registers the slot serves the transform's
+  // exchanges and then the interleaved output, so no third buffer is needed
+  // and three CTAs fit on an SM.
+  constexpr int rowsz = hp > nxh ? hp : nxh;
+  const size_t tsz = (size_t)rpc * F * rowsz;
   C *bufs = reinterpret_cast<C *>(smem_raw);
-  C *xbuf = bufs + 3 * tsz;  // exchanges of the row transforms
-  C *stw = xbuf + (size_t)rpc * F * hp;  // n-th roots of unity (pre-processing)
+  C *stw = bufs + 2 * tsz;                 // n-th roots of unity (pre-processing)
   C *stg = stw + n;                        // stage table of the length n/2 transform
   load_twiddles<T>(stw, tw, n);
   load_stage_twiddles<T, L - 1, 1>(stg, tw);
@@ -222,7 +225,7 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
     const C *rsrc = row_src(r2, f2);
     for (int qq = threadIdx.x; qq < total; qq += blockDim.x) {
       const bool ok = row0 + r2 < nrows;
-      cp_async_elem(buf + qq, ok ? rsrc + col : in, ok);
+      cp_async_elem(buf + (size_t)(r2 * F + f2) * rowsz + col, ok ? rsrc + col : in, ok);
       col += blockDim.x;
       if (col >= nxh) {
         do {
@@ -236,16 +239,14 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
   int64_t tile = blockIdx.x;
   if (tile < ntiles) issue(bufs, tile);
   cp_async_commit();
-  if (tile + gridDim.x < ntiles) issue(bufs + tsz, tile + gridDim.x);
-  cp_async_commit();
   for (int it = 0; tile < ntiles; ++it, tile += gridDim.x) {
-    const C *cur = bufs + (size_t)(it % 3) * tsz;
-    const int64_t next = tile + 2 * (int64_t)gridDim.x;
-    if (next < ntiles) issue(bufs + (size_t)((it + 2) % 3) * tsz, next);
+    C *cur = bufs + (size_t)(it & 1) * tsz;
+    const int64_t next = tile + gridDim.x;
+    if (next < ntiles) issue(bufs + (size_t)((it + 1) & 1) * tsz, next);
     cp_async_commit();
-    cp_async_wait<2>();
+    cp_async_wait<1>();
     __syncthreads();
-    const C *X = cur + (size_t)(rr * F + f) * nxh;
+    C *X = cur + (size_t)(rr * F + f) * rowsz;
     C v[kEPT];
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) {
@@ -262,12 +263,13 @@ __global__ void k_c2r_pipe(const cplx_t<T> *__restrict__ in, T *__restrict__ out
         v[e] = cmk<C, T>(Ar - ci, Ai + cr);          // A + i conj(w) B
       }
     }
-    ct_fft<T, +1, L - 1, true, 1, (TPT <= 32)>(v, t, stg, xbuf + (size_t)(rr * F + f) * hp, 1);
-    // interleave the F fields of the tile's rows in shared memory (the
-    // exchange buffer is free once every thread is past its transform), then
-    // store the tile's contiguous output with vector stores
+    __syncthreads();   // the tile's inputs are in registers: its slots become exchange space
+    ct_fft<T, +1, L - 1, true, 1, (TPT <= 32)>(v, t, stg, X, 1);
+    // interleave the F fields of the tile's rows in the same slots (free once
+    // every thread is past its transform), then store the tile's contiguous
+    // output with vector stores
     __syncthreads();
-    T *so = reinterpret_cast<T *>(xbuf);
+    T *so = reinterpret_cast<T *>(cur);
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) {
       const int m = t + e * TPT;

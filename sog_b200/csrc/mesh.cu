@@ -1768,7 +1768,8 @@ void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nframes, int64_
     const int64_t ntiles = (rows + rpc - 1) / rpc;
     const int nxh = n / 2 + 1;
     const int thr = tpt * F * rpc;
-    const size_t sm = (3 * (size_t)rpc * F * nxh + (size_t)rpc * F * padded_row(n / 2) + n + n / 2) * sizeof(C);
+    const size_t rowsz = std::max<size_t>(nxh, padded_row(n / 2));
+    const size_t sm = (2 * (size_t)rpc * F * rowsz + n + n / 2) * sizeof(C);
     allow_smem(k_c2r_pipe<T, L>);
     k_c2r_pipe<T, L><<<persistent_grid(k_c2r_pipe<T, L>, thr, sm, ntiles), thr, sm, st>>>(
         fspec, freal, F, nzy, rows, rpc, ntiles, p->twx.as<C>());
