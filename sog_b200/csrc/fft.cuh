@@ -14,7 +14,18 @@ struct RadixPlan {
   int n;
   int nst;
   int r[24];
+  // per stage s: n / r[s] and the stride Ns (product of the earlier radices),
+  // each with the multiplier of exact division by it for the small indices of
+  // a transform, q = umulhi(x, m) for m = floor(2^32 / d) + 1, exact for
+  // x < 2^32 / d (Granlund and Montgomery's round-up method)
+  int nR[24], Ns[24];
+  uint32_t m_nR[24], m_Ns[24];
 };
+
+__host__ __device__ __forceinline__ uint32_t fdiv_mul(uint32_t d) {
+  return (uint32_t)((((uint64_t)1) << 32) / d + 1);
+}
+__device__ __forceinline__ int fdiv(int x, uint32_t m) { return (int)__umulhi((uint32_t)x, m); }
 
 // DFT of radix R in registers; DIR = -1 forward (e^{-i}), +1 inverse.
 template <typename T, int DIR>
@@ -101,17 +112,16 @@ __device__ __forceinline__ void dft8(cplx_t<T> *v) {
 }
 
 template <typename T, int DIR, int R>
-__device__ __forceinline__ void stage_body(const cplx_t<T> *src, cplx_t<T> *dst, int n, int Ns,
-                                           int j, int b, int sj, int sb,
+__device__ __forceinline__ void stage_body(const cplx_t<T> *src, cplx_t<T> *dst, int nR, int Ns, uint32_t mNs,
+                                           int step, int j, int b, int sj, int sb,
                                            const cplx_t<T> *__restrict__ tw) {
   using C = cplx_t<T>;
-  const int nR = n / R;
   C v[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) v[r] = src[(j + r * nR) * sj + b * sb];
-  const int k = j % Ns;
+  const int jq = Ns > 1 ? fdiv(j, mNs) : j;
+  const int k = j - jq * Ns;
   if (Ns > 1) {
-    const int step = n / (Ns * R);
 #pragma unroll
     for (int r = 1; r < R; ++r) {
       C w = tw[r * k * step];
@@ -124,7 +134,7 @@ __device__ __forceinline__ void stage_body(const cplx_t<T> *src, cplx_t<T> *dst,
   else if (R == 4) dft4<T, DIR>(v);
   else if (R == 5) dft5<T, DIR>(v);
   else dft8<T, DIR>(v);
-  const int idxD = (j / Ns) * Ns * R + k;
+  const int idxD = jq * Ns * R + k;
 #pragma unroll
   for (int r = 0; r < R; ++r) dst[(idxD + r * Ns) * sj + b * sb] = v[r];
 }
@@ -135,15 +145,15 @@ __device__ __forceinline__ void stage_body(const cplx_t<T> *src, cplx_t<T> *dst,
 // Column layout (sb == 1, sj = 2^lg_cols >= batch): consecutive threads take
 // consecutive transforms of the same element index, so a warp reads
 // consecutive words; row layout (sj == 1): consecutive element indices.
+// Divisions by the stage constants use the plan's multipliers.
 template <typename T, int DIR>
 __device__ cplx_t<T> *fft_smem(cplx_t<T> *a, cplx_t<T> *bbuf, const RadixPlan &rp, int batch,
                                int sj, int sb, const cplx_t<T> *__restrict__ tw, int lg_cols = -1) {
   cplx_t<T> *src = a, *dst = bbuf;
-  int Ns = 1;
-  const int n = rp.n;
   for (int s = 0; s < rp.nst; ++s) {
-    const int R = rp.r[s];
-    const int nR = n / R;
+    const int R = rp.r[s], nR = rp.nR[s], Ns = rp.Ns[s];
+    const uint32_t mnR = rp.m_nR[s], mNs = rp.m_Ns[s];
+    const int step = nR / Ns;   // n / (Ns R)
     const int total = lg_cols >= 0 ? (nR << lg_cols) : batch * nR;
     for (int t = threadIdx.x; t < total; t += blockDim.x) {
       int b, j;
@@ -152,20 +162,19 @@ __device__ cplx_t<T> *fft_smem(cplx_t<T> *a, cplx_t<T> *bbuf, const RadixPlan &r
         j = t >> lg_cols;
         if (b >= batch) continue;
       } else {
-        b = t / nR;
+        b = nR > 1 ? fdiv(t, mnR) : t;
         j = t - b * nR;
       }
       switch (R) {
-        case 2: stage_body<T, DIR, 2>(src, dst, n, Ns, j, b, sj, sb, tw); break;
-        case 3: stage_body<T, DIR, 3>(src, dst, n, Ns, j, b, sj, sb, tw); break;
-        case 4: stage_body<T, DIR, 4>(src, dst, n, Ns, j, b, sj, sb, tw); break;
-        case 5: stage_body<T, DIR, 5>(src, dst, n, Ns, j, b, sj, sb, tw); break;
-        default: stage_body<T, DIR, 8>(src, dst, n, Ns, j, b, sj, sb, tw); break;
+        case 2: stage_body<T, DIR, 2>(src, dst, nR, Ns, mNs, step, j, b, sj, sb, tw); break;
+        case 3: stage_body<T, DIR, 3>(src, dst, nR, Ns, mNs, step, j, b, sj, sb, tw); break;
+        case 4: stage_body<T, DIR, 4>(src, dst, nR, Ns, mNs, step, j, b, sj, sb, tw); break;
+        case 5: stage_body<T, DIR, 5>(src, dst, nR, Ns, mNs, step, j, b, sj, sb, tw); break;
+        default: stage_body<T, DIR, 8>(src, dst, nR, Ns, mNs, step, j, b, sj, sb, tw); break;
       }
     }
     __syncthreads();
     cplx_t<T> *tmp = src; src = dst; dst = tmp;
-    Ns *= R;
   }
   return src;
 }

@@ -103,6 +103,14 @@ void build_radix_plan(int n, RadixPlan *rp) {
   while (m % 2 == 0) { rp->r[rp->nst++] = 2; m /= 2; }
   while (m % 3 == 0) { rp->r[rp->nst++] = 3; m /= 3; }
   while (m % 5 == 0) { rp->r[rp->nst++] = 5; m /= 5; }
+  int ns = 1;
+  for (int s = 0; s < rp->nst; ++s) {
+    rp->nR[s] = n / rp->r[s];
+    rp->Ns[s] = ns;
+    rp->m_nR[s] = fdiv_mul((uint32_t)rp->nR[s]);
+    rp->m_Ns[s] = fdiv_mul((uint32_t)ns);
+    ns *= rp->r[s];
+  }
 }
 
 static std::atomic<unsigned long long> g_launches{0};
