@@ -23,9 +23,9 @@ struct RadixPlan {
 };
 
 __host__ __device__ __forceinline__ uint32_t fdiv_mul(uint32_t d) {
-  return (uint32_t)((((uint64_t)1) << 32) / d + 1);
+  return d <= 1 ? 0u : (uint32_t)((((uint64_t)1) << 32) / d + 1);   // 0 marks d == 1
 }
-__device__ __forceinline__ int fdiv(int x, uint32_t m) { return (int)__umulhi((uint32_t)x, m); }
+__device__ __forceinline__ int fdiv(int x, uint32_t m) { return m ? (int)__umulhi((uint32_t)x, m) : x; }
 
 // DFT of radix R in registers; DIR = -1 forward (e^{-i}), +1 inverse.
 template <typename T, int DIR>
@@ -148,12 +148,14 @@ __device__ __forceinline__ void stage_body(const cplx_t<T> *src, cplx_t<T> *dst,
 // Divisions by the stage constants use the plan's multipliers.
 template <typename T, int DIR>
 __device__ cplx_t<T> *fft_smem(cplx_t<T> *a, cplx_t<T> *bbuf, const RadixPlan &rp, int batch,
-                               int sj, int sb, const cplx_t<T> *__restrict__ tw, int lg_cols = -1) {
+                               int sj, int sb, const cplx_t<T> *__restrict__ tw, int lg_cols = -1,
+                               int tws = 1) {
+  // tws: stride of the root table (2 when tw holds the roots of twice rp.n)
   cplx_t<T> *src = a, *dst = bbuf;
   for (int s = 0; s < rp.nst; ++s) {
     const int R = rp.r[s], nR = rp.nR[s], Ns = rp.Ns[s];
     const uint32_t mnR = rp.m_nR[s], mNs = rp.m_Ns[s];
-    const int step = nR / Ns;   // n / (Ns R)
+    const int step = nR / Ns * tws;   // n / (Ns R), in units of the table
     const int total = lg_cols >= 0 ? (nR << lg_cols) : batch * nR;
     for (int t = threadIdx.x; t < total; t += blockDim.x) {
       int b, j;
@@ -237,6 +239,99 @@ __global__ void k_fft_c2r_x(const cplx_t<T> *__restrict__ in, T *__restrict__ ou
     const int rl = i / (nx * F), rem = i - rl * nx * F;
     const int x = rem / F, f = rem - x * F;
     dst[i] = res[(size_t)(rl * F + f) * ld + x].x;
+  }
+}
+
+// Even nx: real rows as length-h complex transforms (h = nx/2), the standard
+// packing z[m] = x[2m] + i x[2m+1] with the pre/post twiddle of the
+// power-of-two pipelines (fft_pipe.cuh), half the work of a length-nx complex
+// transform.  rph is the plan of h; tw the nx-th roots (read with stride 2).
+template <typename T>
+__global__ void k_fft_r2c_xh(const T *__restrict__ in, cplx_t<T> *__restrict__ out, int nx, int64_t nrows,
+                             int rows_per_cta, RadixPlan rph, const cplx_t<T> *__restrict__ tw) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int h = nx / 2, nxh = h + 1;
+  C *a = reinterpret_cast<C *>(smem_raw);
+  C *b = a + (size_t)rows_per_cta * h;
+  const int64_t row0 = (int64_t)blockIdx.x * rows_per_cta;
+  const int nr = (int)min((int64_t)rows_per_cta, nrows - row0);
+  const C *src = reinterpret_cast<const C *>(in + row0 * nx);   // pairs (x[2m], x[2m+1])
+  for (int i = threadIdx.x; i < nr * h; i += blockDim.x) a[i] = src[i];
+  __syncthreads();
+  C *res = fft_smem<T, -1>(a, b, rph, nr, 1, h, tw, -1, 2);
+  C *dst = out + row0 * nxh;
+  const uint32_t mh = fdiv_mul((uint32_t)h);
+  for (int i = threadIdx.x; i < nr * h; i += blockDim.x) {
+    const int r = fdiv(i, mh), k = i - r * h;
+    const C za = res[r * h + k];
+    const C zb = res[r * h + (k == 0 ? 0 : h - k)];
+    const T er = T(0.5) * (za.x + zb.x), ei = T(0.5) * (za.y - zb.y);   // (Z + conj Z')/2
+    const T dr = T(0.5) * (za.x - zb.x), di = T(0.5) * (za.y + zb.y);   // (Z - conj Z')/2
+    const C w = tw[k];                                                   // W_n^k
+    const T pr = w.x * dr - w.y * di, pi = w.x * di + w.y * dr;          // w * d; -i w d below
+    dst[r * nxh + k] = cmk<C, T>(er + pi, ei - pr);
+    if (k == 0) dst[r * nxh + h] = cmk<C, T>(er - pi, ei + pr);          // k = n/2: W^{n/2} = -1
+  }
+}
+
+// Even nx inverse: per (frame, zy) row and field, Z[k] = A + i conj(W^k) B
+// with A = X[k] + conj X[h-k], B = X[k] - conj X[h-k] (k = 0: the real parts
+// of X[0] and X[h] only, torch.fft.irfftn's treatment), inverse length-h
+// transform, x[2m] = Re z[m], x[2m+1] = Im z[m]; output interleaved as
+// k_fft_c2r_x's.
+template <typename T>
+__global__ void k_fft_c2r_xh(const cplx_t<T> *__restrict__ in, T *__restrict__ out, int nx, int64_t nrows,
+                             int rows_per_cta, RadixPlan rph, const cplx_t<T> *__restrict__ tw, int F,
+                             int64_t nzy) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int h = nx / 2, nxh = h + 1, ld = h + 1;
+  C *a = reinterpret_cast<C *>(smem_raw);
+  C *b = a + (size_t)rows_per_cta * F * ld;
+  const int64_t row0 = (int64_t)blockIdx.x * rows_per_cta;   // (frame, zy) rows
+  const int nr = (int)min((int64_t)rows_per_cta, nrows - row0);
+  const int nt = nr * F;
+  // source row of each transform (rl, f): the 64-bit divisions once per row
+  __shared__ int64_t srow[256];
+  for (int tr = threadIdx.x; tr < nt && tr < 256; tr += blockDim.x) {
+    const int rl = tr / F, f = tr - rl * F;
+    const int64_t row = row0 + rl, frame = row / nzy, zy = row - frame * nzy;
+    srow[tr] = ((frame * F + f) * nzy + zy) * nxh;
+  }
+  __syncthreads();
+  const uint32_t mnxh = fdiv_mul((uint32_t)nxh), mh = fdiv_mul((uint32_t)h);
+  const uint32_t mF = fdiv_mul((uint32_t)F), mnxF = fdiv_mul((uint32_t)(nx * F));
+  for (int i = threadIdx.x; i < nt * nxh; i += blockDim.x) {
+    const int tr = fdiv(i, mnxh), m = i - tr * nxh;
+    b[(size_t)tr * ld + m] = in[srow[tr] + m];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nt * h; i += blockDim.x) {
+    const int tr = fdiv(i, mh), k = i - tr * h;
+    const C *X = b + (size_t)tr * ld;
+    C v;
+    if (k == 0) {
+      const T x0 = X[0].x, xh = X[h].x;
+      v = cmk<C, T>(x0 + xh, x0 - xh);
+    } else {
+      const C xa = X[k], xb = X[h - k];
+      const T Ar = xa.x + xb.x, Ai = xa.y - xb.y;
+      const T Br = xa.x - xb.x, Bi = xa.y + xb.y;
+      const C w = tw[k];
+      const T cr = w.x * Br + w.y * Bi, ci = w.x * Bi - w.y * Br;   // conj(w) * B
+      v = cmk<C, T>(Ar - ci, Ai + cr);
+    }
+    a[(size_t)tr * ld + k] = v;
+  }
+  __syncthreads();
+  C *res = fft_smem<T, +1>(a, b, rph, nt, 1, ld, tw, -1, 2);
+  T *dst = out + row0 * nx * F;
+  for (int i = threadIdx.x; i < nr * nx * F; i += blockDim.x) {
+    const int rl = fdiv(i, mnxF), rem = i - rl * nx * F;
+    const int x = fdiv(rem, mF), f = rem - x * F;
+    const C z = res[(size_t)(rl * F + f) * ld + (x >> 1)];
+    dst[i] = (x & 1) ? z.y : z.x;
   }
 }
 

@@ -1743,6 +1743,10 @@ void pass_x_fwd(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t rows, cudaStream_t
       const int rpc = reg_width<T>(nx, 256, 64 * 1024);
       k_rows_r2c_reg<T><<<nblocks(rows, rpc), (nx / kEPT) * rpc, (size_t)rpc * padded_row(nx) * sizeof(C), st>>>(
           rho, spec, rows, rpc, p->rpx, p->twx.as<C>());
+    } else if (nx % 2 == 0) {
+      const int rpc = rows_per_cta<T>(nx / 2);
+      k_fft_r2c_xh<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx / 2, rpc), st>>>(
+          rho, spec, nx, rows, rpc, p->rpxh, p->twx.as<C>());
     } else {
       const int rpc = rows_per_cta<T>(nx);
       k_fft_r2c_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
@@ -1782,6 +1786,11 @@ void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nframes, int64_
       const size_t sm = std::max((size_t)rpc * F * padded_row(nx) * sizeof(C), (size_t)rpc * nx * F * sizeof(T));
       k_rows_c2r_il<T><<<nblocks(rows, rpc), tpt * F * rpc, sm, st>>>(fspec, freal, F, nzy, rows, rpc, p->rpx,
                                                                         p->twx.as<C>());
+    } else if (nx % 2 == 0) {
+      const int rpc = std::max(1, std::min(256 / F, rows_per_cta<T>(nx / 2 + 1) / F));
+      const int64_t rows = nframes * nzy;
+      k_fft_c2r_xh<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx / 2 + 1, rpc * F), st>>>(
+          fspec, freal, nx, rows, rpc, p->rpxh, p->twx.as<C>(), F, nzy);
     } else {
       const int rpc = std::max(1, rows_per_cta<T>(nx + 1) / F);
       const int64_t rows = nframes * nzy;
@@ -1841,6 +1850,8 @@ void set_fft_smem_attrs() {
   const int big = 200 * 1024;
   allow_smem(k_fft_r2c_x<T>, big);
   allow_smem(k_fft_c2r_x<T>, big);
+  allow_smem(k_fft_r2c_xh<T>, big);
+  allow_smem(k_fft_c2r_xh<T>, big);
   allow_smem(k_fft_strided<T, -1>, big);
   allow_smem(k_fft_strided<T, +1>, big);
   allow_smem(k_cols_reg<T, -1, false>, big);
@@ -2755,6 +2766,7 @@ extern "C" int sog_plan_create(sog_plan **out, const sog_plan_desc *desc) {
   p->ng = (int64_t)d.nx * d.ny * d.nz;
   p->nh = (int64_t)d.nz * d.ny * p->nxh;
   build_radix_plan(d.nx, &p->rpx);
+  if (d.nx % 2 == 0) build_radix_plan(d.nx / 2, &p->rpxh);
   build_radix_plan(d.ny, &p->rpy);
   build_radix_plan(d.nz, &p->rpz);
   p->nb_x = (d.nx + kBin - 1) / kBin;

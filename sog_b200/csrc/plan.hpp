@@ -66,6 +66,7 @@ struct sog_plan {
   int nxh = 0;
   int64_t ng = 0, nh = 0;  // real / half-spectrum points per frame
   sogb::RadixPlan rpx{}, rpy{}, rpz{};
+  sogb::RadixPlan rpxh{};           // nx/2 (even nx: real x rows as half-length transforms)
   sogb::DevBuf twx, twy, twz;   // n-th roots (complex, plan dtype)
   sogb::AxisTables tab;
   // scratch
