@@ -210,6 +210,25 @@ def test_fp32_mode_within_1e5():
     assert _rel(out["forces"].cpu().numpy(), ref["forces"]) < 1e-5
 
 
+@pytest.mark.parametrize("L,n_dl", [(12.0, 0.7), (12.0, 1.0)])   # 36^3 (even: half-length x), 25^3 (odd)
+def test_fp32_generic_sizes_within_1e5(L, n_dl):
+    cell = np.eye(3) * L
+    r, q = _system(6, 500, cell, nch=2)
+    bw = np.array([1.2, 2.0, 3.5, 6.0])
+    amp = 1.0 / (bw * math.sqrt(2 * math.pi)) * bw * bw
+    ref = _oracle_bundle(r, q, cell[None], np.zeros(500, int), amp, bw * bw, O.BSPLINE, 6, n_dl)
+    g = Gaussian(n_dl=n_dl, amp=torch.tensor(amp), bandwidth=torch.tensor(bw * bw),
+                 kernel_param_mode="internal", use_bspline_fft=True, bspline_order=6).to(DEV)
+    qt = _t(q, torch.float32).requires_grad_(True)
+    out = g.compute_bundle(q=qt, r=_t(r, torch.float32), cell=_t(cell[None], torch.float32),
+                           compute_force=True)
+    assert _rel(out["energy"].detach().cpu().numpy(), ref["energy"]) < 1e-5
+    assert _rel(out["forces"].cpu().numpy(), ref["forces"]) < 1e-5
+    # the potential-only field count (dE/dq without forces) takes the same passes
+    (gq,) = torch.autograd.grad(g(q=qt, r=_t(r, torch.float32), cell=_t(cell[None], torch.float32)).sum(), qt)
+    assert _rel(gq.cpu().numpy(), ref["potential"]) < 1e-5
+
+
 def test_config2_full_size_bspline6_vs_oracle_and_deterministic():
     c = load("cfg2_quads6")
     amp, bw2 = c["amp"], c["bw2"]
