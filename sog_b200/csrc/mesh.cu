@@ -72,7 +72,7 @@ __host__ __device__ __forceinline__ uint32_t bin_row(const AtomGrid &ag, int bz,
 #define SOG_ZFUSED_MINB 2
 #endif
 #ifndef SOG_SPREAD_MINB
-#define SOG_SPREAD_MINB 3
+#define SOG_SPREAD_MINB 4
 #endif
 
 // Fractional coordinate along axis a (r @ cell^-1, then remainder 1.0) and the

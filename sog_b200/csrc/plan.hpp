@@ -34,7 +34,10 @@ struct PinnedBuf {
 
 // Spread tile (threads own (x,y) columns and TZ z-values in registers) and the
 // atom-sort bins (cubes of kBin grid cells).
-constexpr int kTileX = 32, kTileY = 8, kTileZ = 16;
+#ifndef SOG_TILE_Z
+#define SOG_TILE_Z 8
+#endif
+constexpr int kTileX = 32, kTileY = 8, kTileZ = SOG_TILE_Z;
 constexpr int kBin = 8;
 
 struct AxisTables {
