@@ -1809,7 +1809,10 @@ void pass_cols(sog_plan *p, cplx_t<T> *data, int n, int64_t inner, int64_t outer
   const bool done = with_pow2(n, [&](auto lc) {
     constexpr int L = decltype(lc)::value;
     constexpr int nn = 1 << L;
-    const int ic = reg_width<T>(nn, 256, 64 * 1024);
+    // fp32 columns are 8 bytes: 512-thread tiles keep each tile row of the
+    // long axes at 64 bytes or more
+    constexpr int thr_cap = sizeof(T) == 4 ? 512 : 256;
+    const int ic = reg_width<T>(nn, thr_cap, thr_cap * 256);
     const int64_t nchunks = (inner + ic - 1) / ic;
     const int64_t ntiles = outer * nchunks;
     const int thr = (nn / kEPT) * ic;
