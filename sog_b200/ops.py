@@ -33,11 +33,21 @@ class Bucket:
     kind: Optional[str] = None   # "realspace" for non-periodic frames, else the spec's kind
     _host: Optional[dict] = None
 
+    _idx: Optional[torch.Tensor] = None
+
     def host(self) -> dict:
         """The per-frame arrays as ctypes arrays, converted on first use."""
         if self._host is None:
             self._host = _lib.host_tables(self.atom_begin, self.atom_count, self.k_sq_max, self.nk)
         return self._host
+
+    def frame_index(self, dev: torch.device) -> torch.Tensor:
+        """The bucket's output positions on `dev`, uploaded once (a fresh
+        upload per call would be a synchronous copy that waits for the
+        device)."""
+        if self._idx is None or self._idx.device != dev:
+            self._idx = torch.tensor(self.frames, device=dev, dtype=torch.long)
+        return self._idx
 
 
 @dataclass
@@ -86,7 +96,7 @@ def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Ten
         if single:
             cells_b, e_b, ga_b, gb_b, v_b = spec.cells, energy, gamp, gbw2, vir
         else:
-            idx = torch.tensor(b.frames, device=dev, dtype=torch.long)
+            idx = b.frame_index(dev)
             cells_b = None if spec.cells is None else spec.cells.index_select(0, idx).contiguous()
             e_b = torch.empty(len(b.frames), dtype=dt, device=dev)
             ga_b = torch.empty(len(b.frames), M, dtype=dt, device=dev) if want_grad else None
