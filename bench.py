@@ -20,7 +20,7 @@ by the longest-processing-time rule (sog_b200.shard), no collective on the
 data path: strong scaling of the fixed batch.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sog_b200|reference]
-                    [--config cfg5|cfg5_eighth|cfg2|cfg4]
+                    [--config cfg5|cfg5_eighth|cfg5_quarter|cfg2|cfg4] [--dtype f64|f32] [--eager]
 """
 from __future__ import annotations
 
