@@ -71,6 +71,9 @@ __host__ __device__ __forceinline__ uint32_t bin_row(const AtomGrid &ag, int bz,
 #ifndef SOG_ZFUSED_MINB
 #define SOG_ZFUSED_MINB 2
 #endif
+#ifndef SOG_GATHER_VEC
+#define SOG_GATHER_VEC 1
+#endif
 #ifndef SOG_SPREAD_MINB
 #define SOG_SPREAD_MINB 4
 #endif
@@ -1517,6 +1520,90 @@ __global__ void __launch_bounds__(256, SOG_GATHER_MINB) k_gather(GatherArgs<T> a
   if (a.want_pot) a.pot_raw[atom * a.nch + a.channel] = acc[a.want_force ? 3 : 0];
 }
 
+// fp64 gather of the three force fields (single-term splines, even P):
+// an atom's stencil row of P points x 3 interleaved fields is 3P contiguous
+// doubles when it does not wrap in x.  The row is read as 3P/2 16-byte loads
+// from its 16-byte-aligned start below it, plus one 8-byte load for rows that
+// start on an odd word, and the lane picks its 3P words from those: 3P/2 + 1
+// load instructions a row instead of 3P, for every lane of a warp alike.
+// Every load stays inside the row [start, start + 3P).  Rows that wrap take
+// the per-point loads of k_gather.
+template <int P>
+__global__ void __launch_bounds__(256, SOG_GATHER_MINB) k_gather_f3v(GatherArgs<double> a) {
+  static_assert(P % 2 == 0, "even stencil widths");
+  const int64_t si = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (si >= a.nslots) return;
+  int64_t s = a.slot_lo + si;
+  if (a.range_lo) {
+    s = (int64_t)*a.range_lo + si;
+    if (s >= (int64_t)*a.range_hi) return;
+  }
+  const int4 an = a.s_anchor[s];
+  double wx[1][P], wy[1][P], wz[1][P];
+  axis_kinds<double, P, 1>(a.spline, a.s_t[s * 3 + 0], wx, a.qc);
+  axis_kinds<double, P, 1>(a.spline, a.s_t[s * 3 + 1], wy, a.qc);
+  axis_kinds<double, P, 1>(a.spline, a.s_t[s * 3 + 2], wz, a.qc);
+  const AtomGrid &ag = a.ag;
+  int ix[P];
+#pragma unroll
+  for (int k = 0; k < P; ++k) { int v = an.x + k; ix[k] = v >= ag.nx ? v - ag.nx : v; }
+  const double *base = a.freal + (int64_t)an.w * 3 * a.ng;
+  // aligned field block: a row's aligned-down start never precedes it
+  const bool nowrap = an.x + P <= ag.nx && (reinterpret_cast<uintptr_t>(base) & 15) == 0;
+  double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0;
+#pragma unroll 1
+  for (int c = 0; c < P; ++c) {
+    int gz = an.z - a.zlo + c;
+    if (gz >= a.zwrap) gz -= a.zwrap;
+#pragma unroll
+    for (int b = 0; b < P; ++b) {
+      int gy = an.y + b;
+      if (gy >= ag.ny) gy -= ag.ny;
+      const int64_t row = ((int64_t)gz * ag.ny + gy) * ag.nx;
+      const double wzy = wy[0][b] * wz[0][c];
+      if (nowrap) {
+        const double *p0 = base + (row + an.x) * 3;
+        const int par = (int)((reinterpret_cast<uintptr_t>(p0) >> 3) & 1);
+        const double2 *q = reinterpret_cast<const double2 *>(p0 - par);
+        double A[3 * P + 1];
+#pragma unroll
+        for (int u = 0; u < 3 * P / 2; ++u) {
+          const double2 t = q[u];
+          A[2 * u] = t.x;
+          A[2 * u + 1] = t.y;
+        }
+        A[3 * P] = par ? p0[3 * P - 1] : 0.0;
+#pragma unroll
+        for (int k = 0; k < P; ++k) {
+          const double wv = wx[0][k] * wzy;
+          const double v0 = par ? A[3 * k + 1] : A[3 * k];
+          const double v1 = par ? A[3 * k + 2] : A[3 * k + 1];
+          const double v2 = par ? A[3 * k + 3] : A[3 * k + 2];
+          acc0 += wv * v0;
+          acc1 += wv * v1;
+          acc2 += wv * v2;
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < P; ++k) {
+          const double wv = wx[0][k] * wzy;
+          const double *pt = base + (row + ix[k]) * 3;
+          acc0 += wv * pt[0];
+          acc1 += wv * pt[1];
+          acc2 += wv * pt[2];
+        }
+      }
+    }
+  }
+  const int64_t atom = a.s_atom[s];
+  const double q = a.s_q[s];
+  const double sc = -q * a.norm;
+  const double v[3] = {sc * acc0, sc * acc1, sc * acc2};
+  for (int c = 0; c < 3; ++c) {
+    if (a.accumulate) a.forces[atom * 3 + c] += v[c]; else a.forces[atom * 3 + c] = v[c];
+  }
+}
+
 // ---- z-slab decomposition: transpose packing and slab dE/dq ----
 // plain copy into another rank's halo planes (peer transport)
 template <typename T>
@@ -1922,6 +2009,15 @@ void dispatch_gather(const GatherArgs<T> &ga, int order, cudaStream_t st, Tracer
     else k_gather<T, 6, 4><<<nb, 256, 0, st>>>(ga);
     after(tr, st, "gather");
     return;
+  }
+  if constexpr (std::is_same<T, double>::value) {
+    // forces only (three interleaved fields): vector row loads
+    if (SOG_GATHER_VEC && ga.nfield == 3 && ga.want_force && !ga.want_pot && (order == 4 || order == 6)) {
+      if (order == 4) k_gather_f3v<4><<<nb, 256, 0, st>>>(ga);
+      else k_gather_f3v<6><<<nb, 256, 0, st>>>(ga);
+      after(tr, st, "gather");
+      return;
+    }
   }
   switch (order) {
     case 4: k_gather<T, 4><<<nb, 256, 0, st>>>(ga); break;
