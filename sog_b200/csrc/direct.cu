@@ -190,11 +190,13 @@ __global__ void __launch_bounds__(kDirThreads) k_direct_extra(DirArgs a, const T
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(128) k_direct_atoms(DirArgs a, const T *__restrict__ pos,
-                                                     const T *__restrict__ q, double norm,
-                                                     T *__restrict__ forces, T *__restrict__ pot) {
-  constexpr int CH = 128;
+// CH threads per block, one atom each, staging CH modes at a time: 128, or
+// one warp for frames of at most 32 atoms (many tiny frames), so that a
+// block's threads are mostly busy.
+template <typename T, int CH = 128>
+__global__ void __launch_bounds__(CH) k_direct_atoms(DirArgs a, const T *__restrict__ pos,
+                                                    const T *__restrict__ q, double norm,
+                                                    T *__restrict__ forces, T *__restrict__ pot) {
   __shared__ double s_k[CH][4];
   __shared__ double s_s[CH][kMaxCh][2];
   const int f = blockIdx.y;
@@ -347,10 +349,15 @@ int direct_impl(sog_direct *d, const sog_direct_args *a, cudaStream_t st) {
     k_direct_extra<T><<<dim3(kb, nf, nch), kDirThreads, 0, st>>>(da, (const T *)a->amp, (const T *)a->bw2,
                                                                  want_grad, want_vir);
   if (want_grad || want_vir) after(tr, st, "direct_extra");
-  if ((a->forces || a->potential) && maxat > 0)
-    k_direct_atoms<T><<<dim3(nblk(maxat, 128), nf), 128, 0, st>>>(da, (const T *)a->positions,
-                                                                  (const T *)a->charges, a->norm_factor,
-                                                                  (T *)a->forces, (T *)a->potential);
+  if ((a->forces || a->potential) && maxat > 0) {
+    if (maxat <= 32)
+      k_direct_atoms<T, 32><<<dim3(1, nf), 32, 0, st>>>(da, (const T *)a->positions, (const T *)a->charges,
+                                                        a->norm_factor, (T *)a->forces, (T *)a->potential);
+    else
+      k_direct_atoms<T><<<dim3(nblk(maxat, 128), nf), 128, 0, st>>>(da, (const T *)a->positions,
+                                                                    (const T *)a->charges, a->norm_factor,
+                                                                    (T *)a->forces, (T *)a->potential);
+  }
   if ((a->forces || a->potential) && maxat > 0) after(tr, st, "direct_atoms");
   reduce_parts(da.part, nf, nch, kb, 2, 2, redE, d->redtmp.as<double>(), st);
   after(tr, st, "reduce");

@@ -169,9 +169,27 @@ inline int reduce_split(int64_t nblk) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(s, 512));
 }
 
+// Few partials per (frame, channel): one thread per accumulated value adds its
+// nblk partials in order (many small frames would otherwise spend a
+// 256-thread tree and its barriers on each of nacc values).
+__global__ void k_reduce_parts_few(const double *__restrict__ part, int nf, int nch, int64_t nblk,
+                                   int stride, int nacc, double *__restrict__ out) {
+  const int f = blockIdx.x, c = blockIdx.y;
+  const double *p = part + (((int64_t)c * nf + f) * nblk) * stride;
+  for (int i = threadIdx.x; i < nacc; i += blockDim.x) {
+    double s = 0.0;
+    for (int64_t b = 0; b < nblk; ++b) s += p[b * stride + i];
+    out[((int64_t)f * nch + c) * nacc + i] = s;
+  }
+}
+
 inline void reduce_parts(const double *part, int nf, int nch, int64_t nblk, int stride, int nacc,
                          double *out, double *tmp, cudaStream_t st) {
   const int split = reduce_split(nblk);
+  if (nblk <= 16) {
+    k_reduce_parts_few<<<dim3(nf, nch, 1), 64, 0, st>>>(part, nf, nch, nblk, stride, nacc, out);
+    return;
+  }
   if (split == 1) {
     k_reduce_parts<<<dim3(nf, nch, 1), 256, 0, st>>>(part, nf, nch, nblk, stride, nacc, out);
     return;
