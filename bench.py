@@ -180,7 +180,9 @@ def algorithmic_bytes(cfg, s: int = 8, nfield: int = 3, parts: int = 1):
 
 def profiled_traffic(kernel: str, config: str):
     """DRAM bytes per launch of `kernel` from the committed ncu summary of the
-    512^3 workload (profiles/dram_mesh512_bspline6.md), or None."""
+    512^3 workload (profiles/dram_mesh512_bspline6.md), or None.  This is a
+    figure copied from that capture, not a measurement of the current run;
+    the JSON line says so next to it."""
     if config != "cfg5":
         return None
     p = os.path.join(ROOT, "profiles", "dram_mesh512_bspline6.md")
@@ -193,6 +195,13 @@ def profiled_traffic(kernel: str, config: str):
     except (OSError, ValueError):
         return None
     return None
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 def measured_peak():
@@ -280,28 +289,77 @@ class ClockSampler:
 # CPU oracle timing (cpu_baseline and the reference arm)
 # ---------------------------------------------------------------------------
 def oracle_eval_time(cfg_name: str, reps: int, warm: int = 1):
+    """E+F of the workload `cfg_name` by the C/OpenMP oracle on every host
+    core; returns (cfg, per-evaluation seconds, threads, last result with the
+    k=0 term added to its energy)."""
     import numpy as np
     from oracle import oracle as O
+    threads = O.set_num_threads(host_cores())
     cfg = workload(cfg_name)
     r, q, cell, amp_raw, bw = make_inputs(cfg, 0)
     nx, ny, nz = mesh_dims(cfg)
     amp = amp_raw * bw * bw
     ksm = (2.0 * math.pi / cfg["n_dl"]) ** 2
     times = []
+    res = None
     for i in range(warm + reps):
         t0 = time.perf_counter()
-        O.mesh_solve(r, q, cell, amp, bw * bw, spline=O.BSPLINE, order=cfg["order"], nx=nx, ny=ny,
-                     nz=nz, k_sq_max=ksm, want_force=True)
+        res = O.mesh_solve(r, q, cell, amp, bw * bw, spline=O.BSPLINE, order=cfg["order"], nx=nx,
+                           ny=ny, nz=nz, k_sq_max=ksm, want_force=True)
         dt = time.perf_counter() - t0
         if i >= warm:
             times.append(dt)
-    return cfg, times, O.num_threads()
+    e0, _, _, _ = O.k0_correction(q[:, None], cell, amp, bw * bw, norm_factor=14.3996454784255,
+                                  remove_self=True)
+    res["energy"] += e0
+    return cfg, times, threads, res
+
+
+def reference_torch_time(cfg_name: str, reps: int = 2, warm: int = 1):
+    """The reference's own torch CPU path on the same sample: QuadS order 6
+    with explicit E+F through Gaussian.compute_bundle (batched direct gate
+    off), fp64, torch threads = host cores.  Runs the reference installed in
+    baseline/_ref; None when it is not there."""
+    path = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(path, "sog")):
+        return None
+    import warnings
+    import torch
+    if path not in sys.path:
+        sys.path.insert(0, path)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        from sog.module.gaussian import Gaussian as RefGaussian
+        cores = host_cores()
+        torch.set_num_threads(cores)
+        cfg = workload(cfg_name)
+        r, q, cell, amp_raw, bw = make_inputs(cfg, 0)
+        g = RefGaussian(n_dl=cfg["n_dl"], amp=torch.tensor(amp_raw), bandwidth=torch.tensor(bw),
+                        use_quads_fft=True, quads_order=cfg["order"], trainable=False)
+        g._enable_batched_direct = False
+        rt, qt = torch.tensor(r), torch.tensor(q)
+        ct = torch.tensor(cell).unsqueeze(0)
+        bt = torch.zeros(len(r), dtype=torch.long)
+        times = []
+        for i in range(warm + reps):
+            t0 = time.perf_counter()
+            with torch.no_grad():
+                g.compute_bundle(q=qt, r=rt, cell=ct, batch=bt, compute_force=True)
+            if i >= warm:
+                times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": cfg["natoms"] / t, "unit": UNIT, "cores": cores, "kind": "reference",
+            "sample": f"{cfg['workload']}; the reference's torch QuadS-{cfg['order']} explicit E+F "
+                      f"(compute_bundle, batched direct gate off), median of {reps} after {warm} "
+                      f"warm-up, {t:.2f} s per evaluation",
+            "note": "QuadS: the reference's Python solvers have no B-spline mesh"}
 
 
 def oracle_batch_time(frames: int = 120):
     """The oracle's E+F on the first `frames` frames of the batched workload."""
     from oracle import oracle as O
     from tests._cases import friendly
+    O.set_num_threads(host_cores())
     counts, r, q, cells, amp_raw, bw = make_batch(0)
     amp = amp_raw * bw * bw
     ksm = (2.0 * math.pi / 1.0) ** 2
@@ -338,7 +396,7 @@ def run_reference(args, rank: int):
         print(json.dumps(line), flush=True)
         return
     sample = "cfg5_eighth"
-    cfg, times, threads = oracle_eval_time(sample, reps=args.steps, warm=args.warmup)
+    cfg, times, threads, _ = oracle_eval_time(sample, reps=args.steps, warm=args.warmup)
     t = statistics.median(times)
     val = cfg["natoms"] / t
     main_cfg = workload(args.config)
@@ -352,6 +410,7 @@ def run_reference(args, rank: int):
                          "sample": f"{cfg['workload']}; one E+F evaluation per step by the C/OpenMP "
                                    "oracle (the reference's B-spline mesh restated), median of steps"},
         "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_torch": reference_torch_time(sample),
     }
     print(json.dumps(line), flush=True)
 
@@ -415,15 +474,18 @@ def run_gpu_batch(args, rank: int, world: int):
     for p in plans:
         p.set_timing(True)
     stream = torch.cuda.current_stream()
+    # every rank starts its clock sampler first; the barrier right before the
+    # first event then lines the ranks up, so no rank's sampler start-up
+    # lands inside another rank's first timed step
     clocks = ClockSampler(local)
-    barrier()
-    torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
-    l0 = _lib.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     gc.collect()
     gc.disable()
+    barrier()
+    torch.cuda.synchronize()
+    l0 = _lib.launch_count()
     ev0.record(stream)
     h0 = time.perf_counter()
     for _ in range(args.steps):
@@ -501,7 +563,7 @@ def run_gpu_batch(args, rank: int, world: int):
                 "algorithmic_bytes_per_step": per_kernel[dom],
                 "note": "rank 0's share; all launches of the kernel in one step (one per mesh bucket)"}
     cpu = None
-    if not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline:
         atoms, t, threads = oracle_batch_time()
         cpu = {"value": atoms / t, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"first 120 frames of the batch ({atoms} atoms), E+F by the C/OpenMP oracle"}
@@ -614,15 +676,18 @@ def run_gpu(args, rank: int, world: int):
             torch.cuda.synchronize()
     if graph is None:
         plan.set_timing(True)
+    # every rank starts its clock sampler first; the barrier right before the
+    # first event then lines the ranks up, so no rank's sampler start-up
+    # lands inside another rank's first timed step
     clocks = ClockSampler(local)
-    barrier()
-    torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     marks = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     gc.collect()
     gc.disable()          # no collector pause inside the timed steps
+    barrier()
+    torch.cuda.synchronize()
     if graph is not None:
         ev0.record(stream)
         h0 = time.perf_counter()
@@ -717,39 +782,75 @@ def run_gpu(args, rank: int, world: int):
         dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
     ms_e2e = float(ms_e2e.item())
 
-    if rank != 0:
-        return
-    # ---- roofline of the dominant kernel ----
-    s = 8 if dt == torch.float64 else 4
-    b_ef, per_kernel = algorithmic_bytes(cfg, s=s, parts=world if slab else 1)
+    # per-rank kernel tables (ms per step), gathered to rank 0 (every rank
+    # takes part in the same collective)
     tot, cnt = {}, {}
     for name, t in kt:
         tot[name] = tot.get(name, 0.0) + t
         cnt[name] = cnt.get(name, 0) + 1
-    kernels = {k: {"launches": cnt[k], "total_ms": tot[k], "avg_ms": tot[k] / cnt[k],
-                   "share": tot[k] / sum(tot.values())} for k in tot}
-    dom = max(tot, key=tot.get) if tot else None
-    peak, peak_kind = measured_peak()
-    roof = None
-    if dom is not None and dom in per_kernel:
-        ach = per_kernel[dom] / (kernels[dom]["avg_ms"] * 1e-3) / 1e9
-        roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
-                "frac": ach / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                "traffic": (profiled_traffic(dom, args.config) / world
-                            if slab and profiled_traffic(dom, args.config) else
-                            profiled_traffic(dom, args.config)),
-                "algorithmic_bytes_per_launch": per_kernel[dom]}
-    for k, v in kernels.items():
-        if k in per_kernel:
-            v["achieved_gbs"] = per_kernel[k] / (v["avg_ms"] * 1e-3) / 1e9
-    step_gbs = b_ef / (ms * 1e-3) / 1e9
-    cpu = None
-    if not args.no_cpu_baseline:
-        ccfg, times, threads = oracle_eval_time("cfg5_eighth", reps=3, warm=1)
+    by_rank = None
+    if world > 1:
+        by_rank = [None] * world
+        dist.all_gather_object(by_rank, {k: round(v / args.steps, 4) for k, v in tot.items()})
+
+    # ---- one evaluation of the 1/8-scale sample checked against the oracle
+    # (outside the timed region; N = 1 only, like the CPU baseline) ----
+    cpu = parity = None
+    if world == 1 and not args.no_cpu_baseline:
+        ccfg, times, threads, oref = oracle_eval_time("cfg5_eighth", reps=3, warm=1)
         tmed = statistics.median(times)
         cpu = {"value": ccfg["natoms"] / tmed, "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"{ccfg['workload']}; C/OpenMP oracle E+F, median of 3 after 1 warm-up, "
                          f"{tmed:.2f} s per evaluation"}
+        rr, qq, cc, ampr, bwr = make_inputs(ccfg, 0)
+        g8 = Sog({"use_atomwise": False, "use_bspline_fft": True, "bspline_order": ccfg["order"],
+                  "n_dl": ccfg["n_dl"], "amp": torch.tensor(ampr, dtype=dt),
+                  "bandwidth": torch.tensor(bwr, dtype=dt), "trainable_kernel": False}).to(dev).gaussian
+        o8 = g8.compute_bundle(q=torch.tensor(qq, dtype=dt, device=dev),
+                               r=torch.tensor(rr, dtype=dt, device=dev),
+                               cell=torch.tensor(cc[None], dtype=dt, device=dev), compute_force=True)
+        e8 = float(o8["energy"][0])
+        f8 = o8["forces"].double().cpu().numpy()
+        fmax = float(np.abs(oref["forces"]).max())
+        parity = {"sample": ccfg["workload"], "against": "oracle (C/OpenMP, fp64)",
+                  "energy_rel_err": abs(e8 - oref["energy"]) / abs(oref["energy"]),
+                  "force_max_abs_err": float(np.abs(f8 - oref["forces"]).max()),
+                  "force_max_rel_err": float(np.abs(f8 - oref["forces"]).max()) / fmax,
+                  "tolerance": ("energy rel 1e-10, force max-abs 1e-9" if dt == torch.float64
+                                else "energy rel 1e-5, force max-abs / max |F| 1e-5")}
+        del o8, g8
+
+    if rank != 0:
+        return
+    # ---- roofline of the dominant kernel (the one with the largest stream
+    # time among those that move mesh arrays; barriers and NCCL sums are
+    # reported in the kernel table but carry no algorithmic bytes) ----
+    s = 8 if dt == torch.float64 else 4
+    b_ef, per_kernel = algorithmic_bytes(cfg, s=s, parts=world if slab else 1)
+    kernels = {k: {"launches": cnt[k], "total_ms": tot[k], "avg_ms": tot[k] / cnt[k],
+                   "share": tot[k] / sum(tot.values())} for k in tot}
+    work = {k: v for k, v in tot.items() if k in per_kernel}
+    dom = max(work, key=work.get) if work else None
+    top = max(tot, key=tot.get) if tot else None
+    peak, peak_kind = measured_peak()
+    roof = None
+    if dom is not None:
+        ach = per_kernel[dom] / (kernels[dom]["avg_ms"] * 1e-3) / 1e9
+        traffic = profiled_traffic(dom, args.config)
+        if traffic is not None and slab:
+            traffic /= world
+        roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                "frac": ach / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                "traffic": traffic,
+                "traffic_source": ("ncu capture committed in profiles/dram_mesh512_bspline6.md "
+                                   "(one launch of this kernel at this size; not measured in this run)"
+                                   if traffic is not None else None),
+                "algorithmic_bytes_per_launch": per_kernel[dom],
+                "largest_stream_time": {"name": top, "share": kernels[top]["share"]}}
+    for k, v in kernels.items():
+        if k in per_kernel:
+            v["achieved_gbs"] = per_kernel[k] / (v["avg_ms"] * 1e-3) / 1e9
+    step_gbs = b_ef / (ms * 1e-3) / 1e9
     systems = 1 if slab else world      # systems evaluated per step by the whole job
     nvlink = None
     if slab:
@@ -760,15 +861,25 @@ def run_gpu(args, rank: int, world: int):
         sent = (share + 3 * share) * (world - 1) / world + (cfg["order"] - 1) * nx * ny * 3 * s
         ex_ms = sum(v["total_ms"] for k, v in kernels.items()
                     if k.startswith("exchange") or k.startswith("barrier")) / args.steps
+        if transport == "peer":
+            # the stores travel inside these kernels: their stream time bounds
+            # the link time from above, so the rate is a lower bound
+            storing = ("fft_y_fwd", "zfused", "halo_push")
+            st_ms = sum(kernels[k]["total_ms"] for k in storing if k in kernels) / args.steps
+            ach_nv = sent / (st_ms * 1e-3) / 1e9 if st_ms > 0 else None
+            note = ("peer: the transposes are stored into the other GPUs' buffers by the y-FFT and "
+                    "fused z kernels (and the halo by halo_push); achieved = bytes sent per rank / "
+                    "those kernels' stream time per step (they compute too, so a lower bound); "
+                    "exchange_ms is the stream time of the barriers and sums")
+        else:
+            st_ms = ex_ms
+            ach_nv = sent / (ex_ms * 1e-3) / 1e9 if ex_ms > 0 else None
+            note = "exchange time is the stream time of the NCCL calls (all-to-all, halo, sums)"
         nvlink = {"bytes_per_rank_per_step": sent, "exchange_ms_per_step": ex_ms,
-                  "achieved_gbs": (sent / (ex_ms * 1e-3) / 1e9
-                                   if ex_ms > 0 and transport == "exchange" else None),
+                  "storing_ms_per_step": st_ms, "achieved_gbs": ach_nv,
+                  "frac": ach_nv / 770.0 if ach_nv else None,
                   "peak": 770.0, "unit": "GB/s", "peak_source": "measured peer copy per direction",
-                  "transport": transport,
-                  "note": ("peer: the transposes travel inside the y-FFT and fused z kernels; "
-                           "exchange_ms is the stream time of the barriers and sums only"
-                           if transport == "peer" else
-                           "exchange time is the stream time of the NCCL calls (all-to-all, halo, sums)")}
+                  "transport": transport, "note": note}
     if slab:
         parallelism = (f"slab{world} (z slabs; transposes stored by the FFT kernels into peer GPUs' "
                        "buffers over NVLink, NCCL sums as barriers)" if transport == "peer" else
@@ -797,8 +908,11 @@ def run_gpu(args, rank: int, world: int):
         "step_ms": [round(x, 4) for x in step_ms],
         "clocks": clk,
         "cpu_baseline": cpu,
+        "parity": parity,
         "energy_frame0": energy0,
     }
+    if by_rank is not None:
+        line["kernels_ms_per_step_by_rank"] = by_rank
     print(json.dumps(line), flush=True)
 
 

@@ -271,17 +271,23 @@ SOG_API int sog_realspace_forward(sog_direct *d, const sog_realspace_args *args,
 #define SOG_NOALLOC_SCRATCH_BYTES (8u << 20)
 #define SOG_NOALLOC_MAX_FRAMES 64
 
-/* Same result as sog_direct_forward (same kernels, same arguments) on the
- * calling thread's current device, for callers that may not allocate device
- * or pinned host memory inside a force call: an MD engine that hands out
- * device memory only from its own arena and forbids cudaMalloc after setup
- * (cudaMalloc / cudaHostAlloc can wait on queued device work and can fail
- * under memory pressure mid-run), or an integrator that keeps no per-context
- * state.  The call makes no allocation: its scratch is a file-scope
- * __device__ array of SOG_NOALLOC_SCRATCH_BYTES bytes, and the per-frame
- * metadata travels as a kernel parameter.
- *  - The first call on each device resolves the array's address (which may
- *    load the module on that device); make it before any stream capture.
+/* Same result as sog_direct_forward (same kernels, same launch shapes, same
+ * arguments) on the calling thread's current device, for callers that may
+ * not allocate device or pinned host memory inside a force call: an MD
+ * engine that hands out device memory only from its own arena and forbids
+ * cudaMalloc after setup (cudaMalloc / cudaHostAlloc can wait on queued
+ * device work and can fail under memory pressure mid-run), or an integrator
+ * that keeps no per-context state.  The call makes no allocation: its
+ * scratch is a file-scope __device__ array of SOG_NOALLOC_SCRATCH_BYTES
+ * bytes, and the per-frame metadata travels as a kernel parameter.
+ *  - status: optional caller-owned device word (NULL: none).  The call sets
+ *    it to its status bits (the SOG_STATUS_* bits of sog_plan_status: e.g.
+ *    non-finite positions or charges, a singular cell) in stream order; read
+ *    it after the stream has passed the call.
+ *  - The first call in each CUDA context (per device, and again after
+ *    cudaDeviceReset or under another driver-API context) resolves the
+ *    array's address there, which may load the module into that context;
+ *    make it before any stream capture.
  *  - A call whose scratch would exceed the array (about 48 bytes per mode of
  *    the largest frame's mode box per frame and channel, more with
  *    parameter gradients or the virial), or with more than
@@ -292,7 +298,8 @@ SOG_API int sog_realspace_forward(sog_direct *d, const sog_realspace_args *args,
  *  - All calls on one device share the array: two calls in flight at once
  *    on one device (different streams or host threads) race.  Serialise
  *    them on one stream or with an event. */
-SOG_API int sog_direct_forward_noalloc(int dtype, const sog_direct_args *args, void *stream);
+SOG_API int sog_direct_forward_noalloc(int dtype, const sog_direct_args *args, unsigned int *status,
+                                       void *stream);
 
 #ifdef __cplusplus
 }

@@ -36,9 +36,14 @@ QUADS = 1
 CUBES2 = 2
 
 
-def build() -> None:
-    """Compile the oracle (and oracle/_ref when the reference tree exists)."""
-    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+def build(reference: Optional[str] = None) -> None:
+    """Compile the oracle, and oracle/_ref when ``reference`` (or the
+    SOG_REFERENCE environment variable) names the reference tree."""
+    ref = reference or os.environ.get("SOG_REFERENCE", "")
+    cmd = ["make", "-s", "-C", _HERE]
+    if ref:
+        cmd.append(f"REF={ref}")
+    subprocess.run(cmd, check=True)
 
 
 def lib():
@@ -376,3 +381,9 @@ def bundle(r, q, cell, batch, amp, bw2, *, solver: str, grids=None, nks=None,
 
 def num_threads() -> int:
     return int(lib().orc_num_threads())
+
+
+def set_num_threads(n: int) -> int:
+    """Use n OpenMP threads from now on; returns the count in effect."""
+    lib().orc_set_num_threads(int(n))
+    return num_threads()

@@ -1063,6 +1063,16 @@ int orc_num_threads(void) {
 #endif
 }
 
+/* threads of the following parallel regions (a launcher's OMP_NUM_THREADS=1
+   would otherwise leave the timed CPU baseline on one core) */
+void orc_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 /* ------------------------------------------------------------------------ */
 /* real-space pair sum (non-periodic frames)                                */
 /* ------------------------------------------------------------------------ */

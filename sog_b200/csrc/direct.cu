@@ -12,6 +12,8 @@
 #include <string>
 #include <vector>
 
+#include <cuda.h>
+
 #include "frames.cuh"
 #include "plan.hpp"
 
@@ -323,7 +325,8 @@ int direct_impl(sog_direct *d, const sog_direct_args *a, cudaStream_t st) {
       d->redtmp.reserve(sizeof(double) * std::max(reduce_tmp_elems(nf, nch, kb, 2),
                                                    reduce_tmp_elems(nf, nch, kb, nx_acc))))
     return fail(SOG_ERR_NOMEM, "device allocation failed (direct)");
-  k_qsums<T><<<dim3(nf, nch, qs), 256, 0, st>>>((const T *)a->charges, nch, geom, d->qpart.as<double>());
+  k_qsums<T><<<dim3(nf, nch, qs), 256, 0, st>>>((const T *)a->charges, nch, geom, d->qpart.as<double>(),
+                                                (const T *)a->positions, d->status.as<unsigned>());
   k_reduce_parts<<<dim3(nf, nch, 1), 256, 0, st>>>(d->qpart.as<double>(), nf, nch, qs, 2, 2,
                                                   d->qsum.as<double>());
   after(tr, st, "qsums");
@@ -490,22 +493,63 @@ __global__ void k_noalloc_frames(const NoAllocFrames p, FrameHost *fh, int *nk, 
   if (threadIdx.x == 0) status[0] = 0u;
 }
 
-// Device address of the scratch array for the current device.  The first
-// call on a device resolves it (this may load the module on that device).
+// Device address of the scratch array in the calling thread's current CUDA
+// context.  A symbol's device address belongs to a context, not to a device
+// ordinal: after cudaDeviceReset, or with another driver-API context current,
+// an address cached per ordinal would be stale.  So the cache is keyed by the
+// context's unique id (cuCtxGetId; ids are never reused within a process,
+// unlike context handles), and the first call in each context resolves the
+// address with cudaGetSymbolAddress (which may load the module into that
+// context).  The two driver entry points come through the runtime, so the
+// library needs no link to the driver library.
+using PfnCtxGetCurrent = CUresult (*)(CUcontext *);
+using PfnCtxGetId = CUresult (*)(CUcontext, unsigned long long *);
+
 int noalloc_scratch(unsigned char **out) {
   static std::mutex mu;
-  static unsigned char *addr[64] = {};
-  int dev = 0;
-  SOG_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return fail(SOG_ERR_UNSUPPORTED, "device ordinal above 63");
+  static PfnCtxGetCurrent get_current = nullptr;
+  static PfnCtxGetId get_id = nullptr;
+  struct Entry {
+    unsigned long long id;
+    unsigned char *addr;
+  };
+  static Entry cache[16] = {};
+  static int next = 0;
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
-    void *p = nullptr;
+  if (!get_current || !get_id) {
+    void *f1 = nullptr, *f2 = nullptr;
+    cudaDriverEntryPointQueryResult q1 = cudaDriverEntryPointSymbolNotFound, q2 = cudaDriverEntryPointSymbolNotFound;
+    SOG_CUDA_TRY(cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1));
+    SOG_CUDA_TRY(cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2));
+    if (q1 != cudaDriverEntryPointSuccess || q2 != cudaDriverEntryPointSuccess || !f1 || !f2)
+      return fail(SOG_ERR_CUDA, "driver entry points cuCtxGetCurrent / cuCtxGetId unavailable");
+    get_current = reinterpret_cast<PfnCtxGetCurrent>(f1);
+    get_id = reinterpret_cast<PfnCtxGetId>(f2);
+  }
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS) return fail(SOG_ERR_CUDA, "cuCtxGetCurrent failed");
+  void *p = nullptr;
+  if (!ctx) {
+    // no context current yet: the runtime call makes the device's primary
+    // context current (and resolves the address in it)
     const cudaError_t e = cudaGetSymbolAddress(&p, g_direct_scratch);
     if (e != cudaSuccess) return fail(SOG_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-    addr[dev] = static_cast<unsigned char *>(p);
+    if (get_current(&ctx) != CUDA_SUCCESS || !ctx) return fail(SOG_ERR_CUDA, "no CUDA context current");
   }
-  *out = addr[dev];
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return fail(SOG_ERR_CUDA, "cuCtxGetId failed");
+  for (const Entry &e : cache)
+    if (e.addr && e.id == id) {
+      *out = e.addr;
+      return SOG_OK;
+    }
+  if (!p) {
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_direct_scratch);
+    if (e != cudaSuccess) return fail(SOG_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+  }
+  cache[next] = Entry{id, static_cast<unsigned char *>(p)};
+  next = (next + 1) % 16;
+  *out = static_cast<unsigned char *>(p);
   return SOG_OK;
 }
 
@@ -520,7 +564,7 @@ struct Carve {
 };
 
 template <typename T>
-int direct_noalloc_impl(const sog_direct_args *a, cudaStream_t st) {
+int direct_noalloc_impl(const sog_direct_args *a, unsigned *status_out, cudaStream_t st) {
   const int nf = a->nframes, nch = a->nchannels, M = a->n_gauss;
   if (nf > kNoAllocFrames) return fail(SOG_ERR_INVALID, "no-alloc direct k-sum: more than 64 frames in one call");
   NoAllocFrames frames;
@@ -574,7 +618,9 @@ int direct_noalloc_impl(const sog_direct_args *a, cudaStream_t st) {
   FrameHost *fhd = reinterpret_cast<FrameHost *>(s + o_fh);
   int *nkd = reinterpret_cast<int *>(s + o_nk);
   FrameGeom *geom = reinterpret_cast<FrameGeom *>(s + o_geom);
-  unsigned *status = reinterpret_cast<unsigned *>(s + o_status);
+  // the caller's status word when given (cleared by the first kernel, then
+  // or-ed by every kernel of the call), else a word of the scratch
+  unsigned *status = status_out ? status_out : reinterpret_cast<unsigned *>(s + o_status);
   double *qsum = reinterpret_cast<double *>(s + o_qsum);
   double *qpart = reinterpret_cast<double *>(s + o_qpart);
   double *tmp = reinterpret_cast<double *>(s + o_tmp);
@@ -584,7 +630,8 @@ int direct_noalloc_impl(const sog_direct_args *a, cudaStream_t st) {
   k_frame_setup<T><<<nblk(nf, 128), 128, 0, st>>>((const T *)a->cells, fhd, geom, nf, SOG_KCONV_PHYSICAL, 1, 1, 1,
                                                   status);
   count_launch();
-  k_qsums<T><<<dim3(nf, nch, qs), 256, 0, st>>>((const T *)a->charges, nch, geom, qpart);
+  k_qsums<T><<<dim3(nf, nch, qs), 256, 0, st>>>((const T *)a->charges, nch, geom, qpart,
+                                                (const T *)a->positions, status);
   k_reduce_parts<<<dim3(nf, nch, 1), 256, 0, st>>>(qpart, nf, nch, qs, 2, 2, qsum);
   count_launch();
   count_launch();
@@ -611,9 +658,14 @@ int direct_noalloc_impl(const sog_direct_args *a, cudaStream_t st) {
     count_launch();
   }
   if ((a->forces || a->potential) && maxat > 0) {
-    k_direct_atoms<T><<<dim3(nblk(maxat, 128), nf), 128, 0, st>>>(da, (const T *)a->positions,
-                                                                  (const T *)a->charges, a->norm_factor,
-                                                                  (T *)a->forces, (T *)a->potential);
+    // the launch shapes of sog_direct_forward: one warp per frame of at most 32 atoms
+    if (maxat <= 32)
+      k_direct_atoms<T, 32><<<dim3(1, nf), 32, 0, st>>>(da, (const T *)a->positions, (const T *)a->charges,
+                                                        a->norm_factor, (T *)a->forces, (T *)a->potential);
+    else
+      k_direct_atoms<T><<<dim3(nblk(maxat, 128), nf), 128, 0, st>>>(da, (const T *)a->positions,
+                                                                    (const T *)a->charges, a->norm_factor,
+                                                                    (T *)a->forces, (T *)a->potential);
     count_launch();
   }
   reduce_parts(da.part, nf, nch, kb, 2, 2, redE, tmp, st);
@@ -661,7 +713,8 @@ int direct_noalloc_impl(const sog_direct_args *a, cudaStream_t st) {
 }  // namespace
 }  // namespace sogb
 
-extern "C" int sog_direct_forward_noalloc(int dtype, const sog_direct_args *a, void *stream) {
+extern "C" int sog_direct_forward_noalloc(int dtype, const sog_direct_args *a, unsigned int *status,
+                                          void *stream) {
   if (!a) return fail(SOG_ERR_INVALID, "null argument");
   if (dtype != SOG_DTYPE_F64 && dtype != SOG_DTYPE_F32) return fail(SOG_ERR_INVALID, "bad dtype");
   if (a->nframes <= 0) return SOG_OK;
@@ -672,6 +725,6 @@ extern "C" int sog_direct_forward_noalloc(int dtype, const sog_direct_args *a, v
     return fail(SOG_ERR_UNSUPPORTED, "direct k-sum supports 1..8 charge channels");
   if (a->n_gauss < 1 || a->n_gauss > kMaxGauss) return fail(SOG_ERR_INVALID, "n_gauss must be in [1, 64]");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (dtype == SOG_DTYPE_F64) return direct_noalloc_impl<double>(a, st);
-  return direct_noalloc_impl<float>(a, st);
+  if (dtype == SOG_DTYPE_F64) return direct_noalloc_impl<double>(a, status, st);
+  return direct_noalloc_impl<float>(a, status, st);
 }

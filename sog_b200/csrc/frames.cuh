@@ -105,18 +105,26 @@ __global__ void k_frame_setup(const T *__restrict__ cells, const FrameHost *__re
 // chunk of the frame's atoms (fixed-order tree); reduced by reduce_parts.
 template <typename T>
 __global__ void k_qsums(const T *__restrict__ q, int nch, const FrameGeom *__restrict__ geom,
-                        double *__restrict__ part) {
+                        double *__restrict__ part, const T *__restrict__ pos = nullptr,
+                        unsigned *status = nullptr) {
   const int f = blockIdx.x, c = blockIdx.y, z = blockIdx.z, nz = gridDim.z;
   const FrameGeom &g = geom[f];
   const int64_t chunk = ((int64_t)g.natoms + nz - 1) / nz;
   const int64_t i0 = (int64_t)z * chunk, i1 = min((int64_t)g.natoms, i0 + chunk);
   double s1 = 0.0, s2 = 0.0;
+  bool bad = false;
   for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
     double v = (double)q[(g.atom_begin + i) * nch + c];
-    if (!isfinite(v)) v = 0.0;
+    if (!isfinite(v)) { v = 0.0; bad = true; }
+    // positions checked once, by the channel-0 blocks (when a status word is given)
+    if (status && c == 0) {
+      const T *r = pos + (g.atom_begin + i) * 3;
+      if (!isfinite((double)r[0]) || !isfinite((double)r[1]) || !isfinite((double)r[2])) bad = true;
+    }
     s1 += v;
     s2 += v * v;
   }
+  if (bad && status) raise_status(status, kStatusNonFinite);
   __shared__ double r1[256], r2[256];
   r1[threadIdx.x] = s1;
   r2[threadIdx.x] = s2;

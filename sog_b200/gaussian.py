@@ -13,20 +13,24 @@ Solvers:
   * particle-mesh with CubeS2 (``use_cubes2_fft=True``, ``cubes2_order`` 4/6;
     cubes2_fft.py:925-1133, Cubes2FFTFunction.backward :747-869).
 Added keys (defaults keep the reference behaviour): ``use_bspline_fft``,
-``bspline_order``, ``mesh_k_convention`` ("physical" | "reference"),
+``bspline_order``, ``mesh_k_convention`` ("reference" | "physical"; default
+"reference" for QuadS and CubeS2, whose Python solvers define it, and
+"physical" for the B-spline mesh, which follows lmp/sog.cpp),
 ``mesh_alias_extent``, and ``mesh_decomposition`` ("none" | "slab") with
 ``process_group`` and ``slab_transport`` ("peer" | "exchange"): "slab"
 splits one frame's mesh over the ranks of the process group (z slabs,
 transposes over NVLink; ``sog_b200.slab``), each rank passing the whole
 system and getting the whole result.
 
-Deliberate differences, each documented in DESIGN.md:
+Deliberate differences from the reference:
   * raw-mode ``amp`` tensors are not scaled in place (gaussian.py:236 does);
   * ``use_quads_fft`` selects the mesh even for all-periodic batches (the
     reference's batched direct gate shadows it, gaussian.py:444-548);
-  * the mesh wave vector is k = 2 pi cell^-1 m (the reciprocal vector; the
-    reference's mesh uses m cell^-1, quads_fft.py:255-257, which differs for
-    triclinic cells) unless ``mesh_k_convention="reference"``;
+  * ``mesh_k_convention="physical"`` (opt-in for QuadS / CubeS2, the default of
+    the B-spline mesh) takes the mesh wave vector k = 2 pi cell^-1 m, the
+    reciprocal vector the direct k-sum uses (gaussian.py:1040); the
+    reference's mesh solvers use m cell^-1 (quads_fft.py:255-257), which
+    differs for triclinic cells and is what "reference" reproduces;
   * explicit forces (and virial) are returned for every solver, including the
     direct k-sum where the reference returns None.
 """
@@ -112,7 +116,7 @@ class Gaussian(nn.Module):
                  use_cubes2_fft: bool = False, cubes2_phi_max: Optional[float] = None,
                  cubes2_order: int = 4, use_quads_fft: bool = False, quads_order: int = 6,
                  use_bspline_fft: bool = False, bspline_order: int = 6,
-                 mesh_k_convention: str = "physical", mesh_alias_extent: int = 8,
+                 mesh_k_convention: Optional[str] = None, mesh_alias_extent: int = 8,
                  mesh_decomposition: str = "none", process_group: Optional[Any] = None,
                  slab_transport: str = "peer", **_kwargs: Any):
         super().__init__()
@@ -230,6 +234,10 @@ class Gaussian(nn.Module):
             raise ValueError("`bspline_order` should be 4, 5 or 6.")
         if self.use_quads_fft and self.quads_order not in (4, 6):
             raise ValueError(f"Unsupported QuadS order: {self.quads_order}. Supported: (4, 6).")
+        if mesh_k_convention is None:
+            # the family _mesh_kind selects: CubeS2 first, then B-spline, then QuadS
+            mesh_k_convention = ("physical" if (self.use_bspline_fft and not self.use_cubes2_fft)
+                                 else "reference")
         self.mesh_k_convention = _normalize_mode(mesh_k_convention, {"physical", "reference"},
                                                  "mesh_k_convention")
         self.mesh_alias_extent = int(mesh_alias_extent)

@@ -17,6 +17,7 @@ from dataclasses import dataclass, field
 from typing import List, Optional, Tuple
 
 import torch
+from torch.autograd.function import once_differentiable
 
 from . import _lib
 
@@ -173,6 +174,7 @@ class SolveFunction(torch.autograd.Function):
         return tuple(outs)
 
     @staticmethod
+    @once_differentiable
     def backward(ctx, gE, gF, gV):
         forces, pot, gamp, gbw2 = ctx.saved_tensors
         grad_q = grad_r = grad_a = grad_b = None

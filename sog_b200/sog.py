@@ -78,7 +78,8 @@ class Sog(nn.Module):
         self.quads_order = int(args.get("quads_order", 6))
         self.use_bspline_fft = bool(args.get("use_bspline_fft", False))
         self.bspline_order = int(args.get("bspline_order", 6))
-        self.mesh_k_convention = str(args.get("mesh_k_convention", "physical"))
+        mkc = args.get("mesh_k_convention", None)
+        self.mesh_k_convention = None if mkc is None else str(mkc)
         self.mesh_alias_extent = int(args.get("mesh_alias_extent", 8))
         self.mesh_decomposition = str(args.get("mesh_decomposition", "none"))
         self.slab_transport = str(args.get("slab_transport", "peer"))

@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this folder by running the reference.
 
-Run in a container that has the reference tree (default /root/reference, or
-$SOG_REFERENCE); the fixtures are committed so the GPU box never needs it:
+Run where the reference tree is checked out, naming it in $SOG_REFERENCE; the
+fixtures are committed so the GPU box never needs it:
 
-    python tests/golden/make_golden.py
+    SOG_REFERENCE=<path to the sog checkout> python tests/golden/make_golden.py
 
 Every case stores its inputs and the reference's outputs (fp64).  Sources:
   * QuadS and CubeS2 mesh paths: ``Gaussian(use_quads_fft=True)`` /
@@ -33,7 +33,9 @@ import warnings
 import numpy as np
 import torch
 
-REF = os.environ.get("SOG_REFERENCE", "/root/reference")
+REF = os.environ.get("SOG_REFERENCE")
+if not REF:
+    raise SystemExit("set SOG_REFERENCE to the reference checkout (the folder holding src/sog)")
 sys.path.insert(0, os.path.join(REF, "src"))
 warnings.filterwarnings("ignore", category=DeprecationWarning)
 
@@ -364,9 +366,52 @@ def realspace_cases():
                                          trainable=True))
 
 
+def cfg3_case():
+    """Config 3 at full size through the reference QuadS order-4 mesh: 20,000
+    atoms in the 40/42/45 A, 80/95/105 degree cell, 96 x 100 x 108 mesh.
+    Inputs come from tests/_cases.cfg3_inputs (seeded numpy); the fixture
+    stores their digest and the reference's outputs only: explicit E, ik
+    forces and virial (quads_fft.py:209-326 via compute_bundle), and autograd
+    dE/dq, dE/d(amp, bw2) and dE/dr (the derivative of the spread weights)
+    of the energy-only call."""
+    sys.path.insert(0, os.path.dirname(os.path.dirname(OUT)))
+    from tests._cases import cfg3_inputs, digest
+    c = cfg3_inputs()
+    r = torch.tensor(c["r"], dtype=F64)
+    q = torch.tensor(c["q"], dtype=F64)
+    cell = torch.tensor(c["cell"], dtype=F64).unsqueeze(0)
+    batch = torch.zeros(r.shape[0], dtype=torch.int64)
+    amp_raw = torch.tensor(c["amp_raw"], dtype=F64)
+    bw = torch.tensor(c["bw"], dtype=F64)
+
+    def make():
+        g = Gaussian(n_dl=c["n_dl"], amp=amp_raw.clone(), bandwidth=bw.clone(), trainable=True,
+                     use_quads_fft=True, quads_order=c["order"])
+        g._enable_batched_direct = False
+        return g
+    g = make()
+    out = g.compute_bundle(q=q, r=r, cell=cell, batch=batch, compute_force=True,
+                           compute_virial=True)
+    g2 = make()
+    qg = q.clone().requires_grad_(True)
+    rg = r.clone().requires_grad_(True)
+    e = g2.compute_bundle(q=qg, r=rg, cell=cell, batch=batch)["energy"]
+    e.sum().backward()
+    rec = dict(digest=np.array(digest(c["r"], c["q"], c["cell"], c["amp_raw"], c["bw"])),
+               amp=g.amp.detach().numpy(), bw2=g.bandwidth.detach().numpy(),
+               energy=out["energy"].detach().numpy(), forces=out["forces"].detach().numpy(),
+               virial=out["virial"].detach().numpy(), grad_q=qg.grad.numpy(),
+               grad_r=rg.grad.numpy(), grad_amp=g2.amp.grad.numpy(),
+               grad_bw2=g2.bandwidth.grad.numpy())
+    np.savez_compressed(os.path.join(OUT, "cfg3_quads4.npz"), **rec)
+    print("cfg3_quads4", rec["energy"])
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    if sys.argv[1:] == ["cubes2"]:
+    if sys.argv[1:] == ["cfg3"]:
+        cfg3_case()
+    elif sys.argv[1:] == ["cubes2"]:
         cubes2_cases()
     elif sys.argv[1:] == ["realspace"]:
         realspace_cases()

@@ -189,7 +189,8 @@ def test_quads_physical_convention_matches_oracle_triclinic():
     amp = 1.0 / (bw * math.sqrt(2 * math.pi)) * bw * bw
     ref = _oracle_bundle(r, q, cell[None], np.zeros(60, int), amp, bw * bw, O.QUADS, 6, 0.7)
     g = Gaussian(n_dl=0.7, amp=torch.tensor(amp), bandwidth=torch.tensor(bw * bw),
-                 kernel_param_mode="internal", use_quads_fft=True, quads_order=6).to(DEV)
+                 kernel_param_mode="internal", use_quads_fft=True, quads_order=6,
+                 mesh_k_convention="physical").to(DEV)
     out = g.compute_bundle(q=_t(q), r=_t(r), cell=_t(cell[None]), compute_force=True)
     assert _rel(out["energy"].detach().cpu().numpy(), ref["energy"]) < E_TOL
     assert np.abs(out["forces"].cpu().numpy() - ref["forces"]).max() < F_TOL
@@ -270,7 +271,7 @@ def test_cubes2_physical_convention_matches_oracle_triclinic(order):
     bw = np.geomspace(1.0, 6.0, 5)
     amp = 1.0 / (bw * np.sqrt(2 * np.pi))
     g = Gaussian(n_dl=0.8, amp=torch.tensor(amp), bandwidth=torch.tensor(bw), use_cubes2_fft=True,
-                 cubes2_order=order, trainable=False).to(DEV)
+                 cubes2_order=order, trainable=False, mesh_k_convention="physical").to(DEV)
     out = g.compute_bundle(q=_t(q), r=_t(r), cell=_t(cell[None]), compute_force=True, compute_virial=True)
     grid, ksm = grid_ndl(cell, 0.8)
     ref = O.bundle(r, q, cell[None], np.zeros(n, dtype=np.int64), g.amp.detach().cpu().numpy(),

@@ -96,6 +96,16 @@ def test_gaussian_validation_errors():
         Gaussian(mesh_k_convention="sideways")
 
 
+def test_mesh_k_convention_defaults_follow_the_reference_solvers():
+    # QuadS / CubeS2 reproduce quads_fft.py:255-257 (m cell^-1) unless asked otherwise
+    assert Gaussian(use_quads_fft=True).mesh_k_convention == "reference"
+    assert Gaussian(use_cubes2_fft=True).mesh_k_convention == "reference"
+    assert Gaussian(use_bspline_fft=True).mesh_k_convention == "physical"
+    assert Gaussian(use_cubes2_fft=True, use_bspline_fft=True).mesh_k_convention == "reference"
+    assert Gaussian(use_quads_fft=True, mesh_k_convention="physical").mesh_k_convention == "physical"
+    assert Sog({"use_atomwise": False, "use_quads_fft": True}).gaussian.mesh_k_convention == "reference"
+
+
 # ---- restated from the reference's test_sog_kernel_modes.py / test_r_cut_sigma.py ----
 def test_auto_tensor_mode_uses_external_for_differentiable_inputs():
     bw2 = torch.tensor([1.2, 1.8], dtype=torch.float64, requires_grad=True)

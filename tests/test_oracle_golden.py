@@ -186,3 +186,23 @@ def test_bspline_mesh_converges_to_direct():
         errs.append(abs(m["energy"] - d["energy"]) / abs(d["energy"]))
         assert np.abs(m["forces"] - d["forces"]).max() < 1e-3
     assert errs[1] < errs[0] < 1e-3
+
+
+def test_oracle_config3_full_size_matches_reference_quads4():
+    """20,000-atom triclinic cell on the 96 x 100 x 108 mesh: the oracle's
+    QuadS-4 (reference wave vector) against the reference itself."""
+    from tests._cases import cfg3_inputs, digest
+    c = cfg3_inputs()
+    g = load("cfg3_quads4")
+    assert str(g["digest"]) == digest(c["r"], c["q"], c["cell"], c["amp_raw"], c["bw"])
+    grid, ksm = grid_ndl(c["cell"], c["n_dl"])
+    assert grid == (96, 100, 108)
+    res = O.bundle(c["r"], c["q"], c["cell"][None], np.zeros(len(c["r"]), int), g["amp"], g["bw2"],
+                   solver="mesh", grids=[grid], k_sq_max=[ksm], spline=O.QUADS, order=4,
+                   want_virial=True, kconv=1)
+    assert abs(res["energy"][0] - g["energy"][0]) < 1e-12 * abs(g["energy"][0])
+    assert np.abs(res["forces"] - g["forces"]).max() < 1e-11
+    assert np.abs(res["virial"] - g["virial"]).max() < 1e-11 * np.abs(g["virial"]).max()
+    assert np.abs(res["potential"][:, 0] - g["grad_q"]).max() < 1e-11
+    assert np.allclose(res["grad_amp"][0], g["grad_amp"], rtol=1e-11, atol=0)
+    assert np.allclose(res["grad_bw2"][0], g["grad_bw2"], rtol=1e-11, atol=0)
