@@ -236,7 +236,9 @@ __global__ void k_finalize_frames(FinalArgs a, int nf) {
   const double sc = a.direct ? 1.0 / (2.0 * V) : 0.5 * V / (N3 * N3);
   const T *amp = (const T *)a.amp;
   const T *bw2 = (const T *)a.bw2;
-  const double diag = (a.redD ? a.redD[f] : a.redE[((int64_t)f * a.nch + 0) * 2 + 1]) / (2.0 * V);
+  // self sum sum_w gS: from the Green-table pass (redD) and / or from the
+  // pass that evaluated the Green function on the fly (channel 0's second sum)
+  const double diag = ((a.redD ? a.redD[f] : 0.0) + a.redE[((int64_t)f * a.nch + 0) * 2 + 1]) / (2.0 * V);
   double E = 0.0, Q = 0.0, QQ = 0.0, pen = 0.0;
   for (int c = 0; c < a.nch; ++c) {
     const double qs = a.qsum[((int64_t)f * a.nch + c) * 2 + 0];

@@ -303,7 +303,7 @@ struct SpreadArgs {
   const T *s_q;        // channel slice [nslots]
   const uint32_t *bin_start;
   const FrameGeom *geom;
-  T *rho;              // [nf][ng]
+  void *rho;           // [nf][ng] of the grid type TG of the kernel (fp64 for every plan)
   AtomGrid ag;
   int spline;
   int ntx, nty, ntz;
@@ -350,7 +350,9 @@ __device__ int axis_bins(int lo, int len, int n, int nb, int *out) {
 // NT stencil terms (StencilTerms): 1 for the separable splines, 3 / 4 for
 // CubeS2 order 4 / 6.  CH candidates per chunk (fewer with three kinds, to
 // keep the staged weights at two CTAs per SM).
-template <typename T, int P, int NT = 1>
+// TG: grid type; the mesh values are accumulated and stored in it (an fp32
+// plan's atom data spread into an fp64 mesh).
+template <typename T, int P, int NT = 1, typename TG = T>
 __global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? SOG_SPREAD_MINB : 2) k_spread(SpreadArgs<T> a) {
   using ST = StencilTerms<NT>;
   constexpr int KK = ST::K;
@@ -449,9 +451,9 @@ __global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? SOG_SPREAD_MINB : 2)
   const int lx = threadIdx.x % kTileX, ly = threadIdx.x / kTileX;
   const int gy = y0 + ly;
   const bool own = lx < txv && ly < tyv;
-  T acc[kTileZ];
+  TG acc[kTileZ];
 #pragma unroll
-  for (int z = 0; z < kTileZ; ++z) acc[z] = T(0);
+  for (int z = 0; z < kTileZ; ++z) acc[z] = TG(0);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const unsigned lt = (1u << lane) - 1u;
@@ -577,7 +579,7 @@ __global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? SOG_SPREAD_MINB : 2)
             const T wxy = c_wx[(ST::x(tt) * P + dx) * CH + j] * c_wy[(ST::y(tt) * P + dy) * CH + j] * qj;
             const T *wz = c_wz + ST::z(tt) * kTileZ * CH + j;
 #pragma unroll
-            for (int z = 0; z < kTileZ; ++z) acc[z] += wxy * wz[z * CH];
+            for (int z = 0; z < kTileZ; ++z) acc[z] += (TG)wxy * (TG)wz[z * CH];
           }
         }
       }
@@ -587,7 +589,7 @@ __global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? SOG_SPREAD_MINB : 2)
   if (own) {
     const int gx = x0 + lx;
     const int64_t plane = (int64_t)ag.nx * ag.ny;
-    T *out = a.rho + (int64_t)f * plane * a.zcnt + (int64_t)gy * ag.nx + gx;
+    TG *out = static_cast<TG *>(a.rho) + (int64_t)f * plane * a.zcnt + (int64_t)gy * ag.nx + gx;
 #pragma unroll
     for (int z = 0; z < kTileZ; ++z)
       if (z < tzv) out[(int64_t)(z0 - a.zlo + z) * plane] = acc[z];
@@ -600,11 +602,15 @@ __global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? SOG_SPREAD_MINB : 2)
 template <typename T>
 struct KsArgs {
   const cplx_t<T> *spec;   // [nf][nh]
-  cplx_t<T> *fspec;        // [nf][F][nh]
+  // [nf][F][nh] field spectra; complex of the field type the writing kernel
+  // is instantiated with (its TO: T itself, or float for the fp32 field path
+  // of an fp32 plan whose spectrum is fp64)
+  void *fspec;
   const FrameGeom *geom;
   const double *tx, *ty, *tz;  // per-axis Green factors
   const double *sx, *sy, *sz;  // B-spline alias sums
-  const T *amp, *bw2;
+  const void *amp, *bw2;   // [M] kernel parameters: float when p32, else double
+  int p32;
   int M, spline, order, alias_extent;
   int nx, ny, nz, nxh;
   int64_t nh;
@@ -629,14 +635,37 @@ struct KsArgs {
   // with zdst[0] set, block b goes to zdst[b] + [nfield][zblk][nyl][nxh]
   // instead (the receive buffer of rank b, possibly on another GPU)
   int zblk;
-  cplx_t<T> *zdst[kMaxSlabRanks];
+  void *zdst[kMaxSlabRanks];
   // column layout of the spectrum rows held by this call: 0 = plain
   // (col = y*nxh + mx); cw > 0 = chunked (col = (xc*nyl + y)*cw + xw,
   // mx = xc*cw + xw), the receive layout of the peer slab transport in which
   // one tile of cw columns is contiguous for every z; with cw > 0 the fields
   // of z block b go to zdst[b] as [nfield][xc*nyl + y][zblk][cw]
   int cw;
+  // 1: the fused z pass computes the Green function of separable frames
+  // (green_separable) on the fly and sums their self term itself; k_green
+  // then only builds the tables of the other frames
+  int green_otf;
 };
+
+// kernel parameter m as a double
+__device__ __forceinline__ double kpar(const void *p, int p32, int m) {
+  return p32 ? (double)static_cast<const float *>(p)[m] : static_cast<const double *>(p)[m];
+}
+
+// complex value converted to the field type TO
+template <typename TO, typename C>
+__device__ __forceinline__ cplx_t<TO> to_field(const C &v) {
+  return cmk<cplx_t<TO>, TO>((TO)v.x, (TO)v.y);
+}
+
+// Frames whose Green function is separable: orthorhombic, no B-spline alias
+// inside the cutoff, at most 16 Gaussians, not CubeS2 (its variance
+// subtraction is not a per-axis product over the Cartesian components it uses)
+template <typename T>
+__device__ __forceinline__ bool green_separable(const KsArgs<T> &a, const FrameGeom &g) {
+  return g.ortho && a.btab && !g.pad && a.M <= 16 && a.spline != SOG_SPLINE_CUBES2;
+}
 
 // Column `col` of the spectrum rows -> (mx, local y); false for the pad
 // columns (mx >= nx/2+1) of the chunked layout.
@@ -842,66 +871,14 @@ __device__ ModeGreen mode_green(const KsArgs<T> &a, const FrameGeom &g, const do
 }
 
 
-template <typename T>
-__global__ void __launch_bounds__(256) k_kspace(KsArgs<T> a) {
-  using C = cplx_t<T>;
-  __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
-  __shared__ double red[2][8];
-  for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
-    s_amp[m] = (double)a.amp[m];
-    s_bw2[m] = (double)a.bw2[m];
-  }
-  __syncthreads();
-  const int f = blockIdx.y;
-  const FrameGeom &g = a.geom[f];
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  double accE = 0.0, accD = 0.0;
-  if (idx < a.nh) {
-    const int mx = (int)(idx % a.nxh);
-    const int64_t zy = idx / a.nxh;
-    const int iy = (int)(zy % a.ny), iz = (int)(zy / a.ny);
-    const double *bt = (g.ortho && a.btab) ? a.btab + (int64_t)f * a.btab_stride : nullptr;
-    const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr, bt);
-    const C r = a.spec[(int64_t)f * a.nh + idx];
-    const double rr = (double)r.x, ri = (double)r.y;
-    const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
-    if (mg.live) {
-      accE = w * mg.gE * (rr * rr + ri * ri);
-      accD = w * mg.gS;
-    }
-    if (a.nfield) {
-      const double inv = 1.0 / ((double)a.nx * a.ny * a.nz);
-      C *out = a.fspec + (int64_t)f * a.nfield * a.nh + idx;
-      int fo = 0;
-      if (a.want_force) {
-        const double sre = mg.gF * rr * inv, sim = mg.gF * ri * inv;
-        for (int c = 0; c < 3; ++c) out[(int64_t)c * a.nh] = cmk<C, T>((T)(-mg.k[c] * sim), (T)(mg.k[c] * sre));
-        fo = 3;
-      }
-      if (a.nfield > fo) out[(int64_t)fo * a.nh] = cmk<C, T>((T)(mg.gE * rr * inv), (T)(mg.gE * ri * inv));
-    }
-  }
-  accE = warp_sum(accE);
-  accD = warp_sum(accD);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) { red[0][warp] = accE; red[1][warp] = accD; }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double e = 0.0, d = 0.0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) { e += red[0][w]; d += red[1][w]; }
-    double *p = a.part + ((int64_t)f * gridDim.x + blockIdx.x) * 2;
-    p[0] = e;
-    p[1] = d;
-  }
-}
-
 // k-space step with the Green function read from k_green's tables (any nz):
 // thread per (iy, mx) column walking its share of the z planes, energy
 // partial sum and the ik / potential field spectra.  Same arithmetic as the
 // field step of k_zfused_g.
-template <typename T>
+template <typename T, typename TO = T>
 __global__ void __launch_bounds__(256) k_kspace_tab(KsArgs<T> a) {
   using C = cplx_t<T>;
+  using CO = cplx_t<TO>;
   __shared__ double red[8];
   const int f = blockIdx.y;
   const FrameGeom &g = a.geom[f];
@@ -918,7 +895,7 @@ __global__ void __launch_bounds__(256) k_kspace_tab(KsArgs<T> a) {
     const C *sp = a.spec + (int64_t)f * a.nh + col;
     const double *ge = a.gtab + (int64_t)f * a.nh + col;
     const double *gf = (g.pad && a.gtabF) ? a.gtabF + (int64_t)f * a.nh + col : nullptr;
-    C *out = a.nfield ? a.fspec + (int64_t)f * a.nfield * a.nh + col : nullptr;
+    CO *out = a.nfield ? static_cast<CO *>(a.fspec) + (int64_t)f * a.nfield * a.nh + col : nullptr;
     double kxy[3];
 #pragma unroll
     for (int c = 0; c < 3; ++c) kxy[c] = g.kmat[c * 3 + 0] * mx + g.kmat[c * 3 + 1] * my;
@@ -937,11 +914,11 @@ __global__ void __launch_bounds__(256) k_kspace_tab(KsArgs<T> a) {
 #pragma unroll
           for (int c = 0; c < 3; ++c) {
             const double kc = kxy[c] + g.kmat[c * 3 + 2] * mz;
-            out[(int64_t)c * a.nh + o] = cmk<C, T>((T)(-kc * sim), (T)(kc * sre));
+            out[(int64_t)c * a.nh + o] = cmk<CO, TO>((TO)(-kc * sim), (TO)(kc * sre));
           }
           fo = 3;
         }
-        if (a.nfield > fo) out[(int64_t)fo * a.nh + o] = cmk<C, T>((T)(gE * inv * rr), (T)(gE * inv * ri));
+        if (a.nfield > fo) out[(int64_t)fo * a.nh + o] = cmk<CO, TO>((TO)(gE * inv * rr), (TO)(gE * inv * ri));
       }
     }
   }
@@ -963,17 +940,18 @@ __global__ void __launch_bounds__(256) k_kspace_tab(KsArgs<T> a) {
 // spectra make an extra round trip through HBM.  Energy / self partial sums per
 // CTA go to a.part[(f*nchunks + chunk)*2].  With write_spec the transformed
 // spectrum is also stored (for k_kspace_extra).
-template <typename T>
+template <typename T, typename TO = T>
 __global__ void __launch_bounds__(256, 2) k_zfused(KsArgs<T> a, int ic, RadixPlan rpz,
                                                  const cplx_t<T> *__restrict__ twz, int write_spec) {
   using C = cplx_t<T>;
+  using CO = cplx_t<TO>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   C *sm = reinterpret_cast<C *>(smem_raw);
   __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
   __shared__ double red[2][32];
   for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
-    s_amp[m] = (double)a.amp[m];
-    s_bw2[m] = (double)a.bw2[m];
+    s_amp[m] = kpar(a.amp, a.p32, m);
+    s_bw2[m] = kpar(a.bw2, a.p32, m);
   }
   __syncthreads();
   const int n = rpz.n, TPT = n / kEPT;
@@ -1023,7 +1001,7 @@ __global__ void __launch_bounds__(256, 2) k_zfused(KsArgs<T> a, int ic, RadixPla
     s_g[(2 * e + 1) * nthr + threadIdx.x] = live ? mg.gE * inv : 0.0;
   }
   const int nfield = a.nfield;
-  C *out = a.fspec ? a.fspec + (int64_t)f * nfield * a.nh + (ok ? col : 0) : nullptr;
+  CO *out = a.fspec ? static_cast<CO *>(a.fspec) + (int64_t)f * nfield * a.nh + (ok ? col : 0) : nullptr;
   for (int fl = 0; fl < nfield; ++fl) {
     const bool force = a.want_force && fl < 3;
     double km = 0.0, kz = 0.0;
@@ -1047,9 +1025,9 @@ __global__ void __launch_bounds__(256, 2) k_zfused(KsArgs<T> a, int ic, RadixPla
     }
     reg_fft<T, +1, true>(wv, t, rpz, twz, sm + c, ic);
     if (ok) {
-      C *o = out + (int64_t)fl * a.nh;
+      CO *o = out + (int64_t)fl * a.nh;
 #pragma unroll
-      for (int e = 0; e < kEPT; ++e) o[(int64_t)(t + e * TPT) * inner] = wv[e];
+      for (int e = 0; e < kEPT; ++e) o[(int64_t)(t + e * TPT) * inner] = to_field<TO>(wv[e]);
     }
   }
   accE = warp_sum(accE);
@@ -1080,14 +1058,20 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
   __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
   __shared__ double red[8];
   for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
-    s_amp[m] = (double)a.amp[m];
-    s_bw2[m] = (double)a.bw2[m];
+    s_amp[m] = kpar(a.amp, a.p32, m);
+    s_bw2[m] = kpar(a.bw2, a.p32, m);
   }
   __syncthreads();
   const int f = blockIdx.y;
   const FrameGeom &g = a.geom[f];
-  const bool sep = g.ortho && a.btab && !g.pad && a.M <= 16 && a.spline != SOG_SPLINE_CUBES2;
-  if (sep != SEP) return;                 // block-uniform: the frame belongs to the other launch
+  const bool sep = green_separable(a, g);
+  if (sep != SEP) {
+    // block-uniform: the frame belongs to the other launch, or (green_otf)
+    // to the fused z pass, which then sums its self term: a zero partial here
+    if (!SEP && a.green_otf && threadIdx.x == 0)
+      a.partD[((int64_t)f * gridDim.z + blockIdx.z) * gridDim.x + blockIdx.x] = 0.0;
+    return;
+  }
   const int64_t inner = cols_inner(a);
   const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // (iy, mx) column
   // z planes of this block: the columns are split over gridDim.z
@@ -1178,19 +1162,23 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
 // NTH threads per CTA: 512 for a 512-point z transform gives tiles of 8
 // columns, so every field row it stores is 128 contiguous bytes (4-column
 // rows of 64 bytes store at half the bandwidth).
-template <typename T, int L, int NTH = 256>
+template <typename T, int L, int NTH = 256, typename TO = T>
 __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfused_g(KsArgs<T> a, int ic,
                                                                                   int64_t ntiles,
                                                      const cplx_t<T> *__restrict__ twz, int write_spec) {
   using C = cplx_t<T>;
+  using CO = cplx_t<TO>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ double red[NTH / 32];
+  __shared__ double red[2][NTH / 32];
+  __shared__ double s_amp[16];
   constexpr int n = 1 << L, TPT = n / kEPT;
   C *buf0 = reinterpret_cast<C *>(smem_raw);
   C *buf1 = buf0 + (size_t)n * ic;
   C *xbuf = buf1 + (size_t)n * ic;
   C *stg = xbuf + (size_t)padded_row(n) * ic;
   load_stage_twiddles<T, L, 0>(stg, twz);
+  if (threadIdx.x < 16) s_amp[threadIdx.x] = threadIdx.x < a.M ? kpar(a.amp, a.p32, threadIdx.x) : 0.0;
+  __syncthreads();
   const int c = threadIdx.x % ic, t = threadIdx.x / ic;
   const int64_t inner = cols_inner(a);
   const int64_t nchunks = (inner + ic - 1) / ic;
@@ -1214,20 +1202,56 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
     int mx = 0, yl = 0;
     const bool ok = col < inner && col_mode(a, col, mx, yl);
     const FrameGeom &g = a.geom[f];
-    // Green values of this thread's modes: loads in flight during the FFT
+    const int iy = a.y0 + yl;
+    const int my = signed_mode(iy, a.ny);
+    const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
+    // Green values of this thread's modes, ready before the tile is: on the
+    // fly for separable frames (K = sum_m amp_m Bx_m By_m Bz_m from the
+    // per-axis factors of lmp/sog.cpp:1375-1476, times the per-axis
+    // deconvolution; the same products in the same order as k_green's
+    // table), else loads from the table, in flight during the FFT
     double gs[kEPT];
-    const double *gp = a.gtab + (int64_t)f * a.nh + (ok ? col : 0);
+    double accD = 0.0;
+    if (a.green_otf && green_separable(a, g)) {   // frame-uniform
+      const int M = a.M;
+      const double *bt = a.btab + (int64_t)f * a.btab_stride;
+      const double *bx = bt, *by = bt + M * a.nxh, *bz = by + M * a.ny;
+      double axy[16];
 #pragma unroll
-    for (int e = 0; e < kEPT; ++e) gs[e] = ok ? gp[(int64_t)(t + e * TPT) * inner] : 0.0;
+      for (int m = 0; m < 16; ++m) axy[m] = (ok && m < M) ? s_amp[m] * bx[m * a.nxh + mx] * by[m * a.ny + iy] : 0.0;
+      const double kx = g.kmat[0] * mx, ky = g.kmat[4] * my;
+      const double kxy2 = kx * kx + ky * ky;
+      const double txy = ok ? a.tx[mx] * a.ty[iy] : 0.0;
+      const bool quads = a.spline == SOG_SPLINE_QUADS;
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) {
+        const int iz = t + e * TPT;
+        const int mz = signed_mode(iz, a.nz);
+        const double kz = g.kmat[8] * mz;
+        const double ksq = kxy2 + kz * kz;
+        const bool live = ok && !((mx | my | mz) == 0) && ksq <= g.k_sq_max;
+        double K = 0.0;
+        if (live) {
+#pragma unroll
+          for (int m = 0; m < 16; ++m)
+            if (m < M) K += axy[m] * bz[m * a.nz + iz];
+        }
+        double D = txy * a.tz[iz];
+        if (quads) D = 1.0 / (D < 1e-20 ? 1e-20 : D);
+        gs[e] = live ? K * D : 0.0;
+        if (live) accD += w * K;
+      }
+    } else {
+      const double *gp = a.gtab + (int64_t)f * a.nh + (ok ? col : 0);
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) gs[e] = ok ? gp[(int64_t)(t + e * TPT) * inner] : 0.0;
+    }
     cp_async_wait<1>();
     __syncthreads();
     C v[kEPT];
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) v[e] = cur[(t + e * TPT) * ic + c];
     ct_fft<T, -1, L, true>(v, t, stg, xbuf + c, ic);
-    const int iy = a.y0 + yl;
-    const int my = signed_mode(iy, a.ny);
-    const double w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
     double accE = 0.0;
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) {
@@ -1243,7 +1267,7 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
       for (int e = 0; e < kEPT; ++e) sp[(int64_t)(t + e * TPT) * inner] = v[e];
     }
     const double *gFp = (g.pad && a.gtabF) ? a.gtabF + (int64_t)f * a.nh + (ok ? col : 0) : nullptr;
-    C *out = a.fspec ? a.fspec + (int64_t)f * nfield * a.nh + (ok ? col : 0) : nullptr;
+    CO *out = a.fspec ? static_cast<CO *>(a.fspec) + (int64_t)f * nfield * a.nh + (ok ? col : 0) : nullptr;
     const int64_t zbs = (int64_t)a.zblk * inner;   // one field's z block
     auto store_field = [&](int fl, const C (&wv)[kEPT]) {
       if (!ok) return;
@@ -1253,10 +1277,12 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
         if (a.cw) {
           // chunked: this tile's cw columns are contiguous for every z
           const int64_t q = col / a.cw;
-          a.zdst[b][(int64_t)fl * zbs + (q * a.zblk + zl) * a.cw + (col - q * a.cw)] = wv[e];
+          static_cast<CO *>(a.zdst[b])[(int64_t)fl * zbs + (q * a.zblk + zl) * a.cw + (col - q * a.cw)] =
+              to_field<TO>(wv[e]);
         } else {
-          C *ob = a.zdst[0] ? a.zdst[b] + (int64_t)fl * zbs + col : out + ((int64_t)b * nfield + fl) * zbs;
-          ob[(int64_t)zl * inner] = wv[e];
+          CO *ob = a.zdst[0] ? static_cast<CO *>(a.zdst[b]) + (int64_t)fl * zbs + col
+                             : out + ((int64_t)b * nfield + fl) * zbs;
+          ob[(int64_t)zl * inner] = to_field<TO>(wv[e]);
         }
       }
     };
@@ -1311,14 +1337,21 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
       store_field(a.want_force ? 3 : 0, wv);
     }
     accE = warp_sum(accE);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = accE;
+    accD = warp_sum(accD);
+    if ((threadIdx.x & 31) == 0) {
+      red[0][threadIdx.x >> 5] = accE;
+      red[1][threadIdx.x >> 5] = accD;
+    }
     __syncthreads();
     if (threadIdx.x == 0) {
-      double e = 0.0;
-      for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) e += red[wi];
+      double e = 0.0, d = 0.0;
+      for (int wi = 0; wi < (int)(blockDim.x >> 5); ++wi) {
+        e += red[0][wi];
+        d += red[1][wi];
+      }
       double *p = a.part + ((int64_t)f * nchunks + chunk) * 2;
       p[0] = e;
-      p[1] = 0.0;
+      p[1] = d;   // self sum of on-the-fly frames (zero for table frames)
     }
     __syncthreads();
   }
@@ -1341,8 +1374,8 @@ __global__ void __launch_bounds__(256) k_kspace_extra(KsArgs<T> a, int want_grad
   __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss];
   __shared__ double red[8][4 * kMaxGauss + 13];
   for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
-    s_amp[m] = (double)a.amp[m];
-    s_bw2[m] = (double)a.bw2[m];
+    s_amp[m] = kpar(a.amp, a.p32, m);
+    s_bw2[m] = kpar(a.bw2, a.p32, m);
   }
   __syncthreads();
   const int f = blockIdx.y;
@@ -1797,6 +1830,16 @@ void allow_smem(K kernel, int bytes = 220 * 1024) {
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+// The plan's roots of unity of axis 0/1/2 in the transform type T (an fp32
+// plan keeps an fp64 copy for its fp64 forward transforms).
+template <typename T>
+const cplx_t<T> *tw_of(const sog_plan *p, int axis) {
+  const bool wide = sizeof(T) == 8 && p->d.dtype == SOG_DTYPE_F32;
+  const DevBuf &b = axis == 0 ? (wide ? p->twx64 : p->twx) : axis == 1 ? (wide ? p->twy64 : p->twy)
+                                                                        : (wide ? p->twz64 : p->twz);
+  return b.as<cplx_t<T>>();
+}
+
 // ---- FFT passes: register-resident kernels for power-of-two axes, the
 // generic shared-memory Stockham otherwise ----
 template <typename T>
@@ -1823,21 +1866,21 @@ void pass_x_fwd(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t rows, cudaStream_t
     const size_t sm = 2 * (size_t)rpc * n * sizeof(T) + ((size_t)rpc * padded_row(n / 2) + n + n / 2) * sizeof(C);
     allow_smem(k_r2c_pipe<T, L>);
     k_r2c_pipe<T, L><<<persistent_grid(k_r2c_pipe<T, L>, thr, sm, ntiles), thr, sm, st>>>(
-        rho, spec, rows, rpc, ntiles, p->twx.as<C>());
+        rho, spec, rows, rpc, ntiles, tw_of<T>(p, 0));
   });
   if (!done) {
     if (is_pow2(nx)) {
       const int rpc = reg_width<T>(nx, 256, 64 * 1024);
       k_rows_r2c_reg<T><<<nblocks(rows, rpc), (nx / kEPT) * rpc, (size_t)rpc * padded_row(nx) * sizeof(C), st>>>(
-          rho, spec, rows, rpc, p->rpx, p->twx.as<C>());
+          rho, spec, rows, rpc, p->rpx, tw_of<T>(p, 0));
     } else if (nx % 2 == 0) {
       const int rpc = rows_per_cta<T>(nx / 2);
       k_fft_r2c_xh<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx / 2, rpc), st>>>(
-          rho, spec, nx, rows, rpc, p->rpxh, p->twx.as<C>());
+          rho, spec, nx, rows, rpc, p->rpxh, tw_of<T>(p, 0));
     } else {
       const int rpc = rows_per_cta<T>(nx);
       k_fft_r2c_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx, rpc), st>>>(
-          rho, spec, nx, rows, rpc, p->rpx, p->twx.as<C>());
+          rho, spec, nx, rows, rpc, p->rpx, tw_of<T>(p, 0));
     }
   }
   after(&p->tr, st, "fft_r2c_x");
@@ -1863,7 +1906,7 @@ void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nframes, int64_
     const size_t sm = (2 * (size_t)rpc * F * rowsz + n + n / 2) * sizeof(C);
     allow_smem(k_c2r_pipe<T, L>);
     k_c2r_pipe<T, L><<<persistent_grid(k_c2r_pipe<T, L>, thr, sm, ntiles), thr, sm, st>>>(
-        fspec, freal, F, nzy, rows, rpc, ntiles, p->twx.as<C>());
+        fspec, freal, F, nzy, rows, rpc, ntiles, tw_of<T>(p, 0));
   });
   if (!done) {
     if (is_pow2(nx)) {
@@ -1872,17 +1915,17 @@ void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nframes, int64_
       const int64_t rows = nframes * nzy;
       const size_t sm = std::max((size_t)rpc * F * padded_row(nx) * sizeof(C), (size_t)rpc * nx * F * sizeof(T));
       k_rows_c2r_il<T><<<nblocks(rows, rpc), tpt * F * rpc, sm, st>>>(fspec, freal, F, nzy, rows, rpc, p->rpx,
-                                                                        p->twx.as<C>());
+                                                                        tw_of<T>(p, 0));
     } else if (nx % 2 == 0) {
       const int rpc = std::max(1, std::min(256 / F, rows_per_cta<T>(nx / 2 + 1) / F));
       const int64_t rows = nframes * nzy;
       k_fft_c2r_xh<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx / 2 + 1, rpc * F), st>>>(
-          fspec, freal, nx, rows, rpc, p->rpxh, p->twx.as<C>(), F, nzy);
+          fspec, freal, nx, rows, rpc, p->rpxh, tw_of<T>(p, 0), F, nzy);
     } else {
       const int rpc = std::max(1, rows_per_cta<T>(nx + 1) / F);
       const int64_t rows = nframes * nzy;
       k_fft_c2r_x<T><<<nblocks(rows, rpc), 256, fft_rows_smem<T>(nx + 1, rpc * F), st>>>(
-          fspec, freal, nx, rows, rpc, p->rpx, p->twx.as<C>(), F, nzy);
+          fspec, freal, nx, rows, rpc, p->rpx, tw_of<T>(p, 0), F, nzy);
     }
   }
   after(&p->tr, st, "fft_c2r_x");
@@ -1960,12 +2003,12 @@ size_t spread_smem() {
   return (size_t)CH * (KK * (kTileZ + 2 * P) + 1) * sizeof(T) + (size_t)CH * sizeof(int);
 }
 
-template <typename T, int P, int NT = 1>
+template <typename T, int P, int NT, typename TG>
 void launch_spread(const SpreadArgs<T> &sa, int nframes, cudaStream_t st, Tracer *tr) {
   const size_t sm = spread_smem<T, P, NT>();
-  allow_smem(k_spread<T, P, NT>, (int)sm);
+  allow_smem(k_spread<T, P, NT, TG>, (int)sm);
   const int64_t tiles = (int64_t)sa.ntx * sa.nty * sa.ntz * nframes;
-  k_spread<T, P, NT><<<(unsigned)tiles, kSpreadThreads, sm, st>>>(sa);
+  k_spread<T, P, NT, TG><<<(unsigned)tiles, kSpreadThreads, sm, st>>>(sa);
   after(tr, st, "spread");
 }
 
@@ -1986,17 +2029,17 @@ inline unsigned green_zsplit(unsigned gblocks, int nf, int nz) {
   return (unsigned)gz;
 }
 
-template <typename T>
+template <typename T, typename TG = T>
 void dispatch_spread(const SpreadArgs<T> &sa, int order, int nframes, cudaStream_t st, Tracer *tr) {
   if (sa.spline == SOG_SPLINE_CUBES2) {
-    if (order == 4) launch_spread<T, 4, 3>(sa, nframes, st, tr);
-    else launch_spread<T, 6, 4>(sa, nframes, st, tr);
+    if (order == 4) launch_spread<T, 4, 3, TG>(sa, nframes, st, tr);
+    else launch_spread<T, 6, 4, TG>(sa, nframes, st, tr);
     return;
   }
   switch (order) {
-    case 4: launch_spread<T, 4>(sa, nframes, st, tr); break;
-    case 5: launch_spread<T, 5>(sa, nframes, st, tr); break;
-    default: launch_spread<T, 6>(sa, nframes, st, tr); break;
+    case 4: launch_spread<T, 4, 1, TG>(sa, nframes, st, tr); break;
+    case 5: launch_spread<T, 5, 1, TG>(sa, nframes, st, tr); break;
+    default: launch_spread<T, 6, 1, TG>(sa, nframes, st, tr); break;
   }
 }
 
@@ -2154,18 +2197,32 @@ int prepare_atoms(sog_plan *p, const sog_mesh_args *a, cudaStream_t st, Prep &pr
   return SOG_OK;
 }
 
+// With ka.green_otf the fused z pass evaluates the separable frames' Green
+// function itself: only the other frames' tables are built here.
 template <typename T>
 void launch_green(const KsArgs<T> &ka, unsigned gblocks, int nf, unsigned gz, cudaStream_t st) {
-  const int zper = (ka.nz + (int)gz - 1) / (int)gz;
-  const size_t sm = ka.M <= 16 ? (size_t)zper * ((ka.M + 1) & ~1) * sizeof(double) : 0;
-  allow_smem(k_green<T, true>);
-  k_green<T, true><<<dim3(gblocks, nf, gz), 256, sm, st>>>(ka);
+  if (!ka.green_otf) {
+    const int zper = (ka.nz + (int)gz - 1) / (int)gz;
+    const size_t sm = ka.M <= 16 ? (size_t)zper * ((ka.M + 1) & ~1) * sizeof(double) : 0;
+    allow_smem(k_green<T, true>);
+    k_green<T, true><<<dim3(gblocks, nf, gz), 256, sm, st>>>(ka);
+    count_launch();
+  }
   k_green<T, false><<<dim3(gblocks, nf, gz), 256, 0, st>>>(ka);
 }
 
+// Precision: the charge grid, the forward transforms, the Green multiply and
+// the energy sums run in fp64 for every plan; an fp32 plan computes its
+// atom data, field spectra, inverse transforms and gather in fp32.  (The
+// k-space energy is a difference of two large sums, the mesh term and the
+// self term, so the forward transform's rounding is amplified by their
+// ratio: in fp32 it alone gave relative energy errors near 2e-5 on the
+// 131,072-atom 256^3 system.)
 template <typename T>
 int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
-  using C = cplx_t<T>;
+  using C = cplx_t<T>;       // field spectra
+  using TF = double;         // grid, forward spectrum, k-space
+  using CF = cplx_t<TF>;
   const int nf = a->nframes, nch = a->nchannels, M = a->n_gauss;
   const int nx = p->d.nx, ny = p->d.ny, nz = p->d.nz, nxh = p->nxh, P = p->d.order;
   const int64_t ng = p->ng, nh = p->nh;
@@ -2187,7 +2244,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   // the fused z pass writes one partial per tile; the generic k-space kernel one per block
   const int64_t part_blocks = std::max<int64_t>(ks_blocks, (int64_t)ny * nxh);
   const int nx_acc = 4 * M + 13;
-  if (p->rho.reserve(sizeof(T) * ng * nf) || p->spec.reserve(sizeof(C) * nh * nf) ||
+  if (p->rho.reserve(sizeof(TF) * ng * nf) || p->spec.reserve(sizeof(CF) * nh * nf) ||
       p->partE.reserve(sizeof(double) * 2 * part_blocks * nf * nch) ||
       (nfield && (p->fspec.reserve(sizeof(C) * nh * nf * nfield) ||
                   p->freal.reserve(sizeof(T) * ng * nf * nfield))) ||
@@ -2206,7 +2263,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   sa.s_t = p->s_t.as<T>();
   sa.bin_start = p->bin_start.as<uint32_t>();
   sa.geom = geom;
-  sa.rho = p->rho.as<T>();
+  sa.rho = p->rho.p;
   sa.ag = ag;
   sa.spline = p->d.spline;
   sa.ntx = (nx + kTileX - 1) / kTileX;
@@ -2216,15 +2273,16 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   sa.zlo = 0;
   sa.zcnt = nz;
 
-  KsArgs<T> ka;
+  KsArgs<TF> ka;
   std::memset(&ka, 0, sizeof(ka));
-  ka.spec = p->spec.as<C>();
-  ka.fspec = nfield ? p->fspec.as<C>() : nullptr;
+  ka.spec = p->spec.as<CF>();
+  ka.fspec = nfield ? p->fspec.p : nullptr;
   ka.geom = geom;
   ka.tx = p->tab.fx.as<double>(); ka.ty = p->tab.fy.as<double>(); ka.tz = p->tab.fz.as<double>();
   ka.sx = p->tab.sx.as<double>(); ka.sy = p->tab.sy.as<double>(); ka.sz = p->tab.sz.as<double>();
-  ka.amp = (const T *)a->amp;
-  ka.bw2 = (const T *)a->bw2;
+  ka.amp = a->amp;
+  ka.bw2 = a->bw2;
+  ka.p32 = p->d.dtype == SOG_DTYPE_F32;
   ka.M = M;
   ka.spline = p->d.spline;
   ka.order = P;
@@ -2268,13 +2326,17 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   gar.range_lo = gar.range_hi = nullptr;
 
   set_fft_smem_attrs<T>();
-  // power-of-two nz: fused z pass; otherwise separate z passes around
-  // k_kspace_tab.  Both read the Green tables k_green writes once per call.
+  if (!std::is_same<T, TF>::value) set_fft_smem_attrs<TF>();
+  // power-of-two nz: fused z pass, which evaluates the Green function of
+  // separable frames itself and reads k_green's tables for the others;
+  // otherwise separate z passes around k_kspace_tab, which reads the tables
+  // of every frame.
   const bool zfuse = is_pow2(nz);
   const bool zgeneric = zfuse && nz > 1024;  // runtime-plan fused pass, Green on the fly
+  ka.green_otf = zfuse && !zgeneric;
   // fused z pass: 512 threads (8-column tiles) for 512 and 1024 points
-  const int zic = zfuse ? (nz >= 512 && nz <= 1024 ? reg_width<T>(nz, 512, 64 * 1024)
-                                                   : reg_width<T>(nz, 256, 32 * 1024))
+  const int zic = zfuse ? (nz >= 512 && nz <= 1024 ? reg_width<TF>(nz, 512, 64 * 1024)
+                                                   : reg_width<TF>(nz, 256, 32 * 1024))
                         : 0;
   const int64_t zchunks = zfuse ? ((int64_t)ny * nxh + zic - 1) / zic : 0;
   const unsigned tblocks = nblocks((int64_t)ny * nxh, 256);
@@ -2294,8 +2356,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
     ka.gtab = p->gtab.as<double>();
     ka.gtabF = aliasable ? p->gtabF.as<double>() : nullptr;
     ka.partD = p->partD.as<double>();
-    launch_green<T>(ka, gblocks, nf, gz, st);
-    count_launch();
+    launch_green<TF>(ka, gblocks, nf, gz, st);
     after(tr, st, "green");
     redD = ka.partD + gparts * nf;
     reduce_parts(ka.partD, nf, 1, gparts, 1, 1, redD, redD + nf, st);
@@ -2303,54 +2364,55 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   }
   auto launch_zfused = [&]() {
     const int write_spec = (want_grad || want_vir) ? 1 : 0;
+    const CF *twz = tw_of<TF>(p, 2);
     const bool done = with_pow2(nz, [&](auto lc) {
       constexpr int L = decltype(lc)::value;
       constexpr int n = 1 << L;
       const int zthr = (n / kEPT) * zic;
-      const size_t zsm = ((2 * (size_t)n + padded_row(n)) * zic + n) * sizeof(C);
+      const size_t zsm = ((2 * (size_t)n + padded_row(n)) * zic + n) * sizeof(CF);
       const int64_t ztiles = zchunks * nf;
       if (zthr == 512) {
-        allow_smem(k_zfused_g<T, L, 512>);
-        k_zfused_g<T, L, 512><<<persistent_grid(k_zfused_g<T, L, 512>, zthr, zsm, ztiles), zthr, zsm, st>>>(
-            ka, zic, ztiles, p->twz.as<C>(), write_spec);
+        allow_smem(k_zfused_g<TF, L, 512, T>);
+        k_zfused_g<TF, L, 512, T><<<persistent_grid(k_zfused_g<TF, L, 512, T>, zthr, zsm, ztiles), zthr, zsm,
+                                    st>>>(ka, zic, ztiles, twz, write_spec);
       } else {
-        allow_smem(k_zfused_g<T, L>);
-        k_zfused_g<T, L><<<persistent_grid(k_zfused_g<T, L>, zthr, zsm, ztiles), zthr, zsm, st>>>(
-            ka, zic, ztiles, p->twz.as<C>(), write_spec);
+        allow_smem(k_zfused_g<TF, L, 256, T>);
+        k_zfused_g<TF, L, 256, T><<<persistent_grid(k_zfused_g<TF, L, 256, T>, zthr, zsm, ztiles), zthr, zsm,
+                                    st>>>(ka, zic, ztiles, twz, write_spec);
       }
     });
     if (!done) {
-      const size_t zsm = (size_t)padded_row(nz) * zic * sizeof(C) +
-                         (size_t)(nz / kEPT) * zic * kEPT * (sizeof(C) + 2 * sizeof(double));
-      k_zfused<T><<<(unsigned)(zchunks * nf), (nz / kEPT) * zic, zsm, st>>>(ka, zic, p->rpz, p->twz.as<C>(),
-                                                                            write_spec);
+      const size_t zsm = (size_t)padded_row(nz) * zic * sizeof(CF) +
+                         (size_t)(nz / kEPT) * zic * kEPT * (sizeof(CF) + 2 * sizeof(double));
+      allow_smem(k_zfused<TF, T>, 200 * 1024);
+      k_zfused<TF, T><<<(unsigned)(zchunks * nf), (nz / kEPT) * zic, zsm, st>>>(ka, zic, p->rpz, twz, write_spec);
     }
   };
   for (int c = 0; c < nch; ++c) {
     sa.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
-    dispatch_spread<T>(sa, P, nf, st, tr);
-    pass_x_fwd<T>(p, p->rho.as<T>(), p->spec.as<C>(), (int64_t)nf * nz * ny, st);
-    pass_cols<T, -1>(p, p->spec.as<C>(), ny, nxh, (int64_t)nf * nz, p->rpy, p->twy.as<C>(), st, "fft_y_fwd");
+    dispatch_spread<T, TF>(sa, P, nf, st, tr);
+    pass_x_fwd<TF>(p, p->rho.as<TF>(), p->spec.as<CF>(), (int64_t)nf * nz * ny, st);
+    pass_cols<TF, -1>(p, p->spec.as<CF>(), ny, nxh, (int64_t)nf * nz, p->rpy, tw_of<TF>(p, 1), st, "fft_y_fwd");
     ka.part = p->partE.as<double>() + (int64_t)c * nf * nblk_e * 2;
     if (zfuse) {
       launch_zfused();
       after(tr, st, "zfused");
     } else {
-      pass_cols<T, -1>(p, p->spec.as<C>(), nz, (int64_t)ny * nxh, nf, p->rpz, p->twz.as<C>(), st, "fft_z_fwd");
-      k_kspace_tab<T><<<dim3(tblocks, nf, tz), 256, 0, st>>>(ka);
+      pass_cols<TF, -1>(p, p->spec.as<CF>(), nz, (int64_t)ny * nxh, nf, p->rpz, tw_of<TF>(p, 2), st, "fft_z_fwd");
+      k_kspace_tab<TF, T><<<dim3(tblocks, nf, tz), 256, 0, st>>>(ka);
       after(tr, st, "kspace");
     }
     if (want_grad || want_vir) {
       ka.partx = p->partX.as<double>() + (int64_t)c * nf * ks_blocks * nx_acc;
-      k_kspace_extra<T><<<dim3(ks_blocks, nf), 256, 0, st>>>(ka, want_grad, want_vir);
+      k_kspace_extra<TF><<<dim3(ks_blocks, nf), 256, 0, st>>>(ka, want_grad, want_vir);
       after(tr, st, "kspace_extra");
     }
     if (nfield) {
       const int64_t nb = (int64_t)nf * nfield;
       if (!zfuse)
-        pass_cols<T, +1>(p, p->fspec.as<C>(), nz, (int64_t)ny * nxh, nb, p->rpz, p->twz.as<C>(), st,
+        pass_cols<T, +1>(p, p->fspec.as<C>(), nz, (int64_t)ny * nxh, nb, p->rpz, tw_of<T>(p, 2), st,
                          "fft_z_inv");
-      pass_cols<T, +1>(p, p->fspec.as<C>(), ny, nxh, nb * nz, p->rpy, p->twy.as<C>(), st, "fft_y_inv");
+      pass_cols<T, +1>(p, p->fspec.as<C>(), ny, nxh, nb * nz, p->rpy, tw_of<T>(p, 1), st, "fft_y_inv");
       pass_x_inv<T>(p, p->fspec.as<C>(), p->freal.as<T>(), nf, (int64_t)nz * ny, nfield, st);
       gar.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
       gar.channel = c;
@@ -2630,8 +2692,10 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
   ka.geom = geom;
   ka.tx = p->tab.fx.as<double>(); ka.ty = p->tab.fy.as<double>(); ka.tz = p->tab.fz.as<double>();
   ka.sx = p->tab.sx.as<double>(); ka.sy = p->tab.sy.as<double>(); ka.sz = p->tab.sz.as<double>();
-  ka.amp = (const T *)a->amp;
-  ka.bw2 = (const T *)a->bw2;
+  ka.amp = a->amp;
+  ka.bw2 = a->bw2;
+  ka.p32 = p->d.dtype == SOG_DTYPE_F32;
+  ka.green_otf = 1;   // the slab path always takes the fused z pass
   ka.M = M;
   ka.spline = p->d.spline;
   ka.order = P;
@@ -2666,7 +2730,6 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
     ka.gtabF = aliasable ? p->gtabF.as<double>() : nullptr;
     ka.partD = p->partD.as<double>();
     launch_green<T>(ka, gblocks, 1, gz, st);
-    count_launch();
     after(tr, st, "green");
     reduce_parts(ka.partD, 1, 1, gparts, 1, 1, red + 2 * nch, ka.partD + gparts + 1, st);
     after(tr, st, "reduce_green", reduce_split(gparts) > 1 ? 2 : 1);
@@ -2879,6 +2942,14 @@ extern "C" int sog_plan_create(sog_plan **out, const sog_plan_desc *desc) {
   if ((rc = upload(p->twy, tw.data(), tw.size())) != SOG_OK) goto bad;
   make_twiddles(d.nz, d.dtype, tw);
   if ((rc = upload(p->twz, tw.data(), tw.size())) != SOG_OK) goto bad;
+  if (d.dtype == SOG_DTYPE_F32) {
+    make_twiddles(d.nx, SOG_DTYPE_F64, tw);
+    if ((rc = upload(p->twx64, tw.data(), tw.size())) != SOG_OK) goto bad;
+    make_twiddles(d.ny, SOG_DTYPE_F64, tw);
+    if ((rc = upload(p->twy64, tw.data(), tw.size())) != SOG_OK) goto bad;
+    make_twiddles(d.nz, SOG_DTYPE_F64, tw);
+    if ((rc = upload(p->twz64, tw.data(), tw.size())) != SOG_OK) goto bad;
+  }
   {
     // per-axis Green factors and alias sums over mode indices of each axis
     auto axis = [&](int n, int len, bool half, DevBuf &fb, DevBuf &sb) -> int {
@@ -2908,7 +2979,7 @@ bad:
 extern "C" int sog_plan_destroy(sog_plan *p) {
   if (!p) return SOG_OK;
   DeviceGuard dg(p->d.device);
-  DevBuf *bufs[] = {&p->twx, &p->twy, &p->twz, &p->tab.fx, &p->tab.fy, &p->tab.fz, &p->tab.sx,
+  DevBuf *bufs[] = {&p->twx, &p->twy, &p->twz, &p->twx64, &p->twy64, &p->twz64, &p->tab.fx, &p->tab.fy, &p->tab.fz, &p->tab.sx,
                     &p->tab.sy, &p->tab.sz, &p->frames_host_dev, &p->geom, &p->status, &p->keys0,
                     &p->vals0, &p->keys1, &p->vals1, &p->hist, &p->scan_tmp, &p->bin_start,
                     &p->s_atom, &p->s_anchor, &p->s_t, &p->s_q, &p->qsum, &p->rho, &p->spec,

@@ -71,6 +71,9 @@ struct sog_plan {
   sogb::RadixPlan rpx{}, rpy{}, rpz{};
   sogb::RadixPlan rpxh{};           // nx/2 (even nx: real x rows as half-length transforms)
   sogb::DevBuf twx, twy, twz;   // n-th roots (complex, plan dtype)
+  // fp32 plans: the same roots in fp64, for the forward transforms (which
+  // run in fp64 for every plan; see mesh_forward_impl)
+  sogb::DevBuf twx64, twy64, twz64;
   sogb::AxisTables tab;
   // scratch
   sogb::DevBuf frames_host_dev, geom, status;
