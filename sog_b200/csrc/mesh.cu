@@ -279,17 +279,25 @@ struct StencilTerms<4> {
 
 // Per-axis kinds of one coordinate: the spline weights (NT = 1) or the
 // CubeS2 kinds.
+// The weights are evaluated in fp64 and rounded once to T.  Evaluated in fp32,
+// the recurrences' own roundings (of 1/3 and 1/5, say) bias every weight the
+// same way, which scales each atom's charge cloud by about 1 + 1e-7 and so its
+// mesh self-energy, while the subtracted self term stays exact: 2.9e-5 of the
+// total energy of the 131,072-atom 256^3 system.  One rounding is unbiased.
 template <typename T, int P, int NT>
 __device__ __forceinline__ void axis_kinds(int spline, T t, T (*kinds)[P], const QuadsCoef &qc) {
   if constexpr (NT == 1) {
-    spline_w<T, P>(spline, t, kinds[0], qc);
+    double w[P];
+    spline_w<double, P>(spline, (double)t, w, qc);
+#pragma unroll
+    for (int j = 0; j < P; ++j) kinds[0][j] = (T)w[j];
   } else {
-    T tmp[3][P];
-    cubes2_axis<T, P>(t, tmp);
+    double tmp[3][P];
+    cubes2_axis<double, P>((double)t, tmp);
 #pragma unroll
     for (int k = 0; k < StencilTerms<NT>::K; ++k)
 #pragma unroll
-      for (int j = 0; j < P; ++j) kinds[k][j] = tmp[k][j];
+      for (int j = 0; j < P; ++j) kinds[k][j] = (T)tmp[k][j];
   }
 }
 
@@ -642,10 +650,14 @@ struct KsArgs {
   // one tile of cw columns is contiguous for every z; with cw > 0 the fields
   // of z block b go to zdst[b] as [nfield][xc*nyl + y][zblk][cw]
   int cw;
-  // 1: the fused z pass computes the Green function of separable frames
-  // (green_separable) on the fly and sums their self term itself; k_green
-  // then only builds the tables of the other frames
-  int green_otf;
+  // Radial kernel tables [nf][krad_stride] of cubic frames (green_radial),
+  // or null: K(k) = sum_m amp_m exp(-bw2_m k^2 / 2) with k^2 = kappa^2 s, s =
+  // mx^2 + my^2 + mz^2, so one fp64 value per integer s serves every mode.
+  // The fused z pass then evaluates those frames' Green function from it
+  // (times the per-axis deconvolution) and sums their self term itself;
+  // k_green builds the tables of the other frames only.
+  const double *krad;
+  int64_t krad_stride;
 };
 
 // kernel parameter m as a double
@@ -665,6 +677,32 @@ __device__ __forceinline__ cplx_t<TO> to_field(const C &v) {
 template <typename T>
 __device__ __forceinline__ bool green_separable(const KsArgs<T> &a, const FrameGeom &g) {
   return g.ortho && a.btab && !g.pad && a.M <= 16 && a.spline != SOG_SPLINE_CUBES2;
+}
+
+// Cubic frames (one wave-vector scale on all three axes, no alias inside the
+// cutoff, not CubeS2) whose kernel comes from the radial table.
+template <typename T>
+__device__ __forceinline__ bool green_radial(const KsArgs<T> &a, const FrameGeom &g) {
+  return a.krad && g.ortho && !g.pad && a.spline != SOG_SPLINE_CUBES2 && g.kmat[0] == g.kmat[4] &&
+         g.kmat[4] == g.kmat[8];
+}
+
+// Radial kernel table of every cubic frame: entry s = sum_m amp_m exp(-bw2_m
+// kappa^2 s / 2), s = 0 .. krad_stride - 1.
+template <typename T>
+__global__ void k_radial_table(KsArgs<T> a) {
+  const int f = blockIdx.y;
+  const FrameGeom &g = a.geom[f];
+  if (!green_radial(a, g)) return;
+  const double k2 = g.kmat[0] * g.kmat[0];
+  double *out = const_cast<double *>(a.krad) + (int64_t)f * a.krad_stride;
+  for (int64_t sidx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; sidx < a.krad_stride;
+       sidx += (int64_t)gridDim.x * blockDim.x) {
+    const double ksq = k2 * (double)sidx;
+    double K = 0.0;
+    for (int m = 0; m < a.M; ++m) K += kpar(a.amp, a.p32, m) * exp(-0.5 * kpar(a.bw2, a.p32, m) * ksq);
+    out[sidx] = K;
+  }
 }
 
 // Column `col` of the spectrum rows -> (mx, local y); false for the pad
@@ -1064,14 +1102,15 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
   __syncthreads();
   const int f = blockIdx.y;
   const FrameGeom &g = a.geom[f];
-  const bool sep = green_separable(a, g);
-  if (sep != SEP) {
-    // block-uniform: the frame belongs to the other launch, or (green_otf)
-    // to the fused z pass, which then sums its self term: a zero partial here
-    if (!SEP && a.green_otf && threadIdx.x == 0)
-      a.partD[((int64_t)f * gridDim.z + blockIdx.z) * gridDim.x + blockIdx.x] = 0.0;
+  // block-uniform: radial frames belong to the fused z pass (which sums
+  // their self term: a zero partial here, written by one of the two
+  // launches), separable ones to the SEP launch, the rest to the other
+  if (green_radial(a, g)) {
+    if (!SEP && threadIdx.x == 0) a.partD[((int64_t)f * gridDim.z + blockIdx.z) * gridDim.x + blockIdx.x] = 0.0;
     return;
   }
+  const bool sep = green_separable(a, g);
+  if (sep != SEP) return;
   const int64_t inner = cols_inner(a);
   const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // (iy, mx) column
   // z planes of this block: the columns are split over gridDim.z
@@ -1170,15 +1209,12 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
   using CO = cplx_t<TO>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ double red[2][NTH / 32];
-  __shared__ double s_amp[16];
   constexpr int n = 1 << L, TPT = n / kEPT;
   C *buf0 = reinterpret_cast<C *>(smem_raw);
   C *buf1 = buf0 + (size_t)n * ic;
   C *xbuf = buf1 + (size_t)n * ic;
   C *stg = xbuf + (size_t)padded_row(n) * ic;
   load_stage_twiddles<T, L, 0>(stg, twz);
-  if (threadIdx.x < 16) s_amp[threadIdx.x] = threadIdx.x < a.M ? kpar(a.amp, a.p32, threadIdx.x) : 0.0;
-  __syncthreads();
   const int c = threadIdx.x % ic, t = threadIdx.x / ic;
   const int64_t inner = cols_inner(a);
   const int64_t nchunks = (inner + ic - 1) / ic;
@@ -1212,15 +1248,11 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
     // table), else loads from the table, in flight during the FFT
     double gs[kEPT];
     double accD = 0.0;
-    if (a.green_otf && green_separable(a, g)) {   // frame-uniform
-      const int M = a.M;
-      const double *bt = a.btab + (int64_t)f * a.btab_stride;
-      const double *bx = bt, *by = bt + M * a.nxh, *bz = by + M * a.ny;
-      double axy[16];
-#pragma unroll
-      for (int m = 0; m < 16; ++m) axy[m] = (ok && m < M) ? s_amp[m] * bx[m * a.nxh + mx] * by[m * a.ny + iy] : 0.0;
+    if (green_radial(a, g)) {   // frame-uniform
+      const double *kr = a.krad + (int64_t)f * a.krad_stride;
       const double kx = g.kmat[0] * mx, ky = g.kmat[4] * my;
       const double kxy2 = kx * kx + ky * ky;
+      const int sxy = mx * mx + my * my;
       const double txy = ok ? a.tx[mx] * a.ty[iy] : 0.0;
       const bool quads = a.spline == SOG_SPLINE_QUADS;
 #pragma unroll
@@ -1228,14 +1260,8 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
         const int iz = t + e * TPT;
         const int mz = signed_mode(iz, a.nz);
         const double kz = g.kmat[8] * mz;
-        const double ksq = kxy2 + kz * kz;
-        const bool live = ok && !((mx | my | mz) == 0) && ksq <= g.k_sq_max;
-        double K = 0.0;
-        if (live) {
-#pragma unroll
-          for (int m = 0; m < 16; ++m)
-            if (m < M) K += axy[m] * bz[m * a.nz + iz];
-        }
+        const bool live = ok && !((mx | my | mz) == 0) && kxy2 + kz * kz <= g.k_sq_max;
+        const double K = live ? kr[sxy + mz * mz] : 0.0;
         double D = txy * a.tz[iz];
         if (quads) D = 1.0 / (D < 1e-20 ? 1e-20 : D);
         gs[e] = live ? K * D : 0.0;
@@ -2197,18 +2223,29 @@ int prepare_atoms(sog_plan *p, const sog_mesh_args *a, cudaStream_t st, Prep &pr
   return SOG_OK;
 }
 
-// With ka.green_otf the fused z pass evaluates the separable frames' Green
-// function itself: only the other frames' tables are built here.
+// Both Green kernels on one grid (each takes its frames); with ka.krad the
+// radial frames are left to the fused z pass.
 template <typename T>
 void launch_green(const KsArgs<T> &ka, unsigned gblocks, int nf, unsigned gz, cudaStream_t st) {
-  if (!ka.green_otf) {
-    const int zper = (ka.nz + (int)gz - 1) / (int)gz;
-    const size_t sm = ka.M <= 16 ? (size_t)zper * ((ka.M + 1) & ~1) * sizeof(double) : 0;
-    allow_smem(k_green<T, true>);
-    k_green<T, true><<<dim3(gblocks, nf, gz), 256, sm, st>>>(ka);
-    count_launch();
-  }
+  const int zper = (ka.nz + (int)gz - 1) / (int)gz;
+  const size_t sm = ka.M <= 16 ? (size_t)zper * ((ka.M + 1) & ~1) * sizeof(double) : 0;
+  allow_smem(k_green<T, true>);
+  k_green<T, true><<<dim3(gblocks, nf, gz), 256, sm, st>>>(ka);
+  count_launch();
   k_green<T, false><<<dim3(gblocks, nf, gz), 256, 0, st>>>(ka);
+}
+
+// Radial tables of the call's cubic frames (sized for the mesh's largest
+// mx^2 + my^2 + mz^2), before the Green tables.
+template <typename T>
+int setup_radial(sog_plan *p, KsArgs<T> &ka, int nf, cudaStream_t st) {
+  const int64_t hx = p->d.nx / 2, hy = p->d.ny / 2, hz = p->d.nz / 2;
+  ka.krad_stride = hx * hx + hy * hy + hz * hz + 1;
+  if (p->krad.reserve(sizeof(double) * ka.krad_stride * nf)) return fail(SOG_ERR_NOMEM, "device allocation failed");
+  ka.krad = p->krad.as<double>();
+  k_radial_table<T><<<dim3((unsigned)std::min<int64_t>((ka.krad_stride + 255) / 256, 1024), nf), 256, 0, st>>>(ka);
+  after(&p->tr, st, "radial_table");
+  return SOG_OK;
 }
 
 // Precision: the charge grid, the forward transforms, the Green multiply and
@@ -2333,7 +2370,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   // of every frame.
   const bool zfuse = is_pow2(nz);
   const bool zgeneric = zfuse && nz > 1024;  // runtime-plan fused pass, Green on the fly
-  ka.green_otf = zfuse && !zgeneric;
+  if (zfuse && !zgeneric && (rc = setup_radial<TF>(p, ka, nf, st)) != SOG_OK) return rc;
   // fused z pass: 512 threads (8-column tiles) for 512 and 1024 points
   const int zic = zfuse ? (nz >= 512 && nz <= 1024 ? reg_width<TF>(nz, 512, 64 * 1024)
                                                    : reg_width<TF>(nz, 256, 32 * 1024))
@@ -2695,7 +2732,6 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
   ka.amp = a->amp;
   ka.bw2 = a->bw2;
   ka.p32 = p->d.dtype == SOG_DTYPE_F32;
-  ka.green_otf = 1;   // the slab path always takes the fused z pass
   ka.M = M;
   ka.spline = p->d.spline;
   ka.order = P;
@@ -2729,6 +2765,7 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
     ka.gtab = p->gtab.as<double>();
     ka.gtabF = aliasable ? p->gtabF.as<double>() : nullptr;
     ka.partD = p->partD.as<double>();
+    if ((rc = setup_radial<T>(p, ka, 1, st)) != SOG_OK) return rc;
     launch_green<T>(ka, gblocks, 1, gz, st);
     after(tr, st, "green");
     reduce_parts(ka.partD, 1, 1, gparts, 1, 1, red + 2 * nch, ka.partD + gparts + 1, st);
@@ -2983,7 +3020,7 @@ extern "C" int sog_plan_destroy(sog_plan *p) {
                     &p->tab.sy, &p->tab.sz, &p->frames_host_dev, &p->geom, &p->status, &p->keys0,
                     &p->vals0, &p->keys1, &p->vals1, &p->hist, &p->scan_tmp, &p->bin_start,
                     &p->s_atom, &p->s_anchor, &p->s_t, &p->s_q, &p->qsum, &p->rho, &p->spec,
-                    &p->fspec, &p->freal, &p->partE, &p->partX, &p->red, &p->redtmp, &p->qpart, &p->btab, &p->gtab, &p->gtabF, &p->partD};
+                    &p->fspec, &p->freal, &p->partE, &p->partX, &p->red, &p->redtmp, &p->qpart, &p->btab, &p->gtab, &p->gtabF, &p->partD, &p->krad};
   for (DevBuf *b : bufs) b->release();
   close_peers(p);
   p->xr_fwd.release();

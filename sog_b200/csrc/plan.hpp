@@ -86,6 +86,7 @@ struct sog_plan {
   sogb::DevBuf redtmp, qpart;   // two-level reduction scratch, charge-sum partials
   sogb::DevBuf btab;            // per-axis kernel factors (orthorhombic frames)
   sogb::DevBuf gtab, gtabF, partD;  // Green tables and self-sum partials of the fused path
+  sogb::DevBuf krad;                // radial kernel tables of cubic frames
   sogb::PinnedBuf up;
   sogb::Tracer tr;
   int nb_x = 0, nb_y = 0, nb_z = 0;  // sort bins per axis
