@@ -231,6 +231,31 @@ typedef struct sog_direct_args {
  * (gaussian.py:1180-1337), whose forces the reference takes by autograd. */
 SOG_API int sog_direct_forward(sog_direct *d, const sog_direct_args *args, void *stream);
 
+/* Hessian-vector products: the double backward of autograd (a force loss in
+ * training differentiates dE/dr again).  For every frame f, with E_f the
+ * frame's energy as the forward computes it (all of its terms: the k-space
+ * or pair sum, the self term, the k=0 term and the neutrality penalty), and
+ * d = (dir_q, dir_r, dir_amp[f], dir_bw2[f]) a direction over the charges,
+ * positions and the kernel parameters:
+ *   out_q, out_r       = the (charges, positions) rows of H(E_f) d, frame by frame
+ *   out_amp[f], out_bw2[f] = the parameter rows of H(E_f) d
+ * A NULL direction counts as zero; every output must be given. */
+typedef struct sog_hvp_args {
+  const void *dir_q;              /* device [N,C], or NULL                       */
+  const void *dir_r;              /* device [N,3], or NULL                       */
+  const void *dir_amp, *dir_bw2;  /* device [nframes,M], or NULL                 */
+  void *out_q;                    /* device [N,C]                                */
+  void *out_r;                    /* device [N,3]                                */
+  void *out_amp, *out_bw2;        /* device [nframes,M]                          */
+} sog_hvp_args;
+
+/* Hessian-vector product of the direct k-sum energy (the second derivatives
+ * the reference takes with torch.autograd through _compute_periodic_direct /
+ * _compute_bundle_direct_batched, gaussian.py:1180-1337, when forces are
+ * built with create_graph=True).  Same inputs as sog_direct_forward (its
+ * energy / derivative outputs are ignored). */
+SOG_API int sog_direct_hvp(sog_direct *d, const sog_direct_args *args, const sog_hvp_args *h, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Real-space pair sum (non-periodic frames)                                 */
 /* ------------------------------------------------------------------------ */

@@ -65,6 +65,11 @@ class RealspaceArgs(ctypes.Structure):
                 ("potential", _vp), ("grad_amp", _vp), ("grad_bw2", _vp), ("virial", _vp)]
 
 
+class HvpArgs(ctypes.Structure):
+    _fields_ = [("dir_q", _vp), ("dir_r", _vp), ("dir_amp", _vp), ("dir_bw2", _vp),
+                ("out_q", _vp), ("out_r", _vp), ("out_amp", _vp), ("out_bw2", _vp)]
+
+
 # int exchange(void *ctx, int kind, int64 send_off, int64 recv_off, int64 bytes, void *stream)
 EXCHANGE_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
                                ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p)
@@ -82,7 +87,8 @@ EXPORTS = ["sog_strerror", "sog_last_error", "sog_version", "sog_launch_count", 
            "sog_plan_destroy", "sog_plan_status", "sog_plan_set_timing", "sog_plan_timings",
            "sog_mesh_forward", "sog_direct_create", "sog_direct_destroy", "sog_direct_set_timing",
            "sog_direct_timings", "sog_direct_forward", "sog_direct_forward_noalloc",
-           "sog_mesh_slab_workspace", "sog_mesh_slab_forward", "sog_realspace_forward"]
+           "sog_mesh_slab_workspace", "sog_mesh_slab_forward", "sog_realspace_forward",
+           "sog_direct_hvp"]
 
 _lib = None
 _lock = threading.Lock()
@@ -118,6 +124,7 @@ def load():
         lib.sog_direct_destroy.argtypes = [_vp]
         lib.sog_direct_forward.argtypes = [_vp, ctypes.POINTER(DirectArgs), _vp]
         lib.sog_realspace_forward.argtypes = [_vp, ctypes.POINTER(RealspaceArgs), _vp]
+        lib.sog_direct_hvp.argtypes = [_vp, ctypes.POINTER(DirectArgs), ctypes.POINTER(HvpArgs), _vp]
         lib.sog_launch_count.restype = ctypes.c_ulonglong
         for name in ("sog_plan_set_timing", "sog_direct_set_timing"):
             getattr(lib, name).argtypes = [_vp, ctypes.c_int]
@@ -404,3 +411,39 @@ def realspace_forward(ctx, *, atom_begin, atom_count, positions, charges, amp, b
         stream = torch.cuda.current_stream(positions.device).cuda_stream
     check(load().sog_realspace_forward(ctx, ctypes.byref(args), ctypes.c_void_p(stream)),
           "sog_realspace_forward")
+
+
+def _hvp_args(dir_q, dir_r, dir_amp, dir_bw2, out_q, out_r, out_amp, out_bw2):
+    h = HvpArgs()
+    h.dir_q, h.dir_r, h.dir_amp, h.dir_bw2 = _ptr(dir_q), _ptr(dir_r), _ptr(dir_amp), _ptr(dir_bw2)
+    h.out_q, h.out_r, h.out_amp, h.out_bw2 = _ptr(out_q), _ptr(out_r), _ptr(out_amp), _ptr(out_bw2)
+    return h
+
+
+def direct_hvp(ctx, *, atom_begin, atom_count, nk, k_sq_max, positions, charges, cells, amp, bw2,
+               norm_factor, self_coeff, remove_self, k0_correction, charge_neutral_lambda, dir_q, dir_r,
+               dir_amp, dir_bw2, out_q, out_r, out_amp, out_bw2, stream=None, **_unused):
+    """sog_direct_hvp: the Hessian of every frame's energy applied to the
+    direction (dir_q, dir_r, dir_amp[f], dir_bw2[f]); outputs written in place."""
+    _require_cuda(positions)
+    nf = len(atom_begin)
+    ab, ac, km = _host_i64(atom_begin), _host_i64(atom_count), _host_f64(k_sq_max)
+    nkflat = _host_nk(nk)
+    args = DirectArgs()
+    args.nframes = nf
+    args.atom_begin = ctypes.cast(ab, _c_i64p)
+    args.atom_count = ctypes.cast(ac, _c_i64p)
+    args.nk = ctypes.cast(nkflat, _c_i32p)
+    args.k_sq_max = ctypes.cast(km, _c_dp)
+    args.nchannels = charges.shape[1]
+    args.positions, args.charges, args.cells = _ptr(positions), _ptr(charges), _ptr(cells)
+    args.n_gauss = amp.numel()
+    args.amp, args.bw2 = _ptr(amp), _ptr(bw2)
+    args.norm_factor, args.self_coeff = float(norm_factor), float(self_coeff)
+    args.remove_self, args.k0_correction = int(remove_self), int(k0_correction)
+    args.charge_neutral_lambda = float(charge_neutral_lambda or 0.0)
+    h = _hvp_args(dir_q, dir_r, dir_amp, dir_bw2, out_q, out_r, out_amp, out_bw2)
+    if stream is None:
+        stream = torch.cuda.current_stream(positions.device).cuda_stream
+    check(load().sog_direct_hvp(ctx, ctypes.byref(args), ctypes.byref(h), ctypes.c_void_p(stream)),
+          "sog_direct_hvp")

@@ -423,7 +423,7 @@ extern "C" int sog_direct_destroy(sog_direct *d) {
   if (!d) return SOG_OK;
   DeviceGuard dg(d->device);
   DevBuf *bufs[] = {&d->frames_host_dev, &d->geom, &d->modes, &d->sfac, &d->part, &d->qsum, &d->status,
-                    &d->qpart, &d->redtmp};
+                    &d->qpart, &d->redtmp, &d->hx, &d->hpart, &d->hred, &d->hdsum, &d->hscal};
   for (DevBuf *b : bufs) b->release();
   d->up.release();
   d->tr.release();
@@ -444,6 +444,504 @@ extern "C" int sog_direct_forward(sog_direct *d, const sog_direct_args *a, void 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (d->dtype == SOG_DTYPE_F64) return direct_impl<double>(d, a, st);
   return direct_impl<float>(d, a, st);
+}
+
+// ==========================================================================
+// Hessian-vector products of the direct k-sum (double backward).
+//
+// With E = beta sum_half K |S|^2 (beta = 1/V), S = sum_j q_j e_j, e_j =
+// exp(i k.r_j), and a direction (a_j on the charges, b_j on the positions,
+// c on the kernel parameters):
+//   S_d = sum_j (a_j + i q_j k.b_j) e_j,   dK = sum_m c . dK/d(amp_m, bw2_m),
+//   X   = K S_d + dK S,
+//   (H d)_{q_j}  = 2 beta sum [Re(conj X e_j) - K (k.b_j) Im(conj S e_j)]
+//   (H d)_{r_j}  = -2 beta sum k [q_j Im(conj X e_j) + a_j K Im(conj S e_j)
+//                                 + q_j K (k.b_j) Re(conj S e_j)]
+//   (H d)_{theta_m} = beta sum [2 dK/dtheta_m Re(conj S S_d) + d(dK)/dtheta_m |S|^2]
+// per channel (positions shared).  The self, k=0 and penalty terms depend on
+// the charges and parameters only; their exact second derivatives are added
+// per frame and per atom from the mode sums D0..D2 of exp(-bw2_m k^2 / 2).
+// ==========================================================================
+namespace sogb {
+namespace {
+
+struct HvpArgs {
+  const void *dq, *dr, *damp, *dbw2;  // directions (null: zero)
+  void *oq, *orr, *oamp, *obw2;       // outputs
+  double *hx;                          // [nf][C][K][2] X sums
+  double *hpart;                       // [nf][nblk][5M] partials: 2M theta rows, D0, D1, D2
+  int nh;                              // 5M
+};
+
+template <typename T>
+__device__ __forceinline__ double ldir(const void *p, int64_t i) {
+  return p ? (double)static_cast<const T *>(p)[i] : 0.0;
+}
+
+// thread per mode: S_d, X = K S_d + dK S, theta partials and the D sums
+template <typename T>
+__global__ void __launch_bounds__(kDirThreads) k_direct_hvp_modes(DirArgs a, HvpArgs h, const T *__restrict__ pos,
+                                                                 const T *__restrict__ q, const T *__restrict__ amp,
+                                                                 const T *__restrict__ bw2) {
+  __shared__ double s_r[kDirThreads][3];
+  __shared__ double s_b[kDirThreads][3];
+  __shared__ double s_q[kDirThreads][kMaxCh];
+  __shared__ double s_a[kDirThreads][kMaxCh];
+  __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss], s_ca[kMaxGauss], s_cb[kMaxGauss];
+  __shared__ double red[kDirThreads / 32];
+  const int f = blockIdx.y;
+  const FrameGeom &g = a.geom[f];
+  for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
+    s_amp[m] = (double)amp[m];
+    s_bw2[m] = (double)bw2[m];
+    s_ca[m] = ldir<T>(h.damp, (int64_t)f * a.M + m);
+    s_cb[m] = ldir<T>(h.dbw2, (int64_t)f * a.M + m);
+  }
+  __syncthreads();
+  const int *nk = a.nk + 3 * f;
+  const int64_t nbox = (int64_t)(nk[0] + 1) * (2 * nk[1] + 1) * (2 * nk[2] + 1);
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  double k[3] = {0.0, 0.0, 0.0}, K = 0.0;
+  if (t < nbox) {
+    const double *kv = a.kvec + ((int64_t)f * a.kmax_modes + t) * 4;
+    k[0] = kv[0]; k[1] = kv[1]; k[2] = kv[2]; K = kv[3];
+  }
+  const bool live = K != 0.0;
+  const double ksq = k[0] * k[0] + k[1] * k[1] + k[2] * k[2];
+  double dr[kMaxCh], di[kMaxCh];
+#pragma unroll
+  for (int c = 0; c < kMaxCh; ++c) { dr[c] = 0.0; di[c] = 0.0; }
+  for (int base = 0; base < g.natoms; base += kDirThreads) {
+    const int i = base + threadIdx.x;
+    __syncthreads();
+    if (i < g.natoms) {
+      const int64_t atom = g.atom_begin + i;
+      for (int c = 0; c < 3; ++c) {
+        s_r[threadIdx.x][c] = (double)pos[atom * 3 + c];
+        s_b[threadIdx.x][c] = ldir<T>(h.dr, atom * 3 + c);
+      }
+      for (int c = 0; c < a.nch; ++c) {
+        s_q[threadIdx.x][c] = (double)q[atom * a.nch + c];
+        s_a[threadIdx.x][c] = ldir<T>(h.dq, atom * a.nch + c);
+      }
+    }
+    __syncthreads();
+    const int cnt = min(kDirThreads, g.natoms - base);
+    if (live) {
+      for (int j = 0; j < cnt; ++j) {
+        const double kr = k[0] * s_r[j][0] + k[1] * s_r[j][1] + k[2] * s_r[j][2];
+        const double kb = k[0] * s_b[j][0] + k[1] * s_b[j][1] + k[2] * s_b[j][2];
+        double sn, cs;
+        sincos(kr, &sn, &cs);
+#pragma unroll
+        for (int c = 0; c < kMaxCh; ++c)
+          if (c < a.nch) {
+            const double av = s_a[j][c], qk = s_q[j][c] * kb;
+            dr[c] += av * cs - qk * sn;
+            di[c] += av * sn + qk * cs;
+          }
+      }
+    }
+  }
+  // dK of the direction and the per-Gaussian factors
+  double dK = 0.0;
+  if (live)
+    for (int m = 0; m < a.M; ++m)
+      dK += (s_ca[m] - 0.5 * ksq * s_amp[m] * s_cb[m]) * exp(-0.5 * s_bw2[m] * ksq);
+  double rsd = 0.0, s2 = 0.0;   // sum_c Re(conj S S_d), sum_c |S|^2
+  if (t < nbox) {
+    for (int c = 0; c < a.nch; ++c) {
+      const double *sp = a.sfac + (((int64_t)f * a.nch + c) * a.kmax_modes + t) * 2;
+      const double sr = sp[0], si = sp[1];
+      rsd += sr * dr[c] + si * di[c];
+      s2 += sr * sr + si * si;
+      double *xp = h.hx + (((int64_t)f * a.nch + c) * a.kmax_modes + t) * 2;
+      xp[0] = live ? K * dr[c] + dK * sr : 0.0;
+      xp[1] = live ? K * di[c] + dK * si : 0.0;
+    }
+  }
+  // partials: theta rows (amp, bw2) and the D sums, over the half space
+  // (weights 2 as k_direct_sfac's energy sums; scaled on the host side)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int M = a.M;
+  double *out = h.hpart + ((int64_t)f * gridDim.x + blockIdx.x) * h.nh;
+  for (int m = 0; m < M; ++m) {
+    const double e = live ? exp(-0.5 * s_bw2[m] * ksq) : 0.0;
+    const double hk = -0.5 * ksq;
+    const double v[5] = {
+        2.0 * (2.0 * e * rsd + s_cb[m] * hk * e * s2),
+        2.0 * (2.0 * hk * s_amp[m] * e * rsd + (s_ca[m] * hk * e + s_cb[m] * hk * hk * s_amp[m] * e) * s2),
+        2.0 * e, 2.0 * hk * e, 2.0 * hk * hk * e};
+#pragma unroll
+    for (int r = 0; r < 5; ++r) {
+      const double w = warp_sum(v[r]);
+      __syncthreads();
+      if (lane == 0) red[warp] = w;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        double sacc = 0.0;
+        for (int wi = 0; wi < kDirThreads / 32; ++wi) sacc += red[wi];
+        out[r * M + m] = sacc;
+      }
+    }
+  }
+}
+
+// thread per atom: the charge and position rows of H d (core term)
+template <typename T, int CH = 128>
+__global__ void __launch_bounds__(CH) k_direct_hvp_atoms(DirArgs a, HvpArgs h, const T *__restrict__ pos,
+                                                        const T *__restrict__ q, double norm) {
+  __shared__ double s_k[CH][4];
+  __shared__ double s_s[CH][kMaxCh][2];
+  __shared__ double s_x[CH][kMaxCh][2];
+  const int f = blockIdx.y;
+  const FrameGeom &g = a.geom[f];
+  const int *nk = a.nk + 3 * f;
+  const int64_t nbox = (int64_t)(nk[0] + 1) * (2 * nk[1] + 1) * (2 * nk[2] + 1);
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const bool own = i < g.natoms;
+  const int64_t atom = g.atom_begin + (own ? i : 0);
+  double r[3] = {0, 0, 0}, b[3] = {0, 0, 0}, qi[kMaxCh], ai[kMaxCh];
+  if (own)
+    for (int c = 0; c < 3; ++c) {
+      r[c] = (double)pos[atom * 3 + c];
+      b[c] = ldir<T>(h.dr, atom * 3 + c);
+    }
+#pragma unroll
+  for (int c = 0; c < kMaxCh; ++c) {
+    qi[c] = (own && c < a.nch) ? (double)q[atom * a.nch + c] : 0.0;
+    ai[c] = (own && c < a.nch) ? ldir<T>(h.dq, atom * a.nch + c) : 0.0;
+  }
+  double px[kMaxCh], bs[kMaxCh];
+#pragma unroll
+  for (int c = 0; c < kMaxCh; ++c) { px[c] = 0.0; bs[c] = 0.0; }
+  double fr[3] = {0, 0, 0};   // sum k (q Im X + a K Im S + q K kb Re S)
+  for (int64_t base = 0; base < nbox; base += CH) {
+    __syncthreads();
+    const int64_t t = base + threadIdx.x;
+    if (t < nbox) {
+      const double *kv = a.kvec + ((int64_t)f * a.kmax_modes + t) * 4;
+      for (int c = 0; c < 4; ++c) s_k[threadIdx.x][c] = kv[c];
+      for (int c = 0; c < a.nch; ++c) {
+        const int64_t o = (((int64_t)f * a.nch + c) * a.kmax_modes + t) * 2;
+        s_s[threadIdx.x][c][0] = a.sfac[o];
+        s_s[threadIdx.x][c][1] = a.sfac[o + 1];
+        s_x[threadIdx.x][c][0] = h.hx[o];
+        s_x[threadIdx.x][c][1] = h.hx[o + 1];
+      }
+    } else {
+      s_k[threadIdx.x][3] = 0.0;
+    }
+    __syncthreads();
+    const int cnt = (int)min((int64_t)CH, nbox - base);
+    if (own) {
+      for (int j = 0; j < cnt; ++j) {
+        const double K = s_k[j][3];
+        if (K == 0.0) continue;
+        const double kr = s_k[j][0] * r[0] + s_k[j][1] * r[1] + s_k[j][2] * r[2];
+        const double kb = s_k[j][0] * b[0] + s_k[j][1] * b[1] + s_k[j][2] * b[2];
+        double sn, cs;
+        sincos(kr, &sn, &cs);
+        double tsum = 0.0;
+#pragma unroll
+        for (int c = 0; c < kMaxCh; ++c) {
+          if (c < a.nch) {
+            const double sr = s_s[j][c][0], si = s_s[j][c][1];
+            const double xr = s_x[j][c][0], xi = s_x[j][c][1];
+            const double reS = sr * cs + si * sn, imS = sr * sn - si * cs;
+            const double reX = xr * cs + xi * sn, imX = xr * sn - xi * cs;
+            px[c] += reX;
+            bs[c] += K * kb * imS;
+            tsum += qi[c] * imX + ai[c] * K * imS + qi[c] * K * kb * reS;
+          }
+        }
+        fr[0] += tsum * s_k[j][0];
+        fr[1] += tsum * s_k[j][1];
+        fr[2] += tsum * s_k[j][2];
+      }
+    }
+  }
+  if (!own) return;
+  const double sc = 2.0 * norm / g.vol;
+  T *oq = static_cast<T *>(h.oq), *orr = static_cast<T *>(h.orr);
+  for (int c = 0; c < a.nch; ++c) oq[atom * a.nch + c] = (T)(sc * (px[c] - bs[c]));
+  for (int c = 0; c < 3; ++c) orr[atom * 3 + c] = (T)(-sc * fr[c]);
+}
+
+// direction sums per frame and channel: sum a, sum q a
+template <typename T>
+__global__ void k_hvp_dsums(const T *__restrict__ q, const void *dq, int nch, const FrameGeom *__restrict__ geom,
+                            double *__restrict__ out) {
+  const int f = blockIdx.x, c = blockIdx.y;
+  const FrameGeom &g = geom[f];
+  double s1 = 0.0, s2 = 0.0;
+  for (int64_t i = threadIdx.x; i < g.natoms; i += blockDim.x) {
+    const int64_t o = (g.atom_begin + i) * nch + c;
+    const double av = ldir<T>(dq, o);
+    s1 += av;
+    s2 += (double)q[o] * av;
+  }
+  __shared__ double r1[256], r2[256];
+  r1[threadIdx.x] = s1;
+  r2[threadIdx.x] = s2;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if (threadIdx.x < o) { r1[threadIdx.x] += r1[threadIdx.x + o]; r2[threadIdx.x] += r2[threadIdx.x + o]; }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    out[((int64_t)f * nch + c) * 2 + 0] = r1[0];
+    out[((int64_t)f * nch + c) * 2 + 1] = r2[0];
+  }
+}
+
+struct HvpFinal {
+  const FrameGeom *geom;
+  const double *hred;   // [nf][5M]: theta rows (amp, bw2), D0, D1, D2 (half-space weight 2)
+  const double *qsum;   // [nf][C][2] sum q, sum q^2
+  const double *dsum;   // [nf][C][2] sum a, sum q a
+  const void *amp, *bw2, *damp, *dbw2;
+  void *oamp, *obw2;
+  double *scal;         // [nf][8] per-frame scalars for the atom pass
+  int M, nch;
+  double norm, self_coeff, lambda;
+  int remove_self, k0;
+};
+
+// Parameter rows of H d per frame (core + self + k=0 terms) and the scalars
+// of the charge rows' self / k=0 / penalty terms.
+//   self:  E_s = -norm (rs D + self_coeff) sum_c |q_c|^2,  D = sum_m amp_m D0_m / 2V
+//   k=0:   E_0 = norm kfe (Q^2 - rs QQ) / 2V,  kfe = sum_m amp_m exp(-bw2_m kmin^2 / 2)
+//   pen:   E_p = lambda sum_c mean_c(q)^2
+template <typename T>
+__global__ void k_hvp_finalize_frames(HvpFinal a, int nf) {
+  const int f = blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= nf) return;
+  const FrameGeom &g = a.geom[f];
+  const double V = g.vol, i2v = 1.0 / (2.0 * V);
+  const int M = a.M;
+  const T *amp = (const T *)a.amp, *bw2 = (const T *)a.bw2;
+  const double *x = a.hred + (int64_t)f * 5 * M;
+  const double *D0 = x + 2 * M, *D1 = x + 3 * M, *D2 = x + 4 * M;
+  double Q = 0, QQ = 0, A = 0, QA = 0;
+  for (int c = 0; c < a.nch; ++c) {
+    Q += a.qsum[((int64_t)f * a.nch + c) * 2 + 0];
+    QQ += a.qsum[((int64_t)f * a.nch + c) * 2 + 1];
+    A += a.dsum[((int64_t)f * a.nch + c) * 2 + 0];
+    QA += a.dsum[((int64_t)f * a.nch + c) * 2 + 1];
+  }
+  const double rs = a.remove_self ? 1.0 : 0.0;
+  const double kmin2 = g.kmin2;
+  double diag = 0.0, ddiag = 0.0, kfe = 0.0, dkfe = 0.0;
+  for (int m = 0; m < M; ++m) {
+    const double am = (double)amp[m], ca = ldir<T>(a.damp, (int64_t)f * M + m), cb = ldir<T>(a.dbw2, (int64_t)f * M + m);
+    const double Em = exp(-0.5 * (double)bw2[m] * kmin2);
+    diag += am * D0[m] * i2v;
+    ddiag += (ca * D0[m] + cb * am * D1[m]) * i2v;
+    kfe += am * Em;
+    dkfe += ca * Em + cb * am * (-0.5 * kmin2) * Em;
+  }
+  for (int m = 0; m < M; ++m) {
+    const double am = (double)amp[m], ca = ldir<T>(a.damp, (int64_t)f * M + m), cb = ldir<T>(a.dbw2, (int64_t)f * M + m);
+    const double Em = exp(-0.5 * (double)bw2[m] * kmin2);
+    // core rows (the half-space sums carry 2, E carries 1/2V)
+    double ga = a.norm * i2v * x[m], gb = a.norm * i2v * x[M + m];
+    // self term: d/dtheta of -norm rs QQ D, along the direction
+    const double dD_a = D0[m] * i2v, dD_b = am * D1[m] * i2v;          // dD/damp_m, dD/dbw2_m
+    const double hD_a = cb * D1[m] * i2v;                               // (d2 D . c)_amp_m
+    const double hD_b = (ca * D1[m] + cb * am * D2[m]) * i2v;           // (d2 D . c)_bw2_m
+    ga += -a.norm * rs * (2.0 * QA * dD_a + QQ * hD_a);
+    gb += -a.norm * rs * (2.0 * QA * dD_b + QQ * hD_b);
+    if (a.k0) {
+      const double dk_a = Em, dk_b = am * (-0.5 * kmin2) * Em;
+      const double hk_a = cb * (-0.5 * kmin2) * Em;
+      const double hk_b = ca * (-0.5 * kmin2) * Em + cb * am * 0.25 * kmin2 * kmin2 * Em;
+      const double lin = 2.0 * Q * A - 2.0 * rs * QA, quad = Q * Q - rs * QQ;
+      ga += a.norm * i2v * (dk_a * lin + hk_a * quad);
+      gb += a.norm * i2v * (dk_b * lin + hk_b * quad);
+    }
+    ((T *)a.oamp)[(int64_t)f * M + m] = (T)ga;
+    ((T *)a.obw2)[(int64_t)f * M + m] = (T)gb;
+  }
+  double *s = a.scal + (int64_t)f * 8;
+  s[0] = rs * diag + a.self_coeff;
+  s[1] = rs * ddiag;
+  s[2] = a.k0 ? kfe : 0.0;
+  s[3] = a.k0 ? dkfe : 0.0;
+  s[4] = Q;
+  s[5] = A;
+  s[6] = rs;
+  s[7] = 0.0;
+}
+
+// Charge rows: self, k=0 and penalty terms added to the core term.
+template <typename T>
+__global__ void k_hvp_finalize_atoms(const FrameGeom *__restrict__ geom, const double *__restrict__ scal,
+                                     const double *__restrict__ dsum, const T *__restrict__ q, const void *dq,
+                                     T *__restrict__ oq, int nch, double norm, double lambda) {
+  const int f = blockIdx.y;
+  const FrameGeom &g = geom[f];
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= g.natoms) return;
+  const double *s = scal + (int64_t)f * 8;
+  const double i2v = 1.0 / (2.0 * g.vol);
+  const int64_t atom = g.atom_begin + i;
+  for (int c = 0; c < nch; ++c) {
+    const int64_t o = atom * nch + c;
+    const double qi = (double)q[o], ai = ldir<T>(dq, o);
+    double v = (double)oq[o];
+    v += -2.0 * norm * (ai * s[0] + qi * s[1]);
+    v += norm * i2v * (s[2] * (2.0 * s[5] - 2.0 * s[6] * ai) + s[3] * (2.0 * s[4] - 2.0 * s[6] * qi));
+    if (lambda > 0.0 && g.natoms > 0)
+      v += 2.0 * lambda * dsum[((int64_t)f * nch + c) * 2 + 0] / ((double)g.natoms * g.natoms);
+    oq[o] = (T)v;
+  }
+}
+
+template <typename T>
+int direct_hvp_impl(sog_direct *d, const sog_direct_args *a, const sog_hvp_args *hv, cudaStream_t st) {
+  const int nf = a->nframes, nch = a->nchannels, M = a->n_gauss;
+  std::vector<FrameHost> fh(nf);
+  int64_t kmax = 1, maxat = 0, slots = 0;
+  for (int f = 0; f < nf; ++f) {
+    for (int c = 0; c < 3; ++c)
+      if (a->nk[3 * f + c] < 0 || a->nk[3 * f + c] > 4096) return fail(SOG_ERR_INVALID, "nk out of range");
+    const int64_t nbox = (int64_t)(a->nk[3 * f] + 1) * (2 * a->nk[3 * f + 1] + 1) * (2 * a->nk[3 * f + 2] + 1);
+    kmax = std::max(kmax, nbox);
+    maxat = std::max<int64_t>(maxat, a->atom_count[f]);
+    fh[f].atom_begin = a->atom_begin[f];
+    fh[f].natoms = a->atom_count[f];
+    fh[f].slot_base = slots;
+    fh[f].k_sq_max = a->k_sq_max[f];
+    slots += a->atom_count[f];
+  }
+  if (kmax > ((int64_t)1 << 31)) return fail(SOG_ERR_INVALID, "mode box too large");
+  const unsigned kb = nblk(kmax, kDirThreads);
+  const int nh = 5 * M;
+  int rc;
+  if ((rc = d->up.reserve(sizeof(FrameHost) * nf + sizeof(int) * 3 * nf)) != SOG_OK) return rc;
+  if ((rc = d->up.wait()) != SOG_OK) return rc;
+  std::memcpy(d->up.p, fh.data(), sizeof(FrameHost) * nf);
+  std::memcpy((char *)d->up.p + sizeof(FrameHost) * nf, a->nk, sizeof(int) * 3 * nf);
+  const int qs = (int)std::max<int64_t>(1, std::min<int64_t>(256, (maxat + 16383) / 16384));
+  if (d->frames_host_dev.reserve(sizeof(FrameHost) * nf + sizeof(int) * 3 * nf) ||
+      d->geom.reserve(sizeof(FrameGeom) * nf) || d->status.reserve(16) ||
+      d->modes.reserve(sizeof(double) * 4 * kmax * nf) || d->sfac.reserve(sizeof(double) * 2 * kmax * nf * nch) ||
+      d->part.reserve(sizeof(double) * 2 * kb * nf * nch) || d->qsum.reserve(sizeof(double) * 2 * nf * nch) ||
+      d->qpart.reserve(sizeof(double) * 2 * (int64_t)nf * nch * qs) ||
+      d->hx.reserve(sizeof(double) * 2 * kmax * nf * nch) || d->hpart.reserve(sizeof(double) * nh * kb * nf) ||
+      d->hred.reserve(sizeof(double) * nh * nf) || d->hdsum.reserve(sizeof(double) * 2 * nf * nch) ||
+      d->hscal.reserve(sizeof(double) * 8 * nf) ||
+      d->redtmp.reserve(sizeof(double) * std::max<int64_t>(reduce_tmp_elems(nf, 1, kb, nh), 1)))
+    return fail(SOG_ERR_NOMEM, "device allocation failed (direct HVP)");
+  SOG_CUDA_TRY(cudaMemcpyAsync(d->frames_host_dev.p, d->up.p, sizeof(FrameHost) * nf + sizeof(int) * 3 * nf,
+                               cudaMemcpyHostToDevice, st));
+  SOG_CUDA_TRY(cudaEventRecord(d->up.done, st));
+  d->up.pending = true;
+  FrameGeom *geom = d->geom.as<FrameGeom>();
+  const FrameHost *fhd = d->frames_host_dev.as<FrameHost>();
+  const int *nkd = reinterpret_cast<const int *>(fhd + nf);
+  Tracer *tr = &d->tr;
+  tr->begin(st);
+  k_frame_setup<T><<<nblk(nf, 128), 128, 0, st>>>((const T *)a->cells, fhd, geom, nf, SOG_KCONV_PHYSICAL, 1, 1, 1,
+                                                  d->status.as<unsigned>());
+  after(tr, st, "frame_setup");
+  k_qsums<T><<<dim3(nf, nch, qs), 256, 0, st>>>((const T *)a->charges, nch, geom, d->qpart.as<double>());
+  k_reduce_parts<<<dim3(nf, nch, 1), 256, 0, st>>>(d->qpart.as<double>(), nf, nch, qs, 2, 2, d->qsum.as<double>());
+  after(tr, st, "qsums");
+  count_launch();
+  DirArgs da;
+  da.geom = geom;
+  da.nk = nkd;
+  da.kmax_modes = kmax;
+  da.nch = nch;
+  da.M = M;
+  da.kvec = d->modes.as<double>();
+  da.sfac = d->sfac.as<double>();
+  da.part = d->part.as<double>();
+  da.partx = nullptr;
+  da.nx_acc = 0;
+  k_direct_sfac<T><<<dim3(kb, nf), kDirThreads, 0, st>>>(da, (const T *)a->positions, (const T *)a->charges,
+                                                         (const T *)a->amp, (const T *)a->bw2);
+  after(tr, st, "direct_sfac");
+  HvpArgs h;
+  h.dq = hv->dir_q;
+  h.dr = hv->dir_r;
+  h.damp = hv->dir_amp;
+  h.dbw2 = hv->dir_bw2;
+  h.oq = hv->out_q;
+  h.orr = hv->out_r;
+  h.oamp = hv->out_amp;
+  h.obw2 = hv->out_bw2;
+  h.hx = d->hx.as<double>();
+  h.hpart = d->hpart.as<double>();
+  h.nh = nh;
+  k_direct_hvp_modes<T><<<dim3(kb, nf), kDirThreads, 0, st>>>(da, h, (const T *)a->positions,
+                                                              (const T *)a->charges, (const T *)a->amp,
+                                                              (const T *)a->bw2);
+  after(tr, st, "hvp_modes");
+  if (maxat > 0) {
+    if (maxat <= 32)
+      k_direct_hvp_atoms<T, 32><<<dim3(1, nf), 32, 0, st>>>(da, h, (const T *)a->positions, (const T *)a->charges,
+                                                            a->norm_factor);
+    else
+      k_direct_hvp_atoms<T><<<dim3(nblk(maxat, 128), nf), 128, 0, st>>>(da, h, (const T *)a->positions,
+                                                                        (const T *)a->charges, a->norm_factor);
+    after(tr, st, "hvp_atoms");
+  }
+  reduce_parts(h.hpart, nf, 1, kb, nh, nh, d->hred.as<double>(), d->redtmp.as<double>(), st);
+  after(tr, st, "reduce");
+  if (reduce_split(kb) > 1) count_launch();
+  k_hvp_dsums<T><<<dim3(nf, nch), 256, 0, st>>>((const T *)a->charges, hv->dir_q, nch, geom, d->hdsum.as<double>());
+  after(tr, st, "hvp_dsums");
+  HvpFinal hf;
+  hf.geom = geom;
+  hf.hred = d->hred.as<double>();
+  hf.qsum = d->qsum.as<double>();
+  hf.dsum = d->hdsum.as<double>();
+  hf.amp = a->amp;
+  hf.bw2 = a->bw2;
+  hf.damp = hv->dir_amp;
+  hf.dbw2 = hv->dir_bw2;
+  hf.oamp = hv->out_amp;
+  hf.obw2 = hv->out_bw2;
+  hf.scal = d->hscal.as<double>();
+  hf.M = M;
+  hf.nch = nch;
+  hf.norm = a->norm_factor;
+  hf.self_coeff = a->self_coeff;
+  hf.lambda = a->charge_neutral_lambda;
+  hf.remove_self = a->remove_self;
+  hf.k0 = a->k0_correction;
+  k_hvp_finalize_frames<T><<<nblk(nf, 64), 64, 0, st>>>(hf, nf);
+  after(tr, st, "hvp_finalize_frames");
+  if (maxat > 0) {
+    k_hvp_finalize_atoms<T><<<dim3(nblk(maxat, 256), nf), 256, 0, st>>>(
+        geom, d->hscal.as<double>(), d->hdsum.as<double>(), (const T *)a->charges, hv->dir_q, (T *)hv->out_q, nch,
+        a->norm_factor, a->charge_neutral_lambda);
+    after(tr, st, "hvp_finalize_atoms");
+  }
+  SOG_CUDA_TRY(cudaGetLastError());
+  return SOG_OK;
+}
+
+}  // namespace
+}  // namespace sogb
+
+extern "C" int sog_direct_hvp(sog_direct *d, const sog_direct_args *a, const sog_hvp_args *h, void *stream) {
+  if (!d || !a || !h) return fail(SOG_ERR_INVALID, "null argument");
+  if (a->nframes <= 0) return SOG_OK;
+  if (!a->atom_begin || !a->atom_count || !a->nk || !a->k_sq_max || !a->positions || !a->charges ||
+      !a->cells || !a->amp || !a->bw2)
+    return fail(SOG_ERR_INVALID, "missing input array");
+  if (!h->out_q || !h->out_r || !h->out_amp || !h->out_bw2) return fail(SOG_ERR_INVALID, "missing HVP output array");
+  if (a->nchannels < 1 || a->nchannels > kMaxCh)
+    return fail(SOG_ERR_UNSUPPORTED, "direct k-sum supports 1..8 charge channels");
+  if (a->n_gauss < 1 || a->n_gauss > kMaxGauss) return fail(SOG_ERR_INVALID, "n_gauss must be in [1, 64]");
+  DeviceGuard dg(d->device);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (d->dtype == SOG_DTYPE_F64) return direct_hvp_impl<double>(d, a, h, st);
+  return direct_hvp_impl<float>(d, a, h, st);
 }
 
 // ==========================================================================

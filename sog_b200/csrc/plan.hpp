@@ -100,6 +100,9 @@ struct sog_plan {
 struct sog_direct {
   int dtype = 0, device = 0;
   sogb::DevBuf frames_host_dev, geom, modes, sfac, part, qsum, status, qpart, redtmp;
+  // Hessian-vector products: the modes' X sums, per-block partials, reduced
+  // sums, direction sums and per-frame scalars
+  sogb::DevBuf hx, hpart, hred, hdsum, hscal;
   sogb::PinnedBuf up;
   sogb::Tracer tr;
 };

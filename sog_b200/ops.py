@@ -151,9 +151,58 @@ def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Ten
     return energy, forces, pot, gamp, gbw2, vir
 
 
+def run_hvp(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Tensor, bw2: torch.Tensor,
+            dq: Optional[torch.Tensor], dr: Optional[torch.Tensor], damp: Optional[torch.Tensor],
+            dbw2: Optional[torch.Tensor]):
+    """Hessian of every frame's energy applied to a direction: dq [N,C] on the
+    charges, dr [N,3] on the positions, damp / dbw2 [nf,M] per frame on the
+    kernel parameters (None: zero).  Returns (out_q [N,C], out_r [N,3],
+    out_amp [nf,M], out_bw2 [nf,M]).  The double backward of the solver."""
+    dev, dt = r.device, r.dtype
+    nf, M, N, C = spec.nframes, amp.numel(), r.shape[0], q.shape[1]
+    out_q = torch.zeros(N, C, dtype=dt, device=dev)
+    out_r = torch.zeros(N, 3, dtype=dt, device=dev)
+    out_a = torch.zeros(nf, M, dtype=dt, device=dev)
+    out_b = torch.zeros(nf, M, dtype=dt, device=dev)
+    contig = lambda t: None if t is None else t.contiguous()
+    q, r, amp, bw2 = q.contiguous(), r.contiguous(), amp.contiguous(), bw2.contiguous()
+    dq, dr, damp, dbw2 = contig(dq), contig(dr), contig(damp), contig(dbw2)
+    single = len(spec.buckets) == 1 and spec.buckets[0].frames == list(range(nf))
+    for b in spec.buckets:
+        kind = b.kind or spec.kind
+        if kind != "direct":
+            raise NotImplementedError(
+                "second derivatives (create_graph=True through the forces) are implemented for the "
+                "direct k-sum; the mesh solvers and the real-space pair sum raise here")
+        if single:
+            cells_b, da_b, db_b, oa_b, ob_b = spec.cells, damp, dbw2, out_a, out_b
+        else:
+            idx = b.frame_index(dev)
+            cells_b = spec.cells.index_select(0, idx).contiguous()
+            da_b = None if damp is None else damp.index_select(0, idx).contiguous()
+            db_b = None if dbw2 is None else dbw2.index_select(0, idx).contiguous()
+            oa_b = torch.zeros(len(b.frames), M, dtype=dt, device=dev)
+            ob_b = torch.zeros(len(b.frames), M, dtype=dt, device=dev)
+        h = b.host()
+        ctx = _lib.direct_ctx(dev.index if dev.index is not None else torch.cuda.current_device(),
+                              _lib.dtype_code(dt))
+        _lib.direct_hvp(ctx, atom_begin=h["atom_begin"], atom_count=h["atom_count"], nk=h["nk"],
+                        k_sq_max=h["k_sq_max"], positions=r, charges=q, cells=cells_b, amp=amp, bw2=bw2,
+                        norm_factor=spec.norm_factor, self_coeff=spec.self_coeff,
+                        remove_self=spec.remove_self, k0_correction=spec.k0_correction,
+                        charge_neutral_lambda=spec.charge_neutral_lambda, dir_q=dq, dir_r=dr,
+                        dir_amp=da_b, dir_bw2=db_b, out_q=out_q, out_r=out_r, out_amp=oa_b,
+                        out_bw2=ob_b)
+        if not single:
+            out_a.index_copy_(0, idx, oa_b)
+            out_b.index_copy_(0, idx, ob_b)
+    return out_q, out_r, out_a, out_b
+
+
 class SolveFunction(torch.autograd.Function):
     """energy[nf] = SOG(q, r; amp, bw2); explicit forces / virial as extra,
-    non-differentiable outputs."""
+    non-differentiable outputs.  The backward is differentiable again
+    (GradFunction) when a graph is being built (create_graph=True)."""
 
     @staticmethod
     def forward(ctx, q, r, amp, bw2, spec: SolveSpec, want_force_out: bool, want_virial_out: bool):
@@ -163,8 +212,8 @@ class SolveFunction(torch.autograd.Function):
         energy, forces, pot, gamp, gbw2, vir = run_solver(
             spec, q, r, amp, bw2, want_force=want_force, want_pot=bool(need_q),
             want_grad=want_grad, want_virial=bool(want_virial_out))
-        ctx.spec_frame = spec.frame_of_atom
-        ctx.save_for_backward(forces if need_r else None, pot, gamp, gbw2)
+        ctx.spec = spec
+        ctx.save_for_backward(q, r, amp, bw2, forces if need_r else None, pot, gamp, gbw2)
         f_out = forces if want_force_out else None
         v_out = vir if want_virial_out else None
         outs = [energy, f_out, v_out]
@@ -174,19 +223,78 @@ class SolveFunction(torch.autograd.Function):
         return tuple(outs)
 
     @staticmethod
-    @once_differentiable
     def backward(ctx, gE, gF, gV):
-        forces, pot, gamp, gbw2 = ctx.saved_tensors
-        grad_q = grad_r = grad_a = grad_b = None
+        q, r, amp, bw2, forces, pot, gamp, gbw2 = ctx.saved_tensors
         if gE is None:
             return None, None, None, None, None, None, None
-        ga = gE.index_select(0, ctx.spec_frame)
-        if ctx.needs_input_grad[0] and pot is not None:
-            grad_q = pot * ga[:, None]
-        if ctx.needs_input_grad[1] and forces is not None:
-            grad_r = -forces * ga[:, None]
-        if ctx.needs_input_grad[2] and gamp is not None:
-            grad_a = (gE[:, None] * gamp).sum(0)
-        if ctx.needs_input_grad[3] and gbw2 is not None:
-            grad_b = (gE[:, None] * gbw2).sum(0)
-        return grad_q, grad_r, grad_a, grad_b, None, None, None
+        needs = tuple(ctx.needs_input_grad[:4])
+        dEdr = None if forces is None else -forces
+        if torch.is_grad_enabled():
+            # create_graph=True: the gradients are differentiable functions of
+            # (gE, q, r, amp, bw2); their own backward is the Hessian-vector
+            # product of the solver (run_hvp)
+            outs = GradFunction.apply(gE, q, r, amp, bw2, pot, dEdr, gamp, gbw2, ctx.spec, needs)
+            gq, gr, ga, gb = outs
+        else:
+            gq, gr, ga, gb = _first_order(gE, ctx.spec.frame_of_atom, pot, dEdr, gamp, gbw2, needs)
+        return gq, gr, ga, gb, None, None, None
+
+
+def _first_order(gE, frame_of_atom, pot, dEdr, gamp, gbw2, needs):
+    """gE-weighted first derivatives: dE/dq, dE/dr per atom (its frame's
+    weight) and dE/d(amp, bw2) summed over frames."""
+    ga = gE.index_select(0, frame_of_atom)
+    gq = pot * ga[:, None] if needs[0] and pot is not None else None
+    gr = dEdr * ga[:, None] if needs[1] and dEdr is not None else None
+    gam = (gE[:, None] * gamp).sum(0) if needs[2] and gamp is not None else None
+    gbw = (gE[:, None] * gbw2).sum(0) if needs[3] and gbw2 is not None else None
+    return gq, gr, gam, gbw
+
+
+class GradFunction(torch.autograd.Function):
+    """(dE/dq, dE/dr, dE/damp, dE/dbw2) weighted by the energy cotangent gE, as
+    a differentiable function of (gE, q, r, amp, bw2).  Its backward is the
+    solver's Hessian-vector product: the second derivatives a force loss needs
+    (the reference gets them from torch autograd through its direct k-sum,
+    gaussian.py:1180-1337, and through the differentiable ops of its Python
+    mesh solvers)."""
+
+    @staticmethod
+    def forward(ctx, gE, q, r, amp, bw2, pot, dEdr, gamp, gbw2, spec, needs):
+        ctx.spec = spec
+        ctx.needs = needs
+        ctx.save_for_backward(gE, q, r, amp, bw2, pot, dEdr, gamp, gbw2)
+        return _first_order(gE, spec.frame_of_atom, pot, dEdr, gamp, gbw2, needs)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, uq, ur, ua, ub):
+        gE, q, r, amp, bw2, pot, dEdr, gamp, gbw2 = ctx.saved_tensors
+        spec = ctx.spec
+        fa = spec.frame_of_atom
+        ga = gE.index_select(0, fa)
+        # d/dgE: the directional derivative of each frame's energy
+        d_gE = None
+        if ctx.needs_input_grad[0]:
+            d_gE = torch.zeros_like(gE)
+            if uq is not None and pot is not None:
+                d_gE.index_add_(0, fa, (uq * pot).sum(1))
+            if ur is not None and dEdr is not None:
+                d_gE.index_add_(0, fa, (ur * dEdr).sum(1))
+            if ua is not None and gamp is not None:
+                d_gE += gamp @ ua
+            if ub is not None and gbw2 is not None:
+                d_gE += gbw2 @ ub
+        want_hvp = any(ctx.needs_input_grad[1:5])
+        g_q = g_r = g_a = g_b = None
+        if want_hvp:
+            dq = None if uq is None else uq * ga[:, None]
+            dr = None if ur is None else ur * ga[:, None]
+            da = None if ua is None else gE[:, None] * ua[None, :]
+            db = None if ub is None else gE[:, None] * ub[None, :]
+            oq, orr, oa, ob = run_hvp(spec, q, r, amp, bw2, dq, dr, da, db)
+            g_q = oq if ctx.needs_input_grad[1] else None
+            g_r = orr if ctx.needs_input_grad[2] else None
+            g_a = oa.sum(0) if ctx.needs_input_grad[3] else None
+            g_b = ob.sum(0) if ctx.needs_input_grad[4] else None
+        return d_gE, g_q, g_r, g_a, g_b, None, None, None, None, None, None

@@ -407,9 +407,85 @@ def cfg3_case():
     print("cfg3_quads4", rec["energy"])
 
 
+def run_hvp_case(name, r, q, cell, batch, sog_args=None, gauss_kwargs=None, seed=0):
+    """Second derivatives through the reference's direct k-sum (torch autograd
+    with create_graph=True, as a force-matching loss needs them): forces F =
+    -dE/dr and charge gradients P = dE/dq built with create_graph=True, then
+    loss = sum(U * F) + sum(W * F^2) + sum(Z * P) + sum(e_w * E) with fixed
+    seeded weights; the fixture holds d loss / d(q, r, amp, bw2)."""
+    torch.manual_seed(0)
+    if sog_args is not None:
+        g = Sog(dict(sog_args)).gaussian
+    else:
+        g = Gaussian(**gauss_kwargs)
+    gen = torch.Generator().manual_seed(seed)
+    rg = r.clone().requires_grad_(True)
+    qg = q.clone().requires_grad_(True)
+    e = g(q=qg, r=rg, cell=cell, batch=batch)
+    e_w = torch.arange(1, e.shape[0] + 1, dtype=F64)
+    gr, gq = torch.autograd.grad((e * e_w).sum(), (rg, qg), create_graph=True)
+    F = -gr
+    U = torch.randn(F.shape, generator=gen, dtype=F64)
+    W = torch.rand(F.shape, generator=gen, dtype=F64)
+    Z = torch.randn(gq.shape, generator=gen, dtype=F64)
+    loss = (U * F).sum() + (W * F * F).sum() + (Z * gq).sum() + (e * e_w).sum()
+    loss.backward()
+    rec = dict(r=r.numpy(), q=q.numpy(), cell=cell.numpy(), batch=batch.numpy(),
+               amp=g.amp.detach().to(F64).numpy(), bw2=g.bandwidth.detach().to(F64).numpy(),
+               amp_dtype=str(g.amp.dtype), self_coeff=float(g.self_coeff),
+               remove_self=int(g.remove_self_interaction),
+               lam=-1.0 if g.charge_neutral_lambda is None else float(g.charge_neutral_lambda),
+               n_dl=-1.0 if g.n_dl is None else float(g.n_dl), e_w=e_w.numpy(), U=U.numpy(),
+               W=W.numpy(), Z=Z.numpy(), loss=loss.detach().numpy(), grad_q=qg.grad.numpy(),
+               grad_r=rg.grad.numpy())
+    if isinstance(g.amp, torch.nn.Parameter) and g.amp.grad is not None:
+        rec["grad_amp"] = g.amp.grad.to(F64).numpy()
+        rec["grad_bw2"] = g.bandwidth.grad.to(F64).numpy()
+    np.savez_compressed(os.path.join(OUT, f"{name}.npz"), **rec)
+    print(name, float(loss))
+
+
+def hvp_cases():
+    """Second-derivative fixtures of the direct k-sum; own generator."""
+    gen = torch.Generator().manual_seed(2027)
+    # README quickstart box, default (fp32-created) trainable parameters
+    n = 16
+    r = torch.rand(n, 3, generator=gen, dtype=F64) * 12.0
+    q = torch.rand(n, generator=gen, dtype=F64) - 0.5
+    q = q - q.mean()
+    run_hvp_case("hvp_direct_quickstart", r, q, torch.eye(3, dtype=F64).unsqueeze(0) * 12.0,
+                 torch.zeros(n, dtype=torch.int64), sog_args={"use_atomwise": False}, seed=1)
+    # two triclinic frames, two channels, internal trainable parameters
+    na, nb = 14, 11
+    cells = torch.stack([triclinic(9.0, 8.6, 9.3, 84.0, 93.0, 101.0),
+                         torch.tensor([[8.5, 0.0, 0.0], [0.4, 9.1, 0.0], [-0.3, 0.5, 8.8]], dtype=F64)])
+    r = torch.cat([torch.rand(na, 3, generator=gen, dtype=F64) @ cells[0],
+                   torch.rand(nb, 3, generator=gen, dtype=F64) @ cells[1]])
+    q = torch.rand(na + nb, 2, generator=gen, dtype=F64) - 0.5
+    batch = torch.cat([torch.zeros(na, dtype=torch.int64), torch.ones(nb, dtype=torch.int64)])
+    run_hvp_case("hvp_direct_triclinic_2ch", r, q, cells, batch,
+                 gauss_kwargs=dict(n_dl=1.6, amp=torch.tensor([0.7, 1.1, 1.4], dtype=F64),
+                                   bandwidth=torch.tensor([1.3, 2.1, 3.4], dtype=F64),
+                                   kernel_param_mode="internal", trainable=True), seed=2)
+    # non-neutral charges (k=0 term), self term kept, neutrality penalty, fastsog r_cut convention
+    n = 18
+    r = torch.rand(n, 3, generator=gen, dtype=F64) * 10.0
+    q = torch.rand(n, generator=gen, dtype=F64) - 0.4
+    run_hvp_case("hvp_direct_k0_penalty", r, q, torch.eye(3, dtype=F64).unsqueeze(0) * 10.0,
+                 torch.zeros(n, dtype=torch.int64),
+                 gauss_kwargs=dict(rcut=5.0, m=6, remove_self_interaction=False, charge_neutral_lambda=0.3,
+                                   trainable=True), seed=3)
+    # the fastsog convention with the self term removed (self_coeff != 0)
+    run_hvp_case("hvp_direct_rcut", r, q - q.mean(), torch.eye(3, dtype=F64).unsqueeze(0) * 10.0,
+                 torch.zeros(n, dtype=torch.int64),
+                 sog_args={"use_atomwise": False, "r_cut": 5.0, "m": 8}, seed=4)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    if sys.argv[1:] == ["cfg3"]:
+    if sys.argv[1:] == ["hvp"]:
+        hvp_cases()
+    elif sys.argv[1:] == ["cfg3"]:
         cfg3_case()
     elif sys.argv[1:] == ["cubes2"]:
         cubes2_cases()
