@@ -59,6 +59,12 @@ def workload(name: str):
                              "512 x 512 x 128 mesh, B-spline order 6, 12 Gaussians bw 1.2-60 A "
                              "(profiling case: about 3 GB on the device)", natoms=1 << 18, L=220.0,
                     box=(220.0, 220.0, 55.0), n_dl=0.86, order=6, m=12, bw_lo=1.2, bw_hi=60.0, qstd=0.6)
+    if name == "cfg5_zslab":
+        return dict(workload="half-width column of the large system: 262,144 atoms, 110 x 110 x 220 A, "
+                             "256 x 256 x 512 mesh, B-spline order 6, 12 Gaussians bw 1.2-60 A "
+                             "(profiling case for the 512-point z pass: about 3 GB on the device)",
+                    natoms=1 << 18, L=220.0, box=(110.0, 110.0, 220.0), n_dl=0.86, order=6, m=12,
+                    bw_lo=1.2, bw_hi=60.0, qstd=0.6)
     if name == "cfg2":
         return dict(workload="water-like box: 3,000 atoms, 31 A cubic, 64^3 mesh, B-spline order 6, "
                              "12 Gaussians bw 1.2*1.62^m", natoms=3000, L=31.0, n_dl=1.0, order=6,
@@ -922,7 +928,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="sog_b200", choices=["sog_b200", "reference"])
-    ap.add_argument("--config", default="cfg5", choices=["cfg5", "cfg5_eighth", "cfg5_quarter", "cfg2", "cfg4"])
+    ap.add_argument("--config", default="cfg5", choices=["cfg5", "cfg5_eighth", "cfg5_quarter", "cfg5_zslab", "cfg2", "cfg4"])
     ap.add_argument("--dtype", default="f64", choices=["f64", "f32"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--transport", default="peer", choices=["peer", "exchange"],

@@ -392,7 +392,6 @@ __global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? SOG_SPREAD_MINB : 2)
   const int txv = min(kTileX, ag.nx - x0), tyv = min(kTileY, ag.ny - y0);
   const int tzv = min(kTileZ, a.zlo + a.zcnt - z0);
   const FrameGeom &g = a.geom[f];
-  const T scale = (T)g.scale;
 
   for (int i = threadIdx.x; i < NW * NK; i += blockDim.x) (&kcnt[0][0])[i] = 0;
   if (threadIdx.x < 32) {
@@ -564,7 +563,7 @@ __global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? SOG_SPREAD_MINB : 2)
           c_wz[(kk * kTileZ + z) * CH + slot] = wz;
         }
       }
-      c_q[slot] = qv * scale;
+      c_q[slot] = qv;
       c_ay[slot] = an.y;
     }
     __syncthreads();
@@ -598,9 +597,14 @@ __global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? SOG_SPREAD_MINB : 2)
     const int gx = x0 + lx;
     const int64_t plane = (int64_t)ag.nx * ag.ny;
     TG *out = static_cast<TG *>(a.rho) + (int64_t)f * plane * a.zcnt + (int64_t)gy * ag.nx + gx;
+    // the charge scale N_g / V (quads_fft.py:287) applied once, in the grid
+    // type: an fp32 copy of it would scale the whole mesh energy by its
+    // rounding (1e-4 of the total energy of the 1,048,576-atom system, whose
+    // mesh and self terms are a thousand times the total)
+    const TG scale = (TG)g.scale;
 #pragma unroll
     for (int z = 0; z < kTileZ; ++z)
-      if (z < tzv) out[(int64_t)(z0 - a.zlo + z) * plane] = acc[z];
+      if (z < tzv) out[(int64_t)(z0 - a.zlo + z) * plane] = acc[z] * scale;
   }
 }
 
