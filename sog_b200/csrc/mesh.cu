@@ -662,6 +662,9 @@ struct KsArgs {
   // k_green builds the tables of the other frames only.
   const double *krad;
   int64_t krad_stride;
+  // 1: the fused z pass stores Y1 / Y2 of orthorhombic frames in field slots
+  // 0 / 2 for k_cols_fields (single-device calls with forces)
+  int two_slot;
 };
 
 // kernel parameter m as a double
@@ -1321,39 +1324,71 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
     // transforms serve all three: Y1 = IFFT(s rho), Y2 = IFFT(i mz s rho),
     // field a = i kxy_a Y1 + kz_a Y2.  The potential field (s = gE) is Y1
     // itself unless the force uses the alias-summed gF.
+    // With two_slot, orthorhombic frames store Y1 and Y2 as they are (slots
+    // 0 and 2): each field is then one of them times a factor that depends on
+    // mx or my only, which k_cols_fields applies around the inverse y
+    // transform, so a third of the field bytes never go to HBM.  Y2's input
+    // waits in the tile buffer (in this thread's own slots) while Y1 is
+    // transformed, so one transform's data is in registers at a time.
     bool pot_done = !(nfield > (a.want_force ? 3 : 0));
+    const bool two = a.two_slot && g.ortho && a.want_force;   // frame-uniform
     if (a.want_force) {
-      C y1[kEPT], y2[kEPT];
-#pragma unroll
-      for (int e = 0; e < kEPT; ++e) {
-        const int slot = (t + e * TPT) * ic + c;
-        const C r = cur[slot];
-        const double sc = gFp ? (ok ? gFp[(int64_t)(t + e * TPT) * inner] * inv : 0.0) : gs[e];
-        y1[e] = cmk<C, T>((T)(sc * (double)r.x), (T)(sc * (double)r.y));
-      }
-      ct_fft<T, +1, L, true>(y1, t, stg, xbuf + c, ic);
-#pragma unroll
-      for (int e = 0; e < kEPT; ++e) {
-        const int slot = (t + e * TPT) * ic + c;
-        const C r = cur[slot];
-        const double sc = gFp ? (ok ? gFp[(int64_t)(t + e * TPT) * inner] * inv : 0.0) : gs[e];
-        const double mzs = (double)signed_mode(t + e * TPT, a.nz) * sc;
-        y2[e] = cmk<C, T>((T)(-mzs * (double)r.y), (T)(mzs * (double)r.x));
-      }
-      ct_fft<T, +1, L, true>(y2, t, stg, xbuf + c, ic);
-      for (int fl = 0; fl < 3; ++fl) {
-        const double kxy = g.kmat[fl * 3 + 0] * mx + g.kmat[fl * 3 + 1] * my;
-        const double kz = g.kmat[fl * 3 + 2];
+      if (!pot_done && gFp) {
+        // alias frame: the potential's own Green function, from the spectrum
+        // while it is still in the tile buffer
         C wv[kEPT];
 #pragma unroll
-        for (int e = 0; e < kEPT; ++e)
-          wv[e] = cmk<C, T>((T)(-kxy * (double)y1[e].y + kz * (double)y2[e].x),
-                            (T)(kxy * (double)y1[e].x + kz * (double)y2[e].y));
-        store_field(fl, wv);
-      }
-      if (!pot_done && !gFp) {
-        store_field(3, y1);
+        for (int e = 0; e < kEPT; ++e) {
+          const C r = cur[(t + e * TPT) * ic + c];
+          wv[e] = cmk<C, T>((T)(gs[e] * (double)r.x), (T)(gs[e] * (double)r.y));
+        }
+        ct_fft<T, +1, L, true>(wv, t, stg, xbuf + c, ic);
+        store_field(3, wv);
         pot_done = true;
+      }
+      C y[kEPT];
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) {
+        const int slot = (t + e * TPT) * ic + c;
+        const C r = cur[slot];
+        const double sc = gFp ? (ok ? gFp[(int64_t)(t + e * TPT) * inner] * inv : 0.0) : gs[e];
+        y[e] = cmk<C, T>((T)(sc * (double)r.x), (T)(sc * (double)r.y));
+        const double mzs = (double)signed_mode(t + e * TPT, a.nz) * sc;
+        cur[slot] = cmk<C, T>((T)(-mzs * (double)r.y), (T)(mzs * (double)r.x));   // Y2's input
+      }
+      ct_fft<T, +1, L, true>(y, t, stg, xbuf + c, ic);
+      if (two) {
+        store_field(0, y);
+#pragma unroll
+        for (int e = 0; e < kEPT; ++e) y[e] = cur[(t + e * TPT) * ic + c];
+        ct_fft<T, +1, L, true>(y, t, stg, xbuf + c, ic);
+        store_field(2, y);
+        pot_done = true;   // k_cols_fields takes the potential from Y1
+      } else {
+        if (!pot_done) {
+          store_field(3, y);
+          pot_done = true;
+        }
+        C w[kEPT];
+#pragma unroll
+        for (int e = 0; e < kEPT; ++e) {
+          const int slot = (t + e * TPT) * ic + c;
+          w[e] = cur[slot];
+          cur[slot] = y[e];   // Y1 waits in the tile buffer
+        }
+        ct_fft<T, +1, L, true>(w, t, stg, xbuf + c, ic);
+        for (int fl = 0; fl < 3; ++fl) {
+          const double kxy = g.kmat[fl * 3 + 0] * mx + g.kmat[fl * 3 + 1] * my;
+          const double kz = g.kmat[fl * 3 + 2];
+          C wv[kEPT];
+#pragma unroll
+          for (int e = 0; e < kEPT; ++e) {
+            const C y1 = cur[(t + e * TPT) * ic + c];
+            wv[e] = cmk<C, T>((T)(-kxy * (double)y1.y + kz * (double)w[e].x),
+                              (T)(kxy * (double)y1.x + kz * (double)w[e].y));
+          }
+          store_field(fl, wv);
+        }
       }
     }
     if (!pot_done) {
@@ -1364,7 +1399,7 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
         wv[e] = cmk<C, T>((T)(gs[e] * (double)r.x), (T)(gs[e] * (double)r.y));
       }
       ct_fft<T, +1, L, true>(wv, t, stg, xbuf + c, ic);
-      store_field(a.want_force ? 3 : 0, wv);
+      store_field(0, wv);
     }
     accE = warp_sum(accE);
     accD = warp_sum(accD);
@@ -1387,6 +1422,115 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
   }
   cp_async_wait<0>();
   if (a.zdst[0]) __threadfence_system();
+}
+
+// Inverse y transform of the field spectra [nf][F][nz][ny][nx/2+1], in place,
+// forming the fields of two-slot frames (k_zfused_g): tile = (plane o =
+// (f*F + s)*nz + z, ic columns mx).  An orthorhombic frame holds Y1 in slot 0
+// and Y2 in slot 2: slot 0 yields field x = i kx mx IFFT(Y1) (and the
+// potential IFFT(Y1) into slot 3, unless the z pass stored the frame's own
+// potential there) and field y = ky IFFT(i my Y1) into slot 1; slot 2 yields
+// field z = kz IFFT(Y2).  Slot 1, and slot 3 when it was not stored, have no
+// input and are skipped.  Other frames: a plain inverse transform of every
+// slot.  Same pipeline as k_cols_pipe.
+template <typename T, bool PAD, int L>
+__global__ void k_cols_fields(cplx_t<T> *__restrict__ data, const FrameGeom *__restrict__ geom, int F, int nz,
+                              int64_t inner, int ic, int64_t ntiles, const cplx_t<T> *__restrict__ tw,
+                              int two_slot, int want_pot) {
+  using C = cplx_t<T>;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  constexpr int n = 1 << L, TPT = n / kEPT;
+  C *buf0 = reinterpret_cast<C *>(smem_raw);
+  C *buf1 = buf0 + (size_t)n * ic;
+  C *xbuf = buf1 + (size_t)n * ic;
+  C *stg = xbuf + (size_t)(PAD ? padded_row(n) : n) * ic;
+  load_stage_twiddles<T, L, 0>(stg, tw);
+  const int c = threadIdx.x % ic, t = threadIdx.x / ic;
+  const int64_t nchunks = (inner + ic - 1) / ic;
+  // role of a tile: 0 skip, 1 plain, 2 slot 0 (fields x, y, potential), 3 slot 2 (field z)
+  auto role = [&](int64_t tile) -> int {
+    const int64_t fs = tile / nchunks / nz;
+    const int f = (int)(fs / F), sl = (int)(fs - (int64_t)f * F);
+    const FrameGeom &g = geom[f];
+    if (!(two_slot && g.ortho)) return 1;
+    if (sl == 0) return 2;
+    if (sl == 2) return 3;
+    if (sl == 3 && g.pad) return 1;
+    return 0;
+  };
+  int64_t tile = blockIdx.x;
+  if (tile < ntiles && role(tile)) cols_issue<T>(buf0, data, inner, n, ic, nchunks, tile);
+  cp_async_commit();
+  for (int it = 0; tile < ntiles; ++it, tile += gridDim.x) {
+    C *cur = (it & 1) ? buf1 : buf0;
+    C *nxt = (it & 1) ? buf0 : buf1;
+    const int64_t next = tile + gridDim.x;
+    if (next < ntiles && role(next)) cols_issue<T>(nxt, data, inner, n, ic, nchunks, next);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const int rl = role(tile);   // block-uniform
+    if (rl) {
+      const int64_t o = tile / nchunks;
+      const int64_t i0 = (tile - o * nchunks) * ic;
+      const int64_t fs = o / nz;
+      const int f = (int)(fs / F);
+      const FrameGeom &g = geom[f];
+      const bool okc = i0 + c < inner;
+      const int mx = (int)(i0 + c);
+      const int64_t pl = (int64_t)n * inner;   // one z plane of one slot
+      C *base = data + o * pl + i0 + c;        // this slot
+      const int64_t sl = fs - (int64_t)f * F;
+      C *slot0 = base - (sl * nz) * pl;        // slot 0 of the same (frame, z)
+      C v[kEPT];
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) v[e] = cur[(t + e * TPT) * ic + c];
+      ct_fft<T, +1, L, PAD>(v, t, stg, xbuf + c, ic);
+      if (rl == 1) {
+        if (okc) {
+#pragma unroll
+          for (int e = 0; e < kEPT; ++e) base[(int64_t)(t + e * TPT) * inner] = v[e];
+        }
+      } else if (rl == 3) {
+        const double kz = g.kmat[8];
+        if (okc) {
+#pragma unroll
+          for (int e = 0; e < kEPT; ++e)
+            base[(int64_t)(t + e * TPT) * inner] = cmk<C, T>((T)(kz * (double)v[e].x), (T)(kz * (double)v[e].y));
+        }
+      } else {
+        const double kxm = g.kmat[0] * mx;
+        if (okc) {
+#pragma unroll
+          for (int e = 0; e < kEPT; ++e)
+            slot0[(int64_t)(t + e * TPT) * inner] =
+                cmk<C, T>((T)(-kxm * (double)v[e].y), (T)(kxm * (double)v[e].x));
+          if (want_pot && !g.pad) {
+            C *p3 = slot0 + (int64_t)3 * nz * pl;
+#pragma unroll
+            for (int e = 0; e < kEPT; ++e) p3[(int64_t)(t + e * TPT) * inner] = v[e];
+          }
+        }
+        // field y: ky IFFT(i my Y1), Y1 still in the tile buffer
+#pragma unroll
+        for (int e = 0; e < kEPT; ++e) {
+          const C r = cur[(t + e * TPT) * ic + c];
+          const double my = (double)signed_mode(t + e * TPT, n);
+          v[e] = cmk<C, T>((T)(-my * (double)r.y), (T)(my * (double)r.x));
+        }
+        ct_fft<T, +1, L, PAD>(v, t, stg, xbuf + c, ic);
+        const double ky = g.kmat[4];
+        if (okc) {
+          C *s1 = slot0 + (int64_t)nz * pl;
+#pragma unroll
+          for (int e = 0; e < kEPT; ++e)
+            s1[(int64_t)(t + e * TPT) * inner] = cmk<C, T>((T)(ky * (double)v[e].x), (T)(ky * (double)v[e].y));
+        }
+      }
+    }
+    __syncthreads();  // every thread is done with `cur` before it is refilled
+  }
+  cp_async_wait<0>();
 }
 
 // Extras: dE/d(amp_m, bw2_m) partial sums (cubes2_fft.py:822-862) and the
@@ -2008,6 +2152,36 @@ void pass_cols(sog_plan *p, cplx_t<T> *data, int n, int64_t inner, int64_t outer
   after(&p->tr, st, name);
 }
 
+// Inverse y pass of the field spectra with the field formation of two-slot
+// frames (k_cols_fields); power-of-two ny.
+template <typename T>
+void pass_cols_fields(sog_plan *p, cplx_t<T> *fspec, const FrameGeom *geom, int nf, int F, int two_slot,
+                      int want_pot, cudaStream_t st) {
+  using C = cplx_t<T>;
+  const int ny = p->d.ny, nz = p->d.nz;
+  const int64_t inner = p->nxh;
+  with_pow2(ny, [&](auto lc) {
+    constexpr int L = decltype(lc)::value;
+    constexpr int nn = 1 << L;
+    constexpr int thr_cap = sizeof(T) == 4 ? 512 : 256;
+    const int ic = reg_width<T>(nn, thr_cap, thr_cap * 256);
+    const int64_t ntiles = (int64_t)nf * F * nz * ((inner + ic - 1) / ic);
+    const int thr = (nn / kEPT) * ic;
+    if (ic >= 8) {
+      const size_t sm = (3 * (size_t)nn * ic + nn) * sizeof(C);
+      allow_smem(k_cols_fields<T, false, L>);
+      k_cols_fields<T, false, L><<<persistent_grid(k_cols_fields<T, false, L>, thr, sm, ntiles), thr, sm, st>>>(
+          fspec, geom, F, nz, inner, ic, ntiles, tw_of<T>(p, 1), two_slot, want_pot);
+    } else {
+      const size_t sm = ((2 * (size_t)nn + padded_row(nn)) * ic + nn) * sizeof(C);
+      allow_smem(k_cols_fields<T, true, L>);
+      k_cols_fields<T, true, L><<<persistent_grid(k_cols_fields<T, true, L>, thr, sm, ntiles), thr, sm, st>>>(
+          fspec, geom, F, nz, inner, ic, ntiles, tw_of<T>(p, 1), two_slot, want_pot);
+    }
+  });
+  after(&p->tr, st, "fft_y_inv");
+}
+
 template <typename T>
 void set_fft_smem_attrs() {
   const int big = 200 * 1024;
@@ -2375,6 +2549,8 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   const bool zfuse = is_pow2(nz);
   const bool zgeneric = zfuse && nz > 1024;  // runtime-plan fused pass, Green on the fly
   if (zfuse && !zgeneric && (rc = setup_radial<TF>(p, ka, nf, st)) != SOG_OK) return rc;
+  // two-slot field spectra (fused z pass -> k_cols_fields) for power-of-two ny
+  ka.two_slot = (zfuse && !zgeneric && want_force && is_pow2(ny) && ny <= 1024) ? 1 : 0;
   // fused z pass: 512 threads (8-column tiles) for 512 and 1024 points
   const int zic = zfuse ? (nz >= 512 && nz <= 1024 ? reg_width<TF>(nz, 512, 64 * 1024)
                                                    : reg_width<TF>(nz, 256, 32 * 1024))
@@ -2453,7 +2629,10 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
       if (!zfuse)
         pass_cols<T, +1>(p, p->fspec.as<C>(), nz, (int64_t)ny * nxh, nb, p->rpz, tw_of<T>(p, 2), st,
                          "fft_z_inv");
-      pass_cols<T, +1>(p, p->fspec.as<C>(), ny, nxh, nb * nz, p->rpy, tw_of<T>(p, 1), st, "fft_y_inv");
+      if (ka.two_slot)
+        pass_cols_fields<T>(p, p->fspec.as<C>(), geom, nf, nfield, 1, want_pot ? 1 : 0, st);
+      else
+        pass_cols<T, +1>(p, p->fspec.as<C>(), ny, nxh, nb * nz, p->rpy, tw_of<T>(p, 1), st, "fft_y_inv");
       pass_x_inv<T>(p, p->fspec.as<C>(), p->freal.as<T>(), nf, (int64_t)nz * ny, nfield, st);
       gar.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
       gar.channel = c;
