@@ -287,6 +287,12 @@ typedef struct sog_realspace_args {
  * direct-solver context (its scratch and timing); dtype as the context's. */
 SOG_API int sog_realspace_forward(sog_direct *d, const sog_realspace_args *args, void *stream);
 
+/* Hessian-vector product of the real-space pair-sum energy (sog_hvp_args as
+ * for sog_direct_hvp): the second derivatives the reference takes with
+ * torch.autograd through compute_potential_realspace (gaussian.py:822-845). */
+SOG_API int sog_realspace_hvp(sog_direct *d, const sog_realspace_args *args, const sog_hvp_args *h,
+                              void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Direct k-sum without allocation (no counterpart in the reference)         */
 /* ------------------------------------------------------------------------ */

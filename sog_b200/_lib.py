@@ -88,7 +88,7 @@ EXPORTS = ["sog_strerror", "sog_last_error", "sog_version", "sog_launch_count", 
            "sog_mesh_forward", "sog_direct_create", "sog_direct_destroy", "sog_direct_set_timing",
            "sog_direct_timings", "sog_direct_forward", "sog_direct_forward_noalloc",
            "sog_mesh_slab_workspace", "sog_mesh_slab_forward", "sog_realspace_forward",
-           "sog_direct_hvp"]
+           "sog_direct_hvp", "sog_realspace_hvp"]
 
 _lib = None
 _lock = threading.Lock()
@@ -125,6 +125,7 @@ def load():
         lib.sog_direct_forward.argtypes = [_vp, ctypes.POINTER(DirectArgs), _vp]
         lib.sog_realspace_forward.argtypes = [_vp, ctypes.POINTER(RealspaceArgs), _vp]
         lib.sog_direct_hvp.argtypes = [_vp, ctypes.POINTER(DirectArgs), ctypes.POINTER(HvpArgs), _vp]
+        lib.sog_realspace_hvp.argtypes = [_vp, ctypes.POINTER(RealspaceArgs), ctypes.POINTER(HvpArgs), _vp]
         lib.sog_launch_count.restype = ctypes.c_ulonglong
         for name in ("sog_plan_set_timing", "sog_direct_set_timing"):
             getattr(lib, name).argtypes = [_vp, ctypes.c_int]
@@ -447,3 +448,28 @@ def direct_hvp(ctx, *, atom_begin, atom_count, nk, k_sq_max, positions, charges,
         stream = torch.cuda.current_stream(positions.device).cuda_stream
     check(load().sog_direct_hvp(ctx, ctypes.byref(args), ctypes.byref(h), ctypes.c_void_p(stream)),
           "sog_direct_hvp")
+
+
+def realspace_hvp(ctx, *, atom_begin, atom_count, positions, charges, amp, bw2, norm_factor, remove_self,
+                  charge_neutral_lambda, dir_q, dir_r, dir_amp, dir_bw2, out_q, out_r, out_amp, out_bw2,
+                  stream=None, **_unused):
+    """sog_realspace_hvp on a direct-solver context (non-periodic frames)."""
+    _require_cuda(positions)
+    nf = len(atom_begin)
+    ab, ac = _host_i64(atom_begin), _host_i64(atom_count)
+    args = RealspaceArgs()
+    args.nframes = nf
+    args.atom_begin = ctypes.cast(ab, _c_i64p)
+    args.atom_count = ctypes.cast(ac, _c_i64p)
+    args.nchannels = charges.shape[1]
+    args.positions, args.charges = _ptr(positions), _ptr(charges)
+    args.n_gauss = amp.numel()
+    args.amp, args.bw2 = _ptr(amp), _ptr(bw2)
+    args.norm_factor = float(norm_factor)
+    args.remove_self = int(remove_self)
+    args.charge_neutral_lambda = float(charge_neutral_lambda or 0.0)
+    h = _hvp_args(dir_q, dir_r, dir_amp, dir_bw2, out_q, out_r, out_amp, out_bw2)
+    if stream is None:
+        stream = torch.cuda.current_stream(positions.device).cuda_stream
+    check(load().sog_realspace_hvp(ctx, ctypes.byref(args), ctypes.byref(h), ctypes.c_void_p(stream)),
+          "sog_realspace_hvp")

@@ -410,7 +410,7 @@ struct RsLayout {
   int64_t natoms_end = 0;
 };
 
-int rs_layout(const sog_realspace_args *a, int sm_count, RsLayout &L) {
+int rs_layout(const sog_realspace_args *a, int sm_count, RsLayout &L, bool allow_split = true) {
   const int nf = a->nframes;
   L.frames.resize(nf);
   int64_t itiles = 0;
@@ -429,7 +429,7 @@ int rs_layout(const sog_realspace_args *a, int sm_count, RsLayout &L) {
     F.atom_begin = a->atom_begin[f];
     F.natoms = n;
     const int64_t cap = std::max<int64_t>(1, n / kRsChunkMin);
-    int ns = (int)std::min<int64_t>(std::min<int64_t>(want, cap), kRsMaxSplit);
+    int ns = allow_split ? (int)std::min<int64_t>(std::min<int64_t>(want, cap), kRsMaxSplit) : 1;
     int chunk = n;
     if (ns > 1) {
       chunk = (n + ns - 1) / ns;
@@ -536,6 +536,360 @@ int realspace_impl(sog_direct *d, const sog_realspace_args *a, cudaStream_t st) 
   return SOG_OK;
 }
 
+
+// ==========================================================================
+// Hessian-vector products (double backward) of the pair sum.
+// With Q_ij = q_i . q_j, u = r_i - r_j, s = |u|^2, K(s) = sum_m amp_m e_m,
+// e_m = exp(-s / 2 bw2_m), K1 = dK/ds, K2 = d2K/ds2, and a direction (a_i on
+// the charges, b_i on the positions, c on (amp, bw2)):
+//   ds = 2 u.(b_i - b_j),  dK = sum_m c . dK/d(amp_m, bw2_m),  dK1 = d(dK)/ds,
+//   (H d)_{q_ic} = norm sum_j [a_jc K + q_jc (K1 ds + dK)]
+//   (H d)_{r_i}  = norm sum_j [(a_i.q_j + q_i.a_j) 2u K1
+//                             + Q_ij (2u K2 ds + 2 K1 (b_i - b_j) + 2u dK1)]
+//   (H d)_{theta_m} = norm/2 sum_{i != j} [(a_i.q_j + q_i.a_j) dK/dtheta_m
+//                                          + Q_ij (dK1/dtheta_m ds + d(dK)/dtheta_m)]
+// plus the self term (remove_self = 0) and the neutrality penalty, which
+// depend on the charges and amp only.
+// ==========================================================================
+template <typename T>
+struct RsHvp {
+  const void *dq, *dr, *damp, *dbw2;
+  void *oq, *orr, *oamp, *obw2;
+};
+
+template <typename T>
+__device__ __forceinline__ double rs_dir(const void *p, int64_t i) {
+  return p ? (double)static_cast<const T *>(p)[i] : 0.0;
+}
+
+template <typename T, int NCH>
+__global__ void __launch_bounds__(kRsThreads, 1) k_rs_hvp_pairs(RsArgs<T> a, RsHvp<T> h) {
+  __shared__ double s_nh[kMaxGauss], s_a[kMaxGauss], s_ib[kMaxGauss], s_ca[kMaxGauss], s_cb[kMaxGauss];
+  __shared__ union {
+    struct {
+      double x[kRsStage], y[kRsStage], z[kRsStage], bx[kRsStage], by[kRsStage], bz[kRsStage];
+      double q[NCH][kRsStage], d[NCH][kRsStage];
+    } st;
+    double red[kRsLanes][kRsI][3 + NCH];
+  } sm;
+  const RsTile t = a.tiles[blockIdx.x];
+  const RsFrame fr = a.frames[t.frame];
+  for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
+    const double b = (double)a.bw2[m];
+    s_nh[m] = -0.5 / b;
+    s_a[m] = (double)a.amp[m];
+    s_ib[m] = 1.0 / b;
+    s_ca[m] = rs_dir<T>(h.damp, (int64_t)t.frame * a.M + m);
+    s_cb[m] = rs_dir<T>(h.dbw2, (int64_t)t.frame * a.M + m);
+  }
+  const int il = threadIdx.x & (kRsI - 1), jl = threadIdx.x / kRsI;
+  const int i = t.i0 + il;
+  const bool own = i < fr.natoms;
+  const int64_t ai = fr.atom_begin + (own ? i : 0);
+  const int nch = a.nch, M = a.M;
+  double ri[3] = {0, 0, 0}, bi[3] = {0, 0, 0}, qi[NCH], di[NCH];
+  if (own)
+    for (int c = 0; c < 3; ++c) {
+      ri[c] = (double)a.pos[ai * 3 + c];
+      bi[c] = rs_dir<T>(h.dr, ai * 3 + c);
+    }
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    qi[c] = (own && c < nch) ? (double)a.q[ai * nch + c] : 0.0;
+    di[c] = (own && c < nch) ? rs_dir<T>(h.dq, ai * nch + c) : 0.0;
+  }
+  double acc[3 + NCH];
+#pragma unroll
+  for (int w = 0; w < 3 + NCH; ++w) acc[w] = 0.0;
+  for (int jb = t.j0; jb < t.j1; jb += kRsStage) {
+    __syncthreads();
+    const int jj = jb + threadIdx.x;
+    if (jj < t.j1) {
+      const int64_t aj = fr.atom_begin + jj;
+      sm.st.x[threadIdx.x] = (double)a.pos[aj * 3 + 0];
+      sm.st.y[threadIdx.x] = (double)a.pos[aj * 3 + 1];
+      sm.st.z[threadIdx.x] = (double)a.pos[aj * 3 + 2];
+      sm.st.bx[threadIdx.x] = rs_dir<T>(h.dr, aj * 3 + 0);
+      sm.st.by[threadIdx.x] = rs_dir<T>(h.dr, aj * 3 + 1);
+      sm.st.bz[threadIdx.x] = rs_dir<T>(h.dr, aj * 3 + 2);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+        if (c < nch) {
+          sm.st.q[c][threadIdx.x] = (double)a.q[aj * nch + c];
+          sm.st.d[c][threadIdx.x] = rs_dir<T>(h.dq, aj * nch + c);
+        }
+    }
+    __syncthreads();
+    const int cnt = min(kRsStage, t.j1 - jb);
+    if (!own) continue;
+    for (int k = jl; k < cnt; k += kRsLanes) {
+      if (jb + k == i) continue;
+      const double ux = ri[0] - sm.st.x[k], uy = ri[1] - sm.st.y[k], uz = ri[2] - sm.st.z[k];
+      const double dbx = bi[0] - sm.st.bx[k], dby = bi[1] - sm.st.by[k], dbz = bi[2] - sm.st.bz[k];
+      const double s2 = ux * ux + uy * uy + uz * uz;
+      const double ds = 2.0 * (ux * dbx + uy * dby + uz * dbz);
+      double K = 0, K1 = 0, K2 = 0, dK = 0, dK1 = 0;
+      for (int m = 0; m < M; ++m) {
+        const double e = exp(s2 * s_nh[m]);
+        const double ib = s_ib[m], am = s_a[m];
+        K += am * e;
+        K1 += -0.5 * ib * am * e;
+        K2 += 0.25 * ib * ib * am * e;
+        dK += (s_ca[m] + s_cb[m] * am * 0.5 * s2 * ib * ib) * e;
+        dK1 += (-0.5 * ib * s_ca[m] + s_cb[m] * am * (0.5 * ib * ib - 0.25 * s2 * ib * ib * ib)) * e;
+      }
+      double Q = 0.0, AQ = 0.0;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+        if (c < nch) {
+          const double qj = sm.st.q[c][k], dj = sm.st.d[c][k];
+          Q += qi[c] * qj;
+          AQ += di[c] * qj + qi[c] * dj;
+          acc[3 + c] += dj * K + qj * (K1 * ds + dK);
+        }
+      const double su = 2.0 * (AQ * K1 + Q * (K2 * ds + dK1));
+      const double sb = 2.0 * Q * K1;
+      acc[0] += su * ux + sb * dbx;
+      acc[1] += su * uy + sb * dby;
+      acc[2] += su * uz + sb * dbz;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < 3 + NCH; ++w)
+    if (w < 3 + nch) sm.red[jl][il][w] = acc[w];
+  __syncthreads();
+  if (jl != 0 || !own) return;
+  double tot[3 + NCH];
+#pragma unroll
+  for (int w = 0; w < 3 + NCH; ++w) tot[w] = 0.0;
+  for (int l = 0; l < kRsLanes; ++l)
+#pragma unroll
+    for (int w = 0; w < 3 + NCH; ++w)
+      if (w < 3 + nch) tot[w] += sm.red[l][il][w];
+  T *orr = static_cast<T *>(h.orr), *oq = static_cast<T *>(h.oq);
+  for (int d = 0; d < 3; ++d) orr[ai * 3 + d] = (T)(a.norm * tot[d]);
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+    if (c < nch) oq[ai * nch + c] = (T)(a.norm * tot[3 + c]);
+}
+
+// Parameter rows per tile and chunk of 8 Gaussian terms (ordered pairs; the
+// frames kernel halves them).
+template <typename T, int NCH>
+__global__ void __launch_bounds__(kRsThreads, 2) k_rs_hvp_grad(RsArgs<T> a, RsHvp<T> h, double *gpart) {
+  __shared__ double s_nh[kMaxGauss], s_a[kMaxGauss], s_ib[kMaxGauss], s_ca[kMaxGauss], s_cb[kMaxGauss];
+  __shared__ struct {
+    double x[kRsStage], y[kRsStage], z[kRsStage], bx[kRsStage], by[kRsStage], bz[kRsStage];
+    double q[NCH][kRsStage], d[NCH][kRsStage];
+  } st;
+  __shared__ double red[kRsThreads / 32][2 * kRsMChunk];
+  const RsTile t = a.tiles[blockIdx.x];
+  const RsFrame fr = a.frames[t.frame];
+  for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
+    const double b = (double)a.bw2[m];
+    s_nh[m] = -0.5 / b;
+    s_a[m] = (double)a.amp[m];
+    s_ib[m] = 1.0 / b;
+    s_ca[m] = rs_dir<T>(h.damp, (int64_t)t.frame * a.M + m);
+    s_cb[m] = rs_dir<T>(h.dbw2, (int64_t)t.frame * a.M + m);
+  }
+  const int m0 = blockIdx.y * kRsMChunk;
+  const int mc = min(kRsMChunk, a.M - m0);
+  const int il = threadIdx.x & (kRsI - 1), jl = threadIdx.x / kRsI;
+  const int i = t.i0 + il;
+  const bool own = i < fr.natoms;
+  const int64_t ai = fr.atom_begin + (own ? i : 0);
+  const int nch = a.nch;
+  double ri[3] = {0, 0, 0}, bi[3] = {0, 0, 0}, qi[NCH], di[NCH];
+  if (own)
+    for (int c = 0; c < 3; ++c) {
+      ri[c] = (double)a.pos[ai * 3 + c];
+      bi[c] = rs_dir<T>(h.dr, ai * 3 + c);
+    }
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    qi[c] = (own && c < nch) ? (double)a.q[ai * nch + c] : 0.0;
+    di[c] = (own && c < nch) ? rs_dir<T>(h.dq, ai * nch + c) : 0.0;
+  }
+  double v[2 * kRsMChunk];
+#pragma unroll
+  for (int k = 0; k < 2 * kRsMChunk; ++k) v[k] = 0.0;
+  for (int jb = t.j0; jb < t.j1; jb += kRsStage) {
+    __syncthreads();
+    const int jj = jb + threadIdx.x;
+    if (jj < t.j1) {
+      const int64_t aj = fr.atom_begin + jj;
+      st.x[threadIdx.x] = (double)a.pos[aj * 3 + 0];
+      st.y[threadIdx.x] = (double)a.pos[aj * 3 + 1];
+      st.z[threadIdx.x] = (double)a.pos[aj * 3 + 2];
+      st.bx[threadIdx.x] = rs_dir<T>(h.dr, aj * 3 + 0);
+      st.by[threadIdx.x] = rs_dir<T>(h.dr, aj * 3 + 1);
+      st.bz[threadIdx.x] = rs_dir<T>(h.dr, aj * 3 + 2);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+        if (c < nch) {
+          st.q[c][threadIdx.x] = (double)a.q[aj * nch + c];
+          st.d[c][threadIdx.x] = rs_dir<T>(h.dq, aj * nch + c);
+        }
+    }
+    __syncthreads();
+    const int cnt = min(kRsStage, t.j1 - jb);
+    if (!own) continue;
+    for (int k = jl; k < cnt; k += kRsLanes) {
+      if (jb + k == i) continue;
+      const double ux = ri[0] - st.x[k], uy = ri[1] - st.y[k], uz = ri[2] - st.z[k];
+      const double s2 = ux * ux + uy * uy + uz * uz;
+      const double ds = 2.0 * (ux * (bi[0] - st.bx[k]) + uy * (bi[1] - st.by[k]) + uz * (bi[2] - st.bz[k]));
+      double Q = 0.0, AQ = 0.0;
+#pragma unroll
+      for (int c = 0; c < NCH; ++c)
+        if (c < nch) {
+          Q += qi[c] * st.q[c][k];
+          AQ += di[c] * st.q[c][k] + qi[c] * st.d[c][k];
+        }
+#pragma unroll
+      for (int m = 0; m < kRsMChunk; ++m)
+        if (m < mc) {
+          const int mm = m0 + m;
+          const double e = exp(s2 * s_nh[mm]), ib = s_ib[mm], am = s_a[mm];
+          const double g = 0.5 * s2 * ib * ib * e;            // dK/dbw2_m / amp_m
+          v[m] += AQ * e + Q * (-0.5 * ib * e * ds + s_cb[mm] * g);
+          v[kRsMChunk + m] += AQ * am * g + Q * (am * e * (0.5 * ib * ib - 0.25 * s2 * ib * ib * ib) * ds +
+                                                 s_ca[mm] * g +
+                                                 s_cb[mm] * am * e * s2 * (0.25 * s2 * ib * ib * ib * ib - ib * ib * ib));
+        }
+    }
+  }
+  block_sum<2 * kRsMChunk>(v, red);
+  if (threadIdx.x == 0) {
+    double *o = gpart + ((int64_t)blockIdx.x * gridDim.y + blockIdx.y) * (2 * kRsMChunk);
+    for (int k = 0; k < 2 * kRsMChunk; ++k) o[k] = v[k];
+  }
+}
+
+// One block per frame: parameter rows, and the self / penalty terms of the charge rows.
+template <typename T>
+__global__ void __launch_bounds__(256) k_rs_hvp_frames(RsArgs<T> a, RsHvp<T> h, const double *gpart, int nmc,
+                                                      double lambda) {
+  __shared__ double sh[8][1 + kRsCh];
+  __shared__ double s_sum[1 + kRsCh];
+  const int f = blockIdx.x;
+  const RsFrame fr = a.frames[f];
+  const int nch = a.nch, M = a.M;
+  double v[1 + kRsCh];   // sum_i q_i . a_i, sum_i a_ic
+#pragma unroll
+  for (int k = 0; k < 1 + kRsCh; ++k) v[k] = 0.0;
+  for (int i = threadIdx.x; i < fr.natoms; i += blockDim.x) {
+    const int64_t ai = fr.atom_begin + i;
+#pragma unroll
+    for (int c = 0; c < kRsCh; ++c)
+      if (c < nch) {
+        const double dc = rs_dir<T>(h.dq, ai * nch + c);
+        v[0] += (double)a.q[ai * nch + c] * dc;
+        v[1 + c] += dc;
+      }
+  }
+  block_sum<1 + kRsCh>(v, sh);
+  if (threadIdx.x == 0)
+    for (int k = 0; k < 1 + kRsCh; ++k) s_sum[k] = v[k];
+  __syncthreads();
+  const double self = a.remove_self ? 0.0 : 1.0;
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    const int mc = m / kRsMChunk, mm = m % kRsMChunk;
+    double ga = 0.0, gb = 0.0;
+    for (int t = 0; t < fr.ntiles; ++t) {
+      const double *o = gpart + ((int64_t)(fr.tile_begin + t) * nmc + mc) * (2 * kRsMChunk);
+      ga += o[mm];
+      gb += o[kRsMChunk + mm];
+    }
+    ga = a.norm * (0.5 * ga + self * s_sum[0]);
+    gb = a.norm * 0.5 * gb;
+    static_cast<T *>(h.oamp)[(int64_t)f * M + m] = (T)ga;
+    static_cast<T *>(h.obw2)[(int64_t)f * M + m] = (T)gb;
+  }
+  double asum = 0.0, dA = 0.0;
+  for (int m = 0; m < M; ++m) {
+    asum += (double)a.amp[m];
+    dA += rs_dir<T>(h.damp, (int64_t)f * M + m);
+  }
+  const bool pen = lambda > 0.0 && fr.natoms > 0;
+  T *oq = static_cast<T *>(h.oq);
+  for (int i = threadIdx.x; i < fr.natoms; i += blockDim.x) {
+    const int64_t ai = fr.atom_begin + i;
+    for (int c = 0; c < nch; ++c) {
+      const int64_t o = ai * nch + c;
+      double val = (double)oq[o];
+      val += a.norm * self * (rs_dir<T>(h.dq, o) * asum + (double)a.q[o] * dA);
+      if (pen) val += 2.0 * lambda * s_sum[1 + c] / ((double)fr.natoms * fr.natoms);
+      oq[o] = (T)val;
+    }
+  }
+}
+
+template <typename T>
+int realspace_hvp_impl(sog_direct *d, const sog_realspace_args *a, const sog_hvp_args *hv, cudaStream_t st) {
+  const int nf = a->nframes, nch = a->nchannels, M = a->n_gauss;
+  RsLayout L;
+  int rc = rs_layout(a, 148, L, false);
+  if (rc != SOG_OK) return rc;
+  const size_t bf = sizeof(RsFrame) * nf, bt = sizeof(RsTile) * L.tiles.size();
+  const size_t up_bytes = bf + bt;
+  if ((rc = d->up.reserve(up_bytes)) != SOG_OK) return rc;
+  if ((rc = d->up.wait()) != SOG_OK) return rc;
+  std::memcpy(d->up.p, L.frames.data(), bf);
+  if (bt) std::memcpy((char *)d->up.p + bf, L.tiles.data(), bt);
+  const int nmc = (M + kRsMChunk - 1) / kRsMChunk;
+  if (d->frames_host_dev.reserve(up_bytes) ||
+      d->hpart.reserve(sizeof(double) * 2 * kRsMChunk * std::max<size_t>(1, L.tiles.size()) * nmc))
+    return fail(SOG_ERR_NOMEM, "device allocation failed (real-space HVP)");
+  SOG_CUDA_TRY(cudaMemcpyAsync(d->frames_host_dev.p, d->up.p, up_bytes, cudaMemcpyHostToDevice, st));
+  SOG_CUDA_TRY(cudaEventRecord(d->up.done, st));
+  d->up.pending = true;
+  RsArgs<T> ra;
+  std::memset(&ra, 0, sizeof(ra));
+  ra.frames = d->frames_host_dev.as<RsFrame>();
+  ra.tiles = reinterpret_cast<const RsTile *>((const char *)d->frames_host_dev.p + bf);
+  ra.pos = (const T *)a->positions;
+  ra.q = (const T *)a->charges;
+  ra.amp = (const T *)a->amp;
+  ra.bw2 = (const T *)a->bw2;
+  ra.nch = nch;
+  ra.M = M;
+  ra.norm = a->norm_factor;
+  ra.remove_self = a->remove_self;
+  RsHvp<T> h;
+  h.dq = hv->dir_q;
+  h.dr = hv->dir_r;
+  h.damp = hv->dir_amp;
+  h.dbw2 = hv->dir_bw2;
+  h.oq = hv->out_q;
+  h.orr = hv->out_r;
+  h.oamp = hv->out_amp;
+  h.obw2 = hv->out_bw2;
+  Tracer *tr = &d->tr;
+  tr->begin(st);
+  const unsigned ntiles = (unsigned)L.tiles.size();
+  double *gp = d->hpart.as<double>();
+  if (ntiles) {
+    if (nch == 1) k_rs_hvp_pairs<T, 1><<<ntiles, kRsThreads, 0, st>>>(ra, h);
+    else if (nch == 2) k_rs_hvp_pairs<T, 2><<<ntiles, kRsThreads, 0, st>>>(ra, h);
+    else if (nch <= 4) k_rs_hvp_pairs<T, 4><<<ntiles, kRsThreads, 0, st>>>(ra, h);
+    else k_rs_hvp_pairs<T, kRsCh><<<ntiles, kRsThreads, 0, st>>>(ra, h);
+    after(tr, st, "rs_hvp_pairs");
+    const dim3 g(ntiles, nmc);
+    if (nch == 1) k_rs_hvp_grad<T, 1><<<g, kRsThreads, 0, st>>>(ra, h, gp);
+    else if (nch == 2) k_rs_hvp_grad<T, 2><<<g, kRsThreads, 0, st>>>(ra, h, gp);
+    else if (nch <= 4) k_rs_hvp_grad<T, 4><<<g, kRsThreads, 0, st>>>(ra, h, gp);
+    else k_rs_hvp_grad<T, kRsCh><<<g, kRsThreads, 0, st>>>(ra, h, gp);
+    after(tr, st, "rs_hvp_grad");
+  }
+  const double lam = a->charge_neutral_lambda > 0.0 ? a->charge_neutral_lambda : 0.0;
+  k_rs_hvp_frames<T><<<nf, 256, 0, st>>>(ra, h, gp, nmc, lam);
+  after(tr, st, "rs_hvp_frames");
+  SOG_CUDA_TRY(cudaGetLastError());
+  return SOG_OK;
+}
 }  // namespace
 }  // namespace sogb
 
@@ -553,4 +907,19 @@ extern "C" int sog_realspace_forward(sog_direct *d, const sog_realspace_args *a,
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (d->dtype == SOG_DTYPE_F64) return realspace_impl<double>(d, a, st);
   return realspace_impl<float>(d, a, st);
+}
+
+extern "C" int sog_realspace_hvp(sog_direct *d, const sog_realspace_args *a, const sog_hvp_args *h, void *stream) {
+  if (!d || !a || !h) return fail(SOG_ERR_INVALID, "null argument");
+  if (a->nframes <= 0) return SOG_OK;
+  if (!a->atom_begin || !a->atom_count || !a->positions || !a->charges || !a->amp || !a->bw2)
+    return fail(SOG_ERR_INVALID, "missing input array");
+  if (!h->out_q || !h->out_r || !h->out_amp || !h->out_bw2) return fail(SOG_ERR_INVALID, "missing HVP output array");
+  if (a->nchannels < 1 || a->nchannels > kRsCh)
+    return fail(SOG_ERR_UNSUPPORTED, "real-space pair sum supports 1..8 charge channels");
+  if (a->n_gauss < 1 || a->n_gauss > kMaxGauss) return fail(SOG_ERR_INVALID, "n_gauss must be in [1, 64]");
+  DeviceGuard dg(d->device);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (d->dtype == SOG_DTYPE_F64) return realspace_hvp_impl<double>(d, a, h, st);
+  return realspace_hvp_impl<float>(d, a, h, st);
 }

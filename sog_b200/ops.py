@@ -170,15 +170,15 @@ def run_hvp(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Tensor
     single = len(spec.buckets) == 1 and spec.buckets[0].frames == list(range(nf))
     for b in spec.buckets:
         kind = b.kind or spec.kind
-        if kind != "direct":
+        if kind not in ("direct", "realspace"):
             raise NotImplementedError(
-                "second derivatives (create_graph=True through the forces) are implemented for the "
-                "direct k-sum; the mesh solvers and the real-space pair sum raise here")
+                "second derivatives (create_graph=True through the forces or dE/dq) are implemented "
+                "for the direct k-sum and the real-space pair sum; the mesh solvers raise here")
         if single:
             cells_b, da_b, db_b, oa_b, ob_b = spec.cells, damp, dbw2, out_a, out_b
         else:
             idx = b.frame_index(dev)
-            cells_b = spec.cells.index_select(0, idx).contiguous()
+            cells_b = None if spec.cells is None else spec.cells.index_select(0, idx).contiguous()
             da_b = None if damp is None else damp.index_select(0, idx).contiguous()
             db_b = None if dbw2 is None else dbw2.index_select(0, idx).contiguous()
             oa_b = torch.zeros(len(b.frames), M, dtype=dt, device=dev)
@@ -186,13 +186,16 @@ def run_hvp(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Tensor
         h = b.host()
         ctx = _lib.direct_ctx(dev.index if dev.index is not None else torch.cuda.current_device(),
                               _lib.dtype_code(dt))
-        _lib.direct_hvp(ctx, atom_begin=h["atom_begin"], atom_count=h["atom_count"], nk=h["nk"],
-                        k_sq_max=h["k_sq_max"], positions=r, charges=q, cells=cells_b, amp=amp, bw2=bw2,
-                        norm_factor=spec.norm_factor, self_coeff=spec.self_coeff,
-                        remove_self=spec.remove_self, k0_correction=spec.k0_correction,
-                        charge_neutral_lambda=spec.charge_neutral_lambda, dir_q=dq, dir_r=dr,
-                        dir_amp=da_b, dir_bw2=db_b, out_q=out_q, out_r=out_r, out_amp=oa_b,
-                        out_bw2=ob_b)
+        # each bucket's atoms get their rows written; the others keep theirs
+        common = dict(atom_begin=h["atom_begin"], atom_count=h["atom_count"], positions=r, charges=q,
+                      amp=amp, bw2=bw2, norm_factor=spec.norm_factor, remove_self=spec.remove_self,
+                      charge_neutral_lambda=spec.charge_neutral_lambda, dir_q=dq, dir_r=dr,
+                      dir_amp=da_b, dir_bw2=db_b, out_q=out_q, out_r=out_r, out_amp=oa_b, out_bw2=ob_b)
+        if kind == "realspace":
+            _lib.realspace_hvp(ctx, **common)
+        else:
+            _lib.direct_hvp(ctx, nk=h["nk"], k_sq_max=h["k_sq_max"], cells=cells_b,
+                            self_coeff=spec.self_coeff, k0_correction=spec.k0_correction, **common)
         if not single:
             out_a.index_copy_(0, idx, oa_b)
             out_b.index_copy_(0, idx, ob_b)

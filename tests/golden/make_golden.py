@@ -430,7 +430,9 @@ def run_hvp_case(name, r, q, cell, batch, sog_args=None, gauss_kwargs=None, seed
     Z = torch.randn(gq.shape, generator=gen, dtype=F64)
     loss = (U * F).sum() + (W * F * F).sum() + (Z * gq).sum() + (e * e_w).sum()
     loss.backward()
-    rec = dict(r=r.numpy(), q=q.numpy(), cell=cell.numpy(), batch=batch.numpy(),
+    rec = dict(r=r.numpy(), q=q.numpy(), has_cell=int(cell is not None),
+               cell=np.zeros((0, 3, 3)) if cell is None else cell.numpy(),
+               batch=np.zeros(r.shape[0], dtype=np.int64) if batch is None else batch.numpy(),
                amp=g.amp.detach().to(F64).numpy(), bw2=g.bandwidth.detach().to(F64).numpy(),
                amp_dtype=str(g.amp.dtype), self_coeff=float(g.self_coeff),
                remove_self=int(g.remove_self_interaction),
@@ -443,6 +445,39 @@ def run_hvp_case(name, r, q, cell, batch, sog_args=None, gauss_kwargs=None, seed
         rec["grad_bw2"] = g.bandwidth.grad.to(F64).numpy()
     np.savez_compressed(os.path.join(OUT, f"{name}.npz"), **rec)
     print(name, float(loss))
+
+
+def hvp_realspace_cases():
+    """Second-derivative fixtures of the real-space pair sum (cell=None and a
+    singular cell next to a periodic frame); own generator."""
+    gen = torch.Generator().manual_seed(2028)
+    n = 24
+    r = torch.rand(n, 3, generator=gen, dtype=F64) * 7.0
+    q = torch.rand(n, generator=gen, dtype=F64) - 0.5
+    run_hvp_case("hvp_realspace_molecule", r, q, None, None,
+                 gauss_kwargs=dict(n_dl=2.0, amp=torch.tensor([0.7, 1.1, 1.4], dtype=F64),
+                                   bandwidth=torch.tensor([1.3, 2.1, 3.4], dtype=F64),
+                                   kernel_param_mode="internal", trainable=True), seed=5)
+    nloc = [9, 1, 13]
+    batch = torch.cat([torch.full((k,), i, dtype=torch.int64) for i, k in enumerate(nloc)])
+    batch = batch[torch.randperm(batch.numel(), generator=gen)]
+    nt = sum(nloc)
+    r = torch.randn(nt, 3, generator=gen, dtype=F64) * 2.5
+    q = torch.rand(nt, 2, generator=gen, dtype=F64) - 0.5
+    amp4, bw4 = params_log(4, 1.2, 5.0)
+    run_hvp_case("hvp_realspace_batch_2ch_keepself", r, q, None, batch,
+                 gauss_kwargs=dict(n_dl=2.0, amp=amp4.clone(), bandwidth=bw4.clone(),
+                                   remove_self_interaction=False, charge_neutral_lambda=0.2,
+                                   trainable=True), seed=6)
+    na, nb = 14, 12
+    cells = torch.stack([torch.tensor([[9.0, 0.0, 0.0], [0.8, 8.5, 0.0], [0.4, 0.6, 8.2]], dtype=F64),
+                         torch.zeros(3, 3, dtype=F64)])
+    r = torch.cat([torch.rand(na, 3, generator=gen, dtype=F64) @ cells[0],
+                   torch.randn(nb, 3, generator=gen, dtype=F64) * 2.0])
+    q = torch.rand(na + nb, generator=gen, dtype=F64) - 0.5
+    batch = torch.cat([torch.zeros(na, dtype=torch.int64), torch.ones(nb, dtype=torch.int64)])
+    run_hvp_case("hvp_realspace_mixed_cells", r, q, cells, batch,
+                 gauss_kwargs=dict(n_dl=2.0, amp=amp4.clone(), bandwidth=bw4.clone(), trainable=True), seed=7)
 
 
 def hvp_cases():
@@ -485,6 +520,7 @@ if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     if sys.argv[1:] == ["hvp"]:
         hvp_cases()
+        hvp_realspace_cases()
     elif sys.argv[1:] == ["cfg3"]:
         cfg3_case()
     elif sys.argv[1:] == ["cubes2"]:

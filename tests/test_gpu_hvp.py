@@ -5,7 +5,9 @@ charge gradients dE/dq are built with create_graph=True and a loss on them is
 backpropagated to the charges, positions and kernel parameters.  The
 reference gets these derivatives from torch autograd through its direct
 k-sum (src/sog/module/gaussian.py:1180-1337); the fixtures hold its values
-for the loss  sum(U F) + sum(W F^2) + sum(Z dE/dq) + sum(e_w E).
+for the loss  sum(U F) + sum(W F^2) + sum(Z dE/dq) + sum(e_w E), and
+likewise through its real-space pair sum for frames without a periodic cell
+(gaussian.py:822-845).
 
 Tolerances: fp64 gradients max-abs 1e-9 (relative 1e-10 for the parameter
 gradients); parameters created in fp32 by the reference (its defaults) carry
@@ -22,7 +24,8 @@ from tests._cases import direct_n_dl, load
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 F64 = torch.float64
-HVP_CASES = ["hvp_direct_quickstart", "hvp_direct_triclinic_2ch", "hvp_direct_k0_penalty", "hvp_direct_rcut"]
+HVP_CASES = ["hvp_direct_quickstart", "hvp_direct_triclinic_2ch", "hvp_direct_k0_penalty", "hvp_direct_rcut",
+             "hvp_realspace_molecule", "hvp_realspace_batch_2ch_keepself", "hvp_realspace_mixed_cells"]
 
 
 def _t(a, dtype=F64):
@@ -44,7 +47,8 @@ def _model(c):
 
 
 def _loss(g, r, q, c):
-    e = g(q=q, r=r, cell=_t(c["cell"]), batch=_t(c["batch"], torch.long))
+    cell = _t(c["cell"]) if int(c.get("has_cell", 1)) else None
+    e = g(q=q, r=r, cell=cell, batch=_t(c["batch"], torch.long))
     e_w = _t(c["e_w"])
     gr, gq = torch.autograd.grad((e * e_w).sum(), (r, q), create_graph=True)
     F = -gr
@@ -52,7 +56,7 @@ def _loss(g, r, q, c):
 
 
 @pytest.mark.parametrize("name", HVP_CASES)
-def test_direct_second_derivatives_match_reference(name):
+def test_second_derivatives_match_reference(name):
     c = load(name)
     g = _model(c)
     r = _t(c["r"]).requires_grad_(True)
@@ -89,6 +93,40 @@ def test_direct_hvp_matches_finite_differences_of_first_derivatives():
         g = Gaussian(n_dl=1.5, amp=_t(amp0 + eps * da), bandwidth=_t(bw0 + eps * db),
                      kernel_param_mode="internal", charge_neutral_lambda=0.2, trainable=True).to(DEV)
         e = (g(q=q, r=r, cell=_t(cells), batch=batch) * ew).sum()
+        out = torch.autograd.grad(e, (r, q, g.amp, g.bandwidth), create_graph=create_graph)
+        return out, (r, q, g)
+
+    (gr, gq, ga, gb), (r, q, g) = grads(0.0, create_graph=True)
+    dot = (gr * _t(dr)).sum() + (gq * _t(dq)).sum() + (ga * _t(da)).sum() + (gb * _t(db)).sum()
+    hr, hq, ha, hb = torch.autograd.grad(dot, (r, q, g.amp, g.bandwidth))
+    h = 1e-4
+    (pr, pq, pa, pb), _ = grads(h)
+    (mr, mq, ma, mb), _ = grads(-h)
+    for an, p, m in ((hr, pr, mr), (hq, pq, mq), (ha, pa, ma), (hb, pb, mb)):
+        fd = ((p - m) / (2 * h)).cpu().numpy()
+        assert _rel(an.cpu().numpy(), fd) < 1e-6
+
+
+def test_realspace_hvp_matches_finite_differences_of_first_derivatives():
+    """The pair-sum Hessian-vector product against central differences of the
+    GPU's own first derivatives (two molecules, two channels, self term kept)."""
+    rng = np.random.default_rng(10)
+    n0, n1 = 11, 17
+    r0 = rng.standard_normal((n0 + n1, 3)) * 2.0
+    q0 = rng.standard_normal((n0 + n1, 2)) * 0.5
+    batch = _t(np.repeat([0, 1], [n0, n1]), torch.long)
+    amp0, bw0 = np.array([0.6, 1.0, 1.3]), np.array([1.1, 2.4, 4.0])
+    dr, dq = rng.standard_normal(r0.shape), rng.standard_normal(q0.shape)
+    da, db = rng.standard_normal(3), rng.standard_normal(3)
+    ew = _t([1.0, 0.7])
+
+    def grads(eps, create_graph=False):
+        r = _t(r0 + eps * dr).requires_grad_(True)
+        q = _t(q0 + eps * dq).requires_grad_(True)
+        g = Gaussian(n_dl=1.5, amp=_t(amp0 + eps * da), bandwidth=_t(bw0 + eps * db),
+                     kernel_param_mode="internal", remove_self_interaction=False,
+                     charge_neutral_lambda=0.2, trainable=True).to(DEV)
+        e = (g(q=q, r=r, cell=None, batch=batch) * ew).sum()
         out = torch.autograd.grad(e, (r, q, g.amp, g.bandwidth), create_graph=create_graph)
         return out, (r, q, g)
 
