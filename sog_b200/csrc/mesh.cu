@@ -77,6 +77,13 @@ __host__ __device__ __forceinline__ uint32_t bin_row(const AtomGrid &ag, int bz,
 #ifndef SOG_SPREAD_MINB
 #define SOG_SPREAD_MINB 4
 #endif
+// 1: separable splines spread with one warp per 8^3 block (k_spread_blk)
+#ifndef SOG_SPREAD_BLK
+#define SOG_SPREAD_BLK 1
+#endif
+#ifndef SOG_SPREAD_BLK_MINB
+#define SOG_SPREAD_BLK_MINB 6
+#endif
 
 // Fractional coordinate along axis a (r @ cell^-1, then remainder 1.0) and the
 // anchor (first stencil node, wrapped) with the in-cell offset t
@@ -605,6 +612,160 @@ __global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? SOG_SPREAD_MINB : 2)
 #pragma unroll
     for (int z = 0; z < kTileZ; ++z)
       if (z < tzv) out[(int64_t)(z0 - a.zlo + z) * plane] = acc[z] * scale;
+  }
+}
+
+// ------------------------------------------------------------------------
+// spread, separable splines: one warp per 8 x 8 x 8 block of mesh points
+// ------------------------------------------------------------------------
+// A warp owns one block and writes each of its points once.  Its candidates
+// are the cell-sorted atoms of the (at most 3 x 3 x 3) bins that hold the
+// anchors able to reach the block; lane i takes candidate i of a chunk of 32,
+// evaluates its spline weights (fp64) at the block's 8 x, 8 y and 8 z
+// points (zero where the stencil does not reach), the relevant ones are
+// compacted in lane order, and every lane then adds them, in that order, to
+// its 2 x 8 points (x = lane % 8, y = lane / 8 and lane / 8 + 4, all z).  So
+// the summation order at every point is the fixed candidate order: bitwise
+// reproducible, no atomics, and no block-wide barriers (the warps of a CTA
+// are independent blocks).
+constexpr int kWarpsPerSpreadCta = 4;
+
+template <typename T, int P, typename TG>
+__global__ void __launch_bounds__(32 * kWarpsPerSpreadCta, SOG_SPREAD_BLK_MINB) k_spread_blk(SpreadArgs<T> a, int nbx, int nby,
+                                                                          int nbz, int64_t nblk) {
+  constexpr int kSeg = 18;
+  __shared__ TG s_w[kWarpsPerSpreadCta][32][24];   // per warp and lane: a candidate's x (times q), y, z weights
+  __shared__ uint32_t s_lo[kWarpsPerSpreadCta][kSeg], s_pre[kWarpsPerSpreadCta][kSeg + 1];
+  __shared__ int s_bl[kWarpsPerSpreadCta][3][4];
+  __shared__ int s_nb[kWarpsPerSpreadCta][3];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t blk = (int64_t)blockIdx.x * kWarpsPerSpreadCta + warp;
+  if (blk >= nblk) return;   // the whole warp
+  const AtomGrid &ag = a.ag;
+  const int64_t per_f = (int64_t)nbx * nby * nbz;
+  const int f = (int)(blk / per_f);
+  int64_t rem = blk - (int64_t)f * per_f;
+  const int bz = (int)(rem / ((int64_t)nbx * nby));
+  rem -= (int64_t)bz * nbx * nby;
+  const int by = (int)(rem / nbx), bx = (int)(rem - (int64_t)by * nbx);
+  const int x0 = bx * 8, y0 = by * 8, z0 = a.zlo + bz * 8;
+  const int xv = min(8, ag.nx - x0), yv = min(8, ag.ny - y0), zv = min(8, a.zlo + a.zcnt - z0);
+  // ---- segments of the sorted atom array holding the candidates ----
+  int nsg;
+  if (lane < 3) {
+    const int lo = (lane == 0 ? x0 : lane == 1 ? y0 : z0) - P + 1;
+    const int len = (lane == 0 ? xv : lane == 1 ? yv : zv) + P - 1;
+    const int n = lane == 0 ? ag.nx : lane == 1 ? ag.ny : ag.nz;
+    const int nb = lane == 0 ? ag.nbx : lane == 1 ? ag.nby : ag.nbz;
+    s_nb[warp][lane] = axis_bins(lo, len, n, nb, s_bl[warp][lane]);
+  }
+  __syncwarp();
+  const int nxl = s_nb[warp][0], nyl = s_nb[warp][1], nzl = s_nb[warp][2];
+  uint32_t lo2[2] = {0, 0}, cnt2[2] = {0, 0};
+  if (lane < nzl * nyl) {
+    const int iz = lane / nyl, iy = lane - iz * nyl;
+    const uint32_t row = (uint32_t)f * ag.bins_per_frame + bin_row(ag, s_bl[warp][2][iz], s_bl[warp][1][iy]);
+    int brk = nxl;   // x bins are ascending with at most one break
+    for (int i = 1; i < nxl; ++i)
+      if (brk == nxl && s_bl[warp][0][i] != s_bl[warp][0][i - 1] + 1) brk = i;
+    lo2[0] = a.bin_start[row + s_bl[warp][0][0]];
+    cnt2[0] = a.bin_start[row + s_bl[warp][0][brk - 1] + 1] - lo2[0];
+    if (brk < nxl) {
+      lo2[1] = a.bin_start[row + s_bl[warp][0][brk]];
+      cnt2[1] = a.bin_start[row + s_bl[warp][0][nxl - 1] + 1] - lo2[1];
+    }
+  }
+  {
+    const int ne = (cnt2[0] > 0) + (cnt2[1] > 0);
+    int eo = ne;
+    uint32_t co = cnt2[0] + cnt2[1];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int ue = __shfl_up_sync(0xffffffffu, eo, o);
+      const uint32_t uc = __shfl_up_sync(0xffffffffu, co, o);
+      if (lane >= o) { eo += ue; co += uc; }
+    }
+    int sg = eo - ne;
+    uint32_t pre = co - (cnt2[0] + cnt2[1]);
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      if (cnt2[h] > 0) {
+        s_lo[warp][sg] = lo2[h];
+        s_pre[warp][sg] = pre;
+        pre += cnt2[h];
+        ++sg;
+      }
+    if (lane == 31) s_pre[warp][eo] = co;
+    nsg = __shfl_sync(0xffffffffu, eo, 31);   // segments in all
+    __syncwarp();
+  }
+  const uint32_t ncand = s_pre[warp][nsg];
+  const int xl = lane & 7, yl0 = lane >> 3, yl1 = yl0 + 4;
+  TG acc0[8], acc1[8];
+#pragma unroll
+  for (int z = 0; z < 8; ++z) { acc0[z] = TG(0); acc1[z] = TG(0); }
+  for (uint32_t c0 = 0; c0 < ncand; c0 += 32) {
+    const uint32_t ci = c0 + lane;
+    bool rel = false;
+    TG *w = s_w[warp][lane];   // this lane's candidate: x weights (times q), y, z
+    if (ci < ncand) {
+      int lo = 0, hi = nsg - 1;
+      while (lo < hi) {   // last segment with s_pre <= ci
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_pre[warp][mid] <= ci) lo = mid; else hi = mid - 1;
+      }
+      const uint32_t sidx = s_lo[warp][lo] + (ci - s_pre[warp][lo]);
+      const int4 an = a.s_anchor[sidx];
+      const int anc[3] = {an.x, an.y, an.z};
+      const int base[3] = {x0, y0, z0}, lim[3] = {xv, yv, zv}, nn[3] = {ag.nx, ag.ny, ag.nz};
+      const double qv = (double)a.s_q[sidx];
+      bool has = true;
+#pragma unroll
+      for (int ax = 0; ax < 3; ++ax) {
+        double w1[P];
+        spline_w<double, P>(a.spline, (double)a.s_t[(int64_t)sidx * 3 + ax], w1, a.qc);
+        bool h = false;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int k = imod(base[ax] + i - anc[ax], nn[ax]);
+          double v = 0.0;
+#pragma unroll
+          for (int jj = 0; jj < P; ++jj) v = (k == jj) ? w1[jj] : v;
+          if (i >= lim[ax]) v = 0.0;
+          h |= (k < P && i < lim[ax]);
+          w[ax * 8 + i] = (TG)(ax == 0 ? v * qv : v);
+        }
+        has = has && h;
+      }
+      rel = has;
+    }
+    unsigned mask = __ballot_sync(0xffffffffu, rel);
+    __syncwarp();
+    while (mask) {   // the relevant candidates in lane order
+      const int j = __ffs(mask) - 1;
+      mask &= mask - 1u;
+      const TG *wj = s_w[warp][j];
+      const TG a0 = wj[xl] * wj[8 + yl0], a1 = wj[xl] * wj[8 + yl1];
+#pragma unroll
+      for (int z = 0; z < 8; ++z) {
+        const TG wzz = wj[16 + z];
+        acc0[z] += a0 * wzz;
+        acc1[z] += a1 * wzz;
+      }
+    }
+    __syncwarp();
+  }
+  const int64_t plane = (int64_t)ag.nx * ag.ny;
+  TG *out = static_cast<TG *>(a.rho) + (int64_t)f * plane * a.zcnt;
+  const TG scale = (TG)a.geom[f].scale;
+  if (xl < xv) {
+#pragma unroll
+    for (int z = 0; z < 8; ++z) {
+      if (z >= zv) break;
+      const int64_t zo = (int64_t)(z0 - a.zlo + z) * plane + x0 + xl;
+      if (yl0 < yv) out[zo + (int64_t)(y0 + yl0) * ag.nx] = acc0[z] * scale;
+      if (yl1 < yv) out[zo + (int64_t)(y0 + yl1) * ag.nx] = acc1[z] * scale;
+    }
   }
 }
 
@@ -2233,8 +2394,26 @@ inline unsigned green_zsplit(unsigned gblocks, int nf, int nz) {
   return (unsigned)gz;
 }
 
+// Separable splines: one warp per 8^3 block of mesh points (k_spread_blk).
+template <typename T, int P, typename TG>
+void launch_spread_blk(const SpreadArgs<T> &sa, int nframes, cudaStream_t st, Tracer *tr) {
+  const int nbx = (sa.ag.nx + 7) / 8, nby = (sa.ag.ny + 7) / 8, nbz = (sa.zcnt + 7) / 8;
+  const int64_t nblk = (int64_t)nbx * nby * nbz * nframes;
+  const unsigned grid = (unsigned)((nblk + kWarpsPerSpreadCta - 1) / kWarpsPerSpreadCta);
+  if (grid) k_spread_blk<T, P, TG><<<grid, 32 * kWarpsPerSpreadCta, 0, st>>>(sa, nbx, nby, nbz, nblk);
+  after(tr, st, "spread");
+}
+
 template <typename T, typename TG = T>
 void dispatch_spread(const SpreadArgs<T> &sa, int order, int nframes, cudaStream_t st, Tracer *tr) {
+  if (SOG_SPREAD_BLK && sa.spline != SOG_SPLINE_CUBES2) {
+    switch (order) {
+      case 4: launch_spread_blk<T, 4, TG>(sa, nframes, st, tr); break;
+      case 5: launch_spread_blk<T, 5, TG>(sa, nframes, st, tr); break;
+      default: launch_spread_blk<T, 6, TG>(sa, nframes, st, tr); break;
+    }
+    return;
+  }
   if (sa.spline == SOG_SPLINE_CUBES2) {
     if (order == 4) launch_spread<T, 4, 3, TG>(sa, nframes, st, tr);
     else launch_spread<T, 6, 4, TG>(sa, nframes, st, tr);
