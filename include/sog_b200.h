@@ -127,6 +127,12 @@ typedef struct sog_mesh_args {
   void *grad_amp;            /* [nframes,M] dE/damp                           */
   void *grad_bw2;            /* [nframes,M] dE/dbw2                           */
   void *virial;              /* [nframes,3,3] (cubes2_fft.py:874-921)          */
+  /* [N,3] the exact gradient dE/dr of the returned energy: the derivatives of
+   * the spline weights on the potential field, which is what torch autograd
+   * gives through the reference's QuadS spread (quads_fft.py:34-73); `forces`
+   * holds the ik-differentiated explicit forces of quads_fft.py:301-313.
+   * B-spline and QuadS meshes; single-device calls only. */
+  void *dedr;
 } sog_mesh_args;
 
 /* Energy (+ ik forces, dE/dq, dE/d(amp,bw2), virial) of every frame of the

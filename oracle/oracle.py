@@ -100,7 +100,7 @@ class _MeshIn(ctypes.Structure):
         ("self_coeff", ctypes.c_double),
         ("remove_self", ctypes.c_int), ("want_force", ctypes.c_int),
         ("want_pot", ctypes.c_int), ("want_param_grad", ctypes.c_int),
-        ("want_virial", ctypes.c_int),
+        ("want_virial", ctypes.c_int), ("want_dedr", ctypes.c_int),
     ]
 
 
@@ -108,7 +108,7 @@ class _MeshOut(ctypes.Structure):
     _fields_ = [
         ("energy", ctypes.c_double), ("diag_sum", ctypes.c_double),
         ("forces", _dp), ("potential", _dp), ("grad_amp", _dp), ("grad_bw2", _dp),
-        ("virial", ctypes.c_double * 9),
+        ("virial", ctypes.c_double * 9), ("dedr", _dp),
     ]
 
 
@@ -178,8 +178,11 @@ def mesh_solve(r, q, cell, amp, bw2, *, spline: int, order: int, nx: int, ny: in
                self_coeff: float = 0.0, remove_self: bool = True,
                want_force: bool = True, want_pot: bool = False,
                want_param_grad: bool = False, want_virial: bool = False,
-               alias_extent: int = 8, kconv: int = 0) -> Dict[str, np.ndarray]:
-    """One frame, one charge channel.  Energy excludes the k=0 correction."""
+               alias_extent: int = 8, kconv: int = 0, want_dedr: bool = False) -> Dict[str, np.ndarray]:
+    """One frame, one charge channel.  Energy excludes the k=0 correction.
+    want_dedr: the exact gradient of the mesh energy w.r.t. the positions
+    (derivatives of the spline weights, B-spline and QuadS), as autograd
+    through the reference's QuadS spread gives it."""
     r = _f64(r).reshape(-1, 3)
     q = _f64(q).reshape(-1)
     amp = _f64(amp).reshape(-1)
@@ -195,15 +198,18 @@ def mesh_solve(r, q, cell, amp, bw2, *, spline: int, order: int, nx: int, ny: in
     inp.k_sq_max, inp.norm_factor, inp.self_coeff = k_sq_max, norm_factor, self_coeff
     inp.remove_self, inp.want_force, inp.want_pot = int(remove_self), int(want_force), int(want_pot)
     inp.want_param_grad, inp.want_virial = int(want_param_grad), int(want_virial)
+    inp.want_dedr = int(want_dedr)
     f = np.zeros((n, 3)) if want_force else None
+    dedr = np.zeros((n, 3)) if want_dedr else None
     p = np.zeros(n) if want_pot else None
     ga = np.zeros(M) if want_param_grad else None
     gb = np.zeros(M) if want_param_grad else None
     out = _MeshOut()
     out.forces, out.potential, out.grad_amp, out.grad_bw2 = _ptr(f), _ptr(p), _ptr(ga), _ptr(gb)
+    out.dedr = _ptr(dedr)
     lib().orc_mesh_solve(ctypes.byref(inp), ctypes.byref(out))
     res = {"energy": out.energy, "diag_sum": out.diag_sum, "forces": f, "potential": p,
-           "grad_amp": ga, "grad_bw2": gb}
+           "grad_amp": ga, "grad_bw2": gb, "dedr": dedr}
     if want_virial:
         res["virial"] = np.array(out.virial[:]).reshape(3, 3)
     return res

@@ -65,6 +65,16 @@ void orc_bspline_weights(int n, double t, double *w) {
   }
 }
 
+/* d w[a] / dt of the order-n B-spline weights: the derivative of the
+ * cardinal B-spline, M_n'(x) = M_{n-1}(x) - M_{n-1}(x - 1), i.e.
+ * w_n'[a] = w_{n-1}[a-1] - w_{n-1}[a] at the same offset t (the exact
+ * derivative of the recurrence above). */
+void orc_bspline_dweights(int n, double t, double *dw) {
+  double w1[8];
+  orc_bspline_weights(n - 1, t, w1);
+  for (int a = 0; a < n; ++a) dw[a] = (a >= 1 ? w1[a - 1] : 0.0) - (a < n - 1 ? w1[a] : 0.0);
+}
+
 /* QuadS xi for order 4/6: quads_spline.py:12-13 (Table I). */
 double orc_quads_xi(int order) {
   return order == 4 ? 1.0 / sqrt(3.0) : 0.72879488;
@@ -132,6 +142,17 @@ void orc_quads_weights(int order, double t, double *w) {
     double v = 0.0, tp = 1.0;
     for (int p = 0; p < order; ++p) { v += coef[k * order + p] * tp; tp *= t; }
     w[k] = v;
+  }
+}
+
+/* d w[k] / dt of the QuadS weights (the derivative of the polynomials). */
+void orc_quads_dweights(int order, double t, double *dw) {
+  double coef[36];
+  orc_quads_coeffs(order, coef);
+  for (int k = 0; k < order; ++k) {
+    double v = 0.0, tp = 1.0;
+    for (int p = 1; p < order; ++p) { v += (double)p * coef[k * order + p] * tp; tp *= t; }
+    dw[k] = v;
   }
 }
 
@@ -513,6 +534,7 @@ typedef struct {
   const double *amp, *bw2;
   double k_sq_max, norm_factor, self_coeff;
   int remove_self, want_force, want_pot, want_param_grad, want_virial;
+  int want_dedr;       /* exact dE/dr of the mesh energy (spline-weight derivatives) */
 } orc_mesh_in;
 
 typedef struct {
@@ -523,6 +545,7 @@ typedef struct {
   double *grad_amp;  /* [M] or NULL */
   double *grad_bw2;  /* [M] or NULL */
   double virial[9];
+  double *dedr;      /* [N,3] exact dE/dr, or NULL (B-spline and QuadS) */
 } orc_mesh_out;
 
 static void inv3(const double *c, double *ci, double *det_out) {
@@ -803,7 +826,8 @@ int orc_mesh_solve(const orc_mesh_in *in, orc_mesh_out *out) {
   green_ctx g;
   setup_green(&g, in, ci);
   const int nf = in->want_force ? 3 : 0;
-  const int nfield = nf + (in->want_pot ? 1 : 0);
+  const int want_phi = in->want_pot || in->want_dedr;   /* the potential field */
+  const int nfield = nf + (want_phi ? 1 : 0);
   cplx *fields = nfield ? calloc(nh * nfield, sizeof(cplx)) : NULL;
   const double s2 = 1.0 / (N3 * N3);
 
@@ -853,7 +877,7 @@ int orc_mesh_solve(const orc_mesh_in *in, orc_mesh_out *out) {
               fields[a * nh + idx].im = k[a] * sre;
             }
           }
-          if (in->want_pot) {
+          if (want_phi) {
             fields[nf * nh + idx].re = gE * r.re / N3;
             fields[nf * nh + idx].im = gE * r.im / N3;
           }
@@ -927,6 +951,20 @@ int orc_mesh_solve(const orc_mesh_in *in, orc_mesh_out *out) {
         }
       } else {
       atom_stencil(in->spline, p, ci, in->r + 3 * i, nx, ny, nz, i0, wx, wy, wz);
+      double dw[3][8], g3[3] = {0, 0, 0};
+      if (in->want_dedr) {
+        /* derivative weights d w / d t_a along each axis at the same t */
+        const int n3[3] = {nx, ny, nz};
+        for (int a = 0; a < 3; ++a) {
+          double f = in->r[3 * i + 0] * ci[0 * 3 + a] + in->r[3 * i + 1] * ci[1 * 3 + a] +
+                     in->r[3 * i + 2] * ci[2 * 3 + a];
+          f = f - floor(f);
+          const double fx = f * (double)n3[a];
+          const double t = fx - floor(fx);
+          if (in->spline == ORC_QUADS) orc_quads_dweights(p, t, dw[a]);
+          else orc_bspline_dweights(p, t, dw[a]);
+        }
+      }
       for (int c = 0; c < p; ++c) {
         const int gz = (i0[2] + c) % nz;
         for (int b = 0; b < p; ++b) {
@@ -936,7 +974,22 @@ int orc_mesh_solve(const orc_mesh_in *in, orc_mesh_out *out) {
             const long idx = ((long)gz * ny + gy) * nx + gx;
             const double w = wx[a] * wy[b] * wz[c];
             for (int f = 0; f < nfield; ++f) accf[f] += w * grids[f * ng + idx];
+            if (in->want_dedr) {
+              const double phi = grids[nf * ng + idx];
+              g3[0] += dw[0][a] * wy[b] * wz[c] * phi;
+              g3[1] += wx[a] * dw[1][b] * wz[c] * phi;
+              g3[2] += wx[a] * wy[b] * dw[2][c] * phi;
+            }
           }
+        }
+      }
+      if (in->want_dedr) {
+        /* t_a = n_a (r . cell^-1)_a + const: d t_a / d r_b = n_a ci[b][a] */
+        const double n3d[3] = {(double)nx, (double)ny, (double)nz};
+        for (int b = 0; b < 3; ++b) {
+          double v = 0.0;
+          for (int a = 0; a < 3; ++a) v += n3d[a] * ci[b * 3 + a] * g3[a];
+          out->dedr[3 * i + b] = in->q[i] * v * in->norm_factor;
         }
       }
       }

@@ -42,7 +42,8 @@ class MeshArgs(ctypes.Structure):
                 ("bw2", _vp), ("norm_factor", ctypes.c_double), ("self_coeff", ctypes.c_double),
                 ("remove_self", ctypes.c_int), ("k0_correction", ctypes.c_int),
                 ("charge_neutral_lambda", ctypes.c_double), ("energy", _vp), ("forces", _vp),
-                ("potential", _vp), ("grad_amp", _vp), ("grad_bw2", _vp), ("virial", _vp)]
+                ("potential", _vp), ("grad_amp", _vp), ("grad_bw2", _vp), ("virial", _vp),
+                ("dedr", _vp)]
 
 
 class DirectArgs(ctypes.Structure):
@@ -333,7 +334,7 @@ def mesh_slab_forward(plan: "Plan", group, *, atom_begin, atom_count, k_sq_max, 
 def mesh_forward(plan: Plan, *, atom_begin, atom_count, k_sq_max, positions, charges, cells, amp,
                  bw2, norm_factor, self_coeff, remove_self, k0_correction, charge_neutral_lambda,
                  energy, forces=None, potential=None, grad_amp=None, grad_bw2=None, virial=None,
-                 stream=None):
+                 dedr=None, stream=None):
     """One C-ABI mesh call.  All tensors must be contiguous CUDA tensors of the
     plan dtype; outputs are written in place."""
     _require_cuda(positions)
@@ -353,6 +354,7 @@ def mesh_forward(plan: Plan, *, atom_begin, atom_count, k_sq_max, positions, cha
     args.charge_neutral_lambda = float(charge_neutral_lambda or 0.0)
     args.energy, args.forces, args.potential = _ptr(energy), _ptr(forces), _ptr(potential)
     args.grad_amp, args.grad_bw2, args.virial = _ptr(grad_amp), _ptr(grad_bw2), _ptr(virial)
+    args.dedr = _ptr(dedr)
     if stream is None:
         stream = torch.cuda.current_stream(positions.device).cuda_stream
     check(load().sog_mesh_forward(plan.handle, ctypes.byref(args), ctypes.c_void_p(stream)),

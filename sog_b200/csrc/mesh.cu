@@ -200,6 +200,27 @@ __device__ __forceinline__ void spline_w(int spline, T t, T *w, const QuadsCoef 
   }
 }
 
+// d w[k] / dt of the separable splines at offset t: the B-spline's
+// M_p' = M_{p-1}(x) - M_{p-1}(x - 1), i.e. w_p'[a] = w_{p-1}[a-1] - w_{p-1}[a],
+// and the QuadS polynomials' derivatives (quads_spline.py:69-158).
+template <int P>
+__device__ __forceinline__ void spline_dw(int spline, double t, double *dw, const QuadsCoef &qc) {
+  if (spline == SOG_SPLINE_QUADS) {
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      double v = 0.0, tp = 1.0;
+#pragma unroll
+      for (int p = 1; p < P; ++p) { v += (double)p * qc.c[k * P + p] * tp; tp *= t; }
+      dw[k] = v;
+    }
+  } else {
+    double w1[P - 1];
+    bspline_w<double, P - 1>(t, w1);
+#pragma unroll
+    for (int a = 0; a < P; ++a) dw[a] = (a >= 1 ? w1[a - 1] : 0.0) - (a < P - 1 ? w1[a] : 0.0);
+  }
+}
+
 // CubeS2 (cubes2_spline.py): every node weight is a sum of products of 1-D
 // polynomials of the three offsets, and summing the classes node by node
 // gives a sum of separable stencils over the P = order window
@@ -1822,6 +1843,9 @@ struct GatherArgs {
   // when set, the slot range is [*range_lo, *range_hi) read on the device
   // (the sorted-atom bin offsets of a z slab) and nslots bounds the grid
   const uint32_t *range_lo, *range_hi;
+  // exact dE/dr (k_gather_dedr): frame geometry and the [N,3] output
+  const FrameGeom *geom;
+  T *dedr;
 };
 
 // NT stencil terms as in k_spread (the weight of node (k, b, c) is
@@ -1886,6 +1910,64 @@ __global__ void __launch_bounds__(256, SOG_GATHER_MINB) k_gather(GatherArgs<T> a
     }
   }
   if (a.want_pot) a.pot_raw[atom * a.nch + a.channel] = acc[a.want_force ? 3 : 0];
+}
+
+// Exact gradient of the mesh energy w.r.t. the positions (separable
+// splines): the potential field (the last of the F interleaved fields)
+// gathered with the derivatives of the spline weights,
+//   dE/dr_i = q_i norm sum_g grad_r w_i(g) Phi(g),  d t_a / d r_b = n_a (cell^-1)_{ba},
+// the derivative of the energy the forward returns (as autograd through
+// quads_fft.py's spread gives it).  Summed over the channels (accumulate).
+template <typename T, int P>
+__global__ void __launch_bounds__(256) k_gather_dedr(GatherArgs<T> a) {
+  const int64_t si = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (si >= a.nslots) return;
+  const int64_t s = a.slot_lo + si;
+  const int4 an = a.s_anchor[s];
+  double w[3][P], dw[3][P];
+#pragma unroll
+  for (int ax = 0; ax < 3; ++ax) {
+    const double t = (double)a.s_t[s * 3 + ax];
+    spline_w<double, P>(a.spline, t, w[ax], a.qc);
+    spline_dw<P>(a.spline, t, dw[ax], a.qc);
+  }
+  const AtomGrid &ag = a.ag;
+  const int F = a.nfield;
+  const T *base = a.freal + (int64_t)an.w * F * a.ng + (F - 1);
+  double g3[3] = {0.0, 0.0, 0.0};
+#pragma unroll 1
+  for (int c = 0; c < P; ++c) {
+    int gz = an.z - a.zlo + c;
+    if (gz >= a.zwrap) gz -= a.zwrap;
+#pragma unroll
+    for (int b = 0; b < P; ++b) {
+      int gy = an.y + b;
+      if (gy >= ag.ny) gy -= ag.ny;
+      const int64_t row = ((int64_t)gz * ag.ny + gy) * ag.nx;
+      const double wyz = w[1][b] * w[2][c], dyz = dw[1][b] * w[2][c], ydz = w[1][b] * dw[2][c];
+#pragma unroll
+      for (int k = 0; k < P; ++k) {
+        int gx = an.x + k;
+        if (gx >= ag.nx) gx -= ag.nx;
+        const double phi = (double)base[(row + gx) * F];
+        g3[0] += dw[0][k] * wyz * phi;
+        g3[1] += w[0][k] * dyz * phi;
+        g3[2] += w[0][k] * ydz * phi;
+      }
+    }
+  }
+  const FrameGeom &g = a.geom[an.w];
+  const double n3[3] = {(double)ag.nx, (double)ag.ny, (double)ag.nz};
+  const int64_t atom = a.s_atom[s];
+  const double qn = (double)a.s_q[s] * a.norm;
+#pragma unroll
+  for (int b = 0; b < 3; ++b) {
+    double v = 0.0;
+#pragma unroll
+    for (int ax = 0; ax < 3; ++ax) v += n3[ax] * g.cinv[b * 3 + ax] * g3[ax];
+    v *= qn;
+    if (a.accumulate) a.dedr[atom * 3 + b] += (T)v; else a.dedr[atom * 3 + b] = (T)v;
+  }
 }
 
 // fp64 gather of the three force fields (single-term splines, even P):
@@ -2453,6 +2535,18 @@ void dispatch_gather(const GatherArgs<T> &ga, int order, cudaStream_t st, Tracer
   after(tr, st, "gather");
 }
 
+template <typename T>
+void dispatch_gather_dedr(const GatherArgs<T> &ga, int order, cudaStream_t st, Tracer *tr) {
+  const unsigned nb = nblocks(ga.nslots, 256);
+  if (nb == 0) return;
+  switch (order) {
+    case 4: k_gather_dedr<T, 4><<<nb, 256, 0, st>>>(ga); break;
+    case 5: k_gather_dedr<T, 5><<<nb, 256, 0, st>>>(ga); break;
+    default: k_gather_dedr<T, 6><<<nb, 256, 0, st>>>(ga); break;
+  }
+  after(tr, st, "gather_dedr");
+}
+
 // Frames, geometry, cell sort and charge sums of one call (shared by the
 // single-device and the slab paths).
 struct Prep {
@@ -2633,7 +2727,9 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   const bool want_pot = a->potential != nullptr;
   const bool want_grad = a->grad_amp != nullptr || a->grad_bw2 != nullptr;
   const bool want_vir = a->virial != nullptr;
-  const int nfield = (want_force ? 3 : 0) + (want_pot ? 1 : 0);
+  const bool want_dedr = a->dedr != nullptr;
+  const bool pot_field = want_pot || want_dedr;   // the exact gradient gathers the potential field
+  const int nfield = (want_force ? 3 : 0) + (pot_field ? 1 : 0);
   const unsigned ks_blocks = nblocks(nh, 256);
   // the fused z pass writes one partial per tile; the generic k-space kernel one per block
   const int64_t part_blocks = std::max<int64_t>(ks_blocks, (int64_t)ny * nxh);
@@ -2718,6 +2814,8 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   gar.zlo = 0;
   gar.zwrap = nz;
   gar.range_lo = gar.range_hi = nullptr;
+  gar.geom = geom;
+  gar.dedr = (T *)a->dedr;
 
   set_fft_smem_attrs<T>();
   if (!std::is_same<T, TF>::value) set_fft_smem_attrs<TF>();
@@ -2809,14 +2907,15 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
         pass_cols<T, +1>(p, p->fspec.as<C>(), nz, (int64_t)ny * nxh, nb, p->rpz, tw_of<T>(p, 2), st,
                          "fft_z_inv");
       if (ka.two_slot)
-        pass_cols_fields<T>(p, p->fspec.as<C>(), geom, nf, nfield, 1, want_pot ? 1 : 0, st);
+        pass_cols_fields<T>(p, p->fspec.as<C>(), geom, nf, nfield, 1, pot_field ? 1 : 0, st);
       else
         pass_cols<T, +1>(p, p->fspec.as<C>(), ny, nxh, nb * nz, p->rpy, tw_of<T>(p, 1), st, "fft_y_inv");
       pass_x_inv<T>(p, p->fspec.as<C>(), p->freal.as<T>(), nf, (int64_t)nz * ny, nfield, st);
       gar.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
       gar.channel = c;
       gar.accumulate = c > 0;
-      dispatch_gather<T>(gar, P, st, tr);
+      if (want_force || want_pot) dispatch_gather<T>(gar, P, st, tr);
+      if (want_dedr) dispatch_gather_dedr<T>(gar, P, st, tr);
     }
   }
   // ---- reductions / finalisation ----
@@ -3413,6 +3512,8 @@ extern "C" int sog_mesh_forward(sog_plan *p, const sog_mesh_args *a, void *strea
     return fail(SOG_ERR_INVALID, "missing input array");
   if (a->nchannels < 1) return fail(SOG_ERR_INVALID, "nchannels must be >= 1");
   if (a->n_gauss < 1 || a->n_gauss > kMaxGauss) return fail(SOG_ERR_INVALID, "n_gauss must be in [1, 64]");
+  if (a->dedr && p->d.spline == SOG_SPLINE_CUBES2)
+    return fail(SOG_ERR_UNSUPPORTED, "exact dE/dr is computed for the B-spline and QuadS meshes");
   DeviceGuard dg(p->d.device);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (p->d.dtype == SOG_DTYPE_F64) return mesh_forward_impl<double>(p, a, st);
@@ -3453,6 +3554,7 @@ extern "C" int sog_mesh_slab_forward(sog_plan *p, const sog_mesh_args *a, const 
     return fail(SOG_ERR_INVALID, "missing input array");
   if (a->nchannels < 1 || a->nchannels > 8) return fail(SOG_ERR_INVALID, "slab mode takes 1..8 charge channels");
   if (a->n_gauss < 1 || a->n_gauss > kMaxGauss) return fail(SOG_ERR_INVALID, "n_gauss must be in [1, 64]");
+  if (a->dedr) return fail(SOG_ERR_UNSUPPORTED, "slab mode computes explicit (ik) forces; exact dE/dr needs one device");
   if (a->grad_amp || a->grad_bw2 || a->virial)
     return fail(SOG_ERR_UNSUPPORTED, "slab mode computes energy, forces and dE/dq only");
   if (!sd->exchange || !sd->workspace) return fail(SOG_ERR_INVALID, "slab needs an exchange callback and a workspace");

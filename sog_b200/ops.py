@@ -71,10 +71,25 @@ class SolveSpec:
     slab: Optional[object] = None    # sog_b200.slab.SlabGroup: one frame over several ranks
 
 
+def exact_position_gradient(spec: SolveSpec) -> bool:
+    """Whether the mesh buckets of ``spec`` give dE/dr as the exact gradient
+    of their energy (spline-weight derivatives: the B-spline and QuadS meshes
+    on one device) rather than as the ik-differentiated force.  The
+    reference's QuadS solver is plain torch, so autograd differentiates its
+    spread weights (quads_fft.py:34-73); its CubeS2 backward returns the ik
+    force (cubes2_fft.py:763-779), which CubeS2 keeps here."""
+    return (spec.kind == "mesh" and spec.slab is None
+            and spec.spline in (_lib.SPLINE_BSPLINE, _lib.SPLINE_QUADS))
+
+
 def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Tensor,
                bw2: torch.Tensor, *, want_force: bool, want_pot: bool, want_grad: bool,
-               want_virial: bool):
-    """Launch every bucket of ``spec``; returns (energy, forces, pot, gamp, gbw2, virial)."""
+               want_virial: bool, want_dedr: bool = False):
+    """Launch every bucket of ``spec``; returns (energy, forces, pot, gamp,
+    gbw2, virial, dedr).  With want_dedr the mesh buckets also write the exact
+    dE/dr of their atoms and the other buckets (frames without a periodic
+    cell) their forces, so dE/dr = dedr on mesh atoms and -forces elsewhere
+    (see position_gradient)."""
     dev = r.device
     dt = r.dtype
     nf = spec.nframes
@@ -86,7 +101,9 @@ def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Ten
     amp = amp.contiguous()
     bw2 = bw2.contiguous()
     energy = torch.empty(nf, dtype=dt, device=dev)
-    forces = torch.zeros(N, 3, dtype=dt, device=dev) if want_force else None
+    mixed = want_dedr and any((b.kind or spec.kind) != "mesh" for b in spec.buckets)
+    forces = torch.zeros(N, 3, dtype=dt, device=dev) if (want_force or mixed) else None
+    dedr = torch.zeros(N, 3, dtype=dt, device=dev) if want_dedr else None
     pot = torch.zeros(N, C, dtype=dt, device=dev) if want_pot else None
     gamp = torch.empty(nf, M, dtype=dt, device=dev) if want_grad else None
     gbw2 = torch.empty(nf, M, dtype=dt, device=dev) if want_grad else None
@@ -136,7 +153,9 @@ def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Ten
             plan = _lib.PLANS.get(dev.index if dev.index is not None else torch.cuda.current_device(),
                                   dcode, spec.spline, spec.order, b.dims, spec.kconv,
                                   spec.alias_extent)
-            _lib.mesh_forward(plan, **common)
+            if not want_force:
+                common["forces"] = None   # the exact gradient only
+            _lib.mesh_forward(plan, dedr=dedr, **common)
         else:
             ctx = _lib.direct_ctx(dev.index if dev.index is not None else torch.cuda.current_device(),
                                   dcode)
@@ -148,7 +167,20 @@ def run_solver(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Ten
                 gbw2.index_copy_(0, idx, gb_b)
             if want_virial:
                 vir.index_copy_(0, idx, v_b)
-    return energy, forces, pot, gamp, gbw2, vir
+    return energy, forces, pot, gamp, gbw2, vir, dedr
+
+
+def position_gradient(spec: SolveSpec, forces, dedr):
+    """dE/dr of every atom from run_solver's outputs."""
+    if dedr is None:
+        return None if forces is None else -forces
+    if forces is None or all((b.kind or spec.kind) == "mesh" for b in spec.buckets):
+        return dedr
+    exact_frames = torch.zeros(spec.nframes, dtype=torch.bool, device=dedr.device)
+    for b in spec.buckets:
+        if (b.kind or spec.kind) == "mesh":
+            exact_frames[b.frame_index(dedr.device)] = True
+    return torch.where(exact_frames.index_select(0, spec.frame_of_atom)[:, None], dedr, -forces)
 
 
 def run_hvp(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Tensor, bw2: torch.Tensor,
@@ -211,12 +243,14 @@ class SolveFunction(torch.autograd.Function):
     def forward(ctx, q, r, amp, bw2, spec: SolveSpec, want_force_out: bool, want_virial_out: bool):
         need_q, need_r, need_a, need_b = ctx.needs_input_grad[:4]
         want_grad = bool(need_a or need_b)
-        want_force = bool(need_r or want_force_out)
-        energy, forces, pot, gamp, gbw2, vir = run_solver(
+        exact = bool(need_r) and exact_position_gradient(spec)
+        want_force = bool(want_force_out or (need_r and not exact))
+        energy, forces, pot, gamp, gbw2, vir, dedr = run_solver(
             spec, q, r, amp, bw2, want_force=want_force, want_pot=bool(need_q),
-            want_grad=want_grad, want_virial=bool(want_virial_out))
+            want_grad=want_grad, want_virial=bool(want_virial_out), want_dedr=exact)
         ctx.spec = spec
-        ctx.save_for_backward(q, r, amp, bw2, forces if need_r else None, pot, gamp, gbw2)
+        dEdr = position_gradient(spec, forces, dedr) if need_r else None
+        ctx.save_for_backward(q, r, amp, bw2, dEdr, pot, gamp, gbw2)
         f_out = forces if want_force_out else None
         v_out = vir if want_virial_out else None
         outs = [energy, f_out, v_out]
@@ -227,11 +261,10 @@ class SolveFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, gE, gF, gV):
-        q, r, amp, bw2, forces, pot, gamp, gbw2 = ctx.saved_tensors
+        q, r, amp, bw2, dEdr, pot, gamp, gbw2 = ctx.saved_tensors
         if gE is None:
             return None, None, None, None, None, None, None
         needs = tuple(ctx.needs_input_grad[:4])
-        dEdr = None if forces is None else -forces
         if torch.is_grad_enabled():
             # create_graph=True: the gradients are differentiable functions of
             # (gE, q, r, amp, bw2); their own backward is the Hessian-vector

@@ -86,10 +86,11 @@ def run_mesh_case(name, r, q, cell, batch, amp_raw, bw_raw, order, n_dl,
     if autograd:
         g2 = make()
         qg = q.clone().requires_grad_(True)
-        e = g2.compute_bundle(q=qg, r=r, cell=cell, batch=batch)["energy"]
+        rg = r.clone().requires_grad_(True)
+        e = g2.compute_bundle(q=qg, r=rg, cell=cell, batch=batch)["energy"]
         w = torch.arange(1, e.shape[0] + 1, dtype=F64)  # distinct per-frame weights
         (e * w).sum().backward()
-        rec.update(grad_weights=w.numpy(), grad_q=qg.grad.numpy(),
+        rec.update(grad_weights=w.numpy(), grad_q=qg.grad.numpy(), grad_r=rg.grad.numpy(),
                    grad_amp=g2.amp.grad.numpy(), grad_bw2=g2.bandwidth.grad.numpy())
     np.savez_compressed(os.path.join(OUT, f"{name}.npz"), **rec)
     print(name, rec["energy"])

@@ -70,8 +70,11 @@ def test_config3_full_size_quads4_matches_reference():
     assert _rel(out["virial"].cpu().numpy(), g_ref["virial"]) < E_TOL
     g2 = make()
     q = _t(c["q"]).requires_grad_(True)
-    g2(q=q, r=_t(c["r"]), cell=_t(c["cell"][None])).sum().backward()
+    r = _t(c["r"]).requires_grad_(True)
+    g2(q=q, r=r, cell=_t(c["cell"][None])).sum().backward()
     assert np.abs(q.grad.cpu().numpy() - g_ref["grad_q"]).max() < F_TOL
+    # the reference's autograd force: derivative of its spread weights
+    assert np.abs(r.grad.cpu().numpy() - g_ref["grad_r"]).max() < F_TOL
     assert _rel(g2.amp.grad.cpu().numpy(), g_ref["grad_amp"]) < E_TOL
     assert _rel(g2.bandwidth.grad.cpu().numpy(), g_ref["grad_bw2"]) < E_TOL
 

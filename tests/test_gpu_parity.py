@@ -49,12 +49,16 @@ def test_quads_matches_reference(name):
     assert _rel(e, c["energy"]) < E_TOL
     assert np.abs(out["forces"].cpu().numpy() - c["forces"]).max() < F_TOL
     assert _rel(out["virial"].cpu().numpy(), c["virial"]) < E_TOL
-    # autograd dE/dq and dE/d(amp, bw2) with per-frame weights
+    # autograd dE/dq, dE/dr and dE/d(amp, bw2) with per-frame weights (dE/dr:
+    # the spline-weight derivative for QuadS, the ik force for CubeS2, as the
+    # reference's autograd gives them)
     g2 = make()
     q = _t(c["q"]).requires_grad_(True)
-    en = g2(q=q, r=_t(c["r"]), cell=_t(c["cell"]), batch=_t(c["batch"], torch.long))
+    r = _t(c["r"]).requires_grad_(True)
+    en = g2(q=q, r=r, cell=_t(c["cell"]), batch=_t(c["batch"], torch.long))
     (en * _t(c["grad_weights"])).sum().backward()
     assert np.abs(q.grad.cpu().numpy().reshape(c["grad_q"].shape) - c["grad_q"]).max() < F_TOL
+    assert np.abs(r.grad.cpu().numpy() - c["grad_r"]).max() < F_TOL
     assert _rel(g2.amp.grad.cpu().numpy(), c["grad_amp"]) < E_TOL
     assert _rel(g2.bandwidth.grad.cpu().numpy(), c["grad_bw2"]) < E_TOL
 

@@ -206,3 +206,61 @@ def test_oracle_config3_full_size_matches_reference_quads4():
     assert np.abs(res["potential"][:, 0] - g["grad_q"]).max() < 1e-11
     assert np.allclose(res["grad_amp"][0], g["grad_amp"], rtol=1e-11, atol=0)
     assert np.allclose(res["grad_bw2"][0], g["grad_bw2"], rtol=1e-11, atol=0)
+
+
+def test_oracle_quads_exact_position_gradient_matches_reference_autograd():
+    """The reference's QuadS forces by autograd differentiate its spread
+    weights (quads_fft.py:34-73 under torch autograd); the oracle's exact
+    gradient reproduces them on the 20,000-atom triclinic system."""
+    from tests._cases import cfg3_inputs
+    c = cfg3_inputs()
+    g = load("cfg3_quads4")
+    grid, ksm = grid_ndl(c["cell"], c["n_dl"])
+    res = O.mesh_solve(c["r"], c["q"], c["cell"], g["amp"], g["bw2"], spline=O.QUADS, order=4, nx=grid[0],
+                       ny=grid[1], nz=grid[2], k_sq_max=ksm, want_force=False, want_dedr=True, kconv=1)
+    assert np.abs(res["dedr"] - g["grad_r"]).max() < 1e-11
+
+
+@pytest.mark.parametrize("spline,order", [(O.BSPLINE, 4), (O.BSPLINE, 5), (O.BSPLINE, 6), (O.QUADS, 6)])
+def test_oracle_exact_position_gradient_matches_finite_differences(spline, order):
+    rng = np.random.default_rng(order + 10 * spline)
+    cell = np.array([[9.0, 0.0, 0.0], [0.7, 9.4, 0.0], [-0.5, 0.6, 8.8]])
+    n = 20
+    r = rng.random((n, 3)) @ cell
+    q = rng.standard_normal(n)
+    q -= q.mean()
+    amp, bw2 = np.array([0.9, 1.3]), np.array([1.4, 4.0])
+    grid, ksm = grid_ndl(cell, 0.8)
+    kw = dict(spline=spline, order=order, nx=grid[0], ny=grid[1], nz=grid[2], k_sq_max=ksm, want_force=False)
+    res = O.mesh_solve(r, q, cell, amp, bw2, want_dedr=True, **kw)
+    h = 1e-5
+    for i in (0, 7):
+        for b in range(3):
+            rp, rm = r.copy(), r.copy()
+            rp[i, b] += h
+            rm[i, b] -= h
+            fd = (O.mesh_solve(rp, q, cell, amp, bw2, **kw)["energy"] -
+                  O.mesh_solve(rm, q, cell, amp, bw2, **kw)["energy"]) / (2 * h)
+            assert abs(fd - res["dedr"][i, b]) < 1e-7 * max(1.0, abs(fd))
+
+
+@pytest.mark.parametrize("name", MESH_CASES + CUBES2_CASES)
+def test_oracle_position_gradient_matches_reference_autograd(name):
+    """The reference's dE/dr by autograd: QuadS differentiates its spread
+    weights (the oracle's exact gradient); CubeS2's backward returns the ik
+    force (cubes2_fft.py:763-779)."""
+    c = load(name)
+    cells = c["cell"].reshape(-1, 3, 3)
+    q = c["q"] if c["q"].ndim == 2 else c["q"][:, None]
+    cubes = name.startswith("cubes2")
+    dedr = np.zeros((len(c["r"]), 3))
+    for f, cl in enumerate(cells):
+        idx = np.nonzero(c["batch"] == f)[0]
+        grid, ksm = grid_ndl(cl, float(c["n_dl"]))
+        for ch in range(q.shape[1]):
+            res = O.mesh_solve(c["r"][idx], q[idx, ch], cl, c["amp"], c["bw2"],
+                               spline=O.CUBES2 if cubes else O.QUADS, order=int(c["order"]), nx=grid[0],
+                               ny=grid[1], nz=grid[2], k_sq_max=ksm, want_force=cubes,
+                               want_dedr=not cubes, kconv=1, remove_self=bool(c["remove_self"]))
+            dedr[idx] += (-res["forces"] if cubes else res["dedr"]) * c["grad_weights"][f]
+    assert np.abs(dedr - c["grad_r"]).max() < 1e-11
