@@ -102,13 +102,13 @@ def bucket_bytes(dims, nframes: int, natoms: int, s: int = 8, nfield: int = 3):
         "spread": s * ng + 4 * s * N,
         "fft_r2c_x": s * ng + 2 * s * nh,
         "fft_y_fwd": 4 * s * nh,
-        "fft_y_inv": nfield * 4 * s * nh,
+        "fft_y_inv": (2 + nfield) * 2 * s * nh if nz & (nz - 1) == 0 else nfield * 4 * s * nh,
         "fft_c2r_x": nfield * (2 * s * nh + s * ng),
         "gather": nfield * s * ng + 7 * s * N,
         "green": s * nh,
     }
-    if nz & (nz - 1) == 0:        # fused z pass
-        out["zfused"] = 2 * s * nh + nfield * 2 * s * nh
+    if nz & (nz - 1) == 0:        # fused z pass: spectrum in, Y1 and Y2 out
+        out["zfused"] = 2 * s * nh + 2 * 2 * s * nh
     else:                         # z passes around the k-space kernel
         out.update({"fft_z_fwd": 4 * s * nh, "kspace": 2 * s * nh + nfield * 2 * s * nh,
                     "fft_z_inv": nfield * 4 * s * nh})
@@ -168,12 +168,14 @@ def algorithmic_bytes(cfg, s: int = 8, nfield: int = 3, parts: int = 1):
         "fft_z_fwd": 4 * s * nh,
         "kspace": 2 * s * nh + nfield * 2 * s * nh,
         "fft_z_inv": nfield * 4 * s * nh,
-        "fft_y_inv": nfield * 4 * s * nh,
+        # inverse y pass of an orthorhombic frame with forces: the two z-pass
+        # outputs Y1, Y2 in, the three ik fields out
+        "fft_y_inv": (2 + nfield) * 2 * s * nh,
         "fft_c2r_x": nfield * (2 * s * nh + s * ng),
         "gather": nfield * s * ng + 4 * s * N + 3 * s * N,
-        # fused z pass: spectrum in, nfield transformed fields out (the Green
-        # table it reads is not part of the minimal pipeline)
-        "zfused": 2 * s * nh + nfield * 2 * s * nh,
+        # fused z pass: spectrum in, the two field spectra Y1, Y2 out (the
+        # Green function comes from a radial table in L2: no HBM bytes)
+        "zfused": 2 * s * nh + 2 * 2 * s * nh,
         # Green table written once per evaluation
         "green": s * nh,
     }
