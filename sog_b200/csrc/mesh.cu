@@ -655,7 +655,9 @@ template <typename T, int P, typename TG>
 __global__ void __launch_bounds__(32 * kWarpsPerSpreadCta, SOG_SPREAD_BLK_MINB) k_spread_blk(SpreadArgs<T> a, int nbx, int nby,
                                                                           int nbz, int64_t nblk) {
   constexpr int kSeg = 18;
-  __shared__ TG s_w[kWarpsPerSpreadCta][32][24];   // per warp and lane: a candidate's x (times q), y, z weights
+  // per warp and lane: a candidate's x (times q), y, z weights; rows of 25
+  // (odd) words so that the lanes' rows start in different banks
+  __shared__ TG s_w[kWarpsPerSpreadCta][32][25];
   __shared__ uint32_t s_lo[kWarpsPerSpreadCta][kSeg], s_pre[kWarpsPerSpreadCta][kSeg + 1];
   __shared__ int s_bl[kWarpsPerSpreadCta][3][4];
   __shared__ int s_nb[kWarpsPerSpreadCta][3];
@@ -745,16 +747,23 @@ __global__ void __launch_bounds__(32 * kWarpsPerSpreadCta, SOG_SPREAD_BLK_MINB) 
       for (int ax = 0; ax < 3; ++ax) {
         double w1[P];
         spline_w<double, P>(a.spline, (double)a.s_t[(int64_t)sidx * 3 + ax], w1, a.qc);
+        if (ax == 0) {
+#pragma unroll
+          for (int jj = 0; jj < P; ++jj) w1[jj] *= qv;
+        }
+        // stencil offset of block point 0 (both in [0, n)), then one step per point
+        int k = base[ax] - anc[ax];
+        if (k < 0) k += nn[ax];
         bool h = false;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int k = imod(base[ax] + i - anc[ax], nn[ax]);
           double v = 0.0;
 #pragma unroll
           for (int jj = 0; jj < P; ++jj) v = (k == jj) ? w1[jj] : v;
-          if (i >= lim[ax]) v = 0.0;
-          h |= (k < P && i < lim[ax]);
-          w[ax * 8 + i] = (TG)(ax == 0 ? v * qv : v);
+          const bool in = i < lim[ax];
+          h |= (k < P && in);
+          w[ax * 8 + i] = (TG)(in ? v : 0.0);
+          if (++k == nn[ax]) k = 0;
         }
         has = has && h;
       }
