@@ -473,11 +473,6 @@ struct HvpArgs {
   int nh;                              // 5M
 };
 
-template <typename T>
-__device__ __forceinline__ double ldir(const void *p, int64_t i) {
-  return p ? (double)static_cast<const T *>(p)[i] : 0.0;
-}
-
 // thread per mode: S_d, X = K S_d + dK S, theta partials and the D sums
 template <typename T>
 __global__ void __launch_bounds__(kDirThreads) k_direct_hvp_modes(DirArgs a, HvpArgs h, const T *__restrict__ pos,
@@ -666,136 +661,6 @@ __global__ void __launch_bounds__(CH) k_direct_hvp_atoms(DirArgs a, HvpArgs h, c
   T *oq = static_cast<T *>(h.oq), *orr = static_cast<T *>(h.orr);
   for (int c = 0; c < a.nch; ++c) oq[atom * a.nch + c] = (T)(sc * (px[c] - bs[c]));
   for (int c = 0; c < 3; ++c) orr[atom * 3 + c] = (T)(-sc * fr[c]);
-}
-
-// direction sums per frame and channel: sum a, sum q a
-template <typename T>
-__global__ void k_hvp_dsums(const T *__restrict__ q, const void *dq, int nch, const FrameGeom *__restrict__ geom,
-                            double *__restrict__ out) {
-  const int f = blockIdx.x, c = blockIdx.y;
-  const FrameGeom &g = geom[f];
-  double s1 = 0.0, s2 = 0.0;
-  for (int64_t i = threadIdx.x; i < g.natoms; i += blockDim.x) {
-    const int64_t o = (g.atom_begin + i) * nch + c;
-    const double av = ldir<T>(dq, o);
-    s1 += av;
-    s2 += (double)q[o] * av;
-  }
-  __shared__ double r1[256], r2[256];
-  r1[threadIdx.x] = s1;
-  r2[threadIdx.x] = s2;
-  __syncthreads();
-  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
-    if (threadIdx.x < o) { r1[threadIdx.x] += r1[threadIdx.x + o]; r2[threadIdx.x] += r2[threadIdx.x + o]; }
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    out[((int64_t)f * nch + c) * 2 + 0] = r1[0];
-    out[((int64_t)f * nch + c) * 2 + 1] = r2[0];
-  }
-}
-
-struct HvpFinal {
-  const FrameGeom *geom;
-  const double *hred;   // [nf][5M]: theta rows (amp, bw2), D0, D1, D2 (half-space weight 2)
-  const double *qsum;   // [nf][C][2] sum q, sum q^2
-  const double *dsum;   // [nf][C][2] sum a, sum q a
-  const void *amp, *bw2, *damp, *dbw2;
-  void *oamp, *obw2;
-  double *scal;         // [nf][8] per-frame scalars for the atom pass
-  int M, nch;
-  double norm, self_coeff, lambda;
-  int remove_self, k0;
-};
-
-// Parameter rows of H d per frame (core + self + k=0 terms) and the scalars
-// of the charge rows' self / k=0 / penalty terms.
-//   self:  E_s = -norm (rs D + self_coeff) sum_c |q_c|^2,  D = sum_m amp_m D0_m / 2V
-//   k=0:   E_0 = norm kfe (Q^2 - rs QQ) / 2V,  kfe = sum_m amp_m exp(-bw2_m kmin^2 / 2)
-//   pen:   E_p = lambda sum_c mean_c(q)^2
-template <typename T>
-__global__ void k_hvp_finalize_frames(HvpFinal a, int nf) {
-  const int f = blockIdx.x * blockDim.x + threadIdx.x;
-  if (f >= nf) return;
-  const FrameGeom &g = a.geom[f];
-  const double V = g.vol, i2v = 1.0 / (2.0 * V);
-  const int M = a.M;
-  const T *amp = (const T *)a.amp, *bw2 = (const T *)a.bw2;
-  const double *x = a.hred + (int64_t)f * 5 * M;
-  const double *D0 = x + 2 * M, *D1 = x + 3 * M, *D2 = x + 4 * M;
-  double Q = 0, QQ = 0, A = 0, QA = 0;
-  for (int c = 0; c < a.nch; ++c) {
-    Q += a.qsum[((int64_t)f * a.nch + c) * 2 + 0];
-    QQ += a.qsum[((int64_t)f * a.nch + c) * 2 + 1];
-    A += a.dsum[((int64_t)f * a.nch + c) * 2 + 0];
-    QA += a.dsum[((int64_t)f * a.nch + c) * 2 + 1];
-  }
-  const double rs = a.remove_self ? 1.0 : 0.0;
-  const double kmin2 = g.kmin2;
-  double diag = 0.0, ddiag = 0.0, kfe = 0.0, dkfe = 0.0;
-  for (int m = 0; m < M; ++m) {
-    const double am = (double)amp[m], ca = ldir<T>(a.damp, (int64_t)f * M + m), cb = ldir<T>(a.dbw2, (int64_t)f * M + m);
-    const double Em = exp(-0.5 * (double)bw2[m] * kmin2);
-    diag += am * D0[m] * i2v;
-    ddiag += (ca * D0[m] + cb * am * D1[m]) * i2v;
-    kfe += am * Em;
-    dkfe += ca * Em + cb * am * (-0.5 * kmin2) * Em;
-  }
-  for (int m = 0; m < M; ++m) {
-    const double am = (double)amp[m], ca = ldir<T>(a.damp, (int64_t)f * M + m), cb = ldir<T>(a.dbw2, (int64_t)f * M + m);
-    const double Em = exp(-0.5 * (double)bw2[m] * kmin2);
-    // core rows (the half-space sums carry 2, E carries 1/2V)
-    double ga = a.norm * i2v * x[m], gb = a.norm * i2v * x[M + m];
-    // self term: d/dtheta of -norm rs QQ D, along the direction
-    const double dD_a = D0[m] * i2v, dD_b = am * D1[m] * i2v;          // dD/damp_m, dD/dbw2_m
-    const double hD_a = cb * D1[m] * i2v;                               // (d2 D . c)_amp_m
-    const double hD_b = (ca * D1[m] + cb * am * D2[m]) * i2v;           // (d2 D . c)_bw2_m
-    ga += -a.norm * rs * (2.0 * QA * dD_a + QQ * hD_a);
-    gb += -a.norm * rs * (2.0 * QA * dD_b + QQ * hD_b);
-    if (a.k0) {
-      const double dk_a = Em, dk_b = am * (-0.5 * kmin2) * Em;
-      const double hk_a = cb * (-0.5 * kmin2) * Em;
-      const double hk_b = ca * (-0.5 * kmin2) * Em + cb * am * 0.25 * kmin2 * kmin2 * Em;
-      const double lin = 2.0 * Q * A - 2.0 * rs * QA, quad = Q * Q - rs * QQ;
-      ga += a.norm * i2v * (dk_a * lin + hk_a * quad);
-      gb += a.norm * i2v * (dk_b * lin + hk_b * quad);
-    }
-    ((T *)a.oamp)[(int64_t)f * M + m] = (T)ga;
-    ((T *)a.obw2)[(int64_t)f * M + m] = (T)gb;
-  }
-  double *s = a.scal + (int64_t)f * 8;
-  s[0] = rs * diag + a.self_coeff;
-  s[1] = rs * ddiag;
-  s[2] = a.k0 ? kfe : 0.0;
-  s[3] = a.k0 ? dkfe : 0.0;
-  s[4] = Q;
-  s[5] = A;
-  s[6] = rs;
-  s[7] = 0.0;
-}
-
-// Charge rows: self, k=0 and penalty terms added to the core term.
-template <typename T>
-__global__ void k_hvp_finalize_atoms(const FrameGeom *__restrict__ geom, const double *__restrict__ scal,
-                                     const double *__restrict__ dsum, const T *__restrict__ q, const void *dq,
-                                     T *__restrict__ oq, int nch, double norm, double lambda) {
-  const int f = blockIdx.y;
-  const FrameGeom &g = geom[f];
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= g.natoms) return;
-  const double *s = scal + (int64_t)f * 8;
-  const double i2v = 1.0 / (2.0 * g.vol);
-  const int64_t atom = g.atom_begin + i;
-  for (int c = 0; c < nch; ++c) {
-    const int64_t o = atom * nch + c;
-    const double qi = (double)q[o], ai = ldir<T>(dq, o);
-    double v = (double)oq[o];
-    v += -2.0 * norm * (ai * s[0] + qi * s[1]);
-    v += norm * i2v * (s[2] * (2.0 * s[5] - 2.0 * s[6] * ai) + s[3] * (2.0 * s[4] - 2.0 * s[6] * qi));
-    if (lambda > 0.0 && g.natoms > 0)
-      v += 2.0 * lambda * dsum[((int64_t)f * nch + c) * 2 + 0] / ((double)g.natoms * g.natoms);
-    oq[o] = (T)v;
-  }
 }
 
 template <typename T>
