@@ -299,6 +299,17 @@ SOG_API int sog_realspace_forward(sog_direct *d, const sog_realspace_args *args,
 SOG_API int sog_realspace_hvp(sog_direct *d, const sog_realspace_args *args, const sog_hvp_args *h,
                               void *stream);
 
+/* Hessian-vector product of the mesh energy (sog_hvp_args as for
+ * sog_direct_hvp; the sog_mesh_args outputs are ignored): the second
+ * derivatives the reference takes with torch.autograd through its QuadS
+ * spread, transforms and gather (compute_quads_fft, quads_fft.py:209-326),
+ * for plans of SOG_SPLINE_QUADS and SOG_SPLINE_BSPLINE, whose position
+ * gradient is the derivative of the spread weights.  A CubeS2 plan returns
+ * SOG_ERR_UNSUPPORTED: the reference's Cubes2FFTFunction backward
+ * (cubes2_fft.py:746-869) is the ik force, whose own derivative is not the
+ * energy's Hessian. */
+SOG_API int sog_mesh_hvp(sog_plan *p, const sog_mesh_args *args, const sog_hvp_args *h, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Direct k-sum without allocation (no counterpart in the reference)         */
 /* ------------------------------------------------------------------------ */

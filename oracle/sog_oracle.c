@@ -632,7 +632,7 @@ static void kvec(const green_ctx *g, double mx, double my, double mz, double *k)
 static int green_at(const green_ctx *g, int mx, int my, int mz, int iy, int iz,
                     double *kout, double *kfac, double *gE, double *gF,
                     double *gS, double *gV, double *kfacv, double *emD,
-                    double *emS) {
+                    double *emS, double *emDb, double *emSb) {
   double k[3];
   kvec(g, mx, my, mz, k);
   const double ksq = k[0] * k[0] + k[1] * k[1] + k[2] * k[2];
@@ -653,6 +653,7 @@ static int green_at(const green_ctx *g, int mx, int my, int mz, int iy, int iz,
     if (emD) for (int m = 0; m < g->M; ++m) {
       const double e = exp(-0.5 * g->bw2[m] * ksq);
       emD[m] = e * D; emS[m] = e;
+      emDb[m] = -0.5 * ksq * emD[m]; emSb[m] = -0.5 * ksq * e;
     }
     return 1;
   }
@@ -664,6 +665,7 @@ static int green_at(const green_ctx *g, int mx, int my, int mz, int iy, int iz,
     if (emD) for (int m = 0; m < g->M; ++m) {
       const double e = exp(-0.5 * g->bw2[m] * ksq);
       emD[m] = e * D; emS[m] = e;
+      emDb[m] = -0.5 * ksq * emD[m]; emSb[m] = -0.5 * ksq * e;
     }
     return 1;
   }
@@ -686,7 +688,7 @@ static int green_at(const green_ctx *g, int mx, int my, int mz, int iy, int iz,
     jlo[a] = lo; jhi[a] = hi;
   }
   double sum0 = 0.0, sum1 = 0.0, sumv = 0.0;
-  if (emD) for (int m = 0; m < g->M; ++m) { emD[m] = 0.0; emS[m] = 0.0; }
+  if (emD) for (int m = 0; m < g->M; ++m) { emD[m] = 0.0; emS[m] = 0.0; emDb[m] = 0.0; emSb[m] = 0.0; }
   const double w0 = orc_bspline_sinc2p(mx, g->nx, g->order, 0) *
                     orc_bspline_sinc2p(my, g->ny, g->order, 0) *
                     orc_bspline_sinc2p(mz, g->nz, g->order, 0);
@@ -710,9 +712,13 @@ static int green_at(const green_ctx *g, int mx, int my, int mz, int iy, int iz,
         sum1 += (k[0] * q[0] + k[1] * q[1] + k[2] * q[2]) * Kq * wp;
         sumv += Kvq * wp;
         if (emD) for (int m = 0; m < g->M; ++m) {
+          /* an alias term's bw2 derivative carries its own -|q|^2 / 2 */
           const double e = exp(-0.5 * g->bw2[m] * qsq);
-          emD[m] += e * wp / denom;
-          emS[m] += (w0 > 1e-20) ? e * wp / w0 : 0.0;
+          const double eD = e * wp / denom, eS = (w0 > 1e-20) ? e * wp / w0 : 0.0;
+          emD[m] += eD;
+          emS[m] += eS;
+          emDb[m] += -0.5 * qsq * eD;
+          emSb[m] += -0.5 * qsq * eS;
         }
       }
   *gE = sum0 / denom;
@@ -837,7 +843,7 @@ int orc_mesh_solve(const orc_mesh_in *in, orc_mesh_out *out) {
 #pragma omp parallel for schedule(static)
   for (int iz = 0; iz < nz; ++iz) {
     double *acc = part + (size_t)iz * nacc;
-    double emD[64], emS[64];
+    double emD[64], emS[64], emDb[64], emSb[64];
     const int mz = iz <= nz / 2 ? iz : iz - nz;
     for (int iy = 0; iy < ny; ++iy) {
       const int my = iy <= ny / 2 ? iy : iy - ny;
@@ -845,7 +851,7 @@ int orc_mesh_solve(const orc_mesh_in *in, orc_mesh_out *out) {
         const long idx = ((long)iz * ny + iy) * nxh + mx;
         double k[3], K = 0, gE = 0, gF = 0, gS = 0, gV = 0, Kv = 0;
         const int live = green_at(&g, mx, my, mz, iy, iz, k, &K, &gE, &gF, &gS, &gV,
-                                  &Kv, in->want_param_grad ? emD : NULL, emS);
+                                  &Kv, in->want_param_grad ? emD : NULL, emS, emDb, emSb);
         if (!live) continue;
         const double w = (mx == 0 || (nx % 2 == 0 && mx == nx / 2)) ? 1.0 : 2.0;
         const cplx r = rk[idx];
@@ -853,12 +859,11 @@ int orc_mesh_solve(const orc_mesh_in *in, orc_mesh_out *out) {
         acc[0] += w * gE * r2;
         acc[1] += w * gS;
         if (in->want_param_grad) {
-          const double ksq = k[0] * k[0] + k[1] * k[1] + k[2] * k[2];
           for (int m = 0; m < M; ++m) {
             acc[2 + m] += w * emD[m] * r2;
             acc[2 + M + m] += w * emS[m];
-            acc[2 + 2 * M + m] += w * (-0.5 * ksq) * in->amp[m] * emD[m] * r2;
-            acc[2 + 3 * M + m] += w * (-0.5 * ksq) * in->amp[m] * emS[m];
+            acc[2 + 2 * M + m] += w * in->amp[m] * emDb[m] * r2;
+            acc[2 + 3 * M + m] += w * in->amp[m] * emSb[m];
           }
         }
         if (in->want_virial) {

@@ -89,7 +89,7 @@ EXPORTS = ["sog_strerror", "sog_last_error", "sog_version", "sog_launch_count", 
            "sog_mesh_forward", "sog_direct_create", "sog_direct_destroy", "sog_direct_set_timing",
            "sog_direct_timings", "sog_direct_forward", "sog_direct_forward_noalloc",
            "sog_mesh_slab_workspace", "sog_mesh_slab_forward", "sog_realspace_forward",
-           "sog_direct_hvp", "sog_realspace_hvp"]
+           "sog_direct_hvp", "sog_realspace_hvp", "sog_mesh_hvp"]
 
 _lib = None
 _lock = threading.Lock()
@@ -126,6 +126,7 @@ def load():
         lib.sog_direct_forward.argtypes = [_vp, ctypes.POINTER(DirectArgs), _vp]
         lib.sog_realspace_forward.argtypes = [_vp, ctypes.POINTER(RealspaceArgs), _vp]
         lib.sog_direct_hvp.argtypes = [_vp, ctypes.POINTER(DirectArgs), ctypes.POINTER(HvpArgs), _vp]
+        lib.sog_mesh_hvp.argtypes = [_vp, ctypes.POINTER(MeshArgs), ctypes.POINTER(HvpArgs), _vp]
         lib.sog_realspace_hvp.argtypes = [_vp, ctypes.POINTER(RealspaceArgs), ctypes.POINTER(HvpArgs), _vp]
         lib.sog_launch_count.restype = ctypes.c_ulonglong
         for name in ("sog_plan_set_timing", "sog_direct_set_timing"):
@@ -331,6 +332,23 @@ def mesh_slab_forward(plan: "Plan", group, *, atom_begin, atom_count, k_sq_max, 
     del keep
 
 
+def mesh_hvp(plan: Plan, *, atom_begin, atom_count, k_sq_max, positions, charges, cells, amp, bw2,
+             norm_factor, self_coeff, remove_self, k0_correction, charge_neutral_lambda, dir_q, dir_r,
+             dir_amp, dir_bw2, out_q, out_r, out_amp, out_bw2, stream=None, **_unused):
+    """sog_mesh_hvp (B-spline / QuadS plans): the Hessian of every frame's
+    mesh energy applied to the direction; outputs written in place."""
+    _require_cuda(positions)
+    args, keep = _mesh_args(atom_begin, atom_count, k_sq_max, positions, charges, cells, amp, bw2,
+                            norm_factor, self_coeff, remove_self, k0_correction, charge_neutral_lambda,
+                            None, None, None, None, None, None)
+    h = _hvp_args(dir_q, dir_r, dir_amp, dir_bw2, out_q, out_r, out_amp, out_bw2)
+    if stream is None:
+        stream = torch.cuda.current_stream(positions.device).cuda_stream
+    check(load().sog_mesh_hvp(plan.handle, ctypes.byref(args), ctypes.byref(h), ctypes.c_void_p(stream)),
+          "sog_mesh_hvp")
+    del keep
+
+
 def mesh_forward(plan: Plan, *, atom_begin, atom_count, k_sq_max, positions, charges, cells, amp,
                  bw2, norm_factor, self_coeff, remove_self, k0_correction, charge_neutral_lambda,
                  energy, forces=None, potential=None, grad_amp=None, grad_bw2=None, virial=None,
@@ -338,27 +356,15 @@ def mesh_forward(plan: Plan, *, atom_begin, atom_count, k_sq_max, positions, cha
     """One C-ABI mesh call.  All tensors must be contiguous CUDA tensors of the
     plan dtype; outputs are written in place."""
     _require_cuda(positions)
-    nf = len(atom_begin)
-    ab, ac, km = _host_i64(atom_begin), _host_i64(atom_count), _host_f64(k_sq_max)
-    args = MeshArgs()
-    args.nframes = nf
-    args.atom_begin = ctypes.cast(ab, _c_i64p)
-    args.atom_count = ctypes.cast(ac, _c_i64p)
-    args.k_sq_max = ctypes.cast(km, _c_dp)
-    args.nchannels = charges.shape[1]
-    args.positions, args.charges, args.cells = _ptr(positions), _ptr(charges), _ptr(cells)
-    args.n_gauss = amp.numel()
-    args.amp, args.bw2 = _ptr(amp), _ptr(bw2)
-    args.norm_factor, args.self_coeff = float(norm_factor), float(self_coeff)
-    args.remove_self, args.k0_correction = int(remove_self), int(k0_correction)
-    args.charge_neutral_lambda = float(charge_neutral_lambda or 0.0)
-    args.energy, args.forces, args.potential = _ptr(energy), _ptr(forces), _ptr(potential)
-    args.grad_amp, args.grad_bw2, args.virial = _ptr(grad_amp), _ptr(grad_bw2), _ptr(virial)
+    args, keep = _mesh_args(atom_begin, atom_count, k_sq_max, positions, charges, cells, amp, bw2,
+                            norm_factor, self_coeff, remove_self, k0_correction, charge_neutral_lambda,
+                            energy, forces, potential, grad_amp, grad_bw2, virial)
     args.dedr = _ptr(dedr)
     if stream is None:
         stream = torch.cuda.current_stream(positions.device).cuda_stream
     check(load().sog_mesh_forward(plan.handle, ctypes.byref(args), ctypes.c_void_p(stream)),
           "sog_mesh_forward")
+    del keep
 
 
 def direct_forward(ctx, *, atom_begin, atom_count, nk, k_sq_max, positions, charges, cells, amp,

@@ -221,6 +221,29 @@ __device__ __forceinline__ void spline_dw(int spline, double t, double *dw, cons
   }
 }
 
+// d^2 w[k] / dt^2: the second difference of the order P-2 B-spline,
+// w_p''[a] = w_{p-2}[a-2] - 2 w_{p-2}[a-1] + w_{p-2}[a], and the QuadS
+// polynomials' second derivatives.
+template <int P>
+__device__ __forceinline__ void spline_d2w(int spline, double t, double *d2, const QuadsCoef &qc) {
+  if (spline == SOG_SPLINE_QUADS) {
+#pragma unroll
+    for (int k = 0; k < P; ++k) {
+      double v = 0.0, tp = 1.0;
+#pragma unroll
+      for (int p = 2; p < P; ++p) { v += (double)(p * (p - 1)) * qc.c[k * P + p] * tp; tp *= t; }
+      d2[k] = v;
+    }
+  } else {
+    double w2[P - 2];
+    bspline_w<double, P - 2>(t, w2);
+#pragma unroll
+    for (int a = 0; a < P; ++a)
+      d2[a] = (a >= 2 ? w2[a - 2] : 0.0) - 2.0 * (a >= 1 && a - 1 < P - 2 ? w2[a - 1] : 0.0) +
+              (a < P - 2 ? w2[a] : 0.0);
+  }
+}
+
 // CubeS2 (cubes2_spline.py): every node weight is a sum of products of 1-D
 // polynomials of the three offsets, and summing the classes node by node
 // gives a sum of separable stencils over the P = order window
@@ -346,6 +369,11 @@ struct SpreadArgs {
   QuadsCoef qc;
   // z planes written: [zlo, zlo + zcnt) of nz, stored as rho[f][zcnt][ny][nx]
   int zlo, zcnt;
+  // direction density of a Hessian-vector product (k_spread_dip): the
+  // direction on the charges [N][nch] (channel `channel`) and positions [N][3]
+  const void *dir_q, *dir_r;
+  const int32_t *s_atom;
+  int nch, channel;
 };
 
 constexpr int kSpreadThreads = kTileX * kTileY;
@@ -651,6 +679,75 @@ __global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? SOG_SPREAD_MINB : 2)
 // are independent blocks).
 constexpr int kWarpsPerSpreadCta = 4;
 
+// Candidate segments of one 8 x 8 x 8 block, built by its warp: the runs of
+// the cell-sorted atom array whose bins hold anchors able to reach the block
+// (at most 3 x 3 x 3 bins; a (z, y) bin row gives at most two runs of x bins,
+// two when the halo wraps), numbered in lane order.  Returns the number of
+// runs; s_pre[nsg] is the candidate count.
+template <typename T, int P>
+__device__ __forceinline__ int blk_segments(const SpreadArgs<T> &a, int f, int x0, int y0, int z0, int xv, int yv,
+                                            int zv, int lane, uint32_t *s_lo, uint32_t *s_pre, int (*s_bl)[4],
+                                            int *s_nb) {
+  const AtomGrid &ag = a.ag;
+  if (lane < 3) {
+    const int lo = (lane == 0 ? x0 : lane == 1 ? y0 : z0) - P + 1;
+    const int len = (lane == 0 ? xv : lane == 1 ? yv : zv) + P - 1;
+    const int n = lane == 0 ? ag.nx : lane == 1 ? ag.ny : ag.nz;
+    const int nb = lane == 0 ? ag.nbx : lane == 1 ? ag.nby : ag.nbz;
+    s_nb[lane] = axis_bins(lo, len, n, nb, s_bl[lane]);
+  }
+  __syncwarp();
+  const int nxl = s_nb[0], nyl = s_nb[1], nzl = s_nb[2];
+  uint32_t lo2[2] = {0, 0}, cnt2[2] = {0, 0};
+  if (lane < nzl * nyl) {
+    const int iz = lane / nyl, iy = lane - iz * nyl;
+    const uint32_t row = (uint32_t)f * ag.bins_per_frame + bin_row(ag, s_bl[2][iz], s_bl[1][iy]);
+    int brk = nxl;   // x bins are ascending with at most one break
+    for (int i = 1; i < nxl; ++i)
+      if (brk == nxl && s_bl[0][i] != s_bl[0][i - 1] + 1) brk = i;
+    lo2[0] = a.bin_start[row + s_bl[0][0]];
+    cnt2[0] = a.bin_start[row + s_bl[0][brk - 1] + 1] - lo2[0];
+    if (brk < nxl) {
+      lo2[1] = a.bin_start[row + s_bl[0][brk]];
+      cnt2[1] = a.bin_start[row + s_bl[0][nxl - 1] + 1] - lo2[1];
+    }
+  }
+  const int ne = (cnt2[0] > 0) + (cnt2[1] > 0);
+  int eo = ne;
+  uint32_t co = cnt2[0] + cnt2[1];
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int ue = __shfl_up_sync(0xffffffffu, eo, o);
+    const uint32_t uc = __shfl_up_sync(0xffffffffu, co, o);
+    if (lane >= o) { eo += ue; co += uc; }
+  }
+  int sg = eo - ne;
+  uint32_t pre = co - (cnt2[0] + cnt2[1]);
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    if (cnt2[h] > 0) {
+      s_lo[sg] = lo2[h];
+      s_pre[sg] = pre;
+      pre += cnt2[h];
+      ++sg;
+    }
+  if (lane == 31) s_pre[eo] = co;
+  const int nsg = __shfl_sync(0xffffffffu, eo, 31);   // segments in all
+  __syncwarp();
+  return nsg;
+}
+
+// the sorted-atom index of candidate ci (last segment with s_pre <= ci)
+__device__ __forceinline__ uint32_t blk_candidate(const uint32_t *s_lo, const uint32_t *s_pre, int nsg, uint32_t ci) {
+  int lo = 0, hi = nsg - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_pre[mid] <= ci) lo = mid; else hi = mid - 1;
+  }
+  return s_lo[lo] + (ci - s_pre[lo]);
+}
+
+
 template <typename T, int P, typename TG>
 __global__ void __launch_bounds__(32 * kWarpsPerSpreadCta, SOG_SPREAD_BLK_MINB) k_spread_blk(SpreadArgs<T> a, int nbx, int nby,
                                                                           int nbz, int64_t nblk) {
@@ -674,54 +771,8 @@ __global__ void __launch_bounds__(32 * kWarpsPerSpreadCta, SOG_SPREAD_BLK_MINB) 
   const int x0 = bx * 8, y0 = by * 8, z0 = a.zlo + bz * 8;
   const int xv = min(8, ag.nx - x0), yv = min(8, ag.ny - y0), zv = min(8, a.zlo + a.zcnt - z0);
   // ---- segments of the sorted atom array holding the candidates ----
-  int nsg;
-  if (lane < 3) {
-    const int lo = (lane == 0 ? x0 : lane == 1 ? y0 : z0) - P + 1;
-    const int len = (lane == 0 ? xv : lane == 1 ? yv : zv) + P - 1;
-    const int n = lane == 0 ? ag.nx : lane == 1 ? ag.ny : ag.nz;
-    const int nb = lane == 0 ? ag.nbx : lane == 1 ? ag.nby : ag.nbz;
-    s_nb[warp][lane] = axis_bins(lo, len, n, nb, s_bl[warp][lane]);
-  }
-  __syncwarp();
-  const int nxl = s_nb[warp][0], nyl = s_nb[warp][1], nzl = s_nb[warp][2];
-  uint32_t lo2[2] = {0, 0}, cnt2[2] = {0, 0};
-  if (lane < nzl * nyl) {
-    const int iz = lane / nyl, iy = lane - iz * nyl;
-    const uint32_t row = (uint32_t)f * ag.bins_per_frame + bin_row(ag, s_bl[warp][2][iz], s_bl[warp][1][iy]);
-    int brk = nxl;   // x bins are ascending with at most one break
-    for (int i = 1; i < nxl; ++i)
-      if (brk == nxl && s_bl[warp][0][i] != s_bl[warp][0][i - 1] + 1) brk = i;
-    lo2[0] = a.bin_start[row + s_bl[warp][0][0]];
-    cnt2[0] = a.bin_start[row + s_bl[warp][0][brk - 1] + 1] - lo2[0];
-    if (brk < nxl) {
-      lo2[1] = a.bin_start[row + s_bl[warp][0][brk]];
-      cnt2[1] = a.bin_start[row + s_bl[warp][0][nxl - 1] + 1] - lo2[1];
-    }
-  }
-  {
-    const int ne = (cnt2[0] > 0) + (cnt2[1] > 0);
-    int eo = ne;
-    uint32_t co = cnt2[0] + cnt2[1];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int ue = __shfl_up_sync(0xffffffffu, eo, o);
-      const uint32_t uc = __shfl_up_sync(0xffffffffu, co, o);
-      if (lane >= o) { eo += ue; co += uc; }
-    }
-    int sg = eo - ne;
-    uint32_t pre = co - (cnt2[0] + cnt2[1]);
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-      if (cnt2[h] > 0) {
-        s_lo[warp][sg] = lo2[h];
-        s_pre[warp][sg] = pre;
-        pre += cnt2[h];
-        ++sg;
-      }
-    if (lane == 31) s_pre[warp][eo] = co;
-    nsg = __shfl_sync(0xffffffffu, eo, 31);   // segments in all
-    __syncwarp();
-  }
+  const int nsg = blk_segments<T, P>(a, f, x0, y0, z0, xv, yv, zv, lane, s_lo[warp], s_pre[warp], s_bl[warp],
+                                     s_nb[warp]);
   const uint32_t ncand = s_pre[warp][nsg];
   const int xl = lane & 7, yl0 = lane >> 3, yl1 = yl0 + 4;
   TG acc0[8], acc1[8];
@@ -732,12 +783,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerSpreadCta, SOG_SPREAD_BLK_MINB) 
     bool rel = false;
     TG *w = s_w[warp][lane];   // this lane's candidate: x weights (times q), y, z
     if (ci < ncand) {
-      int lo = 0, hi = nsg - 1;
-      while (lo < hi) {   // last segment with s_pre <= ci
-        const int mid = (lo + hi + 1) >> 1;
-        if (s_pre[warp][mid] <= ci) lo = mid; else hi = mid - 1;
-      }
-      const uint32_t sidx = s_lo[warp][lo] + (ci - s_pre[warp][lo]);
+      const uint32_t sidx = blk_candidate(s_lo[warp], s_pre[warp], nsg, ci);
       const int4 an = a.s_anchor[sidx];
       const int anc[3] = {an.x, an.y, an.z};
       const int base[3] = {x0, y0, z0}, lim[3] = {xv, yv, zv}, nn[3] = {ag.nx, ag.ny, ag.nz};
@@ -788,6 +834,126 @@ __global__ void __launch_bounds__(32 * kWarpsPerSpreadCta, SOG_SPREAD_BLK_MINB) 
   const int64_t plane = (int64_t)ag.nx * ag.ny;
   TG *out = static_cast<TG *>(a.rho) + (int64_t)f * plane * a.zcnt;
   const TG scale = (TG)a.geom[f].scale;
+  if (xl < xv) {
+#pragma unroll
+    for (int z = 0; z < 8; ++z) {
+      if (z >= zv) break;
+      const int64_t zo = (int64_t)(z0 - a.zlo + z) * plane + x0 + xl;
+      if (yl0 < yv) out[zo + (int64_t)(y0 + yl0) * ag.nx] = acc0[z] * scale;
+      if (yl1 < yv) out[zo + (int64_t)(y0 + yl1) * ag.nx] = acc1[z] * scale;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------
+// Hessian-vector products: the direction density
+// ------------------------------------------------------------------------
+// The derivative of the charge mesh along a direction (a on the charges of
+// channel `channel`, b on the positions):
+//   drho(g) = (N_g / V) sum_j [a_j W_j(g) + q_j sum_x bt_jx dW_j/du_x(g)],
+//   bt_jx = n_x sum_c b_jc (cell^-1)_cx   (the direction in mesh units),
+// with the warp-per-block candidate walk and fixed summation order of
+// k_spread_blk.  A candidate's weight is the sum of three separable terms,
+//   (a w_x + q bt_x w_x') w_y w_z + w_x (q bt_y w_y') w_z + w_x w_y (q bt_z w_z'),
+// so a lane stages six rows of eight (rows of 49 words: odd, bank-spread).
+constexpr int kWarpsPerDipCta = 2;
+
+template <typename T, int P>
+__global__ void __launch_bounds__(32 * kWarpsPerDipCta) k_spread_dip(SpreadArgs<T> a, int nbx, int nby, int nbz,
+                                                                     int64_t nblk) {
+  __shared__ double s_w[kWarpsPerDipCta][32][49];
+  __shared__ uint32_t s_lo[kWarpsPerDipCta][18], s_pre[kWarpsPerDipCta][19];
+  __shared__ int s_bl[kWarpsPerDipCta][3][4];
+  __shared__ int s_nb[kWarpsPerDipCta][3];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t blk = (int64_t)blockIdx.x * kWarpsPerDipCta + warp;
+  if (blk >= nblk) return;   // the whole warp
+  const AtomGrid &ag = a.ag;
+  const int64_t per_f = (int64_t)nbx * nby * nbz;
+  const int f = (int)(blk / per_f);
+  int64_t rem = blk - (int64_t)f * per_f;
+  const int bz = (int)(rem / ((int64_t)nbx * nby));
+  rem -= (int64_t)bz * nbx * nby;
+  const int by = (int)(rem / nbx), bx = (int)(rem - (int64_t)by * nbx);
+  const int x0 = bx * 8, y0 = by * 8, z0 = a.zlo + bz * 8;
+  const int xv = min(8, ag.nx - x0), yv = min(8, ag.ny - y0), zv = min(8, a.zlo + a.zcnt - z0);
+  const int nsg = blk_segments<T, P>(a, f, x0, y0, z0, xv, yv, zv, lane, s_lo[warp], s_pre[warp], s_bl[warp],
+                                     s_nb[warp]);
+  const uint32_t ncand = s_pre[warp][nsg];
+  const FrameGeom &g = a.geom[f];
+  const double n3[3] = {(double)ag.nx, (double)ag.ny, (double)ag.nz};
+  const int xl = lane & 7, yl0 = lane >> 3, yl1 = yl0 + 4;
+  double acc0[8], acc1[8];
+#pragma unroll
+  for (int z = 0; z < 8; ++z) { acc0[z] = 0.0; acc1[z] = 0.0; }
+  for (uint32_t c0 = 0; c0 < ncand; c0 += 32) {
+    const uint32_t ci = c0 + lane;
+    bool rel = false;
+    double *w = s_w[warp][lane];   // rows: w_x, X, w_y, Y, w_z, Z
+    if (ci < ncand) {
+      const uint32_t sidx = blk_candidate(s_lo[warp], s_pre[warp], nsg, ci);
+      const int4 an = a.s_anchor[sidx];
+      const int anc[3] = {an.x, an.y, an.z};
+      const int base[3] = {x0, y0, z0}, lim[3] = {xv, yv, zv}, nn[3] = {ag.nx, ag.ny, ag.nz};
+      const int64_t atom = a.s_atom[sidx];
+      const double qv = (double)a.s_q[sidx];
+      const double av = ldir<T>(a.dir_q, atom * a.nch + a.channel);
+      double br[3], bt[3];
+#pragma unroll
+      for (int c = 0; c < 3; ++c) br[c] = ldir<T>(a.dir_r, atom * 3 + c);
+#pragma unroll
+      for (int ax = 0; ax < 3; ++ax)
+        bt[ax] = n3[ax] * (br[0] * g.cinv[0 * 3 + ax] + br[1] * g.cinv[1 * 3 + ax] + br[2] * g.cinv[2 * 3 + ax]);
+      bool has = true;
+#pragma unroll
+      for (int ax = 0; ax < 3; ++ax) {
+        double w1[P], d1[P];
+        const double t = (double)a.s_t[(int64_t)sidx * 3 + ax];
+        spline_w<double, P>(a.spline, t, w1, a.qc);
+        spline_dw<P>(a.spline, t, d1, a.qc);
+        const double cd = qv * bt[ax], cw = ax == 0 ? av : 0.0;
+        int k = base[ax] - anc[ax];
+        if (k < 0) k += nn[ax];
+        bool h = false;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          double vw = 0.0, vd = 0.0;
+#pragma unroll
+          for (int jj = 0; jj < P; ++jj) {
+            vw = (k == jj) ? w1[jj] : vw;
+            vd = (k == jj) ? d1[jj] : vd;
+          }
+          const bool in = i < lim[ax];
+          h |= (k < P && in);
+          w[ax * 16 + i] = in ? vw : 0.0;
+          w[ax * 16 + 8 + i] = in ? cw * vw + cd * vd : 0.0;
+          if (++k == nn[ax]) k = 0;
+        }
+        has = has && h;
+      }
+      rel = has;
+    }
+    unsigned mask = __ballot_sync(0xffffffffu, rel);
+    __syncwarp();
+    while (mask) {   // the relevant candidates in lane order
+      const int j = __ffs(mask) - 1;
+      mask &= mask - 1u;
+      const double *wj = s_w[warp][j];
+      const double wx = wj[xl], X = wj[8 + xl];
+      const double a0 = X * wj[16 + yl0] + wx * wj[24 + yl0], b0 = wx * wj[16 + yl0];
+      const double a1 = X * wj[16 + yl1] + wx * wj[24 + yl1], b1 = wx * wj[16 + yl1];
+#pragma unroll
+      for (int z = 0; z < 8; ++z) {
+        const double wzz = wj[32 + z], Zz = wj[40 + z];
+        acc0[z] += a0 * wzz + b0 * Zz;
+        acc1[z] += a1 * wzz + b1 * Zz;
+      }
+    }
+    __syncwarp();
+  }
+  const int64_t plane = (int64_t)ag.nx * ag.ny;
+  double *out = static_cast<double *>(a.rho) + (int64_t)f * plane * a.zcnt;
+  const double scale = g.scale;
   if (xl < xv) {
 #pragma unroll
     for (int z = 0; z < 8; ++z) {
@@ -982,12 +1148,24 @@ __device__ __forceinline__ double kernel_sum(const double *amp, const double *bw
   return K;
 }
 
+// Per-Gaussian factors of a mode without alias sums: exp(-bw2 k^2 / 2) times
+// the deconvolution D (gE) or alone (gS), and their bw2 derivatives.
+__device__ __forceinline__ void principal_em(double bw2m, double ksq, double D, double *em) {
+  const double e = exp(-0.5 * bw2m * ksq), h = -0.5 * ksq;
+  em[0] = e * D;
+  em[1] = e;
+  em[2] = h * em[0];
+  em[3] = h * e;
+  em[4] = h * em[2];
+  em[5] = h * em[3];
+}
+
 // B-spline alias sums of lmp/sog.cpp:1516-1578, pruned to the aliases that
 // can fall inside the k_max sphere (rarely taken, kept out of line).
 template <typename T>
 __device__ __noinline__ void alias_green(const KsArgs<T> &a, const FrameGeom &g, const double *amp,
                                          const double *bw2, int mx, int my, int mz, int iy, int iz,
-                                         int mfor, double *emD, double *emS, ModeGreen &r) {
+                                         int mfor, double *em, ModeGreen &r) {
   const double dl = a.sx[mx] * a.sy[iy] * a.sz[iz];
   const double denom = dl * dl;
   const int m3[3] = {mx, my, mz};
@@ -1003,7 +1181,8 @@ __device__ __noinline__ void alias_green(const KsArgs<T> &a, const FrameGeom &g,
   }
   const double w0 = sinc2p_dev(mx, a.nx, a.order, 0) * sinc2p_dev(my, a.ny, a.order, 0) *
                     sinc2p_dev(mz, a.nz, a.order, 0);
-  double s0 = 0.0, s1 = 0.0, sv = 0.0, eD = 0.0, eS = 0.0;
+  double s0 = 0.0, s1 = 0.0, sv = 0.0;
+  double e6[6] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
   for (int jx = jlo[0]; jx <= jhi[0]; ++jx)
     for (int jy = jlo[1]; jy <= jhi[1]; ++jy)
       for (int jz = jlo[2]; jz <= jhi[2]; ++jz) {
@@ -1019,27 +1198,33 @@ __device__ __noinline__ void alias_green(const KsArgs<T> &a, const FrameGeom &g,
         s0 += Kq * wp;
         s1 += (r.k[0] * q[0] + r.k[1] * q[1] + r.k[2] * q[2]) * Kq * wp;
         sv += Kvq * wp;
-        if (emD) {
+        if (em) {
+          // d/d bw2_m of an alias term brings its own -|q|^2 / 2
           const double e = exp(-0.5 * bw2[mfor] * qsq);
-          eD += e * wp / denom;
-          eS += (w0 > 1e-20) ? e * wp / w0 : 0.0;
+          const double eDq = e * wp / denom, eSq = (w0 > 1e-20) ? e * wp / w0 : 0.0;
+          const double h = -0.5 * qsq;
+          e6[0] += eDq; e6[1] += eSq;
+          e6[2] += h * eDq; e6[3] += h * eSq;
+          e6[4] += h * h * eDq; e6[5] += h * h * eSq;
         }
       }
   r.gE = s0 / denom;
   r.gF = s1 / (r.ksq * denom);
   r.gS = (w0 > 1e-20) ? s0 / w0 : 0.0;
   r.gV = sv / denom;
-  if (emD) { *emD = eD; *emS = eS; }
+  if (em)
+    for (int i = 0; i < 6; ++i) em[i] = e6[i];
 }
 
 // Green function of a mode; with `alias` the B-spline alias sums of
 // lmp/sog.cpp:1516-1578 (pruned to aliases inside the k_max sphere), else the
-// principal (separable) form.  If emD/emS are given, the per-Gaussian factors
-// d gE / d amp_m and d gS / d amp_m are returned too.
+// principal (separable) form.  If em is given, the per-Gaussian factors of
+// Gaussian mfor are returned too: em[0] = d gE / d amp_m, em[1] = d gS / d amp_m,
+// em[2..3] their first and em[4..5] their second derivatives w.r.t. bw2_m.
 template <typename T>
 __device__ ModeGreen mode_green(const KsArgs<T> &a, const FrameGeom &g, const double *amp,
-                                const double *bw2, int mx, int iy, int iz, int mfor, double *emD,
-                                double *emS, const double *bt = nullptr) {
+                                const double *bw2, int mx, int iy, int iz, int mfor, double *em,
+                                const double *bt = nullptr) {
   ModeGreen r;
   const int my = signed_mode(iy, a.ny), mz = signed_mode(iz, a.nz);
   for (int c = 0; c < 3; ++c)
@@ -1069,11 +1254,7 @@ __device__ ModeGreen mode_green(const KsArgs<T> &a, const FrameGeom &g, const do
     r.gE = r.gF = r.K * D;
     r.gS = r.K;
     r.gV = r.Kv * D;
-    if (emD) {
-      const double e = exp(-0.5 * bw2[mfor] * r.ksq);
-      *emD = e * D;
-      *emS = e;
-    }
+    if (em) principal_em(bw2[mfor], r.ksq, D, em);
     return r;
   }
   if (a.spline == SOG_SPLINE_QUADS) {
@@ -1083,11 +1264,7 @@ __device__ ModeGreen mode_green(const KsArgs<T> &a, const FrameGeom &g, const do
     r.gE = r.gF = r.K * D;
     r.gS = r.K;
     r.gV = r.Kv * D;
-    if (emD) {
-      const double e = exp(-0.5 * bw2[mfor] * r.ksq);
-      *emD = e * D;
-      *emS = e;
-    }
+    if (em) principal_em(bw2[mfor], r.ksq, D, em);
     return r;
   }
   if (!g.pad) {
@@ -1095,14 +1272,10 @@ __device__ ModeGreen mode_green(const KsArgs<T> &a, const FrameGeom &g, const do
     r.gE = r.gF = r.K * D;
     r.gS = r.K;
     r.gV = r.Kv * D;
-    if (emD) {
-      const double e = exp(-0.5 * bw2[mfor] * r.ksq);
-      *emD = e * D;
-      *emS = e;
-    }
+    if (em) principal_em(bw2[mfor], r.ksq, D, em);
     return r;
   }
-  alias_green<T>(a, g, amp, bw2, mx, my, mz, iy, iz, mfor, emD, emS, r);
+  alias_green<T>(a, g, amp, bw2, mx, my, mz, iy, iz, mfor, em, r);
   return r;
 }
 
@@ -1225,7 +1398,7 @@ __global__ void __launch_bounds__(256, 2) k_zfused(KsArgs<T> a, int ic, RadixPla
 #pragma unroll 1
   for (int e = 0; e < kEPT; ++e) {
     const int iz = t + e * TPT;
-    const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr, bt);
+    const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, bt);
     const bool live = ok && mg.live;
     const C r = s_rho[e * nthr + threadIdx.x];
     if (live) {
@@ -1375,7 +1548,7 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
       double *gfout = (g.pad && a.gtabF) ? a.gtabF + (int64_t)f * a.nh + col : nullptr;
       const double *bt = (g.ortho && a.btab) ? a.btab + (int64_t)f * a.btab_stride : nullptr;
       for (int iz = izb; iz < ize; ++iz) {
-        const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr, bt);
+        const ModeGreen mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, bt);
         gout[(int64_t)iz * inner] = mg.live ? mg.gE : 0.0;
         if (gfout) gfout[(int64_t)iz * inner] = mg.live ? mg.gF : 0.0;
         if (mg.live) accD += w * mg.gS;
@@ -1762,14 +1935,22 @@ __global__ void __launch_bounds__(256) k_kspace_extra(KsArgs<T> a, int want_grad
   }
   ModeGreen mg;
   mg.live = false;
-  if (valid) mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr, nullptr);
+  if (valid) mg = mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr);
   const bool live = valid && mg.live;
   if (want_grad) {
     for (int m = 0; m < M; ++m) {
       double eD = 0.0, eS = 0.0;
+      // bw2 derivatives: -k^2/2 times eD, eS, except with alias sums, whose
+      // terms carry their own |q|^2
+      double hD = -0.5 * mg.ksq, hS = hD;
       if (live) {
         if (a.spline == SOG_SPLINE_BSPLINE && g.pad) {
-          mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, m, &eD, &eS);
+          double em[6];
+          mode_green<T>(a, g, s_amp, s_bw2, mx, iy, iz, m, em);
+          eD = em[0];
+          eS = em[1];
+          hD = eD != 0.0 ? em[2] / eD : 0.0;
+          hS = eS != 0.0 ? em[3] / eS : 0.0;
         } else {
           const double e = exp(-0.5 * s_bw2[m] * mg.ksq);
           eS = e;
@@ -1786,11 +1967,10 @@ __global__ void __launch_bounds__(256) k_kspace_extra(KsArgs<T> a, int want_grad
           }
         }
       }
-      const double hk = -0.5 * mg.ksq * s_amp[m];
       const double v0 = warp_sum(live ? w * eD * rho2 : 0.0);
       const double v1 = warp_sum(live ? w * eS : 0.0);
-      const double v2 = warp_sum(live ? w * hk * eD * rho2 : 0.0);
-      const double v3 = warp_sum(live ? w * hk * eS : 0.0);
+      const double v2 = warp_sum(live ? w * (hD * s_amp[m]) * eD * rho2 : 0.0);
+      const double v3 = warp_sum(live ? w * (hS * s_amp[m]) * eS : 0.0);
       if (lane == 0) {
         red[warp][m] = v0;
         red[warp][M + m] = v1;
@@ -1823,6 +2003,101 @@ __global__ void __launch_bounds__(256) k_kspace_extra(KsArgs<T> a, int want_grad
     if (used)
       for (int wv = 0; wv < (int)(blockDim.x >> 5); ++wv) s += red[wv][i];
     p[i] = s;
+  }
+}
+
+// Hessian-vector product, k-space step of one channel (separable splines).
+// From the spectra of the mesh charge rho^ and of its derivative drho^ along
+// the direction: the potential spectra
+//   Phi^ = gE rho^ / N_g,   Psi^ = (gE drho^ + dgE rho^) / N_g,
+//   dgE = sum_m (da_m eD_m + amp_m db_m deD_m/dbw2_m)
+// in field slots 0 and 1 ([nf][2][nh]), and per block the parameter rows of
+// H d (scaled by V^2 / N_g^2: rho^ = (N_g / V) S(k), the structure factor the
+// shared finalize is written for) and, for channel 0, the self sums
+// D0..D2 = sum w eS_m (1, d/dbw2, d2/dbw2^2).  part: [nf][nch][blocks][5M].
+template <typename TP>
+__global__ void __launch_bounds__(256) k_kspace_hvp(KsArgs<double> a, const cplx_t<double> *__restrict__ dspec,
+                                                    const void *damp, const void *dbw2, int ch, int nch,
+                                                    double *__restrict__ part) {
+  __shared__ double s_amp[kMaxGauss], s_bw2[kMaxGauss], s_da[kMaxGauss], s_db[kMaxGauss];
+  __shared__ double red[8][5 * kMaxGauss];
+  const int f = blockIdx.y;
+  const int M = a.M;
+  for (int m = threadIdx.x; m < M; m += blockDim.x) {
+    s_amp[m] = kpar(a.amp, a.p32, m);
+    s_bw2[m] = kpar(a.bw2, a.p32, m);
+    s_da[m] = ldir<TP>(damp, (int64_t)f * M + m);
+    s_db[m] = ldir<TP>(dbw2, (int64_t)f * M + m);
+  }
+  __syncthreads();
+  const FrameGeom &g = a.geom[f];
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool valid = idx < a.nh;
+  int mx = 0, iy = 0, iz = 0;
+  cplx_t<double> r = {0.0, 0.0}, d = {0.0, 0.0};
+  double w = 0.0;
+  if (valid) {
+    mx = (int)(idx % a.nxh);
+    const int64_t zy = idx / a.nxh;
+    iy = (int)(zy % a.ny);
+    iz = (int)(zy / a.ny);
+    r = a.spec[(int64_t)f * a.nh + idx];
+    d = dspec[(int64_t)f * a.nh + idx];
+    w = (mx == 0 || ((a.nx & 1) == 0 && mx == a.nx / 2)) ? 1.0 : 2.0;
+  }
+  ModeGreen mg;
+  mg.live = false;
+  mg.gE = mg.ksq = 0.0;
+  if (valid) mg = mode_green<double>(a, g, s_amp, s_bw2, mx, iy, iz, 0, nullptr);
+  const bool live = valid && mg.live;
+  double Dfac = 0.0;   // deconvolution of the principal form
+  if (live && !(a.spline == SOG_SPLINE_BSPLINE && g.pad)) {
+    if (a.spline == SOG_SPLINE_QUADS) {
+      double infl = a.tx[mx] * a.ty[iy] * a.tz[iz];
+      if (infl < 1e-20) infl = 1e-20;
+      Dfac = 1.0 / infl;
+    } else {
+      Dfac = a.tx[mx] * a.ty[iy] * a.tz[iz];
+    }
+  }
+  const double rr = r.x * r.x + r.y * r.y, rd = 2.0 * (r.x * d.x + r.y * d.y);
+  double dG = 0.0;
+  for (int m = 0; m < M; ++m) {
+    double em[6] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
+    if (live) {
+      if (a.spline == SOG_SPLINE_BSPLINE && g.pad) mode_green<double>(a, g, s_amp, s_bw2, mx, iy, iz, m, em);
+      else principal_em(s_bw2[m], mg.ksq, Dfac, em);
+    }
+    dG += s_da[m] * em[0] + s_amp[m] * s_db[m] * em[2];
+    const double xa = warp_sum(w * (em[0] * rd + s_db[m] * em[2] * rr));
+    const double xb = warp_sum(w * (s_amp[m] * (em[2] * rd + s_db[m] * em[4] * rr) + s_da[m] * em[2] * rr));
+    const double d0 = warp_sum(ch == 0 ? w * em[1] : 0.0);
+    const double d1 = warp_sum(ch == 0 ? w * em[3] : 0.0);
+    const double d2 = warp_sum(ch == 0 ? w * em[5] : 0.0);
+    if (lane == 0) {
+      red[warp][m] = xa;
+      red[warp][M + m] = xb;
+      red[warp][2 * M + m] = d0;
+      red[warp][3 * M + m] = d1;
+      red[warp][4 * M + m] = d2;
+    }
+  }
+  if (valid) {
+    const double inv = 1.0 / ((double)a.nx * a.ny * a.nz);
+    const double gE = live ? mg.gE : 0.0;
+    cplx_t<double> *out = static_cast<cplx_t<double> *>(a.fspec) + (int64_t)f * 2 * a.nh + idx;
+    out[0] = cplx_t<double>{gE * inv * r.x, gE * inv * r.y};
+    out[a.nh] = cplx_t<double>{(gE * d.x + dG * r.x) * inv, (gE * d.y + dG * r.y) * inv};
+  }
+  __syncthreads();
+  const double vs = g.vol / ((double)a.nx * a.ny * a.nz);
+  const double v2 = vs * vs;
+  double *p = part + (((int64_t)f * nch + ch) * gridDim.x + blockIdx.x) * 5 * M;
+  for (int i = threadIdx.x; i < 5 * M; i += blockDim.x) {
+    double s = 0.0;
+    for (int wv = 0; wv < (int)(blockDim.x >> 5); ++wv) s += red[wv][i];
+    p[i] = i < 2 * M ? s * v2 : s;
   }
 }
 
@@ -1976,6 +2251,94 @@ __global__ void __launch_bounds__(256) k_gather_dedr(GatherArgs<T> a) {
     for (int ax = 0; ax < 3; ++ax) v += n3[ax] * g.cinv[b * 3 + ax] * g3[ax];
     v *= qn;
     if (a.accumulate) a.dedr[atom * 3 + b] += (T)v; else a.dedr[atom * 3 + b] = (T)v;
+  }
+}
+
+// Hessian-vector product, gather of one channel (separable splines): the
+// potential fields Phi (slot 0) and Psi (slot 1, [nf][ng][2]) over the
+// atom's stencil with the spline weights and their first and second
+// derivatives (u: mesh coordinates, J_cx = du_x / dr_c = n_x (cell^-1)_cx,
+// bt = J^T b the position direction in mesh units):
+//   (H d)_q  = norm [sum_g W Psi + sum_x bt_x G_x(Phi)]
+//   (H d)_r += norm J [a G(Phi) + q G(Psi) + q S(Phi) bt]
+// with G_x(f) = sum_g dW/du_x f and S_xy = sum_g d2W/du_x du_y Phi.  The
+// charge rows are written per channel, the position rows summed over the
+// channels (accumulate).
+template <typename T, int P>
+__global__ void __launch_bounds__(256) k_gather_hvp(GatherArgs<T> a, const double *__restrict__ fields,
+                                                    const void *dir_q, const void *dir_r, T *__restrict__ out_q,
+                                                    T *__restrict__ out_r) {
+  const int64_t si = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (si >= a.nslots) return;
+  const int64_t s = a.slot_lo + si;
+  const int4 an = a.s_anchor[s];
+  double w[3][P], dw[3][P], d2[3][P];
+#pragma unroll
+  for (int ax = 0; ax < 3; ++ax) {
+    const double t = (double)a.s_t[s * 3 + ax];
+    spline_w<double, P>(a.spline, t, w[ax], a.qc);
+    spline_dw<P>(a.spline, t, dw[ax], a.qc);
+    spline_d2w<P>(a.spline, t, d2[ax], a.qc);
+  }
+  const AtomGrid &ag = a.ag;
+  const double *base = fields + (int64_t)an.w * 2 * a.ng;
+  double sp = 0.0, gp[3] = {0.0, 0.0, 0.0}, gs[3] = {0.0, 0.0, 0.0};
+  double hs[6] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0};   // xx yy zz xy xz yz
+#pragma unroll 1
+  for (int c = 0; c < P; ++c) {
+    int gz = an.z + c;
+    if (gz >= ag.nz) gz -= ag.nz;
+#pragma unroll
+    for (int b = 0; b < P; ++b) {
+      int gy = an.y + b;
+      if (gy >= ag.ny) gy -= ag.ny;
+      const int64_t row = ((int64_t)gz * ag.ny + gy) * ag.nx;
+      const double wyz = w[1][b] * w[2][c], dyz = dw[1][b] * w[2][c], ydz = w[1][b] * dw[2][c];
+      const double yyz = d2[1][b] * w[2][c], yzz = w[1][b] * d2[2][c], dydz = dw[1][b] * dw[2][c];
+#pragma unroll
+      for (int k = 0; k < P; ++k) {
+        int gx = an.x + k;
+        if (gx >= ag.nx) gx -= ag.nx;
+        const double phi = base[(row + gx) * 2], psi = base[(row + gx) * 2 + 1];
+        const double wx = w[0][k], dx = dw[0][k];
+        sp += wx * wyz * psi;
+        gp[0] += dx * wyz * phi;
+        gp[1] += wx * dyz * phi;
+        gp[2] += wx * ydz * phi;
+        gs[0] += dx * wyz * psi;
+        gs[1] += wx * dyz * psi;
+        gs[2] += wx * ydz * psi;
+        hs[0] += d2[0][k] * wyz * phi;
+        hs[1] += wx * yyz * phi;
+        hs[2] += wx * yzz * phi;
+        hs[3] += dx * dyz * phi;
+        hs[4] += dx * ydz * phi;
+        hs[5] += wx * dydz * phi;
+      }
+    }
+  }
+  const FrameGeom &g = a.geom[an.w];
+  const double n3[3] = {(double)ag.nx, (double)ag.ny, (double)ag.nz};
+  const int64_t atom = a.s_atom[s];
+  const double qv = (double)a.s_q[s];
+  const double av = ldir<T>(dir_q, atom * a.nch + a.channel);
+  double br[3], bt[3];
+#pragma unroll
+  for (int c = 0; c < 3; ++c) br[c] = ldir<T>(dir_r, atom * 3 + c);
+#pragma unroll
+  for (int x = 0; x < 3; ++x)
+    bt[x] = n3[x] * (br[0] * g.cinv[0 * 3 + x] + br[1] * g.cinv[1 * 3 + x] + br[2] * g.cinv[2 * 3 + x]);
+  out_q[atom * a.nch + a.channel] = (T)(a.norm * (sp + bt[0] * gp[0] + bt[1] * gp[1] + bt[2] * gp[2]));
+  const double S[3][3] = {{hs[0], hs[3], hs[4]}, {hs[3], hs[1], hs[5]}, {hs[4], hs[5], hs[2]}};
+  double v[3];
+#pragma unroll
+  for (int x = 0; x < 3; ++x)
+    v[x] = av * gp[x] + qv * (gs[x] + S[x][0] * bt[0] + S[x][1] * bt[1] + S[x][2] * bt[2]);
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    const double o = a.norm * (n3[0] * g.cinv[c * 3 + 0] * v[0] + n3[1] * g.cinv[c * 3 + 1] * v[1] +
+                               n3[2] * g.cinv[c * 3 + 2] * v[2]);
+    if (a.accumulate) out_r[atom * 3 + c] += (T)o; else out_r[atom * 3 + c] = (T)o;
   }
 }
 
@@ -2969,6 +3332,178 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   return SOG_OK;
 }
 
+// Hessian-vector product of the mesh energy (B-spline and QuadS, whose
+// position gradient is the derivative of the spread weights).  Per channel:
+// the charge mesh and its derivative along the direction (k_spread_dip)
+// through the forward transforms, the k-space step k_kspace_hvp, the inverse
+// transforms of the two potential fields and the gather k_gather_hvp; then
+// the parameter rows and the self / k=0 / penalty terms by the finalize
+// kernels every solver shares.  Grids, spectra and fields are fp64 for
+// every plan.
+template <typename T>
+int mesh_hvp_impl(sog_plan *p, const sog_mesh_args *a, const sog_hvp_args *hv, cudaStream_t st) {
+  using CF = cplx_t<double>;
+  const int nf = a->nframes, nch = a->nchannels, M = a->n_gauss;
+  const int nx = p->d.nx, ny = p->d.ny, nz = p->d.nz, nxh = p->nxh, P = p->d.order;
+  const int64_t ng = p->ng, nh = p->nh;
+  Prep pr;
+  int rc = prepare_atoms<T>(p, a, st, pr);
+  if (rc != SOG_OK) return rc;
+  FrameGeom *geom = pr.geom;
+  const int64_t nslots = pr.nslots, maxat = pr.maxat;
+  Tracer *tr = &p->tr;
+  const unsigned kb = nblocks(nh, 256);
+  const int nw = 5 * M;
+  if (p->rho.reserve(sizeof(double) * ng * nf) || p->spec.reserve(sizeof(CF) * nh * nf) ||
+      p->hspec.reserve(sizeof(CF) * nh * nf) || p->fspec.reserve(sizeof(CF) * nh * nf * 2) ||
+      p->freal.reserve(sizeof(double) * ng * nf * 2) ||
+      p->hpart.reserve(sizeof(double) * nw * (int64_t)kb * nf * nch) || p->hred.reserve(sizeof(double) * nw * nf) ||
+      p->hdsum.reserve(sizeof(double) * 2 * nf * nch) || p->hscal.reserve(sizeof(double) * 8 * nf) ||
+      p->redtmp.reserve(sizeof(double) * std::max<int64_t>(1, reduce_tmp_elems(nf, 1, (int64_t)kb * nch, nw))))
+    return fail(SOG_ERR_NOMEM, "device allocation failed (mesh HVP)");
+
+  QuadsCoef qc;
+  std::memset(&qc, 0, sizeof(qc));
+  if (p->d.spline == SOG_SPLINE_QUADS) quads_coeffs(P, qc.c);
+  SpreadArgs<T> sa;
+  std::memset(&sa, 0, sizeof(sa));
+  sa.s_anchor = p->s_anchor.as<int4>();
+  sa.s_t = p->s_t.as<T>();
+  sa.bin_start = p->bin_start.as<uint32_t>();
+  sa.geom = geom;
+  sa.rho = p->rho.p;
+  sa.ag = pr.ag;
+  sa.spline = p->d.spline;
+  sa.ntx = (nx + kTileX - 1) / kTileX;
+  sa.nty = (ny + kTileY - 1) / kTileY;
+  sa.ntz = (nz + kTileZ - 1) / kTileZ;
+  sa.qc = qc;
+  sa.zlo = 0;
+  sa.zcnt = nz;
+  sa.dir_q = hv->dir_q;
+  sa.dir_r = hv->dir_r;
+  sa.s_atom = p->s_atom.as<int32_t>();
+  sa.nch = nch;
+
+  KsArgs<double> ka;
+  std::memset(&ka, 0, sizeof(ka));
+  ka.spec = p->spec.as<CF>();
+  ka.fspec = p->fspec.p;
+  ka.geom = geom;
+  ka.tx = p->tab.fx.as<double>(); ka.ty = p->tab.fy.as<double>(); ka.tz = p->tab.fz.as<double>();
+  ka.sx = p->tab.sx.as<double>(); ka.sy = p->tab.sy.as<double>(); ka.sz = p->tab.sz.as<double>();
+  ka.amp = a->amp;
+  ka.bw2 = a->bw2;
+  ka.p32 = p->d.dtype == SOG_DTYPE_F32;
+  ka.M = M;
+  ka.spline = p->d.spline;
+  ka.order = P;
+  ka.alias_extent = p->d.alias_extent;
+  ka.nx = nx; ka.ny = ny; ka.nz = nz; ka.nxh = nxh;
+  ka.nh = nh;
+  ka.nyl = ny;
+  ka.zblk = nz;
+  ka.nfield = 2;
+
+  GatherArgs<T> gar;
+  std::memset(&gar, 0, sizeof(gar));
+  gar.s_anchor = p->s_anchor.as<int4>();
+  gar.s_t = p->s_t.as<T>();
+  gar.s_atom = p->s_atom.as<int32_t>();
+  gar.nfield = 2;
+  gar.nslots = nslots;
+  gar.ng = ng;
+  gar.ag = pr.ag;
+  gar.spline = p->d.spline;
+  gar.qc = qc;
+  gar.norm = a->norm_factor;
+  gar.nch = nch;
+  gar.zwrap = nz;
+  gar.geom = geom;
+
+  set_fft_smem_attrs<double>();
+  auto forward = [&](CF *spec) {
+    pass_x_fwd<double>(p, p->rho.as<double>(), spec, (int64_t)nf * nz * ny, st);
+    pass_cols<double, -1>(p, spec, ny, nxh, (int64_t)nf * nz, p->rpy, tw_of<double>(p, 1), st, "fft_y_fwd");
+    pass_cols<double, -1>(p, spec, nz, (int64_t)ny * nxh, nf, p->rpz, tw_of<double>(p, 2), st, "fft_z_fwd");
+  };
+  const int nbx = (nx + 7) / 8, nby = (ny + 7) / 8, nbz = (nz + 7) / 8;
+  const int64_t nblk = (int64_t)nbx * nby * nbz * nf;
+  const unsigned dgrid = (unsigned)((nblk + kWarpsPerDipCta - 1) / kWarpsPerDipCta);
+  for (int c = 0; c < nch; ++c) {
+    sa.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
+    sa.channel = c;
+    dispatch_spread<T, double>(sa, P, nf, st, tr);
+    forward(p->spec.as<CF>());
+    if (dgrid) {
+      switch (P) {
+        case 4: k_spread_dip<T, 4><<<dgrid, 32 * kWarpsPerDipCta, 0, st>>>(sa, nbx, nby, nbz, nblk); break;
+        case 5: k_spread_dip<T, 5><<<dgrid, 32 * kWarpsPerDipCta, 0, st>>>(sa, nbx, nby, nbz, nblk); break;
+        default: k_spread_dip<T, 6><<<dgrid, 32 * kWarpsPerDipCta, 0, st>>>(sa, nbx, nby, nbz, nblk); break;
+      }
+      after(tr, st, "spread_dip");
+    }
+    forward(p->hspec.as<CF>());
+    k_kspace_hvp<T><<<dim3(kb, nf), 256, 0, st>>>(ka, p->hspec.as<CF>(), hv->dir_amp, hv->dir_bw2, c, nch,
+                                                  p->hpart.as<double>());
+    after(tr, st, "kspace_hvp");
+    pass_cols<double, +1>(p, p->fspec.as<CF>(), nz, (int64_t)ny * nxh, (int64_t)nf * 2, p->rpz,
+                          tw_of<double>(p, 2), st, "fft_z_inv");
+    pass_cols<double, +1>(p, p->fspec.as<CF>(), ny, nxh, (int64_t)nf * 2 * nz, p->rpy, tw_of<double>(p, 1), st,
+                          "fft_y_inv");
+    pass_x_inv<double>(p, p->fspec.as<CF>(), p->freal.as<double>(), nf, (int64_t)nz * ny, 2, st);
+    gar.s_q = p->s_q.as<T>() + (int64_t)c * nslots;
+    gar.channel = c;
+    gar.accumulate = c > 0;
+    const unsigned gb = nblocks(nslots, 256);
+    if (gb) {
+      const double *fl = p->freal.as<double>();
+      T *oq = (T *)hv->out_q, *orr = (T *)hv->out_r;
+      switch (P) {
+        case 4: k_gather_hvp<T, 4><<<gb, 256, 0, st>>>(gar, fl, hv->dir_q, hv->dir_r, oq, orr); break;
+        case 5: k_gather_hvp<T, 5><<<gb, 256, 0, st>>>(gar, fl, hv->dir_q, hv->dir_r, oq, orr); break;
+        default: k_gather_hvp<T, 6><<<gb, 256, 0, st>>>(gar, fl, hv->dir_q, hv->dir_r, oq, orr); break;
+      }
+      after(tr, st, "gather_hvp");
+    }
+  }
+  // the channels' block partials of a frame are contiguous: one reduction
+  reduce_parts(p->hpart.as<double>(), nf, 1, (int64_t)kb * nch, nw, nw, p->hred.as<double>(),
+               p->redtmp.as<double>(), st);
+  after(tr, st, "reduce", reduce_split((int64_t)kb * nch) > 1 ? 2 : 1);
+  k_hvp_dsums<T><<<dim3(nf, nch), 256, 0, st>>>((const T *)a->charges, hv->dir_q, nch, geom, p->hdsum.as<double>());
+  after(tr, st, "hvp_dsums");
+  HvpFinal hf;
+  hf.geom = geom;
+  hf.hred = p->hred.as<double>();
+  hf.qsum = p->qsum.as<double>();
+  hf.dsum = p->hdsum.as<double>();
+  hf.amp = a->amp;
+  hf.bw2 = a->bw2;
+  hf.damp = hv->dir_amp;
+  hf.dbw2 = hv->dir_bw2;
+  hf.oamp = hv->out_amp;
+  hf.obw2 = hv->out_bw2;
+  hf.scal = p->hscal.as<double>();
+  hf.M = M;
+  hf.nch = nch;
+  hf.norm = a->norm_factor;
+  hf.self_coeff = a->self_coeff;
+  hf.lambda = a->charge_neutral_lambda;
+  hf.remove_self = a->remove_self;
+  hf.k0 = a->k0_correction;
+  k_hvp_finalize_frames<T><<<nblocks(nf, 64), 64, 0, st>>>(hf, nf);
+  after(tr, st, "hvp_finalize_frames");
+  if (maxat > 0) {
+    k_hvp_finalize_atoms<T><<<dim3(nblocks(maxat, 256), nf), 256, 0, st>>>(
+        geom, p->hscal.as<double>(), p->hdsum.as<double>(), (const T *)a->charges, hv->dir_q, (T *)hv->out_q, nch,
+        a->norm_factor, a->charge_neutral_lambda);
+    after(tr, st, "hvp_finalize_atoms");
+  }
+  SOG_CUDA_TRY(cudaGetLastError());
+  return SOG_OK;
+}
+
 // ==========================================================================
 // z-slab decomposition of one frame over `size` ranks
 // ==========================================================================
@@ -3490,7 +4025,8 @@ extern "C" int sog_plan_destroy(sog_plan *p) {
                     &p->tab.sy, &p->tab.sz, &p->frames_host_dev, &p->geom, &p->status, &p->keys0,
                     &p->vals0, &p->keys1, &p->vals1, &p->hist, &p->scan_tmp, &p->bin_start,
                     &p->s_atom, &p->s_anchor, &p->s_t, &p->s_q, &p->qsum, &p->rho, &p->spec,
-                    &p->fspec, &p->freal, &p->partE, &p->partX, &p->red, &p->redtmp, &p->qpart, &p->btab, &p->gtab, &p->gtabF, &p->partD, &p->krad};
+                    &p->fspec, &p->freal, &p->partE, &p->partX, &p->red, &p->redtmp, &p->qpart, &p->btab, &p->gtab, &p->gtabF, &p->partD, &p->krad,
+                    &p->hspec, &p->hpart, &p->hred, &p->hdsum, &p->hscal};
   for (DevBuf *b : bufs) b->release();
   close_peers(p);
   p->xr_fwd.release();
@@ -3527,6 +4063,23 @@ extern "C" int sog_mesh_forward(sog_plan *p, const sog_mesh_args *a, void *strea
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (p->d.dtype == SOG_DTYPE_F64) return mesh_forward_impl<double>(p, a, st);
   return mesh_forward_impl<float>(p, a, st);
+}
+
+extern "C" int sog_mesh_hvp(sog_plan *p, const sog_mesh_args *a, const sog_hvp_args *h, void *stream) {
+  if (!p || !a || !h) return fail(SOG_ERR_INVALID, "null argument");
+  if (a->nframes <= 0) return SOG_OK;
+  if (!a->atom_begin || !a->atom_count || !a->k_sq_max || !a->positions || !a->charges || !a->cells ||
+      !a->amp || !a->bw2)
+    return fail(SOG_ERR_INVALID, "missing input array");
+  if (!h->out_q || !h->out_r || !h->out_amp || !h->out_bw2) return fail(SOG_ERR_INVALID, "missing HVP output array");
+  if (a->nchannels < 1) return fail(SOG_ERR_INVALID, "nchannels must be >= 1");
+  if (a->n_gauss < 1 || a->n_gauss > kMaxGauss) return fail(SOG_ERR_INVALID, "n_gauss must be in [1, 64]");
+  if (p->d.spline == SOG_SPLINE_CUBES2)
+    return fail(SOG_ERR_UNSUPPORTED, "second derivatives are computed for the B-spline and QuadS meshes");
+  DeviceGuard dg(p->d.device);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (p->d.dtype == SOG_DTYPE_F64) return mesh_hvp_impl<double>(p, a, h, st);
+  return mesh_hvp_impl<float>(p, a, h, st);
 }
 
 // Checks the slab constraints of a plan for `size` ranks ("" when valid).

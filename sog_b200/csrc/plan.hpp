@@ -87,6 +87,9 @@ struct sog_plan {
   sogb::DevBuf btab;            // per-axis kernel factors (orthorhombic frames)
   sogb::DevBuf gtab, gtabF, partD;  // Green tables and self-sum partials of the fused path
   sogb::DevBuf krad;                // radial kernel tables of cubic frames
+  // Hessian-vector products: direction spectrum, parameter / self partials,
+  // reduced rows, direction sums, per-frame scalars
+  sogb::DevBuf hspec, hpart, hred, hdsum, hscal;
   sogb::PinnedBuf up;
   sogb::Tracer tr;
   int nb_x = 0, nb_y = 0, nb_z = 0;  // sort bins per axis

@@ -202,10 +202,11 @@ def run_hvp(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Tensor
     single = len(spec.buckets) == 1 and spec.buckets[0].frames == list(range(nf))
     for b in spec.buckets:
         kind = b.kind or spec.kind
-        if kind not in ("direct", "realspace"):
+        if kind == "mesh" and (spec.slab is not None or spec.spline == _lib.SPLINE_CUBES2):
             raise NotImplementedError(
                 "second derivatives (create_graph=True through the forces or dE/dq) are implemented "
-                "for the direct k-sum and the real-space pair sum; the mesh solvers raise here")
+                "for the direct k-sum, the real-space pair sum and the B-spline / QuadS meshes "
+                "without slab decomposition; CubeS2 and slab solves raise here")
         if single:
             cells_b, da_b, db_b, oa_b, ob_b = spec.cells, damp, dbw2, out_a, out_b
         else:
@@ -216,13 +217,22 @@ def run_hvp(spec: SolveSpec, q: torch.Tensor, r: torch.Tensor, amp: torch.Tensor
             oa_b = torch.zeros(len(b.frames), M, dtype=dt, device=dev)
             ob_b = torch.zeros(len(b.frames), M, dtype=dt, device=dev)
         h = b.host()
-        ctx = _lib.direct_ctx(dev.index if dev.index is not None else torch.cuda.current_device(),
-                              _lib.dtype_code(dt))
+        device = dev.index if dev.index is not None else torch.cuda.current_device()
         # each bucket's atoms get their rows written; the others keep theirs
         common = dict(atom_begin=h["atom_begin"], atom_count=h["atom_count"], positions=r, charges=q,
                       amp=amp, bw2=bw2, norm_factor=spec.norm_factor, remove_self=spec.remove_self,
                       charge_neutral_lambda=spec.charge_neutral_lambda, dir_q=dq, dir_r=dr,
                       dir_amp=da_b, dir_bw2=db_b, out_q=out_q, out_r=out_r, out_amp=oa_b, out_bw2=ob_b)
+        if kind == "mesh":
+            plan = _lib.PLANS.get(device, _lib.dtype_code(dt), spec.spline, spec.order, b.dims, spec.kconv,
+                                  spec.alias_extent)
+            _lib.mesh_hvp(plan, k_sq_max=h["k_sq_max"], cells=cells_b, self_coeff=spec.self_coeff,
+                          k0_correction=spec.k0_correction, **common)
+            if not single:
+                out_a.index_copy_(0, idx, oa_b)
+                out_b.index_copy_(0, idx, ob_b)
+            continue
+        ctx = _lib.direct_ctx(device, _lib.dtype_code(dt))
         if kind == "realspace":
             _lib.realspace_hvp(ctx, **common)
         else:

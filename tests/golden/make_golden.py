@@ -408,7 +408,7 @@ def cfg3_case():
     print("cfg3_quads4", rec["energy"])
 
 
-def run_hvp_case(name, r, q, cell, batch, sog_args=None, gauss_kwargs=None, seed=0):
+def run_hvp_case(name, r, q, cell, batch, sog_args=None, gauss_kwargs=None, seed=0, mesh_order=0):
     """Second derivatives through the reference's direct k-sum (torch autograd
     with create_graph=True, as a force-matching loss needs them): forces F =
     -dE/dr and charge gradients P = dE/dq built with create_graph=True, then
@@ -419,6 +419,8 @@ def run_hvp_case(name, r, q, cell, batch, sog_args=None, gauss_kwargs=None, seed
         g = Sog(dict(sog_args)).gaussian
     else:
         g = Gaussian(**gauss_kwargs)
+    if mesh_order:
+        g._enable_batched_direct = False   # the reference's QuadS path, as test_batched_mixed.py does
     gen = torch.Generator().manual_seed(seed)
     rg = r.clone().requires_grad_(True)
     qg = q.clone().requires_grad_(True)
@@ -440,7 +442,7 @@ def run_hvp_case(name, r, q, cell, batch, sog_args=None, gauss_kwargs=None, seed
                lam=-1.0 if g.charge_neutral_lambda is None else float(g.charge_neutral_lambda),
                n_dl=-1.0 if g.n_dl is None else float(g.n_dl), e_w=e_w.numpy(), U=U.numpy(),
                W=W.numpy(), Z=Z.numpy(), loss=loss.detach().numpy(), grad_q=qg.grad.numpy(),
-               grad_r=rg.grad.numpy())
+               grad_r=rg.grad.numpy(), quads_order=int(mesh_order))
     if isinstance(g.amp, torch.nn.Parameter) and g.amp.grad is not None:
         rec["grad_amp"] = g.amp.grad.to(F64).numpy()
         rec["grad_bw2"] = g.bandwidth.grad.to(F64).numpy()
@@ -517,11 +519,45 @@ def hvp_cases():
                  sog_args={"use_atomwise": False, "r_cut": 5.0, "m": 8}, seed=4)
 
 
+def hvp_quads_cases():
+    """Second-derivative fixtures of the reference's QuadS mesh (torch
+    autograd through compute_quads_fft, quads_fft.py:209-326, with
+    create_graph=True); own generator."""
+    gen = torch.Generator().manual_seed(2029)
+    n = 20
+    cell = triclinic(9.0, 9.4, 8.8, 82.0, 96.0, 104.0).unsqueeze(0)
+    r = torch.rand(n, 3, generator=gen, dtype=F64) @ cell[0]
+    q = torch.rand(n, generator=gen, dtype=F64) - 0.5
+    q = q - q.mean()
+    run_hvp_case("hvp_quads4_triclinic", r, q, cell, torch.zeros(n, dtype=torch.int64),
+                 gauss_kwargs=dict(n_dl=1.2, amp=torch.tensor([0.7, 1.1, 1.4], dtype=F64),
+                                   bandwidth=torch.tensor([1.3, 2.1, 3.4], dtype=F64),
+                                   kernel_param_mode="internal", trainable=True,
+                                   use_quads_fft=True, quads_order=4), seed=8, mesh_order=4)
+    # two frames of different meshes, two channels, charged (k=0 term), self
+    # term kept, neutrality penalty
+    na, nb = 16, 13
+    cells = torch.stack([torch.eye(3, dtype=F64) * 9.0,
+                         torch.tensor([[8.5, 0.0, 0.0], [0.4, 9.6, 0.0], [-0.3, 0.5, 10.4]], dtype=F64)])
+    r = torch.cat([torch.rand(na, 3, generator=gen, dtype=F64) @ cells[0],
+                   torch.rand(nb, 3, generator=gen, dtype=F64) @ cells[1]])
+    q = torch.rand(na + nb, 2, generator=gen, dtype=F64) - 0.4
+    batch = torch.cat([torch.zeros(na, dtype=torch.int64), torch.ones(nb, dtype=torch.int64)])
+    amp4, bw4 = params_log(4, 1.2, 4.0)
+    run_hvp_case("hvp_quads6_2frames_2ch", r, q, cells, batch,
+                 gauss_kwargs=dict(n_dl=1.1, amp=amp4.clone(), bandwidth=bw4.clone(), trainable=True,
+                                   remove_self_interaction=False, charge_neutral_lambda=0.25,
+                                   use_quads_fft=True, quads_order=6), seed=9, mesh_order=6)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     if sys.argv[1:] == ["hvp"]:
         hvp_cases()
         hvp_realspace_cases()
+        hvp_quads_cases()
+    elif sys.argv[1:] == ["hvp_quads"]:
+        hvp_quads_cases()
     elif sys.argv[1:] == ["cfg3"]:
         cfg3_case()
     elif sys.argv[1:] == ["cubes2"]:

@@ -135,7 +135,7 @@ BSPLINE_CASES = [
     (6, np.eye(3) * 12.0, 60, 1, 0.7),
     (6, _tri(12.0, 12.6, 13.5, 80, 95, 105), 70, 2, 0.7),
     (4, _tri(11.0, 11.5, 12.0, 85, 100, 95), 50, 1, 0.9),
-    (6, np.diag([12.0, 9.0, 16.0]), 40, 1, 0.64),  # 2L/n_dl > N on one axis: alias sums
+    (6, np.diag([12.0, 8.94, 16.0]), 40, 1, 0.64),  # y mesh 27 < 2 L k_max / 2 pi: alias sums
 ]
 
 

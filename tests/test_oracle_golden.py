@@ -264,3 +264,35 @@ def test_oracle_position_gradient_matches_reference_autograd(name):
                                want_dedr=not cubes, kconv=1, remove_self=bool(c["remove_self"]))
             dedr[idx] += (-res["forces"] if cubes else res["dedr"]) * c["grad_weights"][f]
     assert np.abs(dedr - c["grad_r"]).max() < 1e-11
+
+
+@pytest.mark.parametrize("spline,cell", [
+    (O.BSPLINE, np.diag([12.0, 9.0, 16.0])),                                  # coarse: alias sums
+    (O.BSPLINE, np.array([[9.0, 0.0, 0.0], [0.7, 9.4, 0.0], [-0.5, 0.6, 8.8]])),
+    (O.QUADS, np.array([[9.0, 0.0, 0.0], [0.7, 9.4, 0.0], [-0.5, 0.6, 8.8]]))])
+def test_oracle_parameter_gradients_match_finite_differences(spline, cell):
+    """dE/d(amp, bw2) are the derivatives of the returned energy, including a
+    mesh too coarse for k_max, where every alias term of the B-spline Green
+    function brings its own |k + alias|^2 into the bw2 derivative."""
+    rng = np.random.default_rng(21 + spline)
+    n = 24
+    r = rng.random((n, 3)) @ cell
+    q = rng.standard_normal(n)
+    q -= q.mean()
+    amp, bw2 = np.array([0.9, 1.3, 0.7]), np.array([0.8, 1.9, 4.0])
+    grid, ksm = grid_ndl(cell, 0.8)
+    if cell[0, 0] == 12.0:
+        grid = (20, 15, 27)   # below 2 L k_max / 2 pi on every axis
+    kw = dict(spline=spline, order=6, nx=grid[0], ny=grid[1], nz=grid[2], k_sq_max=ksm, want_force=False)
+    res = O.mesh_solve(r, q, cell, amp, bw2, want_param_grad=True, **kw)
+    h = 1e-6
+    for m in range(3):
+        for arr, key in ((amp, "grad_amp"), (bw2, "grad_bw2")):
+            p, mm = arr.copy(), arr.copy()
+            p[m] += h
+            mm[m] -= h
+            args_p = (p, bw2) if key == "grad_amp" else (amp, p)
+            args_m = (mm, bw2) if key == "grad_amp" else (amp, mm)
+            fd = (O.mesh_solve(r, q, cell, *args_p, **kw)["energy"] -
+                  O.mesh_solve(r, q, cell, *args_m, **kw)["energy"]) / (2 * h)
+            assert abs(fd - res[key][m]) < 1e-7 * max(1.0, abs(fd)), (key, m)
