@@ -470,6 +470,14 @@ def run_gpu_batch(args, rank: int, world: int):
         if world > 1:
             dist.barrier()
 
+    def align_streams():
+        # after the host barrier the ranks leave at slightly different times;
+        # a one-element sum enqueued right before the first event lines up
+        # the GPUs' streams themselves, so the first timed step does not
+        # absorb the host-side release skew
+        if world > 1:
+            dist.all_reduce(torch.zeros(1, device=dev))
+
     def step_device():
         return gauss.compute_bundle(q=q_d, r=r_d, cell=c_d, batch=b_d, compute_force=True)
 
@@ -493,6 +501,7 @@ def run_gpu_batch(args, rank: int, world: int):
     gc.disable()
     barrier()
     torch.cuda.synchronize()
+    align_streams()
     l0 = _lib.launch_count()
     ev0.record(stream)
     h0 = time.perf_counter()
@@ -637,6 +646,14 @@ def run_gpu(args, rank: int, world: int):
         if world > 1:
             dist.barrier()
 
+    def align_streams():
+        # after the host barrier the ranks leave at slightly different times;
+        # a one-element sum enqueued right before the first event lines up
+        # the GPUs' streams themselves, so the first timed step does not
+        # absorb the host-side release skew
+        if world > 1:
+            dist.all_reduce(torch.zeros(1, device=dev))
+
     def step_device():
         return gauss.compute_bundle(q=q_d, r=r_d, cell=cell_d, compute_force=True)
 
@@ -696,6 +713,7 @@ def run_gpu(args, rank: int, world: int):
     gc.disable()          # no collector pause inside the timed steps
     barrier()
     torch.cuda.synchronize()
+    align_streams()
     if graph is not None:
         ev0.record(stream)
         h0 = time.perf_counter()

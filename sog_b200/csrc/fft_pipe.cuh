@@ -303,7 +303,10 @@ namespace sogb {
 // which covers the plain layout [outer][n][inner] (rb = n, olo = n*inner,
 // rstride = inner, cw = cstride = 1), the transposed blocks stored straight
 // into the peers' receive buffers (one base pointer per destination rank) in
-// the column-chunked layout, and those blocks read back in place.
+// the column-chunked layout, and those blocks read back in place.  rb, osplit
+// and cw are powers of two (slab sizes divide power-of-two axes): the
+// divisions are shifts (rb_sh, os_sh, cw_sh, set by with_shifts), since the
+// column passes evaluate this map for every element they move.
 // ---------------------------------------------------------------------------
 constexpr int kMaxSlabRanks = 8;
 
@@ -312,13 +315,29 @@ struct RowMap {
   C *tab[kMaxSlabRanks];
   int rb, osplit, cw;
   int64_t bstride, ohi, olo, rstride, cstride;
+  int rb_sh, os_sh, cw_sh;
   __device__ __forceinline__ C *at(int64_t o, int r, int64_t x) const {
-    const int b = r / rb;
-    const int64_t oh = o / osplit, xc = x / cw;
-    return tab[b] + b * bstride + oh * ohi + (o - oh * osplit) * olo + (int64_t)(r - b * rb) * rstride +
-           xc * cstride + (x - xc * cw);
+    const int b = r >> rb_sh;
+    const int64_t oh = o >> os_sh, xc = x >> cw_sh;
+    return tab[b] + b * bstride + oh * ohi + (o - (oh << os_sh)) * olo + (int64_t)(r - (b << rb_sh)) * rstride +
+           xc * cstride + (x - (xc << cw_sh));
   }
 };
+
+inline int log2_exact(int v) {
+  int s = 0;
+  while ((1 << s) < v) ++s;
+  return (1 << s) == v ? s : -1;
+}
+
+// the map with its shifts set; false if rb, osplit or cw is not a power of two
+template <typename C>
+inline bool with_shifts(RowMap<C> &m) {
+  m.rb_sh = log2_exact(m.rb);
+  m.os_sh = log2_exact(m.osplit);
+  m.cw_sh = log2_exact(m.cw);
+  return m.rb_sh >= 0 && m.os_sh >= 0 && m.cw_sh >= 0;
+}
 
 template <typename C>
 inline RowMap<C> plain_map(C *base, int n, int64_t inner) {
@@ -332,6 +351,7 @@ inline RowMap<C> plain_map(C *base, int n, int64_t inner) {
   m.olo = (int64_t)n * inner;
   m.rstride = inner;
   m.cstride = 1;
+  with_shifts(m);
   return m;
 }
 
@@ -355,9 +375,9 @@ __global__ void k_cols_map(RowMap<cplx_t<T>> in, RowMap<cplx_t<T>> out, int64_t 
   auto issue = [&](C *buf, int64_t tile) {
     const int64_t o = tile / nchunks;
     const int64_t i0 = (tile - o * nchunks) * ic;
-    const int total = n * ic;
+    const int total = n * ic, ic_sh = __ffs(ic) - 1;   // ic: a power of two
     for (int q = threadIdx.x; q < total; q += blockDim.x) {
-      const int r = q / ic, col = q - r * ic;
+      const int r = q >> ic_sh, col = q - (r << ic_sh);
       const bool ok = i0 + col < inner;
       const C *src = in.at(o, r, i0 + col);
       cp_async_elem(buf + q, ok ? src : in.tab[0], ok);

@@ -84,6 +84,24 @@ __host__ __device__ __forceinline__ uint32_t bin_row(const AtomGrid &ag, int bz,
 #ifndef SOG_SPREAD_BLK_MINB
 #define SOG_SPREAD_BLK_MINB 6
 #endif
+// threads per CTA of the fp64 column (y) passes: 256 (4 columns of a
+// 512-point axis per tile, 64-byte rows) or 512 (8 columns, 128-byte rows)
+#ifndef SOG_COLS_THR64
+#define SOG_COLS_THR64 256
+#endif
+// the same for the z-slab's row-mapped y passes, and the fused z tile of the
+// slab (256 threads: 4-column tiles, 64-byte peer-store runs; 512: 8 columns,
+// 128-byte runs, which measured slower over 8 ranks: 2.44 against 2.27 ms a
+// step for the 512^3 mesh)
+#ifndef SOG_SLAB_COLS_THR64
+#define SOG_SLAB_COLS_THR64 256
+#endif
+#ifndef SOG_SLAB_ZTHR
+#define SOG_SLAB_ZTHR 256
+#endif
+#ifndef SOG_SLAB_TWO_SLOT
+#define SOG_SLAB_TWO_SLOT 1
+#endif
 
 // Fractional coordinate along axis a (r @ cell^-1, then remainder 1.0) and the
 // anchor (first stencil node, wrapped) with the in-cell offset t
@@ -1797,10 +1815,10 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
 // field z = kz IFFT(Y2).  Slot 1, and slot 3 when it was not stored, have no
 // input and are skipped.  Other frames: a plain inverse transform of every
 // slot.  Same pipeline as k_cols_pipe.
-template <typename T, bool PAD, int L>
+template <typename T, bool PAD, int L, bool MAP = false>
 __global__ void k_cols_fields(cplx_t<T> *__restrict__ data, const FrameGeom *__restrict__ geom, int F, int nz,
                               int64_t inner, int ic, int64_t ntiles, const cplx_t<T> *__restrict__ tw,
-                              int two_slot, int want_pot) {
+                              int two_slot, int want_pot, RowMap<cplx_t<T>> in = {}, RowMap<cplx_t<T>> out = {}) {
   using C = cplx_t<T>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   constexpr int n = 1 << L, TPT = n / kEPT;
@@ -1822,14 +1840,30 @@ __global__ void k_cols_fields(cplx_t<T> *__restrict__ data, const FrameGeom *__r
     if (sl == 3 && g.pad) return 1;
     return 0;
   };
+  // tile loads: in place, or through the input row map (MAP: the z-slab's
+  // received blocks)
+  auto issue = [&](C *buf, int64_t tile) {
+    if constexpr (MAP) {
+      const int64_t o = tile / nchunks;
+      const int64_t i0 = (tile - o * nchunks) * ic;
+      const int ic_sh = __ffs(ic) - 1;   // ic: a power of two
+      for (int q = threadIdx.x; q < n * ic; q += blockDim.x) {
+        const int r = q >> ic_sh, col = q - (r << ic_sh);
+        const bool ok = i0 + col < inner;
+        cp_async_elem(buf + q, ok ? in.at(o, r, i0 + col) : in.tab[0], ok);
+      }
+    } else {
+      cols_issue<T>(buf, data, inner, n, ic, nchunks, tile);
+    }
+  };
   int64_t tile = blockIdx.x;
-  if (tile < ntiles && role(tile)) cols_issue<T>(buf0, data, inner, n, ic, nchunks, tile);
+  if (tile < ntiles && role(tile)) issue(buf0, tile);
   cp_async_commit();
   for (int it = 0; tile < ntiles; ++it, tile += gridDim.x) {
     C *cur = (it & 1) ? buf1 : buf0;
     C *nxt = (it & 1) ? buf0 : buf1;
     const int64_t next = tile + gridDim.x;
-    if (next < ntiles && role(next)) cols_issue<T>(nxt, data, inner, n, ic, nchunks, next);
+    if (next < ntiles && role(next)) issue(nxt, next);
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
@@ -1842,10 +1876,13 @@ __global__ void k_cols_fields(cplx_t<T> *__restrict__ data, const FrameGeom *__r
       const FrameGeom &g = geom[f];
       const bool okc = i0 + c < inner;
       const int mx = (int)(i0 + c);
-      const int64_t pl = (int64_t)n * inner;   // one z plane of one slot
-      C *base = data + o * pl + i0 + c;        // this slot
       const int64_t sl = fs - (int64_t)f * F;
-      C *slot0 = base - (sl * nz) * pl;        // slot 0 of the same (frame, z)
+      const int64_t o0 = o - sl * nz;          // plane of slot 0, same (frame, z)
+      // element e of this thread's column in plane `po` (slot k: po = o0 + k nz)
+      auto put = [&](int64_t po, int e, C val) {
+        if constexpr (MAP) *out.at(po, t + e * TPT, i0 + c) = val;
+        else data[po * ((int64_t)n * inner) + (int64_t)(t + e * TPT) * inner + i0 + c] = val;
+      };
       C v[kEPT];
 #pragma unroll
       for (int e = 0; e < kEPT; ++e) v[e] = cur[(t + e * TPT) * ic + c];
@@ -1853,26 +1890,22 @@ __global__ void k_cols_fields(cplx_t<T> *__restrict__ data, const FrameGeom *__r
       if (rl == 1) {
         if (okc) {
 #pragma unroll
-          for (int e = 0; e < kEPT; ++e) base[(int64_t)(t + e * TPT) * inner] = v[e];
+          for (int e = 0; e < kEPT; ++e) put(o, e, v[e]);
         }
       } else if (rl == 3) {
         const double kz = g.kmat[8];
         if (okc) {
 #pragma unroll
-          for (int e = 0; e < kEPT; ++e)
-            base[(int64_t)(t + e * TPT) * inner] = cmk<C, T>((T)(kz * (double)v[e].x), (T)(kz * (double)v[e].y));
+          for (int e = 0; e < kEPT; ++e) put(o, e, cmk<C, T>((T)(kz * (double)v[e].x), (T)(kz * (double)v[e].y)));
         }
       } else {
         const double kxm = g.kmat[0] * mx;
         if (okc) {
 #pragma unroll
-          for (int e = 0; e < kEPT; ++e)
-            slot0[(int64_t)(t + e * TPT) * inner] =
-                cmk<C, T>((T)(-kxm * (double)v[e].y), (T)(kxm * (double)v[e].x));
+          for (int e = 0; e < kEPT; ++e) put(o0, e, cmk<C, T>((T)(-kxm * (double)v[e].y), (T)(kxm * (double)v[e].x)));
           if (want_pot && !g.pad) {
-            C *p3 = slot0 + (int64_t)3 * nz * pl;
 #pragma unroll
-            for (int e = 0; e < kEPT; ++e) p3[(int64_t)(t + e * TPT) * inner] = v[e];
+            for (int e = 0; e < kEPT; ++e) put(o0 + 3 * (int64_t)nz, e, v[e]);
           }
         }
         // field y: ky IFFT(i my Y1), Y1 still in the tile buffer
@@ -1885,10 +1918,9 @@ __global__ void k_cols_fields(cplx_t<T> *__restrict__ data, const FrameGeom *__r
         ct_fft<T, +1, L, PAD>(v, t, stg, xbuf + c, ic);
         const double ky = g.kmat[4];
         if (okc) {
-          C *s1 = slot0 + (int64_t)nz * pl;
 #pragma unroll
           for (int e = 0; e < kEPT; ++e)
-            s1[(int64_t)(t + e * TPT) * inner] = cmk<C, T>((T)(ky * (double)v[e].x), (T)(ky * (double)v[e].y));
+            put(o0 + nz, e, cmk<C, T>((T)(ky * (double)v[e].x), (T)(ky * (double)v[e].y)));
         }
       }
     }
@@ -2730,7 +2762,7 @@ void pass_cols(sog_plan *p, cplx_t<T> *data, int n, int64_t inner, int64_t outer
     constexpr int nn = 1 << L;
     // fp32 columns are 8 bytes: 512-thread tiles keep each tile row of the
     // long axes at 64 bytes or more
-    constexpr int thr_cap = sizeof(T) == 4 ? 512 : 256;
+    constexpr int thr_cap = sizeof(T) == 4 ? 512 : SOG_COLS_THR64;
     const int ic = reg_width<T>(nn, thr_cap, thr_cap * 256);
     const int64_t nchunks = (inner + ic - 1) / ic;
     const int64_t ntiles = outer * nchunks;
@@ -2778,7 +2810,7 @@ void pass_cols_fields(sog_plan *p, cplx_t<T> *fspec, const FrameGeom *geom, int 
   with_pow2(ny, [&](auto lc) {
     constexpr int L = decltype(lc)::value;
     constexpr int nn = 1 << L;
-    constexpr int thr_cap = sizeof(T) == 4 ? 512 : 256;
+    constexpr int thr_cap = sizeof(T) == 4 ? 512 : SOG_COLS_THR64;
     const int ic = reg_width<T>(nn, thr_cap, thr_cap * 256);
     const int64_t ntiles = (int64_t)nf * F * nz * ((inner + ic - 1) / ic);
     const int thr = (nn / kEPT) * ic;
@@ -3620,13 +3652,16 @@ int peer_setup(sog_plan *p, const sog_slab_desc *sd, unsigned char *ws, const Sl
 
 // Row-mapped column FFT pass (power-of-two n only).
 template <typename T, int DIR>
-void pass_cols_map(sog_plan *p, const RowMap<cplx_t<T>> &in, const RowMap<cplx_t<T>> &out, int n, int64_t inner,
+void pass_cols_map(sog_plan *p, RowMap<cplx_t<T>> in, RowMap<cplx_t<T>> out, int n, int64_t inner,
                    int64_t outer, const cplx_t<T> *tw, cudaStream_t st, const char *name) {
   using C = cplx_t<T>;
+  with_shifts(in);
+  with_shifts(out);
   with_pow2(n, [&](auto lc) {
     constexpr int L = decltype(lc)::value;
     constexpr int nn = 1 << L;
-    const int ic = reg_width<T>(nn, 256, 64 * 1024);
+    constexpr int thr_cap = sizeof(T) == 4 ? 512 : SOG_SLAB_COLS_THR64;
+    const int ic = reg_width<T>(nn, thr_cap, thr_cap * 256);
     const int64_t ntiles = outer * ((inner + ic - 1) / ic);
     const int thr = (nn / kEPT) * ic;
     if (ic >= 8) {
@@ -3642,6 +3677,40 @@ void pass_cols_map(sog_plan *p, const RowMap<cplx_t<T>> &in, const RowMap<cplx_t
     }
   });
   after(&p->tr, st, name);
+}
+
+// Inverse y pass of the z-slab's received field spectra (k_cols_fields
+// through row maps): F slots of zs planes each, two-slot frames' fields formed
+// on the way (power-of-two ny only).
+template <typename T>
+void pass_cols_fields_map(sog_plan *p, RowMap<cplx_t<T>> in, RowMap<cplx_t<T>> out,
+                          const FrameGeom *geom, int F, int zs, int two_slot, int want_pot, cudaStream_t st) {
+  using C = cplx_t<T>;
+  with_shifts(in);
+  with_shifts(out);
+  const int64_t inner = p->nxh;
+  with_pow2(p->d.ny, [&](auto lc) {
+    constexpr int L = decltype(lc)::value;
+    constexpr int nn = 1 << L;
+    constexpr int thr_cap = sizeof(T) == 4 ? 512 : SOG_SLAB_COLS_THR64;
+    const int ic = reg_width<T>(nn, thr_cap, thr_cap * 256);
+    const int64_t ntiles = (int64_t)F * zs * ((inner + ic - 1) / ic);
+    const int thr = (nn / kEPT) * ic;
+    if (ic >= 8) {
+      const size_t sm = (3 * (size_t)nn * ic + nn) * sizeof(C);
+      allow_smem(k_cols_fields<T, false, L, true>);
+      k_cols_fields<T, false, L, true><<<persistent_grid(k_cols_fields<T, false, L, true>, thr, sm, ntiles), thr, sm,
+                                         st>>>(nullptr, geom, F, zs, inner, ic, ntiles, tw_of<T>(p, 1), two_slot,
+                                               want_pot, in, out);
+    } else {
+      const size_t sm = ((2 * (size_t)nn + padded_row(nn)) * ic + nn) * sizeof(C);
+      allow_smem(k_cols_fields<T, true, L, true>);
+      k_cols_fields<T, true, L, true><<<persistent_grid(k_cols_fields<T, true, L, true>, thr, sm, ntiles), thr, sm,
+                                        st>>>(nullptr, geom, F, zs, inner, ic, ntiles, tw_of<T>(p, 1), two_slot,
+                                              want_pot, in, out);
+    }
+  });
+  after(&p->tr, st, "fft_y_inv");
 }
 
 template <typename T>
@@ -3675,8 +3744,9 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
   };
   // spectrum rows of this rank after the transpose: plain [nz][ys][nxh], or
   // with the peer transport chunked into tiles of W = (fused z tile width)
-  // columns, [nz][nxh/W][ys][W], so that every tile a peer stores is contiguous
-  const int zic = reg_width<T>(nz, 256, 32 * 1024);
+  // columns, [nz][nxh/W][ys][W], so that every tile a peer stores is contiguous.
+  const bool z512 = SOG_SLAB_ZTHR == 512 && nz >= 512 && nz <= 1024;
+  const int zic = z512 ? reg_width<T>(nz, 512, 64 * 1024) : reg_width<T>(nz, 256, 32 * 1024);
   const int W = peer ? zic : 0;
   const int64_t inner_loc = peer ? (int64_t)((nxh + W - 1) / W) * ys * W : (int64_t)ys * nxh;
   if (peer) {
@@ -3745,6 +3815,9 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
   ka.nh = nh_loc;
   ka.nfield = nfield;
   ka.want_force = want_force;
+  // two-slot field spectra over the peer transport (orthorhombic frames):
+  // two thirds of the force fields' NVLink bytes
+  ka.two_slot = (SOG_SLAB_TWO_SLOT && peer && want_force && is_pow2(ny) && ny <= 1024) ? 1 : 0;
   ka.nx_acc = 4 * M + 13;
   ka.y0 = y0;
   ka.nyl = ys;
@@ -3849,9 +3922,15 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
         constexpr int n = 1 << Lz;
         const int zthr = (n / kEPT) * zic;
         const size_t zsm = ((2 * (size_t)n + padded_row(n)) * zic + n) * sizeof(C);
-        allow_smem(k_zfused_g<T, Lz>);
-        k_zfused_g<T, Lz><<<persistent_grid(k_zfused_g<T, Lz>, zthr, zsm, zchunks), zthr, zsm, st>>>(
-            ka, zic, zchunks, p->twz.as<C>(), write_spec);
+        if (zthr == 512) {
+          allow_smem(k_zfused_g<T, Lz, 512>);
+          k_zfused_g<T, Lz, 512><<<persistent_grid(k_zfused_g<T, Lz, 512>, zthr, zsm, zchunks), zthr, zsm, st>>>(
+              ka, zic, zchunks, p->twz.as<C>(), write_spec);
+        } else {
+          allow_smem(k_zfused_g<T, Lz>);
+          k_zfused_g<T, Lz><<<persistent_grid(k_zfused_g<T, Lz>, zthr, zsm, zchunks), zthr, zsm, st>>>(
+              ka, zic, zchunks, p->twz.as<C>(), write_spec);
+        }
       });
       if (!done) return fail(SOG_ERR_UNSUPPORTED, "slab mode needs a power-of-two nz up to 1024");
       after(tr, st, "zfused");
@@ -3873,7 +3952,10 @@ int mesh_slab_impl(sog_plan *p, const sog_mesh_args *a, const sog_slab_desc *sd,
         in.cw = W;
         in.cstride = (int64_t)ys * zs * W;               // column chunk xc
         const RowMap<C> out = plain_map(p->fspec.as<C>(), ny, nxh);
-        pass_cols_map<T, +1>(p, in, out, ny, nxh, (int64_t)nfield * zs, p->twy.as<C>(), st, "fft_y_inv");
+        if (ka.two_slot)
+          pass_cols_fields_map<T>(p, in, out, geom, nfield, zs, 1, want_pot ? 1 : 0, st);
+        else
+          pass_cols_map<T, +1>(p, in, out, ny, nxh, (int64_t)nfield * zs, p->twy.as<C>(), st, "fft_y_inv");
         pass_x_inv<T>(p, p->fspec.as<C>(), fields, 1, (int64_t)zs * ny, nfield, st);
         // first order-1 planes to the halo of rank r-1
         const int prev = (rank + size - 1) % size;
