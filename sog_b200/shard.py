@@ -125,9 +125,13 @@ class FrameShards:
         return out
 
     def gather_energy(self, e_local: torch.Tensor, group=None) -> torch.Tensor:
-        """Per-frame results of every rank -> the full [nframes, ...] tensor."""
+        """Per-frame results of every rank -> the full [nframes, ...] tensor.
+        Forward values only: the gathered tensor carries no autograd graph, so
+        a loss is backpropagated on each rank's own local outputs (the
+        gradient of a data-parallel sum of per-rank losses)."""
         return self._gather(e_local, self.max_frames, self._fsel, self._fdst, self.nframes, group)
 
     def gather_atoms(self, x_local: torch.Tensor, group=None) -> torch.Tensor:
-        """Per-atom results (forces, dE/dq) of every rank -> [natoms, ...]."""
+        """Per-atom results (forces, dE/dq) of every rank -> [natoms, ...].
+        Forward values only, as gather_energy."""
         return self._gather(x_local, self.max_atoms, self._asel, self._adst, self.natoms, group)
