@@ -687,10 +687,12 @@ __global__ void __launch_bounds__(kSpreadThreads, NT == 1 ? SOG_SPREAD_MINB : 2)
 // ------------------------------------------------------------------------
 // A warp owns one block and writes each of its points once.  Its candidates
 // are the cell-sorted atoms of the (at most 3 x 3 x 3) bins that hold the
-// anchors able to reach the block; lane i takes candidate i of a chunk of 32,
-// evaluates its spline weights (fp64) at the block's 8 x, 8 y and 8 z
-// points (zero where the stencil does not reach), the relevant ones are
-// compacted in lane order, and every lane then adds them, in that order, to
+// anchors able to reach the block; lanes test 32 candidates at a time from
+// their anchors alone and append the relevant ones (stencil reaching the
+// block on every axis, about a third of them) to a list in candidate order.
+// For each 32 listed candidates, lane j evaluates candidate j's spline
+// weights (fp64) at the block's 8 x, 8 y and 8 z points (zero where the
+// stencil does not reach), and every lane then adds them, in list order, to
 // its 2 x 8 points (x = lane % 8, y = lane / 8 and lane / 8 + 4, all z).  So
 // the summation order at every point is the fixed candidate order: bitwise
 // reproducible, no atomics, and no block-wide barriers (the warps of a CTA
@@ -773,6 +775,7 @@ __global__ void __launch_bounds__(32 * kWarpsPerSpreadCta, SOG_SPREAD_BLK_MINB) 
   // per warp and lane: a candidate's x (times q), y, z weights; rows of 25
   // (odd) words so that the lanes' rows start in different banks
   __shared__ TG s_w[kWarpsPerSpreadCta][32][25];
+  __shared__ uint32_t s_rel[kWarpsPerSpreadCta][64];
   __shared__ uint32_t s_lo[kWarpsPerSpreadCta][kSeg], s_pre[kWarpsPerSpreadCta][kSeg + 1];
   __shared__ int s_bl[kWarpsPerSpreadCta][3][4];
   __shared__ int s_nb[kWarpsPerSpreadCta][3];
@@ -793,20 +796,19 @@ __global__ void __launch_bounds__(32 * kWarpsPerSpreadCta, SOG_SPREAD_BLK_MINB) 
                                      s_nb[warp]);
   const uint32_t ncand = s_pre[warp][nsg];
   const int xl = lane & 7, yl0 = lane >> 3, yl1 = yl0 + 4;
+  const int base[3] = {x0, y0, z0}, lim[3] = {xv, yv, zv}, nn[3] = {ag.nx, ag.ny, ag.nz};
   TG acc0[8], acc1[8];
 #pragma unroll
   for (int z = 0; z < 8; ++z) { acc0[z] = TG(0); acc1[z] = TG(0); }
-  for (uint32_t c0 = 0; c0 < ncand; c0 += 32) {
-    const uint32_t ci = c0 + lane;
-    bool rel = false;
-    TG *w = s_w[warp][lane];   // this lane's candidate: x weights (times q), y, z
-    if (ci < ncand) {
-      const uint32_t sidx = blk_candidate(s_lo[warp], s_pre[warp], nsg, ci);
+  // Weights of the first cnt relevant candidates (lane j: candidate j), then
+  // their sums into this lane's points in list order.
+  auto flush = [&](int cnt) {
+    if (lane < cnt) {
+      const uint32_t sidx = s_rel[warp][lane];
       const int4 an = a.s_anchor[sidx];
       const int anc[3] = {an.x, an.y, an.z};
-      const int base[3] = {x0, y0, z0}, lim[3] = {xv, yv, zv}, nn[3] = {ag.nx, ag.ny, ag.nz};
       const double qv = (double)a.s_q[sidx];
-      bool has = true;
+      TG *w = s_w[warp][lane];   // x weights (times q), y, z
 #pragma unroll
       for (int ax = 0; ax < 3; ++ax) {
         double w1[P];
@@ -815,29 +817,21 @@ __global__ void __launch_bounds__(32 * kWarpsPerSpreadCta, SOG_SPREAD_BLK_MINB) 
 #pragma unroll
           for (int jj = 0; jj < P; ++jj) w1[jj] *= qv;
         }
-        // stencil offset of block point 0 (both in [0, n)), then one step per point
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[ax * 8 + i] = TG(0);
+        // stencil node jj sits at block point (jj - k) mod n
         int k = base[ax] - anc[ax];
         if (k < 0) k += nn[ax];
-        bool h = false;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          double v = 0.0;
-#pragma unroll
-          for (int jj = 0; jj < P; ++jj) v = (k == jj) ? w1[jj] : v;
-          const bool in = i < lim[ax];
-          h |= (k < P && in);
-          w[ax * 8 + i] = (TG)(in ? v : 0.0);
-          if (++k == nn[ax]) k = 0;
+        for (int jj = 0; jj < P; ++jj) {
+          int i = jj - k;
+          if (i < 0) i += nn[ax];
+          if (i < lim[ax]) w[ax * 8 + i] = (TG)w1[jj];
         }
-        has = has && h;
       }
-      rel = has;
     }
-    unsigned mask = __ballot_sync(0xffffffffu, rel);
     __syncwarp();
-    while (mask) {   // the relevant candidates in lane order
-      const int j = __ffs(mask) - 1;
-      mask &= mask - 1u;
+    for (int j = 0; j < cnt; ++j) {
       const TG *wj = s_w[warp][j];
       const TG a0 = wj[xl] * wj[8 + yl0], a1 = wj[xl] * wj[8 + yl1];
 #pragma unroll
@@ -848,7 +842,41 @@ __global__ void __launch_bounds__(32 * kWarpsPerSpreadCta, SOG_SPREAD_BLK_MINB) 
       }
     }
     __syncwarp();
+  };
+  // Relevant candidates (stencil reaches the block on every axis: the offset
+  // k of block point 0 is below P, or the block wraps onto node 0), decided
+  // from the anchors alone and listed in candidate order; weights are
+  // computed for listed candidates only, 32 at a time.
+  const unsigned lt = (1u << lane) - 1u;
+  int nrel = 0;
+  for (uint32_t c0 = 0; c0 < ncand; c0 += 32) {
+    const uint32_t ci = c0 + lane;
+    bool rel = false;
+    uint32_t sidx = 0;
+    if (ci < ncand) {
+      sidx = blk_candidate(s_lo[warp], s_pre[warp], nsg, ci);
+      const int4 an = a.s_anchor[sidx];
+      const int anc[3] = {an.x, an.y, an.z};
+      rel = true;
+#pragma unroll
+      for (int ax = 0; ax < 3; ++ax) {
+        int k = base[ax] - anc[ax];
+        if (k < 0) k += nn[ax];
+        rel = rel && (k < P || k > nn[ax] - lim[ax]);
+      }
+    }
+    const unsigned mask = __ballot_sync(0xffffffffu, rel);
+    if (rel) s_rel[warp][nrel + __popc(mask & lt)] = sidx;
+    nrel += __popc(mask);
+    __syncwarp();
+    if (nrel >= 32) {
+      flush(32);
+      if (lane < nrel - 32) s_rel[warp][lane] = s_rel[warp][32 + lane];   // disjoint halves
+      nrel -= 32;
+      __syncwarp();
+    }
   }
+  if (nrel > 0) flush(nrel);
   const int64_t plane = (int64_t)ag.nx * ag.ny;
   TG *out = static_cast<TG *>(a.rho) + (int64_t)f * plane * a.zcnt;
   const TG scale = (TG)a.geom[f].scale;
