@@ -187,22 +187,26 @@ def algorithmic_bytes(cfg, s: int = 8, nfield: int = 3, parts: int = 1):
 
 
 def profiled_traffic(kernel: str, config: str):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary of the
-    512^3 workload (profiles/dram_mesh512_bspline6.md), or None.  This is a
-    figure copied from that capture, not a measurement of the current run;
-    the JSON line says so next to it."""
+    """DRAM bytes per launch of `kernel` at 512^3 from the committed ncu
+    summary (profiles/dram_mesh256x256x512_bspline6.md: captured on the
+    quarter-size profiling case, scaled by the algorithmic-bytes ratio), or
+    None.  A figure copied from that capture, not a measurement of the
+    current run; the JSON line says so next to it."""
     if config != "cfg5":
         return None
-    p = os.path.join(ROOT, "profiles", "dram_mesh512_bspline6.md")
+    p = os.path.join(ROOT, "profiles", TRAFFIC_PROFILE)
     try:
         with open(p) as f:
             for line in f:
                 cells = [c.strip().strip("`") for c in line.strip().strip("|").split("|")]
-                if len(cells) >= 5 and cells[1] == kernel:
-                    return float(cells[4]) * 1e9
+                if len(cells) >= 10 and cells[1] == kernel:
+                    return float(cells[9]) * 1e9
     except (OSError, ValueError):
         return None
     return None
+
+
+TRAFFIC_PROFILE = "dram_mesh256x256x512_bspline6.md"
 
 
 def host_cores() -> int:
@@ -868,8 +872,9 @@ def run_gpu(args, rank: int, world: int):
         roof = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
                 "frac": ach / peak, "peak_source": f"{peak_kind} hbm_gbs",
                 "traffic": traffic,
-                "traffic_source": ("ncu capture committed in profiles/dram_mesh512_bspline6.md "
-                                   "(one launch of this kernel at this size; not measured in this run)"
+                "traffic_source": (f"ncu capture committed in profiles/{TRAFFIC_PROFILE} (one launch "
+                                   "of this kernel on the quarter-size 256x256x512 case, scaled to this "
+                                   "size by its algorithmic bytes; not measured in this run)"
                                    if traffic is not None else None),
                 "algorithmic_bytes_per_launch": per_kernel[dom],
                 "largest_stream_time": {"name": top, "share": kernels[top]["share"]}}
