@@ -99,6 +99,13 @@ __host__ __device__ __forceinline__ uint32_t bin_row(const AtomGrid &ag, int bz,
 #ifndef SOG_SLAB_ZTHR
 #define SOG_SLAB_ZTHR 256
 #endif
+// fused z tile of the single-device path for 512 and 1024 points: 256
+// threads (4 columns, two CTAs per SM) or 512 (8 columns, 128-byte field
+// rows, one CTA per SM).  With the two-slot output the 256-thread tile is
+// faster at 512^3 (1.90 against 2.06 ms).
+#ifndef SOG_ZTHR
+#define SOG_ZTHR 256
+#endif
 #ifndef SOG_SLAB_TWO_SLOT
 #define SOG_SLAB_TWO_SLOT 1
 #endif
@@ -1615,9 +1622,9 @@ __global__ void __launch_bounds__(256) k_green(KsArgs<T> a) {
 // table: forward z-FFT of ic spectrum columns, energy partial sum, and for
 // every field the scaled spectrum (i k_a gF rho / N or gE rho / N) inverse
 // z-transformed.  Spectrum and gE tiles are double-buffered with cp.async.
-// NTH threads per CTA: 512 for a 512-point z transform gives tiles of 8
-// columns, so every field row it stores is 128 contiguous bytes (4-column
-// rows of 64 bytes store at half the bandwidth).
+// NTH threads per CTA: 256 (two CTAs per SM) or 512 (tiles of 8 columns of
+// a 512-point transform, so that every field row it stores is 128
+// contiguous bytes); see SOG_ZTHR.
 template <typename T, int L, int NTH = 256, typename TO = T>
 __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfused_g(KsArgs<T> a, int ic,
                                                                                   int64_t ntiles,
@@ -3261,7 +3268,7 @@ int mesh_forward_impl(sog_plan *p, const sog_mesh_args *a, cudaStream_t st) {
   // two-slot field spectra (fused z pass -> k_cols_fields) for power-of-two ny
   ka.two_slot = (zfuse && !zgeneric && want_force && is_pow2(ny) && ny <= 1024) ? 1 : 0;
   // fused z pass: 512 threads (8-column tiles) for 512 and 1024 points
-  const int zic = zfuse ? (nz >= 512 && nz <= 1024 ? reg_width<TF>(nz, 512, 64 * 1024)
+  const int zic = zfuse ? (SOG_ZTHR == 512 && nz >= 512 && nz <= 1024 ? reg_width<TF>(nz, 512, 64 * 1024)
                                                    : reg_width<TF>(nz, 256, 32 * 1024))
                         : 0;
   const int64_t zchunks = zfuse ? ((int64_t)ny * nxh + zic - 1) / zic : 0;
