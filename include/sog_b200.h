@@ -59,6 +59,8 @@ extern "C" {
 /* plan status bits (sog_plan_status) */
 #define SOG_STATUS_NONFINITE 1u /* a position or charge was NaN/Inf           */
 #define SOG_STATUS_BAD_CELL 2u  /* a cell had |det| <= eps                    */
+#define SOG_STATUS_WAIT_TIMEOUT 4u /* a kernel's wait for its own tile copies ran
+                                      out of time (one second); results invalid */
 
 SOG_API const char *sog_strerror(int code);
 /* Text of the last failure on this thread (empty string if none). */

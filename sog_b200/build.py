@@ -19,7 +19,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT_DIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(OUT_DIR, "libsog_b200.so")
-SOURCES = ["plan.cu", "mesh.cu", "direct.cu", "realspace.cu"]
+SOURCES = ["plan.cu", "mesh.cu", "fft_tma.cu", "direct.cu", "realspace.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -63,6 +63,7 @@ struct FrameHost {
 enum : unsigned {
   kStatusNonFinite = 1u << 0,
   kStatusBadCell = 1u << 1,
+  kStatusWaitTimeout = 1u << 2,
 };
 
 __device__ __forceinline__ void raise_status(unsigned *status, unsigned bit) {

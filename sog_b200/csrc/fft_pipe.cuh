@@ -154,7 +154,7 @@ __global__ void k_r2c_pipe(const T *__restrict__ in, cplx_t<T> *__restrict__ out
     }
     // a row's TPT threads are consecutive lanes of one warp when TPT <= 32
     constexpr bool kWarpRow = TPT <= 32;
-    ct_fft<T, -1, L - 1, true, 1, kWarpRow>(v, t, stg, zrow, 1);
+    ct_fft<T, -1, L - 1, true, 1, kWarpRow, true>(v, t, stg, zrow, 1);
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) zrow[sidx<true>(t + e * TPT, 1)] = v[e];
     xsync<kWarpRow>();

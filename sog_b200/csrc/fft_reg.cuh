@@ -147,8 +147,40 @@ __device__ __forceinline__ void xsync() {
   else __syncthreads();
 }
 
+// Twiddles of one butterfly, w_r = W^{r k step}, r = 1 .. R-1.  With POW
+// (fp64 only) w_1 comes from the stage table and the other powers are formed
+// by squaring and multiplying (w2 = w1^2, w3 = w2 w1, w4 = w2^2, w5 = w4 w1,
+// w6 = w3^2, w7 = w6 w1: at most three roundings deep, a few ulp), so a
+// radix-8 butterfly reads one 16-byte table entry instead of seven.  It trades
+// shared-memory bandwidth for fp64 products and about 10-45 registers a
+// thread, so only kernels where that measured faster (x forward, fused z) ask
+// for it; the others read every power from the table.
+template <typename T, int DIR, int R, bool POW>
+__device__ __forceinline__ void stage_twiddles(cplx_t<T> (&w)[R], const cplx_t<T> *row1, int NS) {
+  if constexpr (sizeof(T) == 8 && POW) {
+    w[1] = row1[0];
+    if (DIR > 0) w[1].y = -w[1].y;
+    if constexpr (R > 2) {
+      w[2] = cmul(w[1], w[1]);
+      w[3] = cmul(w[2], w[1]);
+    }
+    if constexpr (R > 4) {
+      w[4] = cmul(w[2], w[2]);
+      w[5] = cmul(w[4], w[1]);
+      w[6] = cmul(w[3], w[3]);
+      w[7] = cmul(w[6], w[1]);
+    }
+  } else {
+#pragma unroll
+    for (int r = 1; r < R; ++r) {
+      w[r] = row1[(r - 1) * NS];
+      if (DIR > 0) w[r].y = -w[r].y;
+    }
+  }
+}
+
 // stg: the stage table of the 2^L transform (load_stage_twiddles).
-template <typename T, int DIR, int L, int S, bool PAD, int TWS, bool WSYNC = false>
+template <typename T, int DIR, int L, int S, bool PAD, int TWS, bool WSYNC = false, bool TWP = false>
 __device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx_t<T> *stg,
                                          cplx_t<T> *sbase, int sj) {
   using PP = Pow2Plan<L>;
@@ -166,12 +198,10 @@ __device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx
 #pragma unroll
     for (int r = 0; r < R; ++r) a[r] = v[u + r * B];
     if (S > 0) {
+      cplx_t<T> w[R];
+      stage_twiddles<T, DIR, R, TWP>(w, stg + StageTw<L>::off(S) + k, NS);
 #pragma unroll
-      for (int r = 1; r < R; ++r) {
-        cplx_t<T> w = stg[StageTw<L>::off(S) + (r - 1) * NS + k];
-        if (DIR > 0) w.y = -w.y;
-        a[r] = cmul(a[r], w);
-      }
+      for (int r = 1; r < R; ++r) a[r] = cmul(a[r], w[r]);
     }
     dftR<T, DIR, R>(a);
     if (LAST) {
@@ -191,12 +221,13 @@ __device__ __forceinline__ void ct_stage(cplx_t<T> (&v)[kEPT], int t, const cplx
   }
 }
 
-template <typename T, int DIR, int L, bool PAD, int TWS = 0, bool WSYNC = false, int S = 0>
+// TWP: twiddle powers formed in registers (stage_twiddles)
+template <typename T, int DIR, int L, bool PAD, int TWS = 0, bool WSYNC = false, bool TWP = false, int S = 0>
 __device__ __forceinline__ void ct_fft(cplx_t<T> (&v)[kEPT], int t, const cplx_t<T> *stg, cplx_t<T> *sbase,
                                        int sj) {
   if constexpr (S < Pow2Plan<L>::NST) {
-    ct_stage<T, DIR, L, S, PAD, TWS, WSYNC>(v, t, stg, sbase, sj);
-    ct_fft<T, DIR, L, PAD, TWS, WSYNC, S + 1>(v, t, stg, sbase, sj);
+    ct_stage<T, DIR, L, S, PAD, TWS, WSYNC, TWP>(v, t, stg, sbase, sj);
+    ct_fft<T, DIR, L, PAD, TWS, WSYNC, TWP, S + 1>(v, t, stg, sbase, sj);
   }
 }
 

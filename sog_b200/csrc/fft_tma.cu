@@ -1,0 +1,202 @@
+// Column FFT passes of fp64 spectra along 256- and 512-point axes with TMA
+// tile movement (the y passes of the mesh pipeline, forward and inverse).
+//
+// The spectrum is viewed as a 2-D array of doubles, rows = [outer][n] and
+// 2*inner doubles per row.  A tile is 8 consecutive columns (128 bytes of a
+// row) by n rows; CTA = 8 consumer warps (warp w transforms column w of the
+// tile) + 1 producer warp whose first lane issues the tile loads and stores.
+// Two tile buffers: while the consumers transform tile i in one buffer, the
+// producer stores tile i-1 from the other and loads tile i+1 into it.
+//
+//   full[b]  : the TMA load of buffer b completed (expect_tx, 1 arrival)
+//   ready[b] : the 8 consumer warps wrote their columns back (8 arrivals)
+//
+// Same transform as k_cols_pipe (same radix sequence and twiddle table), so
+// the results are the same numbers.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "fft_tma.cuh"
+#include "fft_tma.hpp"
+
+namespace sogb {
+
+template <int L>
+struct ColsTmaLayout {
+  static constexpr int N = 1 << L;
+  static constexpr int TILE = N * 8;                        // complex elements per tile
+  static constexpr unsigned TBYTES = TILE * 16;
+  static constexpr int BOX = N < 256 ? N : 256;             // rows per TMA box (box dims <= 256)
+  static constexpr size_t bytes = 2 * (size_t)TILE * 16 + 8 * (size_t)WarpFft<L>::XROW * 16 +
+                                  (size_t)StageTw<L>::size * 16 + 2 * 2 * sizeof(uint64_t) + 1024;
+};
+
+template <int DIR, int L>
+__global__ void __launch_bounds__(288, 1) k_cols_tma(const __grid_constant__ CUtensorMap tmap, int64_t nchunks,
+                                                     int64_t ntiles, const double2 *__restrict__ tw,
+                                                     unsigned *status) {
+  using LY = ColsTmaLayout<L>;
+  constexpr int N = LY::N, EPT = WarpFft<L>::EPT, TILE = LY::TILE, BOX = LY::BOX;
+  extern __shared__ __align__(1024) unsigned char smem_tma[];
+  // tile buffers 1024-byte aligned (the swizzle pattern repeats every 8 rows)
+  unsigned char *base = smem_tma + ((1024u - (smem_u32(smem_tma) & 1023u)) & 1023u);
+  double2 *buf = reinterpret_cast<double2 *>(base);
+  double2 *xrow = buf + 2 * TILE;
+  double2 *stg = xrow + 8 * WarpFft<L>::XROW;
+  uint64_t *full = reinterpret_cast<uint64_t *>(stg + StageTw<L>::size);
+  uint64_t *ready = full + 2;
+  const int w = threadIdx.x >> 5, t = threadIdx.x & 31;
+  if (threadIdx.x == 256) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    mbar_init(&ready[0], 8);
+    mbar_init(&ready[1], 8);
+    mbar_init_fence();
+  }
+  load_stage_twiddles<double, L, 0>(stg, tw);
+  __syncthreads();
+  // tiles of this CTA: blockIdx.x, + gridDim.x, ...
+  const int64_t my = ntiles > blockIdx.x ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  if (w == 8) {
+    if (t != 0) return;
+    auto coords = [&](int64_t it, int &x, int &y) {
+      const int64_t tile = blockIdx.x + it * gridDim.x;
+      const int64_t o = tile / nchunks;
+      x = (int)((tile - o * nchunks) * 16);
+      y = (int)(o * N);
+    };
+    bool pending[2] = {false, false};   // a load into the buffer not yet known to have landed
+    unsigned pend_par[2] = {0u, 0u};
+    bool ok = true;
+    for (int64_t it = 0; it < my + 2 && ok; ++it) {
+      const int b = (int)(it & 1);
+      if (it >= 2) {
+        // tile it-2 was transformed in buffer b: store it, then reuse b
+        ok = mbar_wait(&ready[b], (unsigned)(((it - 2) >> 1) & 1), status);
+        if (!ok) break;
+        pending[b] = false;
+        int x, y;
+        coords(it - 2, x, y);
+        for (int h = 0; h < N / BOX; ++h) tma_store_2d(&tmap, x, y + h * BOX, buf + b * TILE + h * BOX * 8);
+        bulk_commit();
+        bulk_wait_read_all();
+      }
+      if (it < my) {
+        int x, y;
+        coords(it, x, y);
+        mbar_expect_tx(&full[b], LY::TBYTES);
+        for (int h = 0; h < N / BOX; ++h) tma_load_2d(buf + b * TILE + h * BOX * 8, &tmap, x, y + h * BOX, &full[b]);
+        pending[b] = true;
+        pend_par[b] = (unsigned)((it >> 1) & 1);
+      }
+    }
+    if (!ok) {
+      // a consumer stopped: let the loads in flight land before the CTA exits
+      for (int b = 0; b < 2; ++b)
+        if (pending[b]) mbar_wait(&full[b], pend_par[b], status);
+    }
+    bulk_wait_all();
+    return;
+  }
+  double2 *row = xrow + w * WarpFft<L>::XROW;
+  for (int64_t it = 0; it < my; ++it) {
+    const int b = (int)(it & 1);
+    if (!mbar_wait(&full[b], (unsigned)((it >> 1) & 1), status)) break;
+    double2 *cur = buf + b * TILE;
+    double2 v[EPT];
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) v[e] = cur[tile_slot(t + 32 * e, w)];
+    warp_fft<DIR, L>(v, t, stg, row);
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) cur[tile_slot(t + 32 * e, w)] = v[e];
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (t == 0) mbar_arrive(&ready[b]);
+  }
+}
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::atomic<void *> fn{nullptr};
+  void *f = fn.load(std::memory_order_acquire);
+  if (!f) {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    cudaGetLastError();
+    if (f) fn.store(f, std::memory_order_release);
+  }
+  return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+}
+
+// one wave of resident CTAs of `kernel` on the current device (cached)
+template <typename K>
+int tiles_grid(K kernel, size_t smem, int64_t ntiles) {
+  static std::mutex mu;
+  static std::map<std::pair<const void *, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_pair(reinterpret_cast<const void *>(kernel), dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto itc = cache.find(key);
+  int total;
+  if (itc != cache.end()) {
+    total = itc->second;
+  } else {
+    int nsm = 1, per = 1;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, 288, smem) != cudaSuccess || per < 1) per = 0;
+    cudaGetLastError();
+    total = per > 0 ? nsm * per : 0;
+    cache[key] = total;
+  }
+  if (total <= 0) return 0;
+  return (int)std::min<int64_t>(ntiles, total);
+}
+
+template <int DIR, int L>
+bool launch_one(double2 *data, int64_t inner, int64_t outer, const double2 *tw, unsigned *status, cudaStream_t st) {
+  using LY = ColsTmaLayout<L>;
+  constexpr int N = 1 << L;
+  auto encode = encode_fn();
+  if (!encode) return false;
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)(2 * inner), (cuuint64_t)(outer * N)};
+  cuuint64_t strides[1] = {(cuuint64_t)(inner * 16)};
+  cuuint32_t box[2] = {16, (cuuint32_t)LY::BOX};
+  cuuint32_t es[2] = {1, 1};
+  if (encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, data, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  const int64_t nchunks = (inner + 7) / 8;
+  const int64_t ntiles = outer * nchunks;
+  const int grid = tiles_grid(k_cols_tma<DIR, L>, LY::bytes, ntiles);
+  if (grid <= 0) return false;
+  k_cols_tma<DIR, L><<<grid, 288, LY::bytes, st>>>(m, nchunks, ntiles, tw, status);
+  return true;
+}
+
+}  // namespace
+
+bool launch_cols_tma(double2 *data, int n, int64_t inner, int64_t outer, int dir, const double2 *tw,
+                     unsigned *status, cudaStream_t st) {
+  // TMA constraints: 16-byte aligned base and row pitch (a complex<double>
+  // row always is), int32 tile coordinates
+  if ((reinterpret_cast<uintptr_t>(data) & 15) || inner < 1 || outer < 1) return false;
+  if (outer * (int64_t)n >= ((int64_t)1 << 31) || 2 * inner + 16 >= ((int64_t)1 << 31)) return false;
+  if (n == 512) return dir < 0 ? launch_one<-1, 9>(data, inner, outer, tw, status, st)
+                               : launch_one<+1, 9>(data, inner, outer, tw, status, st);
+  if (n == 256) return dir < 0 ? launch_one<-1, 8>(data, inner, outer, tw, status, st)
+                               : launch_one<+1, 8>(data, inner, outer, tw, status, st);
+  return false;
+}
+
+}  // namespace sogb

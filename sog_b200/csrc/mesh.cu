@@ -34,6 +34,7 @@
 #include "plan.hpp"
 #include "sort.cuh"
 #include "fft_pipe.cuh"
+#include "fft_tma.hpp"
 #include "frames.cuh"
 
 namespace sogb {
@@ -105,6 +106,11 @@ __host__ __device__ __forceinline__ uint32_t bin_row(const AtomGrid &ag, int bz,
 // faster at 512^3 (1.90 against 2.06 ms).
 #ifndef SOG_ZTHR
 #define SOG_ZTHR 256
+#endif
+// fp64 column passes of 256- and 512-point axes through TMA tiles and
+// warp-resident transforms (fft_tma.cu)
+#ifndef SOG_COLS_TMA
+#define SOG_COLS_TMA 1
 #endif
 #ifndef SOG_SLAB_TWO_SLOT
 #define SOG_SLAB_TWO_SLOT 1
@@ -1701,7 +1707,7 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
     C v[kEPT];
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) v[e] = cur[(t + e * TPT) * ic + c];
-    ct_fft<T, -1, L, true>(v, t, stg, xbuf + c, ic);
+    ct_fft<T, -1, L, true, 0, false, true>(v, t, stg, xbuf + c, ic);
     double accE = 0.0;
 #pragma unroll
     for (int e = 0; e < kEPT; ++e) {
@@ -1759,7 +1765,7 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
           const C r = cur[(t + e * TPT) * ic + c];
           wv[e] = cmk<C, T>((T)(gs[e] * (double)r.x), (T)(gs[e] * (double)r.y));
         }
-        ct_fft<T, +1, L, true>(wv, t, stg, xbuf + c, ic);
+        ct_fft<T, +1, L, true, 0, false, true>(wv, t, stg, xbuf + c, ic);
         store_field(3, wv);
         pot_done = true;
       }
@@ -1773,12 +1779,12 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
         const double mzs = (double)signed_mode(t + e * TPT, a.nz) * sc;
         cur[slot] = cmk<C, T>((T)(-mzs * (double)r.y), (T)(mzs * (double)r.x));   // Y2's input
       }
-      ct_fft<T, +1, L, true>(y, t, stg, xbuf + c, ic);
+      ct_fft<T, +1, L, true, 0, false, true>(y, t, stg, xbuf + c, ic);
       if (two) {
         store_field(0, y);
 #pragma unroll
         for (int e = 0; e < kEPT; ++e) y[e] = cur[(t + e * TPT) * ic + c];
-        ct_fft<T, +1, L, true>(y, t, stg, xbuf + c, ic);
+        ct_fft<T, +1, L, true, 0, false, true>(y, t, stg, xbuf + c, ic);
         store_field(2, y);
         pot_done = true;   // k_cols_fields takes the potential from Y1
       } else {
@@ -1793,7 +1799,7 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
           w[e] = cur[slot];
           cur[slot] = y[e];   // Y1 waits in the tile buffer
         }
-        ct_fft<T, +1, L, true>(w, t, stg, xbuf + c, ic);
+        ct_fft<T, +1, L, true, 0, false, true>(w, t, stg, xbuf + c, ic);
         for (int fl = 0; fl < 3; ++fl) {
           const double kxy = g.kmat[fl * 3 + 0] * mx + g.kmat[fl * 3 + 1] * my;
           const double kz = g.kmat[fl * 3 + 2];
@@ -1815,7 +1821,7 @@ __global__ void __launch_bounds__(NTH, NTH == 512 ? 1 : SOG_ZFUSED_MINB) k_zfuse
         const C r = cur[(t + e * TPT) * ic + c];
         wv[e] = cmk<C, T>((T)(gs[e] * (double)r.x), (T)(gs[e] * (double)r.y));
       }
-      ct_fft<T, +1, L, true>(wv, t, stg, xbuf + c, ic);
+      ct_fft<T, +1, L, true, 0, false, true>(wv, t, stg, xbuf + c, ic);
       store_field(0, wv);
     }
     accE = warp_sum(accE);
@@ -2792,6 +2798,15 @@ template <typename T, int DIR>
 void pass_cols(sog_plan *p, cplx_t<T> *data, int n, int64_t inner, int64_t outer, const RadixPlan &rp,
                const cplx_t<T> *tw, cudaStream_t st, const char *name) {
   using C = cplx_t<T>;
+  if constexpr (sizeof(T) == 8 && SOG_COLS_TMA) {
+    // fp64 256- and 512-point axes: warp-resident transforms fed by TMA tiles
+    if ((n == 256 || n == 512) &&
+        launch_cols_tma(reinterpret_cast<double2 *>(data), n, inner, outer, DIR,
+                        reinterpret_cast<const double2 *>(tw), p->status.as<unsigned>(), st)) {
+      after(&p->tr, st, name);
+      return;
+    }
+  }
   const bool done = with_pow2(n, [&](auto lc) {
     constexpr int L = decltype(lc)::value;
     constexpr int nn = 1 << L;
