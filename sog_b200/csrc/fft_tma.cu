@@ -119,6 +119,160 @@ __global__ void __launch_bounds__(288, 1) k_cols_tma(const __grid_constant__ CUt
   }
 }
 
+// Inverse y pass of the field spectra [nf][F][nz][n][inner] that forms the
+// fields of two-slot frames (the TMA form of k_cols_fields, same results).
+// Work is a sequence of jobs, one inverse transform each; a tile (plane o,
+// 8 columns) gives:
+//   slot 0 of an orthorhombic two-slot frame (Y1): job FY (field y =
+//     ky IFFT(i my Y1) -> slot 1), job POT (IFFT(Y1) -> slot 3, when the
+//     potential is wanted and the frame has no alias-summed potential), job FX
+//     (field x = i kx mx IFFT(Y1), in place) -- in this order, so the in-place
+//     store comes after every read of the tile;
+//   slot 2 of such a frame (Y2): job FZ (field z = kz IFFT(Y2), in place);
+//   every plane of other frames (and slot 3 of alias frames): job PLAIN;
+//   slot 1 (and slot 3 when not stored) of two-slot frames: nothing.
+// The jobs of one tile run back to back on one CTA: the repeated loads of a
+// slot-0 tile come from L2.
+enum : int { kJobFY = 0, kJobPot = 1, kJobFX = 2, kJobFZ = 3, kJobPlain = 4 };
+
+struct FieldJobs {
+  const FrameGeom *geom;
+  int F, nz, two_slot, want_pot;
+  int64_t nchunks;
+  // jobs of the tile starting at plane o: their count, and their kinds packed
+  // four bits each (job j: (kinds >> 4j) & 15), so no local array is needed
+  __device__ __forceinline__ int jobs(int64_t o, int &kinds) const {
+    const int64_t fs = o / nz;
+    const int f = (int)(fs / F), sl = (int)(fs - (int64_t)f * F);
+    const FrameGeom &g = geom[f];
+    if (!(two_slot && g.ortho)) { kinds = kJobPlain; return 1; }
+    if (sl == 0) {
+      if (want_pot && !g.pad) { kinds = kJobFY | (kJobPot << 4) | (kJobFX << 8); return 3; }
+      kinds = kJobFY | (kJobFX << 4);
+      return 2;
+    }
+    if (sl == 2) { kinds = kJobFZ; return 1; }
+    if (sl == 3 && g.pad) { kinds = kJobPlain; return 1; }
+    return 0;
+  }
+  // plane the job's output goes to
+  __device__ __forceinline__ int64_t dst_plane(int64_t o, int kind) const {
+    const int64_t sl = (o / nz) % F;
+    const int64_t o0 = o - sl * nz;
+    if (kind == kJobFY) return o0 + nz;
+    if (kind == kJobPot) return o0 + 3 * (int64_t)nz;
+    return o;
+  }
+};
+
+template <int L>
+__global__ void __launch_bounds__(288, 1) k_cols_fields_tma(const __grid_constant__ CUtensorMap tmap, FieldJobs jb,
+                                                            int64_t ntiles, const double2 *__restrict__ tw,
+                                                            unsigned *status) {
+  using LY = ColsTmaLayout<L>;
+  constexpr int N = LY::N, EPT = WarpFft<L>::EPT, TILE = LY::TILE, BOX = LY::BOX;
+  extern __shared__ __align__(1024) unsigned char smem_tma[];
+  unsigned char *base = smem_tma + ((1024u - (smem_u32(smem_tma) & 1023u)) & 1023u);
+  double2 *buf = reinterpret_cast<double2 *>(base);
+  double2 *xrow = buf + 2 * TILE;
+  double2 *stg = xrow + 8 * WarpFft<L>::XROW;
+  uint64_t *full = reinterpret_cast<uint64_t *>(stg + StageTw<L>::size);
+  uint64_t *ready = full + 2;
+  const int w = threadIdx.x >> 5, t = threadIdx.x & 31;
+  if (threadIdx.x == 256) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    mbar_init(&ready[0], 8);
+    mbar_init(&ready[1], 8);
+    mbar_init_fence();
+  }
+  load_stage_twiddles<double, L, 0>(stg, tw);
+  __syncthreads();
+  if (w == 8) {
+    if (t != 0) return;
+    int tx[2] = {0, 0}, ty[2] = {0, 0};   // store target of the job in each buffer
+    bool pending[2] = {false, false};
+    unsigned pend_par[2] = {0u, 0u};
+    bool ok = true;
+    int64_t it = 0;
+    // store the job that used buffer b (job index jt)
+    auto retire = [&](int64_t jt) -> bool {
+      const int b = (int)(jt & 1);
+      if (!mbar_wait(&ready[b], (unsigned)((jt >> 1) & 1), status)) return false;
+      pending[b] = false;
+      for (int h = 0; h < N / BOX; ++h) tma_store_2d(&tmap, tx[b], ty[b] + h * BOX, buf + b * TILE + h * BOX * 8);
+      bulk_commit();
+      bulk_wait_read_all();
+      return true;
+    };
+    for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+      const int64_t o = tile / jb.nchunks;
+      const int x = (int)((tile - o * jb.nchunks) * 16);
+      int kinds = 0;
+      const int nj = jb.jobs(o, kinds);
+      for (int j = 0; j < nj; ++j, ++it) {
+        const int b = (int)(it & 1);
+        if (it >= 2 && !(ok = retire(it - 2))) break;
+        tx[b] = x;
+        ty[b] = (int)(jb.dst_plane(o, (kinds >> (4 * j)) & 15) * N);
+        mbar_expect_tx(&full[b], LY::TBYTES);
+        for (int h = 0; h < N / BOX; ++h)
+          tma_load_2d(buf + b * TILE + h * BOX * 8, &tmap, x, (int)(o * N) + h * BOX, &full[b]);
+        pending[b] = true;
+        pend_par[b] = (unsigned)((it >> 1) & 1);
+      }
+    }
+    for (int64_t jt = it >= 2 ? it - 2 : 0; jt < it && ok; ++jt) ok = retire(jt);
+    if (!ok) {
+      for (int b = 0; b < 2; ++b)
+        if (pending[b]) mbar_wait(&full[b], pend_par[b], status);
+    }
+    bulk_wait_all();
+    return;
+  }
+  double2 *row = xrow + w * WarpFft<L>::XROW;
+  int64_t it = 0;
+  bool ok = true;
+  for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+    const int64_t o = tile / jb.nchunks;
+    const int mx = (int)((tile - o * jb.nchunks) * 8) + w;
+    const int f = (int)(o / jb.nz / jb.F);
+    int kinds = 0;
+    const int nj = jb.jobs(o, kinds);
+    for (int j = 0; j < nj; ++j, ++it) {
+      const int b = (int)(it & 1);
+      if (!(ok = mbar_wait(&full[b], (unsigned)((it >> 1) & 1), status))) break;
+      double2 *cur = buf + b * TILE;
+      const int kd = (kinds >> (4 * j)) & 15;
+      double2 v[EPT];
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) {
+        v[e] = cur[tile_slot(t + 32 * e, w)];
+        if (kd == kJobFY) {   // i my Y1
+          const double my = (double)signed_mode(t + 32 * e, N);
+          v[e] = make_double2(-my * v[e].y, my * v[e].x);
+        }
+      }
+      warp_fft<+1, L>(v, t, stg, row);
+      const FrameGeom &g = jb.geom[f];
+      if (kd == kJobFY || kd == kJobFZ) {
+        const double k = kd == kJobFY ? g.kmat[4] : g.kmat[8];
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) v[e] = make_double2(k * v[e].x, k * v[e].y);
+      } else if (kd == kJobFX) {   // i kx mx
+        const double kxm = g.kmat[0] * mx;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) v[e] = make_double2(-kxm * v[e].y, kxm * v[e].x);
+      }
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) cur[tile_slot(t + 32 * e, w)] = v[e];
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (t == 0) mbar_arrive(&ready[b]);
+    }
+  }
+}
+
 namespace {
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -184,6 +338,37 @@ bool launch_one(double2 *data, int64_t inner, int64_t outer, const double2 *tw, 
   return true;
 }
 
+template <int L>
+bool launch_fields(double2 *data, const FrameGeom *geom, int nf, int F, int nz, int64_t inner, const double2 *tw,
+                   int two_slot, int want_pot, unsigned *status, cudaStream_t st) {
+  using LY = ColsTmaLayout<L>;
+  constexpr int N = 1 << L;
+  auto encode = encode_fn();
+  if (!encode) return false;
+  const int64_t planes = (int64_t)nf * F * nz;
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)(2 * inner), (cuuint64_t)(planes * N)};
+  cuuint64_t strides[1] = {(cuuint64_t)(inner * 16)};
+  cuuint32_t box[2] = {16, (cuuint32_t)LY::BOX};
+  cuuint32_t es[2] = {1, 1};
+  if (encode(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, data, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  FieldJobs jb;
+  jb.geom = geom;
+  jb.F = F;
+  jb.nz = nz;
+  jb.two_slot = two_slot;
+  jb.want_pot = want_pot;
+  jb.nchunks = (inner + 7) / 8;
+  const int64_t ntiles = planes * jb.nchunks;
+  const int grid = tiles_grid(k_cols_fields_tma<L>, LY::bytes, ntiles);
+  if (grid <= 0) return false;
+  k_cols_fields_tma<L><<<grid, 288, LY::bytes, st>>>(m, jb, ntiles, tw, status);
+  return true;
+}
+
 }  // namespace
 
 bool launch_cols_tma(double2 *data, int n, int64_t inner, int64_t outer, int dir, const double2 *tw,
@@ -196,6 +381,15 @@ bool launch_cols_tma(double2 *data, int n, int64_t inner, int64_t outer, int dir
                                : launch_one<+1, 9>(data, inner, outer, tw, status, st);
   if (n == 256) return dir < 0 ? launch_one<-1, 8>(data, inner, outer, tw, status, st)
                                : launch_one<+1, 8>(data, inner, outer, tw, status, st);
+  return false;
+}
+
+bool launch_cols_fields_tma(double2 *data, const FrameGeom *geom, int nf, int F, int nz, int n, int64_t inner,
+                            const double2 *tw, int two_slot, int want_pot, unsigned *status, cudaStream_t st) {
+  if ((reinterpret_cast<uintptr_t>(data) & 15) || inner < 1 || nf < 1 || F < 1 || nz < 1) return false;
+  if ((int64_t)nf * F * nz * n >= ((int64_t)1 << 31) || 2 * inner + 16 >= ((int64_t)1 << 31)) return false;
+  if (n == 512) return launch_fields<9>(data, geom, nf, F, nz, inner, tw, two_slot, want_pot, status, st);
+  if (n == 256) return launch_fields<8>(data, geom, nf, F, nz, inner, tw, two_slot, want_pot, status, st);
   return false;
 }
 

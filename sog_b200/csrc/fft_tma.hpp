@@ -3,6 +3,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "common.cuh"
+
 namespace sogb {
 
 // In-place column FFT of the fp64 spectrum data [outer][n][inner] along n
@@ -12,5 +14,11 @@ namespace sogb {
 // tensor-map support, alignment); the caller then runs k_cols_pipe.
 bool launch_cols_tma(double2 *data, int n, int64_t inner, int64_t outer, int dir, const double2 *tw,
                      unsigned *status, cudaStream_t st);
+
+// Inverse y pass of the field spectra [nf][F][nz][n][inner] with the field
+// formation of two-slot frames (k_cols_fields' semantics) through TMA tiles,
+// for n = 256 or 512.  False, without launching, when this path does not apply.
+bool launch_cols_fields_tma(double2 *data, const FrameGeom *geom, int nf, int F, int nz, int n, int64_t inner,
+                            const double2 *tw, int two_slot, int want_pot, unsigned *status, cudaStream_t st);
 
 }  // namespace sogb

@@ -2857,6 +2857,15 @@ void pass_cols_fields(sog_plan *p, cplx_t<T> *fspec, const FrameGeom *geom, int 
   using C = cplx_t<T>;
   const int ny = p->d.ny, nz = p->d.nz;
   const int64_t inner = p->nxh;
+  if constexpr (sizeof(T) == 8 && SOG_COLS_TMA) {
+    if ((ny == 256 || ny == 512) &&
+        launch_cols_fields_tma(reinterpret_cast<double2 *>(fspec), geom, nf, F, nz, ny, inner,
+                               reinterpret_cast<const double2 *>(tw_of<T>(p, 1)), two_slot, want_pot,
+                               p->status.as<unsigned>(), st)) {
+      after(&p->tr, st, "fft_y_inv");
+      return;
+    }
+  }
   with_pow2(ny, [&](auto lc) {
     constexpr int L = decltype(lc)::value;
     constexpr int nn = 1 << L;
