@@ -75,6 +75,11 @@ __host__ __device__ __forceinline__ uint32_t bin_row(const AtomGrid &ag, int bz,
 #ifndef SOG_GATHER_VEC
 #define SOG_GATHER_VEC 1
 #endif
+// 1: forces-only fp64 gathers load their stencil rows cooperatively per warp
+// (k_gather_f3c); 0: one thread's 16-byte row loads (k_gather_f3v)
+#ifndef SOG_GATHER_COOP
+#define SOG_GATHER_COOP 1
+#endif
 #ifndef SOG_SPREAD_MINB
 #define SOG_SPREAD_MINB 4
 #endif
@@ -2499,6 +2504,160 @@ __global__ void __launch_bounds__(256, SOG_GATHER_MINB) k_gather_f3v(GatherArgs<
   }
 }
 
+// Forces-only fp64 gather (even orders, three interleaved fields) with the
+// stencil rows loaded by the whole warp.  One thread still owns one sorted
+// atom (weights, sums, output), but the rows are fetched cooperatively: for
+// every stencil row (c, b) the warp copies the 32 atoms' rows -- C 16-byte
+// chunks each, from the row's 16-byte-aligned-down start, plus the odd tail
+// double -- into a warp-private staging area with cp.async, lane l taking
+// chunks j*32 + l.  One copy instruction then covers about three atoms'
+// rows (a few cache lines) instead of 32 rows on 32 lines, and the copies of
+// the next row are in flight while the current one is summed (two staging
+// rows per warp, odd stride S so that the lanes' chunk reads hit distinct
+// banks).  Atoms whose stencil wraps in x (or an unaligned field block) take
+// the per-element loads of k_gather_f3v afterwards.  Same products and sums
+// in the same order as k_gather_f3v: the same numbers.
+template <int P>
+struct GatherCoop {
+  static constexpr int C = 3 * P / 2 + 1;   // chunks per staged row
+  static constexpr int S = C | 1;           // staging stride (chunks)
+  static constexpr size_t smem = (size_t)8 * 2 * 32 * S * sizeof(double2);
+};
+
+template <int P>
+__global__ void __launch_bounds__(256, 2) k_gather_f3c(GatherArgs<double> a) {
+  static_assert(P % 2 == 0, "even stencil widths");
+  constexpr int C = GatherCoop<P>::C, S = GatherCoop<P>::S;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int lane = threadIdx.x & 31;
+  double2 *stg = reinterpret_cast<double2 *>(smem_raw) + (size_t)(threadIdx.x >> 5) * 2 * 32 * S;
+  const int64_t si = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  bool active = si < a.nslots;
+  int64_t s = a.slot_lo + si;
+  if (a.range_lo) {
+    s = (int64_t)*a.range_lo + si;
+    active = active && s < (int64_t)*a.range_hi;
+  }
+  int4 an = make_int4(0, 0, 0, 0);
+  double wx[1][P], wy[1][P], wz[1][P];
+#pragma unroll
+  for (int k = 0; k < P; ++k) wx[0][k] = wy[0][k] = wz[0][k] = 0.0;
+  if (active) {
+    an = a.s_anchor[s];
+    axis_kinds<double, P, 1>(a.spline, a.s_t[s * 3 + 0], wx, a.qc);
+    axis_kinds<double, P, 1>(a.spline, a.s_t[s * 3 + 1], wy, a.qc);
+    axis_kinds<double, P, 1>(a.spline, a.s_t[s * 3 + 2], wz, a.qc);
+  }
+  const AtomGrid &ag = a.ag;
+  const double *base = a.freal + (int64_t)an.w * 3 * a.ng;
+  const bool coop = active && an.x + P <= ag.nx && (reinterpret_cast<uintptr_t>(base) & 15) == 0;
+  // this lane's row (c, b): aligned-down address | parity bit | staged bit
+  auto packed_row = [&](int c, int b) -> unsigned long long {
+    int gz = an.z - a.zlo + c;
+    if (gz >= a.zwrap) gz -= a.zwrap;
+    int gy = an.y + b;
+    if (gy >= ag.ny) gy -= ag.ny;
+    const uintptr_t u = reinterpret_cast<uintptr_t>(base + (((int64_t)gz * ag.ny + gy) * ag.nx + an.x) * 3);
+    const unsigned long long par = (u >> 3) & 1;
+    return coop ? ((unsigned long long)(u - 8 * par) | par | 2ull) : 0ull;
+  };
+  // chunk j*32 + lane of the warp's row: atom (lane) at_j, chunk u_j
+  int at[C], uu[C];
+#pragma unroll
+  for (int j = 0; j < C; ++j) {
+    const int idx = j * 32 + lane;
+    at[j] = idx / C;
+    uu[j] = idx - at[j] * C;
+  }
+  auto issue = [&](double2 *buf, unsigned long long pk) {
+#pragma unroll
+    for (int j = 0; j < C; ++j) {
+      const unsigned long long q = __shfl_sync(0xffffffffu, pk, at[j]);
+      const double *src = reinterpret_cast<const double *>(q & ~15ull);
+      double2 *dst = buf + at[j] * S + uu[j];
+      if (uu[j] < C - 1) {
+        const bool use = (q & 2ull) != 0;
+        cp_async16(dst, use ? (const void *)(src + 2 * uu[j]) : (const void *)a.freal, use);
+      } else {
+        const bool tail = (q & 3ull) == 3ull;   // staged row with an odd start: its last double
+        cp_async8(dst, tail ? (const void *)(src + 2 * uu[j]) : (const void *)a.freal, tail);
+      }
+    }
+  };
+  double acc0 = 0.0, acc1 = 0.0, acc2 = 0.0;
+  issue(stg, packed_row(0, 0));
+  cp_async_commit();
+#pragma unroll 1
+  for (int c = 0; c < P; ++c) {
+#pragma unroll
+    for (int b = 0; b < P; ++b) {
+      const int nc = b + 1 < P ? c : c + 1, nb = b + 1 < P ? b + 1 : 0;
+      if (nc < P) issue(stg + ((b + 1) & 1) * 32 * S, packed_row(nc, nb));
+      cp_async_commit();
+      cp_async_wait<1>();
+      __syncwarp();
+      const double2 *mine = stg + (b & 1) * 32 * S + lane * S;
+      const int par = (int)(packed_row(c, b) & 1ull);
+      double A[3 * P + 1];
+#pragma unroll
+      for (int u = 0; u < 3 * P / 2; ++u) {
+        const double2 t = mine[u];
+        A[2 * u] = t.x;
+        A[2 * u + 1] = t.y;
+      }
+      A[3 * P] = mine[C - 1].x;
+      const double wzy = wy[0][b] * wz[0][c];
+#pragma unroll
+      for (int k = 0; k < P; ++k) {
+        const double wv = wx[0][k] * wzy;
+        const double v0 = par ? A[3 * k + 1] : A[3 * k];
+        const double v1 = par ? A[3 * k + 2] : A[3 * k + 1];
+        const double v2 = par ? A[3 * k + 3] : A[3 * k + 2];
+        acc0 += wv * v0;
+        acc1 += wv * v1;
+        acc2 += wv * v2;
+      }
+      __syncwarp();
+    }
+  }
+  cp_async_wait<0>();
+  if (!active) return;
+  if (!coop) {
+    // stencil wrapping in x (or an unaligned field block): element loads
+    int ix[P];
+#pragma unroll
+    for (int k = 0; k < P; ++k) { int v = an.x + k; ix[k] = v >= ag.nx ? v - ag.nx : v; }
+    acc0 = acc1 = acc2 = 0.0;
+#pragma unroll 1
+    for (int c = 0; c < P; ++c) {
+      int gz = an.z - a.zlo + c;
+      if (gz >= a.zwrap) gz -= a.zwrap;
+#pragma unroll
+      for (int b = 0; b < P; ++b) {
+        int gy = an.y + b;
+        if (gy >= ag.ny) gy -= ag.ny;
+        const int64_t row = ((int64_t)gz * ag.ny + gy) * ag.nx;
+        const double wzy = wy[0][b] * wz[0][c];
+#pragma unroll
+        for (int k = 0; k < P; ++k) {
+          const double wv = wx[0][k] * wzy;
+          const double *pt = base + (row + ix[k]) * 3;
+          acc0 += wv * pt[0];
+          acc1 += wv * pt[1];
+          acc2 += wv * pt[2];
+        }
+      }
+    }
+  }
+  const int64_t atom = a.s_atom[s];
+  const double q = a.s_q[s];
+  const double sc = -q * a.norm;
+  const double v[3] = {sc * acc0, sc * acc1, sc * acc2};
+  for (int c = 0; c < 3; ++c) {
+    if (a.accumulate) a.forces[atom * 3 + c] += v[c]; else a.forces[atom * 3 + c] = v[c];
+  }
+}
+
 // ---- z-slab decomposition: transpose packing and slab dE/dq ----
 // plain copy into another rank's halo planes (peer transport)
 template <typename T>
@@ -2984,8 +3143,19 @@ void dispatch_gather(const GatherArgs<T> &ga, int order, cudaStream_t st, Tracer
   if constexpr (std::is_same<T, double>::value) {
     // forces only (three interleaved fields): vector row loads
     if (SOG_GATHER_VEC && ga.nfield == 3 && ga.want_force && !ga.want_pot && (order == 4 || order == 6)) {
-      if (order == 4) k_gather_f3v<4><<<nb, 256, 0, st>>>(ga);
-      else k_gather_f3v<6><<<nb, 256, 0, st>>>(ga);
+      if (SOG_GATHER_COOP) {
+        if (order == 4) {
+          allow_smem(k_gather_f3c<4>, (int)GatherCoop<4>::smem);
+          k_gather_f3c<4><<<nb, 256, GatherCoop<4>::smem, st>>>(ga);
+        } else {
+          allow_smem(k_gather_f3c<6>, (int)GatherCoop<6>::smem);
+          k_gather_f3c<6><<<nb, 256, GatherCoop<6>::smem, st>>>(ga);
+        }
+      } else if (order == 4) {
+        k_gather_f3v<4><<<nb, 256, 0, st>>>(ga);
+      } else {
+        k_gather_f3v<6><<<nb, 256, 0, st>>>(ga);
+      }
       after(tr, st, "gather");
       return;
     }
