@@ -273,6 +273,140 @@ __global__ void __launch_bounds__(288, 1) k_cols_fields_tma(const __grid_constan
   }
 }
 
+// Inverse C2R x pass of F fields with interleaved real output (the bulk-copy
+// form of k_c2r_pipe, same arithmetic and results), n = 512 reals per row as
+// a 256-point complex transform.  A tile is RPT = 8/F rows x F fields; one
+// consumer warp per (row, field): the pre-twiddle Z[k] = A + i conj(W^k) B
+// from X[k] and X[h-k] of its input row, the warp-local transform with its
+// exchanges in its own row slot, then -- after a named barrier of the row's
+// F warps, which frees the row's slots -- its values written interleaved
+// into the row's region.  The producer warp's first lane moves the rows:
+// a 1-D bulk copy per input row (4112 bytes) on the buffer's full barrier,
+// a 1-D bulk store per output row (n*F doubles) once the consumers arrive on
+// the buffer's ready barrier.
+template <int L>
+struct C2rTmaLayout {
+  static constexpr int N = 1 << L, H = N / 2, NXH = H + 1;
+  static constexpr int HP = H + H / 8;                       // padded exchange row
+  static constexpr int ROWSZ = HP > NXH ? HP : NXH;          // complex slots per (row, field)
+  // shared memory with nw = RPT * F consumer warps (one row-field slot each, two buffers)
+  static constexpr size_t bytes(int nw) {
+    return (2 * (size_t)nw * ROWSZ + N + StageTw<L - 1>::size) * 16 + 4 * sizeof(uint64_t) + 16;
+  }
+};
+
+// NW consumer warps (RPT * F: 6 for three fields, else 8) + 1 producer warp;
+// three CTAs per SM with six consumer warps, two with eight.
+template <int L, int NW>
+__global__ void __launch_bounds__(32 * (NW + 1), NW == 6 ? 3 : 2)
+    k_c2r_tma(const double2 *__restrict__ in, double *__restrict__ out, int F, int rpt, int64_t nzy, int64_t nrows,
+              int64_t ntiles, const double2 *__restrict__ tw, unsigned *status) {
+  using LY = C2rTmaLayout<L>;
+  constexpr int N = LY::N, H = LY::H, NXH = LY::NXH, ROWSZ = LY::ROWSZ, SLOTS = NW * ROWSZ;
+  constexpr int TPT = H / kEPT;
+  static_assert(TPT == 32, "one warp per row-field transform");
+  extern __shared__ __align__(16) unsigned char smem_c2r[];
+  double2 *bufs = reinterpret_cast<double2 *>(smem_c2r);
+  double2 *stw = bufs + 2 * SLOTS;        // n-th roots of unity (pre-twiddle)
+  double2 *stg = stw + N;                 // stage table of the length n/2 transform
+  uint64_t *full = reinterpret_cast<uint64_t *>(stg + StageTw<L - 1>::size);
+  uint64_t *ready = full + 2;
+  constexpr int nw = NW;                  // consumer warps (= rpt * F)
+  const int w = threadIdx.x >> 5, t = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    mbar_init(&ready[0], nw);
+    mbar_init(&ready[1], nw);
+    mbar_init_fence();
+  }
+  load_twiddles<double>(stw, tw, N);
+  load_stage_twiddles<double, L - 1, 1>(stg, tw);
+  __syncthreads();
+  const int64_t my = ntiles > blockIdx.x ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  if (w == nw) {
+    if (t != 0) return;
+    bool pending[2] = {false, false};
+    unsigned pend_par[2] = {0u, 0u};
+    bool ok = true;
+    for (int64_t it = 0; it < my + 2 && ok; ++it) {
+      const int b = (int)(it & 1);
+      double2 *buf = bufs + b * SLOTS;
+      if (it >= 2) {
+        ok = mbar_wait(&ready[b], (unsigned)(((it - 2) >> 1) & 1), status);
+        if (!ok) break;
+        pending[b] = false;
+        const int64_t row0 = (blockIdx.x + (it - 2) * gridDim.x) * rpt;
+        const int nv = (int)min((int64_t)rpt, nrows - row0);
+        for (int r = 0; r < nv; ++r)
+          bulk_store_1d(out + (row0 + r) * N * F, buf + (size_t)r * F * ROWSZ, (unsigned)(N * F * sizeof(double)));
+        bulk_commit();
+        bulk_wait_read_all();
+      }
+      if (it < my) {
+        const int64_t row0 = (blockIdx.x + it * gridDim.x) * rpt;
+        const int nv = (int)min((int64_t)rpt, nrows - row0);
+        mbar_expect_tx(&full[b], (unsigned)(nv * F * NXH * 16));
+        for (int r = 0; r < nv; ++r) {
+          const int64_t row = row0 + r, frame = row / nzy, zy = row - frame * nzy;
+          for (int f = 0; f < F; ++f)
+            bulk_load_1d(buf + (size_t)(r * F + f) * ROWSZ, in + ((frame * F + f) * nzy + zy) * NXH, NXH * 16,
+                         &full[b]);
+        }
+        pending[b] = true;
+        pend_par[b] = (unsigned)((it >> 1) & 1);
+      }
+    }
+    if (!ok) {
+      for (int b = 0; b < 2; ++b)
+        if (pending[b]) mbar_wait(&full[b], pend_par[b], status);
+    }
+    bulk_wait_all();
+    return;
+  }
+  if (w > nw) return;
+  const int rr = w / F, f = w - rr * F;
+  for (int64_t it = 0; it < my; ++it) {
+    const int b = (int)(it & 1);
+    if (!mbar_wait(&full[b], (unsigned)((it >> 1) & 1), status)) break;
+    const int64_t row0 = (blockIdx.x + it * gridDim.x) * rpt;
+    const bool valid = row0 + rr < nrows;   // warp-uniform, and uniform over the row's F warps
+    double2 *cur = bufs + b * SLOTS;
+    if (valid) {
+      double2 *X = cur + (size_t)(rr * F + f) * ROWSZ;
+      double2 v[kEPT];
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) {
+        const int k = t + e * TPT;
+        if (k == 0) {
+          const double x0 = X[0].x, xh = X[H].x;
+          v[e] = make_double2(x0 + xh, x0 - xh);
+        } else {
+          const double2 a = X[k], bb = X[H - k];
+          const double Ar = a.x + bb.x, Ai = a.y - bb.y;
+          const double Br = a.x - bb.x, Bi = a.y + bb.y;
+          const double2 wk = stw[k];
+          const double cr = wk.x * Br + wk.y * Bi, ci = wk.x * Bi - wk.y * Br;
+          v[e] = make_double2(Ar - ci, Ai + cr);
+        }
+      }
+      __syncwarp();   // the row slot's inputs are in registers: it becomes exchange space
+      ct_fft<double, +1, L - 1, true, 1, true>(v, t, stg, X, 1);
+      named_sync(1 + rr, F * 32);   // the row's F transforms are done with their slots
+      double *so = reinterpret_cast<double *>(cur + (size_t)rr * F * ROWSZ);
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) {
+        const int m = t + e * TPT;
+        so[(2 * m) * F + f] = v[e].x;
+        so[(2 * m + 1) * F + f] = v[e].y;
+      }
+      fence_proxy_async_smem();
+    }
+    __syncwarp();
+    if (t == 0) mbar_arrive(&ready[b]);
+  }
+}
+
 namespace {
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -291,7 +425,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // one wave of resident CTAs of `kernel` on the current device (cached)
 template <typename K>
-int tiles_grid(K kernel, size_t smem, int64_t ntiles) {
+int tiles_grid(K kernel, size_t smem, int64_t ntiles, int threads = 288) {
   static std::mutex mu;
   static std::map<std::pair<const void *, int>, int> cache;
   int dev = 0;
@@ -306,7 +440,7 @@ int tiles_grid(K kernel, size_t smem, int64_t ntiles) {
     int nsm = 1, per = 1;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, 288, smem) != cudaSuccess || per < 1) per = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, threads, smem) != cudaSuccess || per < 1) per = 0;
     cudaGetLastError();
     total = per > 0 ? nsm * per : 0;
     cache[key] = total;
@@ -391,6 +525,25 @@ bool launch_cols_fields_tma(double2 *data, const FrameGeom *geom, int nf, int F,
   if (n == 512) return launch_fields<9>(data, geom, nf, F, nz, inner, tw, two_slot, want_pot, status, st);
   if (n == 256) return launch_fields<8>(data, geom, nf, F, nz, inner, tw, two_slot, want_pot, status, st);
   return false;
+}
+
+bool launch_c2r_tma(const double2 *in, double *out, int F, int64_t nzy, int64_t nrows, int n, const double2 *tw,
+                    unsigned *status, cudaStream_t st) {
+  if (n != 512 || F < 1 || F > 8 || nrows < 1) return false;
+  if ((reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) return false;
+  using LY = C2rTmaLayout<9>;
+  const int rpt = 8 / F, nw = rpt * F;
+  if (nw != 6 && nw != 8) return false;
+  const int64_t ntiles = (nrows + rpt - 1) / rpt;
+  const size_t smem = LY::bytes(nw);
+  const int grid = nw == 6 ? tiles_grid(k_c2r_tma<9, 6>, smem, ntiles, 32 * 7)
+                           : tiles_grid(k_c2r_tma<9, 8>, smem, ntiles, 32 * 9);
+  if (grid <= 0) return false;
+  if (nw == 6)
+    k_c2r_tma<9, 6><<<grid, 32 * 7, smem, st>>>(in, out, F, rpt, nzy, nrows, ntiles, tw, status);
+  else
+    k_c2r_tma<9, 8><<<grid, 32 * 9, smem, st>>>(in, out, F, rpt, nzy, nrows, ntiles, tw, status);
+  return true;
 }
 
 }  // namespace sogb

@@ -21,4 +21,10 @@ bool launch_cols_tma(double2 *data, int n, int64_t inner, int64_t outer, int dir
 bool launch_cols_fields_tma(double2 *data, const FrameGeom *geom, int nf, int F, int nz, int n, int64_t inner,
                             const double2 *tw, int two_slot, int want_pot, unsigned *status, cudaStream_t st);
 
+// Inverse C2R x pass of F fields [nframes][F][nzy][n/2+1] -> interleaved real
+// [nframes][nzy][n][F] (k_c2r_pipe's semantics) with bulk-copied rows, for
+// n = 512 and F <= 8.  False, without launching, when this path does not apply.
+bool launch_c2r_tma(const double2 *in, double *out, int F, int64_t nzy, int64_t nrows, int n, const double2 *tw,
+                    unsigned *status, cudaStream_t st);
+
 }  // namespace sogb

@@ -2914,6 +2914,15 @@ template <typename T>
 void pass_x_inv(sog_plan *p, cplx_t<T> *fspec, T *freal, int64_t nframes, int64_t nzy, int F, cudaStream_t st) {
   using C = cplx_t<T>;
   const int nx = p->d.nx;
+  if constexpr (sizeof(T) == 8 && SOG_COLS_TMA) {
+    // fp64 512-point rows: bulk-copied rows, one warp per row and field
+    if (nx == 512 && launch_c2r_tma(reinterpret_cast<const double2 *>(fspec), reinterpret_cast<double *>(freal), F,
+                                    nzy, nframes * nzy, nx, reinterpret_cast<const double2 *>(tw_of<T>(p, 0)),
+                                    p->status.as<unsigned>(), st)) {
+      after(&p->tr, st, "fft_c2r_x");
+      return;
+    }
+  }
   const bool done = nx >= 16 && with_pow2(nx, [&](auto lc) {
     constexpr int L = decltype(lc)::value < 4 ? 4 : decltype(lc)::value;
     constexpr int n = 1 << L;
