@@ -2538,6 +2538,9 @@ __global__ void __launch_bounds__(256, 2) k_gather_f3c(GatherArgs<double> a) {
     s = (int64_t)*a.range_lo + si;
     active = active && s < (int64_t)*a.range_hi;
   }
+  // warps without an atom leave at once (a slab's grid covers every slot but
+  // only its range is live); the others keep all lanes for the shared copies
+  if (!__any_sync(0xffffffffu, active)) return;
   int4 an = make_int4(0, 0, 0, 0);
   double wx[1][P], wy[1][P], wz[1][P];
 #pragma unroll
