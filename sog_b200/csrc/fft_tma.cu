@@ -407,6 +407,120 @@ __global__ void __launch_bounds__(32 * (NW + 1), NW == 6 ? 3 : 2)
   }
 }
 
+// Forward R2C x pass, n = 512 reals per row as a 256-point complex transform
+// (the bulk-copy form of k_r2c_pipe, same arithmetic and results): a tile is
+// 8 rows, one consumer warp per row packs z[m] = x[2m] + i x[2m+1] from its
+// row slot, transforms it with warp-local exchanges in the slot, leaves Z in
+// the slot (padded layout) for the post-processing
+//   X[k] = (Z[k] + conj Z[h-k]) / 2 - i W_n^k (Z[k] - conj Z[h-k]) / 2,
+// and writes X[0 .. h] back to the slot's start for the bulk store.
+template <int L>
+struct R2cTmaLayout {
+  static constexpr int N = 1 << L, H = N / 2, NXH = H + 1;
+  static constexpr int ROWSZ = H + H / 8;                    // padded exchange row (>= NXH and >= N/2)
+  static constexpr size_t bytes = (2 * 8 * (size_t)ROWSZ + N + StageTw<L - 1>::size) * 16 + 4 * sizeof(uint64_t);
+};
+
+template <int L>
+__global__ void __launch_bounds__(288, 2)
+    k_r2c_tma(const double *__restrict__ in, double2 *__restrict__ out, int64_t nrows, int64_t ntiles,
+              const double2 *__restrict__ tw, unsigned *status) {
+  using LY = R2cTmaLayout<L>;
+  constexpr int N = LY::N, H = LY::H, NXH = LY::NXH, ROWSZ = LY::ROWSZ, SLOTS = 8 * ROWSZ;
+  constexpr int TPT = H / kEPT;
+  static_assert(TPT == 32, "one warp per row transform");
+  static_assert(ROWSZ >= NXH, "the output row fits its slot");
+  extern __shared__ __align__(16) unsigned char smem_r2c[];
+  double2 *bufs = reinterpret_cast<double2 *>(smem_r2c);
+  double2 *stw = bufs + 2 * SLOTS;        // n-th roots of unity (post-processing)
+  double2 *stg = stw + N;                 // stage table of the length n/2 transform
+  uint64_t *full = reinterpret_cast<uint64_t *>(stg + StageTw<L - 1>::size);
+  uint64_t *ready = full + 2;
+  const int w = threadIdx.x >> 5, t = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    mbar_init(&ready[0], 8);
+    mbar_init(&ready[1], 8);
+    mbar_init_fence();
+  }
+  load_twiddles<double>(stw, tw, N);
+  load_stage_twiddles<double, L - 1, 1>(stg, tw);
+  __syncthreads();
+  const int64_t my = ntiles > blockIdx.x ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  if (w == 8) {
+    if (t != 0) return;
+    bool pending[2] = {false, false};
+    unsigned pend_par[2] = {0u, 0u};
+    bool ok = true;
+    for (int64_t it = 0; it < my + 2 && ok; ++it) {
+      const int b = (int)(it & 1);
+      double2 *buf = bufs + b * SLOTS;
+      if (it >= 2) {
+        ok = mbar_wait(&ready[b], (unsigned)(((it - 2) >> 1) & 1), status);
+        if (!ok) break;
+        pending[b] = false;
+        const int64_t row0 = (blockIdx.x + (it - 2) * gridDim.x) * 8;
+        const int nv = (int)min((int64_t)8, nrows - row0);
+        for (int r = 0; r < nv; ++r) bulk_store_1d(out + (row0 + r) * NXH, buf + (size_t)r * ROWSZ, NXH * 16);
+        bulk_commit();
+        bulk_wait_read_all();
+      }
+      if (it < my) {
+        const int64_t row0 = (blockIdx.x + it * gridDim.x) * 8;
+        const int nv = (int)min((int64_t)8, nrows - row0);
+        mbar_expect_tx(&full[b], (unsigned)(nv * N * 8));
+        for (int r = 0; r < nv; ++r)
+          bulk_load_1d(buf + (size_t)r * ROWSZ, in + (row0 + r) * N, N * 8, &full[b]);
+        pending[b] = true;
+        pend_par[b] = (unsigned)((it >> 1) & 1);
+      }
+    }
+    if (!ok) {
+      for (int b = 0; b < 2; ++b)
+        if (pending[b]) mbar_wait(&full[b], pend_par[b], status);
+    }
+    bulk_wait_all();
+    return;
+  }
+  for (int64_t it = 0; it < my; ++it) {
+    const int b = (int)(it & 1);
+    if (!mbar_wait(&full[b], (unsigned)((it >> 1) & 1), status)) break;
+    const int64_t row0 = (blockIdx.x + it * gridDim.x) * 8;
+    double2 *zrow = bufs + b * SLOTS + (size_t)w * ROWSZ;
+    if (row0 + w < nrows) {
+      double2 v[kEPT];
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) v[e] = zrow[t + e * TPT];   // (x[2m], x[2m+1]), m = t + e TPT
+      __syncwarp();   // the inputs are in registers: the slot becomes exchange space
+      ct_fft<double, -1, L - 1, true, 1, true, true>(v, t, stg, zrow, 1);
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) zrow[sidx<true>(t + e * TPT, 1)] = v[e];
+      __syncwarp();
+      double2 o[kEPT], oh = make_double2(0.0, 0.0);
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) {
+        const int k = t + e * TPT;
+        const double2 a = v[e];
+        const double2 bb = zrow[sidx<true>((H - k) & (H - 1), 1)];
+        const double er = 0.5 * (a.x + bb.x), ei = 0.5 * (a.y - bb.y);
+        const double dr = 0.5 * (a.x - bb.x), di = 0.5 * (a.y + bb.y);
+        const double2 wk = stw[k];
+        const double pr = wk.x * dr - wk.y * di, pi = wk.x * di + wk.y * dr;
+        o[e] = make_double2(er + pi, ei - pr);
+        if (k == 0) oh = make_double2(er - pi, ei + pr);
+      }
+      __syncwarp();   // every lane has read Z: the slot takes the output row
+#pragma unroll
+      for (int e = 0; e < kEPT; ++e) zrow[t + e * TPT] = o[e];
+      if (t == 0) zrow[H] = oh;
+      fence_proxy_async_smem();
+    }
+    __syncwarp();
+    if (t == 0) mbar_arrive(&ready[b]);
+  }
+}
+
 namespace {
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -543,6 +657,18 @@ bool launch_c2r_tma(const double2 *in, double *out, int F, int64_t nzy, int64_t 
     k_c2r_tma<9, 6><<<grid, 32 * 7, smem, st>>>(in, out, F, rpt, nzy, nrows, ntiles, tw, status);
   else
     k_c2r_tma<9, 8><<<grid, 32 * 9, smem, st>>>(in, out, F, rpt, nzy, nrows, ntiles, tw, status);
+  return true;
+}
+
+bool launch_r2c_tma(const double *in, double2 *out, int64_t nrows, int n, const double2 *tw, unsigned *status,
+                    cudaStream_t st) {
+  if (n != 512 || nrows < 1) return false;
+  if ((reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) return false;
+  using LY = R2cTmaLayout<9>;
+  const int64_t ntiles = (nrows + 7) / 8;
+  const int grid = tiles_grid(k_r2c_tma<9>, LY::bytes, ntiles);
+  if (grid <= 0) return false;
+  k_r2c_tma<9><<<grid, 288, LY::bytes, st>>>(in, out, nrows, ntiles, tw, status);
   return true;
 }
 

@@ -27,4 +27,10 @@ bool launch_cols_fields_tma(double2 *data, const FrameGeom *geom, int nf, int F,
 bool launch_c2r_tma(const double2 *in, double *out, int F, int64_t nzy, int64_t nrows, int n, const double2 *tw,
                     unsigned *status, cudaStream_t st);
 
+// Forward R2C x pass of rows of n reals -> n/2+1 complex (k_r2c_pipe's
+// semantics) with bulk-copied rows, for n = 512.  False, without launching,
+// when this path does not apply.
+bool launch_r2c_tma(const double *in, double2 *out, int64_t nrows, int n, const double2 *tw, unsigned *status,
+                    cudaStream_t st);
+
 }  // namespace sogb

@@ -2880,6 +2880,14 @@ template <typename T>
 void pass_x_fwd(sog_plan *p, T *rho, cplx_t<T> *spec, int64_t rows, cudaStream_t st) {
   using C = cplx_t<T>;
   const int nx = p->d.nx;
+  if constexpr (sizeof(T) == 8 && SOG_COLS_TMA) {
+    // fp64 512-point rows: bulk-copied rows, one warp per row
+    if (nx == 512 && launch_r2c_tma(reinterpret_cast<const double *>(rho), reinterpret_cast<double2 *>(spec), rows, nx,
+                                    reinterpret_cast<const double2 *>(tw_of<T>(p, 0)), p->status.as<unsigned>(), st)) {
+      after(&p->tr, st, "fft_r2c_x");
+      return;
+    }
+  }
   const bool done = nx >= 16 && with_pow2(nx, [&](auto lc) {
     constexpr int L = decltype(lc)::value < 4 ? 4 : decltype(lc)::value;
     constexpr int n = 1 << L;
